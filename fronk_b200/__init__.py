@@ -1,0 +1,305 @@
+"""fronk_b200 - B200-native backend for Fronk's expert neuron-slice compute.
+
+Python mirror of the C ABI in include/fronk_b200.h (ctypes).  The compute is
+the in-tree CUDA library libfronk_b200.so; there is no CPU fallback: every
+entry point raises when the library or an sm_100 device is missing.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libfronk_b200.so")
+
+# src/backend.h:17-18
+OK, INVALID, STATE, NUMERIC, IO, UNSUPPORTED, MISMATCH = 0, -1, -2, -3, -4, -5, -6
+# src/native.h:8
+Q8_0, Q4_K, MXFP4 = 8, 12, 39
+ACT_F32, ACT_Q8 = 0, 1
+RUN_RMSNORM = 1
+MAX_BLOCKS, ROUTED, SHARED, TOPK, ACTIVE, NEURONS, MAX_TOKENS = 20, 512, 512, 10, 11, 32, 16
+LAYERS = 48
+
+_CODES = {OK: "OK", INVALID: "INVALID", STATE: "STATE", NUMERIC: "NUMERIC", IO: "IO",
+          UNSUPPORTED: "UNSUPPORTED", MISMATCH: "MISMATCH"}
+
+
+class FrcError(RuntimeError):
+    def __init__(self, code, where, detail=""):
+        self.code = code
+        super().__init__("%s: %s (%d)%s" % (where, _CODES.get(code, "?"), code, ": " + detail if detail else ""))
+
+
+class Geometry(ctypes.Structure):
+    _fields_ = [("hidden", ctypes.c_uint32), ("layers", ctypes.c_uint32),
+                ("gate_type", ctypes.c_uint32), ("down_type", ctypes.c_uint32)]
+
+    def __repr__(self):
+        return "Geometry(d=%d, layers=%d, gate=%d, down=%d)" % (self.hidden, self.layers, self.gate_type, self.down_type)
+
+
+REFERENCE_GEOMETRY = (2560, LAYERS, Q4_K, MXFP4)   # src/model.h:16, src/native.h:1-3
+BENCH_GEOMETRY = (2048, LAYERS, Q4_K, MXFP4)       # BASELINE configs[0] (down in MXFP4)
+
+_lib = None
+_vp, _u32, _u64, _sz, _int = ctypes.c_void_p, ctypes.c_uint, ctypes.c_uint64, ctypes.c_size_t, ctypes.c_int
+
+_SIGS = {
+    "frc_row_bytes": (_sz, [_u32, _u32]),
+    "frc_slice_bytes": (_sz, [_vp]),
+    "frc_shared_bytes": (_sz, [_vp]),
+    "frc_layer_bytes": (_sz, [_vp]),
+    "frc_unit_bytes": (_u64, [_vp]),
+    "frc_slice_offset": (_u64, [_vp, _u32, _u32]),
+    "frc_geometry_check": (_int, [_vp]),
+    "frc_open": (_int, [_int, _vp, _vp]),
+    "frc_close": (_int, [_vp]),
+    "frc_load_unit": (_int, [_vp, _int, _vp, _sz]),
+    "frc_load_layer": (_int, [_vp, _int, _u32, _vp, _sz]),
+    "frc_unload_unit": (_int, [_vp, _int]),
+    "frc_loaded_mask": (_int, [_vp, _vp]),
+    "frc_run": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _int]),
+    "frc_run_device": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
+    "frc_status": (_int, [_vp, _vp]),
+    "frc_launch_count": (_u64, [_vp]),
+    "frc_strerror": (ctypes.c_char_p, [_int]),
+    "frc_last_error": (ctypes.c_char_p, [_vp]),
+    "frc_rand64": (_u64, [_u64, _u64]),
+    "frc_normal": (ctypes.c_float, [_u64, _u64]),
+    "frc_encode_row": (_int, [_u32, _vp, _u32, _vp]),
+    "frc_synth_slice": (_int, [_vp, _u64, _u64, _vp]),
+    "frc_synth_shared": (_int, [_vp, _u64, _u64, _vp]),
+    "frc_synth_request": (_int, [_u32, _u32, _u64, _vp, _vp, _vp]),
+    "frc_pool_load": (_int, [_vp, _vp, _u32, _vp]),
+    "frc_fill_layer": (_int, [_vp, _int, _u32, _u64]),
+    "frc_pool_pick": (_u32, [_u64, _u32, _u32, _u32, _u32]),
+    "frc_debug_decode": (_int, [_vp, _u32, _vp, _u32, _u32, _vp]),
+    "frc_debug_quantize": (_int, [_vp, _u32, _vp, _vp, _vp, _vp]),
+    "frc_debug_hidden": (_int, [_vp, _vp, _sz, _vp]),
+}
+EXPORTS = sorted(_SIGS) + ["fr_cuda", "fr_cuda_f32", "fr_cuda_select_device", "fr_cuda_close"]
+
+
+def library():
+    """The loaded libfronk_b200.so.  Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FrcError(UNSUPPORTED, "library", "%s missing: run fronk_b200/build.py" % LIB_PATH)
+        lib = ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_GLOBAL)
+        for name, (res, args) in _SIGS.items():
+            f = getattr(lib, name)
+            f.restype, f.argtypes = res, args
+        _lib = lib
+    return _lib
+
+
+def _ptr(a):
+    return None if a is None else ctypes.c_void_p(a.ctypes.data)
+
+
+def geometry(hidden=2048, layers=LAYERS, gate_type=Q4_K, down_type=MXFP4):
+    g = Geometry(hidden, layers, gate_type, down_type)
+    rc = library().frc_geometry_check(ctypes.byref(g))
+    if rc:
+        raise FrcError(rc, "geometry", repr(g))
+    return g
+
+
+def row_bytes(type_, n):
+    return library().frc_row_bytes(type_, n)
+
+
+def slice_bytes(g):
+    return library().frc_slice_bytes(ctypes.byref(g))
+
+
+def shared_bytes(g):
+    return library().frc_shared_bytes(ctypes.byref(g))
+
+
+def layer_bytes(g):
+    return library().frc_layer_bytes(ctypes.byref(g))
+
+
+def unit_bytes(g):
+    return library().frc_unit_bytes(ctypes.byref(g))
+
+
+def slice_offset(g, layer, expert):
+    return library().frc_slice_offset(ctypes.byref(g), layer, expert)
+
+
+# ------------------------------------------------------------ synthetic data
+
+def synth_slice(g, seed, key):
+    out = np.zeros(slice_bytes(g), np.uint8)
+    rc = library().frc_synth_slice(ctypes.byref(g), seed, key, _ptr(out))
+    if rc:
+        raise FrcError(rc, "synth_slice")
+    return out
+
+
+def synth_shared(g, seed, key):
+    out = np.zeros(shared_bytes(g), np.uint8)
+    rc = library().frc_synth_shared(ctypes.byref(g), seed, key, _ptr(out))
+    if rc:
+        raise FrcError(rc, "synth_shared")
+    return out
+
+
+def synth_request(hidden, tokens, seed):
+    """(expert [T,10] u16, gate [T,11] f32, x [T,d] f32) of frc_synth_request."""
+    e = np.zeros((tokens, TOPK), np.uint16)
+    gt = np.zeros((tokens, ACTIVE), np.float32)
+    x = np.zeros((tokens, hidden), np.float32)
+    rc = library().frc_synth_request(hidden, tokens, seed, _ptr(e), _ptr(gt), _ptr(x))
+    if rc:
+        raise FrcError(rc, "synth_request")
+    return e, gt, x
+
+
+def encode_row(type_, w):
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.zeros(row_bytes(type_, w.size), np.uint8)
+    rc = library().frc_encode_row(type_, _ptr(w), w.size, _ptr(out))
+    if rc:
+        raise FrcError(rc, "encode_row")
+    return out
+
+
+def pool_pick(seed, block, layer, expert, count):
+    return library().frc_pool_pick(seed, block, layer, expert, count)
+
+
+def rand64(seed, index):
+    return library().frc_rand64(seed, index)
+
+
+# ------------------------------------------------------------------ context
+
+class Context:
+    """One device context (frc_context): loaded units, scratch, streams."""
+
+    def __init__(self, device=0, hidden=2048, layers=LAYERS, gate_type=Q4_K, down_type=MXFP4):
+        self.lib = library()
+        self.g = geometry(hidden, layers, gate_type, down_type)
+        self.hidden = hidden
+        h = ctypes.c_void_p()
+        rc = self.lib.frc_open(device, ctypes.byref(self.g), ctypes.byref(h))
+        if rc:
+            raise FrcError(rc, "frc_open", "device %d" % device)
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if self.h:
+            self.lib.frc_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc, where):
+        if rc:
+            raise FrcError(rc, where, (self.lib.frc_last_error(self.h) or b"").decode())
+
+    @property
+    def last_error(self):
+        return (self.lib.frc_last_error(self.h) or b"").decode()
+
+    @property
+    def launches(self):
+        return self.lib.frc_launch_count(self.h)
+
+    def load_unit(self, block, unit):
+        return self.lib.frc_load_unit(self.h, block, _ptr(unit), unit.nbytes)
+
+    def load_layer(self, block, layer, data):
+        """data: a numpy uint8 array of layer_bytes (reference layout)."""
+        return self.lib.frc_load_layer(self.h, block, layer, _ptr(data), data.nbytes)
+
+    def unload(self, block):
+        return self.lib.frc_unload_unit(self.h, block)
+
+    def loaded_mask(self):
+        m = ctypes.c_uint32()
+        self._check(self.lib.frc_loaded_mask(self.h, ctypes.byref(m)), "loaded_mask")
+        return m.value
+
+    def run(self, layer, expert, gate, x, act=ACT_Q8, out=None):
+        """Synchronous host-memory run (fr_backend.run semantics).  Returns
+        (rc, y); on failure y is the untouched `out` (or None)."""
+        expert = np.ascontiguousarray(expert, np.uint16)
+        gate = np.ascontiguousarray(gate, np.float32)
+        x = np.ascontiguousarray(x, np.float32)
+        tokens = x.shape[0]
+        y = out if out is not None else np.zeros((tokens, self.hidden), np.float32)
+        rc = self.lib.frc_run(self.h, layer, tokens, _ptr(expert), _ptr(gate), _ptr(x), _ptr(y), act)
+        return rc, y
+
+    def run_device(self, layer, tokens, expert_ptr, gate_ptr, x_ptr, x_add_ptr, x_out_ptr, y_ptr, act=ACT_Q8,
+                   flags=0, stream=None):
+        rc = self.lib.frc_run_device(self.h, layer, tokens, expert_ptr, gate_ptr, x_ptr, x_add_ptr, x_out_ptr,
+                                     y_ptr, act, flags, stream)
+        self._check(rc, "run_device")
+
+    def status(self, stream=None):
+        return self.lib.frc_status(self.h, stream)
+
+    def pool_load(self, slices, shared):
+        slices = np.ascontiguousarray(slices, np.uint8)
+        count = slices.size // slice_bytes(self.g)
+        self._check(self.lib.frc_pool_load(self.h, _ptr(slices), count, _ptr(np.ascontiguousarray(shared))),
+                    "pool_load")
+        return count
+
+    def fill_layer(self, block, layer, seed):
+        self._check(self.lib.frc_fill_layer(self.h, block, layer, seed), "fill_layer")
+
+    def debug_decode(self, type_, rows, n, count):
+        out = np.zeros((count, n), np.float32)
+        self._check(self.lib.frc_debug_decode(self.h, type_, _ptr(np.ascontiguousarray(rows, np.uint8)), n, count,
+                                              _ptr(out)), "debug_decode")
+        return out
+
+    def debug_quantize(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        tokens = x.shape[0]
+        q = np.zeros(x.shape, np.int8)
+        s = np.zeros((tokens, self.hidden // 64), np.float32)
+        deq = np.zeros(x.shape, np.float32)
+        self._check(self.lib.frc_debug_quantize(self.h, tokens, _ptr(x), _ptr(q), _ptr(s), _ptr(deq)),
+                    "debug_quantize")
+        return q, s, deq
+
+    def debug_hidden(self):
+        n = ctypes.c_size_t()
+        self._check(self.lib.frc_debug_hidden(self.h, None, 0, ctypes.byref(n)), "debug_hidden")
+        out = np.zeros(n.value, np.float32)
+        self._check(self.lib.frc_debug_hidden(self.h, _ptr(out), n.value, ctypes.byref(n)), "debug_hidden")
+        return out
+
+
+def cuda_available():
+    """True when the library loads and device 0 is an sm_100 part."""
+    try:
+        lib = library()
+    except FrcError:
+        return False
+    g = Geometry(2048, 1, Q4_K, MXFP4)
+    h = ctypes.c_void_p()
+    rc = lib.frc_open(0, ctypes.byref(g), ctypes.byref(h))
+    if rc == OK:
+        lib.frc_close(h)
+    return rc == OK

@@ -1,0 +1,64 @@
+"""Builds libfronk_b200.so in-tree: the sm_100a kernels, the C ABI and the
+fr_backend plugin table.  nvcc cross-compiles without a GPU."""
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+OUT = os.path.join(HERE, "_build")
+LIB = os.path.join(HERE, "libfronk_b200.so")
+
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+CUDA_SOURCES = ["frc.cu"]
+C_SOURCES = ["frc_synth.c", "fr_cuda_backend.c"]
+DEPS = CUDA_SOURCES + C_SOURCES + ["frc_device.cuh"]
+
+
+def _run(cmd):
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode:
+        sys.stderr.write(proc.stdout + proc.stderr)
+        raise RuntimeError("build step failed: " + " ".join(cmd))
+    return proc.stdout + proc.stderr
+
+
+def _stale(target, sources):
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    headers = [os.path.join(ROOT, "include", h) for h in os.listdir(os.path.join(ROOT, "include"))]
+    return any(os.path.getmtime(s) > t for s in sources + headers)
+
+
+def build(force=False, verbose=False):
+    """Compile when a source is newer than the library; returns its path."""
+    sources = [os.path.join(CSRC, s) for s in DEPS]
+    if not force and not _stale(LIB, sources):
+        return LIB
+    os.makedirs(OUT, exist_ok=True)
+    objs = []
+    for s in CUDA_SOURCES:
+        o = os.path.join(OUT, s + ".o")
+        log = _run([NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xptxas", "-v",
+                    "-c", os.path.join(CSRC, s), "-o", o])
+        with open(os.path.join(OUT, s + ".ptxas.txt"), "w") as f:
+            f.write(log)
+        if verbose:
+            print(log)
+        objs.append(o)
+    for s in C_SOURCES:
+        o = os.path.join(OUT, s + ".o")
+        _run(["gcc", "-O2", "-std=c11", "-fPIC", "-Wall", "-Wextra", "-ffp-contract=off", "-c",
+              os.path.join(CSRC, s), "-o", o])
+        objs.append(o)
+    tmp = LIB + ".tmp"
+    _run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-ldl", "-lm"])
+    os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))

@@ -1,0 +1,337 @@
+// frc_device.cuh - device building blocks of the expert-slice kernels (sm_100a).
+//
+// Exactness: every fp32 operation whose rounding the parity tests pin is
+// written with an explicit _rn intrinsic, so nvcc's FMA contraction cannot
+// change it.  Integer block dot products use dp4a and are exact.
+#pragma once
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace frc {
+
+constexpr unsigned kThreads = 256;     // 8 warps per CTA
+constexpr unsigned kWarps = kThreads / 32;
+constexpr unsigned kGuNeurons = 8;     // neurons per gate/up unit: one per warp
+constexpr unsigned kGuUnits = 32 / kGuNeurons;
+constexpr unsigned kDnRows = 64;       // down rows per down unit
+constexpr unsigned kDnSplit = 4;       // slice interleave of the down partial sums
+constexpr unsigned kMaxTokens = 16;
+constexpr unsigned kMaxUnique = kMaxTokens * 10 + 1;
+constexpr unsigned kMaxChunks = 8192 / kDnRows;
+constexpr unsigned kMaxBlocks = 20;
+
+enum : unsigned { kQ80 = 8, kQ4K = 12, kMXFP4 = 39 };
+enum : unsigned { kStNumeric = 1, kStInvalid = 2, kStTimeout = 4 };
+
+// Work-queue and dependency counters of one context.  Zero between launches:
+// the last CTA of every launch restores them.
+struct Ctl {
+  unsigned next;
+  unsigned exited;
+  unsigned pad[2];
+  unsigned gu_done[kMaxUnique + 3];
+  unsigned chunk_done[kMaxChunks];
+};
+
+// Dynamic shared memory offsets (bytes), computed on the host.
+struct Smem {
+  unsigned ids, gates, first, uid, umask, ugate, rms;
+  unsigned xq, xp, xs, xv, xf, hq, gs, stage;
+  unsigned stage_bytes, total;
+};
+
+struct LayerArgs {
+  const uint8_t* base[kMaxBlocks];  // this layer's region in each loaded block, ascending
+  const uint16_t* expert;           // [T][10]
+  const float* gate;                // [T][11]
+  const float* x;                   // [T][d]
+  const float* x_add;               // [T][d] or null
+  float* x_out;                     // [T][d] or null
+  float* y;                         // [T][d]
+  float* hidden;                    // [kMaxUnique][S][T][32]
+  float* partial;                   // [kMaxUnique][T][d]
+  Ctl* ctl;
+  unsigned* status;
+  Smem sm;
+  unsigned S, T, d;
+  unsigned norm;                    // FRC_RUN_RMSNORM
+  unsigned gate_type, down_type;
+  unsigned row_bytes, proj_bytes;   // routed gate row / gate projection
+  unsigned shared_row, shared_proj; // shared expert (Q8_0)
+  unsigned slice_bytes;
+};
+
+// ------------------------------------------------------------------ PTX
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+// Bulk (untiled) TMA copy global -> shared; both 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+constexpr uint64_t kWaitNs = 2000000000ull;  // every wait gives up after 2 s
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - start > kWaitNs) return false;
+  return true;
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool spin_geq(const unsigned* p, unsigned target) {
+  if (ld_acquire(p) >= target) return true;
+  const uint64_t start = globaltimer();
+  while (ld_acquire(p) < target) {
+    if (globaltimer() - start > kWaitNs) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+// Generic-form byte permute: msb of a selector nibble replicates the sign.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// ------------------------------------------------------------- numerics
+
+__device__ __forceinline__ float h2f(uint32_t bits16) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16)));
+}
+// Exact int -> float for |v| < 2^22 (1.5 * 2^23 magic).
+__device__ __forceinline__ float i2f(int v) {
+  return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
+}
+// Byte k of w as a float, exact.
+__device__ __forceinline__ float byte_f(uint32_t w, unsigned k) {
+  return __fsub_rn(__int_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | k)), 8388608.0f);
+}
+// 2^(e-128) as fp32 (subnormal for e < 2); the MXFP4 scale of the doubled E2M1 table.
+__device__ __forceinline__ float pow2_m128(unsigned e) {
+  return __uint_as_float(e >= 2 ? (e - 1) << 23 : 0x00200000u << e);
+}
+// Doubled E2M1 magnitudes {0,1,2,3,4,6,8,12} for prmt lookups.
+constexpr uint32_t kE2M1Lo = 0x03020100u, kE2M1Hi = 0x0C080604u;
+
+// Stable SiLU(a) * u in double, narrowed to fp32 (backends/ref.c:81-83).
+__device__ __forceinline__ bool swiglu(float a, float u, float* h) {
+  const double ad = a;
+  const double sig = a >= 0 ? 1.0 / (1.0 + exp(-ad)) : exp(ad) / (1.0 + exp(ad));
+  const double v = ad * sig * (double)u;
+  if (!isfinite(v) || fabs(v) > 3.4028234663852886e38) return false;
+  *h = __double2float_rn(v);
+  return true;
+}
+
+// Symmetric int8 quantization of one value of a group with absolute maximum
+// amax (src/q4.c:37-61): scale = amax/127, multiplier 127/amax (x/amax*127 if
+// that overflows), nearest-even, clamp.  Returns the int8 value.
+// q8_round keeps the rounded float (its sign of zero is what the
+// reference's dequantized output carries); q8_value is its integer.
+__device__ __forceinline__ float q8_round(float x, float amax, float scale) {
+  if (scale == 0.0f) return 0.0f;
+  const float inv = __fdiv_rn(127.0f, amax);
+  float v = isfinite(inv) ? __fmul_rn(x, inv) : __fmul_rn(__fdiv_rn(x, amax), 127.0f);
+  v = rintf(v);
+  return fminf(fmaxf(v, -127.0f), 127.0f);
+}
+__device__ __forceinline__ int q8_value(float x, float amax, float scale) {
+  return static_cast<int>(q8_round(x, amax, scale));
+}
+
+// Position of element n (0..31) of a 32-weight block in the "prmt order" that
+// matches an MXFP4 block's nibble bytes (byte j holds elements j and j+16).
+__device__ __forceinline__ unsigned prmt_pos(unsigned n) {
+  const unsigned j = n & 15, hi = n >> 4, m = j >> 2, r = j & 3;
+  return 4 * (2 * m + (r >> 1)) + 2 * (r & 1) + hi;
+}
+// uint4 slot of quad q (0..3) of x group p in the swizzled activation layout.
+__device__ __forceinline__ unsigned xslot(unsigned p, unsigned q) { return 4 * p + (q ^ ((p >> 1) & 3)); }
+
+// ----------------------------------------------------- gate/up pair terms
+// One lane's term for x group p (64 weights = two 32-weight blocks) of a
+// gate or up row, Q8 activations.  Identical operations to the oracle's
+// pair_term.
+
+struct XQ {  // one token's quantized activations in shared memory
+  const uint8_t* q;   // swizzled natural-order int8, d bytes
+  const uint8_t* qp;  // swizzled prmt-order int8 (MXFP4 rows), d bytes
+  const float* v;     // per-32 sums of q, d/32
+};
+
+__device__ __forceinline__ void load_x16(const uint8_t* xq, unsigned p, uint32_t (&x)[16]) {
+#pragma unroll
+  for (unsigned q = 0; q < 4; ++q) {
+    const uint4 w = *reinterpret_cast<const uint4*>(xq + 16 * xslot(p, q));
+    x[4 * q] = w.x; x[4 * q + 1] = w.y; x[4 * q + 2] = w.z; x[4 * q + 3] = w.w;
+  }
+}
+
+// Q4_K: super-block p/4, sub-blocks 2(p%4) and 2(p%4)+1.
+__device__ __forceinline__ float term_q4k(const uint8_t* row, unsigned p, const uint32_t (&x)[16],
+                                          float v0, float v1, bool& bad) {
+  const uint8_t* b = row + (p >> 2) * 144;
+  const uint4 hdr = *reinterpret_cast<const uint4*>(b);
+  const unsigned gp = p & 3;
+  const float d = h2f(hdr.x & 0xffffu), dm = h2f(hdr.x >> 16);
+  bad |= !isfinite(d) || !isfinite(dm);
+  // 6-bit scales/mins of the eight sub-blocks (src/native.c:17-18), four per word.
+  const uint32_t sc_lo = hdr.y & 0x3f3f3f3fu, mi_lo = hdr.z & 0x3f3f3f3fu;
+  const uint32_t sc_hi = (hdr.w & 0x0f0f0f0fu) | ((hdr.y >> 6) & 0x03030303u) << 4;
+  const uint32_t mi_hi = ((hdr.w >> 4) & 0x0f0f0f0fu) | ((hdr.z >> 6) & 0x03030303u) << 4;
+  const uint32_t sw = gp >= 2 ? sc_hi : sc_lo, mw = gp >= 2 ? mi_hi : mi_lo;
+  const unsigned k0 = (2 * gp) & 3;
+  const float ds0 = __fmul_rn(d, byte_f(sw, k0)), ds1 = __fmul_rn(d, byte_f(sw, k0 + 1));
+  const float dm0 = __fmul_rn(dm, byte_f(mw, k0)), dm1 = __fmul_rn(dm, byte_f(mw, k0 + 1));
+  const uint4* qs = reinterpret_cast<const uint4*>(b + 16 + 32 * gp);
+  const uint4 qa = qs[0], qb = qs[1];
+  const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+  int i0 = 0, i1 = 0;
+#pragma unroll
+  for (unsigned m = 0; m < 8; ++m) {
+    i0 = __dp4a(static_cast<int>(w[m] & 0x0f0f0f0fu), static_cast<int>(x[m]), i0);
+    i1 = __dp4a(static_cast<int>((w[m] >> 4) & 0x0f0f0f0fu), static_cast<int>(x[8 + m]), i1);
+  }
+  const float dot = __fmaf_rn(ds1, i2f(i1), __fmul_rn(ds0, i2f(i0)));
+  const float mins = __fmaf_rn(dm1, v1, __fmul_rn(dm0, v0));
+  return __fsub_rn(dot, mins);
+}
+
+// MXFP4 device row: [e: nb bytes][qs: nb x 16 bytes]; x in prmt order.
+__device__ __forceinline__ int idot_mxfp4_16(const uint4 q, const uint32_t* x) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+  int ip = 0, in = 0;
+#pragma unroll
+  for (unsigned m = 0; m < 4; ++m) {
+    const uint32_t lo = w[m], hi = w[m] >> 16, nlo = lo ^ 0x8888u, nhi = hi ^ 0x8888u;
+    ip = __dp4a(static_cast<int>(prmt(kE2M1Lo, kE2M1Hi, lo)), static_cast<int>(x[2 * m]), ip);
+    in = __dp4a(static_cast<int>(prmt(kE2M1Lo, kE2M1Hi, nlo)), static_cast<int>(x[2 * m]), in);
+    ip = __dp4a(static_cast<int>(prmt(kE2M1Lo, kE2M1Hi, hi)), static_cast<int>(x[2 * m + 1]), ip);
+    in = __dp4a(static_cast<int>(prmt(kE2M1Lo, kE2M1Hi, nhi)), static_cast<int>(x[2 * m + 1]), in);
+  }
+  return ip - in;
+}
+__device__ __forceinline__ float term_mxfp4(const uint8_t* row, unsigned nb, unsigned p,
+                                            const uint32_t (&x)[16], bool& bad) {
+  const unsigned e0 = row[2 * p], e1 = row[2 * p + 1];
+  bad |= e0 == 255 || e1 == 255;
+  const uint4* qs = reinterpret_cast<const uint4*>(row + nb + 32 * p);
+  const int i0 = idot_mxfp4_16(qs[0], x), i1 = idot_mxfp4_16(qs[1], x + 8);
+  return __fmaf_rn(pow2_m128(e1), i2f(i1), __fmul_rn(pow2_m128(e0), i2f(i0)));
+}
+
+// Q8_0 device row: [d: nb x 2 bytes][qs: nb x 32 bytes]; x in natural order.
+__device__ __forceinline__ float term_q80(const uint8_t* row, unsigned nb, unsigned p,
+                                          const uint32_t (&x)[16], bool& bad) {
+  const uint32_t dd = *reinterpret_cast<const uint32_t*>(row + 4 * p);
+  const float s0 = h2f(dd & 0xffffu), s1 = h2f(dd >> 16);
+  bad |= !isfinite(s0) || !isfinite(s1);
+  const uint4* qs = reinterpret_cast<const uint4*>(row + 2 * nb + 64 * p);
+  int i0 = 0, i1 = 0;
+#pragma unroll
+  for (unsigned q = 0; q < 2; ++q) {
+    const uint4 a = qs[q], b = qs[2 + q];
+    i0 = __dp4a(static_cast<int>(a.x), static_cast<int>(x[4 * q]), i0);
+    i0 = __dp4a(static_cast<int>(a.y), static_cast<int>(x[4 * q + 1]), i0);
+    i0 = __dp4a(static_cast<int>(a.z), static_cast<int>(x[4 * q + 2]), i0);
+    i0 = __dp4a(static_cast<int>(a.w), static_cast<int>(x[4 * q + 3]), i0);
+    i1 = __dp4a(static_cast<int>(b.x), static_cast<int>(x[8 + 4 * q]), i1);
+    i1 = __dp4a(static_cast<int>(b.y), static_cast<int>(x[8 + 4 * q + 1]), i1);
+    i1 = __dp4a(static_cast<int>(b.z), static_cast<int>(x[8 + 4 * q + 2]), i1);
+    i1 = __dp4a(static_cast<int>(b.w), static_cast<int>(x[8 + 4 * q + 3]), i1);
+  }
+  return __fmaf_rn(s1, i2f(i1), __fmul_rn(s0, i2f(i0)));
+}
+
+// ------------------------------------------------- exact fp32 weight decode
+// The fp32 weight src/native.c:14-30 computes, element j of a device row.
+
+__device__ __forceinline__ float weight_q4k(const uint8_t* row, unsigned j) {
+  const uint8_t* b = row + (j / 256) * 144;
+  const unsigned g = j % 256 / 32;
+  const uint8_t* s = b + 4;
+  unsigned sc, mi;
+  if (g < 4) {
+    sc = s[g] & 63; mi = s[g + 4] & 63;
+  } else {
+    sc = (s[g + 4] & 15) | ((s[g - 4] >> 6) << 4);
+    mi = (s[g + 4] >> 4) | ((s[g] >> 6) << 4);
+  }
+  const float d = h2f(b[0] | b[1] << 8), m = h2f(b[2] | b[3] << 8);
+  const unsigned q = (b[16 + (g / 2) * 32 + j % 32] >> ((g % 2) * 4)) & 15;
+  // (d*sc)*q is exact, m*mi is exact: one rounding of their difference.
+  return __fmaf_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q),
+                   -__fmul_rn(m, static_cast<float>(mi)));
+}
+__device__ __forceinline__ float e2m1(unsigned nib) {
+  const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  float v = 0.0f;
+#pragma unroll
+  for (unsigned i = 0; i < 8; ++i) v = (nib & 7) == i ? mag[i] : v;
+  return nib & 8 ? -v : v;
+}
+__device__ __forceinline__ float weight_mxfp4(const uint8_t* row, unsigned nb, unsigned j) {
+  const unsigned blk = j / 32, n = j % 32, e = row[blk];
+  if (e == 255) return __int_as_float(0x7fc00000);
+  const unsigned nib = (row[nb + 16 * blk + (n & 15)] >> (n >> 4 ? 4 : 0)) & 15;
+  return __fmul_rn(__uint_as_float(e ? e << 23 : 0x00400000u), e2m1(nib));
+}
+__device__ __forceinline__ float weight_q80(const uint8_t* row, unsigned nb, unsigned j) {
+  const unsigned blk = j / 32;
+  const float d = h2f(row[2 * blk] | row[2 * blk + 1] << 8);
+  return __fmul_rn(d, static_cast<float>(static_cast<int8_t>(row[2 * nb + j])));
+}
+__device__ __forceinline__ float weight_any(const uint8_t* row, unsigned type, unsigned n, unsigned j) {
+  if (type == kQ4K) return weight_q4k(row, j);
+  if (type == kMXFP4) return weight_mxfp4(row, n / 32, j);
+  return weight_q80(row, n / 32, j);
+}
+
+// splitmix64 of (seed, index): the same function as frc_rand64 on the host.
+__host__ __device__ __forceinline__ uint64_t rand64(uint64_t seed, uint64_t index) {
+  uint64_t z = seed + 0x9E3779B97F4A7C15ull * (index + 1);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+}  // namespace frc

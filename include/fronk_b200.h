@@ -1,0 +1,172 @@
+/* fronk_b200.h - C ABI of the B200 expert neuron-slice backend.
+ *
+ * One call computes one MoE layer for 1..16 tokens: for every token, the gated
+ * sum over its ten routed experts (plus the shared expert when its gate is
+ * nonzero) of down[:,S] . (SiLU(gate[S,:] . x) * (up[S,:] . x)), over every
+ * 32-neuron slice S loaded into this context.  It replaces the compute of the
+ * reference's fr_backend.run (src/backend.h:52-67, backends/ref.c:57-98) and
+ * takes the hidden size, the routed block formats and the token count as run
+ * time values, so the reference geometry (d = 2560) and the benchmark one
+ * (d = 2048) share one build.
+ *
+ * Plain C types only.  Every function returns an FRC_* status (the reference's
+ * FR_* values, src/backend.h:17-18); nothing throws across this boundary.
+ * A context belongs to one host thread at a time (calls are externally
+ * serialized, as src/backend.h:1-2 requires of backends).
+ */
+#ifndef FRONK_B200_H
+#define FRONK_B200_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes, same values as src/backend.h:17-18. */
+enum { FRC_OK = 0, FRC_INVALID = -1, FRC_STATE = -2, FRC_NUMERIC = -3,
+       FRC_IO = -4, FRC_UNSUPPORTED = -5, FRC_MISMATCH = -6 };
+
+/* Block type ids, same values as src/native.h:8. */
+enum { FRC_Q8_0 = 8, FRC_Q4_K = 12, FRC_MXFP4 = 39 };
+
+/* Activation precision of a run.  FRC_ACT_F32 multiplies exactly decoded
+ * weights by fp32 activations (the arithmetic of backends/ref.c "ref").
+ * FRC_ACT_Q8 first quantizes x per 64 and each 32-neuron hidden slice to int8
+ * with the scheme of src/q4.c:37-61 (the "ref-q8" activation format,
+ * backends/ref.c:66,85) and takes integer block dot products. */
+enum { FRC_ACT_F32 = 0, FRC_ACT_Q8 = 1 };
+
+/* Model constants of src/model.h:18-27. */
+enum { FRC_MAX_BLOCKS = 20, FRC_ROUTED_EXPERTS = 512, FRC_SHARED_EXPERT = 512,
+       FRC_TOPK = 10, FRC_ACTIVE = 11, FRC_NEURONS = 32, FRC_MAX_TOKENS = 16,
+       FRC_MAX_LAYERS = 64 };
+
+/* Shape of one ownership unit (a "block" of the reference: the same 32
+ * neurons of every expert in every layer).  The reference's own layout is
+ * {2560, 48, FRC_Q4_K, FRC_MXFP4} (src/native.h:9-18); the shared expert is
+ * always Q8_0 for gate, up and down. */
+typedef struct {
+    uint32_t hidden;     /* d: a multiple of 512, at most 8192 */
+    uint32_t layers;     /* 1..FRC_MAX_LAYERS */
+    uint32_t gate_type;  /* routed gate and up rows: FRC_Q4_K, FRC_MXFP4 or FRC_Q8_0 */
+    uint32_t down_type;  /* routed down rows (32 neurons each): FRC_MXFP4 or FRC_Q8_0 */
+} frc_geometry;
+
+/* ---- Geometry (host only; mirrors src/native.h:9-21 with run-time d) ---- */
+/* Bytes of one row of n weights of the given type (src/native.h:19-21); 0 if invalid. */
+size_t frc_row_bytes(unsigned type, unsigned n);
+/* Bytes of one routed 32-neuron slice: 32 gate rows, 32 up rows, d down rows. */
+size_t frc_slice_bytes(const frc_geometry *g);
+/* Bytes of the shared expert's slice (three Q8_0 projections). */
+size_t frc_shared_bytes(const frc_geometry *g);
+/* Bytes of one layer: 512 routed slices then the shared slice. */
+size_t frc_layer_bytes(const frc_geometry *g);
+/* Bytes of one unit (all layers); FR_NATIVE_BLOCK_BYTES for the reference geometry. */
+uint64_t frc_unit_bytes(const frc_geometry *g);
+/* Offset of (layer, expert) inside a unit (src/native.h:16-18); expert 512 is shared. */
+uint64_t frc_slice_offset(const frc_geometry *g, unsigned layer, unsigned expert);
+/* FRC_OK when g is a supported geometry. */
+int frc_geometry_check(const frc_geometry *g);
+
+/* ---- Context ---- */
+typedef struct frc_context frc_context;
+
+/* Opens device `device` for units of geometry g.  Allocates all run-time
+ * scratch now; run calls allocate nothing (src/backend.h:5).  FRC_UNSUPPORTED
+ * when the device is not an sm_100 part. */
+int frc_open(int device, const frc_geometry *g, frc_context **out);
+int frc_close(frc_context *c);
+/* Copies a whole unit (frc_unit_bytes, reference byte layout, host memory)
+ * into HBM, re-laid out for aligned 128-bit access.  This is the set-up copy a
+ * discrete GPU needs where the CPU backends borrow the mapping
+ * (src/backend.h:55-60).  Occupied block: FRC_STATE; bad index/size: FRC_INVALID. */
+int frc_load_unit(frc_context *c, int block, const void *unit, size_t len);
+/* Loads only one layer of a unit (frc_layer_bytes from a host buffer).  The
+ * block then counts as loaded; layers never loaded are reported by run as
+ * FRC_STATE.  Used for sparse correctness fixtures. */
+int frc_load_layer(frc_context *c, int block, unsigned layer, const void *layer_bytes, size_t len);
+int frc_unload_unit(frc_context *c, int block);
+/* Bit b set when block b is loaded. */
+int frc_loaded_mask(const frc_context *c, uint32_t *mask);
+
+/* Synchronous run from host memory, the semantics of fr_backend.run
+ * (src/backend.h:1-5, backends/ref.c:41-98): validates the request (ids < 512
+ * and distinct per token, gates finite and >= 0, x finite, FE_TONEAREST),
+ * then computes y[tokens][d].  On any error y is left byte-identical.
+ *   expert: [tokens][10] routed ids      gate: [tokens][11], shared last
+ *   x:      [tokens][d]                  y:    [tokens][d]
+ * Errors: FRC_INVALID, FRC_NUMERIC (nonfinite input, a nonfinite scale in any
+ * referenced block even with gate 0, fp32 overflow), FRC_STATE (nothing loaded). */
+int frc_run(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *expert,
+            const float *gate, const float *x, float *y, int act);
+
+/* Flags of frc_run_device. */
+enum { FRC_RUN_RMSNORM = 1 };
+
+/* Asynchronous run on device memory, enqueued on `stream` (a cudaStream_t, or
+ * NULL for the legacy default stream); nothing is validated on the host and
+ * nothing synchronizes, so it can be captured in a CUDA graph.  The kernel
+ * forms v = x + x_add (x_add may be NULL) and, when x_out is not NULL, stores
+ * v there (a residual stream; x_out must not alias x or x_add).  With
+ * FRC_RUN_RMSNORM the layer's input is v / sqrt(mean(v^2) + 1e-6) per token
+ * (the pre-norm a decoder block applies before its MoE), otherwise v.
+ * Numeric and bounds failures set the context's device status word, read by
+ * frc_status. */
+int frc_run_device(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *expert,
+                   const float *gate, const float *x, const float *x_add, float *x_out,
+                   float *y, int act, unsigned flags, void *stream);
+/* Waits for `stream`, returns and clears the device status (FRC_OK,
+ * FRC_NUMERIC, FRC_INVALID for an out-of-range id, FRC_IO for a timed-out wait). */
+int frc_status(frc_context *c, void *stream);
+/* Count of kernels this context has launched since open. */
+uint64_t frc_launch_count(const frc_context *c);
+const char *frc_strerror(int rc);
+/* Text of the last failure on this context (static storage). */
+const char *frc_last_error(const frc_context *c);
+
+/* ---- Synthetic inputs (host only) ---- */
+/* Counter-based generator: splitmix64 of (seed, index). */
+uint64_t frc_rand64(uint64_t seed, uint64_t index);
+/* Approximately N(0,1): Irwin-Hall sum of four 16-bit uniforms, scaled to unit
+ * variance.  Exact integer-then-one-multiply arithmetic, so every platform
+ * gives the same float. */
+float frc_normal(uint64_t seed, uint64_t index);
+/* Encodes n weights into one row of the given type (reference byte layout):
+ * Q4_K super-blocks of 256, MXFP4 blocks of 32, Q8_0 blocks of 32. */
+int frc_encode_row(unsigned type, const float *w, unsigned n, uint8_t *out);
+/* One routed slice in reference layout, weights ~N(0, 0.02) quantized to the
+ * geometry's formats; `key` selects the slice's random stream. */
+int frc_synth_slice(const frc_geometry *g, uint64_t seed, uint64_t key, uint8_t *out);
+/* The shared expert's slice (Q8_0 x3), weights ~N(0, 0.02). */
+int frc_synth_shared(const frc_geometry *g, uint64_t seed, uint64_t key, uint8_t *out);
+/* A request: x ~ N(0,1); 10 of 512 experts uniform without replacement;
+ * gates softmax(N(0,1)) over the 10; shared gate 0. */
+int frc_synth_request(unsigned hidden, unsigned tokens, uint64_t seed,
+                      uint16_t *expert, float *gate, float *x);
+
+/* ---- Benchmark-scale units without host encoding ---- */
+/* Uploads `count` routed slices and one shared slice (reference layout) as a
+ * device pool. */
+int frc_pool_load(frc_context *c, const uint8_t *slices, unsigned count, const uint8_t *shared);
+/* Fills every routed slot and the shared slot of (block, layer) from the pool
+ * on the device: slot e takes pool slice frc_pool_pick(seed, block, layer, e, count). */
+int frc_fill_layer(frc_context *c, int block, unsigned layer, uint64_t seed);
+unsigned frc_pool_pick(uint64_t seed, unsigned block, unsigned layer, unsigned expert, unsigned count);
+
+/* ---- Diagnostics used by the parity tests ---- */
+/* GPU decode of `rows` rows of n weights (reference layout) to fp32. */
+int frc_debug_decode(frc_context *c, unsigned type, const uint8_t *rows, unsigned n,
+                     unsigned count, float *out);
+/* GPU activation quantization of tokens x d values: int8 values, one fp32
+ * scale per 64, and the dequantized fp32 values of src/q4.c:37-61. */
+int frc_debug_quantize(frc_context *c, unsigned tokens, const float *x, int8_t *q,
+                       float *scale, float *deq);
+/* Hidden activations h of the last frc_run, in item order
+ * [unique expert][loaded block][token][32] (zero where the token does not use
+ * the expert); *count receives the number of floats. */
+int frc_debug_hidden(frc_context *c, float *h, size_t cap, size_t *count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

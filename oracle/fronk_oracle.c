@@ -1,0 +1,574 @@
+/* fronk_oracle.c - CPU restatement of the reference's expert-slice arithmetic.
+ *
+ * TEST INFRASTRUCTURE ONLY: the checker for the CUDA path, never part of it.
+ * Build with -ffp-contract=off: every fp32 rounding below is deliberate.
+ * Each function cites the reference lines it restates (paths inside the
+ * fedesnore/fronk tree).
+ */
+#include "fronk_oracle.h"
+#include <fenv.h>
+#include <float.h>
+#include <stdlib.h>
+#include <math.h>
+#include <string.h>
+
+/* ---------------------------------------------------------------- scalars */
+
+/* src/q4.c:12-20: exact binary16 decode, subnormals and specials included. */
+float or_f16(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 31u, m = h & 1023u;
+    if (!e) {
+        float f = ldexpf((float)m, -24);
+        return sign ? -f : f;
+    }
+    uint32_t bits = sign | (e == 31 ? 0x7f800000u : (e + 112u) << 23) | m << 13;
+    float f;
+    memcpy(&f, &bits, sizeof f);
+    return f;
+}
+
+static uint16_t le16(const uint8_t *p) { return (uint16_t)(p[0] | (uint16_t)p[1] << 8); }
+
+/* src/q4.c:37-61, split so the int8 values and scales are visible.  Groups of
+ * 64 (a final 32-element group is a short group), scale = max/127,
+ * multiplier 127/max (x/max*127 if that overflows), nearest-even, clamp. */
+int or_q8_quantize(const float *x, size_t n, int8_t *q, float *scale) {
+    if (!x || !q || !scale || !n || n % 32 || fegetround() != FE_TONEAREST) return OR_INVALID;
+    for (size_t k = 0; k < n; k += 64) {
+        size_t count = n - k < 64 ? n - k : 64;
+        float max = 0;
+        for (size_t j = 0; j < count; ++j) {
+            if (!isfinite(x[k + j])) return OR_NUMERIC;
+            if (fabsf(x[k + j]) > max) max = fabsf(x[k + j]);
+        }
+        float s = max / 127.0f;
+        scale[k / 64] = s;
+        if (!s) {
+            for (size_t j = 0; j < count; ++j) q[k + j] = 0;
+            continue;
+        }
+        float inv = 127.0f / max;
+        for (size_t j = 0; j < count; ++j) {
+            float v = isfinite(inv) ? x[k + j] * inv : (x[k + j] / max) * 127.0f;
+            v = nearbyintf(v);
+            if (v > 127) v = 127;
+            if (v < -127) v = -127;
+            q[k + j] = (int8_t)v;
+        }
+    }
+    return OR_OK;
+}
+
+/* src/q4.c:37-61 as written: the dequantized value comes from the rounded
+ * float, so a negative input that rounds to zero gives -0.0. */
+int or_q8_activation(const float *x, float *out, size_t n) {
+    if (!x || !out || !n || n % 32 || fegetround() != FE_TONEAREST) return OR_INVALID;
+    for (size_t k = 0; k < n; k += 64) {
+        size_t count = n - k < 64 ? n - k : 64;
+        float max = 0;
+        for (size_t j = 0; j < count; ++j) {
+            if (!isfinite(x[k + j])) return OR_NUMERIC;
+            if (fabsf(x[k + j]) > max) max = fabsf(x[k + j]);
+        }
+        float s = max / 127.0f;
+        if (!s) {
+            for (size_t j = 0; j < count; ++j) out[k + j] = 0;
+            continue;
+        }
+        float inv = 127.0f / max;
+        for (size_t j = 0; j < count; ++j) {
+            float v = isfinite(inv) ? x[k + j] * inv : (x[k + j] / max) * 127.0f;
+            v = nearbyintf(v);
+            if (v > 127) v = 127;
+            if (v < -127) v = -127;
+            double d = (double)v * s; /* capped: rounded max/127 can overshoot FLT_MAX */
+            if (d > FLT_MAX) d = FLT_MAX;
+            if (d < -FLT_MAX) d = -FLT_MAX;
+            out[k + j] = (float)d;
+        }
+    }
+    return OR_OK;
+}
+
+/* src/q4.c:22-35: legacy Q4_0 groups of 32, (nibble - 8) * fp16 scale. */
+int or_q4_0_dot(const uint8_t *q, const float *x, size_t n, double *out) {
+    if (!q || !x || !out || !n || n % 32) return OR_INVALID;
+    double sum = 0;
+    for (size_t k = 0; k < n; k += 32, q += 18) {
+        float s = or_f16(le16(q));
+        if (!isfinite(s)) return OR_NUMERIC;
+        for (unsigned j = 0; j < 32; ++j) {
+            int v = (j < 16 ? q[2 + j] & 15 : q[2 + j - 16] >> 4) - 8;
+            sum += ((double)v * s) * x[k + j];
+        }
+    }
+    if (!isfinite(sum)) return OR_NUMERIC;
+    *out = sum;
+    return OR_OK;
+}
+
+/* E2M1 magnitudes of src/native.c:10 (index = nibble). */
+static const float kE2M1[16] = {0, .5f, 1, 1.5f, 2, 3, 4, 6, 0, -.5f, -1, -1.5f, -2, -3, -4, -6};
+/* The same values doubled, as integers: the MXFP4 integer dot uses them. */
+static const int kE2M1x2[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
+
+/* Q4_K 6-bit scale/min unpacking, src/native.c:17-18. */
+static void q4k_scale_min(const uint8_t *s, unsigned g, unsigned *sc, unsigned *mi) {
+    if (g < 4) {
+        *sc = s[g] & 63;
+        *mi = s[g + 4] & 63;
+    } else {
+        *sc = (s[g + 4] & 15) | ((unsigned)(s[g - 4] >> 6) << 4);
+        *mi = (unsigned)(s[g + 4] >> 4) | ((unsigned)(s[g] >> 6) << 4);
+    }
+}
+
+/* One decoded weight, the fp32 expressions of src/native.c:14-30.
+ * Returns 0 for the reserved MXFP4 exponent 255 (caller reports NUMERIC). */
+static int weight(const uint8_t *p, unsigned type, unsigned j, float *w) {
+    if (type == OR_Q4_K) {
+        const uint8_t *b = p + (size_t)(j / 256) * 144, *s = b + 4;
+        unsigned g = j % 256 / 32, sc, mi;
+        q4k_scale_min(s, g, &sc, &mi);
+        float d = or_f16(le16(b)), m = or_f16(le16(b + 2));
+        unsigned q = (b[16 + (g / 2) * 32 + j % 32] >> ((g % 2) * 4)) & 15;
+        *w = (d * (float)sc) * (float)q - m * (float)mi;
+    } else if (type == OR_MXFP4) {
+        const uint8_t *b = p + (size_t)(j / 32) * 17;
+        if (b[0] == 255) return 0;
+        *w = ldexpf(1.0f, (int)b[0] - 127) * kE2M1[(b[1 + j % 16] >> ((j % 32 / 16) * 4)) & 15];
+    } else {
+        const uint8_t *b = p + (size_t)(j / 32) * 34;
+        *w = or_f16(le16(b)) * (float)(int8_t)b[2 + j % 32];
+    }
+    return 1;
+}
+
+static int type_ok(unsigned type) { return type == OR_Q4_K || type == OR_MXFP4 || type == OR_Q8_0; }
+
+/* src/native.c:7-37. */
+int or_native_dot(const uint8_t *p, unsigned type, const float *x, unsigned n, double *out) {
+    if (!p || !x || !out || !n || !type_ok(type) || n % (type == OR_Q4_K ? 256 : 32)) return OR_INVALID;
+    double sum = 0;
+    for (unsigned j = 0; j < n; ++j) {
+        float w;
+        if (!weight(p, type, j, &w)) return OR_NUMERIC;
+        if (!isfinite(w) || !isfinite(x[j])) return OR_NUMERIC;
+        sum += (double)w * x[j];
+    }
+    if (!isfinite(sum)) return OR_NUMERIC;
+    *out = sum;
+    return OR_OK;
+}
+
+int or_decode_row(const uint8_t *p, unsigned type, unsigned n, float *w) {
+    if (!p || !w || !n || !type_ok(type) || n % (type == OR_Q4_K ? 256 : 32)) return OR_INVALID;
+    int rc = OR_OK;
+    for (unsigned j = 0; j < n; ++j) {
+        if (!weight(p, type, j, &w[j])) {
+            w[j] = NAN;
+            rc = OR_NUMERIC;
+        } else if (!isfinite(w[j])) {
+            rc = OR_NUMERIC;
+        }
+    }
+    return rc;
+}
+
+/* --------------------------------------------------------------- geometry */
+
+/* src/native.h:19-21 */
+size_t or_row_bytes(unsigned type, unsigned n) {
+    if (type == OR_Q4_K) return n % 256 ? 0 : (size_t)n / 256 * 144;
+    if (type == OR_MXFP4) return n % 32 ? 0 : (size_t)n / 32 * 17;
+    if (type == OR_Q8_0) return n % 32 ? 0 : (size_t)n / 32 * 34;
+    if (type == OR_Q4_0) return n % 32 ? 0 : (size_t)n / 32 * 18;
+    return 0;
+}
+/* src/native.h:9-11 with run-time d and formats. */
+size_t or_slice_bytes(unsigned d, unsigned gt, unsigned dt) {
+    return 2 * OR_NEURONS * or_row_bytes(gt, d) + (size_t)d * or_row_bytes(dt, OR_NEURONS);
+}
+/* src/native.h:12-13 */
+size_t or_shared_bytes(unsigned d) { return 3 * (size_t)d * 34; }
+/* src/native.h:14 */
+size_t or_layer_bytes(unsigned d, unsigned gt, unsigned dt) {
+    return OR_ROUTED * or_slice_bytes(d, gt, dt) + or_shared_bytes(d);
+}
+/* src/backend.h:44-48: 513 slices of three Q4_0 projections. */
+size_t or_legacy_layer_bytes(unsigned d) { return (size_t)(OR_ROUTED + 1) * 3 * OR_NEURONS * or_row_bytes(OR_Q4_0, d); }
+
+/* -------------------------------------------------------------- reference */
+
+/* backends/ref.c:37-40 */
+static int narrow(double v, float *out) {
+    if (!isfinite(v) || fabs(v) > FLT_MAX) return OR_NUMERIC;
+    *out = (float)v;
+    return OR_OK;
+}
+
+/* backends/ref.c:41-56 (token count bounded by OR_MAX_TOKENS instead of 8). */
+static int validate(unsigned hidden, unsigned tokens, const uint16_t *expert, const float *gate, const float *x) {
+    if (!expert || !gate || !x || tokens < 1 || tokens > OR_MAX_TOKENS || fegetround() != FE_TONEAREST)
+        return OR_INVALID;
+    for (unsigned t = 0; t < tokens; ++t) {
+        const uint16_t *id = expert + (size_t)t * OR_TOPK;
+        for (unsigned e = 0; e < OR_TOPK; ++e) {
+            if (id[e] >= OR_ROUTED) return OR_INVALID;
+            for (unsigned j = 0; j < e; ++j) if (id[j] == id[e]) return OR_INVALID;
+        }
+        for (unsigned e = 0; e < OR_ACTIVE; ++e) {
+            float g = gate[(size_t)t * OR_ACTIVE + e];
+            if (!isfinite(g)) return OR_NUMERIC;
+            if (g < 0) return OR_INVALID;
+        }
+        for (unsigned j = 0; j < hidden; ++j) if (!isfinite(x[(size_t)t * hidden + j])) return OR_NUMERIC;
+    }
+    return OR_OK;
+}
+
+static int model_ok(const or_model *m) {
+    if (!m || !m->hidden || m->hidden % 256) return 0;
+    if (!m->legacy && (!type_ok(m->gate_type) || (m->down_type != OR_MXFP4 && m->down_type != OR_Q8_0))) return 0;
+    return 1;
+}
+static int any_loaded(const or_model *m) {
+    for (unsigned b = 0; b < OR_BLOCKS; ++b) if (m->layer[b]) return 1;
+    return 0;
+}
+
+/* backends/ref.c:57-98: token, routed experts in request order, shared expert
+ * when its gate is nonzero, ascending blocks, dimension; double sums. */
+int or_ref_run(const or_model *m, unsigned tokens, const uint16_t *expert, const float *gate,
+               const float *x, float *y, int q8) {
+    if (!model_ok(m) || !y) return OR_INVALID;
+    const unsigned d = m->hidden;
+    int rc = validate(d, tokens, expert, gate, x);
+    if (rc) return rc;
+    if (!any_loaded(m)) return OR_STATE;
+    static double acc[8192];
+    static float xq[8192], result[OR_MAX_TOKENS * 8192];
+    if (d > 8192) return OR_INVALID;
+    for (unsigned t = 0; t < tokens; ++t) {
+        memset(acc, 0, d * sizeof(double));
+        const float *xt = x + (size_t)t * d;
+        if (q8) {
+            rc = or_q8_activation(xt, xq, d);
+            if (rc) return rc;
+            xt = xq;
+        }
+        for (unsigned e = 0; e < OR_ACTIVE; ++e) {
+            float g = gate[(size_t)t * OR_ACTIVE + e];
+            if (e == OR_TOPK && g == 0) continue; /* backends/ref.c:68 */
+            unsigned id = e == OR_TOPK ? OR_SHARED : expert[(size_t)t * OR_TOPK + e];
+            for (unsigned b = 0; b < OR_BLOCKS; ++b) {
+                if (!m->layer[b]) continue;
+                unsigned in = id == OR_SHARED ? OR_Q8_0 : m->gate_type;
+                unsigned down = id == OR_SHARED ? OR_Q8_0 : m->down_type;
+                size_t proj, in_row, down_row;
+                const uint8_t *p;
+                if (m->legacy) {
+                    in = down = OR_Q4_0;
+                    in_row = or_row_bytes(OR_Q4_0, d);
+                    proj = OR_NEURONS * in_row;
+                    down_row = 18;
+                    p = m->layer[b] + (size_t)id * 3 * proj;
+                } else {
+                    in_row = or_row_bytes(in, d);
+                    proj = id == OR_SHARED ? (size_t)d * 34 : OR_NEURONS * in_row;
+                    down_row = or_row_bytes(down, OR_NEURONS);
+                    p = m->layer[b] + (size_t)id * or_slice_bytes(d, m->gate_type, m->down_type);
+                }
+                float h[OR_NEURONS];
+                for (unsigned n = 0; n < OR_NEURONS; ++n) {
+                    double ad, ud;
+                    float a, u;
+                    const uint8_t *gr = p + n * in_row, *ur = p + proj + n * in_row;
+                    rc = m->legacy ? or_q4_0_dot(gr, xt, d, &ad) : or_native_dot(gr, in, xt, d, &ad);
+                    if (rc) return rc;
+                    rc = m->legacy ? or_q4_0_dot(ur, xt, d, &ud) : or_native_dot(ur, in, xt, d, &ud);
+                    if (rc) return rc;
+                    if (narrow(ad, &a) || narrow(ud, &u)) return OR_NUMERIC;
+                    double sig = a >= 0 ? 1 / (1 + exp(-(double)a)) : exp((double)a) / (1 + exp((double)a));
+                    if (narrow((double)a * sig * u, &h[n])) return OR_NUMERIC;
+                }
+                if (q8) {
+                    rc = or_q8_activation(h, h, OR_NEURONS);
+                    if (rc) return rc;
+                }
+                for (unsigned r = 0; r < d; ++r) {
+                    double dot;
+                    const uint8_t *row = p + 2 * proj + r * down_row;
+                    rc = m->legacy ? or_q4_0_dot(row, h, OR_NEURONS, &dot) : or_native_dot(row, down, h, OR_NEURONS, &dot);
+                    if (rc) return rc;
+                    acc[r] += (double)g * dot;
+                }
+            }
+        }
+        for (unsigned r = 0; r < d; ++r)
+            if (narrow(acc[r], &result[(size_t)t * d + r])) return OR_NUMERIC;
+    }
+    memcpy(y, result, (size_t)tokens * d * sizeof(float));
+    return OR_OK;
+}
+
+/* ------------------------------------------------------ GPU Q8 arithmetic */
+
+/* Integer dot of one 32-weight block against 32 int8 activations. */
+static int32_t idot_block(const uint8_t *p, unsigned type, unsigned blk, const int8_t *v) {
+    int32_t s = 0;
+    if (type == OR_Q4_K) {
+        const uint8_t *b = p + (size_t)(blk / 8) * 144;
+        unsigned g = blk % 8;
+        for (unsigned j = 0; j < 32; ++j) s += (int32_t)((b[16 + (g / 2) * 32 + j] >> ((g % 2) * 4)) & 15) * v[j];
+    } else if (type == OR_MXFP4) {
+        const uint8_t *b = p + (size_t)blk * 17;
+        for (unsigned j = 0; j < 32; ++j) s += kE2M1x2[(b[1 + j % 16] >> ((j / 16) * 4)) & 15] * v[j];
+    } else {
+        const uint8_t *b = p + (size_t)blk * 34;
+        for (unsigned j = 0; j < 32; ++j) s += (int32_t)(int8_t)b[2 + j] * v[j];
+    }
+    return s;
+}
+
+int or_block_idots(const uint8_t *p, unsigned type, unsigned n, const int8_t *v, int32_t *out) {
+    if (!p || !v || !out || !n || !type_ok(type) || n % (type == OR_Q4_K ? 256 : 32)) return OR_INVALID;
+    for (unsigned b = 0; b < n / 32; ++b) out[b] = idot_block(p, type, b, v + 32 * b);
+    return OR_OK;
+}
+
+/* Scale of block blk for the integer path: fp16 d (Q8_0) or 2^(e-128)
+ * (MXFP4: the E2M1 table is doubled).  0 when the scale is not finite. */
+static int block_scale(const uint8_t *p, unsigned type, unsigned blk, float *s) {
+    if (type == OR_MXFP4) {
+        unsigned e = p[(size_t)blk * 17];
+        if (e == 255) return 0;
+        *s = ldexpf(1.0f, (int)e - 128);
+        return 1;
+    }
+    *s = or_f16(le16(p + (size_t)blk * 34));
+    return isfinite(*s);
+}
+
+typedef struct {
+    unsigned d;
+    const int8_t *q;     /* [d] */
+    const float *scale;  /* [d/64] */
+    const int32_t *sum;  /* [d/32] sums of q per 32 */
+} qx;
+
+/* The term lane L adds for x group p (64 weights): see the kernel's
+ * gateup_pair_*.  Returns 0 on a nonfinite scale. */
+static int pair_term(const uint8_t *row, unsigned type, unsigned p, const qx *x, float *term) {
+    const int8_t *v = x->q + 64 * p;
+    if (type == OR_Q4_K) {
+        const uint8_t *b = row + (size_t)(p / 4) * 144;
+        unsigned gp = p % 4, sc0, mi0, sc1, mi1;
+        float d = or_f16(le16(b)), dm = or_f16(le16(b + 2));
+        if (!isfinite(d) || !isfinite(dm)) return 0;
+        q4k_scale_min(b + 4, 2 * gp, &sc0, &mi0);
+        q4k_scale_min(b + 4, 2 * gp + 1, &sc1, &mi1);
+        int32_t i0 = 0, i1 = 0;
+        for (unsigned j = 0; j < 32; ++j) {
+            uint8_t byte = b[16 + 32 * gp + j];
+            i0 += (int32_t)(byte & 15) * v[j];
+            i1 += (int32_t)(byte >> 4) * v[32 + j];
+        }
+        float ds0 = d * (float)sc0, ds1 = d * (float)sc1, dm0 = dm * (float)mi0, dm1 = dm * (float)mi1;
+        float f0 = (float)x->sum[2 * p], f1 = (float)x->sum[2 * p + 1];
+        float dot = fmaf(ds1, (float)i1, ds0 * (float)i0);
+        float mins = fmaf(dm1, f1, dm0 * f0);
+        *term = dot - mins;
+        return 1;
+    }
+    float s0, s1;
+    if (!block_scale(row, type, 2 * p, &s0) || !block_scale(row, type, 2 * p + 1, &s1)) return 0;
+    int32_t i0 = idot_block(row, type, 2 * p, v), i1 = idot_block(row, type, 2 * p + 1, v + 32);
+    *term = fmaf(s1, (float)i1, s0 * (float)i0);
+    return 1;
+}
+
+/* One gate or up dot as the kernel forms it: lane L accumulates the groups
+ * p = L, L+32, ... with fmaf(scale_p, term_p, acc); then a butterfly of
+ * pairwise sums over offsets 16, 8, 4, 2, 1. */
+static int lane_dot(const uint8_t *row, unsigned type, const qx *x, float *out) {
+    float lane[32];
+    unsigned groups = x->d / 64;
+    for (unsigned L = 0; L < 32; ++L) {
+        float acc = 0;
+        for (unsigned p = L; p < groups; p += 32) {
+            float term;
+            if (!pair_term(row, type, p, x, &term)) return OR_NUMERIC;
+            acc = fmaf(x->scale[p], term, acc);
+        }
+        lane[L] = acc;
+    }
+    for (unsigned off = 16; off; off >>= 1) {
+        float next[32];
+        for (unsigned L = 0; L < 32; ++L) next[L] = lane[L] + lane[L ^ off];
+        memcpy(lane, next, sizeof lane);
+    }
+    *out = lane[0];
+    return OR_OK;
+}
+
+/* Down row r of a slice (32 neurons, one block) against int8 hidden values:
+ * c = scale * (float)I, exact for MXFP4. */
+static int down_term(const uint8_t *down, unsigned type, unsigned r, const int8_t *v, float *c) {
+    float s;
+    if (!block_scale(down, type, r, &s)) return 0;
+    *c = s * (float)idot_block(down, type, r, v);
+    return 1;
+}
+
+enum { PORT_SPLIT = 4 }; /* down-projection partial sums per row (kernel DN_SPLIT) */
+
+int or_port_run(const or_model *m, unsigned tokens, const uint16_t *expert, const float *gate,
+                const float *x, float *y, float *h, size_t h_cap, size_t *h_count) {
+    if (!model_ok(m) || m->legacy || !y) return OR_INVALID;
+    const unsigned d = m->hidden;
+    if (d % 512 || d > 8192) return OR_INVALID;
+    int rc = validate(d, tokens, expert, gate, x);
+    if (rc) return rc;
+    if (!any_loaded(m)) return OR_STATE;
+
+    /* Plan: unique routed experts in first-appearance order (token-major),
+     * then the shared expert if any token gives it a nonzero gate. */
+    unsigned uid[OR_MAX_TOKENS * OR_TOPK + 1], umask[OR_MAX_TOKENS * OR_TOPK + 1], U = 0;
+    float ugate[OR_MAX_TOKENS * OR_TOPK + 1][OR_MAX_TOKENS];
+    memset(ugate, 0, sizeof ugate);
+    for (unsigned t = 0; t < tokens; ++t)
+        for (unsigned e = 0; e < OR_TOPK; ++e) {
+            unsigned id = expert[t * OR_TOPK + e], u = 0;
+            while (u < U && uid[u] != id) ++u;
+            if (u == U) { uid[U] = id; umask[U] = 0; ++U; }
+            umask[u] |= 1u << t;
+            ugate[u][t] = gate[t * OR_ACTIVE + e];
+        }
+    unsigned shared_mask = 0;
+    for (unsigned t = 0; t < tokens; ++t) if (gate[t * OR_ACTIVE + OR_TOPK] != 0) shared_mask |= 1u << t;
+    if (shared_mask) {
+        uid[U] = OR_SHARED; umask[U] = shared_mask;
+        for (unsigned t = 0; t < tokens; ++t) ugate[U][t] = gate[t * OR_ACTIVE + OR_TOPK];
+        ++U;
+    }
+    unsigned blocks[OR_BLOCKS], S = 0;
+    for (unsigned b = 0; b < OR_BLOCKS; ++b) if (m->layer[b]) blocks[S++] = b;
+
+    /* Activations: int8 per 64-group scale, per-32 sums. */
+    static int8_t q[OR_MAX_TOKENS][8192];
+    static float scale[OR_MAX_TOKENS][128];
+    static int32_t sums[OR_MAX_TOKENS][256];
+    qx xs[OR_MAX_TOKENS];
+    for (unsigned t = 0; t < tokens; ++t) {
+        rc = or_q8_quantize(x + (size_t)t * d, d, q[t], scale[t]);
+        if (rc) return rc;
+        for (unsigned k = 0; k < d / 32; ++k) {
+            int32_t s = 0;
+            for (unsigned j = 0; j < 32; ++j) s += q[t][32 * k + j];
+            sums[t][k] = s;
+        }
+        xs[t] = (qx){d, q[t], scale[t], sums[t]};
+    }
+
+    size_t need = (size_t)U * S * tokens * OR_NEURONS;
+    if (h_count) *h_count = need;
+    if (h && h_cap < need) return OR_INVALID;
+    if (h) memset(h, 0, need * sizeof(float));
+
+    /* part[u][t][r]: expert u's down-projection partial for token t. */
+    float *part = calloc((size_t)U * tokens * d, sizeof(float));
+    if (!part) return OR_INVALID;
+    const size_t slice = or_slice_bytes(d, m->gate_type, m->down_type);
+    for (unsigned u = 0; u < U; ++u) {
+        const int shared = uid[u] == OR_SHARED;
+        const unsigned in = shared ? OR_Q8_0 : m->gate_type, down = shared ? OR_Q8_0 : m->down_type;
+        const size_t in_row = or_row_bytes(in, d), proj = shared ? (size_t)d * 34 : OR_NEURONS * in_row;
+        /* Every referenced block is checked, whatever the gate (src/backend.h:58-59). */
+        for (unsigned si = 0; si < S; ++si) {
+            const uint8_t *p = m->layer[blocks[si]] + (size_t)uid[u] * slice;
+            for (unsigned r = 0; r < d; ++r) {
+                float s;
+                if (!block_scale(p + 2 * proj, down, r, &s)) { rc = OR_NUMERIC; goto done; }
+            }
+        }
+        for (unsigned t = 0; t < tokens; ++t) {
+            if (!(umask[u] >> t & 1)) continue;
+            static int8_t hv[OR_BLOCKS][OR_NEURONS];
+            float gs[OR_BLOCKS];
+            for (unsigned si = 0; si < S; ++si) {
+                const uint8_t *p = m->layer[blocks[si]] + (size_t)uid[u] * slice;
+                float hs[OR_NEURONS], hsc;
+                for (unsigned n = 0; n < OR_NEURONS; ++n) {
+                    float a, uu;
+                    rc = lane_dot(p + n * in_row, in, &xs[t], &a);
+                    if (rc) goto done;
+                    rc = lane_dot(p + proj + n * in_row, in, &xs[t], &uu);
+                    if (rc) goto done;
+                    if (!isfinite(a) || !isfinite(uu)) { rc = OR_NUMERIC; goto done; }
+                    double sig = a >= 0 ? 1 / (1 + exp(-(double)a)) : exp((double)a) / (1 + exp((double)a));
+                    if (narrow((double)a * sig * uu, &hs[n])) { rc = OR_NUMERIC; goto done; }
+                }
+                if (h) memcpy(h + (((size_t)u * S + si) * tokens + t) * OR_NEURONS, hs, sizeof hs);
+                rc = or_q8_quantize(hs, OR_NEURONS, hv[si], &hsc);
+                if (rc) goto done;
+                gs[si] = hsc * ugate[u][t];
+            }
+            for (unsigned r = 0; r < d; ++r) {
+                float split[PORT_SPLIT] = {0};
+                for (unsigned si = 0; si < S; ++si) {
+                    const uint8_t *p = m->layer[blocks[si]] + (size_t)uid[u] * slice;
+                    float c;
+                    if (!down_term(p + 2 * proj, down, r, hv[si], &c)) { rc = OR_NUMERIC; goto done; }
+                    split[si % PORT_SPLIT] = fmaf(c, gs[si], split[si % PORT_SPLIT]);
+                }
+                float sum = split[0];
+                for (unsigned k = 1; k < PORT_SPLIT; ++k) sum = sum + split[k];
+                part[((size_t)u * tokens + t) * d + r] = sum;
+            }
+        }
+    }
+    /* Each token sums its routed experts in its own request order, then the
+     * shared expert, so its result does not depend on the rest of the burst. */
+    static float out[OR_MAX_TOKENS * 8192];
+    for (unsigned t = 0; t < tokens; ++t)
+        for (unsigned r = 0; r < d; ++r) {
+            float acc = 0;
+            for (unsigned e = 0; e < OR_TOPK; ++e) {
+                unsigned u = 0;
+                while (uid[u] != expert[t * OR_TOPK + e]) ++u;
+                acc = acc + part[((size_t)u * tokens + t) * d + r];
+            }
+            if (shared_mask >> t & 1) acc = acc + part[((size_t)(U - 1) * tokens + t) * d + r];
+            if (!isfinite(acc)) { rc = OR_NUMERIC; goto done; }
+            out[(size_t)t * d + r] = acc;
+        }
+    memcpy(y, out, (size_t)tokens * d * sizeof(float));
+done:
+    free(part);
+    return rc;
+}
+
+/* --------------------------------------------------------------- metrics */
+
+/* src/backend.c:74-92 */
+int or_compare(const float *ref, const float *actual, size_t n, double out[3]) {
+    if (!ref || !actual || !out || !n) return OR_INVALID;
+    double r2 = 0, a2 = 0, d2 = 0, dot = 0, rmax = 0, dmax = 0;
+    for (size_t i = 0; i < n; ++i) {
+        double r = ref[i], a = actual[i], df = a - r;
+        if (!isfinite(r) || !isfinite(a)) return OR_NUMERIC;
+        r2 += r * r; a2 += a * a; d2 += df * df; dot += r * a;
+        if (fabs(r) > rmax) rmax = fabs(r);
+        if (fabs(df) > dmax) dmax = fabs(df);
+    }
+    if (!r2) {
+        out[0] = a2 ? INFINITY : 0; out[1] = a2 ? INFINITY : 0; out[2] = a2 ? 0 : 1;
+    } else {
+        out[0] = sqrt(d2 / r2); out[1] = dmax / rmax;
+        out[2] = a2 ? dot / (sqrt(r2) * sqrt(a2)) : 0;
+        if (out[2] > 1) out[2] = 1;
+        if (out[2] < -1) out[2] = -1;
+    }
+    return OR_OK;
+}
