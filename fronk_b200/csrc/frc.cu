@@ -248,18 +248,30 @@ __global__ void __launch_bounds__(kThreads) layer_kernel(const LayerArgs a) {
 
   // ---- unit loop, double buffered
   unsigned ph0 = 0, ph1 = 0, st = 0, iter = 0;
+  bool inflight[2] = {k < pl.total, false};  // a copy issued into the stage and not yet waited for
   while (k < pl.total) {
     if (tid == 0) {
-      const unsigned k2 = atomicAdd(&a.ctl->next, 1u);
+      const unsigned k2 = ld_acquire(&a.ctl->abort) ? 0xffffffffu : atomicAdd(&a.ctl->next, 1u);
       misc[(iter + 1) & 1] = k2;
       if (k2 < pl.total) {
         fence_proxy_async();
         issue(k2, st ^ 1);
       }
     }
+    __syncthreads();
+    inflight[st ^ 1] = misc[(iter + 1) & 1] < pl.total;
     const bool ok = mbar_wait(&bar[st], st ? ph1 : ph0);
-    if (st) ph1 ^= 1; else ph0 ^= 1;
-    if (!ok && tid == 0) atomicOr(a.status, kStTimeout);
+    if (ok) {  // on a timeout the copy may still land: keep the parity, drain before leaving
+      if (st) ph1 ^= 1; else ph0 ^= 1;
+      inflight[st] = false;
+    }
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) {
+        atomicOr(a.status, kStTimeout);
+        atomicExch(&a.ctl->abort, 1u);
+      }
+      break;
+    }
     uint8_t* stage = stage0 + st * a.sm.stage_bytes;
 
     if (k < pl.nGU) {
@@ -331,8 +343,13 @@ __global__ void __launch_bounds__(kThreads) layer_kernel(const LayerArgs a) {
       const bool shared = s_uid[u] == 512;
       const unsigned down = shared ? kQ80 : a.down_type;
       const unsigned mask = s_umask[u], cnt = __popc(mask);
-      if (tid == 0 && !spin_geq(&a.ctl->gu_done[u], S * kGuUnits)) atomicOr(a.status, kStTimeout);
-      __syncthreads();
+      bool waited = true;
+      if (tid == 0 && !spin_geq(&a.ctl->gu_done[u], S * kGuUnits, &a.ctl->abort)) {
+        waited = false;
+        atomicOr(a.status, kStTimeout);
+        atomicExch(&a.ctl->abort, 1u);
+      }
+      if (__syncthreads_or(!waited)) break;
       // hidden slices of this expert -> int8 (Q8) or fp32 (F32), [si][k][32]
       for (unsigned idx = warp; idx < S * cnt; idx += kWarps) {
         const unsigned si = idx / cnt, kk = idx % cnt;
@@ -490,7 +507,10 @@ __global__ void __launch_bounds__(kThreads) layer_kernel(const LayerArgs a) {
     ++iter;
   }
 
-  // ---- leave: the last CTA out restores the counters for the next launch
+  // ---- leave: no bulk copy may still be writing this CTA's shared memory
+  for (unsigned b2 = 0; b2 < 2; ++b2)
+    if (inflight[b2] && !mbar_wait(&bar[b2], b2 ? ph1 : ph0) && tid == 0) atomicOr(a.status, kStTimeout);
+  // ---- the last CTA out restores the counters for the next launch
   __syncthreads();
   if (tid == 0) misc[3] = atomicAdd(&a.ctl->exited, 1u) == gridDim.x - 1;
   __syncthreads();
@@ -501,6 +521,7 @@ __global__ void __launch_bounds__(kThreads) layer_kernel(const LayerArgs a) {
     if (tid == 0) {
       a.ctl->next = 0;
       a.ctl->exited = 0;
+      a.ctl->abort = 0;
     }
   }
 }

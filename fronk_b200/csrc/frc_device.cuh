@@ -28,7 +28,8 @@ enum : unsigned { kStNumeric = 1, kStInvalid = 2, kStTimeout = 4 };
 struct Ctl {
   unsigned next;
   unsigned exited;
-  unsigned pad[2];
+  unsigned abort;      // set by a CTA whose bounded wait ran out; every spin bails
+  unsigned pad;
   unsigned gu_done[kMaxUnique + 3];
   unsigned chunk_done[kMaxChunks];
 };
@@ -116,11 +117,12 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ bool spin_geq(const unsigned* p, unsigned target) {
+// Waits until *p >= target; gives up after kWaitNs or once *abort is set.
+__device__ __forceinline__ bool spin_geq(const unsigned* p, unsigned target, const unsigned* abort) {
   if (ld_acquire(p) >= target) return true;
   const uint64_t start = globaltimer();
   while (ld_acquire(p) < target) {
-    if (globaltimer() - start > kWaitNs) return false;
+    if (globaltimer() - start > kWaitNs || ld_acquire(abort)) return false;
     __nanosleep(64);
   }
   return true;
@@ -307,7 +309,7 @@ __device__ __forceinline__ float e2m1(unsigned nib) {
   float v = 0.0f;
 #pragma unroll
   for (unsigned i = 0; i < 8; ++i) v = (nib & 7) == i ? mag[i] : v;
-  return nib & 8 ? -v : v;
+  return nib & 8 && v != 0.0f ? -v : v;  // nibble 8 is +0 in the reference table (src/native.c:10)
 }
 __device__ __forceinline__ float weight_mxfp4(const uint8_t* row, unsigned nb, unsigned j) {
   const unsigned blk = j / 32, n = j % 32, e = row[blk];
