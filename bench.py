@@ -1,0 +1,476 @@
+"""Decode benchmark of the B200 expert-slice backend (one JSON line on rank 0).
+
+Workload: a full decode pass of 48 MoE layers for one
+token, hidden 2048, 512 experts with seeded top-10 routing per layer (fresh
+every step), Q4_K gate/up and MXFP4 down (the reference's routed layout), all
+20 neuron slices split over the N GPUs the way the reference planner splits
+them over nodes, and a sum of the partials after every layer (NCCL all-reduce
+over NVLink; none at N=1).  Layer l+1 depends on layer l: its input is the
+pre-normed residual stream h_{l+1} = h_l + y_l, so layers serialize as in
+real decode.  A step = one token through all 48 layers; value = tokens/s of
+the whole job (every GPU works on the same token: strong scaling).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE decode tokens/s at 1/2/4/8 B200; expert-weight GB/s vs HBM peak"
+HIDDEN, LAYERS, SLICES, TOPK = 2048, 48, 20, 10
+SEED = 0x5EED
+POOL = 64
+SLICE_BYTES = 2 * 32 * (HIDDEN // 256) * 144 + HIDDEN * 17     # 108,544 (Q4_K gate/up + MXFP4 down)
+WORKLOAD = ("decode48 (BASELINE configs[2]): 48 MoE layers, 1 token, d=2048, 512 experts top-10, "
+            "Q4_K gate/up + MXFP4 down, 20 slices split over the GPUs, partial sum after every layer")
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback 6.65 TB/s (MEASURED_PEAKS.json absent)"
+
+
+def step_routing(steps):
+    """Routing and gates for every (step, layer) and the token's x0 per step:
+    the same seeds the CPU baseline harness uses (oracle/ref_bench.c)."""
+    import fronk_b200 as fb
+    ex = np.zeros((steps, LAYERS, TOPK), np.uint16)
+    gt = np.zeros((steps, LAYERS, 11), np.float32)
+    x0 = np.zeros((steps, HIDDEN), np.float32)
+    for s in range(steps):
+        for l in range(LAYERS):
+            e, g, x = fb.synth_request(HIDDEN, 1, fb.rand64(SEED, 1000003 * s + l))
+            ex[s, l], gt[s, l] = e[0], g[0]
+            if l == 0:
+                x0[s] = x[0]
+    return ex, gt, x0
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device, self.rows, self.proc = device, [], None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), "--query-gpu=" + self.Q,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm, mx, util = float(r[1]), float(r[2]), float(r[4])
+            except (ValueError, IndexError):
+                continue
+            maxes.append(mx)
+            if util > 0:
+                sms.append(sm)
+            for n, v in zip(names, r[6:10]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            sms = [float(r[1]) for r in self.rows if len(r) > 1 and r[1].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxes) if maxes else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------ CPU baseline
+
+def cpu_baseline(steps, warmup):
+    """The reference's own AVX2 backend (compiled from its sources into
+    oracle/_ref) on the same seeded workload, all host threads it tunes to."""
+    exe = os.path.join(ROOT, "oracle", "_ref", "ref_bench_2048")
+    if not os.path.exists(exe):
+        return {"unavailable": "reference not compiled (oracle/_ref/ref_bench_2048 missing)"}
+    t0 = time.time()
+    out = subprocess.run([exe, "avx2", str(SLICES), str(POOL), str(steps), str(warmup), str(SEED)],
+                         capture_output=True, text=True, timeout=1800)
+    if out.returncode:
+        return {"unavailable": "ref_bench failed: " + out.stderr.strip()[-200:]}
+    r = json.loads(out.stdout.strip().splitlines()[-1])
+    tok_s = 1e9 / r["ns_per_pass_mean"]
+    return {"value": tok_s, "unit": "tokens/s", "cores": r["workers"], "kind": "reference",
+            "sample": "reference backends/avx2.c (fr_avx2.run), full workload: all 20 slices resident in sparse "
+                      "host units, %d timed 48-layer passes after %d warm-up, d=2048 build" % (steps, warmup),
+            "host": {"cpu": r["cpu"], "cores": r["cores"], "logical_cores": r["logical_cores"]},
+            "ms_per_pass": r["ns_per_pass_mean"] / 1e6, "wall_s": round(time.time() - t0, 1)}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    steps = max(1, min(args.steps, 50))
+    warm = max(1, min(args.warmup, 3))
+    cb = cpu_baseline(steps, warm)
+    if "unavailable" in cb:
+        print(json.dumps({"impl": "reference", "unavailable": cb["unavailable"]}), flush=True)
+        return
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": steps, "warmup": warm, "ms_per_step": cb["ms_per_pass"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic", "config": config(args.gpus),
+            "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config(n):
+    from fronk_b200.planner import equal_shares
+    return {"workload": WORKLOAD, "hidden": HIDDEN, "layers": LAYERS, "tokens_per_step": 1, "experts": 512,
+            "top_k": TOPK, "slices": SLICES, "shares": equal_shares(n), "formats": "Q4_K gate/up, MXFP4 down",
+            "activations": "Q8 per 64 (src/q4.c scheme), fp32 accumulate",
+            "weight_bytes_per_token": LAYERS * TOPK * SLICES * SLICE_BYTES,
+            "l2": "inputs larger than L2: 1.04 GB of expert weights per step, fresh routing every step",
+            "parallelism": "slice-split x%d + all-reduce per layer" % n if n > 1 else "1 GPU, all slices"}
+
+
+# ------------------------------------------------------------------- ours
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="small case for ncu: 2 layers of every slice loaded (2.2 GB), 5 layer launches")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if args.profile:
+        profile_case()
+        return
+    args.warmup = max(args.warmup, 3)
+
+    import torch
+    import fronk_b200 as fb
+    from fronk_b200.planner import owned_blocks
+    from fronk_b200 import build as fbuild
+    fbuild.build()
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    blocks = owned_blocks(rank, world)
+    g = fb.geometry(HIDDEN)
+    ctx = fb.Context(local, HIDDEN)
+
+    # units: a pool of distinct synthetic slices, copied on the device into every slot
+    t0 = time.time()
+    pool = np.concatenate([fb.synth_slice(g, SEED, i) for i in range(POOL)])
+    ctx.pool_load(pool, fb.synth_shared(g, SEED, 1 << 20))
+    for b in blocks:
+        for l in range(LAYERS):
+            ctx.fill_layer(b, l, SEED)
+    log("rank %d: blocks %s filled in %.1fs" % (rank, blocks, time.time() - t0))
+
+    total = args.warmup + args.steps
+    ex, gt, x0 = step_routing(total)
+    d_ex = torch.from_numpy(ex.astype(np.int16)).to(dev)          # ids < 512: int16 holds the u16 bits
+    d_gt = torch.from_numpy(gt).to(dev)
+    d_x0 = torch.from_numpy(x0).to(dev)
+    cur_ex = torch.empty((LAYERS, TOPK), dtype=torch.int16, device=dev)
+    cur_gt = torch.empty((LAYERS, 11), dtype=torch.float32, device=dev)
+    X0 = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
+    H = [torch.zeros(HIDDEN, dtype=torch.float32, device=dev) for _ in range(2)]
+    Y = [torch.zeros(HIDDEN, dtype=torch.float32, device=dev) for _ in range(2)]
+
+    def p(t):
+        return t.data_ptr()
+
+    def one_pass(stream):
+        s = stream.cuda_stream
+        for l in range(LAYERS):
+            x = X0 if l <= 1 else H[(l - 1) % 2]
+            x_add = None if l == 0 else p(Y[(l - 1) % 2])
+            x_out = None if l == 0 else p(H[l % 2])
+            ctx.run_device(l, 1, p(cur_ex[l]), p(cur_gt[l]), p(x), x_add, x_out, p(Y[l % 2]), fb.ACT_Q8,
+                           fb.RUN_RMSNORM, s)
+            if dist is not None:
+                dist.all_reduce(Y[l % 2])
+
+    def load_step(s):
+        cur_ex.copy_(d_ex[s], non_blocking=True)
+        cur_gt.copy_(d_gt[s], non_blocking=True)
+        X0.copy_(d_x0[s], non_blocking=True)
+
+    stream = torch.cuda.current_stream()
+    # capture one pass in a CUDA graph (launch-bound inner loop); eager if capture fails
+    graph = None
+    try:
+        load_step(0)
+        one_pass(stream)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            one_pass(torch.cuda.current_stream())
+    except Exception as exc:  # noqa: BLE001
+        log("graph capture failed, running eagerly:", exc)
+        graph = None
+    rc = ctx.status(stream.cuda_stream)
+    if rc:
+        raise fb.FrcError(rc, "warm-up pass", ctx.last_error)
+
+    def step(s):
+        load_step(s)
+        if graph is not None:
+            graph.replay()
+        else:
+            one_pass(stream)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for s in range(args.warmup, total):
+        step(s)
+    end.record(stream)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = start.elapsed_time(end)
+    rc = ctx.status(stream.cuda_stream)
+    if rc:
+        raise fb.FrcError(rc, "timed passes", ctx.last_error)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    tokens_s = 1000.0 / ms_per_step
+    launches = LAYERS * args.steps
+
+    # ---- kernel alone: event-bracketed launches on the launching stream
+    kt = []
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(LAYERS)]
+    for s in range(min(total, 8)):
+        load_step(s)
+        for l in range(LAYERS):
+            ev[l][0].record(stream)
+            ctx.run_device(l, 1, p(cur_ex[l]), p(cur_gt[l]), p(X0), None, None, p(Y[0]), fb.ACT_Q8,
+                           fb.RUN_RMSNORM, stream.cuda_stream)
+            ev[l][1].record(stream)
+        torch.cuda.synchronize()
+        kt += [a.elapsed_time(b) for a, b in ev]
+    kernel_ms = statistics.mean(kt)
+    bytes_per_launch = TOPK * len(blocks) * SLICE_BYTES
+    peak, peak_src = peaks()
+    achieved = bytes_per_launch / (kernel_ms * 1e-3) / 1e9
+    in_pass = bytes_per_launch * LAYERS / (ms_per_step * 1e-3) / 1e9
+
+    # ---- end to end through the C ABI with host buffers (reference-facing call)
+    e2e_steps = max(3, min(args.steps, 50))
+    e2e = e2e_run(ctx, fb, ex, gt, x0, e2e_steps, dist, dev)
+
+    # ---- parity at full size: one layer of the filled units vs the oracle
+    parity = full_size_parity(ctx, fb, g, pool, blocks)
+
+    used_graph = graph is not None
+    del graph
+    if rank == 0:
+        weight_bytes = LAYERS * TOPK * SLICES * SLICE_BYTES
+        line = {
+            "metric": METRIC, "value": tokens_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config(world),
+            "weight_gbs": weight_bytes * tokens_s / 1e9,
+            "weight_frac_of_peak": weight_bytes * tokens_s / 1e9 / peak,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": ncu_traffic(), "peak_source": peak_src,
+                         "kernel": "layer_kernel<Q8,1> (one launch per layer)",
+                         "algorithmic_bytes_per_launch": bytes_per_launch, "kernel_us": kernel_ms * 1e3,
+                         "in_pass_gbs": in_pass, "in_pass_frac": in_pass / peak},
+            "gpu_launches": launches, "graph": used_graph, "clocks": clocks, "e2e": e2e, "parity": parity,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(3, 1)
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev):
+    """tokens/s through the public call with host buffers: per layer the
+    request is copied in, the layer runs, y is copied out (frc_run; at N>1
+    the device entry point plus the all-reduce)."""
+    import torch
+    h2d = LAYERS * (HIDDEN * 4 + TOPK * 2 + 11 * 4)
+    d2h = LAYERS * HIDDEN * 4
+    if dist is None:
+        t0 = time.perf_counter()
+        for s in range(steps):
+            h = x0[s].copy()
+            for l in range(LAYERS):
+                x = (h / np.sqrt(np.mean(h * h) + np.float32(1e-6))).astype(np.float32)
+                rc, y = ctx.run(l, ex[s, l][None], gt[s, l][None], x[None], fb.ACT_Q8)
+                if rc:
+                    raise fb.FrcError(rc, "e2e", ctx.last_error)
+                h = h + y[0]
+        dt = time.perf_counter() - t0
+    else:
+        pin_x = torch.empty(HIDDEN, dtype=torch.float32).pin_memory()
+        pin_e = torch.empty(TOPK, dtype=torch.int16).pin_memory()
+        pin_g = torch.empty(11, dtype=torch.float32).pin_memory()
+        pin_y = torch.empty(HIDDEN, dtype=torch.float32).pin_memory()
+        dx, de, dg = torch.empty(HIDDEN, device=dev), torch.empty(TOPK, dtype=torch.int16, device=dev), \
+            torch.empty(11, device=dev)
+        dy = torch.empty(HIDDEN, device=dev)
+        st = torch.cuda.current_stream()
+        dist.barrier()
+        t0 = time.perf_counter()
+        for s in range(steps):
+            h = x0[s].copy()
+            for l in range(LAYERS):
+                x = (h / np.sqrt(np.mean(h * h) + np.float32(1e-6))).astype(np.float32)
+                pin_x.numpy()[:] = x
+                pin_e.numpy()[:] = ex[s, l].astype(np.int16)
+                pin_g.numpy()[:] = gt[s, l]
+                dx.copy_(pin_x, non_blocking=True)
+                de.copy_(pin_e, non_blocking=True)
+                dg.copy_(pin_g, non_blocking=True)
+                ctx.run_device(l, 1, de.data_ptr(), dg.data_ptr(), dx.data_ptr(), None, None, dy.data_ptr(),
+                               fb.ACT_Q8, 0, st.cuda_stream)
+                dist.all_reduce(dy)
+                pin_y.copy_(dy, non_blocking=True)
+                st.synchronize()
+                h = h + pin_y.numpy()
+        dt = time.perf_counter() - t0
+        t = torch.tensor([dt], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    rc = ctx.status(None)
+    if rc:
+        raise fb.FrcError(rc, "e2e", ctx.last_error)
+    return {"value": steps / dt, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": steps, "api": "frc_run (host buffers, synchronous per layer)" if dist is None else
+            "frc_run_device + NCCL all_reduce, pinned host copies each layer"}
+
+
+def full_size_parity(ctx, fb, g, pool, blocks):
+    """Layer 5 of the filled units on a fresh request, against the oracle's
+    restatement of the same arithmetic on the host copies of the same slices."""
+    try:
+        from oracle import Oracle, Q4_K, MXFP4
+    except Exception as exc:  # noqa: BLE001
+        return {"skipped": str(exc)}
+    orc = Oracle()
+    e, gate, x = fb.synth_request(HIDDEN, 2, 777)
+    rc, y = ctx.run(5, e, gate, x, fb.ACT_Q8)
+    if rc:
+        return {"error": ctx.last_error}
+    h = ctx.debug_hidden()
+    sb, lb = fb.slice_bytes(g), fb.layer_bytes(g)
+    layers = {}
+    for b in blocks:
+        arr = np.zeros(lb, np.uint8)
+        for ident in set(int(v) for v in e.ravel()):
+            k = fb.pool_pick(SEED, b, 5, ident, POOL)
+            arr[ident * sb:(ident + 1) * sb] = pool[k * sb:(k + 1) * sb]
+        layers[b] = arr
+    rc, y_ref, h_ref = orc.port_run(orc.model(HIDDEN, Q4_K, MXFP4, layers), e, gate, x, want_hidden=True)
+    rel = max(float(np.sqrt(((y_ref[t] - y[t]) ** 2).sum() / (y_ref[t] ** 2).sum())) for t in range(2))
+    return {"layer": 5, "tokens": 2, "blocks": len(blocks), "hidden_bitexact": bool(np.array_equal(
+        h.view(np.uint32), h_ref.view(np.uint32))), "max_rel_l2": rel}
+
+
+def profile_case():
+    """The layer kernel alone on a small device footprint: layers 0 and 1 of
+    all 20 slices (2.2 GB), 5 launches with fresh routing (2 warm-up + 3)."""
+    import torch
+    import fronk_b200 as fb
+    g = fb.geometry(HIDDEN)
+    ctx = fb.Context(0, HIDDEN)
+    pool = np.concatenate([fb.synth_slice(g, SEED, i) for i in range(POOL)])
+    ctx.pool_load(pool, fb.synth_shared(g, SEED, 1 << 20))
+    for b in range(SLICES):
+        for l in range(2):
+            ctx.fill_layer(b, l, SEED)
+    ex, gt, x0 = step_routing(5)
+    dev = torch.device("cuda", 0)
+    x = torch.from_numpy(x0).to(dev)
+    y = torch.zeros(HIDDEN, device=dev)
+    e = torch.from_numpy(ex.astype(np.int16)).to(dev)
+    gg = torch.from_numpy(gt).to(dev)
+    s = torch.cuda.current_stream().cuda_stream
+    for i in range(5):
+        ctx.run_device(i % 2, 1, e[i, i % 2].data_ptr(), gg[i, i % 2].data_ptr(), x[i].data_ptr(), None, None,
+                       y.data_ptr(), fb.ACT_Q8, fb.RUN_RMSNORM, s)
+    rc = ctx.status(s)
+    if rc:
+        raise fb.FrcError(rc, "profile case", ctx.last_error)
+    ctx.close()
+    print("profile case ok")
+
+
+def ncu_traffic():
+    """DRAM bytes per launch of the layer kernel from the committed ncu summary, if any."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "layer_kernel_decode48.json")) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    except (OSError, ValueError):
+        return None
+
+
+if __name__ == "__main__":
+    main()

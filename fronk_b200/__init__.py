@@ -10,7 +10,8 @@ import os
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libfronk_b200.so")
+# FRONK_B200_LIB selects another build (e.g. libfronk_b200_phases.so).
+LIB_PATH = os.environ.get("FRONK_B200_LIB") or os.path.join(HERE, "libfronk_b200.so")
 
 # src/backend.h:17-18
 OK, INVALID, STATE, NUMERIC, IO, UNSUPPORTED, MISMATCH = 0, -1, -2, -3, -4, -5, -6
@@ -77,6 +78,7 @@ _SIGS = {
     "frc_debug_decode": (_int, [_vp, _u32, _vp, _u32, _u32, _vp]),
     "frc_debug_quantize": (_int, [_vp, _u32, _vp, _vp, _vp, _vp]),
     "frc_debug_hidden": (_int, [_vp, _vp, _sz, _vp]),
+    "frc_debug_phases": (_int, [_vp, _vp, _sz, _vp]),
 }
 EXPORTS = sorted(_SIGS) + ["fr_cuda", "fr_cuda_f32", "fr_cuda_select_device", "fr_cuda_close"]
 
@@ -282,6 +284,16 @@ class Context:
         self._check(self.lib.frc_debug_quantize(self.h, tokens, _ptr(x), _ptr(q), _ptr(s), _ptr(deq)),
                     "debug_quantize")
         return q, s, deq
+
+    def debug_phases(self):
+        """[cta][16] globaltimer stamps of the last launch (FRC_PHASES builds)."""
+        n = ctypes.c_size_t()
+        rc = self.lib.frc_debug_phases(self.h, None, 0, ctypes.byref(n))
+        if rc:
+            raise FrcError(rc, "debug_phases", self.last_error)
+        out = np.zeros(n.value, np.uint64)
+        self._check(self.lib.frc_debug_phases(self.h, _ptr(out), n.value, ctypes.byref(n)), "debug_phases")
+        return out.reshape(-1, 16)
 
     def debug_hidden(self):
         n = ctypes.c_size_t()

@@ -9,12 +9,13 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libfronk_b200.so")
+PHASES_LIB = os.path.join(HERE, "libfronk_b200_phases.so")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_SOURCES = ["frc.cu"]
 C_SOURCES = ["frc_synth.c", "fr_cuda_backend.c"]
-DEPS = CUDA_SOURCES + C_SOURCES + ["frc_device.cuh"]
+DEPS = CUDA_SOURCES + C_SOURCES + ["frc_device.cuh", "frc_layer.cuh"]
 
 
 def _run(cmd):
@@ -33,18 +34,21 @@ def _stale(target, sources):
     return any(os.path.getmtime(s) > t for s in sources + headers)
 
 
-def build(force=False, verbose=False):
-    """Compile when a source is newer than the library; returns its path."""
+def build(force=False, verbose=False, phases=False):
+    """Compile when a source is newer than the library; returns its path.
+    phases=True builds the FRC_PHASES variant (per-CTA phase stamps)."""
+    lib = PHASES_LIB if phases else LIB
     sources = [os.path.join(CSRC, s) for s in DEPS]
-    if not force and not _stale(LIB, sources):
-        return LIB
+    if not force and not _stale(lib, sources):
+        return lib
     os.makedirs(OUT, exist_ok=True)
     objs = []
+    tag = "_phases" if phases else ""
     for s in CUDA_SOURCES:
-        o = os.path.join(OUT, s + ".o")
+        o = os.path.join(OUT, s + tag + ".o")
         log = _run([NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xptxas", "-v",
-                    "-c", os.path.join(CSRC, s), "-o", o])
-        with open(os.path.join(OUT, s + ".ptxas.txt"), "w") as f:
+                    *(["-DFRC_PHASES"] if phases else []), "-c", os.path.join(CSRC, s), "-o", o])
+        with open(os.path.join(OUT, s + tag + ".ptxas.txt"), "w") as f:
             f.write(log)
         if verbose:
             print(log)
@@ -54,11 +58,11 @@ def build(force=False, verbose=False):
         _run(["gcc", "-O2", "-std=c11", "-fPIC", "-Wall", "-Wextra", "-ffp-contract=off", "-c",
               os.path.join(CSRC, s), "-o", o])
         objs.append(o)
-    tmp = LIB + ".tmp"
+    tmp = lib + ".tmp"
     _run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-ldl", "-lm"])
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv, phases="--phases" in sys.argv))

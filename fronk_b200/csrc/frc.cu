@@ -1,17 +1,9 @@
-// frc.cu - B200 (sm_100a) expert neuron-slice kernels and the C ABI around them.
-//
-// One launch computes one MoE layer (the work of fr_backend.run,
-// backends/ref.c:57-98) as a queue of units drawn by every CTA:
-//   gate/up unit (item, 8 neurons): 8 gate + 8 up rows of one (expert, slice)
-//     item, TMA-staged in shared memory, integer block dots against the
-//     token's int8 activations, SwiGLU -> hidden[item][token][neuron];
-//   down unit (expert, 64 rows): waits until all gate/up units of the expert
-//     are done, quantizes the expert's hidden slices, forms the 64 down rows of
-//     every slice and writes the expert's partial; the last down unit of a row
-//     chunk sums all experts' partials in a fixed order into y.
-// Gate/up units come first in the queue, so a waiting down unit never blocks
-// the work it waits for; the queue makes the launch deadlock free for any
-// grid size.  No float atomics: results are bitwise repeatable.
+// frc.cu - B200 (sm_100a) expert neuron-slice backend: set-up kernels, the
+// host runtime and the C ABI (include/fronk_b200.h).  The MoE layer kernel
+// itself is in frc_layer.cuh: one cooperative launch per layer, static work
+// split, every CTA's weight bytes requested up front through a TMA ring,
+// integer block dots, a fixed reduction order and no float atomics (results
+// are bitwise repeatable).
 #include <cuda_runtime.h>
 #include <fenv.h>
 #include <math.h>
@@ -25,506 +17,7 @@
 
 using namespace frc;
 
-// ============================================================ layer kernel
-
-struct Plan {  // per-CTA view of the layer's unique experts
-  unsigned U, nGU, nDN, total, nch;
-};
-
-template <int ACT, int MAXT>
-__global__ void __launch_bounds__(kThreads) layer_kernel(const LayerArgs a) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-  unsigned* misc = reinterpret_cast<unsigned*>(smem + 16);  // [0..1] next, [2] last, [3] reset, [4] U
-  uint16_t* s_ids = reinterpret_cast<uint16_t*>(smem + a.sm.ids);
-  float* s_g = reinterpret_cast<float*>(smem + a.sm.gates);
-  int* s_first = reinterpret_cast<int*>(smem + a.sm.first);
-  uint16_t* s_uid = reinterpret_cast<uint16_t*>(smem + a.sm.uid);
-  unsigned* s_umask = reinterpret_cast<unsigned*>(smem + a.sm.umask);
-  float* s_ugate = reinterpret_cast<float*>(smem + a.sm.ugate);
-  uint8_t* stage0 = smem + a.sm.stage;
-
-  const unsigned tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const unsigned T = a.T, S = a.S, d = a.d, P = d / 64;
-
-  if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
-    fence_mbar_init();
-  }
-  // ---- plan: unique experts in first-appearance order, then the shared one
-  for (unsigned i = tid; i < T * 10; i += kThreads) s_ids[i] = a.expert[i];
-  for (unsigned i = tid; i < T * 11; i += kThreads) s_g[i] = a.gate[i];
-  for (unsigned i = tid; i < 512; i += kThreads) s_first[i] = 0x7fffffff;
-  for (unsigned i = tid; i < kMaxUnique; i += kThreads) s_umask[i] = 0;
-  for (unsigned i = tid; i < kMaxUnique * T; i += kThreads) s_ugate[i] = 0.0f;
-  __syncthreads();
-  bool invalid = false;
-  for (unsigned i = tid; i < T * 10; i += kThreads) {
-    const unsigned id = s_ids[i];
-    if (id < 512) atomicMin(&s_first[id], static_cast<int>(i));
-    else invalid = true;
-  }
-  if (invalid) atomicOr(a.status, kStInvalid);
-  __syncthreads();
-  {
-    // rank of each first occurrence; T*10 <= 160 < kThreads
-    const unsigned i = tid;
-    const bool first = i < T * 10 && s_ids[i] < 512 && s_first[s_ids[i]] == static_cast<int>(i);
-    const unsigned ballot = __ballot_sync(0xffffffffu, first);
-    unsigned* wcount = misc + 8;  // 8 words
-    if (lane == 0) wcount[warp] = __popc(ballot);
-    __syncthreads();
-    unsigned off = 0;
-    for (unsigned w = 0; w < warp; ++w) off += wcount[w];
-    const unsigned rank = off + __popc(ballot & ((1u << lane) - 1));
-    if (tid == kThreads - 1) misc[4] = off + __popc(ballot);  // routed unique count
-    __syncthreads();
-    if (first) {
-      s_uid[rank] = s_ids[i];
-      s_first[s_ids[i]] = -1 - static_cast<int>(rank);  // id -> rank
-    }
-    __syncthreads();
-  }
-  unsigned U = misc[4];
-  for (unsigned i = tid; i < T * 10; i += kThreads) {
-    const unsigned id = s_ids[i];
-    if (id >= 512) continue;
-    const unsigned u = static_cast<unsigned>(-1 - s_first[id]), t = i / 10;
-    atomicOr(&s_umask[u], 1u << t);
-    s_ugate[u * T + t] = s_g[t * 11 + i % 10];
-  }
-  __syncthreads();
-  {
-    unsigned shared_mask = 0;
-    for (unsigned t = 0; t < T; ++t)
-      if (s_g[t * 11 + 10] != 0.0f) shared_mask |= 1u << t;
-    if (shared_mask) {
-      if (tid == 0) {
-        s_uid[U] = 512;
-        s_umask[U] = shared_mask;
-      }
-      for (unsigned t = tid; t < T; t += kThreads) s_ugate[U * T + t] = s_g[t * 11 + 10];
-      ++U;
-    }
-  }
-  Plan pl;
-  pl.U = U;
-  pl.nch = d / kDnRows;
-  pl.nGU = U * S * kGuUnits;
-  pl.nDN = U * pl.nch;
-  pl.total = pl.nGU + pl.nDN;
-  __syncthreads();
-
-  // ---- stage issue: bulk copies of one unit's bytes into a stage buffer
-  auto issue = [&](unsigned k, unsigned st) {
-    uint8_t* dst = stage0 + st * a.sm.stage_bytes;
-    if (k < pl.nGU) {
-      const unsigned item = k / kGuUnits, ng = k % kGuUnits, u = item / S, si = item % S;
-      const bool shared = s_uid[u] == 512;
-      const unsigned rowb = shared ? a.shared_row : a.row_bytes, proj = shared ? a.shared_proj : a.proj_bytes;
-      const uint8_t* src = a.base[si] + static_cast<size_t>(s_uid[u]) * a.slice_bytes + ng * kGuNeurons * rowb;
-      const unsigned bytes = kGuNeurons * rowb;
-      mbar_expect_tx(&bar[st], 2 * bytes);
-      bulk_g2s(dst, src, bytes, &bar[st]);
-      bulk_g2s(dst + bytes, src + proj, bytes, &bar[st]);
-    } else {
-      const unsigned j = k - pl.nGU, u = j / pl.nch, c = j % pl.nch;
-      const bool shared = s_uid[u] == 512;
-      const unsigned proj = shared ? a.shared_proj : a.proj_bytes;
-      const bool mx = !shared && a.down_type == kMXFP4;
-      const unsigned hb = mx ? 1 : 2, pb = mx ? 16 : 32;  // scale / payload bytes per row
-      const unsigned ib = kDnRows * (hb + pb);
-      mbar_expect_tx(&bar[st], S * ib);
-      for (unsigned si = 0; si < S; ++si) {
-        const uint8_t* down = a.base[si] + static_cast<size_t>(s_uid[u]) * a.slice_bytes + 2 * proj;
-        bulk_g2s(dst + si * ib, down + c * kDnRows * hb, kDnRows * hb, &bar[st]);
-        bulk_g2s(dst + si * ib + kDnRows * hb, down + d * hb + c * kDnRows * pb, kDnRows * pb, &bar[st]);
-      }
-    }
-  };
-
-  if (tid == 0) {
-    const unsigned k0 = atomicAdd(&a.ctl->next, 1u);
-    misc[0] = k0;
-    if (k0 < pl.total) issue(k0, 0);
-  }
-  __syncthreads();
-  unsigned k = misc[0];
-
-  // ---- activations (CTAs that hold work; CTA 0 always, it owns x_out)
-  if (k < pl.total || blockIdx.x == 0) {
-    const unsigned per_token = d / 4, nvec = T * per_token;
-    const float4* x4 = reinterpret_cast<const float4*>(a.x);
-    const float4* xa4 = reinterpret_cast<const float4*>(a.x_add);
-    float* s_rms = reinterpret_cast<float*>(smem + a.sm.rms);
-    bool bad = false;
-    if (a.norm) {
-      // per-token 1/rms of v = x + x_add: thread partials, warp tree, warps in order
-      float* wsum = reinterpret_cast<float*>(misc + 16);  // 8 floats
-      for (unsigned t = 0; t < T; ++t) {
-        float ss = 0.0f;
-        for (unsigned f = t * per_token + tid; f < (t + 1) * per_token; f += kThreads) {
-          float4 v = x4[f];
-          if (xa4) {
-            const float4 w = xa4[f];
-            v.x = __fadd_rn(v.x, w.x); v.y = __fadd_rn(v.y, w.y); v.z = __fadd_rn(v.z, w.z); v.w = __fadd_rn(v.w, w.w);
-          }
-          ss = __fmaf_rn(v.x, v.x, ss); ss = __fmaf_rn(v.y, v.y, ss);
-          ss = __fmaf_rn(v.z, v.z, ss); ss = __fmaf_rn(v.w, v.w, ss);
-        }
-#pragma unroll
-        for (unsigned o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-        if (lane == 0) wsum[warp] = ss;
-        __syncthreads();
-        if (tid == 0) {
-          float tot = 0.0f;
-          for (unsigned w = 0; w < kWarps; ++w) tot = __fadd_rn(tot, wsum[w]);
-          s_rms[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(d)), 1e-6f)));
-        }
-        __syncthreads();
-      }
-    }
-    for (unsigned base = 0; base < nvec; base += kThreads * 4) {
-      float4 v[4];
-#pragma unroll
-      for (unsigned r = 0; r < 4; ++r) {
-        const unsigned f = base + r * kThreads + tid;
-        if (f < nvec) {
-          v[r] = x4[f];
-          if (xa4) {
-            const float4 w = xa4[f];
-            v[r].x = __fadd_rn(v[r].x, w.x); v[r].y = __fadd_rn(v[r].y, w.y);
-            v[r].z = __fadd_rn(v[r].z, w.z); v[r].w = __fadd_rn(v[r].w, w.w);
-          }
-        }
-      }
-#pragma unroll
-      for (unsigned r = 0; r < 4; ++r) {
-        const unsigned f = base + r * kThreads + tid;
-        if (f >= nvec) continue;  // warp-uniform: nvec is a multiple of 128
-        const unsigned t = f / per_token, j = f % per_token;  // element 4j of token t
-        bad |= !isfinite(v[r].x) || !isfinite(v[r].y) || !isfinite(v[r].z) || !isfinite(v[r].w);
-        if (a.x_out && blockIdx.x == 0) reinterpret_cast<float4*>(a.x_out)[f] = v[r];
-        if (a.norm) {
-          const float g = s_rms[t];
-          v[r].x = __fmul_rn(v[r].x, g); v[r].y = __fmul_rn(v[r].y, g);
-          v[r].z = __fmul_rn(v[r].z, g); v[r].w = __fmul_rn(v[r].w, g);
-        }
-        if (ACT == FRC_ACT_F32) {
-          reinterpret_cast<float4*>(smem + a.sm.xf)[f] = v[r];
-          continue;
-        }
-        // group of 64 = 16 consecutive float4 = one half-warp
-        float amax = fmaxf(fmaxf(fabsf(v[r].x), fabsf(v[r].y)), fmaxf(fabsf(v[r].z), fabsf(v[r].w)));
-#pragma unroll
-        for (unsigned o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        const float scale = __fdiv_rn(amax, 127.0f);
-        const int q0 = q8_value(v[r].x, amax, scale), q1 = q8_value(v[r].y, amax, scale);
-        const int q2 = q8_value(v[r].z, amax, scale), q3 = q8_value(v[r].w, amax, scale);
-        int sum = q0 + q1 + q2 + q3;
-#pragma unroll
-        for (unsigned o = 4; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        const unsigned p = j / 16, wq = j % 16;
-        uint8_t* xt = smem + a.sm.xq + t * d;
-        const uint32_t word = (q0 & 0xff) | (q1 & 0xff) << 8 | (q2 & 0xff) << 16 | static_cast<uint32_t>(q3 & 0xff) << 24;
-        *reinterpret_cast<uint32_t*>(xt + 16 * xslot(p, wq / 4) + 4 * (wq % 4)) = word;
-        if ((lane & 15) == 0) reinterpret_cast<float*>(smem + a.sm.xs)[t * P + p] = scale;
-        if ((lane & 7) == 0) reinterpret_cast<float*>(smem + a.sm.xv)[t * 2 * P + 2 * p + ((lane >> 3) & 1)] = static_cast<float>(sum);
-        if (a.sm.xp) {  // prmt order inside each 32-weight block
-          uint8_t* xp = smem + a.sm.xp + t * d;
-          const int qv[4] = {q0, q1, q2, q3};
-#pragma unroll
-          for (unsigned i = 0; i < 4; ++i) {
-            const unsigned e = 4 * j + i, wi = (e % 64) / 32 * 32 + prmt_pos(e % 32);  // byte index in group
-            xp[16 * xslot(p, wi / 16) + wi % 16] = static_cast<uint8_t>(qv[i] & 0xff);
-          }
-        }
-      }
-    }
-    if (bad) atomicOr(a.status, kStNumeric);
-  }
-  __syncthreads();
-
-  // ---- unit loop, double buffered
-  unsigned ph0 = 0, ph1 = 0, st = 0, iter = 0;
-  bool inflight[2] = {k < pl.total, false};  // a copy issued into the stage and not yet waited for
-  while (k < pl.total) {
-    if (tid == 0) {
-      const unsigned k2 = ld_acquire(&a.ctl->abort) ? 0xffffffffu : atomicAdd(&a.ctl->next, 1u);
-      misc[(iter + 1) & 1] = k2;
-      if (k2 < pl.total) {
-        fence_proxy_async();
-        issue(k2, st ^ 1);
-      }
-    }
-    __syncthreads();
-    inflight[st ^ 1] = misc[(iter + 1) & 1] < pl.total;
-    const bool ok = mbar_wait(&bar[st], st ? ph1 : ph0);
-    if (ok) {  // on a timeout the copy may still land: keep the parity, drain before leaving
-      if (st) ph1 ^= 1; else ph0 ^= 1;
-      inflight[st] = false;
-    }
-    if (__syncthreads_or(!ok)) {
-      if (tid == 0) {
-        atomicOr(a.status, kStTimeout);
-        atomicExch(&a.ctl->abort, 1u);
-      }
-      break;
-    }
-    uint8_t* stage = stage0 + st * a.sm.stage_bytes;
-
-    if (k < pl.nGU) {
-      // ---------------------------------------------------- gate/up unit
-      const unsigned item = k / kGuUnits, ng = k % kGuUnits, u = item / S, si = item % S;
-      const bool shared = s_uid[u] == 512;
-      const unsigned type = shared ? kQ80 : a.gate_type;
-      const unsigned rowb = shared ? a.shared_row : a.row_bytes, nb = d / 32;
-      const uint8_t* grow = stage + warp * rowb;
-      const uint8_t* urow = stage + (kGuNeurons + warp) * rowb;
-      const unsigned n = ng * kGuNeurons + warp;
-      unsigned mask = s_umask[u];
-      bool bad = false;
-      while (mask) {
-        const unsigned t = __ffs(mask) - 1;
-        mask &= mask - 1;
-        float ag = 0.0f, au = 0.0f;
-        if (ACT == FRC_ACT_Q8) {
-          const uint8_t* xq = smem + (type == kMXFP4 ? a.sm.xp : a.sm.xq) + t * d;
-          const float* xs = reinterpret_cast<const float*>(smem + a.sm.xs) + t * P;
-          const float* xv = reinterpret_cast<const float*>(smem + a.sm.xv) + t * 2 * P;
-          for (unsigned p = lane; p < P; p += 32) {
-            uint32_t xw[16];
-            load_x16(xq, p, xw);
-            float tg, tu;
-            if (type == kQ4K) {
-              const float v0 = xv[2 * p], v1 = xv[2 * p + 1];
-              tg = term_q4k(grow, p, xw, v0, v1, bad);
-              tu = term_q4k(urow, p, xw, v0, v1, bad);
-            } else if (type == kMXFP4) {
-              tg = term_mxfp4(grow, nb, p, xw, bad);
-              tu = term_mxfp4(urow, nb, p, xw, bad);
-            } else {
-              tg = term_q80(grow, nb, p, xw, bad);
-              tu = term_q80(urow, nb, p, xw, bad);
-            }
-            ag = __fmaf_rn(xs[p], tg, ag);
-            au = __fmaf_rn(xs[p], tu, au);
-          }
-        } else {
-          const float* xf = reinterpret_cast<const float*>(smem + a.sm.xf) + t * d;
-          for (unsigned p = lane; p < P; p += 32)
-            for (unsigned jj = 0; jj < 64; ++jj) {
-              const unsigned j = 64 * p + jj;
-              const float wg = weight_any(grow, type, d, j), wu = weight_any(urow, type, d, j);
-              bad |= !isfinite(wg) || !isfinite(wu);
-              ag = __fmaf_rn(wg, xf[j], ag);
-              au = __fmaf_rn(wu, xf[j], au);
-            }
-        }
-#pragma unroll
-        for (unsigned o = 16; o; o >>= 1) {
-          ag = __fadd_rn(ag, __shfl_xor_sync(0xffffffffu, ag, o));
-          au = __fadd_rn(au, __shfl_xor_sync(0xffffffffu, au, o));
-        }
-        if (lane == 0) {
-          float h = 0.0f;
-          if (!isfinite(ag) || !isfinite(au) || !swiglu(ag, au, &h)) bad = true;
-          a.hidden[((static_cast<size_t>(u) * S + si) * T + t) * 32 + n] = h;
-        }
-      }
-      if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(a.status, kStNumeric);
-      __threadfence();
-      __syncthreads();
-      if (tid == 0) atomicAdd(&a.ctl->gu_done[u], 1u);
-    } else {
-      // ------------------------------------------------------- down unit
-      const unsigned j = k - pl.nGU, u = j / pl.nch, c = j % pl.nch;
-      const bool shared = s_uid[u] == 512;
-      const unsigned down = shared ? kQ80 : a.down_type;
-      const unsigned mask = s_umask[u], cnt = __popc(mask);
-      bool waited = true;
-      if (tid == 0 && !spin_geq(&a.ctl->gu_done[u], S * kGuUnits, &a.ctl->abort)) {
-        waited = false;
-        atomicOr(a.status, kStTimeout);
-        atomicExch(&a.ctl->abort, 1u);
-      }
-      if (__syncthreads_or(!waited)) break;
-      // hidden slices of this expert -> int8 (Q8) or fp32 (F32), [si][k][32]
-      for (unsigned idx = warp; idx < S * cnt; idx += kWarps) {
-        const unsigned si = idx / cnt, kk = idx % cnt;
-        unsigned mm = mask;
-        for (unsigned z = 0; z < kk; ++z) mm &= mm - 1;
-        const unsigned t = __ffs(mm) - 1;
-        const float h = __ldcg(&a.hidden[((static_cast<size_t>(u) * S + si) * T + t) * 32 + lane]);
-        if (ACT == FRC_ACT_Q8) {
-          float amax = fabsf(h);
-#pragma unroll
-          for (unsigned o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-          const float scale = __fdiv_rn(amax, 127.0f);
-          const int v = q8_value(h, amax, scale);
-          const unsigned pos = down == kMXFP4 ? prmt_pos(lane) : lane;
-          smem[a.sm.hq + idx * 32 + pos] = static_cast<uint8_t>(v & 0xff);
-          if (lane == 0) reinterpret_cast<float*>(smem + a.sm.gs)[idx] = __fmul_rn(scale, s_ugate[u * T + t]);
-        } else {
-          reinterpret_cast<float*>(smem + a.sm.hq)[idx * 32 + lane] = h;
-          if (lane == 0) reinterpret_cast<float*>(smem + a.sm.gs)[idx] = s_ugate[u * T + t];
-        }
-      }
-      __syncthreads();
-      const unsigned r = tid % kDnRows, q = tid / kDnRows;
-      const float* gs = reinterpret_cast<const float*>(smem + a.sm.gs);
-      float acc[MAXT];
-#pragma unroll
-      for (unsigned kk = 0; kk < MAXT; ++kk) acc[kk] = 0.0f;
-      bool bad = false;
-      const bool mx = down == kMXFP4;
-      const unsigned hb = mx ? 1 : 2, ib = kDnRows * (mx ? 17 : 34);
-      for (unsigned si = q; si < S; si += kDnSplit) {
-        const uint8_t* it = stage + si * ib;
-        if (ACT == FRC_ACT_Q8) {
-          if (mx) {
-            const unsigned e = it[r];
-            bad |= e == 255;
-            const float sw = pow2_m128(e);
-            const uint4 w = *reinterpret_cast<const uint4*>(it + kDnRows * hb + 16 * r);
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-            uint32_t pw[8], nw[8];
-#pragma unroll
-            for (unsigned m = 0; m < 4; ++m) {
-              pw[2 * m] = prmt(kE2M1Lo, kE2M1Hi, ww[m]);
-              nw[2 * m] = prmt(kE2M1Lo, kE2M1Hi, ww[m] ^ 0x8888u);
-              pw[2 * m + 1] = prmt(kE2M1Lo, kE2M1Hi, ww[m] >> 16);
-              nw[2 * m + 1] = prmt(kE2M1Lo, kE2M1Hi, (ww[m] >> 16) ^ 0x8888u);
-            }
-#pragma unroll
-            for (unsigned kk = 0; kk < MAXT; ++kk) {
-              if (kk >= cnt) break;
-              const uint4* hv = reinterpret_cast<const uint4*>(smem + a.sm.hq + (si * cnt + kk) * 32);
-              const uint4 h0 = hv[0], h1 = hv[1];
-              const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-              int ip = 0, in = 0;
-#pragma unroll
-              for (unsigned m = 0; m < 8; ++m) {
-                ip = __dp4a(static_cast<int>(pw[m]), static_cast<int>(hw[m]), ip);
-                in = __dp4a(static_cast<int>(nw[m]), static_cast<int>(hw[m]), in);
-              }
-              const float cterm = __fmul_rn(sw, i2f(ip - in));
-              acc[kk] = __fmaf_rn(cterm, gs[si * cnt + kk], acc[kk]);
-            }
-          } else {
-            const float sw = h2f(it[2 * r] | it[2 * r + 1] << 8);
-            bad |= !isfinite(sw);
-            const uint4* wv = reinterpret_cast<const uint4*>(it + kDnRows * hb + 32 * r);
-            const uint4 w0 = wv[0], w1 = wv[1];
-            const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-            for (unsigned kk = 0; kk < MAXT; ++kk) {
-              if (kk >= cnt) break;
-              const uint4* hv = reinterpret_cast<const uint4*>(smem + a.sm.hq + (si * cnt + kk) * 32);
-              const uint4 h0 = hv[0], h1 = hv[1];
-              const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-              int iv = 0;
-#pragma unroll
-              for (unsigned m = 0; m < 8; ++m) iv = __dp4a(static_cast<int>(ww[m]), static_cast<int>(hw[m]), iv);
-              const float cterm = __fmul_rn(sw, i2f(iv));
-              acc[kk] = __fmaf_rn(cterm, gs[si * cnt + kk], acc[kk]);
-            }
-          }
-        } else {
-          // fp32: exact weights times fp32 hidden, neuron order
-          float wrow[32];
-          if (mx) {
-            const unsigned e = it[r];
-            bad |= e == 255;
-            const float sc = __uint_as_float(e ? e << 23 : 0x00400000u);
-            const uint8_t* qb = it + kDnRows + 16 * r;
-#pragma unroll
-            for (unsigned nn = 0; nn < 32; ++nn) wrow[nn] = __fmul_rn(sc, e2m1((qb[nn & 15] >> (nn >> 4 ? 4 : 0)) & 15));
-          } else {
-            const float sw = h2f(it[2 * r] | it[2 * r + 1] << 8);
-            bad |= !isfinite(sw);
-            const int8_t* qb = reinterpret_cast<const int8_t*>(it + 2 * kDnRows + 32 * r);
-#pragma unroll
-            for (unsigned nn = 0; nn < 32; ++nn) wrow[nn] = __fmul_rn(sw, static_cast<float>(qb[nn]));
-          }
-#pragma unroll
-          for (unsigned kk = 0; kk < MAXT; ++kk) {
-            if (kk >= cnt) break;
-            const float* hv = reinterpret_cast<const float*>(smem + a.sm.hq) + (si * cnt + kk) * 32;
-            float dot = 0.0f;
-#pragma unroll
-            for (unsigned nn = 0; nn < 32; ++nn) dot = __fmaf_rn(wrow[nn], hv[nn], dot);
-            acc[kk] = __fmaf_rn(dot, gs[si * cnt + kk], acc[kk]);
-          }
-        }
-      }
-      if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(a.status, kStNumeric);
-      __syncthreads();  // stage fully read: reuse it for the split sums
-      float* red = reinterpret_cast<float*>(stage);  // [kDnSplit][cnt][64]
-#pragma unroll
-      for (unsigned kk = 0; kk < MAXT; ++kk)
-        if (kk < cnt) red[(q * cnt + kk) * kDnRows + r] = acc[kk];
-      __syncthreads();
-      for (unsigned idx = tid; idx < cnt * kDnRows; idx += kThreads) {
-        const unsigned kk = idx / kDnRows, rr = idx % kDnRows;
-        float sum = red[kk * kDnRows + rr];
-        for (unsigned z = 1; z < kDnSplit; ++z) sum = __fadd_rn(sum, red[(z * cnt + kk) * kDnRows + rr]);
-        unsigned mm = mask;
-        for (unsigned z = 0; z < kk; ++z) mm &= mm - 1;
-        const unsigned t = __ffs(mm) - 1;
-        a.partial[(static_cast<size_t>(u) * T + t) * d + c * kDnRows + rr] = sum;
-      }
-      __threadfence();
-      __syncthreads();
-      if (tid == 0) misc[2] = atomicAdd(&a.ctl->chunk_done[c], 1u) == U - 1;
-      __syncthreads();
-      if (misc[2]) {
-        __threadfence();
-        bool nf = false;
-        // each token sums its experts in its own routing order, then the
-        // shared expert: a token's y does not depend on the rest of the burst
-        for (unsigned idx = tid; idx < T * kDnRows; idx += kThreads) {
-          const unsigned t = idx / kDnRows, rr = idx % kDnRows;
-          const size_t col = static_cast<size_t>(t) * d + c * kDnRows + rr;
-          float yv = 0.0f;
-          for (unsigned e = 0; e < 10; ++e) {
-            const unsigned id = s_ids[t * 10 + e];
-            if (id >= 512) continue;
-            const unsigned uu = static_cast<unsigned>(-1 - s_first[id]);
-            yv = __fadd_rn(yv, __ldcg(&a.partial[static_cast<size_t>(uu) * T * d + col]));
-          }
-          if (s_g[t * 11 + 10] != 0.0f) yv = __fadd_rn(yv, __ldcg(&a.partial[static_cast<size_t>(misc[4]) * T * d + col]));
-          nf |= !isfinite(yv);
-          a.y[col] = yv;
-        }
-        if (nf) atomicOr(a.status, kStNumeric);
-      }
-    }
-    __syncthreads();
-    k = misc[(iter + 1) & 1];
-    st ^= 1;
-    ++iter;
-  }
-
-  // ---- leave: no bulk copy may still be writing this CTA's shared memory
-  for (unsigned b2 = 0; b2 < 2; ++b2)
-    if (inflight[b2] && !mbar_wait(&bar[b2], b2 ? ph1 : ph0) && tid == 0) atomicOr(a.status, kStTimeout);
-  // ---- the last CTA out restores the counters for the next launch
-  __syncthreads();
-  if (tid == 0) misc[3] = atomicAdd(&a.ctl->exited, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (misc[3]) {
-    __threadfence();
-    for (unsigned i = tid; i < kMaxUnique + 3; i += kThreads) a.ctl->gu_done[i] = 0;
-    for (unsigned i = tid; i < kMaxChunks; i += kThreads) a.ctl->chunk_done[i] = 0;
-    if (tid == 0) {
-      a.ctl->next = 0;
-      a.ctl->exited = 0;
-      a.ctl->abort = 0;
-    }
-  }
-}
+#include "frc_layer.cuh"
 
 // ===================================================== set-up kernels
 
@@ -627,8 +120,8 @@ struct frc_context {
   uint8_t* layer_ptr[FRC_MAX_BLOCKS][FRC_MAX_LAYERS] = {};
   uint8_t* staging = nullptr;
   float* hidden = nullptr;
-  float* partial = nullptr;
-  Ctl* ctl = nullptr;
+  unsigned long long* phases = nullptr;
+  LayerCtl* ctl = nullptr;
   unsigned* status = nullptr;
   uint16_t* d_expert = nullptr;
   float *d_gate = nullptr, *d_x = nullptr, *d_y = nullptr;
@@ -639,9 +132,9 @@ struct frc_context {
   uint8_t* pool = nullptr;
   unsigned pool_count = 0;
   unsigned long long launches = 0;
-  bool attr_set[2][3] = {};
-  unsigned occ_smem[2][3] = {};
-  int occ_val[2][3] = {};
+  bool attr_set[2] = {};
+  unsigned occ_smem[2] = {};
+  int occ_val[2] = {};
   unsigned last_T = 0, last_S = 0;
   uint16_t last_expert[FRC_MAX_TOKENS * FRC_TOPK] = {};
   float last_gate[FRC_MAX_TOKENS * FRC_ACTIVE] = {};
@@ -665,66 +158,90 @@ static int fail(frc_context* c, int rc, const char* fmt, ...) {
 
 static unsigned align_up(unsigned v, unsigned a) { return (v + a - 1) / a * a; }
 
-static Smem smem_layout(const frc_context* c, unsigned T, unsigned S, int act) {
-  const unsigned d = c->g.hidden, P = d / 64;
-  Smem m{};
-  unsigned o = 64 + 64;  // mbarriers + misc words
-  auto take = [&](unsigned bytes) { unsigned at = o; o = align_up(o + bytes, 16); return at; };
-  m.ids = take(2 * T * 10);
-  m.gates = take(4 * T * 11);
-  m.first = take(4 * 512);
-  m.uid = take(2 * kMaxUnique);
-  m.umask = take(4 * kMaxUnique);
-  m.ugate = take(4 * kMaxUnique * T);
-  m.rms = take(4 * T);
-  if (act == FRC_ACT_Q8) {
-    m.xq = take(T * d);
-    m.xp = c->g.gate_type == FRC_MXFP4 ? take(T * d) : 0;
-    m.xs = take(4 * T * P);
-    m.xv = take(4 * T * 2 * P);
-    m.xf = 0;
-    m.hq = take(32 * S * T);
-  } else {
-    m.xq = m.xp = m.xs = m.xv = 0;
-    m.xf = take(4 * T * d);
-    m.hq = take(4 * 32 * S * T);
+// Shared memory of one layer CTA.  The gate/up ring takes 3 slots of 2*chunk
+// rows; the phase-2 region takes what is left (the kernel batches experts to
+// fit it).  Returns false when even the smallest chunk does not fit.
+static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, LayerSmem* out) {
+  const unsigned d = c->g.hidden, P = d / 64, rmax = (d + G - 1) / G;
+  const unsigned limit = 227 * 1024;
+  if ((T * d / 4 + kActThreads - 1) / kActThreads > kMaxRounds) return false;
+  for (unsigned chunk = kGuChunk; chunk >= 2; chunk /= 2) {
+    LayerSmem m{};
+    unsigned o = 64 + 256;  // mbarriers, then 64 misc words
+    auto take = [&](unsigned bytes) { unsigned at = o; o = align_up(o + bytes, 16); return at; };
+    m.ids = take(2 * T * 10);
+    m.gates = take(4 * T * 11);
+    m.first = take(4 * 512);
+    m.uid = take(2 * kMaxUnique);
+    m.umask = take(4 * kMaxUnique);
+    m.ugate = take(4 * kMaxUnique * T);
+    m.upre = take(4 * (kMaxUnique + 1));
+    m.rms = take(4 * T);
+    m.bases = take(8 * kMaxBlocks);
+    m.rpart = take(4 * 8 * kMaxRounds);
+    m.pairs = take(2 * (T * 11));
+    m.tokpair = take(2 * (T * 11));
+    if (act == FRC_ACT_Q8) {
+      m.xq = take(T * d);
+      m.xp = c->g.gate_type == FRC_MXFP4 ? take(T * d) : 0;
+      m.xs = take(4 * T * P);
+      m.xv = take(4 * T * 2 * P);
+    } else {
+      m.xf = take(4 * T * d);
+    }
+    m.split = take(4 * kDnSplit * (T * 11) * rmax);
+    o = align_up(o, 128);
+    const unsigned routed = 2 * chunk * static_cast<unsigned>(c->row_bytes);
+    const unsigned shared = 4 * static_cast<unsigned>(c->shared_row);  // at least 2 shared neurons
+    m.chunk = chunk;
+    m.slot_bytes = align_up(routed > shared ? routed : shared, 128);
+    m.ring = o;
+    o += kSlots * m.slot_bytes;
+    m.p2 = o;
+    // one expert must fit a phase-2 batch: the shared expert's Q8_0 pieces + staged hidden slices
+    const unsigned piece_q8 = align_up(2 * rmax + 15, 16) + 32 * rmax;
+    const unsigned min_p2 = kMaxBlocks * piece_q8 + kMaxBlocks * T * (act == FRC_ACT_Q8 ? 36 : 132);
+    if (o + min_p2 > limit) continue;
+    m.p2_bytes = (limit - o) & ~15u;
+    m.total = o + m.p2_bytes;
+    *out = m;
+    return true;
   }
-  m.gs = take(4 * S * T);
-  // A stage holds the largest unit: 16 gate/up rows, or one expert's 64 down
-  // rows of every loaded slice; and later the down split sums.
-  const unsigned gu = 2 * kGuNeurons * static_cast<unsigned>(c->row_bytes > c->shared_row ? c->row_bytes : c->shared_row);
-  const unsigned dn = S * kDnRows * 34;  // the shared expert's Q8_0 rows bound the routed MXFP4 ones
-  const unsigned red = 4 * kDnSplit * T * kDnRows;
-  unsigned sb = gu > dn ? gu : dn;
-  if (red > sb) sb = red;
-  m.stage_bytes = align_up(sb, 128);
-  o = align_up(o, 128);
-  m.stage = o;
-  m.total = o + 2 * m.stage_bytes;
-  return m;
+  return false;
 }
 
-template <int ACT, int MAXT>
-static int launch_layer(frc_context* c, const LayerArgs& a, unsigned units, cudaStream_t s) {
-  auto kern = layer_kernel<ACT, MAXT>;
-  const int ai = ACT == FRC_ACT_Q8, mi = MAXT == 1 ? 0 : MAXT == 4 ? 1 : 2;
-  if (!c->attr_set[ai][mi]) {
+template <int ACT>
+static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s) {
+  auto kern = moe_layer_kernel<ACT>;
+  const int ai = ACT == FRC_ACT_Q8;
+  if (!c->attr_set[ai]) {
     CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-    c->attr_set[ai][mi] = true;
+    c->attr_set[ai] = true;
   }
+  // one CTA per SM, all resident (the kernel has a grid barrier)
+  const unsigned G = static_cast<unsigned>(c->sms);
+  if (!smem_layout(c, a.T, G, ACT, &a.sm)) return fail(c, FRC_INVALID, "%u tokens need too much shared memory", a.T);
   int per_sm = 0;
-  if (c->occ_smem[ai][mi] == a.sm.total) {
-    per_sm = c->occ_val[ai][mi];
+  if (c->occ_smem[ai] == a.sm.total) {
+    per_sm = c->occ_val[ai];
   } else {
-    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, a.sm.total));
-    c->occ_smem[ai][mi] = a.sm.total;
-    c->occ_val[ai][mi] = per_sm;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kLayerThreads, a.sm.total));
+    c->occ_smem[ai] = a.sm.total;
+    c->occ_val[ai] = per_sm;
   }
-  if (per_sm < 1) return fail(c, FRC_INVALID, "layer needs %u bytes of shared memory", a.sm.total);
-  unsigned grid = static_cast<unsigned>(per_sm) * c->sms;
-  if (grid > units) grid = units;
-  kern<<<grid, kThreads, a.sm.total, s>>>(a);
-  CK(cudaGetLastError());
+  if (per_sm < 1) return fail(c, FRC_INVALID, "layer kernel does not fit an SM (%u bytes)", a.sm.total);
+  a.rmax = (a.d + G - 1) / G;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.gridDim = dim3(G);
+  cfg.blockDim = dim3(kLayerThreads);
+  cfg.dynamicSmemBytes = a.sm.total;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CK(cudaLaunchKernelEx(&cfg, kern, a));
   ++c->launches;
   return FRC_OK;
 }
@@ -735,7 +252,7 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
   if (!c || !expert || !gate || !x || !y) return fail(c, FRC_INVALID, "null argument");
   if (T < 1 || T > FRC_MAX_TOKENS || layer >= c->g.layers) return fail(c, FRC_INVALID, "tokens or layer out of range");
   if (act != FRC_ACT_Q8 && act != FRC_ACT_F32) return fail(c, FRC_INVALID, "unknown activation mode");
-  LayerArgs a{};
+  LayerParams a{};
   unsigned S = 0;
   for (unsigned b = 0; b < FRC_MAX_BLOCKS; ++b) {
     bool any = false;
@@ -746,27 +263,17 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
   }
   if (!S) return fail(c, FRC_STATE, "no block loaded");
   a.expert = expert; a.gate = gate; a.x = x; a.x_add = x_add; a.x_out = x_out; a.y = y;
-  a.hidden = c->hidden; a.partial = c->partial; a.ctl = c->ctl; a.status = c->status;
+  a.hidden = c->hidden; a.ctl = c->ctl; a.status = c->status;
+  a.phases = c->phases;
   a.S = S; a.T = T; a.d = c->g.hidden;
   a.norm = flags & FRC_RUN_RMSNORM ? 1u : 0u;
   a.gate_type = c->g.gate_type; a.down_type = c->g.down_type;
   a.row_bytes = static_cast<unsigned>(c->row_bytes); a.proj_bytes = static_cast<unsigned>(c->proj_bytes);
   a.shared_row = static_cast<unsigned>(c->shared_row); a.shared_proj = static_cast<unsigned>(c->shared_proj);
   a.slice_bytes = static_cast<unsigned>(c->slice_bytes);
-  a.sm = smem_layout(c, T, S, act);
-  if (a.sm.total > 227 * 1024) return fail(c, FRC_INVALID, "%u tokens need too much shared memory", T);
-  const unsigned umax = (10 * T < 512 ? 10 * T : 512) + 1;
-  const unsigned units = umax * S * kGuUnits + umax * (c->g.hidden / kDnRows);
   c->last_S = S;
-  const int maxt = T == 1 ? 1 : T <= 4 ? 4 : 16;
-  if (act == FRC_ACT_Q8) {
-    if (maxt == 1) return launch_layer<FRC_ACT_Q8, 1>(c, a, units, s);
-    if (maxt == 4) return launch_layer<FRC_ACT_Q8, 4>(c, a, units, s);
-    return launch_layer<FRC_ACT_Q8, 16>(c, a, units, s);
-  }
-  if (maxt == 1) return launch_layer<FRC_ACT_F32, 1>(c, a, units, s);
-  if (maxt == 4) return launch_layer<FRC_ACT_F32, 4>(c, a, units, s);
-  return launch_layer<FRC_ACT_F32, 16>(c, a, units, s);
+  if (act == FRC_ACT_Q8) return launch_layer<FRC_ACT_Q8>(c, a, s);
+  return launch_layer<FRC_ACT_F32>(c, a, s);
 }
 
 static int status_code(unsigned st) {
@@ -818,9 +325,9 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
     if (rc == FRC_OK && cudaMalloc(p, bytes) != cudaSuccess) rc = fail(c, FRC_IO, "cudaMalloc(%zu) failed", bytes);
   };
   if (cudaSetDevice(device) != cudaSuccess) rc = FRC_IO;
-  alloc(reinterpret_cast<void**>(&c->hidden), sizeof(float) * kMaxUnique * kMaxBlocks * kMaxTokens * 32);
-  alloc(reinterpret_cast<void**>(&c->partial), sizeof(float) * kMaxUnique * kMaxTokens * d);
-  alloc(reinterpret_cast<void**>(&c->ctl), sizeof(Ctl));
+  alloc(reinterpret_cast<void**>(&c->hidden), sizeof(float) * kMaxItems * kMaxTokens * 32);
+  alloc(reinterpret_cast<void**>(&c->ctl), sizeof(LayerCtl));
+  alloc(reinterpret_cast<void**>(&c->phases), sizeof(unsigned long long) * 16 * 1024);
   alloc(reinterpret_cast<void**>(&c->status), sizeof(unsigned));
   alloc(reinterpret_cast<void**>(&c->d_expert), sizeof(uint16_t) * kMaxTokens * 10);
   alloc(reinterpret_cast<void**>(&c->d_gate), sizeof(float) * kMaxTokens * 11);
@@ -835,9 +342,9 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
         cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess)
       rc = fail(c, FRC_IO, "pinned buffers or stream");
   }
-  if (rc == FRC_OK && (cudaMemset(c->ctl, 0, sizeof(Ctl)) != cudaSuccess ||
+  if (rc == FRC_OK && (cudaMemset(c->ctl, 0, sizeof(LayerCtl)) != cudaSuccess ||
                        cudaMemset(c->status, 0, sizeof(unsigned)) != cudaSuccess ||
-                       cudaMemset(c->hidden, 0, sizeof(float) * kMaxUnique * kMaxBlocks * kMaxTokens * 32) != cudaSuccess))
+                       cudaMemset(c->hidden, 0, sizeof(float) * kMaxItems * kMaxTokens * 32) != cudaSuccess))
     rc = fail(c, FRC_IO, "cudaMemset");
   if (rc != FRC_OK) {
     frc_close(c);
@@ -853,7 +360,7 @@ int frc_close(frc_context* c) {
   if (c->stream) cudaStreamSynchronize(c->stream);
   for (auto& b : c->layer_ptr)
     for (auto& p : b) if (p) cudaFree(p);
-  cudaFree(c->staging); cudaFree(c->hidden); cudaFree(c->partial); cudaFree(c->ctl); cudaFree(c->status);
+  cudaFree(c->staging); cudaFree(c->hidden); cudaFree(c->phases); cudaFree(c->ctl); cudaFree(c->status);
   cudaFree(c->d_expert); cudaFree(c->d_gate); cudaFree(c->d_x); cudaFree(c->d_y); cudaFree(c->pool);
   cudaFreeHost(c->h_expert); cudaFreeHost(c->h_gate); cudaFreeHost(c->h_x); cudaFreeHost(c->h_y); cudaFreeHost(c->h_status);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -990,6 +497,7 @@ int frc_status(frc_context* c, void* stream) {
   CK(cudaMemsetAsync(c->status, 0, sizeof(unsigned), s));
   CK(cudaStreamSynchronize(s));
   const int rc = status_code(*c->h_status);
+  if (*c->h_status & kStTimeout) CK(cudaMemset(c->ctl, 0, sizeof(LayerCtl)));  // nothing runs now
   if (rc) return fail(c, rc, "device status 0x%x", *c->h_status);
   return FRC_OK;
 }
@@ -1097,6 +605,20 @@ int frc_debug_hidden(frc_context* c, float* h, size_t cap, size_t* count) {
       for (unsigned t = 0; t < T; ++t)
         if (!(umask[u] >> t & 1)) memset(h + ((static_cast<size_t>(u) * S + si) * T + t) * 32, 0, 32 * sizeof(float));
   return FRC_OK;
+}
+
+int frc_debug_phases(frc_context* c, uint64_t* out, size_t cap, size_t* count) {
+  if (!c || !count) return FRC_INVALID;
+  *count = 16 * static_cast<size_t>(c->sms);
+#ifndef FRC_PHASES
+  return fail(c, FRC_UNSUPPORTED, "built without FRC_PHASES");
+#else
+  if (!out) return FRC_OK;
+  if (cap < *count) return fail(c, FRC_INVALID, "buffer too small");
+  CK(cudaSetDevice(c->device));
+  CK(cudaMemcpy(out, c->phases, *count * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+  return FRC_OK;
+#endif
 }
 
 }  // extern "C"

@@ -88,6 +88,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// 16-byte LSU copy global -> shared (L2 only), for many small pieces where a
+// bulk copy per piece would cost more than the bytes it moves.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
   uint32_t ok;
   asm volatile(
@@ -179,6 +186,22 @@ __device__ __forceinline__ float q8_round(float x, float amax, float scale) {
 __device__ __forceinline__ int q8_value(float x, float amax, float scale) {
   return static_cast<int>(q8_round(x, amax, scale));
 }
+// The same quantizer with the group's two divisions done once.
+struct Q8Group {
+  float amax, scale, inv;
+  bool inv_ok;
+  __device__ __forceinline__ explicit Q8Group(float m) : amax(m) {
+    scale = __fdiv_rn(m, 127.0f);
+    inv = scale != 0.0f ? __fdiv_rn(127.0f, m) : 0.0f;
+    inv_ok = isfinite(inv);
+  }
+  __device__ __forceinline__ int q(float x) const {
+    if (scale == 0.0f) return 0;
+    float v = inv_ok ? __fmul_rn(x, inv) : __fmul_rn(__fdiv_rn(x, amax), 127.0f);
+    v = rintf(v);
+    return static_cast<int>(fminf(fmaxf(v, -127.0f), 127.0f));
+  }
+};
 
 // Position of element n (0..31) of a 32-weight block in the "prmt order" that
 // matches an MXFP4 block's nibble bytes (byte j holds elements j and j+16).

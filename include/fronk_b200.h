@@ -165,6 +165,12 @@ int frc_debug_quantize(frc_context *c, unsigned tokens, const float *x, int8_t *
  * [unique expert][loaded block][token][32] (zero where the token does not use
  * the expert); *count receives the number of floats. */
 int frc_debug_hidden(frc_context *c, float *h, size_t cap, size_t *count);
+/* Per-CTA globaltimer stamps of the last layer launch, [cta][16]: entry, plan,
+ * norm sums, activations, gate/up done, barrier done, down done, exit, then
+ * finer points inside the plan (8-10) and the down phase (11-13).
+ * Only libraries built with FRC_PHASES record them (else FRC_UNSUPPORTED);
+ * the counterpart of the reference's compile-time FR_PHASES timers. */
+int frc_debug_phases(frc_context *c, uint64_t *out, size_t cap, size_t *count);
 
 #ifdef __cplusplus
 }
