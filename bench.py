@@ -35,8 +35,15 @@ WORKLOAD = ("decode48: 48 MoE layers, 1 token, d=2048, 512
             "Q4_K gate/up + MXFP4 down, 20 slices split over the GPUs, partial sum after every layer")
 
 
+_out = sys.stdout
+
+
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
+
+
+def emit(line):
+    print(json.dumps(line), file=_out, flush=True)
 
 
 def peaks():
@@ -144,7 +151,7 @@ def run_reference(args, rank):
     warm = max(1, min(args.warmup, 3))
     cb = cpu_baseline(steps, warm)
     if "unavailable" in cb:
-        print(json.dumps({"impl": "reference", "unavailable": cb["unavailable"]}), flush=True)
+        emit({"impl": "reference", "unavailable": cb["unavailable"]})
         return
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": steps, "warmup": warm, "ms_per_step": cb["ms_per_pass"],
@@ -152,7 +159,7 @@ def run_reference(args, rank):
             "data": "synthetic", "config": config(args.gpus),
             "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                         "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def config(n):
@@ -180,6 +187,11 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    # stdout carries exactly one JSON line: libraries that print (NCCL's
+    # version banner) write to stderr instead
+    global _out
+    _out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args, rank)
         return
@@ -343,7 +355,7 @@ def main():
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(3, 1)
-        print(json.dumps(line), flush=True)
+        emit(line)
     ctx.close()
     if dist is not None:
         dist.barrier()
