@@ -62,6 +62,7 @@ _SIGS = {
     "frc_loaded_mask": (_int, [_vp, _vp]),
     "frc_run": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _int]),
     "frc_run_device": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
+    "frc_run_device_fixed": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
     "frc_status": (_int, [_vp, _vp]),
     "frc_launch_count": (_u64, [_vp]),
     "frc_strerror": (ctypes.c_char_p, [_int]),
@@ -255,6 +256,14 @@ class Context:
         rc = self.lib.frc_run_device(self.h, layer, tokens, expert_ptr, gate_ptr, x_ptr, x_add_ptr, x_out_ptr,
                                      y_ptr, act, flags, stream)
         self._check(rc, "run_device")
+
+    def run_device_fixed(self, layer, tokens, expert_ptr, gate_ptr, x_ptr, x_add_ptr, x_out_ptr, y_ptr,
+                         act=ACT_Q8, flags=0, stream=None):
+        """run_device with the hidden hand-off in the library's fixed device
+        array (allocates nothing; see frc_run_device_fixed)."""
+        rc = self.lib.frc_run_device_fixed(self.h, layer, tokens, expert_ptr, gate_ptr, x_ptr, x_add_ptr,
+                                           x_out_ptr, y_ptr, act, flags, stream)
+        self._check(rc, "run_device_fixed")
 
     def status(self, stream=None):
         return self.lib.frc_status(self.h, stream)

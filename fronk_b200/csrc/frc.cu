@@ -12,6 +12,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "../../include/fronk_b200.h"
 #include "frc_device.cuh"
 
@@ -248,7 +250,7 @@ static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s) {
 
 static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t* expert, const float* gate,
                       const float* x, const float* x_add, float* x_out, float* y, int act, unsigned flags,
-                      cudaStream_t s) {
+                      cudaStream_t s, float* hidden = nullptr) {
   if (!c || !expert || !gate || !x || !y) return fail(c, FRC_INVALID, "null argument");
   if (T < 1 || T > FRC_MAX_TOKENS || layer >= c->g.layers) return fail(c, FRC_INVALID, "tokens or layer out of range");
   if (act != FRC_ACT_Q8 && act != FRC_ACT_F32) return fail(c, FRC_INVALID, "unknown activation mode");
@@ -263,7 +265,7 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
   }
   if (!S) return fail(c, FRC_STATE, "no block loaded");
   a.expert = expert; a.gate = gate; a.x = x; a.x_add = x_add; a.x_out = x_out; a.y = y;
-  a.hidden = c->hidden; a.ctl = c->ctl; a.status = c->status;
+  a.hidden = hidden ? hidden : c->hidden; a.ctl = c->ctl; a.status = c->status;
   a.phases = c->phases;
   a.S = S; a.T = T; a.d = c->g.hidden;
   a.norm = flags & FRC_RUN_RMSNORM ? 1u : 0u;
@@ -281,6 +283,39 @@ static int status_code(unsigned st) {
   if (st & kStInvalid) return FRC_INVALID;
   if (st & kStNumeric) return FRC_NUMERIC;
   return FRC_OK;
+}
+
+// ------------------------------------------------ fixed-scratch layer run
+// frc_run_device_fixed is frc_run_device with one difference: the hidden
+// activations the gate/up phase hands to the down phase (the one scratch
+// buffer a launch writes and then reads back) live in the device array
+// below, fixed when the module loads, instead of in the buffer frc_open
+// allocated for the context.  The call itself allocates nothing, on the first
+// call or later: no cudaMalloc, no cudaFree, no allocating library routine.
+// It is meant for embedders whose device memory is carved up once at
+// start-up (a serving process whose own pool owns every free byte after
+// warm-up, so a later allocation fails or synchronises the device) and that
+// want the footprint of a layer run known when the library is linked.
+//
+// Limit: kFixedHiddenBytes.  A run needs (10 T + 1) x S x T x 32 floats for
+// T tokens over S loaded slices (worst case of distinct experts); with all 20
+// slices that is up to 6 tokens per call.  Larger calls are rejected with
+// FRC_INVALID before anything is launched.
+// Nothing in the array has to start at zero: every entry a launch reads was
+// written earlier in the same launch.  The array is shared by every context
+// and stream of a device, so two overlapping fixed-scratch calls on one device
+// (different streams, or different contexts) race on it; callers serialise
+// them.  The first call on each device looks the array's address up (with the
+// context's device current); it does that set-up and nothing else extra, so
+// make it before capturing the call into a CUDA graph.
+constexpr size_t kFixedHiddenBytes = size_t(1) << 20;
+static __device__ __align__(256) float g_fixed_hidden[kFixedHiddenBytes / sizeof(float)];
+constexpr int kFixedDevices = 64;
+static std::mutex g_fixed_mu;
+static float* g_fixed_ptr[kFixedDevices];
+
+static size_t fixed_need(unsigned S, unsigned T) {
+  return sizeof(float) * (size_t(T) * 10 + 1) * S * T * 32;
 }
 
 extern "C" {
@@ -488,6 +523,39 @@ int frc_run_device(frc_context* c, unsigned layer, unsigned tokens, const uint16
   if (!c) return FRC_INVALID;
   if (cudaSetDevice(c->device) != cudaSuccess) return fail(c, FRC_IO, "cudaSetDevice");
   return run_device(c, layer, tokens, expert, gate, x, x_add, x_out, y, act, flags, static_cast<cudaStream_t>(stream));
+}
+
+int frc_run_device_fixed(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* expert,
+                         const float* gate, const float* x, const float* x_add, float* x_out, float* y, int act,
+                         unsigned flags, void* stream) {
+  if (!c) return FRC_INVALID;
+  if (c->device < 0 || c->device >= kFixedDevices) return fail(c, FRC_UNSUPPORTED, "device %d has no fixed scratch slot", c->device);
+  if (tokens < 1 || tokens > FRC_MAX_TOKENS) return fail(c, FRC_INVALID, "tokens or layer out of range");
+  unsigned S = 0;
+  for (unsigned b = 0; b < FRC_MAX_BLOCKS; ++b) {
+    bool any = false;
+    for (unsigned l = 0; l < c->g.layers; ++l) any |= c->layer_ptr[b][l] != nullptr;
+    S += any;
+  }
+  const size_t need = fixed_need(S, tokens);
+  if (need > kFixedHiddenBytes)
+    return fail(c, FRC_INVALID, "frc_run_device_fixed: %u tokens over %u slices need %zu bytes of fixed scratch, limit %zu",
+                tokens, S, need, kFixedHiddenBytes);
+  if (cudaSetDevice(c->device) != cudaSuccess) return fail(c, FRC_IO, "cudaSetDevice");
+  float* hidden = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_fixed_mu);
+    if (!g_fixed_ptr[c->device]) {
+      void* p = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_fixed_hidden);
+      if (e != cudaSuccess || !p)
+        return fail(c, FRC_IO, "cudaGetSymbolAddress(fixed scratch): %s", cudaGetErrorString(e));
+      g_fixed_ptr[c->device] = static_cast<float*>(p);
+    }
+    hidden = g_fixed_ptr[c->device];
+  }
+  return run_device(c, layer, tokens, expert, gate, x, x_add, x_out, y, act, flags, static_cast<cudaStream_t>(stream),
+                    hidden);
 }
 
 int frc_status(frc_context* c, void* stream) {

@@ -115,6 +115,17 @@ enum { FRC_RUN_RMSNORM = 1 };
 int frc_run_device(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *expert,
                    const float *gate, const float *x, const float *x_add, float *x_out,
                    float *y, int act, unsigned flags, void *stream);
+/* frc_run_device with the gate/up -> down hidden hand-off held in a device
+ * array fixed at module load (1 MiB per device) instead of context scratch:
+ * the call allocates nothing.  Up to 6 tokens with 20 slices loaded (more
+ * tokens with fewer slices); a larger call returns FRC_INVALID and launches
+ * nothing.  The array is shared by all contexts and streams of a device:
+ * overlapping calls on one device race, callers serialise them.  The first
+ * call on a device looks the array up; make it before any stream capture.
+ * No counterpart in the reference (backend.h has no device-pointer entry). */
+int frc_run_device_fixed(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *expert,
+                         const float *gate, const float *x, const float *x_add, float *x_out,
+                         float *y, int act, unsigned flags, void *stream);
 /* Waits for `stream`, returns and clears the device status (FRC_OK,
  * FRC_NUMERIC, FRC_INVALID for an out-of-range id, FRC_IO for a timed-out wait). */
 int frc_status(frc_context *c, void *stream);
