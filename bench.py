@@ -247,8 +247,10 @@ def main():
             x = X0 if l <= 1 else H[(l - 1) % 2]
             x_add = None if l == 0 else p(Y[(l - 1) % 2])
             x_out = None if l == 0 else p(H[l % 2])
+            # consecutive layers overlap: layer l+1 plans and starts its weight copies while
+            # layer l (or the all-reduce after it) finishes; it reads x only after that
             ctx.run_device(l, 1, p(cur_ex[l]), p(cur_gt[l]), p(x), x_add, x_out, p(Y[l % 2]), fb.ACT_Q8,
-                           fb.RUN_RMSNORM, s)
+                           fb.RUN_RMSNORM | fb.RUN_OVERLAP, s)
             if dist is not None:
                 dist.all_reduce(Y[l % 2])
 

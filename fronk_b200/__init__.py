@@ -19,6 +19,7 @@ OK, INVALID, STATE, NUMERIC, IO, UNSUPPORTED, MISMATCH = 0, -1, -2, -3, -4, -5, 
 Q8_0, Q4_K, MXFP4 = 8, 12, 39
 ACT_F32, ACT_Q8 = 0, 1
 RUN_RMSNORM = 1
+RUN_OVERLAP = 2
 MAX_BLOCKS, ROUTED, SHARED, TOPK, ACTIVE, NEURONS, MAX_TOKENS = 20, 512, 512, 10, 11, 32, 16
 LAYERS = 48
 

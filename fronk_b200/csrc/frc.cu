@@ -122,6 +122,8 @@ struct frc_context {
   uint8_t* layer_ptr[FRC_MAX_BLOCKS][FRC_MAX_LAYERS] = {};
   uint8_t* staging = nullptr;
   float* hidden = nullptr;
+  float* partial = nullptr;
+  float* gsv = nullptr;
   unsigned long long* phases = nullptr;
   LayerCtl* ctl = nullptr;
   unsigned* status = nullptr;
@@ -160,60 +162,85 @@ static int fail(frc_context* c, int rc, const char* fmt, ...) {
 
 static unsigned align_up(unsigned v, unsigned a) { return (v + a - 1) / a * a; }
 
-// Shared memory of one layer CTA.  The gate/up ring takes 3 slots of 2*chunk
-// rows; the phase-2 region takes what is left (the kernel batches experts to
-// fit it).  Returns false when even the smallest chunk does not fit.
+// fp32 hidden activations of the largest call: [unique expert][slice][token][32]
+constexpr size_t kHiddenBytes = sizeof(float) * kMaxUnique * kMaxBlocks * kMaxTokens * 32;
+
+// Shared memory of one layer CTA and the chunking of an item into ring
+// slots.  A slot is sized for a gate/up chunk of 16 routed neurons (both
+// rows), halved while fewer than four slots fit; the shared expert's chunk
+// and the down chunks are cut to the slot.  Returns false when even two
+// slots of one neuron do not fit.
 static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, LayerSmem* out) {
-  const unsigned d = c->g.hidden, P = d / 64, rmax = (d + G - 1) / G;
+  const unsigned d = c->g.hidden, P = d / 64;
   const unsigned limit = 227 * 1024;
   if ((T * d / 4 + kActThreads - 1) / kActThreads > kMaxRounds) return false;
-  for (unsigned chunk = kGuChunk; chunk >= 2; chunk /= 2) {
-    LayerSmem m{};
-    unsigned o = 64 + 256;  // mbarriers, then 64 misc words
-    auto take = [&](unsigned bytes) { unsigned at = o; o = align_up(o + bytes, 16); return at; };
-    m.ids = take(2 * T * 10);
-    m.gates = take(4 * T * 11);
-    m.first = take(4 * 512);
-    m.uid = take(2 * kMaxUnique);
-    m.umask = take(4 * kMaxUnique);
-    m.ugate = take(4 * kMaxUnique * T);
-    m.upre = take(4 * (kMaxUnique + 1));
-    m.rms = take(4 * T);
-    m.bases = take(8 * kMaxBlocks);
-    m.rpart = take(4 * 8 * kMaxRounds);
-    m.pairs = take(2 * (T * 11));
-    m.tokpair = take(2 * (T * 11));
-    if (act == FRC_ACT_Q8) {
-      m.xq = take(T * d);
-      m.xp = c->g.gate_type == FRC_MXFP4 ? take(T * d) : 0;
-      m.xs = take(4 * T * P);
-      m.xv = take(4 * T * 2 * P);
-    } else {
-      m.xf = take(4 * T * d);
-    }
-    m.split = take(4 * kDnSplit * (T * 11) * rmax);
-    o = align_up(o, 128);
-    const unsigned routed = 2 * chunk * static_cast<unsigned>(c->row_bytes);
-    const unsigned shared = 4 * static_cast<unsigned>(c->shared_row);  // at least 2 shared neurons
-    m.chunk = chunk;
-    m.slot_bytes = align_up(routed > shared ? routed : shared, 128);
-    m.ring = o;
-    o += kSlots * m.slot_bytes;
-    m.p2 = o;
-    // one expert must fit a phase-2 batch: the shared expert's Q8_0 pieces + staged hidden slices
-    const unsigned piece_q8 = align_up(2 * rmax + 15, 16) + 32 * rmax;
-    const unsigned min_p2 = kMaxBlocks * piece_q8 + kMaxBlocks * T * (act == FRC_ACT_Q8 ? 36 : 132);
-    if (o + min_p2 > limit) continue;
-    m.p2_bytes = (limit - o) & ~15u;
-    m.total = o + m.p2_bytes;
-    *out = m;
-    return true;
+  LayerSmem m{};
+  unsigned o = 64 + 256;  // mbarriers, then 64 misc words
+  auto take = [&](unsigned bytes) { unsigned at = o; o = align_up(o + bytes, 16); return at; };
+  m.ids = take(2 * T * 10);
+  m.gates = take(4 * T * 11);
+  m.first = take(4 * 512);
+  m.uid = take(2 * kMaxUnique);
+  m.umask = take(4 * kMaxUnique);
+  m.ugate = take(4 * kMaxUnique * T);
+  m.upre = take(4 * (kMaxUnique + 1));
+  m.rms = take(4 * T);
+  m.bases = take(8 * kMaxBlocks);
+  m.rpart = take(4 * 8 * kMaxRounds);
+  m.tokpair = take(2 * (T * 11));
+  if (act == FRC_ACT_Q8) {
+    m.xq = take(T * d);
+    m.xp = c->g.gate_type == FRC_MXFP4 ? take(T * d) : 0;
+    m.xs = take(4 * T * P);
+    m.xv = take(4 * T * 2 * P);
+    m.hq = take(32 * T);
+  } else {
+    m.xf = take(4 * T * d);
+    m.hq = take(4 * 32 * T);
   }
-  return false;
+  m.gv = take(4 * 32 * T);
+  m.uv = take(4 * 32 * T);
+  m.hg = take(4 * T);
+  o = align_up(o, 128);
+  if (o >= limit) return false;
+  const unsigned avail = limit - o, rowb = static_cast<unsigned>(c->row_bytes);
+  const unsigned srow = static_cast<unsigned>(c->shared_row);
+  const unsigned ss_r = c->g.down_type == FRC_Q8_0 ? 2 : 1, pb_r = c->g.down_type == FRC_Q8_0 ? 32 : 16;
+  unsigned kn = 16;
+  while (kn > 1 && avail / (2 * kn * rowb) < 4) kn /= 2;
+  unsigned slot = 2 * kn * rowb;
+  // the smallest shared chunk (one neuron) and down chunk (16 rows) must fit too
+  slot = slot > 2 * srow ? slot : 2 * srow;
+  slot = slot > 16 * 34 ? slot : 16 * 34;
+  slot = align_up(slot, 128);
+  unsigned K = avail / slot;
+  // the reduce stages one token's terms [11][S][rows], weights [11][S] and
+  // sums [11][rows] in the ring (rows: 4-row units, S up to 20)
+  const unsigned rows4 = 4 * ((d / 4 + G - 1) / G);
+  if (K < 2 || K * slot < 4 * (11 * kMaxBlocks * (rows4 + 1) + 11 * rows4)) return false;
+  K = K < kMaxSlots ? K : kMaxSlots;
+  unsigned kns = 16;
+  while (kns > 1 && 2 * kns * srow > slot) kns /= 2;
+  auto down_rows = [&](unsigned per_row) {
+    unsigned dn = slot / per_row / 16 * 16;
+    dn = dn < d ? dn : d;
+    const unsigned n = (d + dn - 1) / dn;
+    return align_up((d + n - 1) / n, 16);
+  };
+  m.ring = o;
+  m.slot_bytes = slot;
+  m.slots = K;
+  m.kn_r = kn;
+  m.kn_s = kns;
+  m.dn_r = down_rows(ss_r + pb_r);
+  m.dn_s = down_rows(2 + 32);
+  m.total = o + K * slot;
+  *out = m;
+  return true;
 }
 
 template <int ACT>
-static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s) {
+static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s, bool overlap) {
   auto kern = moe_layer_kernel<ACT>;
   const int ai = ACT == FRC_ACT_Q8;
   if (!c->attr_set[ai]) {
@@ -232,11 +259,19 @@ static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s) {
     c->occ_val[ai] = per_sm;
   }
   if (per_sm < 1) return fail(c, FRC_INVALID, "layer kernel does not fit an SM (%u bytes)", a.sm.total);
-  a.rmax = (a.d + G - 1) / G;
+  // Co-residency of the grid (one CTA per SM, checked above) is what the grid
+  // barrier needs.  A plain launch asks the runtime to check it; an overlapped
+  // launch (programmatic stream serialization) gets it as the previous
+  // launch's CTAs leave their SMs.
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  if (overlap) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+  } else {
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+  }
   cfg.gridDim = dim3(G);
   cfg.blockDim = dim3(kLayerThreads);
   cfg.dynamicSmemBytes = a.sm.total;
@@ -248,9 +283,18 @@ static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s) {
   return FRC_OK;
 }
 
+// Device buffers a launch writes and reads back: the down terms and their
+// weights (handed from the item phase to the reduce) and the optional fp32
+// copy of the hidden activations.
+struct RunScratch {
+  float* partial;  // [pair][S][d]
+  float* gsv;      // [pair][S]
+  float* hidden;   // [u*S+s][T][32] or null
+};
+
 static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t* expert, const float* gate,
                       const float* x, const float* x_add, float* x_out, float* y, int act, unsigned flags,
-                      cudaStream_t s, float* hidden = nullptr) {
+                      cudaStream_t s, const RunScratch* scratch = nullptr) {
   if (!c || !expert || !gate || !x || !y) return fail(c, FRC_INVALID, "null argument");
   if (T < 1 || T > FRC_MAX_TOKENS || layer >= c->g.layers) return fail(c, FRC_INVALID, "tokens or layer out of range");
   if (act != FRC_ACT_Q8 && act != FRC_ACT_F32) return fail(c, FRC_INVALID, "unknown activation mode");
@@ -265,7 +309,12 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
   }
   if (!S) return fail(c, FRC_STATE, "no block loaded");
   a.expert = expert; a.gate = gate; a.x = x; a.x_add = x_add; a.x_out = x_out; a.y = y;
-  a.hidden = hidden ? hidden : c->hidden; a.ctl = c->ctl; a.status = c->status;
+  if (scratch) {
+    a.partial = scratch->partial; a.gsv = scratch->gsv; a.hidden = scratch->hidden;
+  } else {
+    a.partial = c->partial; a.gsv = c->gsv; a.hidden = c->hidden;
+  }
+  a.ctl = c->ctl; a.status = c->status;
   a.phases = c->phases;
   a.S = S; a.T = T; a.d = c->g.hidden;
   a.norm = flags & FRC_RUN_RMSNORM ? 1u : 0u;
@@ -274,8 +323,9 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
   a.shared_row = static_cast<unsigned>(c->shared_row); a.shared_proj = static_cast<unsigned>(c->shared_proj);
   a.slice_bytes = static_cast<unsigned>(c->slice_bytes);
   c->last_S = S;
-  if (act == FRC_ACT_Q8) return launch_layer<FRC_ACT_Q8>(c, a, s);
-  return launch_layer<FRC_ACT_F32>(c, a, s);
+  const bool overlap = (flags & FRC_RUN_OVERLAP) != 0;
+  if (act == FRC_ACT_Q8) return launch_layer<FRC_ACT_Q8>(c, a, s, overlap);
+  return launch_layer<FRC_ACT_F32>(c, a, s, overlap);
 }
 
 static int status_code(unsigned st) {
@@ -286,21 +336,22 @@ static int status_code(unsigned st) {
 }
 
 // ------------------------------------------------ fixed-scratch layer run
-// frc_run_device_fixed is frc_run_device with one difference: the hidden
-// activations the gate/up phase hands to the down phase (the one scratch
-// buffer a launch writes and then reads back) live in the device array
-// below, fixed when the module loads, instead of in the buffer frc_open
-// allocated for the context.  The call itself allocates nothing, on the first
-// call or later: no cudaMalloc, no cudaFree, no allocating library routine.
-// It is meant for embedders whose device memory is carved up once at
-// start-up (a serving process whose own pool owns every free byte after
-// warm-up, so a later allocation fails or synchronises the device) and that
-// want the footprint of a layer run known when the library is linked.
+// frc_run_device_fixed is frc_run_device with one difference: the buffers a
+// launch writes and then reads back (the down terms and their weights, handed
+// from the item phase to the reduce) live in the device array below, fixed
+// when the module loads, instead of in the buffers frc_open allocated for the
+// context, and no fp32 copy of the hidden activations is kept.  The call
+// itself allocates nothing, on the first call or later: no cudaMalloc, no
+// cudaFree, no allocating library routine.  It is meant for embedders whose
+// device memory is carved up once at start-up (a serving process whose own
+// pool owns every free byte after warm-up, so a later allocation fails or
+// synchronises the device) and that want the footprint of a layer run known
+// when the library is linked.
 //
-// Limit: kFixedHiddenBytes.  A run needs (10 T + 1) x S x T x 32 floats for
-// T tokens over S loaded slices (worst case of distinct experts); with all 20
-// slices that is up to 6 tokens per call.  Larger calls are rejected with
-// FRC_INVALID before anything is launched.
+// Limit: kFixedScratchBytes.  A run needs 11 T x S x (d + 1) floats for T
+// tokens over S loaded slices (every token's ten routed experts plus the
+// shared one); with all 20 slices at d = 2048 that is up to 4 tokens a call.
+// Larger calls are rejected with FRC_INVALID before anything is launched.
 // Nothing in the array has to start at zero: every entry a launch reads was
 // written earlier in the same launch.  The array is shared by every context
 // and stream of a device, so two overlapping fixed-scratch calls on one device
@@ -308,14 +359,17 @@ static int status_code(unsigned st) {
 // them.  The first call on each device looks the array's address up (with the
 // context's device current); it does that set-up and nothing else extra, so
 // make it before capturing the call into a CUDA graph.
-constexpr size_t kFixedHiddenBytes = size_t(1) << 20;
-static __device__ __align__(256) float g_fixed_hidden[kFixedHiddenBytes / sizeof(float)];
+constexpr size_t kFixedScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) float g_fixed_scratch[kFixedScratchBytes / sizeof(float)];
 constexpr int kFixedDevices = 64;
 static std::mutex g_fixed_mu;
 static float* g_fixed_ptr[kFixedDevices];
 
-static size_t fixed_need(unsigned S, unsigned T) {
-  return sizeof(float) * (size_t(T) * 10 + 1) * S * T * 32;
+// Floats of the down terms ([pair][S][d]) of the largest T-token call; the
+// weights ([pair][S]) follow them.
+static size_t fixed_partial(unsigned S, unsigned T, unsigned d) { return size_t(11) * T * S * d; }
+static size_t fixed_need(unsigned S, unsigned T, unsigned d) {
+  return sizeof(float) * (fixed_partial(S, T, d) + size_t(11) * T * S);
 }
 
 extern "C" {
@@ -360,7 +414,9 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
     if (rc == FRC_OK && cudaMalloc(p, bytes) != cudaSuccess) rc = fail(c, FRC_IO, "cudaMalloc(%zu) failed", bytes);
   };
   if (cudaSetDevice(device) != cudaSuccess) rc = FRC_IO;
-  alloc(reinterpret_cast<void**>(&c->hidden), sizeof(float) * kMaxItems * kMaxTokens * 32);
+  alloc(reinterpret_cast<void**>(&c->hidden), kHiddenBytes);
+  alloc(reinterpret_cast<void**>(&c->partial), sizeof(float) * kMaxPairs * kMaxBlocks * d);
+  alloc(reinterpret_cast<void**>(&c->gsv), sizeof(float) * kMaxPairs * kMaxBlocks);
   alloc(reinterpret_cast<void**>(&c->ctl), sizeof(LayerCtl));
   alloc(reinterpret_cast<void**>(&c->phases), sizeof(unsigned long long) * 16 * 1024);
   alloc(reinterpret_cast<void**>(&c->status), sizeof(unsigned));
@@ -379,7 +435,7 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
   }
   if (rc == FRC_OK && (cudaMemset(c->ctl, 0, sizeof(LayerCtl)) != cudaSuccess ||
                        cudaMemset(c->status, 0, sizeof(unsigned)) != cudaSuccess ||
-                       cudaMemset(c->hidden, 0, sizeof(float) * kMaxItems * kMaxTokens * 32) != cudaSuccess))
+                       cudaMemset(c->hidden, 0, kHiddenBytes) != cudaSuccess))
     rc = fail(c, FRC_IO, "cudaMemset");
   if (rc != FRC_OK) {
     frc_close(c);
@@ -395,7 +451,7 @@ int frc_close(frc_context* c) {
   if (c->stream) cudaStreamSynchronize(c->stream);
   for (auto& b : c->layer_ptr)
     for (auto& p : b) if (p) cudaFree(p);
-  cudaFree(c->staging); cudaFree(c->hidden); cudaFree(c->phases); cudaFree(c->ctl); cudaFree(c->status);
+  cudaFree(c->staging); cudaFree(c->hidden); cudaFree(c->partial); cudaFree(c->gsv); cudaFree(c->phases); cudaFree(c->ctl); cudaFree(c->status);
   cudaFree(c->d_expert); cudaFree(c->d_gate); cudaFree(c->d_x); cudaFree(c->d_y); cudaFree(c->pool);
   cudaFreeHost(c->h_expert); cudaFreeHost(c->h_gate); cudaFreeHost(c->h_x); cudaFreeHost(c->h_y); cudaFreeHost(c->h_status);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -537,25 +593,26 @@ int frc_run_device_fixed(frc_context* c, unsigned layer, unsigned tokens, const 
     for (unsigned l = 0; l < c->g.layers; ++l) any |= c->layer_ptr[b][l] != nullptr;
     S += any;
   }
-  const size_t need = fixed_need(S, tokens);
-  if (need > kFixedHiddenBytes)
+  const size_t need = fixed_need(S, tokens, c->g.hidden);
+  if (need > kFixedScratchBytes)
     return fail(c, FRC_INVALID, "frc_run_device_fixed: %u tokens over %u slices need %zu bytes of fixed scratch, limit %zu",
-                tokens, S, need, kFixedHiddenBytes);
+                tokens, S, need, kFixedScratchBytes);
   if (cudaSetDevice(c->device) != cudaSuccess) return fail(c, FRC_IO, "cudaSetDevice");
-  float* hidden = nullptr;
+  float* base = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_fixed_mu);
     if (!g_fixed_ptr[c->device]) {
       void* p = nullptr;
-      const cudaError_t e = cudaGetSymbolAddress(&p, g_fixed_hidden);
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_fixed_scratch);
       if (e != cudaSuccess || !p)
         return fail(c, FRC_IO, "cudaGetSymbolAddress(fixed scratch): %s", cudaGetErrorString(e));
       g_fixed_ptr[c->device] = static_cast<float*>(p);
     }
-    hidden = g_fixed_ptr[c->device];
+    base = g_fixed_ptr[c->device];
   }
+  const RunScratch sc{base, base + fixed_partial(S, tokens, c->g.hidden), nullptr};
   return run_device(c, layer, tokens, expert, gate, x, x_add, x_out, y, act, flags, static_cast<cudaStream_t>(stream),
-                    hidden);
+                    &sc);
 }
 
 int frc_status(frc_context* c, void* stream) {

@@ -9,58 +9,14 @@
 
 namespace frc {
 
-constexpr unsigned kThreads = 256;     // 8 warps per CTA
-constexpr unsigned kWarps = kThreads / 32;
-constexpr unsigned kGuNeurons = 8;     // neurons per gate/up unit: one per warp
-constexpr unsigned kGuUnits = 32 / kGuNeurons;
-constexpr unsigned kDnRows = 64;       // down rows per down unit
 constexpr unsigned kDnSplit = 4;       // slice interleave of the down partial sums
 constexpr unsigned kMaxTokens = 16;
 constexpr unsigned kMaxUnique = kMaxTokens * 10 + 1;
-constexpr unsigned kMaxChunks = 8192 / kDnRows;
+constexpr unsigned kMaxPairs = kMaxTokens * 11;  // (expert, token) pairs of one call
 constexpr unsigned kMaxBlocks = 20;
 
 enum : unsigned { kQ80 = 8, kQ4K = 12, kMXFP4 = 39 };
 enum : unsigned { kStNumeric = 1, kStInvalid = 2, kStTimeout = 4 };
-
-// Work-queue and dependency counters of one context.  Zero between launches:
-// the last CTA of every launch restores them.
-struct Ctl {
-  unsigned next;
-  unsigned exited;
-  unsigned abort;      // set by a CTA whose bounded wait ran out; every spin bails
-  unsigned pad;
-  unsigned gu_done[kMaxUnique + 3];
-  unsigned chunk_done[kMaxChunks];
-};
-
-// Dynamic shared memory offsets (bytes), computed on the host.
-struct Smem {
-  unsigned ids, gates, first, uid, umask, ugate, rms;
-  unsigned xq, xp, xs, xv, xf, hq, gs, stage;
-  unsigned stage_bytes, total;
-};
-
-struct LayerArgs {
-  const uint8_t* base[kMaxBlocks];  // this layer's region in each loaded block, ascending
-  const uint16_t* expert;           // [T][10]
-  const float* gate;                // [T][11]
-  const float* x;                   // [T][d]
-  const float* x_add;               // [T][d] or null
-  float* x_out;                     // [T][d] or null
-  float* y;                         // [T][d]
-  float* hidden;                    // [kMaxUnique][S][T][32]
-  float* partial;                   // [kMaxUnique][T][d]
-  Ctl* ctl;
-  unsigned* status;
-  Smem sm;
-  unsigned S, T, d;
-  unsigned norm;                    // FRC_RUN_RMSNORM
-  unsigned gate_type, down_type;
-  unsigned row_bytes, proj_bytes;   // routed gate row / gate projection
-  unsigned shared_row, shared_proj; // shared expert (Q8_0)
-  unsigned slice_bytes;
-};
 
 // ------------------------------------------------------------------ PTX
 

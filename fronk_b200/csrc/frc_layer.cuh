@@ -1,24 +1,33 @@
 // frc_layer.cuh - the MoE layer kernel (sm_100a): one cooperative launch per
-// layer, one 512-thread CTA per SM, a static work split, and every byte of a
-// CTA's weights requested in the first microseconds.
+// layer, one 512-thread CTA per SM, item-major work.
 //
-//   prologue - routing and x are loaded at once; the plan (unique experts,
-//     token masks) is built in parallel.  Warp 0 starts the TMA ring for the
-//     CTA's gate/up rows; warps 8-15 issue the 16-byte cp.async loads of its
-//     down rows; warps 0-7 quantize x meanwhile.
-//   phase 1 - gate/up.  Items (unique expert u, loaded slice s) are laid out
-//     item-major as 32 neurons each; CTA c owns neurons [N*c/G, N*(c+1)/G),
-//     in chunks of up to 16 neurons (one warp each).  Hidden values go to HBM.
+// An item is (unique expert u, loaded slice s): 32 neurons, their gate and up
+// rows and their columns of the down projection, all in one region of the
+// slice (src/q4.c layout, transcoded to device form at load).  Items are
+// dealt to CTAs in snake order, the shared expert's items (twice the bytes)
+// first, so each CTA streams whole items and keeps the hidden activations on
+// chip.
+//
+//   prologue - routing and x are loaded at once and the plan (unique
+//     experts, token masks, (expert, token) pairs) is built.  Warp 8 starts
+//     the TMA ring (cp.async.bulk, one mbarrier a slot) on the CTA's first
+//     chunks; warps 0-7 form the layer input and quantize it meanwhile.
+//   items - per item: gate/up chunks (a warp per neuron, or per row when a
+//     chunk has fewer neurons than warps), SwiGLU in double and the Q8
+//     quantization of the hidden slice (one group of 32) in shared memory,
+//     then the down chunk(s), a thread per row: c = scale * int_dot goes to
+//     the partial buffer [pair][slice][row].  The last warp to finish with a
+//     ring slot refills it, so loads stream with no producer warp.
 //   grid barrier (bounded wait).
-//   phase 2 - down.  CTA c owns output rows [d*c/G, d*(c+1)/G) of every
-//     token: it quantizes the hidden slices it needs (src/q4.c:37-61 scheme,
-//     one group of 32), forms its rows of every expert's down projection and
-//     writes its rows of y (no partial sums leave the CTA).
+//   reduce - CTA k owns rows [d*k/G, d*(k+1)/G) of every token: per (token,
+//     row, routing slot) four slice-interleaved fmaf chains of c * gs,
+//     combined ((p0+p1)+p2)+p3; then the token's routed experts in its own
+//     routing order, then the shared expert.
 //
 // Arithmetic order (restated by the oracle's or_port_run): gate/up lanes take
-// x groups p = lane, lane+32, ...; butterfly sum; per (expert, token, row) four
-// slice-interleaved fmaf chains combined ((p0+p1)+p2)+p3; per token its experts
-// in its own routing order, then the shared expert.
+// x groups p = lane, lane+32, ...; butterfly sum; the reduce above.  Results
+// are bitwise repeatable and a token's output does not depend on the rest of
+// the burst.
 #pragma once
 #include "frc_device.cuh"
 
@@ -26,23 +35,25 @@ namespace frc {
 
 constexpr unsigned kLayerThreads = 512;
 constexpr unsigned kLayerWarps = kLayerThreads / 32;
-constexpr unsigned kActThreads = 256;          // warps 0-7: activations; 8-15: down-row loads
-constexpr unsigned kSlots = 4;                 // TMA ring depth (phase 1)
-constexpr unsigned kGuChunk = 16;              // neurons per gate/up chunk (one per warp)
-constexpr unsigned kMaxItems = kMaxUnique * kMaxBlocks;
+constexpr unsigned kActThreads = 256;          // warps 0-7: activations
+constexpr unsigned kMaxSlots = 8;              // TMA ring depth limit
 constexpr unsigned kXRegs = 4;                 // float4 activations a thread keeps in registers
-constexpr unsigned kMaxRounds = 64;            // 256-float4 rounds of the activation pass
+constexpr unsigned kMaxRounds = 128;           // 256-float4 rounds of the activation pass
 
 struct LayerCtl {
-  unsigned bar_count, bar_gen;  // generation barrier: count returns to 0, gen only grows
+  unsigned long long arrived;   // grid barrier arrivals, all launches (never wraps)
   unsigned abort;               // set by a CTA whose bounded wait ran out
   unsigned pad;
 };
 
+// Byte offsets of one CTA's dynamic shared memory, and the chunking of an
+// item into ring slots (computed on the host).
 struct LayerSmem {
-  unsigned ids, gates, first, uid, umask, ugate, upre, rms, bases, rpart, pairs, tokpair;
-  unsigned xq, xp, xs, xv, xf, split, ring, p2, total;
-  unsigned slot_bytes, p2_bytes, chunk;
+  unsigned ids, gates, first, uid, umask, ugate, upre, rms, bases, rpart, tokpair;
+  unsigned xq, xp, xs, xv, xf, gv, uv, hq, hg, ring, total;
+  unsigned slot_bytes, slots;
+  unsigned kn_r, kn_s;  // neurons per gate/up chunk: routed, shared items (powers of two)
+  unsigned dn_r, dn_s;  // rows per down chunk: routed, shared items (multiples of 16)
 };
 
 struct LayerParams {
@@ -53,41 +64,53 @@ struct LayerParams {
   const float* x_add;
   float* x_out;
   float* y;
-  float* hidden;     // [item][T][32] fp32
+  float* hidden;     // [u*S+s][T][32] fp32 copy of the hidden activations, or null
+  float* partial;    // [pair][S][d] down terms c
+  float* gsv;        // [pair][S] hidden scale x routing weight
   LayerCtl* ctl;
   unsigned* status;
   unsigned long long* phases;  // FRC_PHASES builds: [cta][16] globaltimer stamps
   LayerSmem sm;
-  unsigned S, T, d, norm, rmax;
+  unsigned S, T, d, norm;
   unsigned gate_type, down_type;
   unsigned row_bytes, proj_bytes, shared_row, shared_proj, slice_bytes;
 };
 
-__device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Programmatic dependent launch: the next launch on the stream may start its
+// CTAs (as SMs free up) once every CTA of this one has signalled; a launch
+// waits for its predecessor's completion and memory before it reads x or
+// writes anything the predecessor reads.  Both are no-ops without the launch
+// attribute.
+__device__ __forceinline__ void pdl_signal() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 // Barrier among the activation warps (0-7) only.
 __device__ __forceinline__ void act_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Barrier among the plan warps (8-15) only.
+__device__ __forceinline__ void plan_sync() { asm volatile("bar.sync 2, 256;" ::: "memory"); }
 
-// Bounded generation barrier over the co-resident grid.
+// Bounded barrier over the co-resident grid, one round trip: every CTA adds
+// itself to a counter that only grows and waits for the next multiple of the
+// grid size.  A timed-out launch leaves the counter off that lattice;
+// frc_status zeroes it before anything runs again.
 __device__ __forceinline__ bool grid_sync(LayerCtl* ctl, unsigned* flag_smem) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    const unsigned gen = ld_acquire(&ctl->bar_gen);
+    const unsigned long long old = atomicAdd(&ctl->arrived, 1ull);
+    const unsigned long long target = (old / gridDim.x + 1) * gridDim.x;
     bool ok = true;
-    if (atomicAdd(&ctl->bar_count, 1u) == gridDim.x - 1) {
-      atomicExch(&ctl->bar_count, 0u);
-      __threadfence();
-      st_release(&ctl->bar_gen, gen + 1);
-    } else {
-      const uint64_t start = globaltimer();
-      unsigned spins = 0;
-      while (ld_acquire(&ctl->bar_gen) == gen) {
-        if ((++spins & 255) == 0 && (globaltimer() - start > kWaitNs || ld_acquire(&ctl->abort))) {
-          ok = false;
-          break;
-        }
+    const uint64_t start = globaltimer();
+    unsigned spins = 0;
+    while (ld_acquire64(&ctl->arrived) < target) {
+      if ((++spins & 255) == 0 && (globaltimer() - start > kWaitNs || ld_acquire(&ctl->abort))) {
+        ok = false;
+        break;
       }
     }
     *flag_smem = ok;
@@ -97,8 +120,10 @@ __device__ __forceinline__ bool grid_sync(LayerCtl* ctl, unsigned* flag_smem) {
 }
 
 // Compile-time phase stamps (the reference's FR_PHASES counterpart,
-// backends/avx2.c:38-42): entry, plan, loads issued, activations, phase 1,
-// barrier, phase 2, exit.
+// backends/avx2.c:38-42): 0 entry, 8 prologue loads, 10 plan, 1 first copies
+// issued, 2 norm sums, 3 activations, 15/12 first/second chunk landed, 9
+// first item's gate/up, 13 its hidden slice, 14 its down chunk landed, 6 its
+// down done, 4 items done, 5 grid barrier, 11 reduce chains, 7 exit.
 #ifdef FRC_PHASES
 #define PHASE_AT(k, th) \
   do { if (threadIdx.x == (th) && a.phases) a.phases[blockIdx.x * 16 + (k)] = globaltimer(); } while (0)
@@ -110,8 +135,9 @@ __device__ __forceinline__ bool grid_sync(LayerCtl* ctl, unsigned* flag_smem) {
 template <int ACT>
 __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const LayerParams a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);                 // kSlots mbarriers
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);                // kMaxSlots mbarriers
   unsigned* misc = reinterpret_cast<unsigned*>(smem + 64);           // 64 words
+  unsigned* s_cnt = misc + 40;                                       // ring slot release counts
   uint16_t* s_ids = reinterpret_cast<uint16_t*>(smem + a.sm.ids);
   float* s_g = reinterpret_cast<float*>(smem + a.sm.gates);
   int* s_first = reinterpret_cast<int*>(smem + a.sm.first);
@@ -120,14 +146,13 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
   float* s_ugate = reinterpret_cast<float*>(smem + a.sm.ugate);
   unsigned* s_upre = reinterpret_cast<unsigned*>(smem + a.sm.upre);  // first pair of each expert
   float* s_rms = reinterpret_cast<float*>(smem + a.sm.rms);
-  const uint8_t** s_base = reinterpret_cast<const uint8_t**>(smem + a.sm.bases);
   float* s_rpart = reinterpret_cast<float*>(smem + a.sm.rpart);      // [round][warp] sums of squares
-  uint16_t* s_pair = reinterpret_cast<uint16_t*>(smem + a.sm.pairs);   // pair -> expert << 5 | token
   uint16_t* s_tokpair = reinterpret_cast<uint16_t*>(smem + a.sm.tokpair);  // [token][11] -> pair
+  float* s_gv = reinterpret_cast<float*>(smem + a.sm.gv);            // [neuron][k] gate dots
+  float* s_uv = reinterpret_cast<float*>(smem + a.sm.uv);            // [neuron][k] up dots
+  uint8_t* s_hq = smem + a.sm.hq;                                    // [k][32] int8, or [k][32] f32
   uint8_t* ring = smem + a.sm.ring;
-  uint8_t* p2 = smem + a.sm.p2;
-  float* split = reinterpret_cast<float*>(smem + a.sm.split);      // [pair][row][4]
-  const unsigned SLOT = a.sm.slot_bytes;
+  const unsigned SLOT = a.sm.slot_bytes, K = a.sm.slots;
 
   const unsigned tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const unsigned T = a.T, S = a.S, d = a.d, P = d / 64, G = gridDim.x, cta = blockIdx.x;
@@ -135,235 +160,90 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
   const bool xregs = rounds <= kXRegs;
 
   PHASE(0);
-  // ------------------------------------------------ loads that need nothing
-  float4 xv4[kXRegs];
-  if (tid < kActThreads && xregs) {
-    const float4* x4 = reinterpret_cast<const float4*>(a.x);
-    const float4* xa4 = reinterpret_cast<const float4*>(a.x_add);
-#pragma unroll
-    for (unsigned r = 0; r < kXRegs; ++r) {
-      const unsigned f = r * kActThreads + tid;
-      xv4[r] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      if (r < rounds && f < nvec) {
-        xv4[r] = x4[f];
-        if (xa4) {
-          const float4 w = xa4[f];
-          xv4[r].x = __fadd_rn(xv4[r].x, w.x); xv4[r].y = __fadd_rn(xv4[r].y, w.y);
-          xv4[r].z = __fadd_rn(xv4[r].z, w.z); xv4[r].w = __fadd_rn(xv4[r].w, w.w);
+  pdl_signal();
+  // -------------------------------------------------- this CTA's items
+  // Global item order: the shared expert's S items, then routed (u, s)
+  // expert-major.  Round r deals items r*G .. r*G+G-1, alternating direction.
+  // UR (routed unique experts) and SH (slices of the shared expert, 0 when
+  // no token uses it) come from the plan; setup() derives this CTA's list.
+  unsigned UR = 0, SH = 0, U = 0, NI = 0, n_my = 0, nsh = 0, n_ch = 0;
+  auto item_at = [&](unsigned r) { return r * G + ((r & 1) ? G - 1 - cta : cta); };
+  auto item_us = [&](unsigned j, unsigned& u, unsigned& s) {
+    if (j < SH) { u = UR; s = j; }
+    else { u = (j - SH) / S; s = (j - SH) % S; }
+  };
+  const unsigned kn_r = a.sm.kn_r, kn_s = a.sm.kn_s, dn_r = a.sm.dn_r, dn_s = a.sm.dn_s;
+  const unsigned ngu_r = 32 / kn_r, ngu_s = 32 / kn_s;
+  const unsigned ndn_r = (d + dn_r - 1) / dn_r, ndn_s = (d + dn_s - 1) / dn_s;
+  const unsigned ch_r = ngu_r + ndn_r, ch_s = ngu_s + ndn_s;
+  const unsigned ss_r = a.down_type == kQ80 ? 2 : 1, pb_r = a.down_type == kQ80 ? 32 : 16;
+  auto setup = [&]() {
+    UR = misc[4];
+    U = UR + (misc[5] ? 1 : 0);
+    SH = misc[5] ? S : 0;
+    NI = U * S;
+    n_my = 0;
+    while (item_at(n_my) < NI) ++n_my;
+    nsh = 0;
+    while (nsh < n_my && item_at(nsh) < SH) ++nsh;
+    n_ch = nsh * ch_s + (n_my - nsh) * ch_r;
+  };
+
+  // chunk c of this CTA -> (item round r, chunk k within the item)
+  auto chunk_at = [&](unsigned c, unsigned& r, unsigned& k) {
+    if (c < nsh * ch_s) { r = c / ch_s; k = c % ch_s; }
+    else { r = nsh + (c - nsh * ch_s) / ch_r; k = (c - nsh * ch_s) % ch_r; }
+  };
+  // Gate/up chunk k: gate rows k*kn.. then up rows k*kn.. (two copies).
+  // Down chunk: rows [r0, r0+nr): their scales, then their payloads.
+  auto issue = [&](unsigned c) {
+    unsigned r, k, u, s;
+    chunk_at(c, r, k);
+    item_us(item_at(r), u, s);
+    const bool sh = u >= UR;
+    const unsigned rowb = sh ? a.shared_row : a.row_bytes, proj = sh ? a.shared_proj : a.proj_bytes;
+    const unsigned kn = sh ? kn_s : kn_r, ngu = sh ? ngu_s : ngu_r, dn = sh ? dn_s : dn_r;
+    const unsigned ss = sh ? 2 : ss_r, pb = sh ? 32 : pb_r;
+    const uint8_t* src = a.base[s] + static_cast<size_t>(s_uid[u]) * a.slice_bytes;
+    const unsigned slot = c % K;
+    uint8_t* dst = ring + slot * SLOT;
+    if (k < ngu) {
+      const unsigned bytes = kn * rowb;
+      mbar_expect_tx(&full[slot], 2 * bytes);
+      bulk_g2s(dst, src + k * bytes, bytes, &full[slot]);
+      bulk_g2s(dst + bytes, src + proj + k * bytes, bytes, &full[slot]);
+    } else {
+      const unsigned r0 = (k - ngu) * dn, nr = min(dn, d - r0);
+      const uint8_t* down = src + 2 * proj;
+      mbar_expect_tx(&full[slot], nr * (ss + pb));
+      bulk_g2s(dst, down + r0 * ss, nr * ss, &full[slot]);
+      bulk_g2s(dst + nr * ss, down + d * ss + r0 * pb, nr * pb, &full[slot]);
+    }
+  };
+
+  if (warp < kActThreads / 32) {
+    // ------------------------------------------- warps 0-7: activations
+    // (needs only x: runs while warps 8-15 plan and start the weight copies)
+    pdl_wait();
+    float4 xv4[kXRegs];
+    if (xregs) {
+      const float4* x4 = reinterpret_cast<const float4*>(a.x);
+      const float4* xa4 = reinterpret_cast<const float4*>(a.x_add);
+  #pragma unroll
+      for (unsigned r = 0; r < kXRegs; ++r) {
+        const unsigned f = r * kActThreads + tid;
+        xv4[r] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (r < rounds && f < nvec) {
+          xv4[r] = x4[f];
+          if (xa4) {
+            const float4 w = xa4[f];
+            xv4[r].x = __fadd_rn(xv4[r].x, w.x); xv4[r].y = __fadd_rn(xv4[r].y, w.y);
+            xv4[r].z = __fadd_rn(xv4[r].z, w.z); xv4[r].w = __fadd_rn(xv4[r].w, w.w);
+          }
         }
       }
     }
-  }
-  if (tid == 0) {
-    for (unsigned i = 0; i < kSlots; ++i) mbar_init(&bar[i], 1);
-    fence_mbar_init();
-  }
-  for (unsigned i = tid; i < T * 10; i += kLayerThreads) s_ids[i] = a.expert[i];
-  for (unsigned i = tid; i < T * 11; i += kLayerThreads) s_g[i] = a.gate[i];
-  for (unsigned i = tid; i < S; i += kLayerThreads) s_base[i] = a.base[i];
-  for (unsigned i = tid; i < 512; i += kLayerThreads) s_first[i] = 0x7fffffff;
-  for (unsigned i = tid; i < kMaxUnique; i += kLayerThreads) s_umask[i] = 0;
-  for (unsigned i = tid; i < kMaxUnique * T; i += kLayerThreads) s_ugate[i] = 0.0f;
-  __syncthreads();
-  PHASE(8);
 
-  // ---------------------------------------------------------------- plan
-  if (T == 1) {
-    // one token: its ten experts in request order are the unique experts
-    if (tid < 10) {
-      unsigned id = s_ids[tid];
-      if (id >= 512) {
-        atomicOr(a.status, kStInvalid);
-        id = 0;  // keeps every address in range; the launch reports INVALID
-      }
-      s_uid[tid] = static_cast<uint16_t>(id);
-      s_umask[tid] = 1;
-      s_ugate[tid] = s_g[tid];
-    }
-    if (tid == 0) misc[4] = 10;
-  } else {
-  {
-    bool invalid = false;
-    for (unsigned i = tid; i < T * 10; i += kLayerThreads) {
-      const unsigned id = s_ids[i];
-      if (id < 512) atomicMin(&s_first[id], static_cast<int>(i));
-      else invalid = true;
-    }
-    if (invalid) atomicOr(a.status, kStInvalid);
-  }
-  __syncthreads();
-  {
-    const unsigned i = tid;  // T*10 <= 160 < kLayerThreads
-    const bool first = i < T * 10 && s_ids[i] < 512 && s_first[s_ids[i]] == static_cast<int>(i);
-    const unsigned ballot = __ballot_sync(0xffffffffu, first);
-    if (lane == 0) misc[16 + warp] = __popc(ballot);
-    __syncthreads();
-    unsigned off = 0;
-    for (unsigned w = 0; w < warp; ++w) off += misc[16 + w];
-    const unsigned rank = off + __popc(ballot & ((1u << lane) - 1));
-    if (tid == kLayerThreads - 1) misc[4] = off + __popc(ballot);  // routed experts
-    if (first) s_uid[rank] = s_ids[i];
-    __syncthreads();
-    if (first) s_first[s_ids[i]] = -1 - static_cast<int>(rank);
-    __syncthreads();
-  }
-  for (unsigned i = tid; i < T * 10; i += kLayerThreads) {
-    const unsigned id = s_ids[i];
-    if (id >= 512) continue;
-    const unsigned u = static_cast<unsigned>(-1 - s_first[id]), t = i / 10;
-    atomicOr(&s_umask[u], 1u << t);
-    s_ugate[u * T + t] = s_g[t * 11 + i % 10];
-  }
-  }
-  __syncthreads();
-  const unsigned UR = misc[4];  // routed experts
-  unsigned shared_mask = 0;
-  for (unsigned t = 0; t < T; ++t)
-    if (s_g[t * 11 + 10] != 0.0f) shared_mask |= 1u << t;
-  const unsigned U = UR + (shared_mask ? 1 : 0);
-  if (shared_mask) {
-    if (tid == 0) {
-      s_uid[UR] = 512;
-      s_umask[UR] = shared_mask;
-    }
-    for (unsigned t = tid; t < T; t += kLayerThreads) s_ugate[UR * T + t] = s_g[t * 11 + 10];
-  }
-  __syncthreads();
-  if (warp == 0) {  // pair offsets: exclusive scan of the token counts, 6 experts a lane
-    unsigned cnt[6], tot = 0;
-#pragma unroll
-    for (unsigned k = 0; k < 6; ++k) {
-      const unsigned u = lane * 6 + k;
-      cnt[k] = u < U ? __popc(s_umask[u]) : 0;
-      tot += cnt[k];
-    }
-    unsigned inc = tot;
-#pragma unroll
-    for (unsigned o = 1; o < 32; o <<= 1) {
-      const unsigned v = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += v;
-    }
-    unsigned run = inc - tot;
-#pragma unroll
-    for (unsigned k = 0; k < 6; ++k) {
-      const unsigned u = lane * 6 + k;
-      if (u <= U) s_upre[u] = run;
-      run += cnt[k];
-    }
-  }
-  __syncthreads();
-  for (unsigned u = tid; u < U; u += kLayerThreads) {  // pair -> (expert, token) and (token, slot) -> pair
-    unsigned mm = s_umask[u], k = s_upre[u];
-    while (mm) {
-      const unsigned t = __ffs(mm) - 1;
-      mm &= mm - 1;
-      s_pair[k++] = static_cast<uint16_t>(u << 5 | t);
-    }
-  }
-  for (unsigned i = tid; i < T * 11; i += kLayerThreads) {
-    const unsigned t = i / 11, e = i % 11;
-    unsigned pair = 0xffff;
-    if (e < 10) {
-      const unsigned id = s_ids[t * 10 + e];
-      if (id < 512) {
-        const unsigned u = T == 1 ? e : static_cast<unsigned>(-1 - s_first[id]);
-        pair = s_upre[u] + __popc(s_umask[u] & ((1u << t) - 1));
-      }
-    } else if (shared_mask >> t & 1) {
-      pair = s_upre[UR] + __popc(shared_mask & ((1u << t) - 1));
-    }
-    s_tokpair[i] = static_cast<uint16_t>(pair);
-  }
-  __syncthreads();
-
-  PHASE(10);
-  // -------------------------------------------------- this CTA's work
-  const unsigned NR = UR * S * 32, N1 = U * S * 32;
-  const unsigned n_begin = N1 * cta / G, n_end = N1 * (cta + 1) / G;  // N1*G < 2^32
-  const unsigned r0 = d * cta / G, r1 = d * (cta + 1) / G;
-  const unsigned R = r1 - r0;
-  // gate/up chunks: a grid of cr neurons over routed items, cs over shared ones
-  // (both divide 32, so no chunk crosses an item)
-  const unsigned cr = a.sm.chunk;
-  unsigned cs = kGuChunk;
-  while (cs > 2 && 2 * cs * a.shared_row > SLOT) cs >>= 1;
-  const unsigned m0 = n_begin / cr, m1 = n_begin < NR ? (min(n_end, NR) + cr - 1) / cr : m0;
-  const unsigned n_rch = m1 - m0;
-  const unsigned s_lo = n_end > NR ? (max(n_begin, NR) - NR) / cs : 0;
-  const unsigned n_sch = n_end > NR ? (n_end - NR + cs - 1) / cs - s_lo : 0;
-  const unsigned n_gu = n_rch + n_sch;
-  auto chunk = [&](unsigned jj, unsigned& lo, unsigned& hi) {
-    if (jj < n_rch) {
-      lo = max(n_begin, (m0 + jj) * cr);
-      hi = min(min(n_end, NR), (m0 + jj + 1) * cr);
-    } else {
-      const unsigned k = s_lo + jj - n_rch;
-      lo = max(n_begin, NR + k * cs);
-      hi = min(n_end, NR + (k + 1) * cs);
-    }
-  };
-  // One item's piece of the down projection for rows [r0, r1): the scale
-  // bytes widened to 16-byte boundaries, then the rows' payloads.
-  const unsigned mx_lo = r0 & ~15u, mx_hi = (r1 + 15) & ~15u;            // MXFP4: 1 scale byte a row
-  const unsigned q8_lo = (2 * r0) & ~15u, q8_hi = (2 * r1 + 15) & ~15u;  // Q8_0: 2 bytes a row
-  const unsigned piece_mx = (mx_hi - mx_lo) + 16 * R, piece_q8 = (q8_hi - q8_lo) + 32 * R;
-  const unsigned piece_r = a.down_type == kQ80 ? piece_q8 : piece_mx;
-  // phase-2 batches: every expert at once when it fits, else k at a time
-  const unsigned ent_bytes = ACT == FRC_ACT_Q8 ? 36 : 132;  // staged hidden slice + its scale
-  const unsigned all_bytes = S * (UR * piece_r + (U - UR) * piece_q8) + S * s_upre[U] * ent_bytes;
-  const unsigned per_batch =
-      all_bytes <= a.sm.p2_bytes ? U : max(1u, a.sm.p2_bytes / (S * piece_q8 + S * T * ent_bytes));
-  const unsigned n_batch = R ? (U + per_batch - 1) / per_batch : 0;
-  // offset of item (u, s) in the batch that starts at expert u0
-  auto piece_off = [&](unsigned u0, unsigned u, unsigned s) {
-    const unsigned ur = min(u, UR) > u0 ? min(u, UR) - u0 : 0;
-    return ur * S * piece_r + s * (u >= UR ? piece_q8 : piece_r);
-  };
-  auto batch_pieces = [&](unsigned u0, unsigned u1) {
-    const unsigned ur = min(u1, UR) > u0 ? min(u1, UR) - u0 : 0;
-    return S * (ur * piece_r + (u1 > UR ? piece_q8 : 0));
-  };
-
-  // ------------------------------------------------ phase-1 producer (TMA)
-  auto issue = [&](unsigned jj) {  // one lane per chunk
-    unsigned lo, hi;
-    chunk(jj, lo, hi);
-    const unsigned item = lo / 32, u = item / S, si = item % S, cnt = hi - lo;
-    const bool shared = u >= UR;
-    const unsigned rowb = shared ? a.shared_row : a.row_bytes, proj = shared ? a.shared_proj : a.proj_bytes;
-    const uint8_t* src = s_base[si] + static_cast<size_t>(s_uid[u]) * a.slice_bytes + (lo % 32) * rowb;
-    const unsigned slot = jj % kSlots;
-    uint8_t* dst = ring + slot * SLOT;
-    mbar_expect_tx(&bar[slot], 2 * cnt * rowb);
-    bulk_g2s(dst, src, cnt * rowb, &bar[slot]);
-    bulk_g2s(dst + cnt * rowb, src + proj, cnt * rowb, &bar[slot]);
-  };
-  if (warp == 0 && lane < kSlots && lane < n_gu) issue(lane);
-
-  // --------------------------------------- phase-2 loads: one warp per item
-  auto issue_batch = [&](unsigned bi, unsigned w0, unsigned nw) {
-    const unsigned u0 = bi * per_batch, u1 = min(U, u0 + per_batch);
-    for (unsigned it = w0; it < (u1 - u0) * S; it += nw) {
-      const unsigned u = u0 + it / S, s = it % S;
-      const bool q8 = u >= UR || a.down_type == kQ80;
-      const unsigned proj = u >= UR ? a.shared_proj : a.proj_bytes;
-      const uint8_t* down = s_base[s] + static_cast<size_t>(s_uid[u]) * a.slice_bytes + 2 * proj;
-      const unsigned lo = q8 ? q8_lo : mx_lo, hi = q8 ? q8_hi : mx_hi, pb = q8 ? 32 : 16;
-      const unsigned ce = (hi - lo) / 16, cpe = ce + pb * R / 16;
-      uint8_t* dst = p2 + piece_off(u0, u, s);
-      for (unsigned k = lane; k < cpe; k += 32)
-        cp_async16(dst + 16 * k, k < ce ? down + lo + 16 * k : down + (q8 ? 2 : 1) * d + pb * r0 + 16 * (k - ce));
-    }
-    cp_async_commit();
-  };
-  PHASE(1);
-
-  if (warp >= kActThreads / 32) {
-    // ---------------------------------------- warps 8-15: down-row loads
-    if (n_batch) issue_batch(0, warp - kActThreads / 32, kLayerWarps - kActThreads / 32);
-    PHASE_AT(11, kActThreads);
-  } else {
-    // --------------------------------------------- warps 0-7: activations
     const float4* x4 = reinterpret_cast<const float4*>(a.x);
     const float4* xa4 = reinterpret_cast<const float4*>(a.x_add);
     auto load4 = [&](unsigned f, unsigned r) {
@@ -450,243 +330,439 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
       }
     }
     if (bad) atomicOr(a.status, kStNumeric);
-    PHASE(14);
+  } else {
+    // ------------------------------------------------ warps 8-15: plan
+    const unsigned ptid = tid - kActThreads, pw = warp - kActThreads / 32;
+    if (ptid < kMaxSlots) s_cnt[ptid] = 0;
+    if (T == 1) {
+      // one token: its ten experts in request order are the unique experts,
+      // each with one (expert, token) pair
+      if (warp == 8) {
+        unsigned id = 0;
+        float gv = 0.0f;
+        if (lane < 10) {
+          id = a.expert[lane];
+          gv = a.gate[lane];
+          if (id >= 512) {
+            atomicOr(a.status, kStInvalid);
+            id = 0;  // keeps every address in range; the launch reports INVALID
+          }
+        }
+        const float sg = a.gate[10];
+        if (lane < 10) {
+          s_uid[lane] = static_cast<uint16_t>(id);
+          s_umask[lane] = 1;
+          s_ugate[lane] = gv;
+        }
+        if (lane == 10 && sg != 0.0f) {
+          s_uid[10] = 512;
+          s_umask[10] = 1;
+          s_ugate[10] = sg;
+        }
+        if (lane < 12) s_upre[lane] = lane;
+        if (lane < 11) s_tokpair[lane] = static_cast<uint16_t>(lane < 10 ? lane : (sg != 0.0f ? 10u : 0xffffu));
+        if (lane == 0) {
+          misc[4] = 10;
+          misc[5] = sg != 0.0f ? 1u : 0u;
+        }
+        PHASE_AT(8, kActThreads);
+      }
+    } else {
+      for (unsigned i = ptid; i < T * 10; i += kActThreads) s_ids[i] = a.expert[i];
+      for (unsigned i = ptid; i < T * 11; i += kActThreads) s_g[i] = a.gate[i];
+      for (unsigned i = ptid; i < 512; i += kActThreads) s_first[i] = 0x7fffffff;
+      for (unsigned i = ptid; i < kMaxUnique; i += kActThreads) s_umask[i] = 0;
+      for (unsigned i = ptid; i < kMaxUnique * T; i += kActThreads) s_ugate[i] = 0.0f;
+      plan_sync();
+      PHASE_AT(8, kActThreads);
+      bool invalid = false;
+      for (unsigned i = ptid; i < T * 10; i += kActThreads) {
+        const unsigned id = s_ids[i];
+        if (id < 512) atomicMin(&s_first[id], static_cast<int>(i));
+        else invalid = true;
+      }
+      if (invalid) atomicOr(a.status, kStInvalid);
+      plan_sync();
+      // unique experts in first-appearance order: rank = earlier first appearances
+      const unsigned i = ptid;  // T*10 <= 160 < 256
+      const bool first = i < T * 10 && s_ids[i] < 512 && s_first[s_ids[i]] == static_cast<int>(i);
+      const unsigned ballot = __ballot_sync(0xffffffffu, first);
+      if (lane == 0) misc[16 + pw] = __popc(ballot);
+      plan_sync();
+      unsigned off = 0;
+      for (unsigned w = 0; w < pw; ++w) off += misc[16 + w];
+      const unsigned rank = off + __popc(ballot & ((1u << lane) - 1));
+      if (ptid == kActThreads - 1) misc[4] = off + __popc(ballot);  // routed experts
+      if (first) s_uid[rank] = s_ids[i];
+      plan_sync();
+      if (first) s_first[s_ids[i]] = -1 - static_cast<int>(rank);
+      plan_sync();
+      for (unsigned k = ptid; k < T * 10; k += kActThreads) {
+        const unsigned id = s_ids[k];
+        if (id >= 512) continue;
+        const unsigned u = static_cast<unsigned>(-1 - s_first[id]), t = k / 10;
+        atomicOr(&s_umask[u], 1u << t);
+        s_ugate[u * T + t] = s_g[t * 11 + k % 10];
+      }
+      plan_sync();
+      const unsigned ur = misc[4];
+      unsigned shared_mask = 0;
+      for (unsigned t = 0; t < T; ++t)
+        if (s_g[t * 11 + 10] != 0.0f) shared_mask |= 1u << t;
+      const unsigned nu = ur + (shared_mask ? 1 : 0);
+      if (ptid == 0) {
+        misc[5] = shared_mask;
+        if (shared_mask) {
+          s_uid[ur] = 512;
+          s_umask[ur] = shared_mask;
+        }
+      }
+      if (shared_mask)
+        for (unsigned t = ptid; t < T; t += kActThreads) s_ugate[ur * T + t] = s_g[t * 11 + 10];
+      plan_sync();
+      if (warp == 8) {  // pair offsets: exclusive scan of the token counts, 6 experts a lane
+        unsigned cnt[6], tot = 0;
+    #pragma unroll
+        for (unsigned k = 0; k < 6; ++k) {
+          const unsigned u = lane * 6 + k;
+          cnt[k] = u < nu ? __popc(s_umask[u]) : 0;
+          tot += cnt[k];
+        }
+        unsigned inc = tot;
+    #pragma unroll
+        for (unsigned o = 1; o < 32; o <<= 1) {
+          const unsigned v = __shfl_up_sync(0xffffffffu, inc, o);
+          if (lane >= o) inc += v;
+        }
+        unsigned run = inc - tot;
+    #pragma unroll
+        for (unsigned k = 0; k < 6; ++k) {
+          const unsigned u = lane * 6 + k;
+          if (u <= nu) s_upre[u] = run;
+          run += cnt[k];
+        }
+      }
+      plan_sync();
+      for (unsigned k = ptid; k < T * 11; k += kActThreads) {  // (token, routing slot) -> pair
+        const unsigned t = k / 11, e = k % 11;
+        unsigned pair = 0xffff;
+        if (e < 10) {
+          const unsigned id = s_ids[t * 10 + e];
+          if (id < 512) {
+            const unsigned u = static_cast<unsigned>(-1 - s_first[id]);
+            pair = s_upre[u] + __popc(s_umask[u] & ((1u << t) - 1));
+          }
+        } else if (shared_mask >> t & 1) {
+          pair = s_upre[ur] + __popc(shared_mask & ((1u << t) - 1));
+        }
+        s_tokpair[k] = static_cast<uint16_t>(pair);
+      }
+    }
+    plan_sync();
+    PHASE_AT(10, kActThreads);
+    if (warp == 8) {  // the first K chunks, while the activations are still being formed
+      if (lane == 0) {
+        for (unsigned k = 0; k < K; ++k) mbar_init(&full[k], 1);
+        fence_mbar_init();
+      }
+      __syncwarp();
+      setup();
+      if (lane < K && lane < n_ch) issue(lane);
+      PHASE_AT(1, kActThreads);
+    }
+    pdl_wait();
   }
   __syncthreads();
+  setup();
   PHASE(3);
 
-  // ------------------------------------------------------------- phase 1
-  bool aborted = false;
-  unsigned j = 0;
-  for (; j < n_gu; ++j) {
-    const bool ok = mbar_wait(&bar[j % kSlots], (j / kSlots) & 1);
-    if (__syncthreads_or(!ok)) {
-      if (tid == 0) {
-        atomicOr(a.status, kStTimeout);
-        atomicExch(&a.ctl->abort, 1u);
+  // --------------------------------------------------------------- items
+  // A warp done with ring chunk c counts itself out of the slot; the last of
+  // the 16 (fence.cta orders their shared-memory reads first) refills the
+  // slot with chunk c+K.  A warp whose wait ran out stops counting, so
+  // nothing is issued into a slot that a copy may still be writing.
+  bool timed_out = false, aborted = false;  // warp-uniform, block-uniform
+  auto release = [&](unsigned c) {
+    __syncwarp();
+    if (lane == 0 && !timed_out) {
+      __threadfence_block();
+      const unsigned slot = c % K, round = c / K;
+      if (atomicAdd(&s_cnt[slot], 1u) == kLayerWarps * (round + 1) - 1 && c + K < n_ch) {
+        __threadfence_block();
+        fence_proxy_async();
+        issue(c + K);
       }
-      aborted = true;
-      break;
     }
-    if (j == 0) PHASE(15);
-    unsigned lo, hi;
-    chunk(j, lo, hi);
-    const uint8_t* slot = ring + (j % kSlots) * SLOT;
-    const unsigned item = lo / 32, u = item / S, nl = lo % 32, cnt = hi - lo;
-    const bool shared = u >= UR;
-    const unsigned type = shared ? kQ80 : a.gate_type;
-    const unsigned rowb = shared ? a.shared_row : a.row_bytes, nb = d / 32;
-    bool bad = false;
-    if (warp < cnt) {
-      const unsigned n = nl + warp;
-      const uint8_t* grow = slot + warp * rowb;
-      const uint8_t* urow = slot + (cnt + warp) * rowb;
-      unsigned mm = s_umask[u];
-      while (mm) {
-        const unsigned t = __ffs(mm) - 1;
-        mm &= mm - 1;
-        float ag = 0.0f, au = 0.0f;
-        if (ACT == FRC_ACT_Q8) {
-          const uint8_t* xq = smem + (type == kMXFP4 ? a.sm.xp : a.sm.xq) + t * d;
-          const float* xs = reinterpret_cast<const float*>(smem + a.sm.xs) + t * P;
-          const float* xv = reinterpret_cast<const float*>(smem + a.sm.xv) + t * 2 * P;
-          for (unsigned p = lane; p < P; p += 32) {
-            uint32_t xw[16];
-            load_x16(xq, p, xw);
-            float tg, tu;
-            if (type == kQ4K) {
-              const float v0 = xv[2 * p], v1 = xv[2 * p + 1];
-              tg = term_q4k(grow, p, xw, v0, v1, bad);
-              tu = term_q4k(urow, p, xw, v0, v1, bad);
-            } else if (type == kMXFP4) {
-              tg = term_mxfp4(grow, nb, p, xw, bad);
-              tu = term_mxfp4(urow, nb, p, xw, bad);
+  };
+  auto wait_chunk = [&](unsigned c) {
+    if (!timed_out) timed_out = __any_sync(0xffffffffu, !mbar_wait(&full[c % K], (c / K) & 1));
+    return !timed_out;
+  };
+  unsigned c = 0;
+  bool bad = false;
+  for (unsigned r = 0; r < n_my && !aborted; ++r) {
+    unsigned u, s;
+    item_us(item_at(r), u, s);
+    const bool sh = u >= UR;
+    const unsigned type = sh ? kQ80 : a.gate_type, dtype = sh ? kQ80 : a.down_type;
+    const unsigned rowb = sh ? a.shared_row : a.row_bytes, nb = d / 32;
+    const unsigned kn = sh ? kn_s : kn_r, ngu = sh ? ngu_s : ngu_r, dn = sh ? dn_s : dn_r, ndn = sh ? ndn_s : ndn_r;
+    const unsigned mask = s_umask[u], nt = __popc(mask), gp0 = s_upre[u];
+    // gate/up: a task is a neuron (both rows, sharing the x loads) when the
+    // chunk has a neuron for every warp, else a single row
+    const bool by_neuron = kn >= kLayerWarps;
+    const unsigned ntask = by_neuron ? kn : 2 * kn;
+    for (unsigned k = 0; k < ngu; ++k, ++c) {
+      if (wait_chunk(c)) {
+        if (c == 0) PHASE(15);
+        if (c == 1) PHASE(12);
+        const uint8_t* slot = ring + (c % K) * SLOT;
+        for (unsigned task = warp; task < ntask; task += kLayerWarps) {
+          const bool up_only = !by_neuron && task >= kn;
+          const unsigned nl = up_only ? task - kn : task;   // neuron within the chunk
+          const uint8_t* r1 = slot + (up_only ? kn + nl : nl) * rowb;   // gate row (or the up row)
+          const uint8_t* r2 = slot + (kn + nl) * rowb;                   // up row when by_neuron
+          const unsigned n = k * kn + nl;
+          unsigned mm = mask;
+          for (unsigned kk = 0; kk < nt; ++kk) {
+            const unsigned t = __ffs(mm) - 1;
+            mm &= mm - 1;
+            float a1 = 0.0f, a2 = 0.0f;
+            if (ACT == FRC_ACT_Q8) {
+              const uint8_t* xq = smem + (type == kMXFP4 ? a.sm.xp : a.sm.xq) + t * d;
+              const float* xs = reinterpret_cast<const float*>(smem + a.sm.xs) + t * P;
+              const float* xv = reinterpret_cast<const float*>(smem + a.sm.xv) + t * 2 * P;
+              for (unsigned p = lane; p < P; p += 32) {
+                uint32_t xw[16];
+                load_x16(xq, p, xw);
+                float t1, t2 = 0.0f;
+                if (type == kQ4K) {
+                  const float v0 = xv[2 * p], v1 = xv[2 * p + 1];
+                  t1 = term_q4k(r1, p, xw, v0, v1, bad);
+                  if (by_neuron) t2 = term_q4k(r2, p, xw, v0, v1, bad);
+                } else if (type == kMXFP4) {
+                  t1 = term_mxfp4(r1, nb, p, xw, bad);
+                  if (by_neuron) t2 = term_mxfp4(r2, nb, p, xw, bad);
+                } else {
+                  t1 = term_q80(r1, nb, p, xw, bad);
+                  if (by_neuron) t2 = term_q80(r2, nb, p, xw, bad);
+                }
+                a1 = __fmaf_rn(xs[p], t1, a1);
+                a2 = __fmaf_rn(xs[p], t2, a2);
+              }
             } else {
-              tg = term_q80(grow, nb, p, xw, bad);
-              tu = term_q80(urow, nb, p, xw, bad);
+              const float* xf = reinterpret_cast<const float*>(smem + a.sm.xf) + t * d;
+              for (unsigned p = lane; p < P; p += 32)
+                for (unsigned jj = 0; jj < 64; ++jj) {
+                  const unsigned e = 64 * p + jj;
+                  const float w1 = weight_any(r1, type, d, e);
+                  bad |= !isfinite(w1);
+                  a1 = __fmaf_rn(w1, xf[e], a1);
+                  if (by_neuron) {
+                    const float w2 = weight_any(r2, type, d, e);
+                    bad |= !isfinite(w2);
+                    a2 = __fmaf_rn(w2, xf[e], a2);
+                  }
+                }
             }
-            ag = __fmaf_rn(xs[p], tg, ag);
-            au = __fmaf_rn(xs[p], tu, au);
-          }
-        } else {
-          const float* xf = reinterpret_cast<const float*>(smem + a.sm.xf) + t * d;
-          for (unsigned p = lane; p < P; p += 32)
-            for (unsigned jj = 0; jj < 64; ++jj) {
-              const unsigned e = 64 * p + jj;
-              const float wg = weight_any(grow, type, d, e), wu = weight_any(urow, type, d, e);
-              bad |= !isfinite(wg) || !isfinite(wu);
-              ag = __fmaf_rn(wg, xf[e], ag);
-              au = __fmaf_rn(wu, xf[e], au);
-            }
-        }
 #pragma unroll
-        for (unsigned o = 16; o; o >>= 1) {
-          ag = __fadd_rn(ag, __shfl_xor_sync(0xffffffffu, ag, o));
-          au = __fadd_rn(au, __shfl_xor_sync(0xffffffffu, au, o));
-        }
-        if (lane == 0) {
-          float h = 0.0f;
-          if (!isfinite(ag) || !isfinite(au) || !swiglu(ag, au, &h)) bad = true;
-          a.hidden[(static_cast<size_t>(item) * T + t) * 32 + n] = h;
+            for (unsigned o = 16; o; o >>= 1) {
+              a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, o));
+              a2 = __fadd_rn(a2, __shfl_xor_sync(0xffffffffu, a2, o));
+            }
+            if (lane == 0) {
+              (up_only ? s_uv : s_gv)[n * T + kk] = a1;
+              if (by_neuron) s_uv[n * T + kk] = a2;
+            }
+          }
         }
       }
+      release(c);
     }
-    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(a.status, kStNumeric);
-    if (j == 0) PHASE(9);
+    if (r == 0) PHASE(9);
+    if (__syncthreads_or(timed_out)) { aborted = true; break; }
+    // SwiGLU and the hidden slice's Q8 quantization (src/q4.c:37-61, one group of 32)
+    for (unsigned kk = warp; kk < nt; kk += kLayerWarps) {
+      unsigned mm = mask;
+      for (unsigned z = 0; z < kk; ++z) mm &= mm - 1;
+      const unsigned t = __ffs(mm) - 1;
+      const float g = s_gv[lane * T + kk], uu = s_uv[lane * T + kk];
+      float h = 0.0f;
+      if (!isfinite(g) || !isfinite(uu) || !swiglu(g, uu, &h)) { bad = true; h = 0.0f; }
+      if (a.hidden) a.hidden[((static_cast<size_t>(u) * S + s) * T + t) * 32 + lane] = h;
+      float gs;
+      if (ACT == FRC_ACT_Q8) {
+        float amax = fabsf(h);
+#pragma unroll
+        for (unsigned o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const Q8Group qg(amax);
+        s_hq[kk * 32 + (dtype == kMXFP4 ? prmt_pos(lane) : lane)] = static_cast<uint8_t>(qg.q(h) & 0xff);
+        gs = __fmul_rn(qg.scale, s_ugate[u * T + t]);
+      } else {
+        reinterpret_cast<float*>(s_hq)[kk * 32 + lane] = h;
+        gs = s_ugate[u * T + t];
+      }
+      if (lane == 0) a.gsv[(gp0 + kk) * S + s] = gs;
+    }
     __syncthreads();
-    if (warp == 0 && lane == 0 && j + kSlots < n_gu) {
-      fence_proxy_async();
-      issue(j + kSlots);
+    if (r == 0) PHASE(13);
+    // down: rows of chunk k, one a thread; c = scale * int_dot (or the fp32 dot)
+    for (unsigned k = 0; k < ndn; ++k, ++c) {
+      const unsigned r0 = k * dn, nr = min(dn, d - r0);
+      float* out = a.partial + (static_cast<size_t>(gp0) * S + s) * d + r0;
+      if (wait_chunk(c)) {
+        if (r == 0 && k == 0) PHASE(14);
+        const uint8_t* slot = ring + (c % K) * SLOT;
+        auto cterm = [&](unsigned rr, unsigned kk) -> float {
+          if (dtype == kMXFP4) {
+            const unsigned e = slot[rr];
+            bad |= e == 255;
+            const uint4 w = *reinterpret_cast<const uint4*>(slot + nr + 16 * rr);
+            if (ACT == FRC_ACT_Q8) {
+              const uint4 h0 = reinterpret_cast<const uint4*>(s_hq)[2 * kk];
+              const uint4 h1 = reinterpret_cast<const uint4*>(s_hq)[2 * kk + 1];
+              const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+              return __fmul_rn(pow2_m128(e), i2f(idot_mxfp4_16(w, hw)));
+            }
+            const float* hv = reinterpret_cast<const float*>(s_hq) + kk * 32;
+            const float sc = __uint_as_float(e ? e << 23 : 0x00400000u);
+            const uint8_t* qb = slot + nr + 16 * rr;
+            float dot = 0.0f;
+            for (unsigned nn = 0; nn < 32; ++nn)
+              dot = __fmaf_rn(__fmul_rn(sc, e2m1((qb[nn & 15] >> (nn >> 4 ? 4 : 0)) & 15)), hv[nn], dot);
+            return dot;
+          }
+          const float sw = h2f(slot[2 * rr] | slot[2 * rr + 1] << 8);
+          bad |= !isfinite(sw);
+          if (ACT == FRC_ACT_Q8) {
+            const uint4* wv = reinterpret_cast<const uint4*>(slot + 2 * nr + 32 * rr);
+            const uint4 w0 = wv[0], w1 = wv[1];
+            const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            const uint4 h0 = reinterpret_cast<const uint4*>(s_hq)[2 * kk];
+            const uint4 h1 = reinterpret_cast<const uint4*>(s_hq)[2 * kk + 1];
+            const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+            int iv = 0;
+#pragma unroll
+            for (unsigned m = 0; m < 8; ++m) iv = __dp4a(static_cast<int>(ww[m]), static_cast<int>(hw[m]), iv);
+            return __fmul_rn(sw, i2f(iv));
+          }
+          const float* hv = reinterpret_cast<const float*>(s_hq) + kk * 32;
+          const int8_t* qb = reinterpret_cast<const int8_t*>(slot + 2 * nr + 32 * rr);
+          float dot = 0.0f;
+          for (unsigned nn = 0; nn < 32; ++nn) dot = __fmaf_rn(__fmul_rn(sw, static_cast<float>(qb[nn])), hv[nn], dot);
+          return dot;
+        };
+        if (nt == 1 && nr <= 4 * kLayerThreads) {
+          // one token, at most four rows a thread: hold the terms in registers,
+          // hand the slot back, then store (the release need not wait for them)
+          const float h0 = tid < nr ? cterm(tid, 0) : 0.0f;
+          const float h1 = tid + kLayerThreads < nr ? cterm(tid + kLayerThreads, 0) : 0.0f;
+          const float h2 = tid + 2 * kLayerThreads < nr ? cterm(tid + 2 * kLayerThreads, 0) : 0.0f;
+          const float h3 = tid + 3 * kLayerThreads < nr ? cterm(tid + 3 * kLayerThreads, 0) : 0.0f;
+          release(c);
+          if (tid < nr) out[tid] = h0;
+          if (tid + kLayerThreads < nr) out[tid + kLayerThreads] = h1;
+          if (tid + 2 * kLayerThreads < nr) out[tid + 2 * kLayerThreads] = h2;
+          if (tid + 3 * kLayerThreads < nr) out[tid + 3 * kLayerThreads] = h3;
+          continue;
+        }
+        for (unsigned rr = tid; rr < nr; rr += kLayerThreads)
+          for (unsigned kk = 0; kk < nt; ++kk) out[static_cast<size_t>(kk) * S * d + rr] = cterm(rr, kk);
+      }
+      release(c);
     }
+    if (r == 0) PHASE(6);
   }
+  if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(a.status, kStNumeric);
+  if (__syncthreads_or(timed_out)) aborted = true;
+  PHASE(4);
 
   // -------------------------------------------------------- grid barrier
-  PHASE(4);
-  if (!aborted && !grid_sync(a.ctl, misc + 3)) {
+  if (aborted) {
+    if (tid == 0) {
+      atomicOr(a.status, kStTimeout);
+      atomicExch(&a.ctl->abort, 1u);
+    }
+  } else if (!grid_sync(a.ctl, misc + 3)) {
     aborted = true;
     if (tid == 0) atomicOr(a.status, kStTimeout);
   }
   PHASE(5);
 
-  // ------------------------------------------------------------- phase 2
-  for (unsigned bi = 0; bi < n_batch && !aborted; ++bi) {
-    const unsigned u0 = bi * per_batch, u1 = min(U, u0 + per_batch);
-    if (bi) issue_batch(bi, warp, kLayerWarps);
-    // quantize the hidden slices of this batch: entry (pair, s), pair = token k of expert u
-    const unsigned pair0 = s_upre[u0], npair = s_upre[u1] - pair0, E = S * npair;
-    uint8_t* hqs = p2 + batch_pieces(u0, u1);
-    float* gss = reinterpret_cast<float*>(hqs + (ACT == FRC_ACT_Q8 ? 32 : 128) * E);
-    constexpr unsigned kEnt = 16;  // entries a warp keeps in flight
-    for (unsigned e0 = warp; e0 < E; e0 += kLayerWarps * kEnt) {
-      float hv[kEnt];
-#pragma unroll
-      for (unsigned z = 0; z < kEnt; ++z) {
-        const unsigned ent = e0 + z * kLayerWarps;
-        hv[z] = 0.0f;
-        if (ent < E) {
-          const unsigned pu = s_pair[pair0 + ent / S], s = ent % S;
-          hv[z] = __ldcg(&a.hidden[((static_cast<size_t>(pu >> 5) * S + s) * T + (pu & 31)) * 32 + lane]);
-        }
-      }
-#pragma unroll
-      for (unsigned z = 0; z < kEnt; ++z) {
-        const unsigned ent = e0 + z * kLayerWarps;
-        if (ent >= E) break;
-        const unsigned pu = s_pair[pair0 + ent / S], u = pu >> 5, t = pu & 31;
-        if (ACT == FRC_ACT_Q8) {
-          float amax = fabsf(hv[z]);
-#pragma unroll
-          for (unsigned o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-          const Q8Group qg(amax);
-          const int v = qg.q(hv[z]);
-          const bool mxd = u < UR && a.down_type == kMXFP4;
-          hqs[ent * 32 + (mxd ? prmt_pos(lane) : lane)] = static_cast<uint8_t>(v & 0xff);
-          if (lane == 0) gss[ent] = __fmul_rn(qg.scale, s_ugate[u * T + t]);
-        } else {
-          reinterpret_cast<float*>(hqs)[ent * 32 + lane] = hv[z];  // fp32 mode keeps the hidden values
-          if (lane == 0) gss[ent] = s_ugate[u * T + t];
-        }
-      }
-    }
-    cp_async_wait_all();
-    PHASE(12);
-    __syncthreads();
-    PHASE(13);
-    const unsigned tasks = npair * R * kDnSplit;
-    bool bad = false;
-    for (unsigned task = tid; task < tasks; task += kLayerThreads) {
-      const unsigned q = task % kDnSplit, rr = (task / kDnSplit) % R, pair = pair0 + task / (kDnSplit * R);
-      const unsigned u = s_pair[pair] >> 5;
-      const bool q8 = u >= UR || a.down_type == kQ80;
-      const unsigned pb = u >= UR ? piece_q8 : piece_r, lo = q8 ? q8_lo : mx_lo, hi = q8 ? q8_hi : mx_hi;
-      const uint8_t* ubase = p2 + piece_off(u0, u, 0);
-      const unsigned r = r0 + rr;
-      float acc = 0.0f;
-      for (unsigned s = q; s < S; s += kDnSplit) {
-        const uint8_t* pc = ubase + s * pb;
-        const unsigned ent = (pair - pair0) * S + s;
-        const float g = gss[ent];
-        float cterm;
-        if (ACT == FRC_ACT_Q8) {
-          const uint4 h0 = reinterpret_cast<const uint4*>(hqs)[2 * ent];
-          const uint4 h1 = reinterpret_cast<const uint4*>(hqs)[2 * ent + 1];
-          const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-          if (!q8) {
-            const unsigned e = pc[r - lo];
-            bad |= e == 255;
-            const uint4 w = *reinterpret_cast<const uint4*>(pc + (hi - lo) + 16 * rr);
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-            int ip = 0, in = 0;
-#pragma unroll
-            for (unsigned m = 0; m < 4; ++m) {
-              ip = __dp4a(static_cast<int>(prmt(kE2M1Lo, kE2M1Hi, ww[m])), static_cast<int>(hw[2 * m]), ip);
-              in = __dp4a(static_cast<int>(prmt(kE2M1Lo, kE2M1Hi, ww[m] ^ 0x8888u)), static_cast<int>(hw[2 * m]), in);
-              ip = __dp4a(static_cast<int>(prmt(kE2M1Lo, kE2M1Hi, ww[m] >> 16)), static_cast<int>(hw[2 * m + 1]), ip);
-              in = __dp4a(static_cast<int>(prmt(kE2M1Lo, kE2M1Hi, (ww[m] >> 16) ^ 0x8888u)),
-                          static_cast<int>(hw[2 * m + 1]), in);
-            }
-            cterm = __fmul_rn(pow2_m128(e), i2f(ip - in));
-          } else {
-            const float sw = h2f(pc[2 * r - lo] | pc[2 * r - lo + 1] << 8);
-            bad |= !isfinite(sw);
-            const uint4* wv = reinterpret_cast<const uint4*>(pc + (hi - lo) + 32 * rr);
-            const uint4 w0 = wv[0], w1 = wv[1];
-            const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-            int iv = 0;
-#pragma unroll
-            for (unsigned m = 0; m < 8; ++m) iv = __dp4a(static_cast<int>(ww[m]), static_cast<int>(hw[m]), iv);
-            cterm = __fmul_rn(sw, i2f(iv));
-          }
-        } else {
-          const float* hvf = reinterpret_cast<const float*>(hqs) + ent * 32;
-          float dot = 0.0f;
-          if (!q8) {
-            const unsigned e = pc[r - lo];
-            bad |= e == 255;
-            const float sc = __uint_as_float(e ? e << 23 : 0x00400000u);
-            const uint8_t* qb = pc + (hi - lo) + 16 * rr;
-            for (unsigned nn = 0; nn < 32; ++nn)
-              dot = __fmaf_rn(__fmul_rn(sc, e2m1((qb[nn & 15] >> (nn >> 4 ? 4 : 0)) & 15)), hvf[nn], dot);
-          } else {
-            const float sw = h2f(pc[2 * r - lo] | pc[2 * r - lo + 1] << 8);
-            bad |= !isfinite(sw);
-            const int8_t* qb = reinterpret_cast<const int8_t*>(pc + (hi - lo) + 32 * rr);
-            for (unsigned nn = 0; nn < 32; ++nn) dot = __fmaf_rn(__fmul_rn(sw, static_cast<float>(qb[nn])), hvf[nn], dot);
-          }
-          cterm = dot;
-        }
-        acc = __fmaf_rn(cterm, g, acc);
-      }
-      split[(pair * R + rr) * kDnSplit + q] = acc;
-    }
-    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(a.status, kStNumeric);
-    __syncthreads();  // p2 is rewritten by the next batch
-  }
-  PHASE(6);
-  // every token's rows: its experts in its routing order, then the shared expert
+  // ------------------------------------------------------------- reduce
+  // CTA k owns 4-row units [d/4*k/G, d/4*(k+1)/G): its rows of every
+  // (pair, slice) term vector arrive by 16-byte cp.async into the idle ring,
+  // the weights gs by plain loads, then the chains run from shared memory.
+  const unsigned NU = d / 4, u0r = NU * cta / G, nu = NU * (cta + 1) / G - u0r;
+  const unsigned y0 = 4 * u0r, R = 4 * nu;
   if (!aborted && R) {
+    const unsigned per_tok = 11 * S * (R + 1) + 11 * R;  // floats staged per token
+    const unsigned tb = max(1u, min(T, (K * SLOT) / (4 * per_tok)));  // the host checks that one token fits
+    float* st = reinterpret_cast<float*>(ring);
     bool nf = false;
-    for (unsigned idx = tid; idx < T * R; idx += kLayerThreads) {
-      const unsigned t = idx / R, rr = idx % R;
-      float yv = 0.0f;
-      for (unsigned e = 0; e <= 10; ++e) {
-        const unsigned pair = s_tokpair[t * 11 + e];
-        if (pair == 0xffff) continue;
-        const float* sp = split + (pair * R + rr) * kDnSplit;
-        float part = sp[0];
-        for (unsigned z = 1; z < kDnSplit; ++z) part = __fadd_rn(part, sp[z]);
-        yv = __fadd_rn(yv, part);
+    for (unsigned t0 = 0; t0 < T; t0 += tb) {
+      const unsigned tn = min(tb, T - t0);
+      float* terms = st;                        // [tl][e][s][R]
+      float* gsr = st + tn * 11 * S * R;        // [tl][e][s]
+      float* part = gsr + tn * 11 * S;          // [tl][e][R]
+      for (unsigned q = tid; q < tn * 11 * S * nu; q += kLayerThreads) {
+        const unsigned un = q % nu, rest = q / nu, s = rest % S, te = rest / S;  // te = tl*11 + e
+        const unsigned pair = s_tokpair[(t0 + te / 11) * 11 + te % 11];
+        if (pair != 0xffff)
+          cp_async16(terms + (te * S + s) * R + 4 * un,
+                     a.partial + (static_cast<size_t>(pair) * S + s) * d + y0 + 4 * un);
       }
-      nf |= !isfinite(yv);
-      a.y[static_cast<size_t>(t) * d + r0 + rr] = yv;
+      cp_async_commit();
+      for (unsigned q = tid; q < tn * 11 * S; q += kLayerThreads) {
+        const unsigned s = q % S, te = q / S;
+        const unsigned pair = s_tokpair[(t0 + te / 11) * 11 + te % 11];
+        gsr[q] = pair != 0xffff ? __ldcg(a.gsv + pair * S + s) : 0.0f;
+      }
+      cp_async_wait_all();
+      __syncthreads();
+      if (t0 == 0) PHASE(11);
+      for (unsigned q = tid; q < tn * 11 * R; q += kLayerThreads) {
+        const unsigned rr = q % R, te = q / R;
+        const float* tv = terms + te * S * R + rr;
+        const float* gv = gsr + te * S;
+        // chain j takes slices s = j mod 4 in ascending order
+        float p0 = 0.0f, p1 = 0.0f, p2 = 0.0f, p3 = 0.0f;
+        unsigned s = 0;
+        for (; s + 4 <= S; s += 4) {
+          p0 = __fmaf_rn(tv[s * R], gv[s], p0);
+          p1 = __fmaf_rn(tv[(s + 1) * R], gv[s + 1], p1);
+          p2 = __fmaf_rn(tv[(s + 2) * R], gv[s + 2], p2);
+          p3 = __fmaf_rn(tv[(s + 3) * R], gv[s + 3], p3);
+        }
+        if (s < S) p0 = __fmaf_rn(tv[s * R], gv[s], p0);
+        if (s + 1 < S) p1 = __fmaf_rn(tv[(s + 1) * R], gv[s + 1], p1);
+        if (s + 2 < S) p2 = __fmaf_rn(tv[(s + 2) * R], gv[s + 2], p2);
+        part[q] = __fadd_rn(__fadd_rn(__fadd_rn(p0, p1), p2), p3);
+      }
+      __syncthreads();
+      for (unsigned q = tid; q < tn * R; q += kLayerThreads) {
+        const unsigned tl = q / R, rr = q % R, t = t0 + tl;
+        float yv = 0.0f;
+        for (unsigned e = 0; e <= 10; ++e)
+          if (s_tokpair[t * 11 + e] != 0xffff) yv = __fadd_rn(yv, part[(tl * 11 + e) * R + rr]);
+        nf |= !isfinite(yv);
+        a.y[static_cast<size_t>(t) * d + y0 + rr] = yv;
+      }
+      __syncthreads();
     }
     if (nf) atomicOr(a.status, kStNumeric);
   }
   PHASE(7);
-  // nothing may still be writing this CTA's shared memory when it leaves
-  cp_async_wait_all();
-  if (aborted)
-    for (unsigned jj = j; jj < n_gu && jj < j + kSlots; ++jj) mbar_wait(&bar[jj % kSlots], (jj / kSlots) & 1);
+  // Nothing may still be writing this CTA's shared memory when it leaves.
+  // After an abort, wait (bounded) for the last copy issued into each slot:
+  // slot i got its first chunk at start and one more per completed release
+  // round that had a chunk left to issue.
+  if (aborted && tid == 0)
+    for (unsigned i = 0; i < K && i < n_ch; ++i) {
+      unsigned n = 1;
+      while (n <= s_cnt[i] / kLayerWarps && i + K * n < n_ch) ++n;
+      mbar_wait(&full[i], (n - 1) & 1);
+    }
 }
 
 }  // namespace frc

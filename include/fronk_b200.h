@@ -100,8 +100,14 @@ int frc_loaded_mask(const frc_context *c, uint32_t *mask);
 int frc_run(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *expert,
             const float *gate, const float *x, float *y, int act);
 
-/* Flags of frc_run_device. */
-enum { FRC_RUN_RMSNORM = 1 };
+/* Flags of frc_run_device.
+ * FRC_RUN_OVERLAP: the launch may start while the kernel before it on the
+ * stream is finishing (programmatic dependent launch): it plans and starts
+ * streaming this layer's weights at once and waits for that kernel only
+ * before it reads x / x_add or writes anything.  The caller guarantees that
+ * the preceding kernel writes neither the weights nor expert / gate (writing
+ * x, as a previous layer or an all-reduce does, is fine). */
+enum { FRC_RUN_RMSNORM = 1, FRC_RUN_OVERLAP = 2 };
 
 /* Asynchronous run on device memory, enqueued on `stream` (a cudaStream_t, or
  * NULL for the legacy default stream); nothing is validated on the host and
@@ -115,13 +121,16 @@ enum { FRC_RUN_RMSNORM = 1 };
 int frc_run_device(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *expert,
                    const float *gate, const float *x, const float *x_add, float *x_out,
                    float *y, int act, unsigned flags, void *stream);
-/* frc_run_device with the gate/up -> down hidden hand-off held in a device
- * array fixed at module load (1 MiB per device) instead of context scratch:
- * the call allocates nothing.  Up to 6 tokens with 20 slices loaded (more
- * tokens with fewer slices); a larger call returns FRC_INVALID and launches
- * nothing.  The array is shared by all contexts and streams of a device:
- * overlapping calls on one device race, callers serialise them.  The first
- * call on a device looks the array up; make it before any stream capture.
+/* frc_run_device with the hand-off between the kernel's item phase and its
+ * reduce (the down terms and their weights) held in a device array fixed at
+ * module load (8 MiB per device) instead of context scratch: the call
+ * allocates nothing.  Needs 11 x tokens x slices x (hidden + 1) floats: up
+ * to 4 tokens with 20 slices at hidden 2048 (more with fewer slices); a
+ * larger call returns FRC_INVALID and launches nothing.  No fp32 copy of the
+ * hidden activations is kept (frc_debug_hidden does not see these calls).
+ * The array is shared by all contexts and streams of a device: overlapping
+ * calls on one device race, callers serialise them.  The first call on a
+ * device looks the array up; make it before any stream capture.
  * No counterpart in the reference (backend.h has no device-pointer entry). */
 int frc_run_device_fixed(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *expert,
                          const float *gate, const float *x, const float *x_add, float *x_out,

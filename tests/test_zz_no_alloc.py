@@ -25,7 +25,7 @@ def test_fixed_scratch_matches_context_scratch(gpu):
     import torch
     hidden, layer = 2048, 3
     g = fb.geometry(hidden)
-    cases = [request(hidden, 4, SEED + 91, 0.5), request(hidden, 6, SEED + 92, 0.0)]
+    cases = [request(hidden, 4, SEED + 91, 0.5), request(hidden, 3, SEED + 92, 0.0)]
     experts = np.concatenate([c[0].ravel() for c in cases])
     with fb.Context(0, hidden) as ctx:
         for b, arr in make_layers(g, SEED, list(range(20)), experts, shared=True).items():
@@ -52,15 +52,15 @@ def test_fixed_scratch_rejects_oversize_call(gpu):
     import torch
     hidden, layer = 2048, 0
     g = fb.geometry(hidden)
-    e, gate, x = request(hidden, 7, SEED + 93, 0.0)
+    e, gate, x = request(hidden, 5, SEED + 93, 0.0)
     with fb.Context(0, hidden) as ctx:
         for b, arr in make_layers(g, SEED, list(range(20)), e, shared=True).items():
             assert ctx.load_layer(b, layer, arr) == OK, ctx.last_error
         de, dg, dx = _device(torch, e.astype(np.uint16)), _device(torch, gate), _device(torch, x)
-        y = torch.zeros((7, hidden), dtype=torch.float32, device="cuda")
+        y = torch.zeros((5, hidden), dtype=torch.float32, device="cuda")
         before = ctx.launches
         with pytest.raises(fb.FrcError) as err:
-            ctx.run_device_fixed(layer, 7, de.data_ptr(), dg.data_ptr(), dx.data_ptr(), None, None, y.data_ptr(),
+            ctx.run_device_fixed(layer, 5, de.data_ptr(), dg.data_ptr(), dx.data_ptr(), None, None, y.data_ptr(),
                                  fb.ACT_Q8, 0, torch.cuda.current_stream().cuda_stream)
         assert err.value.code == INVALID and "fixed scratch" in ctx.last_error
         assert ctx.launches == before
