@@ -480,10 +480,13 @@ def profile_case():
 def ncu_traffic():
     """DRAM bytes per launch of the layer kernel from the committed ncu summary, if any."""
     try:
-        with open(os.path.join(ROOT, "profiles", "layer_kernel_decode48.json")) as f:
-            return json.load(f).get("dram_bytes_per_launch")
+        with open(os.path.join(ROOT, "profiles", "layer_kernel_decode48_full.md")) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_launch:"):
+                    return int(line.split(":")[1])
     except (OSError, ValueError):
-        return None
+        pass
+    return None
 
 
 if __name__ == "__main__":
