@@ -177,7 +177,7 @@ def config(n):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -328,8 +328,12 @@ def main():
     kernel_ms = statistics.mean(kt)
     bytes_per_launch = TOPK * len(blocks) * SLICE_BYTES
     peak, peak_src = peaks()
-    achieved = bytes_per_launch / (kernel_ms * 1e-3) / 1e9
-    in_pass = bytes_per_launch * LAYERS / (ms_per_step * 1e-3) / 1e9
+    # average launch duration over the timed region: at N=1 the passes hold
+    # nothing but the layer kernel (profiles/layer_kernel_decode48_launches.md);
+    # at N>1 it includes the per-layer all-reduce
+    launch_us = ms_per_step * 1e3 / LAYERS
+    achieved = bytes_per_launch / (launch_us * 1e-6) / 1e9
+    alone = bytes_per_launch / (kernel_ms * 1e-3) / 1e9
 
     # ---- end to end through the C ABI with host buffers (reference-facing call)
     e2e_steps = max(3, min(args.steps, 50))
@@ -351,8 +355,10 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": ncu_traffic(), "peak_source": peak_src,
                          "kernel": "layer_kernel<Q8,1> (one launch per layer)",
-                         "algorithmic_bytes_per_launch": bytes_per_launch, "kernel_us": kernel_ms * 1e3,
-                         "in_pass_gbs": in_pass, "in_pass_frac": in_pass / peak},
+                         "algorithmic_bytes_per_launch": bytes_per_launch, "launch_us": launch_us,
+                         "launch_us_source": "CUDA events over the timed passes / launches"
+                                             + (" (includes the all-reduce)" if world > 1 else ""),
+                         "kernel_alone_us": kernel_ms * 1e3, "kernel_alone_gbs": alone},
             "gpu_launches": launches, "graph": used_graph, "clocks": clocks, "e2e": e2e, "parity": parity,
         }
         if world == 1 and not args.no_cpu_baseline:
