@@ -376,17 +376,14 @@ def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev):
     the device entry point plus the all-reduce)."""
     import torch
     h2d = LAYERS * (HIDDEN * 4 + TOPK * 2 + 11 * 4)
-    d2h = LAYERS * HIDDEN * 4
+    d2h = LAYERS * (HIDDEN * 4 + (16 if dist is None else 0))  # y (+ the status word frc_run reads with it)
     if dist is None:
+        # the layer loop in C over the host-buffer call (frc_host_pass -> frc_run per layer)
+        hs = [np.ascontiguousarray(x0[s], np.float32).copy() for s in range(steps)]
+        es = [np.ascontiguousarray(ex[s], np.uint16) for s in range(steps)]
         t0 = time.perf_counter()
         for s in range(steps):
-            h = x0[s].copy()
-            for l in range(LAYERS):
-                x = (h / np.sqrt(np.mean(h * h) + np.float32(1e-6))).astype(np.float32)
-                rc, y = ctx.run(l, ex[s, l][None], gt[s, l][None], x[None], fb.ACT_Q8)
-                if rc:
-                    raise fb.FrcError(rc, "e2e", ctx.last_error)
-                h = h + y[0]
+            ctx.host_pass(0, es[s], gt[s], hs[s], fb.ACT_Q8)
         dt = time.perf_counter() - t0
     else:
         pin_x = torch.empty(HIDDEN, dtype=torch.float32).pin_memory()
@@ -423,7 +420,7 @@ def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev):
     if rc:
         raise fb.FrcError(rc, "e2e", ctx.last_error)
     return {"value": steps / dt, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "steps": steps, "api": "frc_run (host buffers, synchronous per layer)" if dist is None else
+            "steps": steps, "api": "frc_host_pass: frc_run per layer (host buffers, synchronous)" if dist is None else
             "frc_run_device + NCCL all_reduce, pinned host copies each layer"}
 
 

@@ -64,6 +64,7 @@ _SIGS = {
     "frc_run": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _int]),
     "frc_run_device": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
     "frc_run_device_fixed": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
+    "frc_host_pass": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _u32, _int]),
     "frc_status": (_int, [_vp, _vp]),
     "frc_launch_count": (_u64, [_vp]),
     "frc_strerror": (ctypes.c_char_p, [_int]),
@@ -265,6 +266,15 @@ class Context:
         rc = self.lib.frc_run_device_fixed(self.h, layer, tokens, expert_ptr, gate_ptr, x_ptr, x_add_ptr,
                                            x_out_ptr, y_ptr, act, flags, stream)
         self._check(rc, "run_device_fixed")
+
+    def host_pass(self, first_layer, expert, gate, h, act=ACT_Q8):
+        """Decode pass from the host (frc_host_pass): h is updated in place."""
+        expert = np.ascontiguousarray(expert, np.uint16)
+        gate = np.ascontiguousarray(gate, np.float32)
+        assert h.dtype == np.float32 and h.flags.c_contiguous
+        rc = self.lib.frc_host_pass(self.h, first_layer, expert.shape[0], _ptr(expert), _ptr(gate), _ptr(h),
+                                    h.size, act)
+        self._check(rc, "host_pass")
 
     def status(self, stream=None):
         return self.lib.frc_status(self.h, stream)

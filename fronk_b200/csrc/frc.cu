@@ -127,11 +127,11 @@ struct frc_context {
   unsigned long long* phases = nullptr;
   LayerCtl* ctl = nullptr;
   unsigned* status = nullptr;
-  uint16_t* d_expert = nullptr;
-  float *d_gate = nullptr, *d_x = nullptr, *d_y = nullptr;
-  uint16_t* h_expert = nullptr;
-  float *h_gate = nullptr, *h_x = nullptr, *h_y = nullptr;
-  unsigned* h_status = nullptr;
+  // frc_run staging: one copy in ([x][gate][expert], packed for the call's
+  // token count) and one copy out ([status word, 16 B][y]).
+  uint8_t *d_in = nullptr, *d_out = nullptr, *h_in = nullptr, *h_out = nullptr;
+  float *d_y = nullptr, *h_y = nullptr;  // inside d_out / h_out
+  unsigned* h_status = nullptr;          // start of h_out
   cudaStream_t stream = nullptr;
   uint8_t* pool = nullptr;
   unsigned pool_count = 0;
@@ -161,6 +161,9 @@ static int fail(frc_context* c, int rc, const char* fmt, ...) {
   } while (0)
 
 static unsigned align_up(unsigned v, unsigned a) { return (v + a - 1) / a * a; }
+
+// Bytes of one token's frc_run input: x, gate, expert ids.
+static size_t kInBytesPerToken(unsigned d) { return sizeof(float) * (d + FRC_ACTIVE) + sizeof(uint16_t) * FRC_TOPK; }
 
 // fp32 hidden activations of the largest call: [unique expert][slice][token][32]
 constexpr size_t kHiddenBytes = sizeof(float) * kMaxUnique * kMaxBlocks * kMaxTokens * 32;
@@ -419,19 +422,20 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
   alloc(reinterpret_cast<void**>(&c->gsv), sizeof(float) * kMaxPairs * kMaxBlocks);
   alloc(reinterpret_cast<void**>(&c->ctl), sizeof(LayerCtl));
   alloc(reinterpret_cast<void**>(&c->phases), sizeof(unsigned long long) * 16 * 1024);
-  alloc(reinterpret_cast<void**>(&c->status), sizeof(unsigned));
-  alloc(reinterpret_cast<void**>(&c->d_expert), sizeof(uint16_t) * kMaxTokens * 10);
-  alloc(reinterpret_cast<void**>(&c->d_gate), sizeof(float) * kMaxTokens * 11);
-  alloc(reinterpret_cast<void**>(&c->d_x), sizeof(float) * kMaxTokens * d);
-  alloc(reinterpret_cast<void**>(&c->d_y), sizeof(float) * kMaxTokens * d);
+  const size_t in_bytes = kInBytesPerToken(d) * kMaxTokens, out_bytes = 16 + sizeof(float) * kMaxTokens * d;
+  alloc(reinterpret_cast<void**>(&c->d_in), in_bytes);
+  alloc(reinterpret_cast<void**>(&c->d_out), out_bytes);
   if (rc == FRC_OK) {
-    if (cudaMallocHost(reinterpret_cast<void**>(&c->h_expert), sizeof(uint16_t) * kMaxTokens * 10) != cudaSuccess ||
-        cudaMallocHost(reinterpret_cast<void**>(&c->h_gate), sizeof(float) * kMaxTokens * 11) != cudaSuccess ||
-        cudaMallocHost(reinterpret_cast<void**>(&c->h_x), sizeof(float) * kMaxTokens * d) != cudaSuccess ||
-        cudaMallocHost(reinterpret_cast<void**>(&c->h_y), sizeof(float) * kMaxTokens * d) != cudaSuccess ||
-        cudaMallocHost(reinterpret_cast<void**>(&c->h_status), sizeof(unsigned)) != cudaSuccess ||
+    c->status = reinterpret_cast<unsigned*>(c->d_out);
+    c->d_y = reinterpret_cast<float*>(c->d_out + 16);
+    if (cudaMallocHost(reinterpret_cast<void**>(&c->h_in), in_bytes) != cudaSuccess ||
+        cudaMallocHost(reinterpret_cast<void**>(&c->h_out), out_bytes) != cudaSuccess ||
         cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess)
       rc = fail(c, FRC_IO, "pinned buffers or stream");
+  }
+  if (rc == FRC_OK) {
+    c->h_status = reinterpret_cast<unsigned*>(c->h_out);
+    c->h_y = reinterpret_cast<float*>(c->h_out + 16);
   }
   if (rc == FRC_OK && (cudaMemset(c->ctl, 0, sizeof(LayerCtl)) != cudaSuccess ||
                        cudaMemset(c->status, 0, sizeof(unsigned)) != cudaSuccess ||
@@ -451,9 +455,9 @@ int frc_close(frc_context* c) {
   if (c->stream) cudaStreamSynchronize(c->stream);
   for (auto& b : c->layer_ptr)
     for (auto& p : b) if (p) cudaFree(p);
-  cudaFree(c->staging); cudaFree(c->hidden); cudaFree(c->partial); cudaFree(c->gsv); cudaFree(c->phases); cudaFree(c->ctl); cudaFree(c->status);
-  cudaFree(c->d_expert); cudaFree(c->d_gate); cudaFree(c->d_x); cudaFree(c->d_y); cudaFree(c->pool);
-  cudaFreeHost(c->h_expert); cudaFreeHost(c->h_gate); cudaFreeHost(c->h_x); cudaFreeHost(c->h_y); cudaFreeHost(c->h_status);
+  cudaFree(c->staging); cudaFree(c->hidden); cudaFree(c->partial); cudaFree(c->gsv); cudaFree(c->phases); cudaFree(c->ctl);
+  cudaFree(c->d_in); cudaFree(c->d_out); cudaFree(c->pool);
+  cudaFreeHost(c->h_in); cudaFreeHost(c->h_out);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
   return FRC_OK;
@@ -555,21 +559,27 @@ int frc_run(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* exp
   int rc = validate(c, tokens, expert, gate, x);
   if (rc) return fail(c, rc, "request rejected");
   CK(cudaSetDevice(c->device));
-  const size_t xb = sizeof(float) * tokens * c->g.hidden;
-  memcpy(c->h_expert, expert, sizeof(uint16_t) * tokens * FRC_TOPK);
-  memcpy(c->h_gate, gate, sizeof(float) * tokens * FRC_ACTIVE);
-  memcpy(c->h_x, x, xb);
-  CK(cudaMemcpyAsync(c->d_expert, c->h_expert, sizeof(uint16_t) * tokens * FRC_TOPK, cudaMemcpyHostToDevice, c->stream));
-  CK(cudaMemcpyAsync(c->d_gate, c->h_gate, sizeof(float) * tokens * FRC_ACTIVE, cudaMemcpyHostToDevice, c->stream));
-  CK(cudaMemcpyAsync(c->d_x, c->h_x, xb, cudaMemcpyHostToDevice, c->stream));
-  rc = run_device(c, layer, tokens, c->d_expert, c->d_gate, c->d_x, nullptr, nullptr, c->d_y, act, 0, c->stream);
+  // one copy in: [x][gate][expert] packed for this call's token count
+  const size_t xb = sizeof(float) * tokens * c->g.hidden, gb = sizeof(float) * tokens * FRC_ACTIVE;
+  const size_t eb = sizeof(uint16_t) * tokens * FRC_TOPK;
+  memcpy(c->h_in, x, xb);
+  memcpy(c->h_in + xb, gate, gb);
+  memcpy(c->h_in + xb + gb, expert, eb);
+  CK(cudaMemcpyAsync(c->d_in, c->h_in, xb + gb + eb, cudaMemcpyHostToDevice, c->stream));
+  rc = run_device(c, layer, tokens, reinterpret_cast<const uint16_t*>(c->d_in + xb + gb),
+                  reinterpret_cast<const float*>(c->d_in + xb), reinterpret_cast<const float*>(c->d_in), nullptr,
+                  nullptr, c->d_y, act, 0, c->stream);
   if (rc) return rc;
   c->last_T = tokens;
-  memcpy(c->last_expert, expert, sizeof(uint16_t) * tokens * FRC_TOPK);
-  memcpy(c->last_gate, gate, sizeof(float) * tokens * FRC_ACTIVE);
-  CK(cudaMemcpyAsync(c->h_y, c->d_y, xb, cudaMemcpyDeviceToHost, c->stream));
-  rc = frc_status(c, c->stream);
-  if (rc) return rc;
+  memcpy(c->last_expert, expert, eb);
+  memcpy(c->last_gate, gate, gb);
+  // one copy out: the status word and y
+  CK(cudaMemcpyAsync(c->h_out, c->d_out, 16 + xb, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaMemsetAsync(c->status, 0, sizeof(unsigned), c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  const unsigned st = *c->h_status;
+  if (st & kStTimeout) CK(cudaMemset(c->ctl, 0, sizeof(LayerCtl)));  // nothing runs now
+  if (status_code(st)) return fail(c, status_code(st), "device status 0x%x", st);
   memcpy(y, c->h_y, xb);  // published only after the whole layer succeeded
   return FRC_OK;
 }

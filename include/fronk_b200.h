@@ -135,6 +135,15 @@ int frc_run_device(frc_context *c, unsigned layer, unsigned tokens, const uint16
 int frc_run_device_fixed(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *expert,
                          const float *gate, const float *x, const float *x_add, float *x_out,
                          float *y, int act, unsigned flags, void *stream);
+/* A decode pass for one token driven from the host, layer by layer through
+ * frc_run (host buffers, one synchronous call per layer):
+ * x = h / sqrt(mean(h^2) + 1e-6), y = run(layer, x), h += y, for layers
+ * first_layer .. first_layer + layers - 1.  expert: [layers][10], gate:
+ * [layers][11]; h (hidden floats) is the residual stream, updated in place.
+ * The end-to-end path of a host that owns the layer loop (the reference's
+ * head calls fr_backend.run once per layer the same way). */
+int frc_host_pass(frc_context *c, unsigned first_layer, unsigned layers, const uint16_t *expert,
+                  const float *gate, float *h, unsigned hidden, int act);
 /* Waits for `stream`, returns and clears the device status (FRC_OK,
  * FRC_NUMERIC, FRC_INVALID for an out-of-range id, FRC_IO for a timed-out wait). */
 int frc_status(frc_context *c, void *stream);

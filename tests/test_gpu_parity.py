@@ -203,3 +203,29 @@ def test_failures_leave_output_untouched(gpu):
             for act in (fb.ACT_Q8, fb.ACT_F32):
                 rc, y = ctx.run(0, e, gate, x, act, out=sentinel.copy())
                 assert rc == NUMERIC and np.array_equal(y, sentinel), (offset, act)
+
+
+def test_host_pass_equals_layer_by_layer_runs(gpu):
+    """frc_host_pass (the C layer loop over frc_run) against the same chain
+    driven call by call from Python: identical residual stream."""
+    hidden, layers = 2048, 3
+    g = fb.geometry(hidden)
+    routes = [request(hidden, 1, SEED + 300 + l, 0.0) for l in range(layers)]
+    experts = np.concatenate([r[0].ravel() for r in routes])
+    with fb.Context(0, hidden) as ctx:
+        lay = make_layers(g, SEED, [2, 9], experts, shared=True)
+        for l in range(layers):
+            for b, arr in lay.items():
+                assert ctx.load_layer(b, l, arr) == OK, ctx.last_error
+        h0 = routes[0][2][0].astype(np.float32)
+        h = h0.copy()
+        for l in range(layers):
+            ss = float(np.sum(h.astype(np.float64) ** 2))
+            inv = np.float32(1.0 / np.sqrt(ss / hidden + 1e-6))
+            x = (h * inv).astype(np.float32)
+            rc, y = ctx.run(l, routes[l][0], routes[l][1], x[None], fb.ACT_Q8)
+            assert rc == OK, ctx.last_error
+            h = (h + y[0]).astype(np.float32)
+        hp = h0.copy()
+        ctx.host_pass(0, np.concatenate([r[0] for r in routes]), np.concatenate([r[1] for r in routes]), hp)
+        assert np.array_equal(hp.view(np.uint32), h.view(np.uint32))
