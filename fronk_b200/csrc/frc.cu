@@ -139,7 +139,7 @@ struct frc_context {
   bool attr_set[2] = {};
   unsigned occ_smem[2] = {};
   int occ_val[2] = {};
-  unsigned last_T = 0, last_S = 0;
+  unsigned last_T = 0, last_S = 0, last_G = 0;
   uint16_t last_expert[FRC_MAX_TOKENS * FRC_TOPK] = {};
   float last_gate[FRC_MAX_TOKENS * FRC_ACTIVE] = {};
   char err[256] = {};
@@ -168,14 +168,18 @@ static size_t kInBytesPerToken(unsigned d) { return sizeof(float) * (d + FRC_ACT
 // fp32 hidden activations of the largest call: [unique expert][slice][token][32]
 constexpr size_t kHiddenBytes = sizeof(float) * kMaxUnique * kMaxBlocks * kMaxTokens * 32;
 
-// Shared memory of one layer CTA and the chunking of an item into ring
-// slots.  A slot is sized for a gate/up chunk of 16 routed neurons (both
-// rows), halved while fewer than four slots fit; the shared expert's chunk
-// and the down chunks are cut to the slot.  Returns false when even two
-// slots of one neuron do not fit.
-static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, LayerSmem* out) {
+// Dynamic shared memory a CTA may use with two CTAs an SM (228 KB an SM,
+// 1 KB reserved a CTA), and with one.
+constexpr unsigned kSmemTwoPerSm = (228 * 1024 - 2 * 1024) / 2;
+constexpr unsigned kSmemOnePerSm = 227 * 1024;
+
+// Shared memory of one layer CTA within `limit` bytes and the chunking of an
+// item into ring slots.  A slot is sized for a gate/up chunk of 16 routed
+// neurons (both rows), halved while fewer than four slots fit; the shared
+// expert's chunk and the down chunks are cut to the slot.  Returns false
+// when two slots of one neuron pair do not fit.
+static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, unsigned limit, LayerSmem* out) {
   const unsigned d = c->g.hidden, P = d / 64;
-  const unsigned limit = 227 * 1024;
   if ((T * d / 4 + kActThreads - 1) / kActThreads > kMaxRounds) return false;
   LayerSmem m{};
   unsigned o = 64 + 256;  // mbarriers, then 64 misc words
@@ -189,7 +193,7 @@ static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, L
   m.upre = take(4 * (kMaxUnique + 1));
   m.rms = take(4 * T);
   m.bases = take(8 * kMaxBlocks);
-  m.rpart = take(4 * 8 * kMaxRounds);
+  m.rpart = take(4 * kActWarps * kMaxRounds);
   m.tokpair = take(2 * (T * 11));
   if (act == FRC_ACT_Q8) {
     m.xq = take(T * d);
@@ -210,10 +214,10 @@ static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, L
   const unsigned srow = static_cast<unsigned>(c->shared_row);
   const unsigned ss_r = c->g.down_type == FRC_Q8_0 ? 2 : 1, pb_r = c->g.down_type == FRC_Q8_0 ? 32 : 16;
   unsigned kn = 16;
-  while (kn > 1 && avail / (2 * kn * rowb) < 4) kn /= 2;
+  while (kn > 4 && avail / (2 * kn * rowb) < 4) kn /= 2;
   unsigned slot = 2 * kn * rowb;
-  // the smallest shared chunk (one neuron) and down chunk (16 rows) must fit too
-  slot = slot > 2 * srow ? slot : 2 * srow;
+  // the smallest shared chunk (four neurons) and down chunk (16 rows) must fit too
+  slot = slot > 8 * srow ? slot : 8 * srow;
   slot = slot > 16 * 34 ? slot : 16 * 34;
   slot = align_up(slot, 128);
   unsigned K = avail / slot;
@@ -224,6 +228,7 @@ static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, L
   K = K < kMaxSlots ? K : kMaxSlots;
   unsigned kns = 16;
   while (kns > 1 && 2 * kns * srow > slot) kns /= 2;
+  if (kn < 4 || kns < 4) return false;  // a gate/up chunk holds at least one warp's four neurons
   auto down_rows = [&](unsigned per_row) {
     unsigned dn = slot / per_row / 16 * 16;
     dn = dn < d ? dn : d;
@@ -250,18 +255,33 @@ static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s, bool ove
     CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
     c->attr_set[ai] = true;
   }
-  // one CTA per SM, all resident (the kernel has a grid barrier)
-  const unsigned G = static_cast<unsigned>(c->sms);
-  if (!smem_layout(c, a.T, G, ACT, &a.sm)) return fail(c, FRC_INVALID, "%u tokens need too much shared memory", a.T);
-  int per_sm = 0;
-  if (c->occ_smem[ai] == a.sm.total) {
-    per_sm = c->occ_val[ai];
-  } else {
-    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kLayerThreads, a.sm.total));
-    c->occ_smem[ai] = a.sm.total;
-    c->occ_val[ai] = per_sm;
+  // Two CTAs an SM when their shared memory fits, else one; all resident
+  // (the kernel has a grid barrier).
+  auto occupancy = [&](unsigned bytes, int* per_sm) -> int {
+    if (c->occ_smem[ai] == bytes) {
+      *per_sm = c->occ_val[ai];
+      return FRC_OK;
+    }
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, kern, kLayerThreads, bytes));
+    c->occ_smem[ai] = bytes;
+    c->occ_val[ai] = *per_sm;
+    return FRC_OK;
+  };
+  unsigned per = 2, G = 2 * static_cast<unsigned>(c->sms);
+  int per_sm = 0, orc;
+  bool fits = smem_layout(c, a.T, G, ACT, kSmemTwoPerSm, &a.sm);
+  if (fits) {
+    if ((orc = occupancy(a.sm.total, &per_sm))) return orc;
+    fits = per_sm >= 2;
   }
-  if (per_sm < 1) return fail(c, FRC_INVALID, "layer kernel does not fit an SM (%u bytes)", a.sm.total);
+  if (!fits) {
+    per = 1;
+    G = static_cast<unsigned>(c->sms);
+    if (!smem_layout(c, a.T, G, ACT, kSmemOnePerSm, &a.sm))
+      return fail(c, FRC_INVALID, "%u tokens need too much shared memory", a.T);
+    if ((orc = occupancy(a.sm.total, &per_sm))) return orc;
+  }
+  if (per_sm < static_cast<int>(per)) return fail(c, FRC_INVALID, "layer kernel does not fit an SM (%u bytes)", a.sm.total);
   // Co-residency of the grid (one CTA per SM, checked above) is what the grid
   // barrier needs.  A plain launch asks the runtime to check it; an overlapped
   // launch (programmatic stream serialization) gets it as the previous
@@ -276,6 +296,7 @@ static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s, bool ove
     attr[0].val.cooperative = 1;
   }
   cfg.gridDim = dim3(G);
+  c->last_G = G;
   cfg.blockDim = dim3(kLayerThreads);
   cfg.dynamicSmemBytes = a.sm.total;
   cfg.stream = s;
@@ -744,7 +765,7 @@ int frc_debug_hidden(frc_context* c, float* h, size_t cap, size_t* count) {
 
 int frc_debug_phases(frc_context* c, uint64_t* out, size_t cap, size_t* count) {
   if (!c || !count) return FRC_INVALID;
-  *count = 16 * static_cast<size_t>(c->sms);
+  *count = 16 * static_cast<size_t>(c->last_G ? c->last_G : c->sms);
 #ifndef FRC_PHASES
   return fail(c, FRC_UNSUPPORTED, "built without FRC_PHASES");
 #else

@@ -90,6 +90,15 @@ __device__ __forceinline__ bool spin_geq(const unsigned* p, unsigned target, con
   }
   return true;
 }
+// Division by a run-time divisor 1 <= dv < 2^16 through multiply-high:
+// exact for dividends x < 2^16.
+struct Div {
+  unsigned dv, m;
+  __device__ __forceinline__ explicit Div(unsigned v) : dv(v), m(v > 1 ? 0xffffffffu / v + 1 : 0) {}
+  __device__ __forceinline__ unsigned q(unsigned x) const { return dv > 1 ? __umulhi(x, m) : x; }
+  __device__ __forceinline__ unsigned r(unsigned x) const { return x - q(x) * dv; }
+};
+
 // Generic-form byte permute: msb of a selector nibble replicates the sign.
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
@@ -165,8 +174,15 @@ __device__ __forceinline__ unsigned prmt_pos(unsigned n) {
   const unsigned j = n & 15, hi = n >> 4, m = j >> 2, r = j & 3;
   return 4 * (2 * m + (r >> 1)) + 2 * (r & 1) + hi;
 }
-// uint4 slot of quad q (0..3) of x group p in the swizzled activation layout.
-__device__ __forceinline__ unsigned xslot(unsigned p, unsigned q) { return 4 * p + (q ^ ((p >> 1) & 3)); }
+// uint4 slot of quad q (0..3) of x group p in the activation layout.  Groups
+// are stored span-interleaved, position (p % 4) * nspan + p / 4 (nspan = d /
+// 256), so the eight lanes of a row reading group p % 4 of consecutive spans
+// read consecutive positions; the four quads of a position are swizzled
+// across the 128-byte bank window.  Conflict-free for those reads.
+__device__ __forceinline__ unsigned xslot(unsigned p, unsigned q, unsigned nspan) {
+  const unsigned pos = (p & 3) * nspan + (p >> 2);
+  return 4 * pos + (q ^ ((pos >> 1) & 3));
+}
 
 // ----------------------------------------------------- gate/up pair terms
 // One lane's term for x group p (64 weights = two 32-weight blocks) of a
@@ -179,12 +195,19 @@ struct XQ {  // one token's quantized activations in shared memory
   const float* v;     // per-32 sums of q, d/32
 };
 
-__device__ __forceinline__ void load_x16(const uint8_t* xq, unsigned p, uint32_t (&x)[16]) {
+__device__ __forceinline__ void load_x16(const uint8_t* xq, unsigned p, unsigned nspan, uint32_t (&x)[16]) {
 #pragma unroll
   for (unsigned q = 0; q < 4; ++q) {
-    const uint4 w = *reinterpret_cast<const uint4*>(xq + 16 * xslot(p, q));
+    const uint4 w = *reinterpret_cast<const uint4*>(xq + 16 * xslot(p, q, nspan));
     x[4 * q] = w.x; x[4 * q + 1] = w.y; x[4 * q + 2] = w.z; x[4 * q + 3] = w.w;
   }
+}
+
+// dp4a with unsigned bytes in a and signed bytes in b.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
 
 // Q4_K: super-block p/4, sub-blocks 2(p%4) and 2(p%4)+1.
@@ -210,8 +233,9 @@ __device__ __forceinline__ float term_q4k(const uint8_t* row, unsigned p, const 
 #pragma unroll
   for (unsigned m = 0; m < 8; ++m) {
     i0 = __dp4a(static_cast<int>(w[m] & 0x0f0f0f0fu), static_cast<int>(x[m]), i0);
-    i1 = __dp4a(static_cast<int>((w[m] >> 4) & 0x0f0f0f0fu), static_cast<int>(x[8 + m]), i1);
+    i1 = dp4a_us(w[m] & 0xf0f0f0f0u, x[8 + m], i1);  // 16x the high-nibble dot
   }
+  i1 >>= 4;  // exact: a multiple of 16
   const float dot = __fmaf_rn(ds1, i2f(i1), __fmul_rn(ds0, i2f(i0)));
   const float mins = __fmaf_rn(dm1, v1, __fmul_rn(dm0, v0));
   return __fsub_rn(dot, mins);

@@ -1,5 +1,6 @@
 // frc_layer.cuh - the MoE layer kernel (sm_100a): one cooperative launch per
-// layer, one 512-thread CTA per SM, item-major work.
+// layer of 256-thread CTAs, two per SM when their shared memory fits (one
+// otherwise), item-major work.
 //
 // An item is (unique expert u, loaded slice s): 32 neurons, their gate and up
 // rows and their columns of the down projection, all in one region of the
@@ -9,23 +10,24 @@
 // chip.
 //
 //   prologue - routing and x are loaded at once and the plan (unique
-//     experts, token masks, (expert, token) pairs) is built.  Warp 8 starts
-//     the TMA ring (cp.async.bulk, one mbarrier a slot) on the CTA's first
-//     chunks; warps 0-7 form the layer input and quantize it meanwhile.
-//   items - per item: gate/up chunks (a warp per neuron, or per row when a
-//     chunk has fewer neurons than warps), SwiGLU in double and the Q8
-//     quantization of the hidden slice (one group of 32) in shared memory,
-//     then the down chunk(s), a thread per row: c = scale * int_dot goes to
-//     the partial buffer [pair][slice][row].  The last warp to finish with a
+//     experts, token masks, (expert, token) pairs) is built by warps 4-7;
+//     warp 4 starts the TMA ring (cp.async.bulk, one mbarrier a slot) on the
+//     CTA's first chunks; warps 0-3 form the layer input and quantize it
+//     meanwhile.
+//   items - per item: gate/up chunks (a warp per four neurons, eight lanes a
+//     neuron, which also form its SwiGLU in double), the Q8 quantization of
+//     the hidden slice (one group of 32) in shared memory, then the down chunk(s), a thread per
+//     row: c = scale * int_dot goes to the partial buffer [pair][slice][row].  The last warp to finish with a
 //     ring slot refills it, so loads stream with no producer warp.
 //   grid barrier (bounded wait).
-//   reduce - CTA k owns rows [d*k/G, d*(k+1)/G) of every token: per (token,
+//   reduce - CTA k owns 4-row units [d/4*k/G, d/4*(k+1)/G) of every token: per (token,
 //     row, routing slot) four slice-interleaved fmaf chains of c * gs,
 //     combined ((p0+p1)+p2)+p3; then the token's routed experts in its own
 //     routing order, then the shared expert.
 //
-// Arithmetic order (restated by the oracle's or_port_run): gate/up lanes take
-// x groups p = lane, lane+32, ...; butterfly sum; the reduce above.  Results
+// Arithmetic order (restated by the oracle's or_port_run): eight lanes a
+// gate/up row, lane l taking the 256-element spans l, l+8, ... (groups in
+// order); butterfly over the eight; the reduce above.  Results
 // are bitwise repeatable and a token's output does not depend on the rest of
 // the burst.
 #pragma once
@@ -33,12 +35,16 @@
 
 namespace frc {
 
-constexpr unsigned kLayerThreads = 512;
+constexpr unsigned kLayerThreads = 256;        // two CTAs an SM when their shared memory fits
 constexpr unsigned kLayerWarps = kLayerThreads / 32;
-constexpr unsigned kActThreads = 256;          // warps 0-7: activations
+constexpr unsigned kActThreads = 128;          // warps 0-3 form the layer input
+constexpr unsigned kActWarps = kActThreads / 32;
+constexpr unsigned kPlanWarps = 4;             // warps 4-7 build the plan
+constexpr unsigned kPlanThreads = 32 * kPlanWarps;
+constexpr unsigned kFirstPlanWarp = kLayerWarps - kPlanWarps;
 constexpr unsigned kMaxSlots = 8;              // TMA ring depth limit
 constexpr unsigned kXRegs = 4;                 // float4 activations a thread keeps in registers
-constexpr unsigned kMaxRounds = 128;           // 256-float4 rounds of the activation pass
+constexpr unsigned kMaxRounds = 256;           // 128-float4 rounds of the activation pass
 
 struct LayerCtl {
   unsigned long long arrived;   // grid barrier arrivals, all launches (never wraps)
@@ -89,10 +95,10 @@ __device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long l
   asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-// Barrier among the activation warps (0-7) only.
-__device__ __forceinline__ void act_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-// Barrier among the plan warps (8-15) only.
-__device__ __forceinline__ void plan_sync() { asm volatile("bar.sync 2, 256;" ::: "memory"); }
+// Barrier among the activation warps (0-3) only.
+__device__ __forceinline__ void act_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Barrier among the plan warps (4-7) only.
+__device__ __forceinline__ void plan_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 
 // Bounded barrier over the co-resident grid, one round trip: every CTA adds
 // itself to a counter that only grows and waits for the next multiple of the
@@ -133,7 +139,7 @@ __device__ __forceinline__ bool grid_sync(LayerCtl* ctl, unsigned* flag_smem) {
 #define PHASE(k) PHASE_AT(k, 0)
 
 template <int ACT>
-__global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const LayerParams a) {
+__global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const LayerParams a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);                // kMaxSlots mbarriers
   unsigned* misc = reinterpret_cast<unsigned*>(smem + 64);           // 64 words
@@ -148,8 +154,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
   float* s_rms = reinterpret_cast<float*>(smem + a.sm.rms);
   float* s_rpart = reinterpret_cast<float*>(smem + a.sm.rpart);      // [round][warp] sums of squares
   uint16_t* s_tokpair = reinterpret_cast<uint16_t*>(smem + a.sm.tokpair);  // [token][11] -> pair
-  float* s_gv = reinterpret_cast<float*>(smem + a.sm.gv);            // [neuron][k] gate dots
-  float* s_uv = reinterpret_cast<float*>(smem + a.sm.uv);            // [neuron][k] up dots
+  float* s_gv = reinterpret_cast<float*>(smem + a.sm.gv);            // [neuron][k] hidden values
   uint8_t* s_hq = smem + a.sm.hq;                                    // [k][32] int8, or [k][32] f32
   uint8_t* ring = smem + a.sm.ring;
   const unsigned SLOT = a.sm.slot_bytes, K = a.sm.slots;
@@ -221,9 +226,162 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
     }
   };
 
-  if (warp < kActThreads / 32) {
-    // ------------------------------------------- warps 0-7: activations
-    // (needs only x: runs while warps 8-15 plan and start the weight copies)
+  if (warp >= kFirstPlanWarp) {
+    // ------------------------------------------------- warps 4-7: plan
+    const unsigned ptid = tid - 32 * kFirstPlanWarp, pw = warp - kFirstPlanWarp;
+    if (ptid < kMaxSlots) s_cnt[ptid] = 0;
+    if (T == 1) {
+      // one token: its ten experts in request order are the unique experts,
+      // each with one (expert, token) pair
+      if (pw == 0) {
+        unsigned id = 0;
+        float gv = 0.0f;
+        if (lane < 10) {
+          id = a.expert[lane];
+          gv = a.gate[lane];
+          if (id >= 512) {
+            atomicOr(a.status, kStInvalid);
+            id = 0;  // keeps every address in range; the launch reports INVALID
+          }
+        }
+        const float sg = a.gate[10];
+        if (lane < 10) {
+          s_uid[lane] = static_cast<uint16_t>(id);
+          s_umask[lane] = 1;
+          s_ugate[lane] = gv;
+        }
+        if (lane == 10 && sg != 0.0f) {
+          s_uid[10] = 512;
+          s_umask[10] = 1;
+          s_ugate[10] = sg;
+        }
+        if (lane < 12) s_upre[lane] = lane;
+        if (lane < 11) s_tokpair[lane] = static_cast<uint16_t>(lane < 10 ? lane : (sg != 0.0f ? 10u : 0xffffu));
+        if (lane == 0) {
+          misc[4] = 10;
+          misc[5] = sg != 0.0f ? 1u : 0u;
+        }
+        PHASE_AT(8, kPlanThreads);
+      }
+    } else {
+      for (unsigned i = ptid; i < T * 10; i += kPlanThreads) s_ids[i] = a.expert[i];
+      for (unsigned i = ptid; i < T * 11; i += kPlanThreads) s_g[i] = a.gate[i];
+      for (unsigned i = ptid; i < 512; i += kPlanThreads) s_first[i] = 0x7fffffff;
+      for (unsigned i = ptid; i < kMaxUnique; i += kPlanThreads) s_umask[i] = 0;
+      for (unsigned i = ptid; i < kMaxUnique * T; i += kPlanThreads) s_ugate[i] = 0.0f;
+      plan_sync();
+      PHASE_AT(8, kPlanThreads);
+      bool invalid = false;
+      for (unsigned i = ptid; i < T * 10; i += kPlanThreads) {
+        const unsigned id = s_ids[i];
+        if (id < 512) atomicMin(&s_first[id], static_cast<int>(i));
+        else invalid = true;
+      }
+      if (invalid) atomicOr(a.status, kStInvalid);
+      plan_sync();
+      // unique experts in first-appearance order: rank = earlier first
+      // appearances; up to 160 entries, 128 at a time
+      unsigned total = 0;
+      for (unsigned base = 0; base < T * 10; base += kPlanThreads) {
+        const unsigned i = base + ptid;
+        const unsigned id = i < T * 10 ? s_ids[i] : 0xffffu;
+        const bool first = id < 512 && s_first[id] == static_cast<int>(i);
+        const unsigned ballot = __ballot_sync(0xffffffffu, first);
+        if (lane == 0) misc[16 + pw] = __popc(ballot);
+        plan_sync();
+        unsigned off = total, all = 0;
+        for (unsigned w = 0; w < kPlanWarps; ++w) {
+          if (w < pw) off += misc[16 + w];
+          all += misc[16 + w];
+        }
+        plan_sync();  // every first-appearance test of this round is done; misc is free
+        if (first) {
+          const unsigned rank = off + __popc(ballot & ((1u << lane) - 1));
+          s_uid[rank] = static_cast<uint16_t>(id);
+          s_first[id] = -1 - static_cast<int>(rank);
+        }
+        total += all;
+      }
+      if (ptid == 0) misc[4] = total;  // routed experts
+      plan_sync();
+      for (unsigned k = ptid; k < T * 10; k += kPlanThreads) {
+        const unsigned id = s_ids[k];
+        if (id >= 512) continue;
+        const unsigned u = static_cast<unsigned>(-1 - s_first[id]), t = k / 10;
+        atomicOr(&s_umask[u], 1u << t);
+        s_ugate[u * T + t] = s_g[t * 11 + k % 10];
+      }
+      plan_sync();
+      const unsigned ur = misc[4];
+      unsigned shared_mask = 0;
+      for (unsigned t = 0; t < T; ++t)
+        if (s_g[t * 11 + 10] != 0.0f) shared_mask |= 1u << t;
+      const unsigned nu = ur + (shared_mask ? 1 : 0);
+      if (ptid == 0) {
+        misc[5] = shared_mask;
+        if (shared_mask) {
+          s_uid[ur] = 512;
+          s_umask[ur] = shared_mask;
+        }
+      }
+      if (shared_mask)
+        for (unsigned t = ptid; t < T; t += kPlanThreads) s_ugate[ur * T + t] = s_g[t * 11 + 10];
+      plan_sync();
+      if (pw == 0) {  // pair offsets: exclusive scan of the token counts, 6 experts a lane
+        unsigned cnt[6], tot = 0;
+    #pragma unroll
+        for (unsigned k = 0; k < 6; ++k) {
+          const unsigned u = lane * 6 + k;
+          cnt[k] = u < nu ? __popc(s_umask[u]) : 0;
+          tot += cnt[k];
+        }
+        unsigned inc = tot;
+    #pragma unroll
+        for (unsigned o = 1; o < 32; o <<= 1) {
+          const unsigned v = __shfl_up_sync(0xffffffffu, inc, o);
+          if (lane >= o) inc += v;
+        }
+        unsigned run = inc - tot;
+    #pragma unroll
+        for (unsigned k = 0; k < 6; ++k) {
+          const unsigned u = lane * 6 + k;
+          if (u <= nu) s_upre[u] = run;
+          run += cnt[k];
+        }
+      }
+      plan_sync();
+      for (unsigned k = ptid; k < T * 11; k += kPlanThreads) {  // (token, routing slot) -> pair
+        const unsigned t = k / 11, e = k % 11;
+        unsigned pair = 0xffff;
+        if (e < 10) {
+          const unsigned id = s_ids[t * 10 + e];
+          if (id < 512) {
+            const unsigned u = static_cast<unsigned>(-1 - s_first[id]);
+            pair = s_upre[u] + __popc(s_umask[u] & ((1u << t) - 1));
+          }
+        } else if (shared_mask >> t & 1) {
+          pair = s_upre[ur] + __popc(shared_mask & ((1u << t) - 1));
+        }
+        s_tokpair[k] = static_cast<uint16_t>(pair);
+      }
+    }
+    plan_sync();
+    PHASE_AT(10, kPlanThreads);
+    if (pw == 0) {  // the first K chunks, while the activations are still being formed
+      if (lane == 0) {
+        for (unsigned k = 0; k < K; ++k) mbar_init(&full[k], 1);
+        fence_mbar_init();
+      }
+      __syncwarp();
+      setup();
+      if (lane < K && lane < n_ch) issue(lane);
+      PHASE_AT(1, kPlanThreads);
+    }
+    pdl_wait();
+  }
+  if (warp < kActWarps) {
+    // ------------------------------------------- warps 0-3: layer input
+    // (needs only x: runs while warps 4-7 plan and start the weight copies)
     pdl_wait();
     float4 xv4[kXRegs];
     if (xregs) {
@@ -273,26 +431,27 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
         }
 #pragma unroll
         for (unsigned o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-        if (lane == 0) s_rpart[r * 8 + warp] = ss;
+        if (lane == 0) s_rpart[r * kActWarps + warp] = ss;
       }
       act_sync();
       PHASE(2);
+      // token t's sums are the warp-rounds (32 float4 each, index r * 4 + w)
+      // [t * d/128, (t+1) * d/128), added in that order
       for (unsigned t = tid; t < T; t += kActThreads) {
         float tot = 0.0f;
-        for (unsigned r = 0; r < rounds; ++r)
-          for (unsigned w = 0; w < 8; ++w) {
-            const unsigned f = r * kActThreads + w * 32;
-            if (f < nvec && f / per_token == t) tot = __fadd_rn(tot, s_rpart[r * 8 + w]);
-          }
+        const unsigned per = d / 128;
+        for (unsigned b = t * per; b < (t + 1) * per; ++b) tot = __fadd_rn(tot, s_rpart[b]);
         s_rms[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(d)), 1e-6f)));
       }
       act_sync();
     }
+    // f / per_token by multiply-high: exact for f < 2^16, per_token <= 2048
+    const unsigned pt_magic = 0xffffffffu / per_token + 1;
     for (unsigned r = 0; r < rounds; ++r) {
       const unsigned f = r * kActThreads + tid;
       if (f >= nvec) continue;  // warp-uniform: nvec is a multiple of 128
       float4 v = load4(f, r);
-      const unsigned t = f / per_token, j = f % per_token;
+      const unsigned t = __umulhi(f, pt_magic), j = f - t * per_token;
       bad |= !isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w);
       if (a.x_out && cta == 0) reinterpret_cast<float4*>(a.x_out)[f] = v;
       if (a.norm) {
@@ -315,7 +474,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
       const unsigned p = j / 16, wq = j % 16;
       uint8_t* xt = smem + a.sm.xq + t * d;
       const uint32_t word = (q0 & 0xff) | (q1 & 0xff) << 8 | (q2 & 0xff) << 16 | static_cast<uint32_t>(q3 & 0xff) << 24;
-      *reinterpret_cast<uint32_t*>(xt + 16 * xslot(p, wq / 4) + 4 * (wq % 4)) = word;
+      *reinterpret_cast<uint32_t*>(xt + 16 * xslot(p, wq / 4, d / 256) + 4 * (wq % 4)) = word;
       if ((lane & 15) == 0) reinterpret_cast<float*>(smem + a.sm.xs)[t * P + p] = scale;
       if ((lane & 7) == 0)
         reinterpret_cast<float*>(smem + a.sm.xv)[t * 2 * P + 2 * p + ((lane >> 3) & 1)] = static_cast<float>(sum);
@@ -325,152 +484,11 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
 #pragma unroll
         for (unsigned i = 0; i < 4; ++i) {
           const unsigned e = 4 * j + i, wi = (e % 64) / 32 * 32 + prmt_pos(e % 32);
-          xp[16 * xslot(p, wi / 16) + wi % 16] = static_cast<uint8_t>(qv[i] & 0xff);
+          xp[16 * xslot(p, wi / 16, d / 256) + wi % 16] = static_cast<uint8_t>(qv[i] & 0xff);
         }
       }
     }
     if (bad) atomicOr(a.status, kStNumeric);
-  } else {
-    // ------------------------------------------------ warps 8-15: plan
-    const unsigned ptid = tid - kActThreads, pw = warp - kActThreads / 32;
-    if (ptid < kMaxSlots) s_cnt[ptid] = 0;
-    if (T == 1) {
-      // one token: its ten experts in request order are the unique experts,
-      // each with one (expert, token) pair
-      if (warp == 8) {
-        unsigned id = 0;
-        float gv = 0.0f;
-        if (lane < 10) {
-          id = a.expert[lane];
-          gv = a.gate[lane];
-          if (id >= 512) {
-            atomicOr(a.status, kStInvalid);
-            id = 0;  // keeps every address in range; the launch reports INVALID
-          }
-        }
-        const float sg = a.gate[10];
-        if (lane < 10) {
-          s_uid[lane] = static_cast<uint16_t>(id);
-          s_umask[lane] = 1;
-          s_ugate[lane] = gv;
-        }
-        if (lane == 10 && sg != 0.0f) {
-          s_uid[10] = 512;
-          s_umask[10] = 1;
-          s_ugate[10] = sg;
-        }
-        if (lane < 12) s_upre[lane] = lane;
-        if (lane < 11) s_tokpair[lane] = static_cast<uint16_t>(lane < 10 ? lane : (sg != 0.0f ? 10u : 0xffffu));
-        if (lane == 0) {
-          misc[4] = 10;
-          misc[5] = sg != 0.0f ? 1u : 0u;
-        }
-        PHASE_AT(8, kActThreads);
-      }
-    } else {
-      for (unsigned i = ptid; i < T * 10; i += kActThreads) s_ids[i] = a.expert[i];
-      for (unsigned i = ptid; i < T * 11; i += kActThreads) s_g[i] = a.gate[i];
-      for (unsigned i = ptid; i < 512; i += kActThreads) s_first[i] = 0x7fffffff;
-      for (unsigned i = ptid; i < kMaxUnique; i += kActThreads) s_umask[i] = 0;
-      for (unsigned i = ptid; i < kMaxUnique * T; i += kActThreads) s_ugate[i] = 0.0f;
-      plan_sync();
-      PHASE_AT(8, kActThreads);
-      bool invalid = false;
-      for (unsigned i = ptid; i < T * 10; i += kActThreads) {
-        const unsigned id = s_ids[i];
-        if (id < 512) atomicMin(&s_first[id], static_cast<int>(i));
-        else invalid = true;
-      }
-      if (invalid) atomicOr(a.status, kStInvalid);
-      plan_sync();
-      // unique experts in first-appearance order: rank = earlier first appearances
-      const unsigned i = ptid;  // T*10 <= 160 < 256
-      const bool first = i < T * 10 && s_ids[i] < 512 && s_first[s_ids[i]] == static_cast<int>(i);
-      const unsigned ballot = __ballot_sync(0xffffffffu, first);
-      if (lane == 0) misc[16 + pw] = __popc(ballot);
-      plan_sync();
-      unsigned off = 0;
-      for (unsigned w = 0; w < pw; ++w) off += misc[16 + w];
-      const unsigned rank = off + __popc(ballot & ((1u << lane) - 1));
-      if (ptid == kActThreads - 1) misc[4] = off + __popc(ballot);  // routed experts
-      if (first) s_uid[rank] = s_ids[i];
-      plan_sync();
-      if (first) s_first[s_ids[i]] = -1 - static_cast<int>(rank);
-      plan_sync();
-      for (unsigned k = ptid; k < T * 10; k += kActThreads) {
-        const unsigned id = s_ids[k];
-        if (id >= 512) continue;
-        const unsigned u = static_cast<unsigned>(-1 - s_first[id]), t = k / 10;
-        atomicOr(&s_umask[u], 1u << t);
-        s_ugate[u * T + t] = s_g[t * 11 + k % 10];
-      }
-      plan_sync();
-      const unsigned ur = misc[4];
-      unsigned shared_mask = 0;
-      for (unsigned t = 0; t < T; ++t)
-        if (s_g[t * 11 + 10] != 0.0f) shared_mask |= 1u << t;
-      const unsigned nu = ur + (shared_mask ? 1 : 0);
-      if (ptid == 0) {
-        misc[5] = shared_mask;
-        if (shared_mask) {
-          s_uid[ur] = 512;
-          s_umask[ur] = shared_mask;
-        }
-      }
-      if (shared_mask)
-        for (unsigned t = ptid; t < T; t += kActThreads) s_ugate[ur * T + t] = s_g[t * 11 + 10];
-      plan_sync();
-      if (warp == 8) {  // pair offsets: exclusive scan of the token counts, 6 experts a lane
-        unsigned cnt[6], tot = 0;
-    #pragma unroll
-        for (unsigned k = 0; k < 6; ++k) {
-          const unsigned u = lane * 6 + k;
-          cnt[k] = u < nu ? __popc(s_umask[u]) : 0;
-          tot += cnt[k];
-        }
-        unsigned inc = tot;
-    #pragma unroll
-        for (unsigned o = 1; o < 32; o <<= 1) {
-          const unsigned v = __shfl_up_sync(0xffffffffu, inc, o);
-          if (lane >= o) inc += v;
-        }
-        unsigned run = inc - tot;
-    #pragma unroll
-        for (unsigned k = 0; k < 6; ++k) {
-          const unsigned u = lane * 6 + k;
-          if (u <= nu) s_upre[u] = run;
-          run += cnt[k];
-        }
-      }
-      plan_sync();
-      for (unsigned k = ptid; k < T * 11; k += kActThreads) {  // (token, routing slot) -> pair
-        const unsigned t = k / 11, e = k % 11;
-        unsigned pair = 0xffff;
-        if (e < 10) {
-          const unsigned id = s_ids[t * 10 + e];
-          if (id < 512) {
-            const unsigned u = static_cast<unsigned>(-1 - s_first[id]);
-            pair = s_upre[u] + __popc(s_umask[u] & ((1u << t) - 1));
-          }
-        } else if (shared_mask >> t & 1) {
-          pair = s_upre[ur] + __popc(shared_mask & ((1u << t) - 1));
-        }
-        s_tokpair[k] = static_cast<uint16_t>(pair);
-      }
-    }
-    plan_sync();
-    PHASE_AT(10, kActThreads);
-    if (warp == 8) {  // the first K chunks, while the activations are still being formed
-      if (lane == 0) {
-        for (unsigned k = 0; k < K; ++k) mbar_init(&full[k], 1);
-        fence_mbar_init();
-      }
-      __syncwarp();
-      setup();
-      if (lane < K && lane < n_ch) issue(lane);
-      PHASE_AT(1, kActThreads);
-    }
-    pdl_wait();
   }
   __syncthreads();
   setup();
@@ -508,72 +526,74 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
     const unsigned rowb = sh ? a.shared_row : a.row_bytes, nb = d / 32;
     const unsigned kn = sh ? kn_s : kn_r, ngu = sh ? ngu_s : ngu_r, dn = sh ? dn_s : dn_r, ndn = sh ? ndn_s : ndn_r;
     const unsigned mask = s_umask[u], nt = __popc(mask), gp0 = s_upre[u];
-    // gate/up: a task is a neuron (both rows, sharing the x loads) when the
-    // chunk has a neuron for every warp, else a single row
-    const bool by_neuron = kn >= kLayerWarps;
-    const unsigned ntask = by_neuron ? kn : 2 * kn;
+    // gate/up: warp w takes neurons 4 (w % (kn/4)) .. +3 of chunk w / (kn/4),
+    // eight lanes a neuron.  Lane l8 takes the 256-element spans q = l8,
+    // l8+8, ... of both the gate and the up row (they share the x loads),
+    // groups in order; butterfly over the eight lanes; lane l8 == 0 then
+    // forms the neuron's SwiGLU (double, backends/ref.c:81-83).
+    const unsigned quads = kn / 4, my_chunk = warp / quads, l8 = lane & 7, nspan = d / 256;
     for (unsigned k = 0; k < ngu; ++k, ++c) {
-      if (wait_chunk(c)) {
+      if (wait_chunk(c) && k == my_chunk) {
         if (c == 0) PHASE(15);
         if (c == 1) PHASE(12);
         const uint8_t* slot = ring + (c % K) * SLOT;
-        for (unsigned task = warp; task < ntask; task += kLayerWarps) {
-          const bool up_only = !by_neuron && task >= kn;
-          const unsigned nl = up_only ? task - kn : task;   // neuron within the chunk
-          const uint8_t* r1 = slot + (up_only ? kn + nl : nl) * rowb;   // gate row (or the up row)
-          const uint8_t* r2 = slot + (kn + nl) * rowb;                   // up row when by_neuron
-          const unsigned n = k * kn + nl;
-          unsigned mm = mask;
-          for (unsigned kk = 0; kk < nt; ++kk) {
-            const unsigned t = __ffs(mm) - 1;
-            mm &= mm - 1;
-            float a1 = 0.0f, a2 = 0.0f;
-            if (ACT == FRC_ACT_Q8) {
-              const uint8_t* xq = smem + (type == kMXFP4 ? a.sm.xp : a.sm.xq) + t * d;
-              const float* xs = reinterpret_cast<const float*>(smem + a.sm.xs) + t * P;
-              const float* xv = reinterpret_cast<const float*>(smem + a.sm.xv) + t * 2 * P;
-              for (unsigned p = lane; p < P; p += 32) {
+        const unsigned nl = 4 * (warp % quads) + (lane >> 3);  // neuron within the chunk
+        const uint8_t* gr = slot + nl * rowb;
+        const uint8_t* ur = slot + (kn + nl) * rowb;
+        const unsigned n = k * kn + nl;
+        unsigned mm = mask;
+        for (unsigned kk = 0; kk < nt; ++kk) {
+          const unsigned t = __ffs(mm) - 1;
+          mm &= mm - 1;
+          float ag = 0.0f, au = 0.0f;
+          if (ACT == FRC_ACT_Q8) {
+            const uint8_t* xq = smem + (type == kMXFP4 ? a.sm.xp : a.sm.xq) + t * d;
+            const float* xs = reinterpret_cast<const float*>(smem + a.sm.xs) + t * P;
+            const float* xv = reinterpret_cast<const float*>(smem + a.sm.xv) + t * 2 * P;
+            for (unsigned q = l8; q < nspan; q += 8) {
+#pragma unroll
+              for (unsigned gp = 0; gp < 4; ++gp) {
+                const unsigned p = 4 * q + gp;
                 uint32_t xw[16];
-                load_x16(xq, p, xw);
-                float t1, t2 = 0.0f;
+                load_x16(xq, p, nspan, xw);
+                float tg, tu;
                 if (type == kQ4K) {
                   const float v0 = xv[2 * p], v1 = xv[2 * p + 1];
-                  t1 = term_q4k(r1, p, xw, v0, v1, bad);
-                  if (by_neuron) t2 = term_q4k(r2, p, xw, v0, v1, bad);
+                  tg = term_q4k(gr, p, xw, v0, v1, bad);
+                  tu = term_q4k(ur, p, xw, v0, v1, bad);
                 } else if (type == kMXFP4) {
-                  t1 = term_mxfp4(r1, nb, p, xw, bad);
-                  if (by_neuron) t2 = term_mxfp4(r2, nb, p, xw, bad);
+                  tg = term_mxfp4(gr, nb, p, xw, bad);
+                  tu = term_mxfp4(ur, nb, p, xw, bad);
                 } else {
-                  t1 = term_q80(r1, nb, p, xw, bad);
-                  if (by_neuron) t2 = term_q80(r2, nb, p, xw, bad);
+                  tg = term_q80(gr, nb, p, xw, bad);
+                  tu = term_q80(ur, nb, p, xw, bad);
                 }
-                a1 = __fmaf_rn(xs[p], t1, a1);
-                a2 = __fmaf_rn(xs[p], t2, a2);
+                ag = __fmaf_rn(xs[p], tg, ag);
+                au = __fmaf_rn(xs[p], tu, au);
               }
-            } else {
-              const float* xf = reinterpret_cast<const float*>(smem + a.sm.xf) + t * d;
-              for (unsigned p = lane; p < P; p += 32)
-                for (unsigned jj = 0; jj < 64; ++jj) {
-                  const unsigned e = 64 * p + jj;
-                  const float w1 = weight_any(r1, type, d, e);
-                  bad |= !isfinite(w1);
-                  a1 = __fmaf_rn(w1, xf[e], a1);
-                  if (by_neuron) {
-                    const float w2 = weight_any(r2, type, d, e);
-                    bad |= !isfinite(w2);
-                    a2 = __fmaf_rn(w2, xf[e], a2);
-                  }
-                }
             }
+          } else {
+            const float* xf = reinterpret_cast<const float*>(smem + a.sm.xf) + t * d;
+            for (unsigned q = l8; q < nspan; q += 8)
+              for (unsigned e = 256 * q; e < 256 * q + 256; ++e) {
+                const float wg = weight_any(gr, type, d, e), wu = weight_any(ur, type, d, e);
+                bad |= !isfinite(wg) || !isfinite(wu);
+                ag = __fmaf_rn(wg, xf[e], ag);
+                au = __fmaf_rn(wu, xf[e], au);
+              }
+          }
 #pragma unroll
-            for (unsigned o = 16; o; o >>= 1) {
-              a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, o));
-              a2 = __fadd_rn(a2, __shfl_xor_sync(0xffffffffu, a2, o));
+          for (unsigned o = 4; o; o >>= 1) {
+            ag = __fadd_rn(ag, __shfl_xor_sync(0xffffffffu, ag, o));
+            au = __fadd_rn(au, __shfl_xor_sync(0xffffffffu, au, o));
+          }
+          if (l8 == 0) {
+            float h = 0.0f;
+            if (!isfinite(ag) || !isfinite(au) || !swiglu(ag, au, &h)) {
+              bad = true;
+              h = 0.0f;
             }
-            if (lane == 0) {
-              (up_only ? s_uv : s_gv)[n * T + kk] = a1;
-              if (by_neuron) s_uv[n * T + kk] = a2;
-            }
+            s_gv[n * T + kk] = h;
           }
         }
       }
@@ -581,14 +601,12 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
     }
     if (r == 0) PHASE(9);
     if (__syncthreads_or(timed_out)) { aborted = true; break; }
-    // SwiGLU and the hidden slice's Q8 quantization (src/q4.c:37-61, one group of 32)
+    // the hidden slice's Q8 quantization (src/q4.c:37-61, one group of 32)
     for (unsigned kk = warp; kk < nt; kk += kLayerWarps) {
       unsigned mm = mask;
       for (unsigned z = 0; z < kk; ++z) mm &= mm - 1;
       const unsigned t = __ffs(mm) - 1;
-      const float g = s_gv[lane * T + kk], uu = s_uv[lane * T + kk];
-      float h = 0.0f;
-      if (!isfinite(g) || !isfinite(uu) || !swiglu(g, uu, &h)) { bad = true; h = 0.0f; }
+      const float h = s_gv[lane * T + kk];
       if (a.hidden) a.hidden[((static_cast<size_t>(u) * S + s) * T + t) * 32 + lane] = h;
       float gs;
       if (ACT == FRC_ACT_Q8) {
@@ -705,24 +723,25 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
       float* terms = st;                        // [tl][e][s][R]
       float* gsr = st + tn * 11 * S * R;        // [tl][e][s]
       float* part = gsr + tn * 11 * S;          // [tl][e][R]
+      const Div by_nu(nu), by_s(S), by_r(R);
       for (unsigned q = tid; q < tn * 11 * S * nu; q += kLayerThreads) {
-        const unsigned un = q % nu, rest = q / nu, s = rest % S, te = rest / S;  // te = tl*11 + e
-        const unsigned pair = s_tokpair[(t0 + te / 11) * 11 + te % 11];
+        const unsigned rest = by_nu.q(q), un = q - rest * nu, te = by_s.q(rest), s = rest - te * S;  // te = tl*11 + e
+        const unsigned pair = s_tokpair[t0 * 11 + te];
         if (pair != 0xffff)
           cp_async16(terms + (te * S + s) * R + 4 * un,
                      a.partial + (static_cast<size_t>(pair) * S + s) * d + y0 + 4 * un);
       }
       cp_async_commit();
       for (unsigned q = tid; q < tn * 11 * S; q += kLayerThreads) {
-        const unsigned s = q % S, te = q / S;
-        const unsigned pair = s_tokpair[(t0 + te / 11) * 11 + te % 11];
+        const unsigned te = by_s.q(q), s = q - te * S;
+        const unsigned pair = s_tokpair[t0 * 11 + te];
         gsr[q] = pair != 0xffff ? __ldcg(a.gsv + pair * S + s) : 0.0f;
       }
       cp_async_wait_all();
       __syncthreads();
       if (t0 == 0) PHASE(11);
       for (unsigned q = tid; q < tn * 11 * R; q += kLayerThreads) {
-        const unsigned rr = q % R, te = q / R;
+        const unsigned te = by_r.q(q), rr = q - te * R;
         const float* tv = terms + te * S * R + rr;
         const float* gv = gsr + te * S;
         // chain j takes slices s = j mod 4 in ascending order
@@ -741,7 +760,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
       }
       __syncthreads();
       for (unsigned q = tid; q < tn * R; q += kLayerThreads) {
-        const unsigned tl = q / R, rr = q % R, t = t0 + tl;
+        const unsigned tl = by_r.q(q), rr = q - tl * R, t = t0 + tl;
         float yv = 0.0f;
         for (unsigned e = 0; e <= 10; ++e)
           if (s_tokpair[t * 11 + e] != 0xffff) yv = __fadd_rn(yv, part[(tl * 11 + e) * R + rr]);

@@ -388,24 +388,28 @@ static int pair_term(const uint8_t *row, unsigned type, unsigned p, const qx *x,
     return 1;
 }
 
-/* One gate or up dot as the kernel forms it: lane L accumulates the groups
- * p = L, L+32, ... with fmaf(scale_p, term_p, acc); then a butterfly of
- * pairwise sums over offsets 16, 8, 4, 2, 1. */
+/* One gate or up dot as the kernel forms it: eight lanes share the row;
+ * lane L takes the 256-element spans (four x groups of 64: a Q4_K
+ * super-block, eight MXFP4 / Q8_0 blocks) q = L, L+8, ..., and within a span
+ * its groups in order, accumulating fmaf(scale[p], term, acc); then a
+ * butterfly over the eight lanes (xor 4, 2, 1). */
+enum { PORT_ROW_LANES = 8 };
 static int lane_dot(const uint8_t *row, unsigned type, const qx *x, float *out) {
-    float lane[32];
-    unsigned groups = x->d / 64;
-    for (unsigned L = 0; L < 32; ++L) {
+    float lane[PORT_ROW_LANES];
+    const unsigned spans = x->d / 256;
+    for (unsigned L = 0; L < PORT_ROW_LANES; ++L) {
         float acc = 0;
-        for (unsigned p = L; p < groups; p += 32) {
-            float term;
-            if (!pair_term(row, type, p, x, &term)) return OR_NUMERIC;
-            acc = fmaf(x->scale[p], term, acc);
-        }
+        for (unsigned q = L; q < spans; q += PORT_ROW_LANES)
+            for (unsigned p = 4 * q; p < 4 * q + 4; ++p) {
+                float term;
+                if (!pair_term(row, type, p, x, &term)) return OR_NUMERIC;
+                acc = fmaf(x->scale[p], term, acc);
+            }
         lane[L] = acc;
     }
-    for (unsigned off = 16; off; off >>= 1) {
-        float next[32];
-        for (unsigned L = 0; L < 32; ++L) next[L] = lane[L] + lane[L ^ off];
+    for (unsigned off = PORT_ROW_LANES / 2; off; off >>= 1) {
+        float next[PORT_ROW_LANES];
+        for (unsigned L = 0; L < PORT_ROW_LANES; ++L) next[L] = lane[L] + lane[L ^ off];
         memcpy(lane, next, sizeof lane);
     }
     *out = lane[0];
