@@ -243,6 +243,8 @@ static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, u
   m.dn_r = down_rows(ss_r + pb_r);
   m.dn_s = down_rows(2 + 32);
   m.total = o + K * slot;
+  m.mag_ch_r = div_magic(32 / m.kn_r + (d + m.dn_r - 1) / m.dn_r);
+  m.mag_ch_s = div_magic(32 / m.kn_s + (d + m.dn_s - 1) / m.dn_s);
   *out = m;
   return true;
 }
@@ -341,6 +343,7 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
   a.ctl = c->ctl; a.status = c->status;
   a.phases = c->phases;
   a.S = S; a.T = T; a.d = c->g.hidden;
+  a.mag_S = div_magic(S);
   a.norm = flags & FRC_RUN_RMSNORM ? 1u : 0u;
   a.gate_type = c->g.gate_type; a.down_type = c->g.down_type;
   a.row_bytes = static_cast<unsigned>(c->row_bytes); a.proj_bytes = static_cast<unsigned>(c->proj_bytes);

@@ -92,9 +92,11 @@ __device__ __forceinline__ bool spin_geq(const unsigned* p, unsigned target, con
 }
 // Division by a run-time divisor 1 <= dv < 2^16 through multiply-high:
 // exact for dividends x < 2^16.
+__host__ __device__ constexpr unsigned div_magic(unsigned v) { return v > 1 ? 0xffffffffu / v + 1 : 0u; }
 struct Div {
   unsigned dv, m;
-  __device__ __forceinline__ explicit Div(unsigned v) : dv(v), m(v > 1 ? 0xffffffffu / v + 1 : 0) {}
+  __device__ __forceinline__ explicit Div(unsigned v) : dv(v), m(div_magic(v)) {}
+  __device__ __forceinline__ Div(unsigned v, unsigned magic) : dv(v), m(magic) {}  // magic from div_magic(v)
   __device__ __forceinline__ unsigned q(unsigned x) const { return dv > 1 ? __umulhi(x, m) : x; }
   __device__ __forceinline__ unsigned r(unsigned x) const { return x - q(x) * dv; }
 };

@@ -60,6 +60,7 @@ struct LayerSmem {
   unsigned slot_bytes, slots;
   unsigned kn_r, kn_s;  // neurons per gate/up chunk: routed, shared items (powers of two)
   unsigned dn_r, dn_s;  // rows per down chunk: routed, shared items (multiples of 16)
+  unsigned mag_ch_r, mag_ch_s;  // div_magic of the chunks per routed / shared item
 };
 
 struct LayerParams {
@@ -78,6 +79,7 @@ struct LayerParams {
   unsigned long long* phases;  // FRC_PHASES builds: [cta][16] globaltimer stamps
   LayerSmem sm;
   unsigned S, T, d, norm;
+  unsigned mag_S;  // div_magic(S)
   unsigned gate_type, down_type;
   unsigned row_bytes, proj_bytes, shared_row, shared_proj, slice_bytes;
 };
@@ -173,14 +175,16 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
   // no token uses it) come from the plan; setup() derives this CTA's list.
   unsigned UR = 0, SH = 0, U = 0, NI = 0, n_my = 0, nsh = 0, n_ch = 0;
   auto item_at = [&](unsigned r) { return r * G + ((r & 1) ? G - 1 - cta : cta); };
+  const Div by_S(S, a.mag_S);
   auto item_us = [&](unsigned j, unsigned& u, unsigned& s) {
     if (j < SH) { u = UR; s = j; }
-    else { u = (j - SH) / S; s = (j - SH) % S; }
+    else { u = by_S.q(j - SH); s = j - SH - u * S; }
   };
   const unsigned kn_r = a.sm.kn_r, kn_s = a.sm.kn_s, dn_r = a.sm.dn_r, dn_s = a.sm.dn_s;
   const unsigned ngu_r = 32 / kn_r, ngu_s = 32 / kn_s;
   const unsigned ndn_r = (d + dn_r - 1) / dn_r, ndn_s = (d + dn_s - 1) / dn_s;
   const unsigned ch_r = ngu_r + ndn_r, ch_s = ngu_s + ndn_s;
+  const Div by_ch_r(ch_r, a.sm.mag_ch_r), by_ch_s(ch_s, a.sm.mag_ch_s);
   const unsigned ss_r = a.down_type == kQ80 ? 2 : 1, pb_r = a.down_type == kQ80 ? 32 : 16;
   auto setup = [&]() {
     UR = misc[4];
@@ -196,8 +200,8 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
 
   // chunk c of this CTA -> (item round r, chunk k within the item)
   auto chunk_at = [&](unsigned c, unsigned& r, unsigned& k) {
-    if (c < nsh * ch_s) { r = c / ch_s; k = c % ch_s; }
-    else { r = nsh + (c - nsh * ch_s) / ch_r; k = (c - nsh * ch_s) % ch_r; }
+    if (c < nsh * ch_s) { r = by_ch_s.q(c); k = c - r * ch_s; }
+    else { const unsigned cr = c - nsh * ch_s, rr = by_ch_r.q(cr); r = nsh + rr; k = cr - rr * ch_r; }
   };
   // Gate/up chunk k: gate rows k*kn.. then up rows k*kn.. (two copies).
   // Down chunk: rows [r0, r0+nr): their scales, then their payloads.
@@ -230,6 +234,10 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
     // ------------------------------------------------- warps 4-7: plan
     const unsigned ptid = tid - 32 * kFirstPlanWarp, pw = warp - kFirstPlanWarp;
     if (ptid < kMaxSlots) s_cnt[ptid] = 0;
+    if (ptid == 0) {  // the ring's barriers, while the routing loads are in flight
+      for (unsigned k = 0; k < K; ++k) mbar_init(&full[k], 1);
+      fence_mbar_init();
+    }
     if (T == 1) {
       // one token: its ten experts in request order are the unique experts,
       // each with one (expert, token) pair
@@ -368,11 +376,6 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
     plan_sync();
     PHASE_AT(10, kPlanThreads);
     if (pw == 0) {  // the first K chunks, while the activations are still being formed
-      if (lane == 0) {
-        for (unsigned k = 0; k < K; ++k) mbar_init(&full[k], 1);
-        fence_mbar_init();
-      }
-      __syncwarp();
       setup();
       if (lane < K && lane < n_ch) issue(lane);
       PHASE_AT(1, kPlanThreads);
