@@ -162,14 +162,16 @@ def run_reference(args, rank):
     emit(line)
 
 
-def config(n):
+def config(n, reduce="peer"):
     from fronk_b200.planner import equal_shares
     return {"workload": WORKLOAD, "hidden": HIDDEN, "layers": LAYERS, "tokens_per_step": 1, "experts": 512,
             "top_k": TOPK, "slices": SLICES, "shares": equal_shares(n), "formats": "Q4_K gate/up, MXFP4 down",
             "activations": "Q8 per 64 (src/q4.c scheme), fp32 accumulate",
             "weight_bytes_per_token": LAYERS * TOPK * SLICES * SLICE_BYTES,
             "l2": "inputs larger than L2: 1.04 GB of expert weights per step, fresh routing every step",
-            "parallelism": "slice-split x%d + all-reduce per layer" % n if n > 1 else "1 GPU, all slices"}
+            "parallelism": ("slice-split x%d, per-layer sum of the partials %s" %
+                            (n, "in the layer kernel over NVLink peer memory" if reduce == "peer" else "by NCCL all-reduce"))
+                           if n > 1 else "1 GPU, all slices"}
 
 
 # ------------------------------------------------------------------- ours
@@ -181,6 +183,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--reduce", default="peer", choices=["peer", "nccl"],
+                    help="per-layer sum of the GPUs' partials: in-kernel over NVLink peer memory, or NCCL all-reduce")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu: 2 layers of every slice loaded (2.2 GB), 5 layer launches")
     args = ap.parse_args()
@@ -226,6 +230,15 @@ def main():
         for l in range(LAYERS):
             ctx.fill_layer(b, l, SEED)
     log("rank %d: blocks %s filled in %.1fs" % (rank, blocks, time.time() - t0))
+    # in-box reduce: the layer kernels sum the ranks' partials through each
+    # other's inboxes over NVLink (FRC_RUN_PEER); --reduce nccl keeps an NCCL
+    # all-reduce after every layer instead
+    peer = world > 1 and args.reduce == "peer"
+    if peer:
+        handles = [None] * world
+        dist.all_gather_object(handles, ctx.peer_export(world))
+        ctx.peer_attach(rank, world, handles)
+    run_flags = fb.RUN_RMSNORM | fb.RUN_OVERLAP | (fb.RUN_PEER if peer else 0)
 
     total = args.warmup + args.steps
     ex, gt, x0 = step_routing(total)
@@ -250,8 +263,8 @@ def main():
             # consecutive layers overlap: layer l+1 plans and starts its weight copies while
             # layer l (or the all-reduce after it) finishes; it reads x only after that
             ctx.run_device(l, 1, p(cur_ex[l]), p(cur_gt[l]), p(x), x_add, x_out, p(Y[l % 2]), fb.ACT_Q8,
-                           fb.RUN_RMSNORM | fb.RUN_OVERLAP, s)
-            if dist is not None:
+                           run_flags, s)
+            if dist is not None and not peer:
                 dist.all_reduce(Y[l % 2])
 
     def load_step(s):
@@ -337,7 +350,7 @@ def main():
 
     # ---- end to end through the C ABI with host buffers (reference-facing call)
     e2e_steps = max(3, min(args.steps, 50))
-    e2e = e2e_run(ctx, fb, ex, gt, x0, e2e_steps, dist, dev)
+    e2e = e2e_run(ctx, fb, ex, gt, x0, e2e_steps, dist, dev, peer)
 
     # ---- parity at full size: one layer of the filled units vs the oracle
     parity = full_size_parity(ctx, fb, g, pool, blocks)
@@ -349,7 +362,7 @@ def main():
         line = {
             "metric": METRIC, "value": tokens_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config(world),
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config(world, args.reduce),
             "weight_gbs": weight_bytes * tokens_s / 1e9,
             "weight_frac_of_peak": weight_bytes * tokens_s / 1e9 / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -370,7 +383,7 @@ def main():
         dist.destroy_process_group()
 
 
-def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev):
+def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev, peer=False):
     """tokens/s through the public call with host buffers: per layer the
     request is copied in, the layer runs, y is copied out (frc_run; at N>1
     the device entry point plus the all-reduce)."""
@@ -407,8 +420,9 @@ def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev):
                 de.copy_(pin_e, non_blocking=True)
                 dg.copy_(pin_g, non_blocking=True)
                 ctx.run_device(l, 1, de.data_ptr(), dg.data_ptr(), dx.data_ptr(), None, None, dy.data_ptr(),
-                               fb.ACT_Q8, 0, st.cuda_stream)
-                dist.all_reduce(dy)
+                               fb.ACT_Q8, fb.RUN_PEER if peer else 0, st.cuda_stream)
+                if not peer:
+                    dist.all_reduce(dy)
                 pin_y.copy_(dy, non_blocking=True)
                 st.synchronize()
                 h = h + pin_y.numpy()
@@ -421,7 +435,8 @@ def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev):
         raise fb.FrcError(rc, "e2e", ctx.last_error)
     return {"value": steps / dt, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": steps, "api": "frc_host_pass: frc_run per layer (host buffers, synchronous)" if dist is None else
-            "frc_run_device + NCCL all_reduce, pinned host copies each layer"}
+            ("frc_run_device with the in-kernel NVLink reduce" if peer else "frc_run_device + NCCL all_reduce")
+            + ", pinned host copies each layer"}
 
 
 def full_size_parity(ctx, fb, g, pool, blocks):

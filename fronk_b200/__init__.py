@@ -20,6 +20,8 @@ Q8_0, Q4_K, MXFP4 = 8, 12, 39
 ACT_F32, ACT_Q8 = 0, 1
 RUN_RMSNORM = 1
 RUN_OVERLAP = 2
+RUN_PEER = 4
+PEER_HANDLE_BYTES = 64
 MAX_BLOCKS, ROUTED, SHARED, TOPK, ACTIVE, NEURONS, MAX_TOKENS = 20, 512, 512, 10, 11, 32, 16
 LAYERS = 48
 
@@ -65,6 +67,9 @@ _SIGS = {
     "frc_run_device": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
     "frc_run_device_fixed": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
     "frc_host_pass": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _u32, _int]),
+    "frc_peer_export": (_int, [_vp, _u32, _vp]),
+    "frc_peer_attach": (_int, [_vp, _u32, _u32, _vp]),
+    "frc_peer_detach": (_int, [_vp]),
     "frc_status": (_int, [_vp, _vp]),
     "frc_launch_count": (_u64, [_vp]),
     "frc_strerror": (ctypes.c_char_p, [_int]),
@@ -275,6 +280,20 @@ class Context:
         rc = self.lib.frc_host_pass(self.h, first_layer, expert.shape[0], _ptr(expert), _ptr(gate), _ptr(h),
                                     h.size, act)
         self._check(rc, "host_pass")
+
+    def peer_export(self, world):
+        """Allocates this context's in-box reduce inbox; returns its IPC handle (bytes)."""
+        h = ctypes.create_string_buffer(PEER_HANDLE_BYTES)
+        self._check(self.lib.frc_peer_export(self.h, world, h), "peer_export")
+        return h.raw
+
+    def peer_attach(self, rank, world, handles):
+        """handles: every rank's peer_export bytes, in rank order."""
+        buf = ctypes.create_string_buffer(b"".join(handles), PEER_HANDLE_BYTES * world)
+        self._check(self.lib.frc_peer_attach(self.h, rank, world, buf), "peer_attach")
+
+    def peer_detach(self):
+        self._check(self.lib.frc_peer_detach(self.h), "peer_detach")
 
     def status(self, stream=None):
         return self.lib.frc_status(self.h, stream)

@@ -140,6 +140,12 @@ struct frc_context {
   unsigned occ_smem[2] = {};
   int occ_val[2] = {};
   unsigned last_T = 0, last_S = 0, last_G = 0;
+  // in-box reduce: this rank's inbox (IPC-exported), every rank's inbox as
+  // mapped here, the per-CTA launch counters
+  uint8_t* inbox = nullptr;
+  uint8_t* peer[kMaxPeers] = {};
+  unsigned* epoch = nullptr;
+  unsigned rank = 0, world = 0, peer_gmax = 0;
   uint16_t last_expert[FRC_MAX_TOKENS * FRC_TOPK] = {};
   float last_gate[FRC_MAX_TOKENS * FRC_ACTIVE] = {};
   char err[256] = {};
@@ -208,6 +214,7 @@ static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, u
   m.gv = take(4 * 32 * T);
   m.uv = take(4 * 32 * T);
   m.hg = take(4 * T);
+  m.ylocal = take(4 * T * 4 * ((d / 4 + G - 1) / G));
   o = align_up(o, 128);
   if (o >= limit) return false;
   const unsigned avail = limit - o, rowb = static_cast<unsigned>(c->row_bytes);
@@ -341,6 +348,13 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
     a.partial = c->partial; a.gsv = c->gsv; a.hidden = c->hidden;
   }
   a.ctl = c->ctl; a.status = c->status;
+  if (flags & FRC_RUN_PEER) {
+    if (c->world < 2) return fail(c, FRC_STATE, "FRC_RUN_PEER without frc_peer_attach");
+    for (unsigned r = 0; r < c->world; ++r) a.peer[r] = c->peer[r];
+    a.rank = c->rank; a.world = c->world; a.peer_gmax = c->peer_gmax; a.epoch = c->epoch;
+  } else {
+    a.world = 1;
+  }
   a.phases = c->phases;
   a.S = S; a.T = T; a.d = c->g.hidden;
   a.mag_S = div_magic(S);
@@ -477,6 +491,7 @@ int frc_close(frc_context* c) {
   if (!c) return FRC_INVALID;
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
+  frc_peer_detach(c);
   for (auto& b : c->layer_ptr)
     for (auto& p : b) if (p) cudaFree(p);
   cudaFree(c->staging); cudaFree(c->hidden); cudaFree(c->partial); cudaFree(c->gsv); cudaFree(c->phases); cudaFree(c->ctl);
@@ -647,6 +662,69 @@ int frc_run_device_fixed(frc_context* c, unsigned layer, unsigned tokens, const 
   const RunScratch sc{base, base + fixed_partial(S, tokens, c->g.hidden), nullptr};
   return run_device(c, layer, tokens, expert, gate, x, x_add, x_out, y, act, flags, static_cast<cudaStream_t>(stream),
                     &sc);
+}
+
+// ------------------------------------------------------ in-box reduce
+// Inbox bytes for `world` ranks: double-buffered slots [2][world][16][d] f32,
+// then the flags [world][2 * SMs] u32 (one per source rank and CTA).
+static size_t inbox_bytes(const frc_context* c, unsigned world, unsigned gmax) {
+  return 2 * static_cast<size_t>(world) * kMaxTokens * c->g.hidden * sizeof(float) +
+         static_cast<size_t>(world) * gmax * sizeof(unsigned);
+}
+
+int frc_peer_export(frc_context* c, unsigned world, void* handle) {
+  if (!c || !handle || world < 2 || world > kMaxPeers) return fail(c, FRC_INVALID, "world must be 2..%u", kMaxPeers);
+  if (c->inbox) return fail(c, FRC_STATE, "inbox already exported");
+  CK(cudaSetDevice(c->device));
+  const unsigned gmax = 2 * static_cast<unsigned>(c->sms);
+  const size_t bytes = inbox_bytes(c, world, gmax);
+  CK(cudaMalloc(&c->inbox, bytes));
+  CK(cudaMemset(c->inbox, 0, bytes));
+  CK(cudaMalloc(&c->epoch, gmax * sizeof(unsigned)));
+  CK(cudaMemset(c->epoch, 0, gmax * sizeof(unsigned)));
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, c->inbox));
+  static_assert(sizeof(h) == FRC_PEER_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof h);
+  c->world = world;
+  c->peer_gmax = gmax;
+  return FRC_OK;
+}
+
+int frc_peer_attach(frc_context* c, unsigned rank, unsigned world, const void* handles) {
+  if (!c || !handles || rank >= world || world != c->world || !c->inbox)
+    return fail(c, FRC_INVALID, "attach needs the exported world, rank < world and every handle");
+  CK(cudaSetDevice(c->device));
+  const uint8_t* hs = static_cast<const uint8_t*>(handles);
+  for (unsigned r = 0; r < world; ++r) {
+    if (r == rank) {
+      c->peer[r] = c->inbox;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, hs + r * FRC_PEER_HANDLE_BYTES, sizeof h);
+    void* p = nullptr;
+    CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    c->peer[r] = static_cast<uint8_t*>(p);
+  }
+  c->rank = rank;
+  return FRC_OK;
+}
+
+int frc_peer_detach(frc_context* c) {
+  if (!c) return FRC_INVALID;
+  cudaSetDevice(c->device);
+  for (unsigned r = 0; r < kMaxPeers; ++r) {
+    if (c->peer[r] && c->peer[r] != c->inbox) cudaIpcCloseMemHandle(c->peer[r]);
+    c->peer[r] = nullptr;
+  }
+  cudaFree(c->inbox);
+  cudaFree(c->epoch);
+  c->inbox = nullptr;
+  c->epoch = nullptr;
+  c->world = 0;
+  c->rank = 0;
+  return FRC_OK;
 }
 
 int frc_status(frc_context* c, void* stream) {

@@ -45,6 +45,7 @@ constexpr unsigned kFirstPlanWarp = kLayerWarps - kPlanWarps;
 constexpr unsigned kMaxSlots = 8;              // TMA ring depth limit
 constexpr unsigned kXRegs = 4;                 // float4 activations a thread keeps in registers
 constexpr unsigned kMaxRounds = 256;           // 128-float4 rounds of the activation pass
+constexpr unsigned kMaxPeers = 8;              // GPUs of one in-box reduce
 
 struct LayerCtl {
   unsigned long long arrived;   // grid barrier arrivals, all launches (never wraps)
@@ -56,7 +57,7 @@ struct LayerCtl {
 // item into ring slots (computed on the host).
 struct LayerSmem {
   unsigned ids, gates, first, uid, umask, ugate, upre, rms, bases, rpart, tokpair;
-  unsigned xq, xp, xs, xv, xf, gv, uv, hq, hg, ring, total;
+  unsigned xq, xp, xs, xv, xf, gv, uv, hq, hg, ylocal, ring, total;
   unsigned slot_bytes, slots;
   unsigned kn_r, kn_s;  // neurons per gate/up chunk: routed, shared items (powers of two)
   unsigned dn_r, dn_s;  // rows per down chunk: routed, shared items (multiples of 16)
@@ -77,6 +78,13 @@ struct LayerParams {
   LayerCtl* ctl;
   unsigned* status;
   unsigned long long* phases;  // FRC_PHASES builds: [cta][16] globaltimer stamps
+  // In-box reduce over peer memory (world > 1): every rank's inbox as mapped
+  // here (peer[rank] is this rank's own), this rank, and this context's
+  // per-CTA count of such launches.  Inbox: slots [2][world][16][d] f32, then
+  // flags [world][peer_gmax] u32.
+  uint8_t* peer[kMaxPeers];
+  unsigned rank, world, peer_gmax;
+  unsigned* epoch;
   LayerSmem sm;
   unsigned S, T, d, norm;
   unsigned mag_S;  // div_magic(S)
@@ -158,6 +166,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
   uint16_t* s_tokpair = reinterpret_cast<uint16_t*>(smem + a.sm.tokpair);  // [token][11] -> pair
   float* s_gv = reinterpret_cast<float*>(smem + a.sm.gv);            // [neuron][k] hidden values
   uint8_t* s_hq = smem + a.sm.hq;                                    // [k][32] int8, or [k][32] f32
+  float* s_ylocal = reinterpret_cast<float*>(smem + a.sm.ylocal);    // [t][rows]: this GPU's partial (peer reduce)
   uint8_t* ring = smem + a.sm.ring;
   const unsigned SLOT = a.sm.slot_bytes, K = a.sm.slots;
 
@@ -710,6 +719,68 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
   }
   PHASE(5);
 
+  // --------------------------------------------- in-box reduce over NVLink
+  // This CTA's rows of every token (this GPU's partial, s_ylocal) go to the
+  // same rows of every rank's inbox with plain stores (peer memory over
+  // NVLink; no multicast), then a release store of this launch's epoch to the
+  // rank's flag for (this rank, this CTA).  Once every rank's flag for this
+  // CTA reads the epoch (bounded wait) the rows are summed in rank order, so
+  // y is identical on every rank.  Slots alternate by epoch parity: a rank
+  // reuses a slot only after every rank has signalled the launch after the
+  // one that read it.
+  auto peer_reduce = [&](unsigned y0, unsigned R) -> bool {
+    const unsigned W = a.world;
+    const size_t slot_bytes = static_cast<size_t>(kMaxTokens) * d * sizeof(float);  // one source's [16][d]
+    const size_t flags_off = 2 * static_cast<size_t>(W) * slot_bytes;
+    if (tid == 0) {
+      const unsigned e = a.epoch[cta] + 1;
+      a.epoch[cta] = e;
+      misc[6] = e;
+    }
+    __syncthreads();
+    const unsigned e = misc[6], par = e & 1;
+    const Div by_tr(T * R), by_r2(R);
+    for (unsigned q = tid; q < W * T * R; q += kLayerThreads) {
+      const unsigned dst = by_tr.q(q), rem = q - dst * T * R, t = by_r2.q(rem), rr = rem - t * R;
+      float* slot = reinterpret_cast<float*>(a.peer[dst] + (static_cast<size_t>(par) * W + a.rank) * slot_bytes) +
+                    static_cast<size_t>(t) * d + y0 + rr;
+      *slot = s_ylocal[t * R + rr];
+    }
+    __syncthreads();
+    bool ok = true;
+    if (tid < W) {  // the release store is cumulative: it orders the whole CTA's slot stores (bar.sync above)
+      unsigned* flag = reinterpret_cast<unsigned*>(a.peer[tid] + flags_off) + a.rank * a.peer_gmax + cta;
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(e) : "memory");
+      const unsigned* mine = reinterpret_cast<const unsigned*>(a.peer[a.rank] + flags_off) + tid * a.peer_gmax + cta;
+      const uint64_t start = globaltimer();
+      for (;;) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+        if (static_cast<int>(v - e) >= 0) break;
+        if (globaltimer() - start > kWaitNs) {
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (!__syncthreads_and(ok)) {
+      if (tid == 0) atomicOr(a.status, kStTimeout);
+      return false;
+    }
+    const float* inbox = reinterpret_cast<const float*>(a.peer[a.rank]) + static_cast<size_t>(par) * W * kMaxTokens * d;
+    bool bad_y = false;
+    for (unsigned q = tid; q < T * R; q += kLayerThreads) {
+      const unsigned t = by_r2.q(q), rr = q - t * R;
+      float yv = 0.0f;
+      for (unsigned src = 0; src < W; ++src)
+        yv = __fadd_rn(yv, __ldcg(inbox + (static_cast<size_t>(src) * kMaxTokens + t) * d + y0 + rr));
+      bad_y |= !isfinite(yv);
+      a.y[static_cast<size_t>(t) * d + y0 + rr] = yv;
+    }
+    if (bad_y) atomicOr(a.status, kStNumeric);
+    return true;
+  };
+
   // ------------------------------------------------------------- reduce
   // CTA k owns 4-row units [d/4*k/G, d/4*(k+1)/G): its rows of every
   // (pair, slice) term vector arrive by 16-byte cp.async into the idle ring,
@@ -768,10 +839,12 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
         for (unsigned e = 0; e <= 10; ++e)
           if (s_tokpair[t * 11 + e] != 0xffff) yv = __fadd_rn(yv, part[(tl * 11 + e) * R + rr]);
         nf |= !isfinite(yv);
-        a.y[static_cast<size_t>(t) * d + y0 + rr] = yv;
+        if (a.world > 1) s_ylocal[t * R + rr] = yv;
+        else a.y[static_cast<size_t>(t) * d + y0 + rr] = yv;
       }
       __syncthreads();
     }
+    if (a.world > 1 && !peer_reduce(y0, R)) aborted = true;
     if (nf) atomicOr(a.status, kStNumeric);
   }
   PHASE(7);

@@ -106,8 +106,12 @@ int frc_run(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *exp
  * streaming this layer's weights at once and waits for that kernel only
  * before it reads x / x_add or writes anything.  The caller guarantees that
  * the preceding kernel writes neither the weights nor expert / gate (writing
- * x, as a previous layer or an all-reduce does, is fine). */
-enum { FRC_RUN_RMSNORM = 1, FRC_RUN_OVERLAP = 2 };
+ * x, as a previous layer or an all-reduce does, is fine).
+ * FRC_RUN_PEER: y is the sum over every rank of the in-box reduce group
+ * (frc_peer_attach) of each rank's partial, added in rank order: identical
+ * on every rank.  Every rank must make the same sequence of FRC_RUN_PEER
+ * calls (same token counts), one process per GPU. */
+enum { FRC_RUN_RMSNORM = 1, FRC_RUN_OVERLAP = 2, FRC_RUN_PEER = 4 };
 
 /* Asynchronous run on device memory, enqueued on `stream` (a cudaStream_t, or
  * NULL for the legacy default stream); nothing is validated on the host and
@@ -135,6 +139,22 @@ int frc_run_device(frc_context *c, unsigned layer, unsigned tokens, const uint16
 int frc_run_device_fixed(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *expert,
                          const float *gate, const float *x, const float *x_add, float *x_out,
                          float *y, int act, unsigned flags, void *stream);
+/* ---- In-box reduce over NVLink peer memory (replaces the per-layer
+ * all-reduce of the slice partials; the reference's fanout/plane gather,
+ * src/plane.c:110-121, inside one box).  One process per GPU:
+ *   1. every rank: frc_peer_export(c, world, handle) - allocates this
+ *      context's inbox and writes its IPC handle (FRC_PEER_HANDLE_BYTES);
+ *   2. the ranks exchange handles (any host channel);
+ *   3. every rank: frc_peer_attach(c, rank, world, handles[world]);
+ *   4. run with FRC_RUN_PEER.  A rank whose peers stop answering gets
+ *      FRC_IO from frc_status after a bounded wait; the group then detaches
+ *      and attaches again.
+ * No counterpart in the reference (its gather is TCP/UDP between nodes). */
+enum { FRC_PEER_HANDLE_BYTES = 64 };
+int frc_peer_export(frc_context *c, unsigned world, void *handle);
+int frc_peer_attach(frc_context *c, unsigned rank, unsigned world, const void *handles);
+int frc_peer_detach(frc_context *c);
+
 /* A decode pass for one token driven from the host, layer by layer through
  * frc_run (host buffers, one synchronous call per layer):
  * x = h / sqrt(mean(h^2) + 1e-6), y = run(layer, x), h += y, for layers
