@@ -186,7 +186,7 @@ constexpr unsigned kSmemOnePerSm = 227 * 1024;
 // when two slots of one neuron pair do not fit.
 static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, unsigned limit, LayerSmem* out) {
   const unsigned d = c->g.hidden, P = d / 64;
-  if ((T * d / 4 + kActThreads - 1) / kActThreads > kMaxRounds) return false;
+  if (T * d / 512 > kActWarps * kMaxRounds) return false;  // activation sums: one a warp-pass of 512 floats
   LayerSmem m{};
   unsigned o = 64 + 256;  // mbarriers, then 64 misc words
   auto take = [&](unsigned bytes) { unsigned at = o; o = align_up(o + bytes, 16); return at; };

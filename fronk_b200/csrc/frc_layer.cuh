@@ -43,8 +43,7 @@ constexpr unsigned kPlanWarps = 4;             // warps 4-7 build the plan
 constexpr unsigned kPlanThreads = 32 * kPlanWarps;
 constexpr unsigned kFirstPlanWarp = kLayerWarps - kPlanWarps;
 constexpr unsigned kMaxSlots = 8;              // TMA ring depth limit
-constexpr unsigned kXRegs = 4;                 // float4 activations a thread keeps in registers
-constexpr unsigned kMaxRounds = 256;           // 128-float4 rounds of the activation pass
+constexpr unsigned kMaxRounds = 256;           // warp-passes of the activation sums per warp (512 floats each)
 constexpr unsigned kMaxPeers = 8;              // GPUs of one in-box reduce
 
 struct LayerCtl {
@@ -172,8 +171,6 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
 
   const unsigned tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const unsigned T = a.T, S = a.S, d = a.d, P = d / 64, G = gridDim.x, cta = blockIdx.x;
-  const unsigned per_token = d / 4, nvec = T * per_token, rounds = (nvec + kActThreads - 1) / kActThreads;
-  const bool xregs = rounds <= kXRegs;
 
   PHASE(0);
   pdl_signal();
@@ -395,108 +392,118 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
     // ------------------------------------------- warps 0-3: layer input
     // (needs only x: runs while warps 4-7 plan and start the weight copies)
     pdl_wait();
-    float4 xv4[kXRegs];
-    if (xregs) {
-      const float4* x4 = reinterpret_cast<const float4*>(a.x);
-      const float4* xa4 = reinterpret_cast<const float4*>(a.x_add);
-  #pragma unroll
-      for (unsigned r = 0; r < kXRegs; ++r) {
-        const unsigned f = r * kActThreads + tid;
-        xv4[r] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (r < rounds && f < nvec) {
-          xv4[r] = x4[f];
-          if (xa4) {
-            const float4 w = xa4[f];
-            xv4[r].x = __fadd_rn(xv4[r].x, w.x); xv4[r].y = __fadd_rn(xv4[r].y, w.y);
-            xv4[r].z = __fadd_rn(xv4[r].z, w.z); xv4[r].w = __fadd_rn(xv4[r].w, w.w);
-          }
-        }
-      }
-    }
-
-    const float4* x4 = reinterpret_cast<const float4*>(a.x);
-    const float4* xa4 = reinterpret_cast<const float4*>(a.x_add);
-    auto load4 = [&](unsigned f, unsigned r) {
-      float4 v = xv4[0];
-      if (xregs) {
+    // A unit is a quarter of a 64-element x group: 16 floats, one thread.
+    // Four consecutive lanes hold a group, so its max and sums take two
+    // shuffles, and a thread's 16 int8 values are one 16-byte store.
+    const unsigned units = T * d / 16, upt = d / 16;  // units in all, per token
+    const unsigned upt_magic = 0xffffffffu / upt + 1;  // unit / upt by multiply-high (exact: unit < 2^16)
+    auto load_unit = [&](unsigned u, float (&v)[16]) {
+      const float4* x4 = reinterpret_cast<const float4*>(a.x) + 4 * u;
+      const float4* xa4 = a.x_add ? reinterpret_cast<const float4*>(a.x_add) + 4 * u : nullptr;
 #pragma unroll
-        for (unsigned q = 0; q < kXRegs; ++q) if (q == r) v = xv4[q];
-        return v;
+      for (unsigned k = 0; k < 4; ++k) {
+        float4 w = x4[k];
+        if (xa4) {
+          const float4 z = xa4[k];
+          w.x = __fadd_rn(w.x, z.x); w.y = __fadd_rn(w.y, z.y); w.z = __fadd_rn(w.z, z.z); w.w = __fadd_rn(w.w, z.w);
+        }
+        v[4 * k] = w.x; v[4 * k + 1] = w.y; v[4 * k + 2] = w.z; v[4 * k + 3] = w.w;
       }
-      v = x4[f];
-      if (xa4) {
-        const float4 w = xa4[f];
-        v.x = __fadd_rn(v.x, w.x); v.y = __fadd_rn(v.y, w.y); v.z = __fadd_rn(v.z, w.z); v.w = __fadd_rn(v.w, w.w);
-      }
-      return v;
     };
+    float v0[16];  // the first unit stays in registers from the sums to the quantization
+    if (tid < units) load_unit(tid, v0);
     bool bad = false;
     if (a.norm) {
-      // sums of squares per (round, warp); every warp-round lies in one token
-      for (unsigned r = 0; r < rounds; ++r) {
-        const unsigned f = r * kActThreads + tid;
+      // sums of squares per (pass, warp): a warp-pass covers 512 floats, all in one token
+      for (unsigned u0 = 0; u0 < units; u0 += kActThreads) {
+        const unsigned u = u0 + tid;
         float ss = 0.0f;
-        if (f < nvec) {
-          const float4 v = load4(f, r);
-          ss = __fmaf_rn(v.x, v.x, ss); ss = __fmaf_rn(v.y, v.y, ss);
-          ss = __fmaf_rn(v.z, v.z, ss); ss = __fmaf_rn(v.w, v.w, ss);
+        if (u < units) {
+          float v[16];
+          if (u0 == 0) {
+#pragma unroll
+            for (unsigned k = 0; k < 16; ++k) v[k] = v0[k];
+          } else {
+            load_unit(u, v);
+          }
+#pragma unroll
+          for (unsigned k = 0; k < 16; ++k) ss = __fmaf_rn(v[k], v[k], ss);
         }
 #pragma unroll
         for (unsigned o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-        if (lane == 0) s_rpart[r * kActWarps + warp] = ss;
+        if (lane == 0) s_rpart[u0 / 32 + warp] = ss;
       }
       act_sync();
       PHASE(2);
-      // token t's sums are the warp-rounds (32 float4 each, index r * 4 + w)
-      // [t * d/128, (t+1) * d/128), added in that order
-      for (unsigned t = tid; t < T; t += kActThreads) {
+      // token t: warp-passes [t * d/512, (t+1) * d/512); warp w takes tokens
+      // w, w+4, ...; lane L adds passes L, L+32, ...; butterfly
+      for (unsigned t = warp; t < T; t += kActWarps) {
+        const unsigned per = d / 512;
         float tot = 0.0f;
-        const unsigned per = d / 128;
-        for (unsigned b = t * per; b < (t + 1) * per; ++b) tot = __fadd_rn(tot, s_rpart[b]);
-        s_rms[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(d)), 1e-6f)));
+        for (unsigned b = lane; b < per; b += 32) tot = __fadd_rn(tot, s_rpart[t * per + b]);
+#pragma unroll
+        for (unsigned o = 16; o; o >>= 1) tot = __fadd_rn(tot, __shfl_xor_sync(0xffffffffu, tot, o));
+        if (lane == 0) s_rms[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(d)), 1e-6f)));
       }
       act_sync();
     }
-    // f / per_token by multiply-high: exact for f < 2^16, per_token <= 2048
-    const unsigned pt_magic = 0xffffffffu / per_token + 1;
-    for (unsigned r = 0; r < rounds; ++r) {
-      const unsigned f = r * kActThreads + tid;
-      if (f >= nvec) continue;  // warp-uniform: nvec is a multiple of 128
-      float4 v = load4(f, r);
-      const unsigned t = __umulhi(f, pt_magic), j = f - t * per_token;
-      bad |= !isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w);
-      if (a.x_out && cta == 0) reinterpret_cast<float4*>(a.x_out)[f] = v;
+    for (unsigned u0 = 0; u0 < units; u0 += kActThreads) {
+      const unsigned u = u0 + tid;
+      if (u >= units) break;  // warp-uniform: units is a multiple of 32
+      float v[16];
+      if (u0 == 0) {
+#pragma unroll
+        for (unsigned k = 0; k < 16; ++k) v[k] = v0[k];
+      } else {
+        load_unit(u, v);
+      }
+      const unsigned t = __umulhi(u, upt_magic), j16 = u - t * upt, p = j16 >> 2, qd = j16 & 3;
+#pragma unroll
+      for (unsigned k = 0; k < 16; ++k) bad |= !isfinite(v[k]);
+      if (a.x_out && cta == 0) {
+        float4* xo = reinterpret_cast<float4*>(a.x_out) + 4 * u;
+#pragma unroll
+        for (unsigned k = 0; k < 4; ++k) xo[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+      }
       if (a.norm) {
         const float g = s_rms[t];
-        v.x = __fmul_rn(v.x, g); v.y = __fmul_rn(v.y, g); v.z = __fmul_rn(v.z, g); v.w = __fmul_rn(v.w, g);
+#pragma unroll
+        for (unsigned k = 0; k < 16; ++k) v[k] = __fmul_rn(v[k], g);
       }
       if (ACT == FRC_ACT_F32) {
-        reinterpret_cast<float4*>(smem + a.sm.xf)[f] = v;
+        float4* xf = reinterpret_cast<float4*>(smem + a.sm.xf) + 4 * u;
+#pragma unroll
+        for (unsigned k = 0; k < 4; ++k) xf[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
         continue;
       }
-      float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+      float amax = 0.0f;
 #pragma unroll
-      for (unsigned o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      for (unsigned k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(v[k]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
       const Q8Group qg(amax);
-      const float scale = qg.scale;
-      const int q0 = qg.q(v.x), q1 = qg.q(v.y), q2 = qg.q(v.z), q3 = qg.q(v.w);
-      int sum = q0 + q1 + q2 + q3;
+      int qv[16], sum = 0;
 #pragma unroll
-      for (unsigned o = 4; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      const unsigned p = j / 16, wq = j % 16;
-      uint8_t* xt = smem + a.sm.xq + t * d;
-      const uint32_t word = (q0 & 0xff) | (q1 & 0xff) << 8 | (q2 & 0xff) << 16 | static_cast<uint32_t>(q3 & 0xff) << 24;
-      *reinterpret_cast<uint32_t*>(xt + 16 * xslot(p, wq / 4, d / 256) + 4 * (wq % 4)) = word;
-      if ((lane & 15) == 0) reinterpret_cast<float*>(smem + a.sm.xs)[t * P + p] = scale;
-      if ((lane & 7) == 0)
-        reinterpret_cast<float*>(smem + a.sm.xv)[t * 2 * P + 2 * p + ((lane >> 3) & 1)] = static_cast<float>(sum);
+      for (unsigned k = 0; k < 16; ++k) {
+        qv[k] = qg.q(v[k]);
+        sum += qv[k];
+      }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);  // quarters 0+1 and 2+3: the two 32-element halves
+      uint32_t w[4];
+#pragma unroll
+      for (unsigned k = 0; k < 4; ++k)
+        w[k] = (qv[4 * k] & 0xff) | (qv[4 * k + 1] & 0xff) << 8 | (qv[4 * k + 2] & 0xff) << 16 |
+               static_cast<uint32_t>(qv[4 * k + 3] & 0xff) << 24;
+      *reinterpret_cast<uint4*>(smem + a.sm.xq + t * d + 16 * xslot(p, qd, d / 256)) = make_uint4(w[0], w[1], w[2], w[3]);
+      if (qd == 0) reinterpret_cast<float*>(smem + a.sm.xs)[t * P + p] = qg.scale;
+      if ((qd & 1) == 0)
+        reinterpret_cast<float*>(smem + a.sm.xv)[t * 2 * P + 2 * p + (qd >> 1)] = static_cast<float>(sum);
       if (a.sm.xp) {
         uint8_t* xp = smem + a.sm.xp + t * d;
-        const int qv[4] = {q0, q1, q2, q3};
 #pragma unroll
-        for (unsigned i = 0; i < 4; ++i) {
-          const unsigned e = 4 * j + i, wi = (e % 64) / 32 * 32 + prmt_pos(e % 32);
-          xp[16 * xslot(p, wi / 16, d / 256) + wi % 16] = static_cast<uint8_t>(qv[i] & 0xff);
+        for (unsigned k = 0; k < 16; ++k) {
+          const unsigned e = 16 * qd + k, wi = (e / 32) * 32 + prmt_pos(e % 32);
+          xp[16 * xslot(p, wi / 16, d / 256) + wi % 16] = static_cast<uint8_t>(qv[k] & 0xff);
         }
       }
     }
