@@ -10,7 +10,11 @@ pre-normed residual stream h_{l+1} = h_l + y_l, so layers serialize as in
 real decode.  A step = one token through all 48 layers; value = tokens/s of
 the whole job (every GPU works on the same token: strong scaling).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+--tokens T (BASELINE configs[3] with T=16): T concurrent tokens per step, each
+with its own seeded top-10 routing per layer; one launch per layer serves the
+union of their experts.  value = T x steps/s.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl ours|reference]
 """
 import argparse
 import json
@@ -31,8 +35,15 @@ HIDDEN, LAYERS, SLICES, TOPK = 2048, 48, 20, 10
 SEED = 0x5EED
 POOL = 64
 SLICE_BYTES = 2 * 32 * (HIDDEN // 256) * 144 + HIDDEN * 17     # 108,544 (Q4_K gate/up + MXFP4 down)
-WORKLOAD = ("decode48 (BASELINE configs[2]): 48 MoE layers, 1 token, d=2048, 512 experts top-10, "
-            "Q4_K gate/up + MXFP4 down, 20 slices split over the GPUs, partial sum after every layer")
+
+
+def workload(tokens):
+    if tokens == 1:
+        return ("decode48 (BASELINE configs[2]): 48 MoE layers, 1 token, d=2048, 512 experts top-10, "
+                "Q4_K gate/up + MXFP4 down, 20 slices split over the GPUs, partial sum after every layer")
+    return ("decode48x%d (BASELINE configs[3]): 48 MoE layers, %d concurrent tokens with independent top-10 "
+            "routing (one launch per layer over the union of their experts), d=2048, 512 experts, Q4_K gate/up "
+            "+ MXFP4 down, 20 slices split over the GPUs, partial sum after every layer" % (tokens, tokens))
 
 
 _out = sys.stdout
@@ -55,19 +66,20 @@ def peaks():
         return 6650.0, "fallback 6.65 TB/s (MEASURED_PEAKS.json absent)"
 
 
-def step_routing(steps):
-    """Routing and gates for every (step, layer) and the token's x0 per step:
-    the same seeds the CPU baseline harness uses (oracle/ref_bench.c)."""
+def step_routing(steps, tokens=1):
+    """Routing and gates for every (step, layer, token) and the tokens' x0 per
+    step: the same seeds the CPU baseline harness uses (oracle/ref_bench.c).
+    Shapes [steps][48][T][10], [steps][48][T][11], [steps][T][2048]."""
     import fronk_b200 as fb
-    ex = np.zeros((steps, LAYERS, TOPK), np.uint16)
-    gt = np.zeros((steps, LAYERS, 11), np.float32)
-    x0 = np.zeros((steps, HIDDEN), np.float32)
+    ex = np.zeros((steps, LAYERS, tokens, TOPK), np.uint16)
+    gt = np.zeros((steps, LAYERS, tokens, 11), np.float32)
+    x0 = np.zeros((steps, tokens, HIDDEN), np.float32)
     for s in range(steps):
         for l in range(LAYERS):
-            e, g, x = fb.synth_request(HIDDEN, 1, fb.rand64(SEED, 1000003 * s + l))
-            ex[s, l], gt[s, l] = e[0], g[0]
+            e, g, x = fb.synth_request(HIDDEN, tokens, fb.rand64(SEED, 1000003 * s + l))
+            ex[s, l], gt[s, l] = e, g
             if l == 0:
-                x0[s] = x[0]
+                x0[s] = x
     return ex, gt, x0
 
 
@@ -124,22 +136,24 @@ class ClockSampler:
 
 # ------------------------------------------------------------ CPU baseline
 
-def cpu_baseline(steps, warmup):
+def cpu_baseline(steps, warmup, tokens=1):
     """The reference's own AVX2 backend (compiled from its sources into
-    oracle/_ref) on the same seeded workload, all host threads it tunes to."""
+    oracle/_ref) on the same seeded workload, all host threads it tunes to
+    (bursts of at most 8 tokens per call, the reference's FR_MAX_BURST)."""
     exe = os.path.join(ROOT, "oracle", "_ref", "ref_bench_2048")
     if not os.path.exists(exe):
         return {"unavailable": "reference not compiled (oracle/_ref/ref_bench_2048 missing)"}
     t0 = time.time()
-    out = subprocess.run([exe, "avx2", str(SLICES), str(POOL), str(steps), str(warmup), str(SEED)],
+    out = subprocess.run([exe, "avx2", str(SLICES), str(POOL), str(steps), str(warmup), str(SEED), str(tokens)],
                          capture_output=True, text=True, timeout=1800)
     if out.returncode:
         return {"unavailable": "ref_bench failed: " + out.stderr.strip()[-200:]}
     r = json.loads(out.stdout.strip().splitlines()[-1])
-    tok_s = 1e9 / r["ns_per_pass_mean"]
+    tok_s = tokens * 1e9 / r["ns_per_pass_mean"]
     return {"value": tok_s, "unit": "tokens/s", "cores": r["workers"], "kind": "reference",
             "sample": "reference backends/avx2.c (fr_avx2.run), full workload: all 20 slices resident in sparse "
-                      "host units, %d timed 48-layer passes after %d warm-up, d=2048 build" % (steps, warmup),
+                      "host units, %d timed 48-layer passes of %d token(s) after %d warm-up, d=2048 build"
+                      % (steps, tokens, warmup),
             "host": {"cpu": r["cpu"], "cores": r["cores"], "logical_cores": r["logical_cores"]},
             "ms_per_pass": r["ns_per_pass_mean"] / 1e6, "wall_s": round(time.time() - t0, 1)}
 
@@ -147,28 +161,30 @@ def cpu_baseline(steps, warmup):
 def run_reference(args, rank):
     if rank != 0:
         return
-    steps = max(1, min(args.steps, 50))
-    warm = max(1, min(args.warmup, 3))
-    cb = cpu_baseline(steps, warm)
+    steps = max(1, min(args.steps, 50 if args.tokens == 1 else 3))
+    warm = max(1, min(args.warmup, 3 if args.tokens == 1 else 1))
+    cb = cpu_baseline(steps, warm, args.tokens)
     if "unavailable" in cb:
         emit({"impl": "reference", "unavailable": cb["unavailable"]})
         return
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": steps, "warmup": warm, "ms_per_step": cb["ms_per_pass"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic", "config": config(args.gpus),
+            "data": "synthetic", "config": config(args.gpus, tokens=args.tokens),
             "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                         "d2h_bytes_per_step": 0}}
     emit(line)
 
 
-def config(n, reduce="peer"):
+def config(n, reduce="peer", tokens=1, unique_per_layer=TOPK):
     from fronk_b200.planner import equal_shares
-    return {"workload": WORKLOAD, "hidden": HIDDEN, "layers": LAYERS, "tokens_per_step": 1, "experts": 512,
-            "top_k": TOPK, "slices": SLICES, "shares": equal_shares(n), "formats": "Q4_K gate/up, MXFP4 down",
-            "activations": "Q8 per 64 (src/q4.c scheme), fp32 accumulate",
-            "weight_bytes_per_token": LAYERS * TOPK * SLICES * SLICE_BYTES,
-            "l2": "inputs larger than L2: 1.04 GB of expert weights per step, fresh routing every step",
+    step_bytes = LAYERS * unique_per_layer * SLICES * SLICE_BYTES
+    return {"workload": workload(tokens), "hidden": HIDDEN, "layers": LAYERS, "tokens_per_step": tokens,
+            "experts": 512, "top_k": TOPK, "slices": SLICES, "shares": equal_shares(n),
+            "formats": "Q4_K gate/up, MXFP4 down", "activations": "Q8 per 64 (src/q4.c scheme), fp32 accumulate",
+            "unique_experts_per_layer": unique_per_layer, "weight_bytes_per_step": int(step_bytes),
+            "l2": "inputs larger than L2: %.2f GB of expert weights per step, fresh routing every step"
+                  % (step_bytes / 1e9),
             "parallelism": ("slice-split x%d, per-layer sum of the partials %s" %
                             (n, "in the layer kernel over NVLink peer memory" if reduce == "peer" else "by NCCL all-reduce"))
                            if n > 1 else "1 GPU, all slices"}
@@ -182,6 +198,8 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=1, choices=range(1, 17), metavar="T",
+                    help="concurrent tokens per step (1: configs[2], the headline; 16: configs[3])")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--reduce", default="peer", choices=["peer", "nccl"],
                     help="per-layer sum of the GPUs' partials: in-kernel over NVLink peer memory, or NCCL all-reduce")
@@ -241,15 +259,16 @@ def main():
     run_flags = fb.RUN_RMSNORM | fb.RUN_OVERLAP | (fb.RUN_PEER if peer else 0)
 
     total = args.warmup + args.steps
-    ex, gt, x0 = step_routing(total)
+    T = args.tokens
+    ex, gt, x0 = step_routing(total, T)
     d_ex = torch.from_numpy(ex.astype(np.int16)).to(dev)          # ids < 512: int16 holds the u16 bits
     d_gt = torch.from_numpy(gt).to(dev)
     d_x0 = torch.from_numpy(x0).to(dev)
-    cur_ex = torch.empty((LAYERS, TOPK), dtype=torch.int16, device=dev)
-    cur_gt = torch.empty((LAYERS, 11), dtype=torch.float32, device=dev)
-    X0 = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
-    H = [torch.zeros(HIDDEN, dtype=torch.float32, device=dev) for _ in range(2)]
-    Y = [torch.zeros(HIDDEN, dtype=torch.float32, device=dev) for _ in range(2)]
+    cur_ex = torch.empty((LAYERS, T, TOPK), dtype=torch.int16, device=dev)
+    cur_gt = torch.empty((LAYERS, T, 11), dtype=torch.float32, device=dev)
+    X0 = torch.empty((T, HIDDEN), dtype=torch.float32, device=dev)
+    H = [torch.zeros((T, HIDDEN), dtype=torch.float32, device=dev) for _ in range(2)]
+    Y = [torch.zeros((T, HIDDEN), dtype=torch.float32, device=dev) for _ in range(2)]
 
     def p(t):
         return t.data_ptr()
@@ -262,7 +281,7 @@ def main():
             x_out = None if l == 0 else p(H[l % 2])
             # consecutive layers overlap: layer l+1 plans and starts its weight copies while
             # layer l (or the all-reduce after it) finishes; it reads x only after that
-            ctx.run_device(l, 1, p(cur_ex[l]), p(cur_gt[l]), p(x), x_add, x_out, p(Y[l % 2]), fb.ACT_Q8,
+            ctx.run_device(l, T, p(cur_ex[l]), p(cur_gt[l]), p(x), x_add, x_out, p(Y[l % 2]), fb.ACT_Q8,
                            run_flags, s)
             if dist is not None and not peer:
                 dist.all_reduce(Y[l % 2])
@@ -323,8 +342,10 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_per_step = ms / args.steps
-    tokens_s = 1000.0 / ms_per_step
+    tokens_s = T * 1000.0 / ms_per_step
     launches = LAYERS * args.steps
+    # distinct experts a launch reads (the union over the step's tokens; 10 at T=1)
+    unique = float(np.mean([len(np.unique(ex[s, l])) for s in range(args.warmup, total) for l in range(LAYERS)]))
 
     # ---- kernel alone: event-bracketed launches on the launching stream
     kt = []
@@ -333,13 +354,13 @@ def main():
         load_step(s)
         for l in range(LAYERS):
             ev[l][0].record(stream)
-            ctx.run_device(l, 1, p(cur_ex[l]), p(cur_gt[l]), p(X0), None, None, p(Y[0]), fb.ACT_Q8,
+            ctx.run_device(l, T, p(cur_ex[l]), p(cur_gt[l]), p(X0), None, None, p(Y[0]), fb.ACT_Q8,
                            fb.RUN_RMSNORM, stream.cuda_stream)
             ev[l][1].record(stream)
         torch.cuda.synchronize()
         kt += [a.elapsed_time(b) for a, b in ev]
     kernel_ms = statistics.mean(kt)
-    bytes_per_launch = TOPK * len(blocks) * SLICE_BYTES
+    bytes_per_launch = unique * len(blocks) * SLICE_BYTES
     peak, peak_src = peaks()
     # average launch duration over the timed region: at N=1 the passes hold
     # nothing but the layer kernel (profiles/layer_kernel_decode48_launches.md);
@@ -350,7 +371,7 @@ def main():
 
     # ---- end to end through the C ABI with host buffers (reference-facing call)
     e2e_steps = max(3, min(args.steps, 50))
-    e2e = e2e_run(ctx, fb, ex, gt, x0, e2e_steps, dist, dev, peer)
+    e2e = e2e_run(ctx, fb, ex, gt, x0, e2e_steps, dist, dev, peer, T)
 
     # ---- parity at full size: one layer of the filled units vs the oracle
     parity = full_size_parity(ctx, fb, g, pool, blocks)
@@ -358,16 +379,17 @@ def main():
     used_graph = graph is not None
     del graph
     if rank == 0:
-        weight_bytes = LAYERS * TOPK * SLICES * SLICE_BYTES
+        weight_bytes = LAYERS * unique * SLICES * SLICE_BYTES      # per step, all GPUs
         line = {
             "metric": METRIC, "value": tokens_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config(world, args.reduce),
-            "weight_gbs": weight_bytes * tokens_s / 1e9,
-            "weight_frac_of_peak": weight_bytes * tokens_s / 1e9 / peak,
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": config(world, args.reduce, T, unique),
+            "weight_gbs": weight_bytes * 1e3 / ms_per_step / 1e9,
+            "weight_frac_of_peak": weight_bytes * 1e3 / ms_per_step / 1e9 / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": ncu_traffic(), "peak_source": peak_src,
-                         "kernel": "layer_kernel<Q8,1> (one launch per layer)",
+                         "kernel": "moe_layer_kernel<Q8> (one launch per layer, %d token(s))" % T,
                          "algorithmic_bytes_per_launch": bytes_per_launch, "launch_us": launch_us,
                          "launch_us_source": "CUDA events over the timed passes / launches"
                                              + (" (includes the all-reduce)" if world > 1 else ""),
@@ -375,7 +397,7 @@ def main():
             "gpu_launches": launches, "graph": used_graph, "clocks": clocks, "e2e": e2e, "parity": parity,
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(3, 1)
+            line["cpu_baseline"] = cpu_baseline(3, 1) if T == 1 else cpu_baseline(1, 1, T)
         emit(line)
     ctx.close()
     if dist is not None:
@@ -383,13 +405,13 @@ def main():
         dist.destroy_process_group()
 
 
-def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev, peer=False):
+def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev, peer=False, T=1):
     """tokens/s through the public call with host buffers: per layer the
     request is copied in, the layer runs, y is copied out (frc_run; at N>1
     the device entry point plus the all-reduce)."""
     import torch
-    h2d = LAYERS * (HIDDEN * 4 + TOPK * 2 + 11 * 4)
-    d2h = LAYERS * (HIDDEN * 4 + (16 if dist is None else 0))  # y (+ the status word frc_run reads with it)
+    h2d = LAYERS * T * (HIDDEN * 4 + TOPK * 2 + 11 * 4)
+    d2h = LAYERS * (T * HIDDEN * 4 + (16 if dist is None else 0))  # y (+ the status word frc_run reads with it)
     if dist is None:
         # the layer loop in C over the host-buffer call (frc_host_pass -> frc_run per layer)
         hs = [np.ascontiguousarray(x0[s], np.float32).copy() for s in range(steps)]
@@ -399,27 +421,27 @@ def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev, peer=False):
             ctx.host_pass(0, es[s], gt[s], hs[s], fb.ACT_Q8)
         dt = time.perf_counter() - t0
     else:
-        pin_x = torch.empty(HIDDEN, dtype=torch.float32).pin_memory()
-        pin_e = torch.empty(TOPK, dtype=torch.int16).pin_memory()
-        pin_g = torch.empty(11, dtype=torch.float32).pin_memory()
-        pin_y = torch.empty(HIDDEN, dtype=torch.float32).pin_memory()
-        dx, de, dg = torch.empty(HIDDEN, device=dev), torch.empty(TOPK, dtype=torch.int16, device=dev), \
-            torch.empty(11, device=dev)
-        dy = torch.empty(HIDDEN, device=dev)
+        pin_x = torch.empty((T, HIDDEN), dtype=torch.float32).pin_memory()
+        pin_e = torch.empty((T, TOPK), dtype=torch.int16).pin_memory()
+        pin_g = torch.empty((T, 11), dtype=torch.float32).pin_memory()
+        pin_y = torch.empty((T, HIDDEN), dtype=torch.float32).pin_memory()
+        dx, de, dg = torch.empty((T, HIDDEN), device=dev), torch.empty((T, TOPK), dtype=torch.int16, device=dev), \
+            torch.empty((T, 11), device=dev)
+        dy = torch.empty((T, HIDDEN), device=dev)
         st = torch.cuda.current_stream()
         dist.barrier()
         t0 = time.perf_counter()
         for s in range(steps):
             h = x0[s].copy()
             for l in range(LAYERS):
-                x = (h / np.sqrt(np.mean(h * h) + np.float32(1e-6))).astype(np.float32)
+                x = (h / np.sqrt(np.mean(h * h, axis=-1, keepdims=True) + np.float32(1e-6))).astype(np.float32)
                 pin_x.numpy()[:] = x
                 pin_e.numpy()[:] = ex[s, l].astype(np.int16)
                 pin_g.numpy()[:] = gt[s, l]
                 dx.copy_(pin_x, non_blocking=True)
                 de.copy_(pin_e, non_blocking=True)
                 dg.copy_(pin_g, non_blocking=True)
-                ctx.run_device(l, 1, de.data_ptr(), dg.data_ptr(), dx.data_ptr(), None, None, dy.data_ptr(),
+                ctx.run_device(l, T, de.data_ptr(), dg.data_ptr(), dx.data_ptr(), None, None, dy.data_ptr(),
                                fb.ACT_Q8, fb.RUN_PEER if peer else 0, st.cuda_stream)
                 if not peer:
                     dist.all_reduce(dy)
@@ -433,7 +455,7 @@ def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev, peer=False):
     rc = ctx.status(None)
     if rc:
         raise fb.FrcError(rc, "e2e", ctx.last_error)
-    return {"value": steps / dt, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+    return {"value": T * steps / dt, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": steps, "api": "frc_host_pass: frc_run per layer (host buffers, synchronous)" if dist is None else
             ("frc_run_device with the in-kernel NVLink reduce" if peer else "frc_run_device + NCCL all_reduce")
             + ", pinned host copies each layer"}

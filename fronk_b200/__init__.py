@@ -66,7 +66,7 @@ _SIGS = {
     "frc_run": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _int]),
     "frc_run_device": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
     "frc_run_device_fixed": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
-    "frc_host_pass": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _u32, _int]),
+    "frc_host_pass": (_int, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _u32, _int]),
     "frc_peer_export": (_int, [_vp, _u32, _vp]),
     "frc_peer_attach": (_int, [_vp, _u32, _u32, _vp]),
     "frc_peer_detach": (_int, [_vp]),
@@ -273,12 +273,15 @@ class Context:
         self._check(rc, "run_device_fixed")
 
     def host_pass(self, first_layer, expert, gate, h, act=ACT_Q8):
-        """Decode pass from the host (frc_host_pass): h is updated in place."""
+        """Decode pass from the host (frc_host_pass).  expert: [layers][10] or
+        [layers][tokens][10]; h ([hidden] or [tokens][hidden], fp32) is updated in place."""
         expert = np.ascontiguousarray(expert, np.uint16)
         gate = np.ascontiguousarray(gate, np.float32)
         assert h.dtype == np.float32 and h.flags.c_contiguous
-        rc = self.lib.frc_host_pass(self.h, first_layer, expert.shape[0], _ptr(expert), _ptr(gate), _ptr(h),
-                                    h.size, act)
+        tokens = expert.shape[1] if expert.ndim == 3 else 1
+        hidden = h.shape[-1]
+        rc = self.lib.frc_host_pass(self.h, first_layer, expert.shape[0], tokens, _ptr(expert), _ptr(gate), _ptr(h),
+                                    hidden, act)
         self._check(rc, "host_pass")
 
     def peer_export(self, world):

@@ -155,15 +155,16 @@ int frc_peer_export(frc_context *c, unsigned world, void *handle);
 int frc_peer_attach(frc_context *c, unsigned rank, unsigned world, const void *handles);
 int frc_peer_detach(frc_context *c);
 
-/* A decode pass for one token driven from the host, layer by layer through
- * frc_run (host buffers, one synchronous call per layer):
+/* A decode pass for `tokens` tokens driven from the host, layer by layer
+ * through frc_run (host buffers, one synchronous call per layer): per token
  * x = h / sqrt(mean(h^2) + 1e-6), y = run(layer, x), h += y, for layers
- * first_layer .. first_layer + layers - 1.  expert: [layers][10], gate:
- * [layers][11]; h (hidden floats) is the residual stream, updated in place.
- * The end-to-end path of a host that owns the layer loop (the reference's
- * head calls fr_backend.run once per layer the same way). */
-int frc_host_pass(frc_context *c, unsigned first_layer, unsigned layers, const uint16_t *expert,
-                  const float *gate, float *h, unsigned hidden, int act);
+ * first_layer .. first_layer + layers - 1.  expert: [layers][tokens][10],
+ * gate: [layers][tokens][11]; h ([tokens][hidden]) is the residual stream,
+ * updated in place.  The end-to-end path of a host that owns the layer loop
+ * (the reference's head calls fr_backend.run once per layer the same way).
+ * Not reentrant (static staging). */
+int frc_host_pass(frc_context *c, unsigned first_layer, unsigned layers, unsigned tokens,
+                  const uint16_t *expert, const float *gate, float *h, unsigned hidden, int act);
 /* Waits for `stream`, returns and clears the device status (FRC_OK,
  * FRC_NUMERIC, FRC_INVALID for an out-of-range id, FRC_IO for a timed-out wait). */
 int frc_status(frc_context *c, void *stream);

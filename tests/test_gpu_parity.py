@@ -205,27 +205,29 @@ def test_failures_leave_output_untouched(gpu):
                 assert rc == NUMERIC and np.array_equal(y, sentinel), (offset, act)
 
 
-def test_host_pass_equals_layer_by_layer_runs(gpu):
+@pytest.mark.parametrize("tokens", [1, 3])
+def test_host_pass_equals_layer_by_layer_runs(gpu, tokens):
     """frc_host_pass (the C layer loop over frc_run) against the same chain
     driven call by call from Python: identical residual stream."""
     hidden, layers = 2048, 3
     g = fb.geometry(hidden)
-    routes = [request(hidden, 1, SEED + 300 + l, 0.0) for l in range(layers)]
+    routes = [request(hidden, tokens, SEED + 300 + l, 0.3 if l == 1 else 0.0) for l in range(layers)]
     experts = np.concatenate([r[0].ravel() for r in routes])
     with fb.Context(0, hidden) as ctx:
         lay = make_layers(g, SEED, [2, 9], experts, shared=True)
         for l in range(layers):
             for b, arr in lay.items():
                 assert ctx.load_layer(b, l, arr) == OK, ctx.last_error
-        h0 = routes[0][2][0].astype(np.float32)
+        h0 = routes[0][2].astype(np.float32)
         h = h0.copy()
         for l in range(layers):
-            ss = float(np.sum(h.astype(np.float64) ** 2))
-            inv = np.float32(1.0 / np.sqrt(ss / hidden + 1e-6))
+            ss = np.sum(h.astype(np.float64) ** 2, axis=1, keepdims=True)
+            inv = (1.0 / np.sqrt(ss / hidden + 1e-6)).astype(np.float32)
             x = (h * inv).astype(np.float32)
-            rc, y = ctx.run(l, routes[l][0], routes[l][1], x[None], fb.ACT_Q8)
+            rc, y = ctx.run(l, routes[l][0], routes[l][1], x, fb.ACT_Q8)
             assert rc == OK, ctx.last_error
-            h = (h + y[0]).astype(np.float32)
-        hp = h0.copy()
-        ctx.host_pass(0, np.concatenate([r[0] for r in routes]), np.concatenate([r[1] for r in routes]), hp)
-        assert np.array_equal(hp.view(np.uint32), h.view(np.uint32))
+            h = (h + y).astype(np.float32)
+        hp = h0.copy() if tokens > 1 else h0[0].copy()
+        ctx.host_pass(0, np.stack([r[0] for r in routes]) if tokens > 1 else np.concatenate([r[0] for r in routes]),
+                      np.stack([r[1] for r in routes]) if tokens > 1 else np.concatenate([r[1] for r in routes]), hp)
+        assert np.array_equal(hp.reshape(h.shape).view(np.uint32), h.view(np.uint32))
