@@ -23,6 +23,7 @@ RUN_OVERLAP = 2
 RUN_PEER = 4
 PEER_HANDLE_BYTES = 64
 MAX_BLOCKS, ROUTED, SHARED, TOPK, ACTIVE, NEURONS, MAX_TOKENS = 20, 512, 512, 10, 11, 32, 16
+MAX_PREFILL_TOKENS = 512
 LAYERS = 48
 
 _CODES = {OK: "OK", INVALID: "INVALID", STATE: "STATE", NUMERIC: "NUMERIC", IO: "IO",
@@ -79,6 +80,7 @@ _SIGS = {
     "frc_encode_row": (_int, [_u32, _vp, _u32, _vp]),
     "frc_synth_slice": (_int, [_vp, _u64, _u64, _vp]),
     "frc_synth_shared": (_int, [_vp, _u64, _u64, _vp]),
+    "frc_synth_request_zipf": (_int, [_u32, _u32, _u64, ctypes.c_double, _vp, _vp, _vp]),
     "frc_synth_request": (_int, [_u32, _u32, _u64, _vp, _vp, _vp]),
     "frc_pool_load": (_int, [_vp, _vp, _u32, _vp]),
     "frc_fill_layer": (_int, [_vp, _int, _u32, _u64]),
@@ -86,6 +88,8 @@ _SIGS = {
     "frc_debug_decode": (_int, [_vp, _u32, _vp, _u32, _u32, _vp]),
     "frc_debug_quantize": (_int, [_vp, _u32, _vp, _vp, _vp, _vp]),
     "frc_debug_hidden": (_int, [_vp, _vp, _sz, _vp]),
+    "frc_debug_umma": (_int, [_vp, _u32, _u32, _vp, _vp, _vp]),
+    "frc_debug_prefill_hidden": (_int, [_vp, _vp, _vp, _sz, _vp]),
     "frc_debug_phases": (_int, [_vp, _vp, _sz, _vp]),
 }
 EXPORTS = sorted(_SIGS) + ["fr_cuda", "fr_cuda_f32", "fr_cuda_select_device", "fr_cuda_close"]
@@ -159,12 +163,16 @@ def synth_shared(g, seed, key):
     return out
 
 
-def synth_request(hidden, tokens, seed):
-    """(expert [T,10] u16, gate [T,11] f32, x [T,d] f32) of frc_synth_request."""
+def synth_request(hidden, tokens, seed, zipf=None):
+    """(expert [T,10] u16, gate [T,11] f32, x [T,d] f32) of frc_synth_request
+    (frc_synth_request_zipf with exponent `zipf`)."""
     e = np.zeros((tokens, TOPK), np.uint16)
     gt = np.zeros((tokens, ACTIVE), np.float32)
     x = np.zeros((tokens, hidden), np.float32)
-    rc = library().frc_synth_request(hidden, tokens, seed, _ptr(e), _ptr(gt), _ptr(x))
+    if zipf is None:
+        rc = library().frc_synth_request(hidden, tokens, seed, _ptr(e), _ptr(gt), _ptr(x))
+    else:
+        rc = library().frc_synth_request_zipf(hidden, tokens, seed, float(zipf), _ptr(e), _ptr(gt), _ptr(x))
     if rc:
         raise FrcError(rc, "synth_request")
     return e, gt, x
@@ -326,6 +334,25 @@ class Context:
         self._check(self.lib.frc_debug_quantize(self.h, tokens, _ptr(x), _ptr(q), _ptr(s), _ptr(deq)),
                     "debug_quantize")
         return q, s, deq
+
+    def debug_umma(self, a, b):
+        """int32 a[128][k] @ b[n][k]^T through the tcgen05 kind::i8 check kernel."""
+        a = np.ascontiguousarray(a, np.int8)
+        b = np.ascontiguousarray(b, np.int8)
+        d = np.zeros((128, b.shape[0]), np.int32)
+        self._check(self.lib.frc_debug_umma(self.h, b.shape[0], a.shape[1], _ptr(a), _ptr(b), _ptr(d)), "debug_umma")
+        return d
+
+    def debug_prefill_hidden(self):
+        """(hq [pair][block][32] int8, hs [pair][block] f32) of the last prefill burst."""
+        n = ctypes.c_size_t()
+        self._check(self.lib.frc_debug_prefill_hidden(self.h, None, None, 0, ctypes.byref(n)), "debug_prefill_hidden")
+        S = bin(self.loaded_mask()).count("1")
+        hq = np.zeros((n.value, S, 32), np.int8)
+        hs = np.zeros((n.value, S), np.float32)
+        self._check(self.lib.frc_debug_prefill_hidden(self.h, _ptr(hq), _ptr(hs), n.value, ctypes.byref(n)),
+                    "debug_prefill_hidden")
+        return hq, hs
 
     def debug_phases(self):
         """[cta][16] globaltimer stamps of the last launch (FRC_PHASES builds)."""

@@ -20,6 +20,8 @@
 using namespace frc;
 
 #include "frc_layer.cuh"
+#include "frc_umma.cuh"
+#include "frc_prefill.cuh"
 
 // ===================================================== set-up kernels
 
@@ -113,6 +115,64 @@ __global__ void quantize_kernel(const float* x, unsigned n, int8_t* q, float* sc
   deq[64 * g + 2 * lane + 1] = __double2float_rn(d1);
 }
 
+// Tensor-core check: D[128][N] = A[128][K] * B[N][K]^T in int32 through
+// tcgen05 (K/32 MMA steps, accumulators in tensor memory, read back with
+// tcgen05.ld).  One CTA of 128 threads; K a multiple of 32 up to 256, N a
+// multiple of 16 up to 256.
+__global__ void __launch_bounds__(128) umma_check_kernel(const int8_t* A, const int8_t* B, int32_t* D, unsigned N,
+                                                         unsigned K, unsigned* status) {
+  extern __shared__ __align__(1024) uint8_t sm[];
+  __shared__ uint64_t bar;
+  __shared__ uint32_t taddr_s;
+  uint8_t* As = sm;
+  uint8_t* Bs = sm + 128 * K;
+  const unsigned tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, kc = K / 16;
+  for (unsigned i = tid; i < 128 * kc; i += 128) {
+    const unsigned r = i / kc, c = i % kc;
+    *reinterpret_cast<uint4*>(As + umma_off(r, 16 * c, K)) = *reinterpret_cast<const uint4*>(A + r * K + 16 * c);
+  }
+  for (unsigned i = tid; i < N * kc; i += 128) {
+    const unsigned r = i / kc, c = i % kc;
+    *reinterpret_cast<uint4*>(Bs + umma_off(r, 16 * c, K)) = *reinterpret_cast<const uint4*>(B + r * K + 16 * c);
+  }
+  fence_proxy_async();
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  const unsigned ncols = N <= 32 ? 32 : N <= 64 ? 64 : N <= 128 ? 128 : 256;
+  if (warp == 0) {
+    tmem_alloc(&taddr_s, ncols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t taddr = taddr_s;
+  if (tid == 0) {
+    const uint32_t a0 = smem_u32(As), b0 = smem_u32(Bs), idesc = umma_idesc_i8(128, N);
+    for (unsigned s = 0; s < K / 32; ++s)
+      umma_i8(taddr, umma_desc(a0 + 256 * s, 128, 8 * K), umma_desc(b0 + 256 * s, 128, 8 * K), idesc, s > 0);
+    umma_commit(&bar);
+  }
+  const bool ok = mbar_wait(&bar, 0);
+  tc_fence_after();
+  if (ok) {
+    for (unsigned c = 0; c < N; c += 16) {
+      uint32_t r[16];
+      tmem_ld16(taddr + ((32 * warp) << 16) + c, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (unsigned j = 0; j < 16; ++j) D[(32 * warp + lane) * N + c + j] = static_cast<int32_t>(r[j]);
+    }
+  } else if (lane == 0) {
+    atomicOr(status, kStTimeout);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(taddr, ncols);
+}
+
 // ========================================================= host runtime
 
 struct frc_context {
@@ -148,8 +208,27 @@ struct frc_context {
   unsigned rank = 0, world = 0, peer_gmax = 0;
   uint16_t last_expert[FRC_MAX_TOKENS * FRC_TOPK] = {};
   float last_gate[FRC_MAX_TOKENS * FRC_ACTIVE] = {};
+  // prefill (bursts above FRC_MAX_TOKENS; MXFP4 gate/up and down only):
+  // activations, pairs, work lists, hidden values and expert partials
+  int8_t* pf_xq = nullptr;
+  float* pf_xs = nullptr;
+  uint16_t* pf_pair_token = nullptr;
+  unsigned* pf_slot_pair = nullptr;
+  unsigned* pf_counts = nullptr;
+  uint4* pf_items_gu = nullptr;
+  uint4* pf_items_dn = nullptr;
+  int8_t* pf_hq = nullptr;
+  float* pf_hs = nullptr;
+  float* pf_ye = nullptr;
+  bool pf_attr = false;
+  unsigned last_pf_S = 0;
   char err[256] = {};
 };
+
+// Prefill bounds: pairs of one call, and work items (tiles of 64 tokens of
+// each expert: at most pairs / 64 + 512 of them).
+constexpr size_t kPfMaxPairs = size_t(FRC_MAX_PREFILL_TOKENS) * FRC_TOPK;
+constexpr size_t kPfMaxTiles = kPfMaxPairs / kPfTile + FRC_ROUTED_EXPERTS;
 
 static int fail(frc_context* c, int rc, const char* fmt, ...) {
   if (c) {
@@ -325,10 +404,16 @@ struct RunScratch {
   float* hidden;   // [u*S+s][T][32] or null
 };
 
+static int run_long(frc_context* c, unsigned layer, unsigned T, const uint16_t* expert, const float* gate,
+                    const float* x, const float* x_add, float* x_out, float* y, int act, unsigned flags,
+                    cudaStream_t s, const struct RunScratch* scratch, bool chunks);
+
 static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t* expert, const float* gate,
                       const float* x, const float* x_add, float* x_out, float* y, int act, unsigned flags,
-                      cudaStream_t s, const RunScratch* scratch = nullptr) {
+                      cudaStream_t s, const RunScratch* scratch = nullptr, bool chunks = false) {
   if (!c || !expert || !gate || !x || !y) return fail(c, FRC_INVALID, "null argument");
+  if (act != FRC_ACT_Q8 && act != FRC_ACT_F32) return fail(c, FRC_INVALID, "unknown activation mode");
+  if (T > FRC_MAX_TOKENS) return run_long(c, layer, T, expert, gate, x, x_add, x_out, y, act, flags, s, scratch, chunks);
   if (T < 1 || T > FRC_MAX_TOKENS || layer >= c->g.layers) return fail(c, FRC_INVALID, "tokens or layer out of range");
   if (act != FRC_ACT_Q8 && act != FRC_ACT_F32) return fail(c, FRC_INVALID, "unknown activation mode");
   LayerParams a{};
@@ -367,6 +452,66 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
   const bool overlap = (flags & FRC_RUN_OVERLAP) != 0;
   if (act == FRC_ACT_Q8) return launch_layer<FRC_ACT_Q8>(c, a, s, overlap);
   return launch_layer<FRC_ACT_F32>(c, a, s, overlap);
+}
+
+// A burst of more than FRC_MAX_TOKENS tokens.  With MXFP4 weights, Q8
+// activations and no run flags it takes the tensor-core prefill path
+// (frc_prefill.cuh; a nonzero shared-expert gate is rejected there);
+// otherwise it runs as bursts of FRC_MAX_TOKENS through the layer kernel
+// (`chunks` forces that).
+static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_t* expert, const float* gate,
+                       const float* x, float* y, cudaStream_t s) {
+  PrefillArgs a{};
+  unsigned S = 0;
+  for (unsigned b = 0; b < FRC_MAX_BLOCKS; ++b) {
+    bool any = false;
+    for (unsigned l = 0; l < c->g.layers; ++l) any |= c->layer_ptr[b][l] != nullptr;
+    if (!any) continue;
+    if (!c->layer_ptr[b][layer]) return fail(c, FRC_STATE, "block %u is loaded but not layer %u", b, layer);
+    a.base[S++] = c->layer_ptr[b][layer];
+  }
+  if (!S) return fail(c, FRC_STATE, "no block loaded");
+  const unsigned d = c->g.hidden;
+  a.x = x; a.expert = expert; a.gate = gate; a.y = y;
+  a.T = T; a.d = d; a.S = S;
+  a.row_bytes = static_cast<unsigned>(c->row_bytes);
+  a.slice_bytes = c->slice_bytes;
+  a.xq = c->pf_xq; a.xs = c->pf_xs; a.pair_token = c->pf_pair_token; a.slot_pair = c->pf_slot_pair;
+  a.counts = c->pf_counts; a.items_gu = c->pf_items_gu; a.items_dn = c->pf_items_dn;
+  a.hq = c->pf_hq; a.hs = c->pf_hs; a.ye = c->pf_ye; a.status = c->status;
+  const unsigned smem = sizeof(PfSmem);
+  if (!c->pf_attr) {
+    CK(cudaFuncSetAttribute(prefill_mma_kernel<kGateUp>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(prefill_mma_kernel<kDown>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    c->pf_attr = true;
+  }
+  const unsigned groups = T * (d / 64);
+  prefill_quantize_kernel<<<(groups + 7) / 8, 256, 0, s>>>(a);
+  prefill_group_kernel<<<1, 1024, 0, s>>>(a);
+  prefill_mma_kernel<kGateUp><<<c->sms, kPfThreads, smem, s>>>(a);
+  prefill_mma_kernel<kDown><<<c->sms, kPfThreads, smem, s>>>(a);
+  prefill_combine_kernel<<<dim3(d / 256, T), 256, 0, s>>>(a);
+  CK(cudaGetLastError());
+  c->launches += 5;
+  c->last_pf_S = S;
+  return FRC_OK;
+}
+
+static int run_long(frc_context* c, unsigned layer, unsigned T, const uint16_t* expert, const float* gate,
+                    const float* x, const float* x_add, float* x_out, float* y, int act, unsigned flags,
+                    cudaStream_t s, const RunScratch* scratch, bool chunks) {
+  if (T > FRC_MAX_PREFILL_TOKENS || layer >= c->g.layers) return fail(c, FRC_INVALID, "tokens or layer out of range");
+  if (!chunks && act == FRC_ACT_Q8 && !flags && !scratch && c->pf_ye)
+    return run_prefill(c, layer, T, expert, gate, x, y, s);
+  const size_t d = c->g.hidden;
+  for (unsigned t0 = 0; t0 < T; t0 += FRC_MAX_TOKENS) {
+    const unsigned n = T - t0 < FRC_MAX_TOKENS ? T - t0 : FRC_MAX_TOKENS;
+    const int rc = run_device(c, layer, n, expert + t0 * FRC_TOPK, gate + t0 * FRC_ACTIVE, x + t0 * d,
+                              x_add ? x_add + t0 * d : nullptr, x_out ? x_out + t0 * d : nullptr, y + t0 * d, act,
+                              flags, s, scratch);
+    if (rc) return rc;
+  }
+  return FRC_OK;
 }
 
 static int status_code(unsigned st) {
@@ -460,7 +605,21 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
   alloc(reinterpret_cast<void**>(&c->gsv), sizeof(float) * kMaxPairs * kMaxBlocks);
   alloc(reinterpret_cast<void**>(&c->ctl), sizeof(LayerCtl));
   alloc(reinterpret_cast<void**>(&c->phases), sizeof(unsigned long long) * 16 * 1024);
-  const size_t in_bytes = kInBytesPerToken(d) * kMaxTokens, out_bytes = 16 + sizeof(float) * kMaxTokens * d;
+  const size_t in_bytes = kInBytesPerToken(d) * FRC_MAX_PREFILL_TOKENS,
+               out_bytes = 16 + sizeof(float) * FRC_MAX_PREFILL_TOKENS * d;
+  if (g->gate_type == FRC_MXFP4 && g->down_type == FRC_MXFP4) {
+    const size_t T = FRC_MAX_PREFILL_TOKENS;
+    alloc(reinterpret_cast<void**>(&c->pf_xq), T * d);
+    alloc(reinterpret_cast<void**>(&c->pf_xs), sizeof(float) * T * (d / 64));
+    alloc(reinterpret_cast<void**>(&c->pf_pair_token), sizeof(uint16_t) * kPfMaxPairs);
+    alloc(reinterpret_cast<void**>(&c->pf_slot_pair), sizeof(unsigned) * kPfMaxPairs);
+    alloc(reinterpret_cast<void**>(&c->pf_counts), sizeof(unsigned) * 4);
+    alloc(reinterpret_cast<void**>(&c->pf_items_gu), sizeof(uint4) * kPfMaxTiles * ((FRC_MAX_BLOCKS + 1) / 2));
+    alloc(reinterpret_cast<void**>(&c->pf_items_dn), sizeof(uint4) * kPfMaxTiles * (d / 128));
+    alloc(reinterpret_cast<void**>(&c->pf_hq), kPfMaxPairs * FRC_MAX_BLOCKS * 32);
+    alloc(reinterpret_cast<void**>(&c->pf_hs), sizeof(float) * kPfMaxPairs * FRC_MAX_BLOCKS);
+    alloc(reinterpret_cast<void**>(&c->pf_ye), sizeof(float) * kPfMaxPairs * d);
+  }
   alloc(reinterpret_cast<void**>(&c->d_in), in_bytes);
   alloc(reinterpret_cast<void**>(&c->d_out), out_bytes);
   if (rc == FRC_OK) {
@@ -496,6 +655,8 @@ int frc_close(frc_context* c) {
     for (auto& p : b) if (p) cudaFree(p);
   cudaFree(c->staging); cudaFree(c->hidden); cudaFree(c->partial); cudaFree(c->gsv); cudaFree(c->phases); cudaFree(c->ctl);
   cudaFree(c->d_in); cudaFree(c->d_out); cudaFree(c->pool);
+  cudaFree(c->pf_xq); cudaFree(c->pf_xs); cudaFree(c->pf_pair_token); cudaFree(c->pf_slot_pair); cudaFree(c->pf_counts);
+  cudaFree(c->pf_items_gu); cudaFree(c->pf_items_dn); cudaFree(c->pf_hq); cudaFree(c->pf_hs); cudaFree(c->pf_ye);
   cudaFreeHost(c->h_in); cudaFreeHost(c->h_out);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
@@ -592,11 +753,13 @@ static int validate(const frc_context* c, unsigned T, const uint16_t* expert, co
 
 int frc_run(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* expert, const float* gate, const float* x,
             float* y, int act) {
-  if (!c || !expert || !gate || !x || !y || tokens < 1 || tokens > FRC_MAX_TOKENS || layer >= c->g.layers ||
+  if (!c || !expert || !gate || !x || !y || tokens < 1 || tokens > FRC_MAX_PREFILL_TOKENS || layer >= c->g.layers ||
       (act != FRC_ACT_Q8 && act != FRC_ACT_F32))
     return fail(c, FRC_INVALID, "bad run arguments");
   int rc = validate(c, tokens, expert, gate, x);
   if (rc) return fail(c, rc, "request rejected");
+  bool shared = false;  // the prefill path has no shared expert: such bursts run in chunks
+  for (unsigned t = 0; t < tokens; ++t) shared |= gate[t * FRC_ACTIVE + FRC_TOPK] != 0.0f;
   CK(cudaSetDevice(c->device));
   // one copy in: [x][gate][expert] packed for this call's token count
   const size_t xb = sizeof(float) * tokens * c->g.hidden, gb = sizeof(float) * tokens * FRC_ACTIVE;
@@ -607,11 +770,13 @@ int frc_run(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* exp
   CK(cudaMemcpyAsync(c->d_in, c->h_in, xb + gb + eb, cudaMemcpyHostToDevice, c->stream));
   rc = run_device(c, layer, tokens, reinterpret_cast<const uint16_t*>(c->d_in + xb + gb),
                   reinterpret_cast<const float*>(c->d_in + xb), reinterpret_cast<const float*>(c->d_in), nullptr,
-                  nullptr, c->d_y, act, 0, c->stream);
+                  nullptr, c->d_y, act, 0, c->stream, nullptr, shared);
   if (rc) return rc;
-  c->last_T = tokens;
-  memcpy(c->last_expert, expert, eb);
-  memcpy(c->last_gate, gate, gb);
+  if (tokens <= FRC_MAX_TOKENS) {
+    c->last_T = tokens;
+    memcpy(c->last_expert, expert, eb);
+    memcpy(c->last_gate, gate, gb);
+  }
   // one copy out: the status word and y
   CK(cudaMemcpyAsync(c->h_out, c->d_out, 16 + xb, cudaMemcpyDeviceToHost, c->stream));
   CK(cudaMemsetAsync(c->status, 0, sizeof(unsigned), c->stream));
@@ -813,6 +978,55 @@ int frc_debug_quantize(frc_context* c, unsigned tokens, const float* x, int8_t* 
   CK(cudaMemcpy(scale, ds, sizeof(float) * n / 64, cudaMemcpyDeviceToHost));
   CK(cudaMemcpy(deq, dd, sizeof(float) * n, cudaMemcpyDeviceToHost));
   cudaFree(dx); cudaFree(dq); cudaFree(ds); cudaFree(dd);
+  return FRC_OK;
+}
+
+int frc_debug_umma(frc_context* c, unsigned n, unsigned k, const int8_t* a, const int8_t* b, int32_t* d) {
+  if (!c || !a || !b || !d || !n || n > 256 || n % 16 || !k || k > 256 || k % 32)
+    return fail(c, FRC_INVALID, "bad umma check shape");
+  CK(cudaSetDevice(c->device));
+  int8_t *da = nullptr, *db = nullptr;
+  int32_t* dd = nullptr;
+  CK(cudaMalloc(&da, 128 * k));
+  CK(cudaMalloc(&db, n * k));
+  CK(cudaMalloc(&dd, sizeof(int32_t) * 128 * n));
+  CK(cudaMemcpy(da, a, 128 * k, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(db, b, n * k, cudaMemcpyHostToDevice));
+  CK(cudaMemsetAsync(c->status, 0, sizeof(unsigned), c->stream));
+  const unsigned smem = (128 + n) * k;
+  CK(cudaFuncSetAttribute(umma_check_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  umma_check_kernel<<<1, 128, smem, c->stream>>>(da, db, dd, n, k, c->status);
+  CK(cudaGetLastError());
+  ++c->launches;
+  CK(cudaStreamSynchronize(c->stream));
+  unsigned st = 0;
+  CK(cudaMemcpy(&st, c->status, sizeof st, cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(d, dd, sizeof(int32_t) * 128 * n, cudaMemcpyDeviceToHost));
+  cudaFree(da); cudaFree(db); cudaFree(dd);
+  return st ? fail(c, FRC_IO, "umma check timed out") : FRC_OK;
+}
+
+int frc_debug_prefill_hidden(frc_context* c, int8_t* hq, float* hs, size_t cap, size_t* pairs) {
+  if (!c || !pairs || !c->pf_counts || !c->last_pf_S) return fail(c, FRC_INVALID, "no prefill run to report");
+  CK(cudaSetDevice(c->device));
+  CK(cudaStreamSynchronize(c->stream));
+  unsigned P = 0;
+  CK(cudaMemcpy(&P, c->pf_counts, sizeof P, cudaMemcpyDeviceToHost));
+  *pairs = P;
+  if (!hq && !hs) return FRC_OK;
+  if (cap < P) return fail(c, FRC_INVALID, "capacity %zu below %u pairs", cap, P);
+  const size_t S = c->last_pf_S, n = static_cast<size_t>(P) * S * 32;
+  if (hq) {
+    int8_t* tmp = static_cast<int8_t*>(malloc(n));
+    if (!tmp) return fail(c, FRC_IO, "host buffer");
+    const cudaError_t e = cudaMemcpy(tmp, c->pf_hq, n, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess)  // device order: prmt order within each 32-block
+      for (size_t blk = 0; blk < n / 32; ++blk)
+        for (unsigned k = 0; k < 32; ++k) hq[32 * blk + k] = tmp[32 * blk + prmt_pos(k)];
+    free(tmp);
+    if (e != cudaSuccess) return fail(c, FRC_IO, "%s", cudaGetErrorString(e));
+  }
+  if (hs) CK(cudaMemcpy(hs, c->pf_hs, sizeof(float) * P * S, cudaMemcpyDeviceToHost));
   return FRC_OK;
 }
 

@@ -172,7 +172,7 @@ struct Q8Group {
 
 // Position of element n (0..31) of a 32-weight block in the "prmt order" that
 // matches an MXFP4 block's nibble bytes (byte j holds elements j and j+16).
-__device__ __forceinline__ unsigned prmt_pos(unsigned n) {
+__host__ __device__ __forceinline__ unsigned prmt_pos(unsigned n) {
   const unsigned j = n & 15, hi = n >> 4, m = j >> 2, r = j & 3;
   return 4 * (2 * m + (r >> 1)) + 2 * (r & 1) + hi;
 }

@@ -1,0 +1,541 @@
+// frc_prefill.cuh - the batched (prefill) path: bursts of up to 512 tokens
+// with MXFP4 gate/up rows on the 5th-generation tensor cores.
+//
+// One layer call is five launches on one stream:
+//   1. prefill_quantize_kernel: x -> int8 per 64 (the ref-q8 scheme of
+//      src/q4.c:37-61), each 32-block stored in the nibble order of an MXFP4
+//      block (prmt order), plus one fp32 scale per 64;
+//   2. prefill_group_kernel (one CTA): validation, the (expert, token) pairs
+//      expert-major with tokens ascending (a bitmap per expert, ranks by
+//      popcount), and the work lists, biggest experts first;
+//   3. prefill_mma_kernel<kGateUp>: item = (expert, pair of loaded blocks,
+//      up to 64 of its tokens).  A = the 128 gate/up rows of the two slices
+//      (int8: doubled E2M1 values), B = the tokens' int8 activations,
+//      D = int32 in tensor memory, one tcgen05.mma kind::i8 per 32-weight
+//      block; the epilogue applies the block's two scales in fp32, then
+//      SwiGLU (double) and Q8 per 32 give hq / hscale per (pair, block);
+//   4. prefill_mma_kernel<kDown>: item = (expert, 128 output rows, tokens);
+//      A = MXFP4 down rows, B = hq, one MMA per loaded block;
+//   5. prefill_combine_kernel: y[t] = sum over the token's experts in
+//      request order of gate * partial, fmaf in fp32.
+// The arithmetic is restated step for step by the oracle's or_prefill_run.
+//
+// Inside an MMA kernel (one CTA per SM, 320 threads) warps have roles:
+//   warps 0-3 convert: raw MXFP4 payload (staged by TMA bulk copies) ->
+//     int8 A tiles in the K-major no-swizzle layout of frc_umma.cuh, and
+//     gather the B rows, row scales and column scales with cp.async;
+//   warps 4-7 are the epilogue (TMEM lanes 0-127 = A rows);
+//   warp 8 issues the bulk copies; warp 9 owns tensor memory and issues
+//   the MMAs (one thread).
+// Rings: 4 raw stages, 2 A/B stages, 4 accumulator buffers of 64 columns.
+// Every wait gives up after 2 s (kStTimeout) so a fault cannot hang the GPU.
+#pragma once
+
+namespace frc {
+
+constexpr unsigned kPfTile = 64;        // tokens per item (MMA N <= 64)
+constexpr unsigned kPfRaw = 4;          // raw payload stages
+constexpr unsigned kPfRawBytes = 16384; // 128 rows x 128 B (gate/up) or 8 blocks x 128 rows x 16 B (down)
+constexpr unsigned kPfA = 128 * 256;    // A stage: 128 rows x K 256
+constexpr unsigned kPfB = kPfTile * 256;
+constexpr unsigned kPfAcc = 4;          // accumulator buffers
+constexpr unsigned kPfThreads = 320;
+enum : unsigned { kGateUp = 0, kDown = 1 };
+
+struct PrefillArgs {
+  const float* x;          // [T][d]
+  const uint16_t* expert;  // [T][10]
+  const float* gate;       // [T][11]
+  float* y;                // [T][d]
+  unsigned T, d, S;        // tokens, hidden size, loaded blocks
+  unsigned row_bytes;      // MXFP4 gate/up row: d/32 scales + d/2 payload
+  unsigned long long slice_bytes;
+  const uint8_t* base[kMaxBlocks];  // this layer of each loaded block, ascending
+  // scratch
+  int8_t* xq;              // [T][d], prmt order per 32-block
+  float* xs;               // [T][d/64]
+  uint16_t* pair_token;    // [P]
+  unsigned* slot_pair;     // [T][10]
+  unsigned* counts;        // [0] pairs, [1] gate/up items, [2] down items
+  uint4* items_gu;         // {expert, first pair, tokens, block pair}
+  uint4* items_dn;         // {expert, first pair, tokens, row tile}
+  int8_t* hq;              // [P][S][32], prmt order per block
+  float* hs;               // [P][S]
+  float* ye;               // [P][d]
+  unsigned* status;
+};
+
+// ------------------------------------------------------------- helpers
+
+__device__ __forceinline__ bool pf_wait(uint64_t* bar, unsigned parity, volatile unsigned* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return false;
+    if (globaltimer() - start > kWaitNs) {
+      *abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
+// The same decision for a whole warp (lane 0 waits): warp-collective
+// instructions after it (tcgen05.ld, __syncwarp) need every lane.
+__device__ __forceinline__ bool pf_wait_warp(uint64_t* bar, unsigned parity, volatile unsigned* abort) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = pf_wait(bar, parity, abort);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// 16 payload bytes of one MXFP4 block (byte j: element j low nibble, element
+// j+16 high nibble) -> 32 int8 doubled E2M1 values in prmt order: for word m,
+// bytes (j, j+16, j+1, j+17) then (j+2, j+18, j+3, j+19), j = 4m.
+__device__ __forceinline__ void mxfp4_to_i8(uint4 q, uint4& lo, uint4& hi) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+  uint32_t o[8];
+#pragma unroll
+  for (unsigned m = 0; m < 4; ++m) {
+#pragma unroll
+    for (unsigned h = 0; h < 2; ++h) {
+      const uint32_t sel = h ? w[m] >> 16 : w[m];
+      const uint32_t pos = prmt(kE2M1Lo, kE2M1Hi, sel), neg = prmt(kE2M1Lo, kE2M1Hi, sel ^ 0x8888u);
+      // byte-wise pos - neg (one of them is 0): no borrow crosses a byte
+      o[2 * m + h] = ((pos | 0x80808080u) - neg) ^ 0x80808080u;
+    }
+  }
+  lo = make_uint4(o[0], o[1], o[2], o[3]);
+  hi = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+// --------------------------------------------------------- 1. quantize
+
+// One warp per 64-group, two values per lane; the operations of
+// quantize_kernel, the int8 values written in prmt order.
+__global__ void prefill_quantize_kernel(PrefillArgs a) {
+  const unsigned g = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
+  const unsigned groups = a.T * (a.d / 64);
+  if (g >= groups) return;
+  const float2 v = reinterpret_cast<const float2*>(a.x + 64 * static_cast<size_t>(g))[lane];
+  const bool bad = !isfinite(v.x) || !isfinite(v.y);
+  if (__any_sync(0xffffffffu, bad)) {
+    if (lane == 0) atomicOr(a.status, kStNumeric);
+    return;
+  }
+  float amax = fmaxf(fabsf(v.x), fabsf(v.y));
+#pragma unroll
+  for (unsigned o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const Q8Group q(amax);
+  int8_t* out = a.xq + 64 * static_cast<size_t>(g);
+  const unsigned n0 = 2 * lane, blk = n0 >> 5, n = n0 & 31;
+  out[32 * blk + prmt_pos(n)] = static_cast<int8_t>(q.q(v.x));
+  out[32 * blk + prmt_pos(n + 1)] = static_cast<int8_t>(q.q(v.y));
+  if (lane == 0) a.xs[g] = q.scale;
+}
+
+// ------------------------------------------------------------ 2. group
+
+// Single CTA of 1024 threads.  Validation (ids < 512 and distinct per token,
+// gates finite and >= 0, shared gate 0), pairs, work lists.
+__global__ void __launch_bounds__(1024) prefill_group_kernel(PrefillArgs a) {
+  __shared__ uint32_t bits[512][16];  // token bitmap per expert (T <= 512)
+  __shared__ unsigned cnt[512], rank_of[512], ibase_gu[513], ibase_dn[513], poff[513];
+  __shared__ unsigned by_rank[512];
+  const unsigned tid = threadIdx.x, T = a.T, words = (T + 31) / 32;
+  for (unsigned i = tid; i < 512 * 16; i += blockDim.x) (&bits[0][0])[i] = 0;
+  __syncthreads();
+  unsigned st = 0;
+  for (unsigned i = tid; i < T * 10; i += blockDim.x) {
+    const unsigned t = i / 10, e = a.expert[i];
+    if (e >= 512) { st |= kStInvalid; continue; }
+    const uint32_t bit = 1u << (t & 31);
+    if (atomicOr(&bits[e][t >> 5], bit) & bit) st |= kStInvalid;  // the same expert twice in one token
+  }
+  for (unsigned i = tid; i < T * 11; i += blockDim.x) {
+    const float g = a.gate[i];
+    if (!isfinite(g)) st |= kStNumeric;
+    else if (g < 0.0f) st |= kStInvalid;
+    else if (i % 11 == 10 && g != 0.0f) st |= kStInvalid;  // shared expert: decode path only
+  }
+  if (st) atomicOr(a.status, st);
+  __syncthreads();
+  for (unsigned e = tid; e < 512; e += blockDim.x) {
+    unsigned c = 0;
+    for (unsigned w = 0; w < words; ++w) c += __popc(bits[e][w]);
+    cnt[e] = c;
+  }
+  __syncthreads();
+  // rank experts by token count descending, ties by id
+  for (unsigned e = tid; e < 512; e += blockDim.x) {
+    const unsigned c = cnt[e];
+    unsigned r = 0;
+    for (unsigned f = 0; f < 512; ++f) r += cnt[f] > c || (cnt[f] == c && f < e);
+    rank_of[e] = r;
+    by_rank[r] = e;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned npairs = (a.S + 1) / 2, nrt = a.d / 128;
+    unsigned p = 0, gu = 0, dn = 0;
+    for (unsigned e = 0; e < 512; ++e) { poff[e] = p; p += cnt[e]; }
+    poff[512] = p;
+    for (unsigned r = 0; r < 512; ++r) {
+      const unsigned e = by_rank[r], tiles = (cnt[e] + kPfTile - 1) / kPfTile;
+      ibase_gu[r] = gu; ibase_dn[r] = dn;
+      gu += tiles * npairs; dn += tiles * nrt;
+    }
+    a.counts[0] = p; a.counts[1] = gu; a.counts[2] = dn;
+  }
+  __syncthreads();
+  for (unsigned i = tid; i < T * 10; i += blockDim.x) {
+    const unsigned t = i / 10, e = a.expert[i];
+    if (e >= 512) { a.slot_pair[i] = 0xffffffffu; continue; }
+    unsigned r = __popc(bits[e][t >> 5] & ((1u << (t & 31)) - 1));
+    for (unsigned w = 0; w < (t >> 5); ++w) r += __popc(bits[e][w]);
+    const unsigned p = poff[e] + r;
+    a.pair_token[p] = static_cast<uint16_t>(t);
+    a.slot_pair[i] = p;
+  }
+  const unsigned npairs = (a.S + 1) / 2, nrt = a.d / 128;
+  for (unsigned e = tid; e < 512; e += blockDim.x) {
+    const unsigned c = cnt[e], tiles = (c + kPfTile - 1) / kPfTile, r = rank_of[e];
+    for (unsigned k = 0; k < tiles; ++k) {
+      const unsigned n = min(kPfTile, c - k * kPfTile), p0 = poff[e] + k * kPfTile;
+      for (unsigned q = 0; q < npairs; ++q) a.items_gu[ibase_gu[r] + k * npairs + q] = make_uint4(e, p0, n, q);
+      for (unsigned q = 0; q < nrt; ++q) a.items_dn[ibase_dn[r] + k * nrt + q] = make_uint4(e, p0, n, q);
+    }
+  }
+}
+
+// ---------------------------------------------------------- 3/4. MMA
+
+struct PfSmem {
+  uint8_t raw[kPfRaw][kPfRawBytes];
+  uint8_t A[2][kPfA];
+  uint8_t B[2][kPfB];
+  float colscale[2][8][kPfTile];  // per block of the chunk, per token
+  uint8_t rowscale[2][8][128];    // per block of the chunk, per A row (E8M0)
+  float amax[4][kPfTile];         // gate/up epilogue: per-warp amax per token
+  uint64_t raw_full[kPfRaw], raw_empty[kPfRaw];
+  uint64_t ab_full[2], ab_empty[2], sc_empty[2];
+  uint64_t acc_full[kPfAcc], acc_empty[kPfAcc];
+  uint32_t taddr;
+  unsigned abort;
+};
+
+template <unsigned MODE>
+__device__ __forceinline__ unsigned pf_chunks(const PrefillArgs& a) {
+  return MODE == kGateUp ? a.d / 256 : (a.S + 7) / 8;
+}
+template <unsigned MODE>
+__device__ __forceinline__ unsigned pf_steps(const PrefillArgs& a, unsigned k) {
+  return MODE == kGateUp ? 8u : min(8u, a.S - 8 * k);
+}
+// Loaded-block index and HBM row (within the slice) of A row m of a gate/up
+// item: warp m/32 holds 16 neurons of one block, lanes 0-15 gate, 16-31 up.
+__device__ __forceinline__ void gu_row(unsigned m, unsigned pair, unsigned& blk, unsigned& hrow) {
+  const unsigned w = m >> 5, l = m & 31;
+  blk = 2 * pair + (w >> 1);
+  hrow = (l >> 4) * 32 + 16 * (w & 1) + (l & 15);
+}
+
+template <unsigned MODE>
+__global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(PrefillArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  PfSmem& s = *reinterpret_cast<PfSmem*>(smem_raw);
+  const unsigned tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const unsigned nitems = a.counts[MODE == kGateUp ? 1 : 2];
+  const uint4* items = MODE == kGateUp ? a.items_gu : a.items_dn;
+  const unsigned nk = pf_chunks<MODE>(a), d = a.d, nb = d / 32;
+  volatile unsigned* abort = &s.abort;
+
+  if (tid == 0) {
+    for (unsigned i = 0; i < kPfRaw; ++i) { mbar_init(&s.raw_full[i], 1); mbar_init(&s.raw_empty[i], 128); }
+    for (unsigned i = 0; i < 2; ++i) {
+      mbar_init(&s.ab_full[i], 128); mbar_init(&s.ab_empty[i], 1); mbar_init(&s.sc_empty[i], 4);
+    }
+    for (unsigned i = 0; i < kPfAcc; ++i) { mbar_init(&s.acc_full[i], 1); mbar_init(&s.acc_empty[i], 4); }
+    s.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(&s.taddr, kPfAcc * kPfTile);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.taddr;
+
+  if (warp == 8) {
+    // ------------------------------------------------ producer: bulk copies
+    unsigned c = 0;
+    for (unsigned it = blockIdx.x; it < nitems && !*abort; it += gridDim.x) {
+      const uint4 item = items[it];
+      for (unsigned k = 0; k < nk; ++k, ++c) {
+        const unsigned st = c % kPfRaw;
+        if (!pf_wait_warp(&s.raw_empty[st], ((c / kPfRaw) & 1) ^ 1, abort)) break;
+        uint8_t* dst = s.raw[st];
+        if (MODE == kGateUp) {
+          const unsigned rows = 2 * item.w + 1 < a.S ? 128 : 64;
+          if (lane == 0) mbar_expect_tx(&s.raw_full[st], rows * 128);
+          __syncwarp();
+          for (unsigned m = lane; m < rows; m += 32) {
+            unsigned blk, hrow;
+            gu_row(m, item.w, blk, hrow);
+            const uint8_t* src = a.base[blk] + item.x * a.slice_bytes + static_cast<size_t>(hrow) * a.row_bytes + nb +
+                                 128 * k;
+            bulk_g2s(dst + 128 * m, src, 128, &s.raw_full[st]);
+          }
+        } else {
+          const unsigned steps = pf_steps<MODE>(a, k);
+          if (lane == 0) mbar_expect_tx(&s.raw_full[st], steps * 2048);
+          __syncwarp();
+          if (lane < steps) {
+            const unsigned blk = 8 * k + lane;
+            const uint8_t* down = a.base[blk] + item.x * a.slice_bytes + 64ull * a.row_bytes;
+            bulk_g2s(dst + 2048 * lane, down + d + static_cast<size_t>(item.w) * 128 * 16, 2048, &s.raw_full[st]);
+          }
+        }
+      }
+    }
+    // every issued copy must have landed before the CTA exits
+    for (unsigned i = 0; i < kPfRaw && c > i; ++i) {
+      const unsigned last = c - 1 - i;  // the most recent uses of each stage
+      if (lane == 0) pf_wait(&s.raw_full[last % kPfRaw], (last / kPfRaw) & 1, abort);
+    }
+    __syncwarp();
+  } else if (warp == 9) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      unsigned c = 0, q = 0;
+      for (unsigned it = blockIdx.x; it < nitems && !*abort; it += gridDim.x) {
+        const uint4 item = items[it];
+        const unsigned npad = (item.z + 15) & ~15u;
+        const uint32_t idesc = umma_idesc_i8(128, npad);
+        for (unsigned k = 0; k < nk && !*abort; ++k, ++c) {
+          const unsigned ab = c & 1;
+          if (!pf_wait(&s.ab_full[ab], (c >> 1) & 1, abort)) break;
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(s.A[ab]), b0 = smem_u32(s.B[ab]);
+          const unsigned steps = pf_steps<MODE>(a, k);
+          for (unsigned st = 0; st < steps; ++st, ++q) {
+            const unsigned buf = q % kPfAcc;
+            if (!pf_wait(&s.acc_empty[buf], ((q / kPfAcc) & 1) ^ 1, abort)) break;
+            tc_fence_after();
+            umma_i8(tmem + buf * kPfTile, umma_desc(a0 + 256 * st, 128, 8 * 256), umma_desc(b0 + 256 * st, 128, 8 * 256),
+                    idesc, false);
+            umma_commit(&s.acc_full[buf]);
+          }
+          umma_commit(&s.ab_empty[ab]);
+        }
+      }
+      // the last commit's arrive must land before the CTA exits
+      if (c) pf_wait(&s.ab_empty[(c - 1) & 1], ((c - 1) >> 1) & 1, abort);
+    }
+    __syncwarp();
+  } else if (warp < 4) {
+    // ------------------------------------------------ converters
+    const unsigned m = tid;  // A row
+    unsigned c = 0;
+    for (unsigned it = blockIdx.x; it < nitems && !*abort; it += gridDim.x) {
+      const uint4 item = items[it];
+      unsigned blk = 0, hrow = 0;
+      if (MODE == kGateUp) gu_row(m, item.w, blk, hrow);
+      const bool row_live = MODE != kGateUp || blk < a.S;
+      for (unsigned k = 0; k < nk; ++k, ++c) {
+        const unsigned st = c % kPfRaw, ab = c & 1, steps = pf_steps<MODE>(a, k);
+        if (!pf_wait(&s.ab_empty[ab], ((c >> 1) & 1) ^ 1, abort)) break;
+        if (!pf_wait(&s.sc_empty[ab], ((c >> 1) & 1) ^ 1, abort)) break;
+        // B rows: the tile's tokens (gate/up: x of the token; down: hq of the pair)
+        for (unsigned i = tid; i < item.z * 16; i += 128) {
+          const unsigned j = i >> 4, piece = i & 15;
+          if (MODE == kDown && piece >= 2 * steps) continue;
+          const int8_t* src = MODE == kGateUp
+                                  ? a.xq + static_cast<size_t>(a.pair_token[item.y + j]) * d + 256 * k + 16 * piece
+                                  : a.hq + (static_cast<size_t>(item.y + j) * a.S + 8 * k) * 32 + 16 * piece;
+          cp_async16(s.B[ab] + umma_off(j, 16 * piece, 256), src);
+        }
+        // scales of the chunk's blocks
+        if (MODE == kGateUp) {
+          if (row_live) {
+            const uint8_t* row = a.base[blk] + item.x * a.slice_bytes + static_cast<size_t>(hrow) * a.row_bytes;
+            cp_async8(&s.rowscale[ab][0][0] + 8 * m, row + 8 * k);  // gate/up: [row][8 blocks]
+          }
+          for (unsigned i = tid; i < item.z * 4; i += 128) {
+            const unsigned j = i >> 2, g = i & 3;
+            const float v = a.xs[static_cast<size_t>(a.pair_token[item.y + j]) * (d / 64) + 4 * k + g];
+            s.colscale[ab][2 * g][j] = v;
+            s.colscale[ab][2 * g + 1][j] = v;
+          }
+        } else {
+          for (unsigned i = tid; i < steps * 8; i += 128) {
+            const unsigned b = i >> 3, piece = i & 7;
+            const uint8_t* down = a.base[8 * k + b] + item.x * a.slice_bytes + 64ull * a.row_bytes;
+            cp_async16(&s.rowscale[ab][b][0] + 16 * piece, down + item.w * 128 + 16 * piece);
+          }
+          for (unsigned i = tid; i < item.z * steps; i += 128) {
+            const unsigned j = i / steps, b = i % steps;
+            s.colscale[ab][b][j] = a.hs[static_cast<size_t>(item.y + j) * a.S + 8 * k + b];
+          }
+        }
+        cp_async_commit();
+        // A: raw payload -> int8
+        if (!pf_wait(&s.raw_full[st], (c / kPfRaw) & 1, abort)) break;
+        uint8_t* A = s.A[ab];
+        if (MODE == kGateUp) {
+          if (row_live) {
+#pragma unroll
+            for (unsigned i = 0; i < 8; ++i) {
+              const unsigned b = (i + m) & 7;  // rotated: conflict-free reads and writes
+              uint4 lo, hi;
+              mxfp4_to_i8(*reinterpret_cast<const uint4*>(s.raw[st] + 128 * m + 16 * b), lo, hi);
+              *reinterpret_cast<uint4*>(A + umma_off(m, 32 * b, 256)) = lo;
+              *reinterpret_cast<uint4*>(A + umma_off(m, 32 * b + 16, 256)) = hi;
+            }
+          }
+        } else {
+          for (unsigned b = 0; b < steps; ++b) {
+            uint4 lo, hi;
+            mxfp4_to_i8(*reinterpret_cast<const uint4*>(s.raw[st] + 2048 * b + 16 * m), lo, hi);
+            *reinterpret_cast<uint4*>(A + umma_off(m, 32 * b, 256)) = lo;
+            *reinterpret_cast<uint4*>(A + umma_off(m, 32 * b + 16, 256)) = hi;
+          }
+        }
+        mbar_arrive(&s.raw_empty[st]);
+        cp_async_wait_all();
+        fence_proxy_async();
+        mbar_arrive(&s.ab_full[ab]);
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 4-7)
+    const unsigned ew = warp - 4, m = 32 * ew + lane;
+    const uint32_t lane_base = tmem + ((32 * ew) << 16);
+    unsigned c = 0, q = 0;
+    bool bad = false;
+    // No abort test in these loops: the four warps must take the same number
+    // of epi_sync barriers; after an abort every wait fails at once.
+    for (unsigned it = blockIdx.x; it < nitems; it += gridDim.x) {
+      const uint4 item = items[it];
+      const unsigned ntok = item.z;
+      float acc[kPfTile];
+#pragma unroll
+      for (unsigned j = 0; j < kPfTile; ++j) acc[j] = 0.0f;
+      bool live = true;
+      if (MODE == kGateUp) {
+        unsigned blk, hrow;
+        gu_row(m, item.w, blk, hrow);
+        live = blk < a.S;
+      }
+      for (unsigned k = 0; k < nk; ++k, ++c) {
+        const unsigned ab = c & 1, steps = pf_steps<MODE>(a, k);
+        // the converters' scales of this chunk (acquired directly: the stage
+        // cannot move on before this warp releases sc_empty below)
+        pf_wait_warp(&s.ab_full[ab], (c >> 1) & 1, abort);
+        for (unsigned st = 0; st < steps; ++st, ++q) {
+          const unsigned buf = q % kPfAcc;
+          if (!pf_wait_warp(&s.acc_full[buf], (q / kPfAcc) & 1, abort)) continue;
+          tc_fence_after();
+          uint32_t v[kPfTile];
+#pragma unroll
+          for (unsigned g = 0; g < kPfTile / 16; ++g)
+            if (16 * g < ntok) tmem_ld16(lane_base + buf * kPfTile + 16 * g, *reinterpret_cast<uint32_t(*)[16]>(v + 16 * g));
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.acc_empty[buf]);
+          const unsigned e8 = MODE == kGateUp ? (&s.rowscale[ab][0][0])[8 * m + st] : s.rowscale[ab][st][m];
+          bad |= live && e8 == 255;
+          const float ws = pow2_m128(e8);
+          const float* cs = s.colscale[ab][st];
+#pragma unroll
+          for (unsigned j = 0; j < kPfTile; ++j)
+            if (j < ntok) acc[j] = __fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), cs[j]), ws, acc[j]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.sc_empty[ab]);
+      }
+      const bool ok = !*abort;
+      if (MODE == kDown) {
+        if (!ok) continue;
+        float* out = a.ye + static_cast<size_t>(item.y) * d + 128 * item.w + m;
+#pragma unroll
+        for (unsigned j = 0; j < kPfTile; ++j)
+          if (j < ntok) out[static_cast<size_t>(j) * d] = acc[j];
+      } else {
+        // SwiGLU: lane l < 16 (gate) takes tokens 0-31, lane l + 16 (up) tokens 32-63
+        const bool up = lane >= 16;
+        float h[32];
+#pragma unroll
+        for (unsigned j = 0; j < 32; ++j) {
+          const float mine = up ? acc[j] : acc[j + 32];
+          const float other = __shfl_xor_sync(0xffffffffu, mine, 16);
+          const float g = up ? other : acc[j], u = up ? acc[j + 32] : other;
+          const unsigned t = j + (up ? 32 : 0);
+          h[j] = 0.0f;
+          if (t < ntok && live && !swiglu(g, u, &h[j])) bad = true;
+        }
+        // amax per token over the block's 32 neurons (16 here, 16 in the partner warp)
+#pragma unroll
+        for (unsigned j = 0; j < 32; ++j) {
+          float am = fabsf(h[j]);
+#pragma unroll
+          for (unsigned o = 8; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+          if ((lane & 15) == 0) s.amax[ew][j + (up ? 32 : 0)] = am;
+        }
+        epi_sync();
+        const unsigned blk = 2 * item.w + (ew >> 1), n = 16 * (ew & 1) + (lane & 15);
+        if (live && ok) {
+          int8_t* hq = a.hq + static_cast<size_t>(item.y) * a.S * 32 + blk * 32 + prmt_pos(n);
+#pragma unroll
+          for (unsigned j = 0; j < 32; ++j) {
+            const unsigned t = j + (up ? 32 : 0);
+            if (t < ntok) {
+              const float am = fmaxf(s.amax[ew][t], s.amax[ew ^ 1][t]);
+              const Q8Group qg(am);
+              hq[static_cast<size_t>(t) * a.S * 32] = static_cast<int8_t>(qg.q(h[j]));
+              if ((ew & 1) == 0 && (lane & 15) == 0) a.hs[static_cast<size_t>(item.y + t) * a.S + blk] = qg.scale;
+            }
+          }
+        }
+        epi_sync();
+      }
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(a.status, kStNumeric);
+  }
+  if (tid == 0 && *abort) atomicOr(a.status, kStTimeout);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) tmem_dealloc(tmem, kPfAcc * kPfTile);
+}
+
+// ---------------------------------------------------------- 5. combine
+
+// y[t][r] = fmaf over the token's ten experts in request order of
+// gate * partial; one thread per (t, r).
+__global__ void prefill_combine_kernel(PrefillArgs a) {
+  const unsigned t = blockIdx.y, r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= a.d) return;
+  const unsigned P = a.counts[0];
+  float acc = 0.0f;
+#pragma unroll
+  for (unsigned j = 0; j < 10; ++j) {
+    const unsigned p = a.slot_pair[t * 10 + j];
+    if (p >= P) {  // an id the group kernel rejected (status already set)
+      acc = 0.0f;
+      break;
+    }
+    acc = __fmaf_rn(a.gate[t * 11 + j], a.ye[static_cast<size_t>(p) * a.d + r], acc);
+  }
+  if (!isfinite(acc)) atomicOr(a.status, kStNumeric);
+  a.y[static_cast<size_t>(t) * a.d + r] = acc;
+}
+
+}  // namespace frc

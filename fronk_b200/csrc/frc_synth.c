@@ -222,7 +222,8 @@ int frc_synth_shared(const frc_geometry *g, uint64_t seed, uint64_t key, uint8_t
 }
 
 int frc_synth_request(unsigned hidden, unsigned tokens, uint64_t seed, uint16_t *expert, float *gate, float *x) {
-    if (!expert || !gate || !x || !hidden || hidden % 32 || !tokens || tokens > FRC_MAX_TOKENS) return FRC_INVALID;
+    if (!expert || !gate || !x || !hidden || hidden % 32 || !tokens || tokens > FRC_MAX_PREFILL_TOKENS)
+        return FRC_INVALID;
     const uint64_t xs = 1ull << 40, rs = 2ull << 40, gs = 3ull << 40;
     for (unsigned t = 0; t < tokens; ++t) {
         for (unsigned j = 0; j < hidden; ++j) x[(size_t)t * hidden + j] = frc_normal(seed, xs + (uint64_t)t * hidden + j);
@@ -241,6 +242,38 @@ int frc_synth_request(unsigned hidden, unsigned tokens, uint64_t seed, uint16_t 
         for (unsigned i = 0; i < FRC_TOPK; ++i) { z[i] = expf(z[i] - m); sum += z[i]; }
         for (unsigned i = 0; i < FRC_TOPK; ++i) gate[t * FRC_ACTIVE + i] = z[i] / sum;
         gate[t * FRC_ACTIVE + FRC_TOPK] = 0;
+    }
+    return FRC_OK;
+}
+
+int frc_synth_request_zipf(unsigned hidden, unsigned tokens, uint64_t seed, double zs, uint16_t *expert,
+                           float *gate, float *x) {
+    if (!(zs >= 0) || zs > 16) return FRC_INVALID;
+    int rc = frc_synth_request(hidden, tokens, seed, expert, gate, x);
+    if (rc) return rc;
+    /* popularity rank: a seeded permutation of the experts */
+    const uint64_t ps = 4ull << 40, us = 5ull << 40;
+    unsigned rank[FRC_ROUTED_EXPERTS];
+    for (unsigned i = 0; i < FRC_ROUTED_EXPERTS; ++i) rank[i] = i;
+    for (unsigned i = FRC_ROUTED_EXPERTS - 1; i > 0; --i) {
+        unsigned j = (unsigned)(frc_rand64(seed, ps + i) % (i + 1));
+        unsigned tmp = rank[i]; rank[i] = rank[j]; rank[j] = tmp;
+    }
+    double logw[FRC_ROUTED_EXPERTS];
+    for (unsigned e = 0; e < FRC_ROUTED_EXPERTS; ++e) logw[e] = -zs * log((double)rank[e] + 1.0);
+    for (unsigned t = 0; t < tokens; ++t) {
+        double key[FRC_ROUTED_EXPERTS];
+        for (unsigned e = 0; e < FRC_ROUTED_EXPERTS; ++e) {
+            const double u = ((double)(frc_rand64(seed, us + (uint64_t)t * FRC_ROUTED_EXPERTS + e) >> 11) + 0.5) *
+                             (1.0 / 9007199254740992.0);
+            key[e] = logw[e] - log(-log(u));
+        }
+        for (unsigned i = 0; i < FRC_TOPK; ++i) { /* selection of the ten largest keys, descending */
+            unsigned best = 0;
+            for (unsigned e = 1; e < FRC_ROUTED_EXPERTS; ++e) if (key[e] > key[best]) best = e;
+            expert[t * FRC_TOPK + i] = (uint16_t)best;
+            key[best] = -INFINITY;
+        }
     }
     return FRC_OK;
 }

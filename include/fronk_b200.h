@@ -39,7 +39,7 @@ enum { FRC_ACT_F32 = 0, FRC_ACT_Q8 = 1 };
 /* Model constants of src/model.h:18-27. */
 enum { FRC_MAX_BLOCKS = 20, FRC_ROUTED_EXPERTS = 512, FRC_SHARED_EXPERT = 512,
        FRC_TOPK = 10, FRC_ACTIVE = 11, FRC_NEURONS = 32, FRC_MAX_TOKENS = 16,
-       FRC_MAX_LAYERS = 64 };
+       FRC_MAX_LAYERS = 64, FRC_MAX_PREFILL_TOKENS = 512 };
 
 /* Shape of one ownership unit (a "block" of the reference: the same 32
  * neurons of every expert in every layer).  The reference's own layout is
@@ -189,10 +189,17 @@ int frc_encode_row(unsigned type, const float *w, unsigned n, uint8_t *out);
 int frc_synth_slice(const frc_geometry *g, uint64_t seed, uint64_t key, uint8_t *out);
 /* The shared expert's slice (Q8_0 x3), weights ~N(0, 0.02). */
 int frc_synth_shared(const frc_geometry *g, uint64_t seed, uint64_t key, uint8_t *out);
-/* A request: x ~ N(0,1); 10 of 512 experts uniform without replacement;
- * gates softmax(N(0,1)) over the 10; shared gate 0. */
+/* A request of up to FRC_MAX_PREFILL_TOKENS tokens: x ~ N(0,1); 10 of 512
+ * experts uniform without replacement; gates softmax(N(0,1)) over the 10;
+ * shared gate 0.  Token t's values do not depend on the token count. */
 int frc_synth_request(unsigned hidden, unsigned tokens, uint64_t seed,
                       uint16_t *expert, float *gate, float *x);
+/* The same with Zipf(s)-skewed expert popularity: expert e has weight
+ * (rank(e) + 1)^-s, rank a seeded permutation of the 512 experts, and each
+ * token draws 10 without replacement in proportion to the weights (Gumbel
+ * top-k), most likely first.  x and gates as frc_synth_request. */
+int frc_synth_request_zipf(unsigned hidden, unsigned tokens, uint64_t seed, double s,
+                           uint16_t *expert, float *gate, float *x);
 
 /* ---- Benchmark-scale units without host encoding ---- */
 /* Uploads `count` routed slices and one shared slice (reference layout) as a
@@ -211,6 +218,16 @@ int frc_debug_decode(frc_context *c, unsigned type, const uint8_t *rows, unsigne
  * scale per 64, and the dequantized fp32 values of src/q4.c:37-61. */
 int frc_debug_quantize(frc_context *c, unsigned tokens, const float *x, int8_t *q,
                        float *scale, float *deq);
+/* Tensor-core (tcgen05 kind::i8) check: d[128][n] = a[128][k] * b[n][k]^T in
+ * int32, row-major host arrays; n a multiple of 16 up to 256, k a multiple of
+ * 32 up to 256. */
+int frc_debug_umma(frc_context *c, unsigned n, unsigned k, const int8_t *a, const int8_t *b, int32_t *d);
+/* Quantized hidden values of the last prefill burst (more than
+ * FRC_MAX_TOKENS tokens on the tensor-core path): hq [pair][loaded block][32]
+ * int8 in neuron order and hs [pair][loaded block] fp32 scales, pairs
+ * (expert, token) expert-major with tokens ascending.  *pairs receives the
+ * pair count; with hq and hs NULL only the count is returned. */
+int frc_debug_prefill_hidden(frc_context *c, int8_t *hq, float *hs, size_t cap, size_t *pairs);
 /* Hidden activations h of the last frc_run, in item order
  * [unique expert][loaded block][token][32] (zero where the token does not use
  * the expert); *count receives the number of floats. */

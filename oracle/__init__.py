@@ -50,6 +50,8 @@ class Oracle:
             "or_legacy_layer_bytes": (ctypes.c_size_t, [ctypes.c_uint]),
             "or_ref_run": (ctypes.c_int, [_vp, ctypes.c_uint, _vp, _vp, _vp, _vp, ctypes.c_int]),
             "or_port_run": (ctypes.c_int, [_vp, ctypes.c_uint, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+            "or_prefill_run": (ctypes.c_int, [_vp, ctypes.c_uint, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t,
+                                              _vp]),
             "or_block_idots": (ctypes.c_int, [_vp, ctypes.c_uint, ctypes.c_uint, _vp, _vp]),
             "or_compare": (ctypes.c_int, [_vp, _vp, ctypes.c_size_t, _vp]),
         }
@@ -130,6 +132,24 @@ class Oracle:
         else:
             rc = self.L.or_port_run(ctypes.byref(m), x.shape[0], _p(e), _p(g), _p(x), _p(y), None, 0, None)
         return rc, y, h
+
+    def prefill_run(self, m, expert, gate, x, want_hidden=False):
+        """The CUDA prefill arithmetic: (rc, y, hq [pair][block][32] | None, hs [pair][block] | None)."""
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.zeros_like(x)
+        e = np.ascontiguousarray(expert, np.uint16)
+        g = np.ascontiguousarray(gate, np.float32)
+        if not want_hidden:
+            return self.L.or_prefill_run(ctypes.byref(m), x.shape[0], _p(e), _p(g), _p(x), _p(y), None, None, 0,
+                                         None), y, None, None
+        S = sum(1 for p in m.layer if p)
+        cap = x.shape[0] * 10
+        hq = np.zeros((cap, S, 32), np.int8)
+        hs = np.zeros((cap, S), np.float32)
+        n = ctypes.c_size_t()
+        rc = self.L.or_prefill_run(ctypes.byref(m), x.shape[0], _p(e), _p(g), _p(x), _p(y), _p(hq), _p(hs), cap,
+                                   ctypes.byref(n))
+        return rc, y, hq[:n.value], hs[:n.value]
 
 
 # ------------------------------------------------------- compiled reference

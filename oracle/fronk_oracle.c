@@ -208,8 +208,9 @@ static int narrow(double v, float *out) {
 }
 
 /* backends/ref.c:41-56 (token count bounded by OR_MAX_TOKENS instead of 8). */
-static int validate(unsigned hidden, unsigned tokens, const uint16_t *expert, const float *gate, const float *x) {
-    if (!expert || !gate || !x || tokens < 1 || tokens > OR_MAX_TOKENS || fegetround() != FE_TONEAREST)
+static int validate_n(unsigned hidden, unsigned tokens, unsigned max_tokens, const uint16_t *expert,
+                      const float *gate, const float *x) {
+    if (!expert || !gate || !x || tokens < 1 || tokens > max_tokens || fegetround() != FE_TONEAREST)
         return OR_INVALID;
     for (unsigned t = 0; t < tokens; ++t) {
         const uint16_t *id = expert + (size_t)t * OR_TOPK;
@@ -225,6 +226,9 @@ static int validate(unsigned hidden, unsigned tokens, const uint16_t *expert, co
         for (unsigned j = 0; j < hidden; ++j) if (!isfinite(x[(size_t)t * hidden + j])) return OR_NUMERIC;
     }
     return OR_OK;
+}
+static int validate(unsigned hidden, unsigned tokens, const uint16_t *expert, const float *gate, const float *x) {
+    return validate_n(hidden, tokens, OR_MAX_TOKENS, expert, gate, x);
 }
 
 static int model_ok(const or_model *m) {
@@ -550,6 +554,133 @@ int or_port_run(const or_model *m, unsigned tokens, const uint16_t *expert, cons
     memcpy(y, out, (size_t)tokens * d * sizeof(float));
 done:
     free(part);
+    return rc;
+}
+
+/* ------------------------------------------------- GPU prefill arithmetic */
+
+/* The batched (prefill) path of the CUDA backend, for bursts of up to
+ * OR_MAX_PREFILL tokens with MXFP4 gate/up rows, MXFP4 or Q8_0 down rows and
+ * no shared expert (the backend runs other requests through the decode
+ * arithmetic, or_port_run, in bursts of 16).  Each token's result depends only
+ * on its own row:
+ *   x: per-64 Q8 quantization (src/q4.c:37-61), as or_port_run;
+ *   gate/up dot of neuron n: over the row's 32-weight blocks b in order,
+ *     acc = fmaf((float)I_b * xscale[b / 2], wscale_b, acc), I_b the exact
+ *     integer block dot (the tensor cores' int32 result);
+ *   h = SwiGLU in double (backends/ref.c:81-83), Q8 per 32 (hq, hscale);
+ *   expert partial row r: over the loaded blocks s in ascending order,
+ *     acc = fmaf((float)I_{s,r} * hscale_s, wscale_{s,r}, acc);
+ *   y[t][r]: over the token's ten routed experts in request order,
+ *     acc = fmaf(gate, partial, acc).
+ * Pairs (expert, token) are numbered expert-major, tokens ascending;
+ * hq [pair][block][32] and hs [pair][block] receive the hidden values when not
+ * NULL (*pairs gets the pair count). */
+static int validate_n(unsigned hidden, unsigned tokens, unsigned max_tokens, const uint16_t *expert,
+                      const float *gate, const float *x);
+
+int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, const float *gate,
+                   const float *x, float *y, int8_t *hq, float *hs, size_t pair_cap, size_t *pairs) {
+    if (!model_ok(m) || m->legacy || !y || m->gate_type != OR_MXFP4) return OR_INVALID;
+    const unsigned d = m->hidden;
+    if (d % 512 || d > 8192) return OR_INVALID;
+    int rc = validate_n(d, tokens, OR_MAX_PREFILL, expert, gate, x);
+    if (rc) return rc;
+    for (unsigned t = 0; t < tokens; ++t)
+        if (gate[(size_t)t * OR_ACTIVE + OR_TOPK] != 0) return OR_INVALID;
+    if (!any_loaded(m)) return OR_STATE;
+    unsigned blocks[OR_BLOCKS], S = 0;
+    for (unsigned b = 0; b < OR_BLOCKS; ++b) if (m->layer[b]) blocks[S++] = b;
+    const unsigned dt = m->down_type, nb = d / 32;
+    const size_t slice = or_slice_bytes(d, m->gate_type, dt), in_row = or_row_bytes(OR_MXFP4, d);
+    const size_t proj = OR_NEURONS * in_row, down_row = or_row_bytes(dt, OR_NEURONS);
+
+    /* pairs, expert-major */
+    unsigned *pair_t = malloc(sizeof(unsigned) * tokens * OR_TOPK), *pair_e = malloc(sizeof(unsigned) * tokens * OR_TOPK);
+    unsigned *slot_pair = malloc(sizeof(unsigned) * tokens * OR_TOPK);
+    int8_t *q = malloc((size_t)tokens * d), *hv = malloc((size_t)tokens * OR_TOPK * S * OR_NEURONS);
+    float *xsc = malloc(sizeof(float) * tokens * (d / 64)), *hsc = malloc(sizeof(float) * tokens * OR_TOPK * S);
+    float *part = malloc(sizeof(float) * (size_t)tokens * OR_TOPK * d), *out = malloc(sizeof(float) * (size_t)tokens * d);
+    rc = OR_INVALID;
+    if (!pair_t || !pair_e || !slot_pair || !q || !hv || !xsc || !hsc || !part || !out) goto done;
+    unsigned P = 0;
+    for (unsigned e = 0; e < OR_ROUTED; ++e)
+        for (unsigned t = 0; t < tokens; ++t)
+            for (unsigned j = 0; j < OR_TOPK; ++j)
+                if (expert[(size_t)t * OR_TOPK + j] == e) {
+                    pair_t[P] = t; pair_e[P] = e; slot_pair[t * OR_TOPK + j] = P; ++P;
+                }
+    if (pairs) *pairs = P;
+    if ((hq || hs) && pair_cap < P) goto done;
+    for (unsigned t = 0; t < tokens; ++t) {
+        rc = or_q8_quantize(x + (size_t)t * d, d, q + (size_t)t * d, xsc + (size_t)t * (d / 64));
+        if (rc) goto done;
+    }
+    /* Every referenced block scale must be finite, whatever the gate. */
+    rc = OR_NUMERIC;
+    for (unsigned p = 0; p < P; ++p)
+        for (unsigned si = 0; si < S; ++si) {
+            const uint8_t *sl = m->layer[blocks[si]] + (size_t)pair_e[p] * slice;
+            float sc;
+            for (unsigned n = 0; n < 2 * OR_NEURONS; ++n)
+                for (unsigned b = 0; b < nb; ++b)
+                    if (!block_scale(sl + n * in_row, OR_MXFP4, b, &sc)) goto done;
+            for (unsigned r = 0; r < d; ++r)
+                if (!block_scale(sl + 2 * proj + r * down_row, dt, 0, &sc)) goto done;
+        }
+    for (unsigned p = 0; p < P; ++p) {
+        const unsigned t = pair_t[p];
+        const int8_t *qt = q + (size_t)t * d;
+        const float *xs = xsc + (size_t)t * (d / 64);
+        for (unsigned si = 0; si < S; ++si) {
+            const uint8_t *sl = m->layer[blocks[si]] + (size_t)pair_e[p] * slice;
+            float h[OR_NEURONS];
+            for (unsigned n = 0; n < OR_NEURONS; ++n) {
+                float gu[2];
+                for (unsigned w = 0; w < 2; ++w) {
+                    const uint8_t *row = sl + (w ? proj : 0) + n * in_row;
+                    float acc = 0, ws;
+                    for (unsigned b = 0; b < nb; ++b) {
+                        block_scale(row, OR_MXFP4, b, &ws);
+                        const float term = (float)idot_block(row, OR_MXFP4, b, qt + 32 * b) * xs[b / 2];
+                        acc = fmaf(term, ws, acc);
+                    }
+                    gu[w] = acc;
+                }
+                if (!isfinite(gu[0]) || !isfinite(gu[1])) goto done;
+                const double a = gu[0];
+                const double sig = a >= 0 ? 1 / (1 + exp(-a)) : exp(a) / (1 + exp(a));
+                if (narrow(a * sig * gu[1], &h[n])) goto done;
+            }
+            int8_t *hp = hv + ((size_t)p * S + si) * OR_NEURONS;
+            if (or_q8_quantize(h, OR_NEURONS, hp, hsc + (size_t)p * S + si)) goto done;
+        }
+        for (unsigned r = 0; r < d; ++r) {
+            float acc = 0;
+            for (unsigned si = 0; si < S; ++si) {
+                const uint8_t *down = m->layer[blocks[si]] + (size_t)pair_e[p] * slice + 2 * proj;
+                float ws;
+                block_scale(down + r * down_row, dt, 0, &ws);
+                const int32_t I = idot_block(down + r * down_row, dt, 0, hv + ((size_t)p * S + si) * OR_NEURONS);
+                acc = fmaf((float)I * hsc[(size_t)p * S + si], ws, acc);
+            }
+            part[(size_t)p * d + r] = acc;
+        }
+    }
+    for (unsigned t = 0; t < tokens; ++t)
+        for (unsigned r = 0; r < d; ++r) {
+            float acc = 0;
+            for (unsigned j = 0; j < OR_TOPK; ++j)
+                acc = fmaf(gate[(size_t)t * OR_ACTIVE + j], part[(size_t)slot_pair[t * OR_TOPK + j] * d + r], acc);
+            if (!isfinite(acc)) goto done;
+            out[(size_t)t * d + r] = acc;
+        }
+    if (hq) memcpy(hq, hv, (size_t)P * S * OR_NEURONS);
+    if (hs) memcpy(hs, hsc, sizeof(float) * P * S);
+    memcpy(y, out, sizeof(float) * (size_t)tokens * d);
+    rc = OR_OK;
+done:
+    free(pair_t); free(pair_e); free(slot_pair); free(q); free(hv); free(xsc); free(hsc); free(part); free(out);
     return rc;
 }
 

@@ -22,7 +22,7 @@
 enum { OR_OK = 0, OR_INVALID = -1, OR_STATE = -2, OR_NUMERIC = -3 };
 enum { OR_Q4_0 = 2, OR_Q8_0 = 8, OR_Q4_K = 12, OR_MXFP4 = 39 };
 enum { OR_BLOCKS = 20, OR_ROUTED = 512, OR_SHARED = 512, OR_TOPK = 10, OR_ACTIVE = 11,
-       OR_NEURONS = 32, OR_MAX_TOKENS = 16 };
+       OR_NEURONS = 32, OR_MAX_TOKENS = 16, OR_MAX_PREFILL = 512 };
 
 /* One layer of every loaded block.  layer[b] points at the first byte of the
  * requested layer inside unit b (NULL: block b not loaded).  Native layout:
@@ -66,6 +66,13 @@ int or_ref_run(const or_model *m, unsigned tokens, const uint16_t *expert, const
  * expert), at most h_cap floats; *h_count gets the size. */
 int or_port_run(const or_model *m, unsigned tokens, const uint16_t *expert, const float *gate,
                 const float *x, float *y, float *h, size_t h_cap, size_t *h_count);
+
+/* The CUDA prefill path's arithmetic (bursts of up to OR_MAX_PREFILL tokens,
+ * MXFP4 gate/up, MXFP4 or Q8_0 down, no shared expert): see fronk_oracle.c.
+ * hq [pair][loaded block][32] / hs [pair][loaded block] (pairs expert-major,
+ * tokens ascending) receive the quantized hidden values when not NULL. */
+int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, const float *gate,
+                   const float *x, float *y, int8_t *hq, float *hs, size_t pair_cap, size_t *pairs);
 
 /* Integer dot products of one row of n weights against int8 activations, one
  * per 32-weight block: Q4_K sum(q*v) with the unsigned nibble q (the sub-block

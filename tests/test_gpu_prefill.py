@@ -1,0 +1,106 @@
+"""Bursts above 16 tokens: the tensor-core prefill path (MXFP4 weights, Q8
+activations) against the oracle's restatement of its arithmetic
+(or_prefill_run), through the C ABI; and the bursts that run as 16-token
+chunks of the decode kernel."""
+import numpy as np
+import pytest
+
+import fronk_b200 as fb
+from oracle import Oracle, MXFP4, OK, INVALID, NUMERIC
+from tests.helpers import make_layers, request, rel_l2
+
+pytestmark = pytest.mark.gpu
+SEED = 0x5EED
+
+
+@pytest.fixture(scope="module")
+def oracle():
+    return Oracle()
+
+
+def _setup(ctx, oracle, blocks, e, hidden=2048):
+    g = fb.geometry(hidden, gate_type=MXFP4, down_type=MXFP4)
+    layers = make_layers(g, SEED, blocks, e, shared=True)
+    for b, arr in layers.items():
+        assert ctx.load_layer(b, 0, arr) == OK, ctx.last_error
+    return oracle.model(hidden, MXFP4, MXFP4, layers), layers
+
+
+@pytest.mark.parametrize("tokens,blocks", [(17, [0]), (40, [0, 3, 7]), (100, [1, 2, 5, 6, 9, 19])])
+def test_prefill_bitexact_with_oracle(gpu, oracle, tokens, blocks):
+    """y, the int8 hidden values and their scales, bit for bit (the kernel and
+    the oracle perform the same fp32 operations in the same order)."""
+    e, gt, x = request(2048, tokens, SEED + tokens)
+    with fb.Context(0, 2048, gate_type=MXFP4, down_type=MXFP4) as ctx:
+        m, layers = _setup(ctx, oracle, blocks, e)
+        rc, y = ctx.run(0, e, gt, x)
+        assert rc == OK, ctx.last_error
+        hq, hs = ctx.debug_prefill_hidden()
+    rc, y_ref, hq_ref, hs_ref = oracle.prefill_run(m, e, gt, x, want_hidden=True)
+    assert rc == OK
+    assert np.array_equal(hq, hq_ref)
+    assert np.array_equal(hs.view(np.uint32), hs_ref.view(np.uint32))
+    assert max(rel_l2(y_ref[t], y[t]) for t in range(tokens)) <= 1e-5
+    assert np.array_equal(y.view(np.uint32), y_ref.view(np.uint32))
+
+
+def test_prefill_zipf_512_tokens_all_blocks(gpu, oracle):
+    """configs[4]'s shape: 512 tokens, Zipf(1.1) expert popularity, all 20
+    blocks (device-filled units).  Tokens are independent, so a sample of
+    them is checked against the oracle bit for bit."""
+    g = fb.geometry(2048, gate_type=MXFP4, down_type=MXFP4)
+    e, gt, x = fb.synth_request(2048, 512, SEED + 512, zipf=1.1)
+    pool = np.concatenate([fb.synth_slice(g, SEED, i) for i in range(16)])
+    sb = fb.slice_bytes(g)
+    with fb.Context(0, 2048, gate_type=MXFP4, down_type=MXFP4) as ctx:
+        ctx.pool_load(pool, fb.synth_shared(g, SEED, 1 << 20))
+        for b in range(20):
+            ctx.fill_layer(b, 0, SEED)
+        rc, y = ctx.run(0, e, gt, x)
+        assert rc == OK, ctx.last_error
+        rc2, y2 = ctx.run(0, e, gt, x)
+        assert rc2 == OK and np.array_equal(y.view(np.uint32), y2.view(np.uint32))  # repeatable
+    sample = [0, 1, 77, 255, 400, 511]
+    layers = {}
+    for b in range(20):
+        arr = np.zeros(fb.layer_bytes(g), np.uint8)
+        for ident in set(int(v) for v in e[sample].ravel()):
+            k = fb.pool_pick(SEED, b, 0, ident, 16)
+            arr[ident * sb:(ident + 1) * sb] = pool[k * sb:(k + 1) * sb]
+        layers[b] = arr
+    m = oracle.model(2048, MXFP4, MXFP4, layers)
+    rc, y_ref, _, _ = oracle.prefill_run(m, e[sample], gt[sample], x[sample])
+    assert rc == OK
+    assert np.array_equal(y[sample].view(np.uint32), y_ref.view(np.uint32))
+
+
+def test_long_bursts_with_a_shared_expert_run_in_chunks(gpu, oracle):
+    """A nonzero shared-expert gate sends a long host burst through the decode
+    kernel, 16 tokens at a time: each chunk matches the decode arithmetic."""
+    e, gt, x = request(2048, 36, SEED + 36, shared_gate=0.3)
+    with fb.Context(0, 2048, gate_type=MXFP4, down_type=MXFP4) as ctx:
+        m, layers = _setup(ctx, oracle, [2, 4], e)
+        rc, y = ctx.run(0, e, gt, x)
+        assert rc == OK, ctx.last_error
+    for t0 in range(0, 36, 16):
+        sl = slice(t0, min(36, t0 + 16))
+        rc, y_ref, _ = oracle.port_run(m, e[sl], gt[sl], x[sl])
+        assert rc == OK
+        assert max(rel_l2(y_ref[t], y[sl][t]) for t in range(y_ref.shape[0])) <= 1e-5
+
+
+def test_prefill_failures_leave_output_untouched(gpu, oracle):
+    e, gt, x = request(2048, 24, SEED + 24)
+    g = fb.geometry(2048, gate_type=MXFP4, down_type=MXFP4)
+    sentinel = np.full(x.shape, 7.0, np.float32)
+    bad = make_layers(g, SEED, [3], e, shared=True)[3]
+    # E8M0 exponent 255: block 3 of up row 8 of a referenced slice (17-byte blocks, scale first)
+    bad[int(e[5, 2]) * fb.slice_bytes(g) + 40 * fb.row_bytes(MXFP4, 2048) + 3 * 17] = 255
+    with fb.Context(0, 2048, gate_type=MXFP4, down_type=MXFP4) as ctx:
+        assert ctx.load_layer(3, 0, bad) == OK
+        rc, y = ctx.run(0, e, gt, x, out=sentinel.copy())
+        assert rc == NUMERIC and np.array_equal(y, sentinel)
+        e2 = e.copy()
+        e2[7, 3] = e2[7, 4]  # the same expert twice in one token
+        rc, y = ctx.run(0, e2, gt, x, out=sentinel.copy())
+        assert rc == INVALID and np.array_equal(y, sentinel)
