@@ -14,7 +14,11 @@ the whole job (every GPU works on the same token: strong scaling).
 with its own seeded top-10 routing per layer; one launch per layer serves the
 union of their experts.  value = T x steps/s.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl ours|reference]
+--prefill: one MoE layer for 512 tokens with Zipf(1.1)
+expert popularity, MXFP4 gate/up/down, on the tensor-core prefill path
+(tcgen05 kind::i8 grouped GEMMs); value = prefill tokens/s.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T | --prefill] [--impl ours|reference]
 """
 import argparse
 import json
@@ -54,7 +58,8 @@ def log(*a):
 
 
 def emit(line):
-    print(json.dumps(line), file=_out, flush=True)
+    # numpy scalars print as plain numbers
+    print(json.dumps(line, default=lambda o: o.item() if hasattr(o, "item") else str(o)), file=_out, flush=True)
 
 
 def peaks():
@@ -161,6 +166,18 @@ def cpu_baseline(steps, warmup, tokens=1):
 def run_reference(args, rank):
     if rank != 0:
         return
+    if args.prefill:
+        steps, warm = max(1, min(args.steps, 5)), 1
+        cb = prefill_cpu_baseline(steps, warm)
+        if "unavailable" in cb:
+            emit({"impl": "reference", "unavailable": cb["unavailable"]})
+            return
+        emit({"impl": "reference", "metric": PF_METRIC, "value": cb["value"], "unit": "tokens/s",
+              "n_gpus": args.gpus, "steps": steps, "warmup": warm, "ms_per_step": cb["ms_per_pass"],
+              "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+              "data": "synthetic", "config": prefill_config(args.gpus), "cpu_baseline": cb,
+              "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+        return
     steps = max(1, min(args.steps, 50 if args.tokens == 1 else 3))
     warm = max(1, min(args.warmup, 3 if args.tokens == 1 else 1))
     cb = cpu_baseline(steps, warm, args.tokens)
@@ -200,11 +217,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--tokens", type=int, default=1, choices=range(1, 17), metavar="T",
                     help="concurrent tokens per step (1: configs[2], the headline; 16: configs[3])")
+    ap.add_argument("--prefill", action="store_true",
+                    help="configs[4]: one layer, 512 tokens, Zipf(1.1) routing, MXFP4, tensor-core prefill path")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--reduce", default="peer", choices=["peer", "nccl"],
                     help="per-layer sum of the GPUs' partials: in-kernel over NVLink peer memory, or NCCL all-reduce")
     ap.add_argument("--profile", action="store_true",
-                    help="small case for ncu: 2 layers of every slice loaded (2.2 GB), 5 layer launches")
+                    help="small case for ncu: 2 layers of every slice loaded (2.2 GB), 5 layer launches "
+                         "(with --prefill: one layer, three 512-token calls)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -217,10 +237,16 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank)
         return
+    if args.profile and args.prefill:
+        prefill_profile_case()
+        return
     if args.profile:
         profile_case()
         return
     args.warmup = max(args.warmup, 3)
+    if args.prefill:
+        run_prefill_bench(args, rank, world, local)
+        return
 
     import torch
     import fronk_b200 as fb
@@ -515,6 +541,294 @@ def profile_case():
         raise fb.FrcError(rc, "profile case", ctx.last_error)
     ctx.close()
     print("profile case ok")
+
+
+# ---------------------------------------------------------------- prefill
+
+PF_TOKENS, PF_ZIPF, PF_SETS = 512, 1.1, 8
+PF_METRIC = "MoE prefill tokens/s (one layer, 512 tokens) at 1/2/4/8 B200; expert-weight GB/s vs HBM peak"
+PF_GU_BYTES = 2 * 32 * (HIDDEN * 17 // 32)       # 69,632: MXFP4 gate + up rows of one slice
+PF_DN_BYTES = HIDDEN * 17                        # 34,816: MXFP4 down rows of one slice
+PF_SLICE_BYTES = PF_GU_BYTES + PF_DN_BYTES       # 104,448
+
+
+def prefill_config(n, unique=None):
+    from fronk_b200.planner import equal_shares
+    cfg = {"workload": "prefill512 (BASELINE configs[4]): one MoE layer, 512 tokens x d=2048, top-10 of 512 experts "
+                       "with Zipf(1.1) popularity (seeded), MXFP4 gate/up/down, 20 slices split over the GPUs, "
+                       "tcgen05 kind::i8 grouped GEMMs, partial sum by NCCL all-reduce at N>1",
+           "hidden": HIDDEN, "layers": 1, "tokens_per_step": PF_TOKENS, "experts": 512, "top_k": TOPK,
+           "zipf": PF_ZIPF, "slices": SLICES, "shares": equal_shares(n), "formats": "MXFP4 gate/up/down",
+           "activations": "Q8 per 64 (src/q4.c scheme), int8 tensor-core dots, fp32 scale application",
+           "routing_sets": PF_SETS,
+           "parallelism": "slice-split x%d, NCCL all-reduce of the 512 x 2048 partial" % n if n > 1 else "1 GPU, all slices"}
+    if unique is not None:
+        cfg["unique_experts"] = unique
+        cfg["weight_bytes_per_step"] = int(unique * SLICES * PF_SLICE_BYTES)
+        cfg["l2"] = "inputs larger than L2: %.2f GB of expert weights per step" % (unique * SLICES * PF_SLICE_BYTES / 1e9)
+    return cfg
+
+
+def prefill_cpu_baseline(steps, warmup):
+    """The reference's AVX2 backend on the same routing (512 tokens in bursts
+    of 8, Zipf 1.1), one layer of all 20 slices.  The reference's unit layout
+    fixes routed gate/up rows to Q4_K (src/native.h:1-3), so it runs the same
+    routing and shapes with Q4_K gate/up instead of MXFP4 (1,152 vs 1,088
+    bytes a row)."""
+    exe = os.path.join(ROOT, "oracle", "_ref", "ref_bench_2048")
+    if not os.path.exists(exe):
+        return {"unavailable": "reference not compiled (oracle/_ref/ref_bench_2048 missing)"}
+    t0 = time.time()
+    out = subprocess.run([exe, "avx2", str(SLICES), str(POOL), str(steps), str(warmup), str(SEED), str(PF_TOKENS),
+                          str(PF_ZIPF), "1"], capture_output=True, text=True, timeout=1800)
+    if out.returncode:
+        return {"unavailable": "ref_bench failed: " + out.stderr.strip()[-200:]}
+    r = json.loads(out.stdout.strip().splitlines()[-1])
+    return {"value": PF_TOKENS * 1e9 / r["ns_per_pass_mean"], "unit": "tokens/s", "cores": r["workers"],
+            "kind": "reference",
+            "sample": "reference backends/avx2.c (fr_avx2.run), one layer of all 20 slices, 512 tokens with Zipf(1.1) "
+                      "routing in bursts of 8, %d timed passes after %d warm-up, d=2048 build, Q4_K gate/up (the "
+                      "reference's routed layout; no MXFP4 gate/up backend)" % (steps, warmup),
+            "host": {"cpu": r["cpu"], "cores": r["cores"], "logical_cores": r["logical_cores"]},
+            "ms_per_pass": r["ns_per_pass_mean"] / 1e6, "wall_s": round(time.time() - t0, 1)}
+
+
+def run_prefill_bench(args, rank, world, local):
+    import torch
+    import fronk_b200 as fb
+    from fronk_b200.planner import owned_blocks
+    from fronk_b200 import build as fbuild
+    fbuild.build()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    blocks = owned_blocks(rank, world)
+    MX = fb.MXFP4
+    g = fb.geometry(HIDDEN, 1, MX, MX)
+    ctx = fb.Context(local, HIDDEN, layers=1, gate_type=MX, down_type=MX)
+    pool = np.concatenate([fb.synth_slice(g, SEED, i) for i in range(POOL)])
+    ctx.pool_load(pool, fb.synth_shared(g, SEED, 1 << 20))
+    for b in blocks:
+        ctx.fill_layer(b, 0, SEED)
+    reqs = [fb.synth_request(HIDDEN, PF_TOKENS, fb.rand64(SEED, 7000 + i), zipf=PF_ZIPF) for i in range(PF_SETS)]
+    uniq = [len(np.unique(r[0])) for r in reqs]
+    d_ex = torch.from_numpy(np.stack([r[0] for r in reqs]).astype(np.int16)).to(dev)
+    d_gt = torch.from_numpy(np.stack([r[1] for r in reqs])).to(dev)
+    d_x = torch.from_numpy(np.stack([r[2] for r in reqs])).to(dev)
+    cur_ex = torch.empty_like(d_ex[0]); cur_gt = torch.empty_like(d_gt[0]); cur_x = torch.empty_like(d_x[0])
+    Y = torch.zeros((PF_TOKENS, HIDDEN), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def launch():
+        ctx.run_device(0, PF_TOKENS, cur_ex.data_ptr(), cur_gt.data_ptr(), cur_x.data_ptr(), None, None,
+                       Y.data_ptr(), fb.ACT_Q8, 0, torch.cuda.current_stream().cuda_stream)
+        if dist is not None:
+            dist.all_reduce(Y)
+
+    def load(s):
+        cur_ex.copy_(d_ex[s % PF_SETS], non_blocking=True)
+        cur_gt.copy_(d_gt[s % PF_SETS], non_blocking=True)
+        cur_x.copy_(d_x[s % PF_SETS], non_blocking=True)
+
+    load(0)
+    launch()
+    torch.cuda.synchronize()
+    rc = ctx.status(stream.cuda_stream)
+    if rc:
+        raise fb.FrcError(rc, "prefill warm-up", ctx.last_error)
+    graph = None
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            launch()
+    except Exception as exc:  # noqa: BLE001
+        log("graph capture failed, running eagerly:", exc)
+        graph = None
+
+    def step(s):
+        load(s)
+        if graph is not None:
+            graph.replay()
+        else:
+            launch()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for s in range(args.warmup, args.warmup + args.steps):
+        step(s)
+    end.record(stream)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = start.elapsed_time(end)
+    rc = ctx.status(stream.cuda_stream)
+    if rc:
+        raise fb.FrcError(rc, "timed prefill", ctx.last_error)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    tokens_s = PF_TOKENS * 1000.0 / ms_per_step
+    unique = float(np.mean([uniq[s % PF_SETS] for s in range(args.warmup, args.warmup + args.steps)]))
+
+    # per-kernel durations: events around each of the five launches, eager calls
+    ctx.prefill_timing(True)
+    stage = []
+    for s in range(2 * PF_SETS):
+        load(s)
+        ctx.run_device(0, PF_TOKENS, cur_ex.data_ptr(), cur_gt.data_ptr(), cur_x.data_ptr(), None, None,
+                       Y.data_ptr(), fb.ACT_Q8, 0, stream.cuda_stream)
+        stage.append(ctx.prefill_times())
+    ctx.prefill_timing(False)
+    stage = np.mean(np.stack(stage[2:]), axis=0)
+    names = ["quantize", "group", "gate/up MMA", "down MMA", "combine"]
+    u_all = float(np.mean(uniq))
+    gu_bytes = u_all * len(blocks) * PF_GU_BYTES
+    dn_bytes = u_all * len(blocks) * PF_DN_BYTES
+    peak, peak_src = peaks()
+    gu_gbs = gu_bytes / (stage[2] * 1e-3) / 1e9
+    dn_gbs = dn_bytes / (stage[3] * 1e-3) / 1e9
+
+    # end to end: host buffers through frc_run (N=1) / device call + all-reduce with pinned copies (N>1)
+    e2e_steps = max(3, min(args.steps, 20))
+    h2d = PF_TOKENS * (HIDDEN * 4 + TOPK * 2 + 11 * 4)
+    d2h = PF_TOKENS * HIDDEN * 4 + (16 if dist is None else 0)
+    if dist is None:
+        t0 = time.perf_counter()
+        for s in range(e2e_steps):
+            e, gt, x = reqs[s % PF_SETS]
+            rc, _ = ctx.run(0, e, gt, x)
+            if rc:
+                raise fb.FrcError(rc, "e2e prefill", ctx.last_error)
+        dt = time.perf_counter() - t0
+    else:
+        pin_x = torch.empty((PF_TOKENS, HIDDEN), dtype=torch.float32).pin_memory()
+        pin_e = torch.empty((PF_TOKENS, TOPK), dtype=torch.int16).pin_memory()
+        pin_g = torch.empty((PF_TOKENS, 11), dtype=torch.float32).pin_memory()
+        pin_y = torch.empty((PF_TOKENS, HIDDEN), dtype=torch.float32).pin_memory()
+        dist.barrier()
+        t0 = time.perf_counter()
+        for s in range(e2e_steps):
+            e, gt, x = reqs[s % PF_SETS]
+            pin_x.numpy()[:] = x
+            pin_e.numpy()[:] = e.astype(np.int16)
+            pin_g.numpy()[:] = gt
+            cur_x.copy_(pin_x, non_blocking=True)
+            cur_ex.copy_(pin_e, non_blocking=True)
+            cur_gt.copy_(pin_g, non_blocking=True)
+            launch()
+            pin_y.copy_(Y, non_blocking=True)
+            stream.synchronize()
+        dt = time.perf_counter() - t0
+        t = torch.tensor([dt], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    e2e = {"value": PF_TOKENS * e2e_steps / dt, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+           "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+           "api": "frc_run (host buffers, synchronous)" if dist is None else
+                  "frc_run_device + NCCL all_reduce, pinned host copies"}
+
+    # parity on a sample of tokens of the first routing set (tokens are independent)
+    parity = prefill_parity(ctx, fb, g, pool, blocks, reqs[0]) if rank == 0 else None
+    used_graph = graph is not None
+    del graph
+    if rank == 0:
+        line = {
+            "metric": PF_METRIC, "value": tokens_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": prefill_config(world, unique),
+            "weight_gbs": unique * SLICES * PF_SLICE_BYTES * 1e3 / ms_per_step / 1e9,
+            "roofline": {"bound": "hbm", "achieved": gu_gbs, "peak": peak, "unit": "GB/s", "frac": gu_gbs / peak,
+                         "traffic": None, "peak_source": peak_src,
+                         "kernel": "prefill_mma_kernel<gate/up> (tcgen05 kind::i8)",
+                         "algorithmic_bytes_per_launch": gu_bytes, "launch_us": float(stage[2] * 1e3),
+                         "launch_us_source": "CUDA events around the launch on its stream (eager calls)",
+                         "down_kernel": {"bytes": dn_bytes, "us": float(stage[3] * 1e3), "gbs": dn_gbs,
+                                         "frac": dn_gbs / peak},
+                         "stage_us": {n: float(v * 1e3) for n, v in zip(names, stage)}},
+            "gpu_launches": 5 * args.steps, "graph": used_graph, "clocks": clocks,
+            "e2e": e2e, "parity": parity,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = prefill_cpu_baseline(2, 1)
+        emit(line)
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def prefill_profile_case():
+    """The prefill path alone on its bench workload (one layer of all 20
+    slices, 1.07 GB on the device): three eager calls of 512 tokens."""
+    import torch
+    import fronk_b200 as fb
+    MX = fb.MXFP4
+    g = fb.geometry(HIDDEN, 1, MX, MX)
+    ctx = fb.Context(0, HIDDEN, layers=1, gate_type=MX, down_type=MX)
+    pool = np.concatenate([fb.synth_slice(g, SEED, i) for i in range(POOL)])
+    ctx.pool_load(pool, fb.synth_shared(g, SEED, 1 << 20))
+    for b in range(SLICES):
+        ctx.fill_layer(b, 0, SEED)
+    dev = torch.device("cuda", 0)
+    y = torch.zeros((PF_TOKENS, HIDDEN), device=dev)
+    s = torch.cuda.current_stream().cuda_stream
+    for i in range(3):
+        e, gt, x = fb.synth_request(HIDDEN, PF_TOKENS, fb.rand64(SEED, 7000 + i), zipf=PF_ZIPF)
+        de = torch.from_numpy(e.astype(np.int16)).to(dev)
+        dg = torch.from_numpy(gt).to(dev)
+        dx = torch.from_numpy(x).to(dev)
+        ctx.run_device(0, PF_TOKENS, de.data_ptr(), dg.data_ptr(), dx.data_ptr(), None, None, y.data_ptr(),
+                       fb.ACT_Q8, 0, s)
+        torch.cuda.synchronize()
+    rc = ctx.status(s)
+    if rc:
+        raise fb.FrcError(rc, "prefill profile case", ctx.last_error)
+    ctx.close()
+    print("prefill profile case ok")
+
+
+def prefill_parity(ctx, fb, g, pool, blocks, req):
+    try:
+        from oracle import Oracle
+    except Exception as exc:  # noqa: BLE001
+        return {"skipped": str(exc)}
+    e, gt, x = req
+    rc, y = ctx.run(0, e, gt, x)
+    if rc:
+        return {"error": ctx.last_error}
+    sample = [0, 5, 100, 300, 511]
+    sb = fb.slice_bytes(g)
+    layers = {}
+    for b in blocks:
+        arr = np.zeros(fb.layer_bytes(g), np.uint8)
+        for ident in set(int(v) for v in e[sample].ravel()):
+            k = fb.pool_pick(SEED, b, 0, ident, POOL)
+            arr[ident * sb:(ident + 1) * sb] = pool[k * sb:(k + 1) * sb]
+        layers[b] = arr
+    orc = Oracle()
+    m = orc.model(HIDDEN, fb.MXFP4, fb.MXFP4, layers)
+    rc, y_ref, _, _ = orc.prefill_run(m, e[sample], gt[sample], x[sample])
+    if rc:
+        return {"error": "oracle rc %d" % rc}
+    return {"tokens_checked": sample, "blocks": len(blocks), "bitexact": bool(np.array_equal(
+        y[sample].view(np.uint32), y_ref.view(np.uint32)))}
 
 
 def ncu_traffic():

@@ -90,6 +90,8 @@ _SIGS = {
     "frc_debug_hidden": (_int, [_vp, _vp, _sz, _vp]),
     "frc_debug_umma": (_int, [_vp, _u32, _u32, _vp, _vp, _vp]),
     "frc_debug_prefill_hidden": (_int, [_vp, _vp, _vp, _sz, _vp]),
+    "frc_prefill_timing": (_int, [_vp, _int]),
+    "frc_prefill_times": (_int, [_vp, _vp]),
     "frc_debug_phases": (_int, [_vp, _vp, _sz, _vp]),
 }
 EXPORTS = sorted(_SIGS) + ["fr_cuda", "fr_cuda_f32", "fr_cuda_select_device", "fr_cuda_close"]
@@ -342,6 +344,15 @@ class Context:
         d = np.zeros((128, b.shape[0]), np.int32)
         self._check(self.lib.frc_debug_umma(self.h, b.shape[0], a.shape[1], _ptr(a), _ptr(b), _ptr(d)), "debug_umma")
         return d
+
+    def prefill_timing(self, enable):
+        self._check(self.lib.frc_prefill_timing(self.h, 1 if enable else 0), "prefill_timing")
+
+    def prefill_times(self):
+        """ms of the last timed prefill call: quantize, group, gate/up MMA, down MMA, combine."""
+        ms = np.zeros(5, np.float32)
+        self._check(self.lib.frc_prefill_times(self.h, _ptr(ms)), "prefill_times")
+        return ms
 
     def debug_prefill_hidden(self):
         """(hq [pair][block][32] int8, hs [pair][block] f32) of the last prefill burst."""

@@ -15,7 +15,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_SOURCES = ["frc.cu"]
 C_SOURCES = ["frc_synth.c", "fr_cuda_backend.c", "frc_host.c"]
-DEPS = CUDA_SOURCES + C_SOURCES + ["frc_device.cuh", "frc_layer.cuh"]
+DEPS = sorted(f for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh", ".c", ".h")))  # every source and header
 
 
 def _run(cmd):

@@ -4,6 +4,8 @@
 // split, every CTA's weight bytes requested up front through a TMA ring,
 // integer block dots, a fixed reduction order and no float atomics (results
 // are bitwise repeatable).
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <fenv.h>
 #include <math.h>
@@ -222,6 +224,12 @@ struct frc_context {
   float* pf_ye = nullptr;
   bool pf_attr = false;
   unsigned last_pf_S = 0;
+  // tensor maps of the loaded layer regions (valid while tmap_of matches layer_ptr)
+  CUtensorMap tmap[FRC_MAX_BLOCKS][FRC_MAX_LAYERS];
+  const uint8_t* tmap_of[FRC_MAX_BLOCKS][FRC_MAX_LAYERS] = {};
+  // optional CUDA events around the five prefill launches (frc_prefill_timing)
+  cudaEvent_t pf_ev[6] = {};
+  bool pf_timing = false, pf_timed = false;
   char err[256] = {};
 };
 
@@ -459,6 +467,41 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
 // (frc_prefill.cuh; a nonzero shared-expert gate is rejected there);
 // otherwise it runs as bursts of FRC_MAX_TOKENS through the layer kernel
 // (`chunks` forces that).
+// The layer region of (block, layer) as a 2D byte array of row_bytes-long
+// rows (every slice of an MXFP4/MXFP4 layer is a whole number of them), for
+// 128-byte x 64-row tiled TMA boxes, 128-byte swizzle.  Encoded once per
+// region through the driver's cuTensorMapEncodeTiled.
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+static std::mutex g_encode_mu;
+
+static int layer_tmap(frc_context* c, unsigned b, unsigned layer, CUtensorMap* out) {
+  const uint8_t* base = c->layer_ptr[b][layer];
+  if (c->tmap_of[b][layer] != base) {
+    {
+      std::lock_guard<std::mutex> lock(g_encode_mu);
+      if (!g_encode_tiled) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn)
+          return fail(c, FRC_IO, "cuTensorMapEncodeTiled not available");
+        g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+      }
+    }
+    const cuuint64_t dims[2] = {c->row_bytes, c->layer_bytes / c->row_bytes};
+    const cuuint64_t strides[1] = {c->row_bytes};
+    const cuuint32_t box[2] = {128, 64}, estr[2] = {1, 1};
+    const CUresult r = g_encode_tiled(&c->tmap[b][layer], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base),
+                                      dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(c, FRC_IO, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    c->tmap_of[b][layer] = base;
+  }
+  *out = c->tmap[b][layer];
+  return FRC_OK;
+}
+
 static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_t* expert, const float* gate,
                        const float* x, float* y, cudaStream_t s) {
   PrefillArgs a{};
@@ -468,6 +511,8 @@ static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_
     for (unsigned l = 0; l < c->g.layers; ++l) any |= c->layer_ptr[b][l] != nullptr;
     if (!any) continue;
     if (!c->layer_ptr[b][layer]) return fail(c, FRC_STATE, "block %u is loaded but not layer %u", b, layer);
+    const int rc = layer_tmap(c, b, layer, &a.tmap[S]);
+    if (rc) return rc;
     a.base[S++] = c->layer_ptr[b][layer];
   }
   if (!S) return fail(c, FRC_STATE, "no block loaded");
@@ -476,9 +521,12 @@ static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_
   a.T = T; a.d = d; a.S = S;
   a.row_bytes = static_cast<unsigned>(c->row_bytes);
   a.slice_bytes = c->slice_bytes;
+  a.slice_rows = static_cast<unsigned>(c->slice_bytes / c->row_bytes);
   a.xq = c->pf_xq; a.xs = c->pf_xs; a.pair_token = c->pf_pair_token; a.slot_pair = c->pf_slot_pair;
   a.counts = c->pf_counts; a.items_gu = c->pf_items_gu; a.items_dn = c->pf_items_dn;
   a.hq = c->pf_hq; a.hs = c->pf_hs; a.ye = c->pf_ye; a.status = c->status;
+  a.phases = c->phases;
+  c->last_G = 4 * c->sms;  // frc_debug_phases: [cta][64] stamps
   const unsigned smem = sizeof(PfSmem);
   if (!c->pf_attr) {
     CK(cudaFuncSetAttribute(prefill_mma_kernel<kGateUp>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -486,11 +534,20 @@ static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_
     c->pf_attr = true;
   }
   const unsigned groups = T * (d / 64);
+  const bool timed = c->pf_timing;
+  auto mark = [&](unsigned i) { if (timed) cudaEventRecord(c->pf_ev[i], s); };
+  mark(0);
   prefill_quantize_kernel<<<(groups + 7) / 8, 256, 0, s>>>(a);
+  mark(1);
   prefill_group_kernel<<<1, 1024, 0, s>>>(a);
+  mark(2);
   prefill_mma_kernel<kGateUp><<<c->sms, kPfThreads, smem, s>>>(a);
+  mark(3);
   prefill_mma_kernel<kDown><<<c->sms, kPfThreads, smem, s>>>(a);
+  mark(4);
   prefill_combine_kernel<<<dim3(d / 256, T), 256, 0, s>>>(a);
+  mark(5);
+  c->pf_timed = timed;
   CK(cudaGetLastError());
   c->launches += 5;
   c->last_pf_S = S;
@@ -607,7 +664,8 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
   alloc(reinterpret_cast<void**>(&c->phases), sizeof(unsigned long long) * 16 * 1024);
   const size_t in_bytes = kInBytesPerToken(d) * FRC_MAX_PREFILL_TOKENS,
                out_bytes = 16 + sizeof(float) * FRC_MAX_PREFILL_TOKENS * d;
-  if (g->gate_type == FRC_MXFP4 && g->down_type == FRC_MXFP4) {
+  if (g->gate_type == FRC_MXFP4 && g->down_type == FRC_MXFP4 && c->slice_bytes % c->row_bytes == 0 &&
+      c->layer_bytes % c->row_bytes == 0) {
     const size_t T = FRC_MAX_PREFILL_TOKENS;
     alloc(reinterpret_cast<void**>(&c->pf_xq), T * d);
     alloc(reinterpret_cast<void**>(&c->pf_xs), sizeof(float) * T * (d / 64));
@@ -659,6 +717,7 @@ int frc_close(frc_context* c) {
   cudaFree(c->pf_items_gu); cudaFree(c->pf_items_dn); cudaFree(c->pf_hq); cudaFree(c->pf_hs); cudaFree(c->pf_ye);
   cudaFreeHost(c->h_in); cudaFreeHost(c->h_out);
   if (c->stream) cudaStreamDestroy(c->stream);
+  for (auto e : c->pf_ev) if (e) cudaEventDestroy(e);
   delete c;
   return FRC_OK;
 }
@@ -1004,6 +1063,23 @@ int frc_debug_umma(frc_context* c, unsigned n, unsigned k, const int8_t* a, cons
   CK(cudaMemcpy(d, dd, sizeof(int32_t) * 128 * n, cudaMemcpyDeviceToHost));
   cudaFree(da); cudaFree(db); cudaFree(dd);
   return st ? fail(c, FRC_IO, "umma check timed out") : FRC_OK;
+}
+
+int frc_prefill_timing(frc_context* c, int enable) {
+  if (!c) return FRC_INVALID;
+  CK(cudaSetDevice(c->device));
+  if (enable && !c->pf_ev[0])
+    for (auto& e : c->pf_ev) CK(cudaEventCreate(&e));
+  c->pf_timing = enable != 0;
+  return FRC_OK;
+}
+
+int frc_prefill_times(frc_context* c, float* ms) {
+  if (!c || !ms || !c->pf_timed) return fail(c, FRC_INVALID, "no timed prefill run");
+  CK(cudaSetDevice(c->device));
+  CK(cudaEventSynchronize(c->pf_ev[5]));
+  for (unsigned i = 0; i < 5; ++i) CK(cudaEventElapsedTime(&ms[i], c->pf_ev[i], c->pf_ev[i + 1]));
+  return FRC_OK;
 }
 
 int frc_debug_prefill_hidden(frc_context* c, int8_t* hq, float* hs, size_t cap, size_t* pairs) {

@@ -20,16 +20,18 @@
 //      request order of gate * partial, fmaf in fp32.
 // The arithmetic is restated step for step by the oracle's or_prefill_run.
 //
-// Inside an MMA kernel (one CTA per SM, 320 threads) warps have roles:
+// Inside an MMA kernel (one CTA per SM, 448 threads) warps have roles:
 //   warps 0-3 convert: raw MXFP4 payload (staged by TMA bulk copies) ->
 //     int8 A tiles in the K-major no-swizzle layout of frc_umma.cuh, and
 //     gather the B rows, row scales and column scales with cp.async;
-//   warps 4-7 are the epilogue (TMEM lanes 0-127 = A rows);
-//   warp 8 issues the bulk copies; warp 9 owns tensor memory and issues
+//   warps 4-11 are the epilogue, two warpgroups splitting the tile's token
+//     columns (TMEM lanes 0-127 = A rows);
+//   warp 12 issues the bulk copies; warp 13 owns tensor memory and issues
 //   the MMAs (one thread).
 // Rings: 4 raw stages, 2 A/B stages, 4 accumulator buffers of 64 columns.
 // Every wait gives up after 2 s (kStTimeout) so a fault cannot hang the GPU.
 #pragma once
+#include <cuda.h>
 
 namespace frc {
 
@@ -39,7 +41,7 @@ constexpr unsigned kPfRawBytes = 16384; // 128 rows x 128 B (gate/up) or 8 block
 constexpr unsigned kPfA = 128 * 256;    // A stage: 128 rows x K 256
 constexpr unsigned kPfB = kPfTile * 256;
 constexpr unsigned kPfAcc = 4;          // accumulator buffers
-constexpr unsigned kPfThreads = 320;
+constexpr unsigned kPfThreads = 448;     // 14 warps
 enum : unsigned { kGateUp = 0, kDown = 1 };
 
 struct PrefillArgs {
@@ -50,7 +52,11 @@ struct PrefillArgs {
   unsigned T, d, S;        // tokens, hidden size, loaded blocks
   unsigned row_bytes;      // MXFP4 gate/up row: d/32 scales + d/2 payload
   unsigned long long slice_bytes;
+  unsigned slice_rows;     // slice_bytes / row_bytes
   const uint8_t* base[kMaxBlocks];  // this layer of each loaded block, ascending
+  // the same layer regions as 2D byte arrays of row_bytes-long rows, for
+  // tiled TMA loads of 128-byte x 64-row boxes with the 128-byte swizzle
+  CUtensorMap tmap[kMaxBlocks];
   // scratch
   int8_t* xq;              // [T][d], prmt order per 32-block
   float* xs;               // [T][d/64]
@@ -63,7 +69,18 @@ struct PrefillArgs {
   float* hs;               // [P][S]
   float* ye;               // [P][d]
   unsigned* status;
+  unsigned long long* phases;  // FRC_PHASES builds: [cta][64] globaltimer stamps
 };
+
+// FRC_PHASES builds: stamps of each CTA's second gate/up item (0 entry; per chunk k:
+// 1+k converters ready, 9+k raw landed, 17+k A/B staged, 25+k MMA start,
+// 33+k MMAs issued, 41+k epilogue done, 50+k copies issued; 49 item done).
+#ifdef FRC_PHASES
+#define PF_STAMP(k, cond) \
+  do { if (MODE == kGateUp && (cond) && a.phases) a.phases[blockIdx.x * 64 + (k)] = globaltimer(); } while (0)
+#else
+#define PF_STAMP(k, cond) do { } while (0)
+#endif
 
 // ------------------------------------------------------------- helpers
 
@@ -92,7 +109,29 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier of one epilogue warpgroup (ids 1 and 2).
+__device__ __forceinline__ void epi_sync(unsigned wg) { asm volatile("bar.sync %0, 128;" ::"r"(wg + 1) : "memory"); }
+// Tiled 2D TMA load (no multicast): box at byte column x, row y of the map.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// SwiGLU of backends/ref.c:81-83 without branches: with e = exp(-|a|) the
+// stable sigmoid is 1/(1+e) for a >= 0 and e/(1+e) for a < 0, the same
+// double operations as swiglu() in frc_device.cuh.  `fail` on a nonfinite
+// or fp32-overflowing result.
+__device__ __forceinline__ float swiglu_nb(float a, float u, bool& fail) {
+  const double ad = a;
+  const double e = exp(-fabs(ad));
+  const double sig = (a >= 0 ? 1.0 : e) / (1.0 + e);
+  const double v = ad * sig * static_cast<double>(u);
+  fail = !(fabs(v) <= 3.4028234663852886e38);
+  return __double2float_rn(v);
+}
 
 // 16 payload bytes of one MXFP4 block (byte j: element j low nibble, element
 // j+16 high nibble) -> 32 int8 doubled E2M1 values in prmt order: for word m,
@@ -246,7 +285,7 @@ __device__ __forceinline__ void gu_row(unsigned m, unsigned pair, unsigned& blk,
 }
 
 template <unsigned MODE>
-__global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(PrefillArgs a) {
+__global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid_constant__ PrefillArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   PfSmem& s = *reinterpret_cast<PfSmem*>(smem_raw);
   const unsigned tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -258,13 +297,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(PrefillArgs 
   if (tid == 0) {
     for (unsigned i = 0; i < kPfRaw; ++i) { mbar_init(&s.raw_full[i], 1); mbar_init(&s.raw_empty[i], 128); }
     for (unsigned i = 0; i < 2; ++i) {
-      mbar_init(&s.ab_full[i], 128); mbar_init(&s.ab_empty[i], 1); mbar_init(&s.sc_empty[i], 4);
+      mbar_init(&s.ab_full[i], 128); mbar_init(&s.ab_empty[i], 1); mbar_init(&s.sc_empty[i], 8);
     }
-    for (unsigned i = 0; i < kPfAcc; ++i) { mbar_init(&s.acc_full[i], 1); mbar_init(&s.acc_empty[i], 4); }
+    for (unsigned i = 0; i < kPfAcc; ++i) { mbar_init(&s.acc_full[i], 1); mbar_init(&s.acc_empty[i], 8); }
     s.abort = 0;
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == 13) {
     tmem_alloc(&s.taddr, kPfAcc * kPfTile);
     tmem_relinquish();
   }
@@ -272,8 +311,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(PrefillArgs 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.taddr;
+  PF_STAMP(0, tid == 0);
 
-  if (warp == 8) {
+  if (warp == 12) {
     // ------------------------------------------------ producer: bulk copies
     unsigned c = 0;
     for (unsigned it = blockIdx.x; it < nitems && !*abort; it += gridDim.x) {
@@ -283,16 +323,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(PrefillArgs 
         if (!pf_wait_warp(&s.raw_empty[st], ((c / kPfRaw) & 1) ^ 1, abort)) break;
         uint8_t* dst = s.raw[st];
         if (MODE == kGateUp) {
-          const unsigned rows = 2 * item.w + 1 < a.S ? 128 : 64;
-          if (lane == 0) mbar_expect_tx(&s.raw_full[st], rows * 128);
-          __syncwarp();
-          for (unsigned m = lane; m < rows; m += 32) {
-            unsigned blk, hrow;
-            gu_row(m, item.w, blk, hrow);
-            const uint8_t* src = a.base[blk] + item.x * a.slice_bytes + static_cast<size_t>(hrow) * a.row_bytes + nb +
-                                 128 * k;
-            bulk_g2s(dst + 128 * m, src, 128, &s.raw_full[st]);
+          // one 128 B x 64-row box per slice: bytes [nb + 128k, +128) of its
+          // 32 gate and 32 up rows, stored 128-byte swizzled
+          const unsigned nsl = 2 * item.w + 1 < a.S ? 2 : 1;
+          if (lane == 0) {
+            mbar_expect_tx(&s.raw_full[st], nsl * 64 * 128);
+            for (unsigned sl = 0; sl < nsl; ++sl)
+              tma_load_2d(dst + 8192 * sl, &a.tmap[2 * item.w + sl], static_cast<int>(nb + 128 * k),
+                          static_cast<int>(item.x * a.slice_rows), &s.raw_full[st]);
           }
+          __syncwarp();
+          PF_STAMP(50 + k, lane == 0 && it == blockIdx.x + gridDim.x && k < 8);
         } else {
           const unsigned steps = pf_steps<MODE>(a, k);
           if (lane == 0) mbar_expect_tx(&s.raw_full[st], steps * 2048);
@@ -311,7 +352,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(PrefillArgs 
       if (lane == 0) pf_wait(&s.raw_full[last % kPfRaw], (last / kPfRaw) & 1, abort);
     }
     __syncwarp();
-  } else if (warp == 9) {
+  } else if (warp == 13) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       unsigned c = 0, q = 0;
@@ -322,18 +363,22 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(PrefillArgs 
         for (unsigned k = 0; k < nk && !*abort; ++k, ++c) {
           const unsigned ab = c & 1;
           if (!pf_wait(&s.ab_full[ab], (c >> 1) & 1, abort)) break;
+          PF_STAMP(25 + k, it == blockIdx.x + gridDim.x && k < 8);
           tc_fence_after();
           const uint32_t a0 = smem_u32(s.A[ab]), b0 = smem_u32(s.B[ab]);
           const unsigned steps = pf_steps<MODE>(a, k);
           for (unsigned st = 0; st < steps; ++st, ++q) {
             const unsigned buf = q % kPfAcc;
             if (!pf_wait(&s.acc_empty[buf], ((q / kPfAcc) & 1) ^ 1, abort)) break;
+            PF_STAMP(62, it == blockIdx.x + gridDim.x && k == 1 && st == 0);
             tc_fence_after();
             umma_i8(tmem + buf * kPfTile, umma_desc(a0 + 256 * st, 128, 8 * 256), umma_desc(b0 + 256 * st, 128, 8 * 256),
                     idesc, false);
             umma_commit(&s.acc_full[buf]);
+            PF_STAMP(63, it == blockIdx.x + gridDim.x && k == 1 && st == 0);
           }
           umma_commit(&s.ab_empty[ab]);
+          PF_STAMP(33 + k, it == blockIdx.x + gridDim.x && k < 8);
         }
       }
       // the last commit's arrive must land before the CTA exits
@@ -353,6 +398,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(PrefillArgs 
         const unsigned st = c % kPfRaw, ab = c & 1, steps = pf_steps<MODE>(a, k);
         if (!pf_wait(&s.ab_empty[ab], ((c >> 1) & 1) ^ 1, abort)) break;
         if (!pf_wait(&s.sc_empty[ab], ((c >> 1) & 1) ^ 1, abort)) break;
+        PF_STAMP(1 + k, tid == 0 && it == blockIdx.x + gridDim.x && k < 8);
         // B rows: the tile's tokens (gate/up: x of the token; down: hq of the pair)
         for (unsigned i = tid; i < item.z * 16; i += 128) {
           const unsigned j = i >> 4, piece = i & 15;
@@ -388,14 +434,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(PrefillArgs 
         cp_async_commit();
         // A: raw payload -> int8
         if (!pf_wait(&s.raw_full[st], (c / kPfRaw) & 1, abort)) break;
+        PF_STAMP(9 + k, tid == 0 && it == blockIdx.x + gridDim.x && k < 8);
         uint8_t* A = s.A[ab];
         if (MODE == kGateUp) {
           if (row_live) {
+            const unsigned R = 64 * (m >> 6) + hrow;  // row of the staged boxes
 #pragma unroll
-            for (unsigned i = 0; i < 8; ++i) {
-              const unsigned b = (i + m) & 7;  // rotated: conflict-free reads and writes
+            for (unsigned b = 0; b < 8; ++b) {
               uint4 lo, hi;
-              mxfp4_to_i8(*reinterpret_cast<const uint4*>(s.raw[st] + 128 * m + 16 * b), lo, hi);
+              // 128-byte swizzle: 16-byte chunk b of row R sits at chunk b ^ (R % 8)
+              mxfp4_to_i8(*reinterpret_cast<const uint4*>(s.raw[st] + 128 * R + 16 * (b ^ (R & 7))), lo, hi);
               *reinterpret_cast<uint4*>(A + umma_off(m, 32 * b, 256)) = lo;
               *reinterpret_cast<uint4*>(A + umma_off(m, 32 * b + 16, 256)) = hi;
             }
@@ -412,22 +460,25 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(PrefillArgs 
         cp_async_wait_all();
         fence_proxy_async();
         mbar_arrive(&s.ab_full[ab]);
+        PF_STAMP(17 + k, tid == 0 && it == blockIdx.x + gridDim.x && k < 8);
       }
     }
   } else {
-    // ------------------------------------------------ epilogue (warps 4-7)
-    const unsigned ew = warp - 4, m = 32 * ew + lane;
+    // ------------------------------------------------ epilogue (warps 4-11)
+    // Two warpgroups: warps 4-7 take tile columns 0-31, warps 8-11 columns
+    // 32-63; warp w reads TMEM lanes 32 (w % 4) .. +31 (A rows).
+    const unsigned wg = (warp - 4) >> 2, ew = warp & 3, m = 32 * ew + lane, col0 = 32 * wg;
     const uint32_t lane_base = tmem + ((32 * ew) << 16);
     unsigned c = 0, q = 0;
     bool bad = false;
-    // No abort test in these loops: the four warps must take the same number
-    // of epi_sync barriers; after an abort every wait fails at once.
+    // No abort test in these loops: the warps of a warpgroup must take the
+    // same number of epi_sync barriers; after an abort every wait fails at once.
     for (unsigned it = blockIdx.x; it < nitems; it += gridDim.x) {
       const uint4 item = items[it];
       const unsigned ntok = item.z;
-      float acc[kPfTile];
+      float acc[32];
 #pragma unroll
-      for (unsigned j = 0; j < kPfTile; ++j) acc[j] = 0.0f;
+      for (unsigned j = 0; j < 32; ++j) acc[j] = 0.0f;
       bool live = true;
       if (MODE == kGateUp) {
         unsigned blk, hrow;
@@ -442,78 +493,118 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(PrefillArgs 
         for (unsigned st = 0; st < steps; ++st, ++q) {
           const unsigned buf = q % kPfAcc;
           if (!pf_wait_warp(&s.acc_full[buf], (q / kPfAcc) & 1, abort)) continue;
+          PF_STAMP(58, tid == 128 && it == blockIdx.x + gridDim.x && k == 1 && st == 0);
           tc_fence_after();
-          uint32_t v[kPfTile];
+          uint32_t v[2][16];
 #pragma unroll
-          for (unsigned g = 0; g < kPfTile / 16; ++g)
-            if (16 * g < ntok) tmem_ld16(lane_base + buf * kPfTile + 16 * g, *reinterpret_cast<uint32_t(*)[16]>(v + 16 * g));
+          for (unsigned g = 0; g < 2; ++g)
+            if (col0 + 16 * g < ntok) tmem_ld16(lane_base + buf * kPfTile + col0 + 16 * g, v[g]);
           tmem_wait_ld();
+          PF_STAMP(60, tid == 128 && it == blockIdx.x + gridDim.x && k == 1 && st == 0);
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&s.acc_empty[buf]);
           const unsigned e8 = MODE == kGateUp ? (&s.rowscale[ab][0][0])[8 * m + st] : s.rowscale[ab][st][m];
           bad |= live && e8 == 255;
           const float ws = pow2_m128(e8);
-          const float* cs = s.colscale[ab][st];
+          const float4* cs = reinterpret_cast<const float4*>(s.colscale[ab][st] + col0);
+          // whole 16-column groups under a warp-uniform branch (columns past
+          // the tile's tokens compute harmless values that are never stored)
 #pragma unroll
-          for (unsigned j = 0; j < kPfTile; ++j)
-            if (j < ntok) acc[j] = __fmaf_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), cs[j]), ws, acc[j]);
+          for (unsigned g = 0; g < 2; ++g) {
+            if (col0 + 16 * g < ntok) {
+#pragma unroll
+              for (unsigned q4 = 0; q4 < 4; ++q4) {
+                const float4 cv = cs[4 * g + q4];
+                const unsigned j = 16 * g + 4 * q4;
+                const uint32_t* vj = &v[g][4 * q4];
+                acc[j] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(vj[0])), cv.x), ws, acc[j]);
+                acc[j + 1] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(vj[1])), cv.y), ws, acc[j + 1]);
+                acc[j + 2] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(vj[2])), cv.z), ws, acc[j + 2]);
+                acc[j + 3] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(vj[3])), cv.w), ws, acc[j + 3]);
+              }
+            }
+          }
+          PF_STAMP(59, tid == 128 && it == blockIdx.x + gridDim.x && k == 1 && st == 0);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.sc_empty[ab]);
+        PF_STAMP(41 + k, tid == 128 && it == blockIdx.x + gridDim.x && k < 8);
       }
       const bool ok = !*abort;
       if (MODE == kDown) {
         if (!ok) continue;
-        float* out = a.ye + static_cast<size_t>(item.y) * d + 128 * item.w + m;
+        float* out = a.ye + (static_cast<size_t>(item.y) + col0) * d + 128 * item.w + m;
 #pragma unroll
-        for (unsigned j = 0; j < kPfTile; ++j)
-          if (j < ntok) out[static_cast<size_t>(j) * d] = acc[j];
+        for (unsigned g = 0; g < 2; ++g)
+          if (col0 + 16 * g < ntok) {
+#pragma unroll
+            for (unsigned jj = 0; jj < 16; ++jj)
+              if (col0 + 16 * g + jj < ntok) out[static_cast<size_t>(16 * g + jj) * d] = acc[16 * g + jj];
+          }
       } else {
-        // SwiGLU: lane l < 16 (gate) takes tokens 0-31, lane l + 16 (up) tokens 32-63
+        // SwiGLU: lane l < 16 holds gate row n, lane l + 16 up row n; of this
+        // warpgroup's 32 tokens lane l takes the even ones col0 + 2i, lane
+        // l + 16 the odd ones col0 + 2i + 1.
         const bool up = lane >= 16;
-        float h[32];
+        const unsigned odd = up ? 1u : 0u;
+        float h[16];
 #pragma unroll
-        for (unsigned j = 0; j < 32; ++j) {
-          const float mine = up ? acc[j] : acc[j + 32];
-          const float other = __shfl_xor_sync(0xffffffffu, mine, 16);
-          const float g = up ? other : acc[j], u = up ? acc[j + 32] : other;
-          const unsigned t = j + (up ? 32 : 0);
-          h[j] = 0.0f;
-          if (t < ntok && live && !swiglu(g, u, &h[j])) bad = true;
+        for (unsigned g = 0; g < 2; ++g) {
+          if (col0 + 16 * g < ntok) {  // tokens col0 + 16g .. +15: warp-uniform
+#pragma unroll
+            for (unsigned i = 8 * g; i < 8 * g + 8; ++i) {
+              const float other = __shfl_xor_sync(0xffffffffu, up ? acc[2 * i] : acc[2 * i + 1], 16);
+              const float gv = up ? other : acc[2 * i], uv = up ? acc[2 * i + 1] : other;
+              bool fail = false;
+              h[i] = swiglu_nb(gv, uv, fail);
+              bad |= fail && live && col0 + 2 * i + odd < ntok;
+            }
+          }
         }
         // amax per token over the block's 32 neurons (16 here, 16 in the partner warp)
 #pragma unroll
-        for (unsigned j = 0; j < 32; ++j) {
-          float am = fabsf(h[j]);
+        for (unsigned g = 0; g < 2; ++g) {
+          if (col0 + 16 * g < ntok) {
 #pragma unroll
-          for (unsigned o = 8; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-          if ((lane & 15) == 0) s.amax[ew][j + (up ? 32 : 0)] = am;
+            for (unsigned i = 8 * g; i < 8 * g + 8; ++i) {
+              float am = fabsf(h[i]);
+#pragma unroll
+              for (unsigned o = 8; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+              if ((lane & 15) == 0) s.amax[ew][col0 + 2 * i + odd] = am;
+            }
+          }
         }
-        epi_sync();
+        epi_sync(wg);
         const unsigned blk = 2 * item.w + (ew >> 1), n = 16 * (ew & 1) + (lane & 15);
         if (live && ok) {
           int8_t* hq = a.hq + static_cast<size_t>(item.y) * a.S * 32 + blk * 32 + prmt_pos(n);
 #pragma unroll
-          for (unsigned j = 0; j < 32; ++j) {
-            const unsigned t = j + (up ? 32 : 0);
-            if (t < ntok) {
-              const float am = fmaxf(s.amax[ew][t], s.amax[ew ^ 1][t]);
-              const Q8Group qg(am);
-              hq[static_cast<size_t>(t) * a.S * 32] = static_cast<int8_t>(qg.q(h[j]));
-              if ((ew & 1) == 0 && (lane & 15) == 0) a.hs[static_cast<size_t>(item.y + t) * a.S + blk] = qg.scale;
+          for (unsigned g = 0; g < 2; ++g) {
+            if (col0 + 16 * g < ntok) {
+#pragma unroll
+              for (unsigned i = 8 * g; i < 8 * g + 8; ++i) {
+                const unsigned t = col0 + 2 * i + odd;
+                if (t < ntok) {
+                  const float am = fmaxf(s.amax[ew][t], s.amax[ew ^ 1][t]);
+                  const Q8Group qg(am);
+                  hq[static_cast<size_t>(t) * a.S * 32] = static_cast<int8_t>(qg.q(h[i]));
+                  if ((ew & 1) == 0 && (lane & 15) == 0) a.hs[static_cast<size_t>(item.y + t) * a.S + blk] = qg.scale;
+                }
+              }
             }
           }
         }
-        epi_sync();
+        epi_sync(wg);
       }
+      PF_STAMP(49, tid == 128 && it == blockIdx.x + gridDim.x);
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(a.status, kStNumeric);
   }
   if (tid == 0 && *abort) atomicOr(a.status, kStTimeout);
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) tmem_dealloc(tmem, kPfAcc * kPfTile);
+  if (warp == 13) tmem_dealloc(tmem, kPfAcc * kPfTile);
 }
 
 // ---------------------------------------------------------- 5. combine

@@ -222,6 +222,14 @@ int frc_debug_quantize(frc_context *c, unsigned tokens, const float *x, int8_t *
  * int32, row-major host arrays; n a multiple of 16 up to 256, k a multiple of
  * 32 up to 256. */
 int frc_debug_umma(frc_context *c, unsigned n, unsigned k, const int8_t *a, const int8_t *b, int32_t *d);
+/* Event timing of the prefill path (bursts above FRC_MAX_TOKENS on the
+ * tensor cores): while enabled, every prefill call records CUDA events on its
+ * stream around its five launches (quantize, group, gate/up MMA, down MMA,
+ * combine); frc_prefill_times waits for the last call's final event and
+ * writes the five durations in ms.  For measurement; leave it disabled in
+ * captured graphs. */
+int frc_prefill_timing(frc_context *c, int enable);
+int frc_prefill_times(frc_context *c, float *ms);
 /* Quantized hidden values of the last prefill burst (more than
  * FRC_MAX_TOKENS tokens on the tensor-core path): hq [pair][loaded block][32]
  * int8 in neuron order and hs [pair][loaded block] fp32 scales, pairs

@@ -9,7 +9,9 @@
  * sparse anonymous mappings of FR_NATIVE_BLOCK_BYTES (as src/native.c:66-75
  * does) holding pool slices in every slot the routing touches.
  *
- *   ref_bench BACKEND BLOCKS POOL STEPS WARMUP SEED [TOKENS]
+ *   ref_bench BACKEND BLOCKS POOL STEPS WARMUP SEED [TOKENS [ZIPF [LAYERS]]]
+ * ZIPF > 0 draws the routing with Zipf(ZIPF) expert popularity
+ * (frc_synth_request_zipf); LAYERS (default 48) shortens the pass.
  * prints one JSON line.
  */
 #define _GNU_SOURCE
@@ -36,16 +38,19 @@ static int cmp(const void *a, const void *b) {
 }
 
 int main(int argc, char **argv) {
-    if (argc != 7 && argc != 8) {
-        fputs("usage: ref_bench BACKEND BLOCKS POOL STEPS WARMUP SEED [TOKENS]\n", stderr);
+    if (argc < 7 || argc > 10) {
+        fputs("usage: ref_bench BACKEND BLOCKS POOL STEPS WARMUP SEED [TOKENS [ZIPF [LAYERS]]]\n", stderr);
         return 2;
     }
     const fr_backend *backend = fr_backend_find(argv[1]);
     unsigned blocks = (unsigned)atoi(argv[2]), pool_n = (unsigned)atoi(argv[3]);
     unsigned steps = (unsigned)atoi(argv[4]), warm = (unsigned)atoi(argv[5]);
     uint64_t seed = strtoull(argv[6], NULL, 0);
-    const unsigned T = argc == 8 ? (unsigned)atoi(argv[7]) : 1;
-    if (!backend || !blocks || blocks > FR_BLOCKS || !pool_n || !steps || !T || T > FRC_MAX_TOKENS) return 2;
+    const unsigned T = argc >= 8 ? (unsigned)atoi(argv[7]) : 1;
+    const double zipf = argc >= 9 ? atof(argv[8]) : 0.0;
+    const unsigned L = argc >= 10 ? (unsigned)atoi(argv[9]) : FR_LAYERS;
+    if (!L || L > FR_LAYERS) return 2;
+    if (!backend || !blocks || blocks > FR_BLOCKS || !pool_n || !steps || !T || T > FRC_MAX_PREFILL_TOKENS) return 2;
     const frc_geometry g = {FR_HIDDEN, FR_LAYERS, FRC_Q4_K, FRC_MXFP4};
     if (frc_slice_bytes(&g) != FR_NATIVE_SLICE_BYTES || frc_unit_bytes(&g) != FR_NATIVE_BLOCK_BYTES) {
         fputs("geometry mismatch\n", stderr);
@@ -57,16 +62,20 @@ int main(int argc, char **argv) {
     for (unsigned i = 0; i < pool_n; ++i) frc_synth_slice(&g, seed, i, pool + (size_t)i * FR_NATIVE_SLICE_BYTES);
     /* Routing for every step, layer and token; x only for layer 0 of each step. */
     const unsigned passes = warm + steps;
-    const size_t rows = (size_t)passes * FR_LAYERS * T;
+    const size_t rows = (size_t)passes * L * T;
     uint16_t *expert = malloc(sizeof(uint16_t) * rows * FR_ACTIVE_ROUTED);
     float *gate = malloc(sizeof(float) * rows * FR_ACTIVE_EXPERTS);
     float *x0 = malloc(sizeof(float) * passes * T * FR_HIDDEN), *tmp = malloc(sizeof(float) * T * FR_HIDDEN);
     for (unsigned s = 0; s < passes; ++s)
-        for (unsigned l = 0; l < FR_LAYERS; ++l) {
+        for (unsigned l = 0; l < L; ++l) {
             uint64_t rs = frc_rand64(seed, 1000003ull * s + l);
-            const size_t r = ((size_t)s * FR_LAYERS + l) * T;
-            frc_synth_request(FR_HIDDEN, T, rs, expert + r * FR_ACTIVE_ROUTED, gate + r * FR_ACTIVE_EXPERTS,
-                              l ? tmp : x0 + (size_t)s * T * FR_HIDDEN);
+            const size_t r = ((size_t)s * L + l) * T;
+            float *xo = l ? tmp : x0 + (size_t)s * T * FR_HIDDEN;
+            if (zipf > 0)
+                frc_synth_request_zipf(FR_HIDDEN, T, rs, zipf, expert + r * FR_ACTIVE_ROUTED,
+                                       gate + r * FR_ACTIVE_EXPERTS, xo);
+            else
+                frc_synth_request(FR_HIDDEN, T, rs, expert + r * FR_ACTIVE_ROUTED, gate + r * FR_ACTIVE_EXPERTS, xo);
         }
     unsigned char *unit[FR_BLOCKS] = {0};
     int rc = 0;
@@ -77,9 +86,9 @@ int main(int argc, char **argv) {
         if (unit[b] == MAP_FAILED) { unit[b] = NULL; rc = 1; break; }
         memset(filled, 0, sizeof filled);
         for (unsigned s = 0; s < passes; ++s)
-            for (unsigned l = 0; l < FR_LAYERS; ++l)
+            for (unsigned l = 0; l < L; ++l)
                 for (unsigned e = 0; e < T * FR_ACTIVE_ROUTED; ++e) {
-                    unsigned id = expert[((size_t)s * FR_LAYERS + l) * T * FR_ACTIVE_ROUTED + e];
+                    unsigned id = expert[((size_t)s * L + l) * T * FR_ACTIVE_ROUTED + e];
                     if (filled[l][id]) continue;
                     filled[l][id] = 1;
                     unsigned pick = frc_pool_pick(seed, b, l, id, pool_n);
@@ -109,8 +118,8 @@ int main(int argc, char **argv) {
     for (unsigned s = 0; s < passes && !rc; ++s) {
         memcpy(h, x0 + (size_t)s * T * FR_HIDDEN, sizeof(float) * T * FR_HIDDEN);
         double t0 = now();
-        for (unsigned l = 0; l < FR_LAYERS && !rc; ++l) {
-            const size_t r = ((size_t)s * FR_LAYERS + l) * T;
+        for (unsigned l = 0; l < L && !rc; ++l) {
+            const size_t r = ((size_t)s * L + l) * T;
             for (unsigned first = 0; first < T && !rc; first += FR_MAX_BURST) {
                 const unsigned n = T - first < FR_MAX_BURST ? T - first : FR_MAX_BURST;
                 for (unsigned k = 0; k < n; ++k) {
@@ -150,10 +159,10 @@ int main(int argc, char **argv) {
     fr_hwinfo hw;
     memset(&hw, 0, sizeof hw);
     hw_probe(&hw);
-    printf("{\"backend\": \"%s\", \"hidden\": %d, \"blocks\": %u, \"tokens\": %u, \"steps\": %u, \"warmup\": %u, "
+    printf("{\"backend\": \"%s\", \"hidden\": %d, \"blocks\": %u, \"tokens\": %u, \"layers\": %u, \"zipf\": %g, \"steps\": %u, \"warmup\": %u, "
            "\"ns_per_pass_mean\": %.1f, \"ns_per_pass_p50\": %.1f, \"workers\": %u, \"cores\": %u, "
            "\"logical_cores\": %u, \"cpu\": \"%s\", \"checksum\": %.9g}\n",
-           backend->name, FR_HIDDEN, blocks, T, steps, warm, total / steps, ns[steps / 2], workers, hw.cores,
+           backend->name, FR_HIDDEN, blocks, T, L, zipf, steps, warm, total / steps, ns[steps / 2], workers, hw.cores,
            hw.logical_cores, hw.cpu, checksum);
     for (unsigned b = 0; b < blocks; ++b) {
         backend->unload((int)b);
