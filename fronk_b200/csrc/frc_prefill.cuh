@@ -28,7 +28,9 @@
 //     columns (TMEM lanes 0-127 = A rows);
 //   warp 12 issues the bulk copies; warp 13 owns tensor memory and issues
 //   the MMAs (one thread).
-// Rings: 4 raw stages, 2 A/B stages, 4 accumulator buffers of 64 columns.
+// Rings: 4 raw stages, 2 A/B stages, 8 accumulator buffers of 64 columns
+// (all of tensor memory) used as two groups of four MMA steps, so that the
+// epilogue takes one barrier and several independent TMEM reads per group.
 // Every wait gives up after 2 s (kStTimeout) so a fault cannot hang the GPU.
 #pragma once
 #include <cuda.h>
@@ -40,7 +42,7 @@ constexpr unsigned kPfRaw = 4;          // raw payload stages
 constexpr unsigned kPfRawBytes = 16384; // 128 rows x 128 B (gate/up) or 8 blocks x 128 rows x 16 B (down)
 constexpr unsigned kPfA = 128 * 256;    // A stage: 128 rows x K 256
 constexpr unsigned kPfB = kPfTile * 256;
-constexpr unsigned kPfAcc = 4;          // accumulator buffers
+constexpr unsigned kPfAcc = 8;          // accumulator buffers (two groups of four MMA steps)
 constexpr unsigned kPfThreads = 448;     // 14 warps
 enum : unsigned { kGateUp = 0, kDown = 1 };
 
@@ -106,6 +108,10 @@ __device__ __forceinline__ bool pf_wait_warp(uint64_t* bar, unsigned parity, vol
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void conv_sync() { asm volatile("bar.sync 3, 128;" ::: "memory"); }
 __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
@@ -254,6 +260,11 @@ __global__ void __launch_bounds__(1024) prefill_group_kernel(PrefillArgs a) {
 
 // ---------------------------------------------------------- 3/4. MMA
 
+struct PfSmem;
+template <unsigned MODE>
+__device__ __forceinline__ void pf_apply16(const PfSmem& s, unsigned ab, unsigned st, unsigned m, unsigned col,
+                                           const uint32_t (&v)[16], float* acc, bool live, bool& bad);
+
 struct PfSmem {
   uint8_t raw[kPfRaw][kPfRawBytes];
   uint8_t A[2][kPfA];
@@ -261,12 +272,34 @@ struct PfSmem {
   float colscale[2][8][kPfTile];  // per block of the chunk, per token
   uint8_t rowscale[2][8][128];    // per block of the chunk, per A row (E8M0)
   float amax[4][kPfTile];         // gate/up epilogue: per-warp amax per token
+  unsigned tok[kPfTile];          // converters: the current item's token ids
   uint64_t raw_full[kPfRaw], raw_empty[kPfRaw];
   uint64_t ab_full[2], ab_empty[2], sc_empty[2];
-  uint64_t acc_full[kPfAcc], acc_empty[kPfAcc];
+  uint64_t acc_full[2], acc_empty[2];
   uint32_t taddr;
   unsigned abort;
 };
+
+// One MMA step's int32 results for 16 token columns (starting at `col`) of
+// A row m: acc[j] = fmaf(float(I) * colscale, rowscale, acc[j]), the row's
+// block scale 2^(e-128) (E8M0 e; 255 is nonfinite).
+template <unsigned MODE>
+__device__ __forceinline__ void pf_apply16(const PfSmem& s, unsigned ab, unsigned st, unsigned m, unsigned col,
+                                           const uint32_t (&v)[16], float* acc, bool live, bool& bad) {
+  const unsigned e8 = MODE == kGateUp ? (&s.rowscale[ab][0][0])[8 * m + st] : s.rowscale[ab][st][m];
+  bad |= live && e8 == 255;
+  const float ws = pow2_m128(e8);
+  const float4* cs = reinterpret_cast<const float4*>(s.colscale[ab][st] + col);
+#pragma unroll
+  for (unsigned q4 = 0; q4 < 4; ++q4) {
+    const float4 cv = cs[q4];
+    const unsigned j = 4 * q4;
+    acc[j] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(v[j])), cv.x), ws, acc[j]);
+    acc[j + 1] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(v[j + 1])), cv.y), ws, acc[j + 1]);
+    acc[j + 2] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(v[j + 2])), cv.z), ws, acc[j + 2]);
+    acc[j + 3] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(v[j + 3])), cv.w), ws, acc[j + 3]);
+  }
+}
 
 template <unsigned MODE>
 __device__ __forceinline__ unsigned pf_chunks(const PrefillArgs& a) {
@@ -299,7 +332,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
     for (unsigned i = 0; i < 2; ++i) {
       mbar_init(&s.ab_full[i], 128); mbar_init(&s.ab_empty[i], 1); mbar_init(&s.sc_empty[i], 8);
     }
-    for (unsigned i = 0; i < kPfAcc; ++i) { mbar_init(&s.acc_full[i], 1); mbar_init(&s.acc_empty[i], 8); }
+    for (unsigned i = 0; i < 2; ++i) { mbar_init(&s.acc_full[i], 1); mbar_init(&s.acc_empty[i], 8); }
     s.abort = 0;
     fence_mbar_init();
   }
@@ -355,7 +388,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
   } else if (warp == 13) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      unsigned c = 0, q = 0;
+      unsigned c = 0, r = 0;
       for (unsigned it = blockIdx.x; it < nitems && !*abort; it += gridDim.x) {
         const uint4 item = items[it];
         const unsigned npad = (item.z + 15) & ~15u;
@@ -367,15 +400,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
           tc_fence_after();
           const uint32_t a0 = smem_u32(s.A[ab]), b0 = smem_u32(s.B[ab]);
           const unsigned steps = pf_steps<MODE>(a, k);
-          for (unsigned st = 0; st < steps; ++st, ++q) {
-            const unsigned buf = q % kPfAcc;
-            if (!pf_wait(&s.acc_empty[buf], ((q / kPfAcc) & 1) ^ 1, abort)) break;
-            PF_STAMP(62, it == blockIdx.x + gridDim.x && k == 1 && st == 0);
+          for (unsigned g0 = 0; g0 < steps; g0 += 4, ++r) {  // groups of up to four steps
+            const unsigned grp = r & 1, n = min(4u, steps - g0);
+            if (!pf_wait(&s.acc_empty[grp], ((r >> 1) & 1) ^ 1, abort)) break;
+            PF_STAMP(62, it == blockIdx.x + gridDim.x && k == 1 && g0 == 0);
             tc_fence_after();
-            umma_i8(tmem + buf * kPfTile, umma_desc(a0 + 256 * st, 128, 8 * 256), umma_desc(b0 + 256 * st, 128, 8 * 256),
-                    idesc, false);
-            umma_commit(&s.acc_full[buf]);
-            PF_STAMP(63, it == blockIdx.x + gridDim.x && k == 1 && st == 0);
+            for (unsigned j = 0; j < n; ++j) {
+              const unsigned st = g0 + j;
+              umma_i8(tmem + (4 * grp + j) * kPfTile, umma_desc(a0 + 256 * st, 128, 8 * 256),
+                      umma_desc(b0 + 256 * st, 128, 8 * 256), idesc, false);
+            }
+            umma_commit(&s.acc_full[grp]);
+            PF_STAMP(63, it == blockIdx.x + gridDim.x && k == 1 && g0 == 0);
           }
           umma_commit(&s.ab_empty[ab]);
           PF_STAMP(33 + k, it == blockIdx.x + gridDim.x && k < 8);
@@ -389,11 +425,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
     // ------------------------------------------------ converters
     const unsigned m = tid;  // A row
     unsigned c = 0;
-    for (unsigned it = blockIdx.x; it < nitems && !*abort; it += gridDim.x) {
+    // No abort test on the item loop: all converter threads must reach every
+    // conv_sync; after an abort each wait fails at once.
+    for (unsigned it = blockIdx.x; it < nitems; it += gridDim.x) {
       const uint4 item = items[it];
       unsigned blk = 0, hrow = 0;
       if (MODE == kGateUp) gu_row(m, item.w, blk, hrow);
       const bool row_live = MODE != kGateUp || blk < a.S;
+      // the item's token ids, read once (no dependent global loads per chunk)
+      conv_sync();
+      if (MODE == kGateUp && tid < item.z) s.tok[tid] = a.pair_token[item.y + tid];
+      conv_sync();
       for (unsigned k = 0; k < nk; ++k, ++c) {
         const unsigned st = c % kPfRaw, ab = c & 1, steps = pf_steps<MODE>(a, k);
         if (!pf_wait(&s.ab_empty[ab], ((c >> 1) & 1) ^ 1, abort)) break;
@@ -404,7 +446,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
           const unsigned j = i >> 4, piece = i & 15;
           if (MODE == kDown && piece >= 2 * steps) continue;
           const int8_t* src = MODE == kGateUp
-                                  ? a.xq + static_cast<size_t>(a.pair_token[item.y + j]) * d + 256 * k + 16 * piece
+                                  ? a.xq + static_cast<size_t>(s.tok[j]) * d + 256 * k + 16 * piece
                                   : a.hq + (static_cast<size_t>(item.y + j) * a.S + 8 * k) * 32 + 16 * piece;
           cp_async16(s.B[ab] + umma_off(j, 16 * piece, 256), src);
         }
@@ -414,11 +456,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
             const uint8_t* row = a.base[blk] + item.x * a.slice_bytes + static_cast<size_t>(hrow) * a.row_bytes;
             cp_async8(&s.rowscale[ab][0][0] + 8 * m, row + 8 * k);  // gate/up: [row][8 blocks]
           }
-          for (unsigned i = tid; i < item.z * 4; i += 128) {
-            const unsigned j = i >> 2, g = i & 3;
-            const float v = a.xs[static_cast<size_t>(a.pair_token[item.y + j]) * (d / 64) + 4 * k + g];
-            s.colscale[ab][2 * g][j] = v;
-            s.colscale[ab][2 * g + 1][j] = v;
+          for (unsigned i = tid; i < item.z * 8; i += 128) {
+            const unsigned j = i >> 3, b = i & 7;  // block b of the chunk: x group b / 2
+            cp_async4(&s.colscale[ab][b][j], a.xs + static_cast<size_t>(s.tok[j]) * (d / 64) + 4 * k + (b >> 1));
           }
         } else {
           for (unsigned i = tid; i < steps * 8; i += 128) {
@@ -428,7 +468,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
           }
           for (unsigned i = tid; i < item.z * steps; i += 128) {
             const unsigned j = i / steps, b = i % steps;
-            s.colscale[ab][b][j] = a.hs[static_cast<size_t>(item.y + j) * a.S + 8 * k + b];
+            cp_async4(&s.colscale[ab][b][j], a.hs + static_cast<size_t>(item.y + j) * a.S + 8 * k + b);
           }
         }
         cp_async_commit();
@@ -463,13 +503,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         PF_STAMP(17 + k, tid == 0 && it == blockIdx.x + gridDim.x && k < 8);
       }
     }
+    cp_async_wait_all();  // no copy may land after the CTA exits
   } else {
     // ------------------------------------------------ epilogue (warps 4-11)
     // Two warpgroups: warps 4-7 take tile columns 0-31, warps 8-11 columns
     // 32-63; warp w reads TMEM lanes 32 (w % 4) .. +31 (A rows).
     const unsigned wg = (warp - 4) >> 2, ew = warp & 3, m = 32 * ew + lane, col0 = 32 * wg;
     const uint32_t lane_base = tmem + ((32 * ew) << 16);
-    unsigned c = 0, q = 0;
+    unsigned c = 0, r = 0;
     bool bad = false;
     // No abort test in these loops: the warps of a warpgroup must take the
     // same number of epi_sync barriers; after an abort every wait fails at once.
@@ -490,42 +531,45 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         // the converters' scales of this chunk (acquired directly: the stage
         // cannot move on before this warp releases sc_empty below)
         pf_wait_warp(&s.ab_full[ab], (c >> 1) & 1, abort);
-        for (unsigned st = 0; st < steps; ++st, ++q) {
-          const unsigned buf = q % kPfAcc;
-          if (!pf_wait_warp(&s.acc_full[buf], (q / kPfAcc) & 1, abort)) continue;
-          PF_STAMP(58, tid == 128 && it == blockIdx.x + gridDim.x && k == 1 && st == 0);
+        for (unsigned g0 = 0; g0 < steps; g0 += 4, ++r) {
+          const unsigned grp = r & 1, n = min(4u, steps - g0);
+          if (!pf_wait_warp(&s.acc_full[grp], (r >> 1) & 1, abort)) continue;
+          PF_STAMP(58, tid == 128 && it == blockIdx.x + gridDim.x && k == 1 && g0 == 0);
           tc_fence_after();
-          uint32_t v[2][16];
+          const uint32_t tg = lane_base + 4 * grp * kPfTile + col0;
+          // one register buffer of four 16-column reads: with at most 16 live
+          // columns here the group's steps are read at once, with 32 two
+          // steps at a time
+          uint32_t v[4][16];
+          if (col0 + 16 < ntok) {  // 32 live columns: two steps at a time
 #pragma unroll
-          for (unsigned g = 0; g < 2; ++g)
-            if (col0 + 16 * g < ntok) tmem_ld16(lane_base + buf * kPfTile + col0 + 16 * g, v[g]);
-          tmem_wait_ld();
-          PF_STAMP(60, tid == 128 && it == blockIdx.x + gridDim.x && k == 1 && st == 0);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&s.acc_empty[buf]);
-          const unsigned e8 = MODE == kGateUp ? (&s.rowscale[ab][0][0])[8 * m + st] : s.rowscale[ab][st][m];
-          bad |= live && e8 == 255;
-          const float ws = pow2_m128(e8);
-          const float4* cs = reinterpret_cast<const float4*>(s.colscale[ab][st] + col0);
-          // whole 16-column groups under a warp-uniform branch (columns past
-          // the tile's tokens compute harmless values that are never stored)
+            for (unsigned jb = 0; jb < 4; jb += 2) {
+              if (jb < n) {
 #pragma unroll
-          for (unsigned g = 0; g < 2; ++g) {
-            if (col0 + 16 * g < ntok) {
+                for (unsigned i = 0; i < 4; ++i)
+                  if (jb + (i >> 1) < n) tmem_ld16(tg + (jb + (i >> 1)) * kPfTile + 16 * (i & 1), v[i]);
+                tmem_wait_ld();
 #pragma unroll
-              for (unsigned q4 = 0; q4 < 4; ++q4) {
-                const float4 cv = cs[4 * g + q4];
-                const unsigned j = 16 * g + 4 * q4;
-                const uint32_t* vj = &v[g][4 * q4];
-                acc[j] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(vj[0])), cv.x), ws, acc[j]);
-                acc[j + 1] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(vj[1])), cv.y), ws, acc[j + 1]);
-                acc[j + 2] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(vj[2])), cv.z), ws, acc[j + 2]);
-                acc[j + 3] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(vj[3])), cv.w), ws, acc[j + 3]);
+                for (unsigned i = 0; i < 4; ++i)
+                  if (jb + (i >> 1) < n)
+                    pf_apply16<MODE>(s, ab, g0 + jb + (i >> 1), m, col0 + 16 * (i & 1), v[i], acc + 16 * (i & 1), live,
+                                     bad);
               }
             }
+          } else if (col0 < ntok) {  // at most 16 live columns: the group's steps at once
+#pragma unroll
+            for (unsigned i = 0; i < 4; ++i)
+              if (i < n) tmem_ld16(tg + i * kPfTile, v[i]);
+            tmem_wait_ld();
+            PF_STAMP(60, tid == 128 && it == blockIdx.x + gridDim.x && k == 1 && g0 == 0);
+#pragma unroll
+            for (unsigned i = 0; i < 4; ++i)
+              if (i < n) pf_apply16<MODE>(s, ab, g0 + i, m, col0, v[i], acc, live, bad);
           }
-          PF_STAMP(59, tid == 128 && it == blockIdx.x + gridDim.x && k == 1 && st == 0);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.acc_empty[grp]);
+          PF_STAMP(59, tid == 128 && it == blockIdx.x + gridDim.x && k == 1 && g0 == 0);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.sc_empty[ab]);
