@@ -545,7 +545,7 @@ static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_
   mark(3);
   prefill_mma_kernel<kDown><<<c->sms, kPfThreads, smem, s>>>(a);
   mark(4);
-  prefill_combine_kernel<<<dim3(d / 256, T), 256, 0, s>>>(a);
+  prefill_combine_kernel<<<dim3((d / 4 + 255) / 256, T), 256, 0, s>>>(a);
   mark(5);
   c->pf_timed = timed;
   CK(cudaGetLastError());

@@ -28,7 +28,7 @@
 //     columns (TMEM lanes 0-127 = A rows);
 //   warp 12 issues the bulk copies; warp 13 owns tensor memory and issues
 //   the MMAs (one thread).
-// Rings: 4 raw stages, 2 A/B stages, 8 accumulator buffers of 64 columns
+// Rings: 3 raw stages, 3 A/B stages, 8 accumulator buffers of 64 columns
 // (all of tensor memory) used as two groups of four MMA steps, so that the
 // epilogue takes one barrier and several independent TMEM reads per group.
 // Every wait gives up after 2 s (kStTimeout) so a fault cannot hang the GPU.
@@ -38,7 +38,8 @@
 namespace frc {
 
 constexpr unsigned kPfTile = 64;        // tokens per item (MMA N <= 64)
-constexpr unsigned kPfRaw = 4;          // raw payload stages
+constexpr unsigned kPfRaw = 3;          // raw payload stages
+constexpr unsigned kPfAB = 3;           // A/B operand stages
 constexpr unsigned kPfRawBytes = 16384; // 128 rows x 128 B (gate/up) or 8 blocks x 128 rows x 16 B (down)
 constexpr unsigned kPfA = 128 * 256;    // A stage: 128 rows x K 256
 constexpr unsigned kPfB = kPfTile * 256;
@@ -111,6 +112,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
+__device__ __forceinline__ void cp_async_wait_group1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void conv_sync() { asm volatile("bar.sync 3, 128;" ::: "memory"); }
 __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -151,8 +153,9 @@ __device__ __forceinline__ void mxfp4_to_i8(uint4 q, uint4& lo, uint4& hi) {
     for (unsigned h = 0; h < 2; ++h) {
       const uint32_t sel = h ? w[m] >> 16 : w[m];
       const uint32_t pos = prmt(kE2M1Lo, kE2M1Hi, sel), neg = prmt(kE2M1Lo, kE2M1Hi, sel ^ 0x8888u);
-      // byte-wise pos - neg (one of them is 0): no borrow crosses a byte
-      o[2 * m + h] = ((pos | 0x80808080u) - neg) ^ 0x80808080u;
+      // byte-wise pos - neg (one of them is 0, both <= 12): with a bias of
+      // 0x80 a byte no borrow crosses a byte; one three-input add
+      o[2 * m + h] = ((pos + 0x80808080u) - neg) ^ 0x80808080u;
     }
   }
   lo = make_uint4(o[0], o[1], o[2], o[3]);
@@ -186,12 +189,40 @@ __global__ void prefill_quantize_kernel(PrefillArgs a) {
 
 // ------------------------------------------------------------ 2. group
 
+// Exclusive prefix sum of v over threads 0..511 of a 1024-thread CTA (the
+// others pass 0); *total receives the sum.  Every thread must call it.
+__device__ __forceinline__ unsigned scan512(unsigned v, unsigned* ws, unsigned& total) {
+  const unsigned lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  unsigned x = v;
+#pragma unroll
+  for (unsigned o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31 && w < 16) ws[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    unsigned t = lane < 16 ? ws[lane] : 0u;
+#pragma unroll
+    for (unsigned o = 1; o < 16; o <<= 1) {
+      const unsigned y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    if (lane < 16) ws[lane] = t;
+  }
+  __syncthreads();
+  const unsigned excl = x - v + (w > 0 && w < 16 ? ws[w - 1] : 0u);
+  total = ws[15];
+  __syncthreads();
+  return excl;
+}
+
 // Single CTA of 1024 threads.  Validation (ids < 512 and distinct per token,
 // gates finite and >= 0, shared gate 0), pairs, work lists.
 __global__ void __launch_bounds__(1024) prefill_group_kernel(PrefillArgs a) {
   __shared__ uint32_t bits[512][16];  // token bitmap per expert (T <= 512)
   __shared__ unsigned cnt[512], rank_of[512], ibase_gu[513], ibase_dn[513], poff[513];
-  __shared__ unsigned by_rank[512];
+  __shared__ unsigned by_rank[512], scan_ws[16];
   const unsigned tid = threadIdx.x, T = a.T, words = (T + 31) / 32;
   for (unsigned i = tid; i < 512 * 16; i += blockDim.x) (&bits[0][0])[i] = 0;
   __syncthreads();
@@ -225,17 +256,19 @@ __global__ void __launch_bounds__(1024) prefill_group_kernel(PrefillArgs a) {
     by_rank[r] = e;
   }
   __syncthreads();
-  if (tid == 0) {
+  {
+    // pair offsets in expert order, item offsets in rank order: block scans
     const unsigned npairs = (a.S + 1) / 2, nrt = a.d / 128;
-    unsigned p = 0, gu = 0, dn = 0;
-    for (unsigned e = 0; e < 512; ++e) { poff[e] = p; p += cnt[e]; }
-    poff[512] = p;
-    for (unsigned r = 0; r < 512; ++r) {
-      const unsigned e = by_rank[r], tiles = (cnt[e] + kPfTile - 1) / kPfTile;
-      ibase_gu[r] = gu; ibase_dn[r] = dn;
-      gu += tiles * npairs; dn += tiles * nrt;
+    unsigned tp, tgu, tdn;
+    const unsigned ep = scan512(tid < 512 ? cnt[tid] : 0u, scan_ws, tp);
+    const unsigned tiles = tid < 512 ? (cnt[by_rank[tid]] + kPfTile - 1) / kPfTile : 0u;
+    const unsigned eg = scan512(tiles * npairs, scan_ws, tgu);
+    const unsigned ed = scan512(tiles * nrt, scan_ws, tdn);
+    if (tid < 512) { poff[tid] = ep; ibase_gu[tid] = eg; ibase_dn[tid] = ed; }
+    if (tid == 0) {
+      poff[512] = tp;
+      a.counts[0] = tp; a.counts[1] = tgu; a.counts[2] = tdn;
     }
-    a.counts[0] = p; a.counts[1] = gu; a.counts[2] = dn;
   }
   __syncthreads();
   for (unsigned i = tid; i < T * 10; i += blockDim.x) {
@@ -267,14 +300,14 @@ __device__ __forceinline__ void pf_apply16(const PfSmem& s, unsigned ab, unsigne
 
 struct PfSmem {
   uint8_t raw[kPfRaw][kPfRawBytes];
-  uint8_t A[2][kPfA];
-  uint8_t B[2][kPfB];
-  float colscale[2][8][kPfTile];  // per block of the chunk, per token
-  uint8_t rowscale[2][8][128];    // per block of the chunk, per A row (E8M0)
+  uint8_t A[kPfAB][kPfA];
+  uint8_t B[kPfAB][kPfB];
+  float colscale[kPfAB][8][kPfTile];  // per block of the chunk, per token
+  uint8_t rowscale[kPfAB][8][128];    // per block of the chunk, per A row (E8M0)
   float amax[4][kPfTile];         // gate/up epilogue: per-warp amax per token
-  unsigned tok[kPfTile];          // converters: the current item's token ids
+  unsigned tok[2][kPfTile];       // converters: token ids of the last two items requested
   uint64_t raw_full[kPfRaw], raw_empty[kPfRaw];
-  uint64_t ab_full[2], ab_empty[2], sc_empty[2];
+  uint64_t ab_full[kPfAB], ab_empty[kPfAB], sc_empty[kPfAB];
   uint64_t acc_full[2], acc_empty[2];
   uint32_t taddr;
   unsigned abort;
@@ -329,7 +362,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
 
   if (tid == 0) {
     for (unsigned i = 0; i < kPfRaw; ++i) { mbar_init(&s.raw_full[i], 1); mbar_init(&s.raw_empty[i], 128); }
-    for (unsigned i = 0; i < 2; ++i) {
+    for (unsigned i = 0; i < kPfAB; ++i) {
       mbar_init(&s.ab_full[i], 128); mbar_init(&s.ab_empty[i], 1); mbar_init(&s.sc_empty[i], 8);
     }
     for (unsigned i = 0; i < 2; ++i) { mbar_init(&s.acc_full[i], 1); mbar_init(&s.acc_empty[i], 8); }
@@ -366,7 +399,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
                           static_cast<int>(item.x * a.slice_rows), &s.raw_full[st]);
           }
           __syncwarp();
-          PF_STAMP(50 + k, lane == 0 && it == blockIdx.x + gridDim.x && k < 8);
+          PF_STAMP(50 + k, lane == 0 && it + gridDim.x >= nitems && k < 8);
         } else {
           const unsigned steps = pf_steps<MODE>(a, k);
           if (lane == 0) mbar_expect_tx(&s.raw_full[st], steps * 2048);
@@ -394,16 +427,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         const unsigned npad = (item.z + 15) & ~15u;
         const uint32_t idesc = umma_idesc_i8(128, npad);
         for (unsigned k = 0; k < nk && !*abort; ++k, ++c) {
-          const unsigned ab = c & 1;
-          if (!pf_wait(&s.ab_full[ab], (c >> 1) & 1, abort)) break;
-          PF_STAMP(25 + k, it == blockIdx.x + gridDim.x && k < 8);
+          const unsigned ab = c % kPfAB;
+          if (!pf_wait(&s.ab_full[ab], (c / kPfAB) & 1, abort)) break;
+          PF_STAMP(25 + k, it + gridDim.x >= nitems && k < 8);
           tc_fence_after();
           const uint32_t a0 = smem_u32(s.A[ab]), b0 = smem_u32(s.B[ab]);
           const unsigned steps = pf_steps<MODE>(a, k);
           for (unsigned g0 = 0; g0 < steps; g0 += 4, ++r) {  // groups of up to four steps
             const unsigned grp = r & 1, n = min(4u, steps - g0);
             if (!pf_wait(&s.acc_empty[grp], ((r >> 1) & 1) ^ 1, abort)) break;
-            PF_STAMP(62, it == blockIdx.x + gridDim.x && k == 1 && g0 == 0);
+            PF_STAMP(62, it + gridDim.x >= nitems && k == 1 && g0 == 0);
             tc_fence_after();
             for (unsigned j = 0; j < n; ++j) {
               const unsigned st = g0 + j;
@@ -411,54 +444,59 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
                       umma_desc(b0 + 256 * st, 128, 8 * 256), idesc, false);
             }
             umma_commit(&s.acc_full[grp]);
-            PF_STAMP(63, it == blockIdx.x + gridDim.x && k == 1 && g0 == 0);
+            PF_STAMP(63, it + gridDim.x >= nitems && k == 1 && g0 == 0);
           }
           umma_commit(&s.ab_empty[ab]);
-          PF_STAMP(33 + k, it == blockIdx.x + gridDim.x && k < 8);
+          PF_STAMP(33 + k, it + gridDim.x >= nitems && k < 8);
         }
       }
       // the last commit's arrive must land before the CTA exits
-      if (c) pf_wait(&s.ab_empty[(c - 1) & 1], ((c - 1) >> 1) & 1, abort);
+      if (c) pf_wait(&s.ab_empty[(c - 1) % kPfAB], ((c - 1) / kPfAB) & 1, abort);
     }
     __syncwarp();
   } else if (warp < 4) {
     // ------------------------------------------------ converters
+    // Software-pipelined: the B rows and scales of chunk c + 1 are requested
+    // (cp.async) before chunk c's weights are converted, so the gather's L2
+    // latency overlaps the conversion.  No abort test on the loops: all
+    // converter threads must reach every conv_sync; after an abort each wait
+    // fails at once.
     const unsigned m = tid;  // A row
-    unsigned c = 0;
-    // No abort test on the item loop: all converter threads must reach every
-    // conv_sync; after an abort each wait fails at once.
-    for (unsigned it = blockIdx.x; it < nitems; it += gridDim.x) {
-      const uint4 item = items[it];
-      unsigned blk = 0, hrow = 0;
-      if (MODE == kGateUp) gu_row(m, item.w, blk, hrow);
-      const bool row_live = MODE != kGateUp || blk < a.S;
-      // the item's token ids, read once (no dependent global loads per chunk)
-      conv_sync();
-      if (MODE == kGateUp && tid < item.z) s.tok[tid] = a.pair_token[item.y + tid];
-      conv_sync();
-      for (unsigned k = 0; k < nk; ++k, ++c) {
-        const unsigned st = c % kPfRaw, ab = c & 1, steps = pf_steps<MODE>(a, k);
-        if (!pf_wait(&s.ab_empty[ab], ((c >> 1) & 1) ^ 1, abort)) break;
-        if (!pf_wait(&s.sc_empty[ab], ((c >> 1) & 1) ^ 1, abort)) break;
-        PF_STAMP(1 + k, tid == 0 && it == blockIdx.x + gridDim.x && k < 8);
+    // the chunk stream being requested
+    unsigned ic = 0, iit = blockIdx.x, ik = 0, iitem = 0;
+    uint4 inext = iit < nitems ? items[iit] : make_uint4(0, 0, 0, 0);
+    auto issue = [&]() -> bool {
+      if (iit >= nitems) return false;
+      const uint4 item = inext;
+      const unsigned k = ik, ab = ic % kPfAB, steps = pf_steps<MODE>(a, k), tb = iitem & 1;
+      if (k == 0) {  // the item's token ids, read once (no dependent global loads per chunk)
+        conv_sync();
+        if (MODE == kGateUp && tid < item.z) s.tok[tb][tid] = a.pair_token[item.y + tid];
+        conv_sync();
+      }
+      const bool ok = pf_wait(&s.ab_empty[ab], ((ic / kPfAB) & 1) ^ 1, abort) &&
+                      pf_wait(&s.sc_empty[ab], ((ic / kPfAB) & 1) ^ 1, abort);
+      if (ok) {
         // B rows: the tile's tokens (gate/up: x of the token; down: hq of the pair)
         for (unsigned i = tid; i < item.z * 16; i += 128) {
           const unsigned j = i >> 4, piece = i & 15;
           if (MODE == kDown && piece >= 2 * steps) continue;
           const int8_t* src = MODE == kGateUp
-                                  ? a.xq + static_cast<size_t>(s.tok[j]) * d + 256 * k + 16 * piece
+                                  ? a.xq + static_cast<size_t>(s.tok[tb][j]) * d + 256 * k + 16 * piece
                                   : a.hq + (static_cast<size_t>(item.y + j) * a.S + 8 * k) * 32 + 16 * piece;
           cp_async16(s.B[ab] + umma_off(j, 16 * piece, 256), src);
         }
         // scales of the chunk's blocks
         if (MODE == kGateUp) {
-          if (row_live) {
+          unsigned blk, hrow;
+          gu_row(m, item.w, blk, hrow);
+          if (blk < a.S) {
             const uint8_t* row = a.base[blk] + item.x * a.slice_bytes + static_cast<size_t>(hrow) * a.row_bytes;
             cp_async8(&s.rowscale[ab][0][0] + 8 * m, row + 8 * k);  // gate/up: [row][8 blocks]
           }
           for (unsigned i = tid; i < item.z * 8; i += 128) {
             const unsigned j = i >> 3, b = i & 7;  // block b of the chunk: x group b / 2
-            cp_async4(&s.colscale[ab][b][j], a.xs + static_cast<size_t>(s.tok[j]) * (d / 64) + 4 * k + (b >> 1));
+            cp_async4(&s.colscale[ab][b][j], a.xs + static_cast<size_t>(s.tok[tb][j]) * (d / 64) + 4 * k + (b >> 1));
           }
         } else {
           for (unsigned i = tid; i < steps * 8; i += 128) {
@@ -471,12 +509,33 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
             cp_async4(&s.colscale[ab][b][j], a.hs + static_cast<size_t>(item.y + j) * a.S + 8 * k + b);
           }
         }
-        cp_async_commit();
+      }
+      cp_async_commit();  // one group per chunk, empty after a failed wait
+      ++ic;
+      if (++ik == nk) {
+        ik = 0;
+        ++iitem;
+        iit += gridDim.x;
+        if (iit < nitems) inext = items[iit];
+      }
+      return true;
+    };
+    issue();
+    unsigned c = 0;
+    for (unsigned it = blockIdx.x; it < nitems; it += gridDim.x) {
+      const uint4 item = items[it];
+      unsigned blk = 0, hrow = 0;
+      if (MODE == kGateUp) gu_row(m, item.w, blk, hrow);
+      const bool row_live = MODE != kGateUp || blk < a.S;
+      for (unsigned k = 0; k < nk; ++k, ++c) {
+        const unsigned st = c % kPfRaw, ab = c % kPfAB, steps = pf_steps<MODE>(a, k);
+        PF_STAMP(1 + k, tid == 0 && it + gridDim.x >= nitems && k < 8);
+        const bool more = issue();  // chunk c + 1
         // A: raw payload -> int8
-        if (!pf_wait(&s.raw_full[st], (c / kPfRaw) & 1, abort)) break;
-        PF_STAMP(9 + k, tid == 0 && it == blockIdx.x + gridDim.x && k < 8);
+        const bool landed = pf_wait(&s.raw_full[st], (c / kPfRaw) & 1, abort);
+        PF_STAMP(9 + k, tid == 0 && it + gridDim.x >= nitems && k < 8);
         uint8_t* A = s.A[ab];
-        if (MODE == kGateUp) {
+        if (landed && MODE == kGateUp) {
           if (row_live) {
             const unsigned R = 64 * (m >> 6) + hrow;  // row of the staged boxes
 #pragma unroll
@@ -488,7 +547,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
               *reinterpret_cast<uint4*>(A + umma_off(m, 32 * b + 16, 256)) = hi;
             }
           }
-        } else {
+        } else if (landed) {
           for (unsigned b = 0; b < steps; ++b) {
             uint4 lo, hi;
             mxfp4_to_i8(*reinterpret_cast<const uint4*>(s.raw[st] + 2048 * b + 16 * m), lo, hi);
@@ -497,10 +556,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
           }
         }
         mbar_arrive(&s.raw_empty[st]);
-        cp_async_wait_all();
+        if (more) cp_async_wait_group1(); else cp_async_wait_all();  // chunk c's copies
         fence_proxy_async();
         mbar_arrive(&s.ab_full[ab]);
-        PF_STAMP(17 + k, tid == 0 && it == blockIdx.x + gridDim.x && k < 8);
+        PF_STAMP(17 + k, tid == 0 && it + gridDim.x >= nitems && k < 8);
       }
     }
     cp_async_wait_all();  // no copy may land after the CTA exits
@@ -527,14 +586,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         live = blk < a.S;
       }
       for (unsigned k = 0; k < nk; ++k, ++c) {
-        const unsigned ab = c & 1, steps = pf_steps<MODE>(a, k);
+        const unsigned ab = c % kPfAB, steps = pf_steps<MODE>(a, k);
         // the converters' scales of this chunk (acquired directly: the stage
         // cannot move on before this warp releases sc_empty below)
-        pf_wait_warp(&s.ab_full[ab], (c >> 1) & 1, abort);
+        pf_wait_warp(&s.ab_full[ab], (c / kPfAB) & 1, abort);
         for (unsigned g0 = 0; g0 < steps; g0 += 4, ++r) {
           const unsigned grp = r & 1, n = min(4u, steps - g0);
           if (!pf_wait_warp(&s.acc_full[grp], (r >> 1) & 1, abort)) continue;
-          PF_STAMP(58, tid == 128 && it == blockIdx.x + gridDim.x && k == 1 && g0 == 0);
+          PF_STAMP(58, tid == 128 && it + gridDim.x >= nitems && k == 1 && g0 == 0);
           tc_fence_after();
           const uint32_t tg = lane_base + 4 * grp * kPfTile + col0;
           // one register buffer of four 16-column reads: with at most 16 live
@@ -561,7 +620,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
             for (unsigned i = 0; i < 4; ++i)
               if (i < n) tmem_ld16(tg + i * kPfTile, v[i]);
             tmem_wait_ld();
-            PF_STAMP(60, tid == 128 && it == blockIdx.x + gridDim.x && k == 1 && g0 == 0);
+            PF_STAMP(60, tid == 128 && it + gridDim.x >= nitems && k == 1 && g0 == 0);
 #pragma unroll
             for (unsigned i = 0; i < 4; ++i)
               if (i < n) pf_apply16<MODE>(s, ab, g0 + i, m, col0, v[i], acc, live, bad);
@@ -569,11 +628,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&s.acc_empty[grp]);
-          PF_STAMP(59, tid == 128 && it == blockIdx.x + gridDim.x && k == 1 && g0 == 0);
+          PF_STAMP(59, tid == 128 && it + gridDim.x >= nitems && k == 1 && g0 == 0);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.sc_empty[ab]);
-        PF_STAMP(41 + k, tid == 128 && it == blockIdx.x + gridDim.x && k < 8);
+        PF_STAMP(41 + k, tid == 128 && it + gridDim.x >= nitems && k < 8);
       }
       const bool ok = !*abort;
       if (MODE == kDown) {
@@ -641,7 +700,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         }
         epi_sync(wg);
       }
-      PF_STAMP(49, tid == 128 && it == blockIdx.x + gridDim.x);
+      PF_STAMP(49, tid == 128 && it + gridDim.x >= nitems);
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(a.status, kStNumeric);
   }
@@ -656,21 +715,26 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
 // y[t][r] = fmaf over the token's ten experts in request order of
 // gate * partial; one thread per (t, r).
 __global__ void prefill_combine_kernel(PrefillArgs a) {
-  const unsigned t = blockIdx.y, r = blockIdx.x * blockDim.x + threadIdx.x;
+  const unsigned t = blockIdx.y, r = 4 * (blockIdx.x * blockDim.x + threadIdx.x);  // four rows a thread
   if (r >= a.d) return;
   const unsigned P = a.counts[0];
-  float acc = 0.0f;
+  float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
   for (unsigned j = 0; j < 10; ++j) {
     const unsigned p = a.slot_pair[t * 10 + j];
     if (p >= P) {  // an id the group kernel rejected (status already set)
-      acc = 0.0f;
+      acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       break;
     }
-    acc = __fmaf_rn(a.gate[t * 11 + j], a.ye[static_cast<size_t>(p) * a.d + r], acc);
+    const float g = a.gate[t * 11 + j];
+    const float4 v = *reinterpret_cast<const float4*>(a.ye + static_cast<size_t>(p) * a.d + r);
+    acc.x = __fmaf_rn(g, v.x, acc.x);
+    acc.y = __fmaf_rn(g, v.y, acc.y);
+    acc.z = __fmaf_rn(g, v.z, acc.z);
+    acc.w = __fmaf_rn(g, v.w, acc.w);
   }
-  if (!isfinite(acc)) atomicOr(a.status, kStNumeric);
-  a.y[static_cast<size_t>(t) * a.d + r] = acc;
+  if (!isfinite(acc.x) || !isfinite(acc.y) || !isfinite(acc.z) || !isfinite(acc.w)) atomicOr(a.status, kStNumeric);
+  *reinterpret_cast<float4*>(a.y + static_cast<size_t>(t) * a.d + r) = acc;
 }
 
 }  // namespace frc
