@@ -755,7 +755,7 @@ def run_prefill_bench(args, rank, world, local):
             "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": prefill_config(world, unique),
             "weight_gbs": unique * SLICES * PF_SLICE_BYTES * 1e3 / ms_per_step / 1e9,
             "roofline": {"bound": "hbm", "achieved": gu_gbs, "peak": peak, "unit": "GB/s", "frac": gu_gbs / peak,
-                         "traffic": None, "peak_source": peak_src,
+                         "traffic": ncu_traffic("prefill_mma_kernels_prefill512_full.md"), "peak_source": peak_src,
                          "kernel": "prefill_mma_kernel<gate/up> (tcgen05 kind::i8)",
                          "algorithmic_bytes_per_launch": gu_bytes, "launch_us": float(stage[2] * 1e3),
                          "launch_us_source": "CUDA events around the launch on its stream (eager calls)",
@@ -831,10 +831,10 @@ def prefill_parity(ctx, fb, g, pool, blocks, req):
         y[sample].view(np.uint32), y_ref.view(np.uint32)))}
 
 
-def ncu_traffic():
-    """DRAM bytes per launch of the layer kernel from the committed ncu summary, if any."""
+def ncu_traffic(name="layer_kernel_decode48_full.md"):
+    """DRAM bytes per launch of the dominant kernel from a committed ncu summary, if any."""
     try:
-        with open(os.path.join(ROOT, "profiles", "layer_kernel_decode48_full.md")) as f:
+        with open(os.path.join(ROOT, "profiles", name)) as f:
             for line in f:
                 if line.startswith("dram_bytes_per_launch:"):
                     return int(line.split(":")[1])
