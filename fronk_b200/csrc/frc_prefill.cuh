@@ -313,9 +313,29 @@ struct PfSmem {
   unsigned abort;
 };
 
+// Packed fp32 pairs (sm_100 f32x2 ops: one instruction, two IEEE results
+// with the same rounding as the scalar operations).
+__device__ __forceinline__ void add2(float& x, float& y, float bx, float by) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(x), "+f"(y) : "f"(bx), "f"(by));
+}
+__device__ __forceinline__ void mul2(float& x, float& y, float bx, float by) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(x), "+f"(y) : "f"(bx), "f"(by));
+}
+// (cx, cy) = fma(a, b, (cx, cy)) pairwise
+__device__ __forceinline__ void fma2(float ax, float ay, float bx, float by, float& cx, float& cy) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%0, %1};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(cx), "+f"(cy) : "f"(ax), "f"(ay), "f"(bx), "f"(by));
+}
+
 // One MMA step's int32 results for 16 token columns (starting at `col`) of
 // A row m: acc[j] = fmaf(float(I) * colscale, rowscale, acc[j]), the row's
-// block scale 2^(e-128) (E8M0 e; 255 is nonfinite).
+// block scale 2^(e-128) (E8M0 e; 255 is nonfinite).  float(I) is exact
+// (|I| < 2^22): the bits of I + 1.5 * 2^23 less that constant.
 template <unsigned MODE>
 __device__ __forceinline__ void pf_apply16(const PfSmem& s, unsigned ab, unsigned st, unsigned m, unsigned col,
                                            const uint32_t (&v)[16], float* acc, bool live, bool& bad) {
@@ -327,10 +347,14 @@ __device__ __forceinline__ void pf_apply16(const PfSmem& s, unsigned ab, unsigne
   for (unsigned q4 = 0; q4 < 4; ++q4) {
     const float4 cv = cs[q4];
     const unsigned j = 4 * q4;
-    acc[j] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(v[j])), cv.x), ws, acc[j]);
-    acc[j + 1] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(v[j + 1])), cv.y), ws, acc[j + 1]);
-    acc[j + 2] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(v[j + 2])), cv.z), ws, acc[j + 2]);
-    acc[j + 3] = __fmaf_rn(__fmul_rn(i2f(static_cast<int>(v[j + 3])), cv.w), ws, acc[j + 3]);
+    float f0 = __int_as_float(static_cast<int>(v[j]) + 0x4B400000), f1 = __int_as_float(static_cast<int>(v[j + 1]) + 0x4B400000);
+    float f2 = __int_as_float(static_cast<int>(v[j + 2]) + 0x4B400000), f3 = __int_as_float(static_cast<int>(v[j + 3]) + 0x4B400000);
+    add2(f0, f1, -12582912.0f, -12582912.0f);
+    add2(f2, f3, -12582912.0f, -12582912.0f);
+    mul2(f0, f1, cv.x, cv.y);
+    mul2(f2, f3, cv.z, cv.w);
+    fma2(f0, f1, ws, ws, acc[j], acc[j + 1]);
+    fma2(f2, f3, ws, ws, acc[j + 2], acc[j + 3]);
   }
 }
 
