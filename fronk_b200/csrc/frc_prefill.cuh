@@ -128,6 +128,18 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// Q8Group::q with the group's scale and multiplier given (the same values):
+// the nearest-even rounding through 1.5 * 2^23 (|v| <= 127 here) and the
+// clamp in integers, no float-to-int conversion.
+__device__ __forceinline__ int q8_fast(float x, float amax, float scale, float inv) {
+  if (scale == 0.0f) return 0;
+  float v;
+  if (isfinite(inv)) v = __fmul_rn(x, inv);
+  else v = __fmul_rn(__fdiv_rn(x, amax), 127.0f);
+  const int r = __float_as_int(__fadd_rn(v, 12582912.0f)) - 0x4B400000;
+  return max(-127, min(127, r));
+}
+
 // SwiGLU of backends/ref.c:81-83 without branches: with e = exp(-|a|) the
 // stable sigmoid is 1/(1+e) for a >= 0 and e/(1+e) for a < 0, the same
 // double operations as swiglu() in frc_device.cuh.  `fail` on a nonfinite
@@ -709,14 +721,20 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
 #pragma unroll
           for (unsigned g = 0; g < 2; ++g) {
             if (col0 + 16 * g < ntok) {
+              // the group's two divisions once per token: lane (lane & 16) + i'
+              // of each half computes them for its half's token i = 8g + i'
+              const unsigned tl = col0 + 2 * (8 * g + (lane & 7)) + odd;
+              const float am_l = fmaxf(s.amax[ew][tl], s.amax[ew ^ 1][tl]);
+              const float sc_l = __fdiv_rn(am_l, 127.0f);
+              const float inv_l = sc_l != 0.0f ? __fdiv_rn(127.0f, am_l) : 0.0f;
 #pragma unroll
               for (unsigned i = 8 * g; i < 8 * g + 8; ++i) {
-                const unsigned t = col0 + 2 * i + odd;
+                const unsigned src = (lane & 16) | (i - 8 * g), t = col0 + 2 * i + odd;
+                const float am = __shfl_sync(0xffffffffu, am_l, src), sc = __shfl_sync(0xffffffffu, sc_l, src);
+                const float inv = __shfl_sync(0xffffffffu, inv_l, src);
                 if (t < ntok) {
-                  const float am = fmaxf(s.amax[ew][t], s.amax[ew ^ 1][t]);
-                  const Q8Group qg(am);
-                  hq[static_cast<size_t>(t) * a.S * 32] = static_cast<int8_t>(qg.q(h[i]));
-                  if ((ew & 1) == 0 && (lane & 15) == 0) a.hs[static_cast<size_t>(item.y + t) * a.S + blk] = qg.scale;
+                  hq[static_cast<size_t>(t) * a.S * 32] = static_cast<int8_t>(q8_fast(h[i], am, sc, inv));
+                  if ((ew & 1) == 0 && (lane & 15) == 0) a.hs[static_cast<size_t>(item.y + t) * a.S + blk] = sc;
                 }
               }
             }
