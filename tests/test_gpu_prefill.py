@@ -44,6 +44,23 @@ def test_prefill_bitexact_with_oracle(gpu, oracle, tokens, blocks):
     assert np.array_equal(y.view(np.uint32), y_ref.view(np.uint32))
 
 
+@pytest.mark.parametrize("hidden,tokens,distinct", [(2560, 20, True), (2048, 300, False)])
+def test_prefill_other_shapes(gpu, oracle, hidden, tokens, distinct):
+    """The reference's own hidden size (d = 2560: ten 256-weight chunks, 20
+    row tiles), and 300 tokens that all pick the same ten experts (five
+    64-token tiles of each expert)."""
+    e, gt, x = request(hidden, tokens, SEED + hidden + tokens, distinct=distinct)
+    with fb.Context(0, hidden, gate_type=MXFP4, down_type=MXFP4) as ctx:
+        m, layers = _setup(ctx, oracle, [5, 6, 12], e, hidden)
+        rc, y = ctx.run(0, e, gt, x)
+        assert rc == OK, ctx.last_error
+        hq, hs = ctx.debug_prefill_hidden()
+    rc, y_ref, hq_ref, hs_ref = oracle.prefill_run(m, e, gt, x, want_hidden=True)
+    assert rc == OK
+    assert np.array_equal(hq, hq_ref) and np.array_equal(hs.view(np.uint32), hs_ref.view(np.uint32))
+    assert np.array_equal(y.view(np.uint32), y_ref.view(np.uint32))
+
+
 def test_prefill_zipf_512_tokens_all_blocks(gpu, oracle):
     """configs[4]'s shape: 512 tokens, Zipf(1.1) expert popularity, all 20
     blocks (device-filled units).  Tokens are independent, so a sample of
