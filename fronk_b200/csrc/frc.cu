@@ -891,9 +891,10 @@ int frc_run_device_fixed(frc_context* c, unsigned layer, unsigned tokens, const 
 // ------------------------------------------------------ in-box reduce
 // Inbox bytes for `world` ranks: double-buffered slots [2][world][16][d] f32,
 // then the flags [world][2 * SMs] u32 (one per source rank and CTA).
-static size_t inbox_bytes(const frc_context* c, unsigned world, unsigned gmax) {
-  return 2 * static_cast<size_t>(world) * kMaxTokens * c->g.hidden * sizeof(float) +
-         static_cast<size_t>(world) * gmax * sizeof(unsigned);
+// Inbox: [2 epoch parities][world sources][16 tokens][d] entries of 8 bytes
+// (the value and the epoch of the launch that wrote it).
+static size_t inbox_bytes(const frc_context* c, unsigned world, unsigned) {
+  return 2 * static_cast<size_t>(world) * kMaxTokens * c->g.hidden * 2 * sizeof(float);
 }
 
 int frc_peer_export(frc_context* c, unsigned world, void* handle) {

@@ -79,8 +79,8 @@ struct LayerParams {
   unsigned long long* phases;  // FRC_PHASES builds: [cta][16] globaltimer stamps
   // In-box reduce over peer memory (world > 1): every rank's inbox as mapped
   // here (peer[rank] is this rank's own), this rank, and this context's
-  // per-CTA count of such launches.  Inbox: slots [2][world][16][d] f32, then
-  // flags [world][peer_gmax] u32.
+  // per-CTA count of such launches (the epoch).  Inbox: [2][world][16][d]
+  // 8-byte entries {value, epoch}.
   uint8_t* peer[kMaxPeers];
   unsigned rank, world, peer_gmax;
   unsigned* epoch;
@@ -728,17 +728,16 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
 
   // --------------------------------------------- in-box reduce over NVLink
   // This CTA's rows of every token (this GPU's partial, s_ylocal) go to the
-  // same rows of every rank's inbox with plain stores (peer memory over
-  // NVLink; no multicast), then a release store of this launch's epoch to the
-  // rank's flag for (this rank, this CTA).  Once every rank's flag for this
-  // CTA reads the epoch (bounded wait) the rows are summed in rank order, so
-  // y is identical on every rank.  Slots alternate by epoch parity: a rank
-  // reuses a slot only after every rank has signalled the launch after the
-  // one that read it.
+  // same rows of every rank's inbox, each value in one 8-byte store together
+  // with this launch's epoch (peer memory over NVLink; no multicast, no
+  // fence: value and epoch land together).  The receiving thread polls its
+  // own inbox until every rank's entry carries the epoch (bounded wait) and
+  // sums the ranks in rank order, so y is identical on every rank.  Slots
+  // alternate by epoch parity: a rank writes a slot again only two launches
+  // later, after every rank has read it.
   auto peer_reduce = [&](unsigned y0, unsigned R) -> bool {
     const unsigned W = a.world;
-    const size_t slot_bytes = static_cast<size_t>(kMaxTokens) * d * sizeof(float);  // one source's [16][d]
-    const size_t flags_off = 2 * static_cast<size_t>(W) * slot_bytes;
+    const size_t slot_entries = static_cast<size_t>(kMaxTokens) * d;  // one source's [16][d] entries of 8 bytes
     if (tid == 0) {
       const unsigned e = a.epoch[cta] + 1;
       a.epoch[cta] = e;
@@ -749,40 +748,46 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
     const Div by_tr(T * R), by_r2(R);
     for (unsigned q = tid; q < W * T * R; q += kLayerThreads) {
       const unsigned dst = by_tr.q(q), rem = q - dst * T * R, t = by_r2.q(rem), rr = rem - t * R;
-      float* slot = reinterpret_cast<float*>(a.peer[dst] + (static_cast<size_t>(par) * W + a.rank) * slot_bytes) +
+      if (dst == a.rank) continue;  // this rank's own share is read from shared memory
+      uint2* slot = reinterpret_cast<uint2*>(a.peer[dst]) + (static_cast<size_t>(par) * W + a.rank) * slot_entries +
                     static_cast<size_t>(t) * d + y0 + rr;
-      *slot = s_ylocal[t * R + rr];
+      // one aligned 64-bit access: value (low word) and epoch (high word) are seen together
+      const unsigned long long word =
+          static_cast<unsigned long long>(__float_as_uint(s_ylocal[t * R + rr])) | static_cast<unsigned long long>(e) << 32;
+      asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(slot), "l"(word) : "memory");
     }
-    __syncthreads();
-    bool ok = true;
-    if (tid < W) {  // the release store is cumulative: it orders the whole CTA's slot stores (bar.sync above)
-      unsigned* flag = reinterpret_cast<unsigned*>(a.peer[tid] + flags_off) + a.rank * a.peer_gmax + cta;
-      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(e) : "memory");
-      const unsigned* mine = reinterpret_cast<const unsigned*>(a.peer[a.rank] + flags_off) + tid * a.peer_gmax + cta;
-      const uint64_t start = globaltimer();
-      for (;;) {
-        unsigned v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
-        if (static_cast<int>(v - e) >= 0) break;
-        if (globaltimer() - start > kWaitNs) {
-          ok = false;
-          break;
+    const uint2* inbox = reinterpret_cast<const uint2*>(a.peer[a.rank]) + static_cast<size_t>(par) * W * slot_entries;
+    bool bad_y = false, ok = true;
+    const uint64_t start = globaltimer();
+    for (unsigned q = tid; q < T * R && ok; q += kLayerThreads) {
+      const unsigned t = by_r2.q(q), rr = q - t * R;
+      float yv = 0.0f;
+      for (unsigned src = 0; src < W; ++src) {
+        float v;
+        if (src == a.rank) {
+          v = s_ylocal[t * R + rr];
+        } else {
+          const uint2* ent = inbox + static_cast<size_t>(src) * slot_entries + static_cast<size_t>(t) * d + y0 + rr;
+          unsigned long long word;
+          unsigned spins = 0;
+          for (;;) {
+            asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(word) : "l"(ent) : "memory");
+            if (static_cast<unsigned>(word >> 32) == e) break;
+            if ((++spins & 63) == 0 && globaltimer() - start > kWaitNs) {
+              ok = false;
+              break;
+            }
+          }
+          v = __uint_as_float(static_cast<unsigned>(word));
         }
+        yv = __fadd_rn(yv, v);
       }
+      bad_y |= !isfinite(yv);
+      a.y[static_cast<size_t>(t) * d + y0 + rr] = yv;
     }
     if (!__syncthreads_and(ok)) {
       if (tid == 0) atomicOr(a.status, kStTimeout);
       return false;
-    }
-    const float* inbox = reinterpret_cast<const float*>(a.peer[a.rank]) + static_cast<size_t>(par) * W * kMaxTokens * d;
-    bool bad_y = false;
-    for (unsigned q = tid; q < T * R; q += kLayerThreads) {
-      const unsigned t = by_r2.q(q), rr = q - t * R;
-      float yv = 0.0f;
-      for (unsigned src = 0; src < W; ++src)
-        yv = __fadd_rn(yv, __ldcg(inbox + (static_cast<size_t>(src) * kMaxTokens + t) * d + y0 + rr));
-      bad_y |= !isfinite(yv);
-      a.y[static_cast<size_t>(t) * d + y0 + rr] = yv;
     }
     if (bad_y) atomicOr(a.status, kStNumeric);
     return true;
