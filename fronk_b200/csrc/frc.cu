@@ -189,6 +189,8 @@ struct frc_context {
   unsigned long long* phases = nullptr;
   LayerCtl* ctl = nullptr;
   unsigned* status = nullptr;
+  float* xchg = nullptr;    // split items: hidden values [item][32]
+  unsigned* xcnt = nullptr; // and the parts that wrote them [item]
   // frc_run staging: one copy in ([x][gate][expert], packed for the call's
   // token count) and one copy out ([status word, 16 B][y]).
   uint8_t *d_in = nullptr, *d_out = nullptr, *h_in = nullptr, *h_out = nullptr;
@@ -198,9 +200,9 @@ struct frc_context {
   uint8_t* pool = nullptr;
   unsigned pool_count = 0;
   unsigned long long launches = 0;
-  bool attr_set[2] = {};
-  unsigned occ_smem[2] = {};
-  int occ_val[2] = {};
+  bool attr_set[2][2] = {};   // [activation mode][split variant]
+  unsigned occ_smem[2][2] = {};
+  int occ_val[2][2] = {};
   unsigned last_T = 0, last_S = 0, last_G = 0;
   // in-box reduce: this rank's inbox (IPC-exported), every rank's inbox as
   // mapped here, the per-CTA launch counters
@@ -345,29 +347,36 @@ static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, u
 
 template <int ACT>
 static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s, bool overlap) {
-  auto kern = moe_layer_kernel<ACT>;
   const int ai = ACT == FRC_ACT_Q8;
-  if (!c->attr_set[ai]) {
-    CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-    c->attr_set[ai] = true;
-  }
-  // Two CTAs an SM when their shared memory fits, else one; all resident
-  // (the kernel has a grid barrier).
-  auto occupancy = [&](unsigned bytes, int* per_sm) -> int {
-    if (c->occ_smem[ai] == bytes) {
-      *per_sm = c->occ_val[ai];
+  auto prepare = [&](void (*kern)(LayerParams), int split) -> int {
+    if (!c->attr_set[ai][split]) {
+      CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+      c->attr_set[ai][split] = true;
+    }
+    return FRC_OK;
+  };
+  // CTAs an SM for `bytes` of shared memory (cached: it depends only on the
+  // kernel variant and the size)
+  auto occupancy = [&](void (*kern)(LayerParams), int split, unsigned bytes, int* per_sm) -> int {
+    if (c->occ_smem[ai][split] == bytes) {
+      *per_sm = c->occ_val[ai][split];
       return FRC_OK;
     }
     CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, kern, kLayerThreads, bytes));
-    c->occ_smem[ai] = bytes;
-    c->occ_val[ai] = *per_sm;
+    c->occ_smem[ai][split] = bytes;
+    c->occ_val[ai][split] = *per_sm;
     return FRC_OK;
   };
+  auto kern = moe_layer_kernel<ACT, false>;
+  int orc;
+  if ((orc = prepare(kern, 0))) return orc;
+  // Two CTAs an SM when their shared memory fits, else one; all resident
+  // (the kernel has a grid barrier).
   unsigned per = 2, G = 2 * static_cast<unsigned>(c->sms);
-  int per_sm = 0, orc;
+  int per_sm = 0;
   bool fits = smem_layout(c, a.T, G, ACT, kSmemTwoPerSm, &a.sm);
   if (fits) {
-    if ((orc = occupancy(a.sm.total, &per_sm))) return orc;
+    if ((orc = occupancy(kern, 0, a.sm.total, &per_sm))) return orc;
     fits = per_sm >= 2;
   }
   if (!fits) {
@@ -375,13 +384,39 @@ static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s, bool ove
     G = static_cast<unsigned>(c->sms);
     if (!smem_layout(c, a.T, G, ACT, kSmemOnePerSm, &a.sm))
       return fail(c, FRC_INVALID, "%u tokens need too much shared memory", a.T);
-    if ((orc = occupancy(a.sm.total, &per_sm))) return orc;
+    if ((orc = occupancy(kern, 0, a.sm.total, &per_sm))) return orc;
   }
   if (per_sm < static_cast<int>(per)) return fail(c, FRC_INVALID, "layer kernel does not fit an SM (%u bytes)", a.sm.total);
-  // Co-residency of the grid (one CTA per SM, checked above) is what the grid
-  // barrier needs.  A plain launch asks the runtime to check it; an overlapped
-  // launch (programmatic stream serialization) gets it as the previous
-  // launch's CTAs leave their SMs.
+  // One token and few items (slices split over several GPUs): split each
+  // item in H parts on H CTAs when all parts fit one round of the grid, so
+  // the weight stream and the chain of each CTA shrink with the item.
+  a.H = 1;
+  a.Hshift = 0;
+  if (a.T == 1)
+    for (unsigned h = 4, sh = 2; h > 1; h >>= 1, --sh)
+      if (h * 11 * a.S <= G && (32 / a.sm.kn_r) % h == 0 && (32 / a.sm.kn_s) % h == 0) {
+        a.H = h;
+        a.Hshift = sh;
+        break;
+      }
+  if (a.H > 1) {
+    auto ks = moe_layer_kernel<ACT, true>;
+    int ps = 0;
+    if ((orc = prepare(ks, 1)) || (orc = occupancy(ks, 1, a.sm.total, &ps))) return orc;
+    if (ps >= static_cast<int>(per)) kern = ks;
+    else { a.H = 1; a.Hshift = 0; }  // the split variant does not fit as many CTAs
+  }
+  {
+    const unsigned d = a.d, H = a.H;
+    a.sm.mag_ch_r = div_magic(32 / a.sm.kn_r / H + (d / H + a.sm.dn_r - 1) / a.sm.dn_r);
+    a.sm.mag_ch_s = div_magic(32 / a.sm.kn_s / H + (d / H + a.sm.dn_s - 1) / a.sm.dn_s);
+  }
+  a.xchg = c->xchg;
+  a.xcnt = c->xcnt;
+  // Co-residency of the grid (checked above) is what the grid barrier needs.
+  // A plain launch asks the runtime to check it; an overlapped launch
+  // (programmatic stream serialization) gets it as the previous launch's
+  // CTAs leave their SMs.
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   if (overlap) {
@@ -661,6 +696,8 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
   alloc(reinterpret_cast<void**>(&c->partial), sizeof(float) * kMaxPairs * kMaxBlocks * d);
   alloc(reinterpret_cast<void**>(&c->gsv), sizeof(float) * kMaxPairs * kMaxBlocks);
   alloc(reinterpret_cast<void**>(&c->ctl), sizeof(LayerCtl));
+  alloc(reinterpret_cast<void**>(&c->xchg), sizeof(float) * kMaxUnique * 32);
+  alloc(reinterpret_cast<void**>(&c->xcnt), sizeof(unsigned) * kMaxUnique);
   alloc(reinterpret_cast<void**>(&c->phases), sizeof(unsigned long long) * 16 * 1024);
   const size_t in_bytes = kInBytesPerToken(d) * FRC_MAX_PREFILL_TOKENS,
                out_bytes = 16 + sizeof(float) * FRC_MAX_PREFILL_TOKENS * d;
@@ -693,6 +730,7 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
     c->h_y = reinterpret_cast<float*>(c->h_out + 16);
   }
   if (rc == FRC_OK && (cudaMemset(c->ctl, 0, sizeof(LayerCtl)) != cudaSuccess ||
+                       cudaMemset(c->xcnt, 0, sizeof(unsigned) * kMaxUnique) != cudaSuccess ||
                        cudaMemset(c->status, 0, sizeof(unsigned)) != cudaSuccess ||
                        cudaMemset(c->hidden, 0, kHiddenBytes) != cudaSuccess))
     rc = fail(c, FRC_IO, "cudaMemset");
@@ -712,6 +750,7 @@ int frc_close(frc_context* c) {
   for (auto& b : c->layer_ptr)
     for (auto& p : b) if (p) cudaFree(p);
   cudaFree(c->staging); cudaFree(c->hidden); cudaFree(c->partial); cudaFree(c->gsv); cudaFree(c->phases); cudaFree(c->ctl);
+  cudaFree(c->xchg); cudaFree(c->xcnt);
   cudaFree(c->d_in); cudaFree(c->d_out); cudaFree(c->pool);
   cudaFree(c->pf_xq); cudaFree(c->pf_xs); cudaFree(c->pf_pair_token); cudaFree(c->pf_slot_pair); cudaFree(c->pf_counts);
   cudaFree(c->pf_items_gu); cudaFree(c->pf_items_dn); cudaFree(c->pf_hq); cudaFree(c->pf_hs); cudaFree(c->pf_ye);
@@ -841,7 +880,10 @@ int frc_run(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* exp
   CK(cudaMemsetAsync(c->status, 0, sizeof(unsigned), c->stream));
   CK(cudaStreamSynchronize(c->stream));
   const unsigned st = *c->h_status;
-  if (st & kStTimeout) CK(cudaMemset(c->ctl, 0, sizeof(LayerCtl)));  // nothing runs now
+  if (st & kStTimeout) {  // nothing runs now
+    CK(cudaMemset(c->ctl, 0, sizeof(LayerCtl)));
+    CK(cudaMemset(c->xcnt, 0, sizeof(unsigned) * kMaxUnique));
+  }
   if (status_code(st)) return fail(c, status_code(st), "device status 0x%x", st);
   memcpy(y, c->h_y, xb);  // published only after the whole layer succeeded
   return FRC_OK;
@@ -959,7 +1001,10 @@ int frc_status(frc_context* c, void* stream) {
   CK(cudaMemsetAsync(c->status, 0, sizeof(unsigned), s));
   CK(cudaStreamSynchronize(s));
   const int rc = status_code(*c->h_status);
-  if (*c->h_status & kStTimeout) CK(cudaMemset(c->ctl, 0, sizeof(LayerCtl)));  // nothing runs now
+  if (*c->h_status & kStTimeout) {  // nothing runs now
+    CK(cudaMemset(c->ctl, 0, sizeof(LayerCtl)));
+    CK(cudaMemset(c->xcnt, 0, sizeof(unsigned) * kMaxUnique));
+  }
   if (rc) return fail(c, rc, "device status 0x%x", *c->h_status);
   return FRC_OK;
 }

@@ -84,6 +84,13 @@ struct LayerParams {
   uint8_t* peer[kMaxPeers];
   unsigned rank, world, peer_gmax;
   unsigned* epoch;
+  // Items split in H parts (1, 2 or 4; one token, one round of parts): part
+  // h takes neurons [32h/H, 32(h+1)/H) of the slice and down rows
+  // [dh/H, d(h+1)/H); the parts' hidden values meet in xchg [item][32]
+  // (xcnt[item] counts the parts that wrote, reset after the grid barrier).
+  unsigned H, Hshift;
+  float* xchg;
+  unsigned* xcnt;
   LayerSmem sm;
   unsigned S, T, d, norm;
   unsigned mag_S;  // div_magic(S)
@@ -147,7 +154,9 @@ __device__ __forceinline__ bool grid_sync(LayerCtl* ctl, unsigned* flag_smem) {
 #endif
 #define PHASE(k) PHASE_AT(k, 0)
 
-template <int ACT>
+// SPLIT: items may be split in a.H parts (one token); without it H is 1 at
+// compile time and the split's bookkeeping folds away.
+template <int ACT, bool SPLIT>
 __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const LayerParams a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);                // kMaxSlots mbarriers
@@ -182,13 +191,18 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
   unsigned UR = 0, SH = 0, U = 0, NI = 0, n_my = 0, nsh = 0, n_ch = 0;
   auto item_at = [&](unsigned r) { return r * G + ((r & 1) ? G - 1 - cta : cta); };
   const Div by_S(S, a.mag_S);
-  auto item_us = [&](unsigned j, unsigned& u, unsigned& s) {
-    if (j < SH) { u = UR; s = j; }
-    else { u = by_S.q(j - SH); s = j - SH - u * S; }
+  const unsigned H = SPLIT ? a.H : 1u, Hs = SPLIT ? a.Hshift : 0u;
+  // part j -> item (u, s) and part h; the item's index ji in item order
+  auto item_us = [&](unsigned j, unsigned& u, unsigned& s, unsigned& h, unsigned& ji) {
+    ji = j >> Hs;
+    h = j & (H - 1);
+    if (ji < SH) { u = UR; s = ji; }
+    else { u = by_S.q(ji - SH); s = ji - SH - u * S; }
   };
   const unsigned kn_r = a.sm.kn_r, kn_s = a.sm.kn_s, dn_r = a.sm.dn_r, dn_s = a.sm.dn_s;
-  const unsigned ngu_r = 32 / kn_r, ngu_s = 32 / kn_s;
-  const unsigned ndn_r = (d + dn_r - 1) / dn_r, ndn_s = (d + dn_s - 1) / dn_s;
+  const unsigned ngu_r = 32 / kn_r / H, ngu_s = 32 / kn_s / H;  // gate/up chunks a part
+  const unsigned dpart = d / H;                                  // down rows a part
+  const unsigned ndn_r = (dpart + dn_r - 1) / dn_r, ndn_s = (dpart + dn_s - 1) / dn_s;
   const unsigned ch_r = ngu_r + ndn_r, ch_s = ngu_s + ndn_s;
   const Div by_ch_r(ch_r, a.sm.mag_ch_r), by_ch_s(ch_s, a.sm.mag_ch_s);
   const unsigned ss_r = a.down_type == kQ80 ? 2 : 1, pb_r = a.down_type == kQ80 ? 32 : 16;
@@ -196,11 +210,11 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
     UR = misc[4];
     U = UR + (misc[5] ? 1 : 0);
     SH = misc[5] ? S : 0;
-    NI = U * S;
+    NI = U * S * H;
     n_my = 0;
     while (item_at(n_my) < NI) ++n_my;
     nsh = 0;
-    while (nsh < n_my && item_at(nsh) < SH) ++nsh;
+    while (nsh < n_my && item_at(nsh) < SH * H) ++nsh;
     n_ch = nsh * ch_s + (n_my - nsh) * ch_r;
   };
 
@@ -212,9 +226,9 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
   // Gate/up chunk k: gate rows k*kn.. then up rows k*kn.. (two copies).
   // Down chunk: rows [r0, r0+nr): their scales, then their payloads.
   auto issue = [&](unsigned c) {
-    unsigned r, k, u, s;
+    unsigned r, k, u, s, h, ji;
     chunk_at(c, r, k);
-    item_us(item_at(r), u, s);
+    item_us(item_at(r), u, s, h, ji);
     const bool sh = u >= UR;
     const unsigned rowb = sh ? a.shared_row : a.row_bytes, proj = sh ? a.shared_proj : a.proj_bytes;
     const unsigned kn = sh ? kn_s : kn_r, ngu = sh ? ngu_s : ngu_r, dn = sh ? dn_s : dn_r;
@@ -223,12 +237,12 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
     const unsigned slot = c % K;
     uint8_t* dst = ring + slot * SLOT;
     if (k < ngu) {
-      const unsigned bytes = kn * rowb;
+      const unsigned bytes = kn * rowb, kg = h * ngu + k;  // chunk of the slice's neurons
       mbar_expect_tx(&full[slot], 2 * bytes);
-      bulk_g2s(dst, src + k * bytes, bytes, &full[slot]);
-      bulk_g2s(dst + bytes, src + proj + k * bytes, bytes, &full[slot]);
+      bulk_g2s(dst, src + kg * bytes, bytes, &full[slot]);
+      bulk_g2s(dst + bytes, src + proj + kg * bytes, bytes, &full[slot]);
     } else {
-      const unsigned r0 = (k - ngu) * dn, nr = min(dn, d - r0);
+      const unsigned r0 = h * dpart + (k - ngu) * dn, nr = min(dn, (h + 1) * dpart - r0);
       const uint8_t* down = src + 2 * proj;
       mbar_expect_tx(&full[slot], nr * (ss + pb));
       bulk_g2s(dst, down + r0 * ss, nr * ss, &full[slot]);
@@ -538,8 +552,8 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
   unsigned c = 0;
   bool bad = false;
   for (unsigned r = 0; r < n_my && !aborted; ++r) {
-    unsigned u, s;
-    item_us(item_at(r), u, s);
+    unsigned u, s, h, ji;
+    item_us(item_at(r), u, s, h, ji);
     const bool sh = u >= UR;
     const unsigned type = sh ? kQ80 : a.gate_type, dtype = sh ? kQ80 : a.down_type;
     const unsigned rowb = sh ? a.shared_row : a.row_bytes, nb = d / 32;
@@ -559,7 +573,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
         const unsigned nl = 4 * (warp % quads) + (lane >> 3);  // neuron within the chunk
         const uint8_t* gr = slot + nl * rowb;
         const uint8_t* ur = slot + (kn + nl) * rowb;
-        const unsigned n = k * kn + nl;
+        const unsigned n = (h * ngu + k) * kn + nl;
         unsigned mm = mask;
         for (unsigned kk = 0; kk < nt; ++kk) {
           const unsigned t = __ffs(mm) - 1;
@@ -620,6 +634,23 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
     }
     if (r == 0) PHASE(9);
     if (__syncthreads_or(timed_out)) { aborted = true; break; }
+    if (SPLIT && H > 1) {
+      // one token: this part's hidden values go to the item's exchange row;
+      // wait (bounded) until all H parts wrote theirs, then take the others
+      const unsigned nn = 32 / H, n0 = h * nn;
+      if (tid < nn) a.xchg[ji * 32 + n0 + tid] = s_gv[n0 + tid];
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) {
+        atomicAdd(&a.xcnt[ji], 1u);
+        bool ok = spin_geq(&a.xcnt[ji], H, &a.ctl->abort);
+        misc[8] = ok ? 1u : 0u;
+      }
+      __syncthreads();
+      if (!misc[8]) { timed_out = true; aborted = true; break; }
+      if (tid < 32 && (tid < n0 || tid >= n0 + nn)) s_gv[tid] = __ldcg(a.xchg + ji * 32 + tid);
+      __syncthreads();
+    }
     // the hidden slice's Q8 quantization (src/q4.c:37-61, one group of 32)
     for (unsigned kk = warp; kk < nt; kk += kLayerWarps) {
       unsigned mm = mask;
@@ -645,7 +676,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
     if (r == 0) PHASE(13);
     // down: rows of chunk k, one a thread; c = scale * int_dot (or the fp32 dot)
     for (unsigned k = 0; k < ndn; ++k, ++c) {
-      const unsigned r0 = k * dn, nr = min(dn, d - r0);
+      const unsigned r0 = h * dpart + k * dn, nr = min(dn, (h + 1) * dpart - r0);
       float* out = a.partial + (static_cast<size_t>(gp0) * S + s) * d + r0;
       if (wait_chunk(c)) {
         if (r == 0 && k == 0) PHASE(14);
@@ -725,6 +756,13 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
     if (tid == 0) atomicOr(a.status, kStTimeout);
   }
   PHASE(5);
+  // every part has passed its exchange: the item's first part clears the count
+  if (SPLIT && H > 1 && !aborted && tid == 0)
+    for (unsigned r = 0; r < n_my; ++r) {
+      unsigned u, s, h, ji;
+      item_us(item_at(r), u, s, h, ji);
+      if (h == 0) a.xcnt[ji] = 0;
+    }
 
   // --------------------------------------------- in-box reduce over NVLink
   // This CTA's rows of every token (this GPU's partial, s_ylocal) go to the
