@@ -375,6 +375,11 @@ static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s, bool ove
   unsigned per = 2, G = 2 * static_cast<unsigned>(c->sms);
   int per_sm = 0;
   bool fits = smem_layout(c, a.T, G, ACT, kSmemTwoPerSm, &a.sm);
+  // Two CTAs an SM only while each keeps a full ring (eight-neuron gate/up
+  // chunks, four slots): with more tokens the activations crowd the ring out
+  // and a CTA waits on its own refills (16 tokens ran 35 % faster on one CTA
+  // an SM with its larger ring; 4 and 8 tokens ran faster on two).
+  if (fits) fits = a.sm.kn_r >= 8 && a.sm.slots >= 4;
   if (fits) {
     if ((orc = occupancy(kern, 0, a.sm.total, &per_sm))) return orc;
     fits = per_sm >= 2;
