@@ -418,6 +418,7 @@ static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s, bool ove
   }
   a.xchg = c->xchg;
   a.xcnt = c->xcnt;
+  a.bar_inc = 2 * static_cast<unsigned>(c->sms) / G;  // G is one or two CTAs an SM
   // Co-residency of the grid (checked above) is what the grid barrier needs.
   // A plain launch asks the runtime to check it; an overlapped launch
   // (programmatic stream serialization) gets it as the previous launch's

@@ -84,6 +84,9 @@ struct LayerParams {
   uint8_t* peer[kMaxPeers];
   unsigned rank, world, peer_gmax;
   unsigned* epoch;
+  // Grid barrier arrivals a CTA adds: (2 x SMs) / grid, so that every launch
+  // adds the same total whatever its grid (one or two CTAs an SM).
+  unsigned bar_inc;
   // Items split in H parts (1, 2 or 4; one token, one round of parts): part
   // h takes neurons [32h/H, 32(h+1)/H) of the slice and down rows
   // [dh/H, d(h+1)/H); the parts' hidden values meet in xchg [item][32]
@@ -117,15 +120,18 @@ __device__ __forceinline__ void act_sync() { asm volatile("bar.sync 1, 128;" :::
 __device__ __forceinline__ void plan_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 
 // Bounded barrier over the co-resident grid, one round trip: every CTA adds
-// itself to a counter that only grows and waits for the next multiple of the
-// grid size.  A timed-out launch leaves the counter off that lattice;
-// frc_status zeroes it before anything runs again.
-__device__ __forceinline__ bool grid_sync(LayerCtl* ctl, unsigned* flag_smem) {
+// `inc` to a counter that only grows and waits for the next multiple of the
+// launch's total (grid x inc, the same for every launch, so launches of one
+// and of two CTAs an SM may follow each other in any order).  A timed-out
+// launch leaves the counter off that lattice; frc_status zeroes it before
+// anything runs again.
+__device__ __forceinline__ bool grid_sync(LayerCtl* ctl, unsigned* flag_smem, unsigned inc) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    const unsigned long long old = atomicAdd(&ctl->arrived, 1ull);
-    const unsigned long long target = (old / gridDim.x + 1) * gridDim.x;
+    const unsigned long long span = static_cast<unsigned long long>(gridDim.x) * inc;
+    const unsigned long long old = atomicAdd(&ctl->arrived, static_cast<unsigned long long>(inc));
+    const unsigned long long target = (old / span + 1) * span;
     bool ok = true;
     const uint64_t start = globaltimer();
     unsigned spins = 0;
@@ -751,7 +757,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
       atomicOr(a.status, kStTimeout);
       atomicExch(&a.ctl->abort, 1u);
     }
-  } else if (!grid_sync(a.ctl, misc + 3)) {
+  } else if (!grid_sync(a.ctl, misc + 3, a.bar_inc)) {
     aborted = true;
     if (tid == 0) atomicOr(a.status, kStTimeout);
   }

@@ -113,6 +113,25 @@ def test_layer_q8_all_twenty_slices(gpu, oracle):
         assert max(rel_l2(r, a) for r, a in zip(y_ref, y)) <= TOL
 
 
+def test_grid_sizes_alternate_on_one_context(gpu, oracle):
+    """16 tokens launch one CTA an SM, one token two: alternating them on one
+    context, an odd number of each in a row, keeps the grid barrier whole
+    and the results right."""
+    hidden = 2048
+    g = fb.geometry(hidden)
+    cases = [request(hidden, t, SEED + 500 + i, 0.0) for i, t in enumerate((16, 1, 1, 16, 16, 1, 16, 1))]
+    experts = np.concatenate([c[0].ravel() for c in cases])
+    with fb.Context(0, hidden) as ctx:
+        layers = _setup(ctx, g, list(range(20)), experts, 2)
+        m = oracle.model(hidden, Q4_K, MXFP4, layers)
+        for e, gate, x in cases:
+            rc, y = ctx.run(2, e, gate, x, fb.ACT_Q8)
+            assert rc == OK, ctx.last_error
+            rc, y_ref, _ = oracle.port_run(m, e, gate, x)
+            assert rc == OK
+            assert max(rel_l2(r, a) for r, a in zip(y_ref, y)) <= TOL
+
+
 @pytest.mark.parametrize("hidden,gt,dt", CONFIGS)
 def test_layer_f32_matches_reference_arithmetic(gpu, oracle, hidden, gt, dt):
     g = fb.geometry(hidden, 48, gt, dt)
