@@ -168,6 +168,12 @@ struct Q8Group {
     v = rintf(v);
     return static_cast<int>(fminf(fmaxf(v, -127.0f), 127.0f));
   }
+  // q(x) when mul_ok(): the multiply form alone.  Callers branch once per
+  // group on mul_ok() so the division fallback stays out of the hot code.
+  __device__ __forceinline__ bool mul_ok() const { return inv_ok && scale != 0.0f; }
+  __device__ __forceinline__ int qm(float x) const {
+    return static_cast<int>(fminf(fmaxf(rintf(__fmul_rn(x, inv)), -127.0f), 127.0f));
+  }
 };
 
 // Position of element n (0..31) of a 32-weight block in the "prmt order" that

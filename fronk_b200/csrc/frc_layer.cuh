@@ -160,6 +160,93 @@ __device__ __forceinline__ bool grid_sync(LayerCtl* ctl, unsigned* flag_smem, un
 #endif
 #define PHASE(k) PHASE_AT(k, 0)
 
+// One lane's gate and up sums over its 256-weight spans q = l8, l8+8, ...
+// (Q8 activations, groups in order).  One instantiation per weight type, so
+// the code a launch runs is one contiguous block.
+template <unsigned TYPE>
+__device__ __forceinline__ void gu_sums(const uint8_t* gr, const uint8_t* ur, const uint8_t* xq, const float* xs,
+                                        const float* xv, unsigned l8, unsigned nspan, unsigned nb, bool& bad,
+                                        float& ag, float& au) {
+  for (unsigned q = l8; q < nspan; q += 8) {
+#pragma unroll
+    for (unsigned gp = 0; gp < 4; ++gp) {
+      const unsigned p = 4 * q + gp;
+      uint32_t xw[16];
+      load_x16(xq, p, nspan, xw);
+      float tg, tu;
+      if (TYPE == kQ4K) {
+        const float v0 = xv[2 * p], v1 = xv[2 * p + 1];
+        tg = term_q4k(gr, p, xw, v0, v1, bad);
+        tu = term_q4k(ur, p, xw, v0, v1, bad);
+      } else if (TYPE == kMXFP4) {
+        tg = term_mxfp4(gr, nb, p, xw, bad);
+        tu = term_mxfp4(ur, nb, p, xw, bad);
+      } else {
+        tg = term_q80(gr, nb, p, xw, bad);
+        tu = term_q80(ur, nb, p, xw, bad);
+      }
+      ag = __fmaf_rn(xs[p], tg, ag);
+      au = __fmaf_rn(xs[p], tu, au);
+    }
+  }
+}
+
+// Down term c of row rr of a staged down chunk ([nr scales][nr payloads]),
+// hidden slice kk: scale x int_dot (Q8 hidden) or the fp32 dot.  One
+// instantiation per weight type.
+template <unsigned DT, int ACT>
+__device__ __forceinline__ float down_term(const uint8_t* slot, unsigned nr, unsigned rr, const uint8_t* s_hq,
+                                           unsigned kk, bool& bad) {
+  if (DT == kMXFP4) {
+    const unsigned e = slot[rr];
+    bad |= e == 255;
+    const uint4 w = *reinterpret_cast<const uint4*>(slot + nr + 16 * rr);
+    if (ACT == FRC_ACT_Q8) {
+      const uint4 h0 = reinterpret_cast<const uint4*>(s_hq)[2 * kk];
+      const uint4 h1 = reinterpret_cast<const uint4*>(s_hq)[2 * kk + 1];
+      const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+      return __fmul_rn(pow2_m128(e), i2f(idot_mxfp4_16(w, hw)));
+    }
+    const float* hv = reinterpret_cast<const float*>(s_hq) + kk * 32;
+    const float sc = __uint_as_float(e ? e << 23 : 0x00400000u);
+    const uint8_t* qb = slot + nr + 16 * rr;
+    float dot = 0.0f;
+    for (unsigned nn = 0; nn < 32; ++nn)
+      dot = __fmaf_rn(__fmul_rn(sc, e2m1((qb[nn & 15] >> (nn >> 4 ? 4 : 0)) & 15)), hv[nn], dot);
+    return dot;
+  }
+  const float sw = h2f(slot[2 * rr] | slot[2 * rr + 1] << 8);
+  bad |= !isfinite(sw);
+  if (ACT == FRC_ACT_Q8) {
+    const uint4* wv = reinterpret_cast<const uint4*>(slot + 2 * nr + 32 * rr);
+    const uint4 w0 = wv[0], w1 = wv[1];
+    const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    const uint4 h0 = reinterpret_cast<const uint4*>(s_hq)[2 * kk];
+    const uint4 h1 = reinterpret_cast<const uint4*>(s_hq)[2 * kk + 1];
+    const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    int iv = 0;
+#pragma unroll
+    for (unsigned m = 0; m < 8; ++m) iv = __dp4a(static_cast<int>(ww[m]), static_cast<int>(hw[m]), iv);
+    return __fmul_rn(sw, i2f(iv));
+  }
+  const float* hv = reinterpret_cast<const float*>(s_hq) + kk * 32;
+  const int8_t* qb = reinterpret_cast<const int8_t*>(slot + 2 * nr + 32 * rr);
+  float dot = 0.0f;
+  for (unsigned nn = 0; nn < 32; ++nn) dot = __fmaf_rn(__fmul_rn(sw, static_cast<float>(qb[nn])), hv[nn], dot);
+  return dot;
+}
+
+// One token: this thread's rows tid + j x kLayerThreads (j < 4) of a down chunk.
+template <unsigned DT, int ACT>
+__device__ __forceinline__ void down_terms4(const uint8_t* slot, unsigned nr, const uint8_t* s_hq, bool& bad,
+                                            float& h0, float& h1, float& h2, float& h3) {
+  const unsigned tid = threadIdx.x;
+  h0 = tid < nr ? down_term<DT, ACT>(slot, nr, tid, s_hq, 0, bad) : 0.0f;
+  h1 = tid + kLayerThreads < nr ? down_term<DT, ACT>(slot, nr, tid + kLayerThreads, s_hq, 0, bad) : 0.0f;
+  h2 = tid + 2 * kLayerThreads < nr ? down_term<DT, ACT>(slot, nr, tid + 2 * kLayerThreads, s_hq, 0, bad) : 0.0f;
+  h3 = tid + 3 * kLayerThreads < nr ? down_term<DT, ACT>(slot, nr, tid + 3 * kLayerThreads, s_hq, 0, bad) : 0.0f;
+}
+
 // SPLIT: items may be split in a.H parts (one token); without it H is 1 at
 // compile time and the split's bookkeeping folds away.
 template <int ACT, bool SPLIT>
@@ -503,10 +590,18 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
       const Q8Group qg(amax);
       int qv[16], sum = 0;
+      if (__builtin_expect(qg.mul_ok(), 1)) {
 #pragma unroll
-      for (unsigned k = 0; k < 16; ++k) {
-        qv[k] = qg.q(v[k]);
-        sum += qv[k];
+        for (unsigned k = 0; k < 16; ++k) {
+          qv[k] = qg.qm(v[k]);
+          sum += qv[k];
+        }
+      } else {
+#pragma unroll
+        for (unsigned k = 0; k < 16; ++k) {
+          qv[k] = qg.q(v[k]);
+          sum += qv[k];
+        }
       }
       sum += __shfl_xor_sync(0xffffffffu, sum, 1);  // quarters 0+1 and 2+3: the two 32-element halves
       uint32_t w[4];
@@ -589,28 +684,9 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
             const uint8_t* xq = smem + (type == kMXFP4 ? a.sm.xp : a.sm.xq) + t * d;
             const float* xs = reinterpret_cast<const float*>(smem + a.sm.xs) + t * P;
             const float* xv = reinterpret_cast<const float*>(smem + a.sm.xv) + t * 2 * P;
-            for (unsigned q = l8; q < nspan; q += 8) {
-#pragma unroll
-              for (unsigned gp = 0; gp < 4; ++gp) {
-                const unsigned p = 4 * q + gp;
-                uint32_t xw[16];
-                load_x16(xq, p, nspan, xw);
-                float tg, tu;
-                if (type == kQ4K) {
-                  const float v0 = xv[2 * p], v1 = xv[2 * p + 1];
-                  tg = term_q4k(gr, p, xw, v0, v1, bad);
-                  tu = term_q4k(ur, p, xw, v0, v1, bad);
-                } else if (type == kMXFP4) {
-                  tg = term_mxfp4(gr, nb, p, xw, bad);
-                  tu = term_mxfp4(ur, nb, p, xw, bad);
-                } else {
-                  tg = term_q80(gr, nb, p, xw, bad);
-                  tu = term_q80(ur, nb, p, xw, bad);
-                }
-                ag = __fmaf_rn(xs[p], tg, ag);
-                au = __fmaf_rn(xs[p], tu, au);
-              }
-            }
+            if (type == kQ4K) gu_sums<kQ4K>(gr, ur, xq, xs, xv, l8, nspan, nb, bad, ag, au);
+            else if (type == kMXFP4) gu_sums<kMXFP4>(gr, ur, xq, xs, xv, l8, nspan, nb, bad, ag, au);
+            else gu_sums<kQ80>(gr, ur, xq, xs, xv, l8, nspan, nb, bad, ag, au);
           } else {
             const float* xf = reinterpret_cast<const float*>(smem + a.sm.xf) + t * d;
             for (unsigned q = l8; q < nspan; q += 8)
@@ -670,7 +746,8 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
 #pragma unroll
         for (unsigned o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         const Q8Group qg(amax);
-        s_hq[kk * 32 + (dtype == kMXFP4 ? prmt_pos(lane) : lane)] = static_cast<uint8_t>(qg.q(h) & 0xff);
+        const int qh = __builtin_expect(qg.mul_ok(), 1) ? qg.qm(h) : qg.q(h);
+        s_hq[kk * 32 + (dtype == kMXFP4 ? prmt_pos(lane) : lane)] = static_cast<uint8_t>(qh & 0xff);
         gs = __fmul_rn(qg.scale, s_ugate[u * T + t]);
       } else {
         reinterpret_cast<float*>(s_hq)[kk * 32 + lane] = h;
@@ -687,52 +764,12 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
       if (wait_chunk(c)) {
         if (r == 0 && k == 0) PHASE(14);
         const uint8_t* slot = ring + (c % K) * SLOT;
-        auto cterm = [&](unsigned rr, unsigned kk) -> float {
-          if (dtype == kMXFP4) {
-            const unsigned e = slot[rr];
-            bad |= e == 255;
-            const uint4 w = *reinterpret_cast<const uint4*>(slot + nr + 16 * rr);
-            if (ACT == FRC_ACT_Q8) {
-              const uint4 h0 = reinterpret_cast<const uint4*>(s_hq)[2 * kk];
-              const uint4 h1 = reinterpret_cast<const uint4*>(s_hq)[2 * kk + 1];
-              const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-              return __fmul_rn(pow2_m128(e), i2f(idot_mxfp4_16(w, hw)));
-            }
-            const float* hv = reinterpret_cast<const float*>(s_hq) + kk * 32;
-            const float sc = __uint_as_float(e ? e << 23 : 0x00400000u);
-            const uint8_t* qb = slot + nr + 16 * rr;
-            float dot = 0.0f;
-            for (unsigned nn = 0; nn < 32; ++nn)
-              dot = __fmaf_rn(__fmul_rn(sc, e2m1((qb[nn & 15] >> (nn >> 4 ? 4 : 0)) & 15)), hv[nn], dot);
-            return dot;
-          }
-          const float sw = h2f(slot[2 * rr] | slot[2 * rr + 1] << 8);
-          bad |= !isfinite(sw);
-          if (ACT == FRC_ACT_Q8) {
-            const uint4* wv = reinterpret_cast<const uint4*>(slot + 2 * nr + 32 * rr);
-            const uint4 w0 = wv[0], w1 = wv[1];
-            const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-            const uint4 h0 = reinterpret_cast<const uint4*>(s_hq)[2 * kk];
-            const uint4 h1 = reinterpret_cast<const uint4*>(s_hq)[2 * kk + 1];
-            const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-            int iv = 0;
-#pragma unroll
-            for (unsigned m = 0; m < 8; ++m) iv = __dp4a(static_cast<int>(ww[m]), static_cast<int>(hw[m]), iv);
-            return __fmul_rn(sw, i2f(iv));
-          }
-          const float* hv = reinterpret_cast<const float*>(s_hq) + kk * 32;
-          const int8_t* qb = reinterpret_cast<const int8_t*>(slot + 2 * nr + 32 * rr);
-          float dot = 0.0f;
-          for (unsigned nn = 0; nn < 32; ++nn) dot = __fmaf_rn(__fmul_rn(sw, static_cast<float>(qb[nn])), hv[nn], dot);
-          return dot;
-        };
         if (nt == 1 && nr <= 4 * kLayerThreads) {
           // one token, at most four rows a thread: hold the terms in registers,
           // hand the slot back, then store (the release need not wait for them)
-          const float h0 = tid < nr ? cterm(tid, 0) : 0.0f;
-          const float h1 = tid + kLayerThreads < nr ? cterm(tid + kLayerThreads, 0) : 0.0f;
-          const float h2 = tid + 2 * kLayerThreads < nr ? cterm(tid + 2 * kLayerThreads, 0) : 0.0f;
-          const float h3 = tid + 3 * kLayerThreads < nr ? cterm(tid + 3 * kLayerThreads, 0) : 0.0f;
+          float h0, h1, h2, h3;
+          if (dtype == kMXFP4) down_terms4<kMXFP4, ACT>(slot, nr, s_hq, bad, h0, h1, h2, h3);
+          else down_terms4<kQ80, ACT>(slot, nr, s_hq, bad, h0, h1, h2, h3);
           release(c);
           if (tid < nr) out[tid] = h0;
           if (tid + kLayerThreads < nr) out[tid + kLayerThreads] = h1;
@@ -740,8 +777,15 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
           if (tid + 3 * kLayerThreads < nr) out[tid + 3 * kLayerThreads] = h3;
           continue;
         }
-        for (unsigned rr = tid; rr < nr; rr += kLayerThreads)
-          for (unsigned kk = 0; kk < nt; ++kk) out[static_cast<size_t>(kk) * S * d + rr] = cterm(rr, kk);
+        if (dtype == kMXFP4) {
+          for (unsigned rr = tid; rr < nr; rr += kLayerThreads)
+            for (unsigned kk = 0; kk < nt; ++kk)
+              out[static_cast<size_t>(kk) * S * d + rr] = down_term<kMXFP4, ACT>(slot, nr, rr, s_hq, kk, bad);
+        } else {
+          for (unsigned rr = tid; rr < nr; rr += kLayerThreads)
+            for (unsigned kk = 0; kk < nt; ++kk)
+              out[static_cast<size_t>(kk) * S * d + rr] = down_term<kQ80, ACT>(slot, nr, rr, s_hq, kk, bad);
+        }
       }
       release(c);
     }
