@@ -254,7 +254,8 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);                // kMaxSlots mbarriers
   unsigned* misc = reinterpret_cast<unsigned*>(smem + 64);           // 64 words
-  unsigned* s_cnt = misc + 40;                                       // ring slot release counts
+  unsigned* s_cnt = misc + 40;                                       // ring slot: readers done with its chunk
+  unsigned* s_iss = misc + 48;                                       // ring slot: chunks issued into it
   uint16_t* s_ids = reinterpret_cast<uint16_t*>(smem + a.sm.ids);
   float* s_g = reinterpret_cast<float*>(smem + a.sm.gates);
   int* s_first = reinterpret_cast<int*>(smem + a.sm.first);
@@ -329,6 +330,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
     const uint8_t* src = a.base[s] + static_cast<size_t>(s_uid[u]) * a.slice_bytes;
     const unsigned slot = c % K;
     uint8_t* dst = ring + slot * SLOT;
+    reinterpret_cast<volatile unsigned*>(s_iss)[slot] = s_iss[slot] + 1;
     if (k < ngu) {
       const unsigned bytes = kn * rowb, kg = h * ngu + k;  // chunk of the slice's neurons
       mbar_expect_tx(&full[slot], 2 * bytes);
@@ -346,7 +348,10 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
   if (warp >= kFirstPlanWarp) {
     // ------------------------------------------------- warps 4-7: plan
     const unsigned ptid = tid - 32 * kFirstPlanWarp, pw = warp - kFirstPlanWarp;
-    if (ptid < kMaxSlots) s_cnt[ptid] = 0;
+    if (ptid < kMaxSlots) {
+      s_cnt[ptid] = 0;
+      s_iss[ptid] = 0;
+    }
     if (ptid == 0) {  // the ring's barriers, while the routing loads are in flight
       for (unsigned k = 0; k < K; ++k) mbar_init(&full[k], 1);
       fence_mbar_init();
@@ -629,25 +634,48 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
   PHASE(3);
 
   // --------------------------------------------------------------- items
-  // A warp done with ring chunk c counts itself out of the slot; the last of
-  // the 16 (fence.cta orders their shared-memory reads first) refills the
-  // slot with chunk c+K.  A warp whose wait ran out stops counting, so
-  // nothing is issued into a slot that a copy may still be writing.
+  // Only the warps that read ring chunk c wait for it: a gate/up chunk's
+  // kn/4 warps, every warp for a down chunk.  A reader done with it counts
+  // itself out of the slot; the last of the `readers` (fence.cta orders
+  // their shared-memory reads first) clears the count and refills the slot
+  // with chunk c+K.  Nothing else touches the count until that chunk lands
+  // (the refill's arrive on the slot's barrier releases the clearing store).
+  // A warp whose wait ran out stops counting, so nothing is issued into a
+  // slot that a copy may still be writing.
   bool timed_out = false, aborted = false;  // warp-uniform, block-uniform
-  auto release = [&](unsigned c) {
+  auto release = [&](unsigned c, unsigned readers) {
     __syncwarp();
     if (lane == 0 && !timed_out) {
       __threadfence_block();
-      const unsigned slot = c % K, round = c / K;
-      if (atomicAdd(&s_cnt[slot], 1u) == kLayerWarps * (round + 1) - 1 && c + K < n_ch) {
-        __threadfence_block();
-        fence_proxy_async();
-        issue(c + K);
+      const unsigned slot = c % K;
+      if (atomicAdd(&s_cnt[slot], 1u) == readers - 1) {
+        s_cnt[slot] = 0;
+        if (c + K < n_ch) {
+          __threadfence_block();
+          fence_proxy_async();
+          issue(c + K);
+        }
       }
     }
   };
+  // A reader waits for chunk c only once it is issued into its slot (the
+  // slot's previous chunk c-K consumed): then the slot's barrier is at chunk
+  // c's phase or past it, and the phase parity names chunk c unambiguously.
   auto wait_chunk = [&](unsigned c) {
-    if (!timed_out) timed_out = __any_sync(0xffffffffu, !mbar_wait(&full[c % K], (c / K) & 1));
+    if (!timed_out) {
+      const unsigned slot = c % K, j = c / K;
+      bool ok = true;
+      if (reinterpret_cast<volatile unsigned*>(s_iss)[slot] <= j) {
+        const uint64_t start = globaltimer();
+        while (reinterpret_cast<volatile unsigned*>(s_iss)[slot] <= j)
+          if (globaltimer() - start > kWaitNs) {
+            ok = false;
+            break;
+          }
+      }
+      ok = ok && mbar_wait(&full[slot], j & 1);
+      timed_out = __any_sync(0xffffffffu, !ok);
+    }
     return !timed_out;
   };
   unsigned c = 0;
@@ -667,7 +695,8 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
     // forms the neuron's SwiGLU (double, backends/ref.c:81-83).
     const unsigned quads = kn / 4, my_chunk = warp / quads, l8 = lane & 7, nspan = d / 256;
     for (unsigned k = 0; k < ngu; ++k, ++c) {
-      if (wait_chunk(c) && k == my_chunk) {
+      if (k != my_chunk) continue;
+      if (wait_chunk(c)) {
         if (c == 0) PHASE(15);
         if (c == 1) PHASE(12);
         const uint8_t* slot = ring + (c % K) * SLOT;
@@ -712,7 +741,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
           }
         }
       }
-      release(c);
+      release(c, quads);
     }
     if (r == 0) PHASE(9);
     if (__syncthreads_or(timed_out)) { aborted = true; break; }
@@ -770,7 +799,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
           float h0, h1, h2, h3;
           if (dtype == kMXFP4) down_terms4<kMXFP4, ACT>(slot, nr, s_hq, bad, h0, h1, h2, h3);
           else down_terms4<kQ80, ACT>(slot, nr, s_hq, bad, h0, h1, h2, h3);
-          release(c);
+          release(c, kLayerWarps);
           if (tid < nr) out[tid] = h0;
           if (tid + kLayerThreads < nr) out[tid + kLayerThreads] = h1;
           if (tid + 2 * kLayerThreads < nr) out[tid + 2 * kLayerThreads] = h2;
@@ -787,7 +816,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
               out[static_cast<size_t>(kk) * S * d + rr] = down_term<kQ80, ACT>(slot, nr, rr, s_hq, kk, bad);
         }
       }
-      release(c);
+      release(c, kLayerWarps);
     }
     if (r == 0) PHASE(6);
   }
@@ -949,15 +978,11 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
   }
   PHASE(7);
   // Nothing may still be writing this CTA's shared memory when it leaves.
-  // After an abort, wait (bounded) for the last copy issued into each slot:
-  // slot i got its first chunk at start and one more per completed release
-  // round that had a chunk left to issue.
+  // After an abort, wait (bounded) for the last copy issued into each slot
+  // (its s_iss-th phase).
   if (aborted && tid == 0)
-    for (unsigned i = 0; i < K && i < n_ch; ++i) {
-      unsigned n = 1;
-      while (n <= s_cnt[i] / kLayerWarps && i + K * n < n_ch) ++n;
-      mbar_wait(&full[i], (n - 1) & 1);
-    }
+    for (unsigned i = 0; i < K; ++i)
+      if (s_iss[i]) mbar_wait(&full[i], (s_iss[i] - 1) & 1);
 }
 
 }  // namespace frc
