@@ -281,14 +281,18 @@ static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, u
   auto take = [&](unsigned bytes) { unsigned at = o; o = align_up(o + bytes, 16); return at; };
   m.ids = take(2 * T * 10);
   m.gates = take(4 * T * 11);
-  m.first = take(4 * 512);
-  m.uid = take(2 * kMaxUnique);
-  m.umask = take(4 * kMaxUnique);
-  m.ugate = take(4 * kMaxUnique * T);
-  m.upre = take(4 * (kMaxUnique + 1));
+  // plan tables sized for this launch's tokens (one token: eleven experts,
+  // no first-appearance table), which leaves the rest to the ring
+  const unsigned mu = T * 10 + 1 < kMaxUnique ? T * 10 + 1 : kMaxUnique;
+  m.max_unique = mu;
+  m.first = T > 1 ? take(4 * 512) : 0;
+  m.uid = take(2 * mu);
+  m.umask = take(4 * mu);
+  m.ugate = take(4 * mu * T);
+  m.upre = take(4 * (mu + 1));
   m.rms = take(4 * T);
   m.bases = take(8 * kMaxBlocks);
-  m.rpart = take(4 * kActWarps * kMaxRounds);
+  m.rpart = take(4 * kActWarps * ((T * d / 16 + kActThreads - 1) / kActThreads));  // [round][warp] sums
   m.tokpair = take(2 * (T * 11));
   if (act == FRC_ACT_Q8) {
     m.xq = take(T * d);
@@ -321,7 +325,10 @@ static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, u
   // sums [11][rows] in the ring (rows: 4-row units, S up to 20)
   const unsigned rows4 = 4 * ((d / 4 + G - 1) / G);
   if (K < 2 || K * slot < 4 * (11 * kMaxBlocks * (rows4 + 1) + 11 * rows4)) return false;
-  K = K < kMaxSlots ? K : kMaxSlots;
+  // At most five copies in flight a CTA: at one token, 4-5 slots ran 1 %
+  // faster than 6 (the extra copies delay every CTA's first chunks); at 16
+  // tokens 5 to 8 slots measured the same.
+  K = K < kRingSlots ? K : kRingSlots;
   unsigned kns = 16;
   while (kns > 1 && 2 * kns * srow > slot) kns /= 2;
   if (kn < 4 || kns < 4) return false;  // a gate/up chunk holds at least one warp's four neurons

@@ -42,7 +42,8 @@ constexpr unsigned kActWarps = kActThreads / 32;
 constexpr unsigned kPlanWarps = 4;             // warps 4-7 build the plan
 constexpr unsigned kPlanThreads = 32 * kPlanWarps;
 constexpr unsigned kFirstPlanWarp = kLayerWarps - kPlanWarps;
-constexpr unsigned kMaxSlots = 8;              // TMA ring depth limit
+constexpr unsigned kMaxSlots = 8;              // TMA ring: barriers and counters reserved
+constexpr unsigned kRingSlots = 5;             // TMA ring: slots a launch uses at most
 constexpr unsigned kMaxRounds = 256;           // warp-passes of the activation sums per warp (512 floats each)
 constexpr unsigned kMaxPeers = 8;              // GPUs of one in-box reduce
 
@@ -61,6 +62,7 @@ struct LayerSmem {
   unsigned kn_r, kn_s;  // neurons per gate/up chunk: routed, shared items (powers of two)
   unsigned dn_r, dn_s;  // rows per down chunk: routed, shared items (multiples of 16)
   unsigned mag_ch_r, mag_ch_s;  // div_magic of the chunks per routed / shared item
+  unsigned max_unique;          // entries of the plan's per-expert tables (10 x tokens + 1)
 };
 
 struct LayerParams {
@@ -393,8 +395,8 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
       for (unsigned i = ptid; i < T * 10; i += kPlanThreads) s_ids[i] = a.expert[i];
       for (unsigned i = ptid; i < T * 11; i += kPlanThreads) s_g[i] = a.gate[i];
       for (unsigned i = ptid; i < 512; i += kPlanThreads) s_first[i] = 0x7fffffff;
-      for (unsigned i = ptid; i < kMaxUnique; i += kPlanThreads) s_umask[i] = 0;
-      for (unsigned i = ptid; i < kMaxUnique * T; i += kPlanThreads) s_ugate[i] = 0.0f;
+      for (unsigned i = ptid; i < a.sm.max_unique; i += kPlanThreads) s_umask[i] = 0;
+      for (unsigned i = ptid; i < a.sm.max_unique * T; i += kPlanThreads) s_ugate[i] = 0.0f;
       plan_sync();
       PHASE_AT(8, kPlanThreads);
       bool invalid = false;
