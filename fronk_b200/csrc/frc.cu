@@ -324,11 +324,13 @@ static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, u
   // the reduce stages one token's terms [11][S][rows], weights [11][S] and
   // sums [11][rows] in the ring (rows: 4-row units, S up to 20)
   const unsigned rows4 = 4 * ((d / 4 + G - 1) / G);
-  if (K < 2 || K * slot < 4 * (11 * kMaxBlocks * (rows4 + 1) + 11 * rows4)) return false;
-  // At most five copies in flight a CTA: at one token, 4-5 slots ran 1 %
-  // faster than 6 (the extra copies delay every CTA's first chunks); at 16
-  // tokens 5 to 8 slots measured the same.
-  K = K < kRingSlots ? K : kRingSlots;
+  const unsigned staged = 4 * (11 * kMaxBlocks * (rows4 + 1) + 11 * rows4);
+  if (K < 2 || K * slot < staged) return false;
+  K = K < kMaxSlots ? K : kMaxSlots;
+  // At most five copies in flight a CTA (one token: 4-5 slots ran 1 % faster
+  // than 6, the extra copies delaying every CTA's first chunks), while five
+  // slots still hold the reduce's staging.
+  if (K > kRingSlots && kRingSlots * slot >= staged) K = kRingSlots;
   unsigned kns = 16;
   while (kns > 1 && 2 * kns * srow > slot) kns /= 2;
   if (kn < 4 || kns < 4) return false;  // a gate/up chunk holds at least one warp's four neurons
