@@ -64,6 +64,9 @@ _SIGS = {
     "frc_load_layer": (_int, [_vp, _int, _u32, _vp, _sz]),
     "frc_unload_unit": (_int, [_vp, _int]),
     "frc_loaded_mask": (_int, [_vp, _vp]),
+    "frc_units_open": (_int, [_vp, ctypes.c_char_p, _u32, _int]),
+    "frc_unit_verify": (_int, [ctypes.c_char_p, _u32, _u64, _int]),
+    "frc_sha256": (_int, [_vp, _sz, _vp]),
     "frc_run": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _int]),
     "frc_run_device": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
     "frc_run_device_fixed": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
@@ -141,6 +144,21 @@ def layer_bytes(g):
 
 def unit_bytes(g):
     return library().frc_unit_bytes(ctypes.byref(g))
+
+
+def sha256(data):
+    """SHA-256 (FIPS 180-4) of a bytes-like object, by the library's frc_sha256."""
+    buf = np.frombuffer(bytes(data), np.uint8)
+    out = np.zeros(32, np.uint8)
+    rc = library().frc_sha256(_ptr(buf) if buf.size else None, buf.size, _ptr(out))
+    if rc:
+        raise FrcError(rc, "sha256", "")
+    return out.tobytes()
+
+
+def unit_verify(directory, block, unit_bytes=0, verify=True):
+    """frc_unit_verify: the unit-file checks of one block without a device; returns the status code."""
+    return library().frc_unit_verify(os.fsencode(directory), block, unit_bytes, 1 if verify else 0)
 
 
 def slice_offset(g, layer, expert):
@@ -244,6 +262,11 @@ class Context:
 
     def load_unit(self, block, unit):
         return self.lib.frc_load_unit(self.h, block, _ptr(unit), unit.nbytes)
+
+    def units_open(self, directory, mask, verify=True):
+        """frc_units_open: load the blocks of `mask` from a unit directory
+        (unit-BB.bin + unit-BB.sha256); returns the status code."""
+        return self.lib.frc_units_open(self.h, os.fsencode(directory), mask, 1 if verify else 0)
 
     def load_layer(self, block, layer, data):
         """data: a numpy uint8 array of layer_bytes (reference layout)."""

@@ -24,6 +24,7 @@ using namespace frc;
 #include "frc_layer.cuh"
 #include "frc_umma.cuh"
 #include "frc_prefill.cuh"
+#include "frc_units.h"
 
 // ===================================================== set-up kernels
 
@@ -832,6 +833,34 @@ int frc_unload_unit(frc_context* c, int block) {
       any = true;
     }
   return any ? FRC_OK : fail(c, FRC_STATE, "block %d not loaded", block);
+}
+
+// The reference node's unit loader (src/units.c:25-75) over frc_load_unit:
+// each block of the mask is mapped and checked (frc_units.c), copied to HBM,
+// and unmapped; a failure unloads the blocks this call loaded.
+int frc_units_open(frc_context* c, const char* directory, uint32_t mask, int verify) {
+  if (!c || !directory || !mask || mask >= (1u << FRC_MAX_BLOCKS)) return fail(c, FRC_INVALID, "bad units_open arguments");
+  const uint64_t want = frc_unit_bytes(&c->g);
+  uint32_t done = 0;
+  int rc = FRC_OK;
+  for (unsigned b = 0; b < FRC_MAX_BLOCKS && rc == FRC_OK; ++b) {
+    if (!(mask >> b & 1)) continue;
+    const void* data = nullptr;
+    size_t len = 0;
+    char why[512];
+    rc = frc_unit_map(directory, b, want, verify, &data, &len, why, sizeof why);
+    if (rc) {
+      fail(c, rc, "%s", why);
+      break;
+    }
+    rc = frc_load_unit(c, static_cast<int>(b), data, len);
+    frc_unit_unmap(data, len);
+    if (rc == FRC_OK) done |= 1u << b;
+  }
+  if (rc)
+    for (unsigned b = 0; b < FRC_MAX_BLOCKS; ++b)
+      if (done >> b & 1) frc_unload_unit(c, static_cast<int>(b));
+  return rc;
 }
 
 int frc_loaded_mask(const frc_context* c, uint32_t* mask) {

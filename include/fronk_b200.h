@@ -89,6 +89,23 @@ int frc_unload_unit(frc_context *c, int block);
 /* Bit b set when block b is loaded. */
 int frc_loaded_mask(const frc_context *c, uint32_t *mask);
 
+/* ---- Units from disk (the reference node's loader, src/units.c:25-75) ----
+ * A unit directory holds unit-BB.bin (block BB's weights, frc_unit_bytes in
+ * the reference layout) and unit-BB.sha256 (64 lowercase hex digits and a
+ * newline).  frc_units_open maps each block of `mask` read-only, checks the
+ * digest file, the size and, with verify, the file's SHA-256, and copies the
+ * unit into HBM (frc_load_unit); the mapping is released after the copy.
+ * On the first failure the blocks this call loaded are unloaded again.
+ * Errors: FRC_IO (a file missing, unreadable or of another size),
+ * FRC_INVALID (a malformed digest file, bad arguments), FRC_MISMATCH (the
+ * SHA-256 differs), FRC_STATE (a block already loaded). */
+int frc_units_open(frc_context *c, const char *directory, uint32_t mask, int verify);
+/* The same file checks for one block, without a device (unit_bytes 0: any
+ * size). */
+int frc_unit_verify(const char *directory, unsigned block, uint64_t unit_bytes, int verify);
+/* SHA-256 (FIPS 180-4) of len bytes into out[32] (src/sha256.c's role). */
+int frc_sha256(const void *data, size_t len, uint8_t out[32]);
+
 /* Synchronous run from host memory, the semantics of fr_backend.run
  * (src/backend.h:1-5, backends/ref.c:41-98): validates the request (ids < 512
  * and distinct per token, gates finite and >= 0, x finite, FE_TONEAREST),
