@@ -67,6 +67,10 @@ _SIGS = {
     "frc_units_open": (_int, [_vp, ctypes.c_char_p, _u32, _int]),
     "frc_unit_verify": (_int, [ctypes.c_char_p, _u32, _u64, _int]),
     "frc_sha256": (_int, [_vp, _sz, _vp]),
+    "frc_plane_open": (_int, [_vp, _u32, _vp]),
+    "frc_plane_run": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _u64, _vp, _vp]),
+    "frc_plane_close": (_int, [_vp]),
+    "frc_round_half": (_int, [_vp, _sz, _vp]),
     "frc_run": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _int]),
     "frc_run_device": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
     "frc_run_device_fixed": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
@@ -154,6 +158,53 @@ def sha256(data):
     if rc:
         raise FrcError(rc, "sha256", "")
     return out.tobytes()
+
+
+def round_half(x):
+    """(rc, x rounded through fp16 as the head sends it) of frc_round_half."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros_like(x)
+    rc = library().frc_round_half(_ptr(x) if x.size else None, x.size, _ptr(out) if x.size else None)
+    return rc, out
+
+
+class Plane:
+    """In-box head plane over contexts (frc_plane_*): one layer fanned out to
+    every participant, the parts done by the deadline summed in order."""
+
+    def __init__(self, contexts):
+        self.lib = library()
+        self.contexts = list(contexts)          # they must outlive the plane
+        arr = (ctypes.c_void_p * len(self.contexts))(*[c.h.value for c in self.contexts])
+        h = ctypes.c_void_p()
+        rc = self.lib.frc_plane_open(arr, len(self.contexts), ctypes.byref(h))
+        if rc:
+            raise FrcError(rc, "plane_open")
+        self.h = h
+        self.hidden = self.contexts[0].hidden
+
+    def run(self, layer, expert, gate, x, deadline_ns=2_000_000_000, out=None):
+        """(rc, y, missing mask)."""
+        expert = np.ascontiguousarray(expert, np.uint16)
+        gate = np.ascontiguousarray(gate, np.float32)
+        x = np.ascontiguousarray(x, np.float32)
+        tokens = x.shape[0]
+        y = out if out is not None else np.zeros((tokens, self.hidden), np.float32)
+        m = ctypes.c_uint32()
+        rc = self.lib.frc_plane_run(self.h, layer, tokens, _ptr(expert), _ptr(gate), _ptr(x), deadline_ns, _ptr(y),
+                                    ctypes.byref(m))
+        return rc, y, m.value
+
+    def close(self):
+        if self.h:
+            self.lib.frc_plane_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
 
 
 def unit_verify(directory, block, unit_bytes=0, verify=True):

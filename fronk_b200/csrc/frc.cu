@@ -4,6 +4,7 @@
 // split, every CTA's weight bytes requested up front through a TMA ring,
 // integer block dots, a fixed reduction order and no float atomics (results
 // are bitwise repeatable).
+#include <chrono>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -1050,6 +1051,172 @@ int frc_status(frc_context* c, void* stream) {
     CK(cudaMemset(c->xcnt, 0, sizeof(unsigned) * kMaxUnique));
   }
   if (rc) return fail(c, rc, "device status 0x%x", *c->h_status);
+  return FRC_OK;
+}
+
+// ------------------------------------------------------ in-box head plane
+// The reference head's fan-out and gather of one layer (src/plane.c:252-374)
+// over the GPUs of one box, one context each.  x is rounded to fp16 once, as
+// the head rounds it for every node and for its own slice
+// (src/plane.c:258-262, src/wire.c:46-67); every participant runs the layer
+// on its own stream; the parts done by the deadline are summed in
+// participant order (the reference adds them in arrival order), and the
+// others are reported in the missing mask and left out, as the reference's
+// head leaves out a node that missed its deadline.
+
+// fp16 round trip of the reference's wire format: round to nearest even to
+// fp16's 11 significant bits (multiples of 2^-24 below 2^-14); a value that
+// is not finite or rounds past fp16's largest finite value (65504) fails.
+static int half_round(float v, float* out) {
+  if (!isfinite(v)) return -1;
+  const float a = fabsf(v);
+  if (a >= 65520.0f) return -1;  // rounds to infinity
+  float q;
+  if (a < 0x1p-14f) {
+    q = nearbyintf(a * 0x1p24f) * 0x1p-24f;  // subnormal spacing 2^-24 (scalings are exact)
+  } else {
+    int e;
+    frexpf(a, &e);                            // a in [2^(e-1), 2^e)
+    const float ulp = ldexpf(1.0f, e - 11);   // 10 fraction bits
+    q = nearbyintf(a / ulp) * ulp;
+  }
+  *out = copysignf(q, v);
+  return 0;
+}
+
+int frc_round_half(const float* x, size_t n, float* out) {
+  if ((!x || !out) && n) return FRC_INVALID;
+  if (fegetround() != FE_TONEAREST) return FRC_INVALID;
+  for (size_t i = 0; i < n; ++i)
+    if (half_round(x[i], &out[i])) return FRC_INVALID;
+  return FRC_OK;
+}
+
+struct frc_plane {
+  unsigned n = 0, d = 0;
+  frc_context* ctx[kMaxPeers] = {};
+  uint8_t* d_in[kMaxPeers] = {};  // [x 16 x d f32][gate 16 x 11 f32][expert 16 x 10 u16]
+  float* d_y[kMaxPeers] = {};
+  uint8_t* h_in[kMaxPeers] = {};  // pinned staging of the same layout
+  float* h_y[kMaxPeers] = {};     // pinned [16][d]
+  cudaEvent_t done[kMaxPeers] = {};
+  bool pending[kMaxPeers] = {};   // this participant's last call may still be running
+  float* xr = nullptr;            // [16][d] rounded x
+};
+
+static size_t plane_in_bytes(unsigned d) {
+  return sizeof(float) * kMaxTokens * d + sizeof(float) * kMaxTokens * FRC_ACTIVE + sizeof(uint16_t) * kMaxTokens * FRC_TOPK;
+}
+
+int frc_plane_close(frc_plane* p) {
+  if (!p) return FRC_INVALID;
+  for (unsigned i = 0; i < p->n; ++i) {
+    if (!p->ctx[i]) continue;
+    cudaSetDevice(p->ctx[i]->device);
+    cudaStreamSynchronize(p->ctx[i]->stream);
+    if (p->done[i]) cudaEventDestroy(p->done[i]);
+    cudaFree(p->d_in[i]);
+    cudaFree(p->d_y[i]);
+    cudaFreeHost(p->h_in[i]);
+    cudaFreeHost(p->h_y[i]);
+  }
+  free(p->xr);
+  delete p;
+  return FRC_OK;
+}
+
+int frc_plane_open(frc_context* const* ctx, unsigned count, frc_plane** out) {
+  if (!ctx || !out || count < 1 || count > kMaxPeers) return FRC_INVALID;
+  *out = nullptr;
+  for (unsigned i = 0; i < count; ++i)
+    if (!ctx[i] || memcmp(&ctx[i]->g, &ctx[0]->g, sizeof(frc_geometry))) return FRC_INVALID;
+  frc_plane* p = new frc_plane();
+  p->n = count;
+  p->d = ctx[0]->g.hidden;
+  p->xr = static_cast<float*>(malloc(sizeof(float) * kMaxTokens * p->d));
+  int rc = p->xr ? FRC_OK : FRC_IO;
+  for (unsigned i = 0; i < count && rc == FRC_OK; ++i) {
+    frc_context* c = ctx[i];
+    p->ctx[i] = c;
+    if (cudaSetDevice(c->device) != cudaSuccess || cudaMalloc(&p->d_in[i], plane_in_bytes(p->d)) != cudaSuccess ||
+        cudaMalloc(&p->d_y[i], sizeof(float) * kMaxTokens * p->d) != cudaSuccess ||
+        cudaMallocHost(&p->h_in[i], plane_in_bytes(p->d)) != cudaSuccess ||
+        cudaMallocHost(&p->h_y[i], sizeof(float) * kMaxTokens * p->d) != cudaSuccess ||
+        cudaEventCreateWithFlags(&p->done[i], cudaEventDisableTiming) != cudaSuccess)
+      rc = fail(c, FRC_IO, "plane buffers");
+  }
+  if (rc) {
+    frc_plane_close(p);
+    return rc;
+  }
+  *out = p;
+  return FRC_OK;
+}
+
+int frc_plane_run(frc_plane* p, unsigned layer, unsigned tokens, const uint16_t* expert, const float* gate,
+                  const float* x, uint64_t deadline_ns, float* y, uint32_t* missing) {
+  if (!p || !expert || !gate || !x || !y || !missing || tokens < 1 || tokens > kMaxTokens || !deadline_ns)
+    return FRC_INVALID;
+  const unsigned d = p->d;
+  const size_t xb = sizeof(float) * tokens * d, gb = sizeof(float) * tokens * FRC_ACTIVE;
+  const size_t eb = sizeof(uint16_t) * tokens * FRC_TOPK;
+  // every participant sees the same rounded activations; nothing is sent
+  // when one of them is not representable
+  if (frc_round_half(x, static_cast<size_t>(tokens) * d, p->xr)) return FRC_INVALID;
+  for (unsigned i = 0; i < p->n; ++i) {
+    frc_context* c = p->ctx[i];
+    CK(cudaSetDevice(c->device));
+    if (p->pending[i]) {  // a late part of an earlier call still owns the staging: wait (bounded)
+      const auto t0 = std::chrono::steady_clock::now();
+      cudaError_t q;
+      while ((q = cudaEventQuery(p->done[i])) == cudaErrorNotReady)
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(2))
+          return fail(c, FRC_IO, "plane participant %u still busy with an earlier layer", i);
+      if (q != cudaSuccess) return fail(c, FRC_IO, "plane participant %u: %s", i, cudaGetErrorString(q));
+      p->pending[i] = false;
+    }
+    memcpy(p->h_in[i], p->xr, xb);
+    memcpy(p->h_in[i] + xb, gate, gb);
+    memcpy(p->h_in[i] + xb + gb, expert, eb);
+    CK(cudaMemcpyAsync(p->d_in[i], p->h_in[i], xb + gb + eb, cudaMemcpyHostToDevice, c->stream));
+    const int rc = run_device(c, layer, tokens, reinterpret_cast<const uint16_t*>(p->d_in[i] + xb + gb),
+                              reinterpret_cast<const float*>(p->d_in[i] + xb), reinterpret_cast<const float*>(p->d_in[i]),
+                              nullptr, nullptr, p->d_y[i], FRC_ACT_Q8, 0, c->stream);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(p->h_y[i], p->d_y[i], xb, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaEventRecord(p->done[i], c->stream));
+    p->pending[i] = true;
+  }
+  // gather until every part is in or the deadline passes
+  uint32_t left = (p->n >= 32 ? 0xffffffffu : (1u << p->n) - 1);
+  const auto start = std::chrono::steady_clock::now();
+  const auto limit = std::chrono::nanoseconds(deadline_ns);
+  for (;;) {
+    for (unsigned i = 0; i < p->n; ++i) {
+      if (!(left >> i & 1)) continue;
+      const cudaError_t q = cudaEventQuery(p->done[i]);
+      if (q == cudaSuccess) {
+        left &= ~(1u << i);
+        p->pending[i] = false;
+      } else if (q != cudaErrorNotReady) {
+        return fail(p->ctx[i], FRC_IO, "plane participant %u: %s", i, cudaGetErrorString(q));
+      }
+    }
+    if (!left || std::chrono::steady_clock::now() - start >= limit) break;
+  }
+  // a part that arrived with a device error fails the call (y untouched)
+  for (unsigned i = 0; i < p->n; ++i)
+    if (!(left >> i & 1)) {
+      const int rc = frc_status(p->ctx[i], p->ctx[i]->stream);
+      if (rc) return rc;
+    }
+  for (size_t k = 0; k < static_cast<size_t>(tokens) * d; ++k) {
+    float s = 0.0f;
+    for (unsigned i = 0; i < p->n; ++i)
+      if (!(left >> i & 1)) s += p->h_y[i][k];
+    y[k] = s;
+  }
+  *missing = left;
   return FRC_OK;
 }
 

@@ -106,6 +106,29 @@ int frc_unit_verify(const char *directory, unsigned block, uint64_t unit_bytes, 
 /* SHA-256 (FIPS 180-4) of len bytes into out[32] (src/sha256.c's role). */
 int frc_sha256(const void *data, size_t len, uint8_t out[32]);
 
+/* ---- In-box head plane (the reference head's fan-out and gather of one
+ * layer, src/plane.c:252-374, over the GPUs of one box) ----
+ * One context per GPU, each holding its share of the blocks (the planner's
+ * split).  frc_plane_run rounds x to fp16 once, as the head does for every
+ * node and its own slice (src/plane.c:258-262, src/wire.c:46-67), runs the
+ * layer on every participant's stream (Q8 activations), and sums the parts
+ * that are done by the deadline in participant order; bit i of *missing is
+ * set for a participant that missed it, and its part is left out, as the
+ * reference head leaves out a late node.  A late participant's next call
+ * waits (bounded) for its earlier one.  FRC_INVALID: bad arguments or an x
+ * value with no finite fp16 form (nothing runs); a participant's device
+ * error fails the call with y untouched.  Contexts must share a geometry and
+ * outlive the plane. */
+typedef struct frc_plane frc_plane;
+int frc_plane_open(frc_context *const *ctx, unsigned count, frc_plane **out);
+int frc_plane_run(frc_plane *p, unsigned layer, unsigned tokens, const uint16_t *expert, const float *gate,
+                  const float *x, uint64_t deadline_ns, float *y, uint32_t *missing);
+int frc_plane_close(frc_plane *p);
+/* x rounded through fp16 as the head sends it: round to nearest even;
+ * FRC_INVALID when a value is not finite or rounds past 65504, or the
+ * rounding mode is not to-nearest. */
+int frc_round_half(const float *x, size_t n, float *out);
+
 /* Synchronous run from host memory, the semantics of fr_backend.run
  * (src/backend.h:1-5, backends/ref.c:41-98): validates the request (ids < 512
  * and distinct per token, gates finite and >= 0, x finite, FE_TONEAREST),
