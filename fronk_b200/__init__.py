@@ -71,6 +71,8 @@ _SIGS = {
     "frc_plane_run": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _u64, _vp, _vp]),
     "frc_plane_close": (_int, [_vp]),
     "frc_round_half": (_int, [_vp, _sz, _vp]),
+    "frc_costmodel_fit": (_int, [_vp, _vp, _u32, _vp]),
+    "frc_costmodel_measure": (_int, [_vp, _vp, _u32, _u32, _u32, _vp]),
     "frc_run": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _int]),
     "frc_run_device": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
     "frc_run_device_fixed": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
@@ -158,6 +160,21 @@ def sha256(data):
     if rc:
         raise FrcError(rc, "sha256", "")
     return out.tobytes()
+
+
+class CostModel(ctypes.Structure):
+    """frc_costmodel (the fields and meaning of the reference's fr_costmodel)."""
+    _fields_ = [("burst_max", ctypes.c_uint), ("t0_ns", ctypes.c_double), ("bw_eff", ctypes.c_double),
+                ("ns", ctypes.c_double * 8), ("bytes", ctypes.c_uint64 * 8)]
+
+
+def costmodel_fit(ns, nbytes):
+    """(rc, CostModel) of frc_costmodel_fit over bursts 1..len(ns)."""
+    ns = np.ascontiguousarray(ns, np.float64)
+    nbytes = np.ascontiguousarray(nbytes, np.uint64)
+    m = CostModel()
+    rc = library().frc_costmodel_fit(_ptr(ns), _ptr(nbytes), len(ns), ctypes.byref(m))
+    return rc, m
 
 
 def round_half(x):
@@ -318,6 +335,12 @@ class Context:
         """frc_units_open: load the blocks of `mask` from a unit directory
         (unit-BB.bin + unit-BB.sha256); returns the status code."""
         return self.lib.frc_units_open(self.h, os.fsencode(directory), mask, 1 if verify else 0)
+
+    def costmodel(self, layer=0, burst_max=4, samples=15):
+        """(rc, CostModel) of frc_costmodel_measure on this context."""
+        m = CostModel()
+        rc = self.lib.frc_costmodel_measure(self.h, ctypes.byref(self.g), layer, burst_max, samples, ctypes.byref(m))
+        return rc, m
 
     def load_layer(self, block, layer, data):
         """data: a numpy uint8 array of layer_bytes (reference layout)."""

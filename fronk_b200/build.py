@@ -14,7 +14,7 @@ PHASES_LIB = os.path.join(HERE, "libfronk_b200_phases.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_SOURCES = ["frc.cu"]
-C_SOURCES = ["frc_synth.c", "fr_cuda_backend.c", "frc_host.c", "frc_units.c"]
+C_SOURCES = ["frc_synth.c", "fr_cuda_backend.c", "frc_host.c", "frc_units.c", "frc_cost.c"]
 DEPS = sorted(f for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh", ".c", ".h")))  # every source and header
 
 

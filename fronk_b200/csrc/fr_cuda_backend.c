@@ -10,7 +10,8 @@
  *    the pointer; unload frees it (backends/ref.c:19-28 borrow instead).
  *  - bench and self_test call the reference's own fr_bench_execute_backend and
  *    fr_native_self_test when the process links them (they are looked up at
- *    call time); otherwise they report FR_UNSUPPORTED.
+ *    call time).  Without them, bench measures and fits the same cost model
+ *    itself (frc_costmodel_measure); self_test reports FR_UNSUPPORTED.
  * Build inside the reference tree with -DFR_USE_REFERENCE_HEADERS and
  * -I<reference>/src to compile against src/backend.h itself.
  */
@@ -146,7 +147,25 @@ typedef int (*self_test_fn)(const fr_backend *);
 static int bench(const fr_backend *b, int burst_max, fr_costmodel *out) {
     if (!out) return FR_INVALID;
     bench_fn f = (bench_fn)dlsym(RTLD_DEFAULT, "fr_bench_execute_backend");
-    return f ? f(b, burst_max, out) : FR_UNSUPPORTED;
+    if (f) return f(b, burst_max, out);
+    /* without the reference's harness: the same measurement and fit over the
+     * loaded blocks (frc_costmodel_measure) */
+    slot_state *s = state_of(b);
+    if (!s || !s->ctx || !any_loaded(s)) return FR_STATE;
+    if (burst_max < 2 || burst_max > FR_MAX_BURST || burst_max > FRC_COST_MAX_BURST) return FR_INVALID;
+    const frc_geometry g = reference_geometry();
+    frc_costmodel m;
+    const int rc = frc_costmodel_measure(s->ctx, &g, 0, (unsigned)burst_max, 15, &m);
+    if (rc) return rc;
+    memset(out, 0, sizeof *out);
+    out->burst_max = m.burst_max;
+    out->t0_ns = m.t0_ns;
+    out->bw_eff = m.bw_eff;
+    for (unsigned i = 0; i < m.burst_max; ++i) {
+        out->ns[i] = m.ns[i];
+        out->bytes[i] = m.bytes[i];
+    }
+    return FR_OK;
 }
 
 static int self_test(const fr_backend *b, const char *dir) {

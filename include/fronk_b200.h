@@ -124,6 +124,30 @@ int frc_plane_open(frc_context *const *ctx, unsigned count, frc_plane **out);
 int frc_plane_run(frc_plane *p, unsigned layer, unsigned tokens, const uint16_t *expert, const float *gate,
                   const float *x, uint64_t deadline_ns, float *y, uint32_t *missing);
 int frc_plane_close(frc_plane *p);
+/* ---- Cost model (fr_costmodel, src/backend.h:30-35) ----
+ * t = t0 + 1e9 * bytes / bw_eff for a burst that reads `bytes` of weights,
+ * the form the reference planner weighs participants with.  Same fields and
+ * meaning as fr_costmodel. */
+enum { FRC_COST_MAX_BURST = 8 };
+typedef struct {
+    unsigned burst_max;
+    double t0_ns, bw_eff;                 /* bytes/second */
+    double ns[FRC_COST_MAX_BURST];        /* median time of a synchronous run, burst b+1 */
+    uint64_t bytes[FRC_COST_MAX_BURST];   /* weight bytes it reads */
+} frc_costmodel;
+/* The reference's fit (src/bench.c:163-191): least squares of ns over bytes
+ * for bursts 1..n (2 <= n <= 8); a negative t0 is clamped to 0 by fitting
+ * through the origin.  FRC_NUMERIC for nonpositive or nonfinite times or a
+ * nonpositive slope. */
+int frc_costmodel_fit(const double *ns, const uint64_t *bytes, unsigned n, frc_costmodel *out);
+/* Measures and fits it on this context: `samples` synchronous frc_run calls
+ * of layer `layer` at each burst 1..burst_max (distinct seeded routing, the
+ * shared expert active), medians, bytes = loaded blocks x (10 x burst x
+ * slice + shared slice) (src/bench.c:157-160).  g: the context's geometry.
+ * FRC_STATE when nothing is loaded. */
+int frc_costmodel_measure(frc_context *c, const frc_geometry *g, unsigned layer, unsigned burst_max,
+                          unsigned samples, frc_costmodel *out);
+
 /* x rounded through fp16 as the head sends it: round to nearest even;
  * FRC_INVALID when a value is not finite or rounds past 65504, or the
  * rounding mode is not to-nearest. */
