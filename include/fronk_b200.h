@@ -118,7 +118,8 @@ int frc_sha256(const void *data, size_t len, uint8_t out[32]);
  * waits (bounded) for its earlier one.  FRC_INVALID: bad arguments or an x
  * value with no finite fp16 form (nothing runs); a participant's device
  * error fails the call with y untouched.  Contexts must share a geometry and
- * outlive the plane. */
+ * outlive the plane; the plane runs on their own streams and scratch, so no
+ * other call may use those contexts while a plane call is in flight. */
 typedef struct frc_plane frc_plane;
 int frc_plane_open(frc_context *const *ctx, unsigned count, frc_plane **out);
 int frc_plane_run(frc_plane *p, unsigned layer, unsigned tokens, const uint16_t *expert, const float *gate,
