@@ -202,9 +202,9 @@ struct frc_context {
   uint8_t* pool = nullptr;
   unsigned pool_count = 0;
   unsigned long long launches = 0;
-  bool attr_set[2][2] = {};   // [activation mode][split variant]
-  unsigned occ_smem[2][2] = {};
-  int occ_val[2][2] = {};
+  bool attr_set[2][3] = {};   // [activation mode][variant: tokens, one token, split items]
+  unsigned occ_smem[2][3] = {};
+  int occ_val[2][3] = {};
   unsigned last_T = 0, last_S = 0, last_G = 0;
   // in-box reduce: this rank's inbox (IPC-exported), every rank's inbox as
   // mapped here, the per-CTA launch counters
@@ -378,9 +378,11 @@ static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s, bool ove
     c->occ_val[ai][split] = *per_sm;
     return FRC_OK;
   };
-  auto kern = moe_layer_kernel<ACT, false>;
+  // one token: the variant with the token count folded to 1
+  const int var = a.T == 1 ? 1 : 0;
+  auto kern = var ? moe_layer_kernel<ACT, false, true> : moe_layer_kernel<ACT, false, false>;
   int orc;
-  if ((orc = prepare(kern, 0))) return orc;
+  if ((orc = prepare(kern, var))) return orc;
   // Two CTAs an SM when their shared memory fits, else one; all resident
   // (the kernel has a grid barrier).
   unsigned per = 2, G = 2 * static_cast<unsigned>(c->sms);
@@ -392,7 +394,7 @@ static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s, bool ove
   // an SM with its larger ring; 4 and 8 tokens ran faster on two).
   if (fits) fits = a.sm.kn_r >= 8 && a.sm.slots >= 4;
   if (fits) {
-    if ((orc = occupancy(kern, 0, a.sm.total, &per_sm))) return orc;
+    if ((orc = occupancy(kern, var, a.sm.total, &per_sm))) return orc;
     fits = per_sm >= 2;
   }
   if (!fits) {
@@ -400,7 +402,7 @@ static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s, bool ove
     G = static_cast<unsigned>(c->sms);
     if (!smem_layout(c, a.T, G, ACT, kSmemOnePerSm, &a.sm))
       return fail(c, FRC_INVALID, "%u tokens need too much shared memory", a.T);
-    if ((orc = occupancy(kern, 0, a.sm.total, &per_sm))) return orc;
+    if ((orc = occupancy(kern, var, a.sm.total, &per_sm))) return orc;
   }
   if (per_sm < static_cast<int>(per)) return fail(c, FRC_INVALID, "layer kernel does not fit an SM (%u bytes)", a.sm.total);
   // One token and few items (slices split over several GPUs): split each
@@ -416,9 +418,9 @@ static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s, bool ove
         break;
       }
   if (a.H > 1) {
-    auto ks = moe_layer_kernel<ACT, true>;
+    auto ks = moe_layer_kernel<ACT, true, true>;
     int ps = 0;
-    if ((orc = prepare(ks, 1)) || (orc = occupancy(ks, 1, a.sm.total, &ps))) return orc;
+    if ((orc = prepare(ks, 2)) || (orc = occupancy(ks, 2, a.sm.total, &ps))) return orc;
     if (ps >= static_cast<int>(per)) kern = ks;
     else { a.H = 1; a.Hshift = 0; }  // the split variant does not fit as many CTAs
   }

@@ -249,9 +249,11 @@ __device__ __forceinline__ void down_terms4(const uint8_t* slot, unsigned nr, co
   h3 = tid + 3 * kLayerThreads < nr ? down_term<DT, ACT>(slot, nr, tid + 3 * kLayerThreads, s_hq, 0, bad) : 0.0f;
 }
 
+// ONE: a one-token launch, the token count folded to 1 at compile time (its
+// loops over tokens and the multi-token plan drop out).  SPLIT implies ONE.
 // SPLIT: items may be split in a.H parts (one token); without it H is 1 at
 // compile time and the split's bookkeeping folds away.
-template <int ACT, bool SPLIT>
+template <int ACT, bool SPLIT, bool ONE>
 __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const LayerParams a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);                // kMaxSlots mbarriers
@@ -275,7 +277,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
   const unsigned SLOT = a.sm.slot_bytes, K = a.sm.slots;
 
   const unsigned tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const unsigned T = a.T, S = a.S, d = a.d, P = d / 64, G = gridDim.x, cta = blockIdx.x;
+  const unsigned T = (ONE || SPLIT) ? 1u : a.T, S = a.S, d = a.d, P = d / 64, G = gridDim.x, cta = blockIdx.x;
 
   PHASE(0);
   pdl_signal();
@@ -689,7 +691,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
     const unsigned type = sh ? kQ80 : a.gate_type, dtype = sh ? kQ80 : a.down_type;
     const unsigned rowb = sh ? a.shared_row : a.row_bytes, nb = d / 32;
     const unsigned kn = sh ? kn_s : kn_r, ngu = sh ? ngu_s : ngu_r, dn = sh ? dn_s : dn_r, ndn = sh ? ndn_s : ndn_r;
-    const unsigned mask = s_umask[u], nt = __popc(mask), gp0 = s_upre[u];
+    const unsigned mask = (ONE || SPLIT) ? 1u : s_umask[u], nt = (ONE || SPLIT) ? 1u : __popc(mask), gp0 = s_upre[u];
     // gate/up: warp w takes neurons 4 (w % (kn/4)) .. +3 of chunk w / (kn/4),
     // eight lanes a neuron.  Lane l8 takes the 256-element spans q = l8,
     // l8+8, ... of both the gate and the up row (they share the x loads),
