@@ -298,9 +298,11 @@ static bool smem_layout(const frc_context* c, unsigned T, unsigned G, int act, u
   m.tokpair = take(2 * (T * 11));
   if (act == FRC_ACT_Q8) {
     m.xq = take(T * d);
+    m.xr = take(T * d);
     m.xp = c->g.gate_type == FRC_MXFP4 ? take(T * d) : 0;
-    m.xs = take(4 * T * P);
-    m.xv = take(4 * T * 2 * P);
+    m.xrp = c->g.gate_type == FRC_MXFP4 ? take(T * d) : 0;
+    m.xst = take(16 * T * P);
+    m.xvr = take(16 * T * P);
     m.hq = take(32 * T);
   } else {
     m.xf = take(4 * T * d);

@@ -192,21 +192,46 @@ __device__ __forceinline__ unsigned xslot(unsigned p, unsigned q, unsigned nspan
   return 4 * pos + (q ^ ((pos >> 1) & 3));
 }
 
-// ----------------------------------------------------- gate/up pair terms
-// One lane's term for x group p (64 weights = two 32-weight blocks) of a
-// gate or up row, Q8 activations.  Identical operations to the oracle's
-// pair_term.
+// ------------------------------------------------------ gate/up row terms
+// The reference multiplies every weight by the dequantized activation
+// X_j = fl32(v_j * s) (src/q4.c:54-58) and sums the products in double
+// (backends/ref.c:74-79).  With the group scale s = M * 2^E (M its 24-bit
+// significand), X_j = v_j * s + r_j * 2^E for an integer |r_j| <= 64, so each
+// block term sum_j w_j * X_j is an exact combination of two integer dots (v
+// and r against the block's integer weights) and a few scales.  The terms
+// below are formed exactly in double and accumulated in double: the gate/up
+// value narrowed to fp32 is then the reference's own, and the Q8 rounding of
+// the hidden slice sees the same inputs.
 
-struct XQ {  // one token's quantized activations in shared memory
-  const uint8_t* q;   // swizzled natural-order int8, d bytes
-  const uint8_t* qp;  // swizzled prmt-order int8 (MXFP4 rows), d bytes
-  const float* v;     // per-32 sums of q, d/32
+// Exact int32 -> double: 2^52 + 2^51 + k carries k in its low bits.
+__device__ __forceinline__ double i2d(int k) {
+  return __hiloint2double(0x43380000 + (k >> 31), k) - 6755399441055744.0;
+}
+// 2^e as a double, -1022 <= e <= 1023.
+__device__ __forceinline__ double pow2d(int e) { return __hiloint2double((e + 1023) << 20, 0); }
+// Exact small-int float -> int (|v| < 2^22).
+__device__ __forceinline__ int f2i_small(float v) {
+  return __float_as_int(__fadd_rn(v, 12582912.0f)) - 0x4B400000;
+}
+// Exponent field of a group scale with subnormals counted as 1: the scale's
+// last significand bit is 2^(ef - 150).
+__device__ __forceinline__ unsigned scale_ef(float s) { return max((__float_as_uint(s) >> 23) & 255u, 1u); }
+
+// One token's quantized activations in shared memory.  v and r are stored in
+// the same swizzled layout (xslot), in natural order for Q4_K / Q8_0 rows and
+// in prmt order for MXFP4 rows; st[p] = {s_p, 2^E_p} per 64-group; vr[p] =
+// {V, RS} of its two 32-blocks (sums of v and of r).
+struct XAct {
+  const uint8_t* v;
+  const uint8_t* r;
+  const double2* st;
+  const int4* vr;
 };
 
-__device__ __forceinline__ void load_x16(const uint8_t* xq, unsigned p, unsigned nspan, uint32_t (&x)[16]) {
+__device__ __forceinline__ void load_x8(const uint8_t* xq, unsigned p, unsigned q0, unsigned nspan, uint32_t (&x)[8]) {
 #pragma unroll
-  for (unsigned q = 0; q < 4; ++q) {
-    const uint4 w = *reinterpret_cast<const uint4*>(xq + 16 * xslot(p, q, nspan));
+  for (unsigned q = 0; q < 2; ++q) {
+    const uint4 w = *reinterpret_cast<const uint4*>(xq + 16 * xslot(p, q0 + q, nspan));
     x[4 * q] = w.x; x[4 * q + 1] = w.y; x[4 * q + 2] = w.z; x[4 * q + 3] = w.w;
   }
 }
@@ -218,38 +243,44 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
   return d;
 }
 
-// Q4_K: super-block p/4, sub-blocks 2(p%4) and 2(p%4)+1.
-__device__ __forceinline__ float term_q4k(const uint8_t* row, unsigned p, const uint32_t (&x)[16],
-                                          float v0, float v1, bool& bad) {
-  const uint8_t* b = row + (p >> 2) * 144;
-  const uint4 hdr = *reinterpret_cast<const uint4*>(b);
-  const unsigned gp = p & 3;
-  const float d = h2f(hdr.x & 0xffffu), dm = h2f(hdr.x >> 16);
-  bad |= !isfinite(d) || !isfinite(dm);
-  // 6-bit scales/mins of the eight sub-blocks (src/native.c:17-18), four per word.
-  const uint32_t sc_lo = hdr.y & 0x3f3f3f3fu, mi_lo = hdr.z & 0x3f3f3f3fu;
-  const uint32_t sc_hi = (hdr.w & 0x0f0f0f0fu) | ((hdr.y >> 6) & 0x03030303u) << 4;
-  const uint32_t mi_hi = ((hdr.w >> 4) & 0x0f0f0f0fu) | ((hdr.z >> 6) & 0x03030303u) << 4;
-  const uint32_t sw = gp >= 2 ? sc_hi : sc_lo, mw = gp >= 2 ? mi_hi : mi_lo;
-  const unsigned k0 = (2 * gp) & 3;
-  const float ds0 = __fmul_rn(d, byte_f(sw, k0)), ds1 = __fmul_rn(d, byte_f(sw, k0 + 1));
-  const float dm0 = __fmul_rn(dm, byte_f(mw, k0)), dm1 = __fmul_rn(dm, byte_f(mw, k0 + 1));
-  const uint4* qs = reinterpret_cast<const uint4*>(b + 16 + 32 * gp);
-  const uint4 qa = qs[0], qb = qs[1];
+// Q4_K super-block header: fp16 d / dmin, and the eight 6-bit scales and
+// mins (src/native.c:17-18) as bytes, sub-blocks 0-3 in sc[0]/mi[0] and 4-7
+// in sc[1]/mi[1].
+struct Q4KHead {
+  float d, m;
+  uint32_t sc[2], mi[2];
+  __device__ __forceinline__ explicit Q4KHead(const uint4 h) {
+    d = h2f(h.x & 0xffffu);
+    m = h2f(h.x >> 16);
+    sc[0] = h.y & 0x3f3f3f3fu;
+    mi[0] = h.z & 0x3f3f3f3fu;
+    sc[1] = (h.w & 0x0f0f0f0fu) | ((h.y >> 6) & 0x03030303u) << 4;
+    mi[1] = ((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 6) & 0x03030303u) << 4;
+  }
+  __device__ __forceinline__ bool ok() const { return isfinite(d) && isfinite(m); }
+};
+
+// Integer dots of one Q4_K group (64 weights: the low nibbles are sub-block
+// 2gp, the high nibbles 2gp+1) against v and r: I0, I1, R0, R1.
+__device__ __forceinline__ void q4k_idots(const uint8_t* qs, const uint32_t (&xlo)[8], const uint32_t (&rlo)[8],
+                                          const uint32_t (&xhi)[8], const uint32_t (&rhi)[8], int& i0, int& i1,
+                                          int& r0, int& r1) {
+  const uint4 qa = reinterpret_cast<const uint4*>(qs)[0], qb = reinterpret_cast<const uint4*>(qs)[1];
   const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-  int i0 = 0, i1 = 0;
+  i0 = i1 = r0 = r1 = 0;
 #pragma unroll
   for (unsigned m = 0; m < 8; ++m) {
-    i0 = __dp4a(static_cast<int>(w[m] & 0x0f0f0f0fu), static_cast<int>(x[m]), i0);
-    i1 = dp4a_us(w[m] & 0xf0f0f0f0u, x[8 + m], i1);  // 16x the high-nibble dot
+    const uint32_t lo = w[m] & 0x0f0f0f0fu, hi = w[m] & 0xf0f0f0f0u;
+    i0 = __dp4a(static_cast<int>(lo), static_cast<int>(xlo[m]), i0);
+    r0 = __dp4a(static_cast<int>(lo), static_cast<int>(rlo[m]), r0);
+    i1 = dp4a_us(hi, xhi[m], i1);  // 16x the high-nibble dot
+    r1 = dp4a_us(hi, rhi[m], r1);
   }
-  i1 >>= 4;  // exact: a multiple of 16
-  const float dot = __fmaf_rn(ds1, i2f(i1), __fmul_rn(ds0, i2f(i0)));
-  const float mins = __fmaf_rn(dm1, v1, __fmul_rn(dm0, v0));
-  return __fsub_rn(dot, mins);
+  i1 >>= 4;  // exact: multiples of 16
+  r1 >>= 4;
 }
 
-// MXFP4 device row: [e: nb bytes][qs: nb x 16 bytes]; x in prmt order.
+// MXFP4 device row: [e: nb bytes][qs: nb x 16 bytes]; x and r in prmt order.
 __device__ __forceinline__ int idot_mxfp4_16(const uint4 q, const uint32_t* x) {
   const uint32_t w[4] = {q.x, q.y, q.z, q.w};
   int ip = 0, in = 0;
@@ -263,36 +294,71 @@ __device__ __forceinline__ int idot_mxfp4_16(const uint4 q, const uint32_t* x) {
   }
   return ip - in;
 }
-__device__ __forceinline__ float term_mxfp4(const uint8_t* row, unsigned nb, unsigned p,
-                                            const uint32_t (&x)[16], bool& bad) {
+// The same block against v and r at once (the E2M1 lookups are shared).
+__device__ __forceinline__ void idot2_mxfp4_16(const uint4 q, const uint32_t* x, const uint32_t* r, int& I, int& R) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+  int ip = 0, in = 0, rp = 0, rn = 0;
+#pragma unroll
+  for (unsigned m = 0; m < 4; ++m) {
+    const uint32_t lo = w[m], hi = w[m] >> 16;
+    const int pl = static_cast<int>(prmt(kE2M1Lo, kE2M1Hi, lo)), nl = static_cast<int>(prmt(kE2M1Lo, kE2M1Hi, lo ^ 0x8888u));
+    const int ph = static_cast<int>(prmt(kE2M1Lo, kE2M1Hi, hi)), nh = static_cast<int>(prmt(kE2M1Lo, kE2M1Hi, hi ^ 0x8888u));
+    ip = __dp4a(pl, static_cast<int>(x[2 * m]), ip);
+    in = __dp4a(nl, static_cast<int>(x[2 * m]), in);
+    rp = __dp4a(pl, static_cast<int>(r[2 * m]), rp);
+    rn = __dp4a(nl, static_cast<int>(r[2 * m]), rn);
+    ip = __dp4a(ph, static_cast<int>(x[2 * m + 1]), ip);
+    in = __dp4a(nh, static_cast<int>(x[2 * m + 1]), in);
+    rp = __dp4a(ph, static_cast<int>(r[2 * m + 1]), rp);
+    rn = __dp4a(nh, static_cast<int>(r[2 * m + 1]), rn);
+  }
+  I = ip - in;
+  R = rp - rn;
+}
+
+// acc + c * (s * I + t * R): the inner value is exact (|s * I| < 2^40 ulps of
+// t), one rounding in the fma.
+__device__ __forceinline__ double block_acc(double acc, double c, const double2 st, int I, int R) {
+  return fma(c, fma(st.x, i2d(I), st.y * i2d(R)), acc);
+}
+
+// Exact group terms (64 weights = blocks 2p, 2p+1) of an MXFP4 row.
+__device__ __forceinline__ double group_mxfp4(double acc, const uint8_t* row, unsigned nb, unsigned p,
+                                              const uint32_t (&x)[16], const uint32_t (&r)[16], const double2 st,
+                                              bool& bad) {
   const unsigned e0 = row[2 * p], e1 = row[2 * p + 1];
   bad |= e0 == 255 || e1 == 255;
   const uint4* qs = reinterpret_cast<const uint4*>(row + nb + 32 * p);
-  const int i0 = idot_mxfp4_16(qs[0], x), i1 = idot_mxfp4_16(qs[1], x + 8);
-  return __fmaf_rn(pow2_m128(e1), i2f(i1), __fmul_rn(pow2_m128(e0), i2f(i0)));
+  int I0, R0, I1, R1;
+  idot2_mxfp4_16(qs[0], x, r, I0, R0);
+  idot2_mxfp4_16(qs[1], x + 8, r + 8, I1, R1);
+  acc = block_acc(acc, pow2d(static_cast<int>(e0) - 128), st, I0, R0);
+  return block_acc(acc, pow2d(static_cast<int>(e1) - 128), st, I1, R1);
 }
 
-// Q8_0 device row: [d: nb x 2 bytes][qs: nb x 32 bytes]; x in natural order.
-__device__ __forceinline__ float term_q80(const uint8_t* row, unsigned nb, unsigned p,
-                                          const uint32_t (&x)[16], bool& bad) {
+// Q8_0 device row: [d: nb x 2 bytes][qs: nb x 32 bytes]; x and r in natural order.
+__device__ __forceinline__ double group_q80(double acc, const uint8_t* row, unsigned nb, unsigned p,
+                                            const uint32_t (&x)[16], const uint32_t (&r)[16], const double2 st,
+                                            bool& bad) {
   const uint32_t dd = *reinterpret_cast<const uint32_t*>(row + 4 * p);
   const float s0 = h2f(dd & 0xffffu), s1 = h2f(dd >> 16);
   bad |= !isfinite(s0) || !isfinite(s1);
   const uint4* qs = reinterpret_cast<const uint4*>(row + 2 * nb + 64 * p);
-  int i0 = 0, i1 = 0;
+  int i0 = 0, i1 = 0, r0 = 0, r1 = 0;
 #pragma unroll
   for (unsigned q = 0; q < 2; ++q) {
     const uint4 a = qs[q], b = qs[2 + q];
-    i0 = __dp4a(static_cast<int>(a.x), static_cast<int>(x[4 * q]), i0);
-    i0 = __dp4a(static_cast<int>(a.y), static_cast<int>(x[4 * q + 1]), i0);
-    i0 = __dp4a(static_cast<int>(a.z), static_cast<int>(x[4 * q + 2]), i0);
-    i0 = __dp4a(static_cast<int>(a.w), static_cast<int>(x[4 * q + 3]), i0);
-    i1 = __dp4a(static_cast<int>(b.x), static_cast<int>(x[8 + 4 * q]), i1);
-    i1 = __dp4a(static_cast<int>(b.y), static_cast<int>(x[8 + 4 * q + 1]), i1);
-    i1 = __dp4a(static_cast<int>(b.z), static_cast<int>(x[8 + 4 * q + 2]), i1);
-    i1 = __dp4a(static_cast<int>(b.w), static_cast<int>(x[8 + 4 * q + 3]), i1);
+    const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (unsigned k = 0; k < 4; ++k) {
+      i0 = __dp4a(static_cast<int>(wa[k]), static_cast<int>(x[4 * q + k]), i0);
+      r0 = __dp4a(static_cast<int>(wa[k]), static_cast<int>(r[4 * q + k]), r0);
+      i1 = __dp4a(static_cast<int>(wb[k]), static_cast<int>(x[8 + 4 * q + k]), i1);
+      r1 = __dp4a(static_cast<int>(wb[k]), static_cast<int>(r[8 + 4 * q + k]), r1);
+    }
   }
-  return __fmaf_rn(s1, i2f(i1), __fmul_rn(s0, i2f(i0)));
+  acc = block_acc(acc, static_cast<double>(s0), st, i0, r0);
+  return block_acc(acc, static_cast<double>(s1), st, i1, r1);
 }
 
 // ------------------------------------------------- exact fp32 weight decode

@@ -57,7 +57,10 @@ struct LayerCtl {
 // item into ring slots (computed on the host).
 struct LayerSmem {
   unsigned ids, gates, first, uid, umask, ugate, upre, rms, bases, rpart, tokpair;
-  unsigned xq, xp, xs, xv, xf, gv, uv, hq, hg, ylocal, ring, total;
+  // activations: v and r in natural order (xq, xr) and prmt order (xp, xrp;
+  // MXFP4 gate/up only), {s, 2^E} per 64-group (xst), {V, RS} per 32-block
+  // (xvr); fp32 activations (xf, the F32 mode)
+  unsigned xq, xr, xp, xrp, xst, xvr, xf, gv, uv, hq, hg, ylocal, ring, total;
   unsigned slot_bytes, slots;
   unsigned kn_r, kn_s;  // neurons per gate/up chunk: routed, shared items (powers of two)
   unsigned dn_r, dn_s;  // rows per down chunk: routed, shared items (multiples of 16)
@@ -163,34 +166,88 @@ __device__ __forceinline__ bool grid_sync(LayerCtl* ctl, unsigned* flag_smem, un
 #define PHASE(k) PHASE_AT(k, 0)
 
 // One lane's gate and up sums over its 256-weight spans q = l8, l8+8, ...
-// (Q8 activations, groups in order).  One instantiation per weight type, so
-// the code a launch runs is one contiguous block.
+// (Q8 activations, groups in order), in double and exact up to double
+// rounding (see the row terms in frc_device.cuh).  Q4_K spans are
+// super-blocks: per group p the integer combinations K1 = sc0*I0 + sc1*I1,
+// K3 = sc0*R0 + sc1*R1, K2 = mi0*V0 + mi1*V1, K4 = mi0*RS0 + mi1*RS1 enter
+// PP = s*K1 + 2^E*K3 and QQ = s*K2 + 2^E*K4 (fma each), and the span adds
+// d*PP - dmin*QQ.  One instantiation per weight type, so the code a launch
+// runs is one contiguous block.
 template <unsigned TYPE>
-__device__ __forceinline__ void gu_sums(const uint8_t* gr, const uint8_t* ur, const uint8_t* xq, const float* xs,
-                                        const float* xv, unsigned l8, unsigned nspan, unsigned nb, bool& bad,
-                                        float& ag, float& au) {
+__device__ __forceinline__ void gu_sums(const uint8_t* gr, const uint8_t* ur, const XAct& xa, unsigned l8,
+                                        unsigned nspan, unsigned nb, bool& bad, double& ag, double& au) {
   for (unsigned q = l8; q < nspan; q += 8) {
+    if (TYPE == kQ4K) {
+      const uint8_t* bg = gr + q * 144;
+      const uint8_t* bu = ur + q * 144;
+      const Q4KHead hg(*reinterpret_cast<const uint4*>(bg)), hu(*reinterpret_cast<const uint4*>(bu));
+      bad |= !hg.ok() || !hu.ok();
+      double pg = 0.0, qg = 0.0, pu = 0.0, qu = 0.0;
 #pragma unroll
-    for (unsigned gp = 0; gp < 4; ++gp) {
-      const unsigned p = 4 * q + gp;
-      uint32_t xw[16];
-      load_x16(xq, p, nspan, xw);
-      float tg, tu;
-      if (TYPE == kQ4K) {
-        const float v0 = xv[2 * p], v1 = xv[2 * p + 1];
-        tg = term_q4k(gr, p, xw, v0, v1, bad);
-        tu = term_q4k(ur, p, xw, v0, v1, bad);
-      } else if (TYPE == kMXFP4) {
-        tg = term_mxfp4(gr, nb, p, xw, bad);
-        tu = term_mxfp4(ur, nb, p, xw, bad);
-      } else {
-        tg = term_q80(gr, nb, p, xw, bad);
-        tu = term_q80(ur, nb, p, xw, bad);
+      for (unsigned gp = 0; gp < 4; ++gp) {
+        const unsigned p = 4 * q + gp, half = gp >> 1, sh = 16 * (gp & 1);
+        uint32_t xlo[8], rlo[8], xhi[8], rhi[8];
+        load_x8(xa.v, p, 0, nspan, xlo);
+        load_x8(xa.r, p, 0, nspan, rlo);
+        load_x8(xa.v, p, 2, nspan, xhi);
+        load_x8(xa.r, p, 2, nspan, rhi);
+        const double2 st = xa.st[p];
+        const int4 vr = xa.vr[p];
+        int i0, i1, r0, r1;
+        q4k_idots(bg + 16 + 32 * gp, xlo, rlo, xhi, rhi, i0, i1, r0, r1);
+        {
+          const int sc0 = (hg.sc[half] >> sh) & 0xff, sc1 = (hg.sc[half] >> (sh + 8)) & 0xff;
+          const int mi0 = (hg.mi[half] >> sh) & 0xff, mi1 = (hg.mi[half] >> (sh + 8)) & 0xff;
+          pg = fma(st.x, i2d(sc0 * i0 + sc1 * i1), pg);
+          pg = fma(st.y, i2d(sc0 * r0 + sc1 * r1), pg);
+          qg = fma(st.x, i2d(mi0 * vr.x + mi1 * vr.z), qg);
+          qg = fma(st.y, i2d(mi0 * vr.y + mi1 * vr.w), qg);
+        }
+        q4k_idots(bu + 16 + 32 * gp, xlo, rlo, xhi, rhi, i0, i1, r0, r1);
+        {
+          const int sc0 = (hu.sc[half] >> sh) & 0xff, sc1 = (hu.sc[half] >> (sh + 8)) & 0xff;
+          const int mi0 = (hu.mi[half] >> sh) & 0xff, mi1 = (hu.mi[half] >> (sh + 8)) & 0xff;
+          pu = fma(st.x, i2d(sc0 * i0 + sc1 * i1), pu);
+          pu = fma(st.y, i2d(sc0 * r0 + sc1 * r1), pu);
+          qu = fma(st.x, i2d(mi0 * vr.x + mi1 * vr.z), qu);
+          qu = fma(st.y, i2d(mi0 * vr.y + mi1 * vr.w), qu);
+        }
       }
-      ag = __fmaf_rn(xs[p], tg, ag);
-      au = __fmaf_rn(xs[p], tu, au);
+      ag = fma(static_cast<double>(hg.d), pg, ag);
+      ag = fma(-static_cast<double>(hg.m), qg, ag);
+      au = fma(static_cast<double>(hu.d), pu, au);
+      au = fma(-static_cast<double>(hu.m), qu, au);
+    } else {
+#pragma unroll
+      for (unsigned gp = 0; gp < 4; ++gp) {
+        const unsigned p = 4 * q + gp;
+        uint32_t xw[16], rw[16];
+        uint32_t(&x0)[8] = *reinterpret_cast<uint32_t(*)[8]>(xw);
+        uint32_t(&x1)[8] = *reinterpret_cast<uint32_t(*)[8]>(xw + 8);
+        uint32_t(&r0)[8] = *reinterpret_cast<uint32_t(*)[8]>(rw);
+        uint32_t(&r1)[8] = *reinterpret_cast<uint32_t(*)[8]>(rw + 8);
+        load_x8(xa.v, p, 0, nspan, x0);
+        load_x8(xa.v, p, 2, nspan, x1);
+        load_x8(xa.r, p, 0, nspan, r0);
+        load_x8(xa.r, p, 2, nspan, r1);
+        const double2 st = xa.st[p];
+        if (TYPE == kMXFP4) {
+          ag = group_mxfp4(ag, gr, nb, p, xw, rw, st, bad);
+          au = group_mxfp4(au, ur, nb, p, xw, rw, st, bad);
+        } else {
+          ag = group_q80(ag, gr, nb, p, xw, rw, st, bad);
+          au = group_q80(au, ur, nb, p, xw, rw, st, bad);
+        }
+      }
     }
   }
+}
+
+// The reference's narrowing of a double sum to fp32 (backends/ref.c:37-40).
+__device__ __forceinline__ bool narrow(double v, float* out) {
+  if (!isfinite(v) || fabs(v) > 3.4028234663852886e38) return false;
+  *out = __double2float_rn(v);
+  return true;
 }
 
 // Down term c of row rr of a staged down chunk ([nr scales][nr payloads]),
@@ -598,7 +655,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
       const Q8Group qg(amax);
-      int qv[16], sum = 0;
+      int qv[16], rv[16], sum = 0, rsum = 0;
       if (__builtin_expect(qg.mul_ok(), 1)) {
 #pragma unroll
         for (unsigned k = 0; k < 16; ++k) {
@@ -612,22 +669,47 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
           sum += qv[k];
         }
       }
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);  // quarters 0+1 and 2+3: the two 32-element halves
-      uint32_t w[4];
+      // Residuals of the reference's dequantized values (src/q4.c:54-58):
+      // X = fl32(v * s), capped at FLT_MAX; X - v*s = r * 2^E exactly, E =
+      // ef - 150.  The fma gives X - v*s exactly; two power-of-two scalings
+      // (each representable) take it to r.
+      const unsigned ef = scale_ef(qg.scale), shr = 150 - ef;
+      const float f1 = __uint_as_float((127 + (shr >> 1)) << 23), f2 = __uint_as_float((127 + shr - (shr >> 1)) << 23);
 #pragma unroll
-      for (unsigned k = 0; k < 4; ++k)
+      for (unsigned k = 0; k < 16; ++k) {
+        const float vf = i2f(qv[k]);
+        float X = __fmul_rn(vf, qg.scale);
+        if (fabsf(X) > 3.40282347e38f) X = copysignf(3.40282347e38f, vf);
+        rv[k] = f2i_small(__fmul_rn(__fmul_rn(__fmaf_rn(-vf, qg.scale, X), f1), f2));
+        rsum += rv[k];
+      }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);  // quarters 0+1 and 2+3: the two 32-element halves
+      rsum += __shfl_xor_sync(0xffffffffu, rsum, 1);
+      uint32_t w[4], wr[4];
+#pragma unroll
+      for (unsigned k = 0; k < 4; ++k) {
         w[k] = (qv[4 * k] & 0xff) | (qv[4 * k + 1] & 0xff) << 8 | (qv[4 * k + 2] & 0xff) << 16 |
                static_cast<uint32_t>(qv[4 * k + 3] & 0xff) << 24;
-      *reinterpret_cast<uint4*>(smem + a.sm.xq + t * d + 16 * xslot(p, qd, d / 256)) = make_uint4(w[0], w[1], w[2], w[3]);
-      if (qd == 0) reinterpret_cast<float*>(smem + a.sm.xs)[t * P + p] = qg.scale;
+        wr[k] = (rv[4 * k] & 0xff) | (rv[4 * k + 1] & 0xff) << 8 | (rv[4 * k + 2] & 0xff) << 16 |
+                static_cast<uint32_t>(rv[4 * k + 3] & 0xff) << 24;
+      }
+      const unsigned slot16 = 16 * xslot(p, qd, d / 256);
+      *reinterpret_cast<uint4*>(smem + a.sm.xq + t * d + slot16) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(smem + a.sm.xr + t * d + slot16) = make_uint4(wr[0], wr[1], wr[2], wr[3]);
+      if (qd == 0)
+        reinterpret_cast<double2*>(smem + a.sm.xst)[t * P + p] =
+            make_double2(static_cast<double>(qg.scale), pow2d(static_cast<int>(ef) - 150));
       if ((qd & 1) == 0)
-        reinterpret_cast<float*>(smem + a.sm.xv)[t * 2 * P + 2 * p + (qd >> 1)] = static_cast<float>(sum);
+        reinterpret_cast<int2*>(smem + a.sm.xvr)[2 * (t * P + p) + (qd >> 1)] = make_int2(sum, rsum);
       if (a.sm.xp) {
         uint8_t* xp = smem + a.sm.xp + t * d;
+        uint8_t* xrp = smem + a.sm.xrp + t * d;
 #pragma unroll
         for (unsigned k = 0; k < 16; ++k) {
           const unsigned e = 16 * qd + k, wi = (e / 32) * 32 + prmt_pos(e % 32);
-          xp[16 * xslot(p, wi / 16, d / 256) + wi % 16] = static_cast<uint8_t>(qv[k] & 0xff);
+          const unsigned at = 16 * xslot(p, wi / 16, d / 256) + wi % 16;
+          xp[at] = static_cast<uint8_t>(qv[k] & 0xff);
+          xrp[at] = static_cast<uint8_t>(rv[k] & 0xff);
         }
       }
     }
@@ -713,13 +795,22 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
           const unsigned t = __ffs(mm) - 1;
           mm &= mm - 1;
           float ag = 0.0f, au = 0.0f;
+          bool nar = true;
           if (ACT == FRC_ACT_Q8) {
-            const uint8_t* xq = smem + (type == kMXFP4 ? a.sm.xp : a.sm.xq) + t * d;
-            const float* xs = reinterpret_cast<const float*>(smem + a.sm.xs) + t * P;
-            const float* xv = reinterpret_cast<const float*>(smem + a.sm.xv) + t * 2 * P;
-            if (type == kQ4K) gu_sums<kQ4K>(gr, ur, xq, xs, xv, l8, nspan, nb, bad, ag, au);
-            else if (type == kMXFP4) gu_sums<kMXFP4>(gr, ur, xq, xs, xv, l8, nspan, nb, bad, ag, au);
-            else gu_sums<kQ80>(gr, ur, xq, xs, xv, l8, nspan, nb, bad, ag, au);
+            const bool mx = type == kMXFP4;
+            const XAct xa{smem + (mx ? a.sm.xp : a.sm.xq) + t * d, smem + (mx ? a.sm.xrp : a.sm.xr) + t * d,
+                          reinterpret_cast<const double2*>(smem + a.sm.xst) + t * P,
+                          reinterpret_cast<const int4*>(smem + a.sm.xvr) + t * P};
+            double dg = 0.0, du = 0.0;
+            if (type == kQ4K) gu_sums<kQ4K>(gr, ur, xa, l8, nspan, nb, bad, dg, du);
+            else if (mx) gu_sums<kMXFP4>(gr, ur, xa, l8, nspan, nb, bad, dg, du);
+            else gu_sums<kQ80>(gr, ur, xa, l8, nspan, nb, bad, dg, du);
+#pragma unroll
+            for (unsigned o = 4; o; o >>= 1) {
+              dg = __dadd_rn(dg, __shfl_xor_sync(0xffffffffu, dg, o));
+              du = __dadd_rn(du, __shfl_xor_sync(0xffffffffu, du, o));
+            }
+            nar = narrow(dg, &ag) && narrow(du, &au);
           } else {
             const float* xf = reinterpret_cast<const float*>(smem + a.sm.xf) + t * d;
             for (unsigned q = l8; q < nspan; q += 8)
@@ -729,15 +820,15 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
                 ag = __fmaf_rn(wg, xf[e], ag);
                 au = __fmaf_rn(wu, xf[e], au);
               }
-          }
 #pragma unroll
-          for (unsigned o = 4; o; o >>= 1) {
-            ag = __fadd_rn(ag, __shfl_xor_sync(0xffffffffu, ag, o));
-            au = __fadd_rn(au, __shfl_xor_sync(0xffffffffu, au, o));
+            for (unsigned o = 4; o; o >>= 1) {
+              ag = __fadd_rn(ag, __shfl_xor_sync(0xffffffffu, ag, o));
+              au = __fadd_rn(au, __shfl_xor_sync(0xffffffffu, au, o));
+            }
           }
           if (l8 == 0) {
             float h = 0.0f;
-            if (!isfinite(ag) || !isfinite(au) || !swiglu(ag, au, &h)) {
+            if (!nar || !isfinite(ag) || !isfinite(au) || !swiglu(ag, au, &h)) {
               bad = true;
               h = 0.0f;
             }

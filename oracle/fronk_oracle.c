@@ -354,65 +354,119 @@ static int block_scale(const uint8_t *p, unsigned type, unsigned blk, float *s) 
     return isfinite(*s);
 }
 
+/* One token's quantized activations as the GPU holds them.  The reference
+ * multiplies each weight by the dequantized activation X_j = fl32(v_j * s)
+ * (src/q4.c:54-58).  With s = M * 2^E (M the 24-bit significand of the
+ * group's scale, E the exponent of its last bit), X_j - v_j * s = r_j * 2^E
+ * for an integer r_j with |r_j| <= 64 (the product has at most 31
+ * significant bits, so rounding drops at most seven).  Hence every block term
+ * of the reference's sum is an exact combination of two integer dots, one
+ * against v and one against r. */
 typedef struct {
     unsigned d;
-    const int8_t *q;     /* [d] */
-    const float *scale;  /* [d/64] */
-    const int32_t *sum;  /* [d/32] sums of q per 32 */
+    const int8_t *q;     /* [d] v */
+    const int8_t *r;     /* [d] rounding residuals of the dequantized values */
+    const float *scale;  /* [d/64] s */
+    const double *ulp;   /* [d/64] 2^E */
+    const int32_t *sum;  /* [d/32] sums of v per 32 */
+    const int32_t *rsum; /* [d/32] sums of r per 32 */
 } qx;
 
-/* The term lane L adds for x group p (64 weights): see the kernel's
- * gateup_pair_*.  Returns 0 on a nonfinite scale. */
-static int pair_term(const uint8_t *row, unsigned type, unsigned p, const qx *x, float *term) {
-    const int8_t *v = x->q + 64 * p;
-    if (type == OR_Q4_K) {
-        const uint8_t *b = row + (size_t)(p / 4) * 144;
-        unsigned gp = p % 4, sc0, mi0, sc1, mi1;
-        float d = or_f16(le16(b)), dm = or_f16(le16(b + 2));
-        if (!isfinite(d) || !isfinite(dm)) return 0;
-        q4k_scale_min(b + 4, 2 * gp, &sc0, &mi0);
-        q4k_scale_min(b + 4, 2 * gp + 1, &sc1, &mi1);
-        int32_t i0 = 0, i1 = 0;
-        for (unsigned j = 0; j < 32; ++j) {
-            uint8_t byte = b[16 + 32 * gp + j];
-            i0 += (int32_t)(byte & 15) * v[j];
-            i1 += (int32_t)(byte >> 4) * v[32 + j];
-        }
-        float ds0 = d * (float)sc0, ds1 = d * (float)sc1, dm0 = dm * (float)mi0, dm1 = dm * (float)mi1;
-        float f0 = (float)x->sum[2 * p], f1 = (float)x->sum[2 * p + 1];
-        float dot = fmaf(ds1, (float)i1, ds0 * (float)i0);
-        float mins = fmaf(dm1, f1, dm0 * f0);
-        *term = dot - mins;
-        return 1;
-    }
-    float s0, s1;
-    if (!block_scale(row, type, 2 * p, &s0) || !block_scale(row, type, 2 * p + 1, &s1)) return 0;
-    int32_t i0 = idot_block(row, type, 2 * p, v), i1 = idot_block(row, type, 2 * p + 1, v + 32);
-    *term = fmaf(s1, (float)i1, s0 * (float)i0);
-    return 1;
+/* 2^E for a group scale s (E = the exponent of s's last significand bit). */
+static double scale_ulp(float s) {
+    uint32_t bits;
+    memcpy(&bits, &s, sizeof bits);
+    int ef = (int)((bits >> 23) & 255u);
+    return ldexp(1.0, (ef ? ef : 1) - 150);
 }
 
-/* One gate or up dot as the kernel forms it: eight lanes share the row;
- * lane L takes the 256-element spans (four x groups of 64: a Q4_K
- * super-block, eight MXFP4 / Q8_0 blocks) q = L, L+8, ..., and within a span
- * its groups in order, accumulating fmaf(scale[p], term, acc); then a
- * butterfly over the eight lanes (xor 4, 2, 1). */
+/* The residuals r_j of one token (see qx), dequantizing exactly as
+ * src/q4.c:54-58 does (the FLT_MAX cap included). */
+static void q8_residuals(const int8_t *v, const float *scale, unsigned d, int8_t *r) {
+    for (unsigned j = 0; j < d; ++j) {
+        const float s = scale[j / 64];
+        double deq = (double)v[j] * s;
+        if (deq > FLT_MAX) deq = FLT_MAX;
+        if (deq < -FLT_MAX) deq = -FLT_MAX;
+        const float X = (float)deq;
+        r[j] = (int8_t)(((double)X - (double)v[j] * s) / scale_ulp(s));
+    }
+}
+
+/* The gate or up dot of one row as the GPU forms it, which is the reference's
+ * sum of w_j * X_j carried out exactly up to double rounding.  Eight lanes
+ * share the row; lane L takes the 256-element spans (four x groups of 64: a
+ * Q4_K super-block, eight MXFP4 / Q8_0 blocks) q = L, L+8, ...; then a
+ * butterfly over the eight lanes (xor 4, 2, 1), in double.
+ *   Q4_K super-block (d, dmin; sub-block scales sc, mins mi; w = d*sc*q -
+ *   dmin*mi, the reference's fp32 weight when that subtraction is exact):
+ *     per group p (sub-blocks k = 2gp, 2gp+1; I_k = sum q*v, R_k = sum q*r,
+ *     V_k = sum v, RS_k = sum r):
+ *       K1 = sc0*I0 + sc1*I1, K3 = sc0*R0 + sc1*R1,
+ *       K2 = mi0*V0 + mi1*V1, K4 = mi0*RS0 + mi1*RS1  (exact integers)
+ *       PP = fma(s, K1, PP); PP = fma(2^E, K3, PP)
+ *       QQ = fma(s, K2, QQ); QQ = fma(2^E, K4, QQ)
+ *     acc = fma(d, PP, acc); acc = fma(-dmin, QQ, acc)
+ *   MXFP4 / Q8_0 block b of group p (c = 2^(e-128) with the doubled E2M1
+ *   table, or the fp16 scale):
+ *       acc = fma(c, fma(s, I_b, 2^E * R_b), acc)   (the inner value is exact)
+ * Returns OR_NUMERIC on a nonfinite scale. */
 enum { PORT_ROW_LANES = 8 };
-static int lane_dot(const uint8_t *row, unsigned type, const qx *x, float *out) {
-    float lane[PORT_ROW_LANES];
+static int lane_dot(const uint8_t *row, unsigned type, const qx *x, double *out) {
+    double lane[PORT_ROW_LANES];
     const unsigned spans = x->d / 256;
     for (unsigned L = 0; L < PORT_ROW_LANES; ++L) {
-        float acc = 0;
-        for (unsigned q = L; q < spans; q += PORT_ROW_LANES)
-            for (unsigned p = 4 * q; p < 4 * q + 4; ++p) {
-                float term;
-                if (!pair_term(row, type, p, x, &term)) return OR_NUMERIC;
-                acc = fmaf(x->scale[p], term, acc);
+        double acc = 0;
+        for (unsigned q = L; q < spans; q += PORT_ROW_LANES) {
+            if (type == OR_Q4_K) {
+                const uint8_t *b = row + (size_t)q * 144;
+                const float d = or_f16(le16(b)), dm = or_f16(le16(b + 2));
+                if (!isfinite(d) || !isfinite(dm)) return OR_NUMERIC;
+                double PP = 0, QQ = 0;
+                for (unsigned gp = 0; gp < 4; ++gp) {
+                    const unsigned p = 4 * q + gp;
+                    const int8_t *v = x->q + 64 * p, *r = x->r + 64 * p;
+                    unsigned sc0, mi0, sc1, mi1;
+                    q4k_scale_min(b + 4, 2 * gp, &sc0, &mi0);
+                    q4k_scale_min(b + 4, 2 * gp + 1, &sc1, &mi1);
+                    int32_t i0 = 0, i1 = 0, r0 = 0, r1 = 0;
+                    for (unsigned j = 0; j < 32; ++j) {
+                        const uint8_t byte = b[16 + 32 * gp + j];
+                        i0 += (int32_t)(byte & 15) * v[j];
+                        i1 += (int32_t)(byte >> 4) * v[32 + j];
+                        r0 += (int32_t)(byte & 15) * r[j];
+                        r1 += (int32_t)(byte >> 4) * r[32 + j];
+                    }
+                    const int32_t K1 = (int32_t)sc0 * i0 + (int32_t)sc1 * i1, K3 = (int32_t)sc0 * r0 + (int32_t)sc1 * r1;
+                    const int32_t K2 = (int32_t)mi0 * x->sum[2 * p] + (int32_t)mi1 * x->sum[2 * p + 1];
+                    const int32_t K4 = (int32_t)mi0 * x->rsum[2 * p] + (int32_t)mi1 * x->rsum[2 * p + 1];
+                    const double s = x->scale[p], t = x->ulp[p];
+                    PP = fma(s, (double)K1, PP);
+                    PP = fma(t, (double)K3, PP);
+                    QQ = fma(s, (double)K2, QQ);
+                    QQ = fma(t, (double)K4, QQ);
+                }
+                acc = fma((double)d, PP, acc);
+                acc = fma(-(double)dm, QQ, acc);
+            } else {
+                for (unsigned gp = 0; gp < 4; ++gp) {
+                    const unsigned p = 4 * q + gp;
+                    const double s = x->scale[p], t = x->ulp[p];
+                    for (unsigned k = 0; k < 2; ++k) {
+                        const unsigned blk = 2 * p + k;
+                        float c;
+                        if (!block_scale(row, type, blk, &c)) return OR_NUMERIC;
+                        const int32_t I = idot_block(row, type, blk, x->q + 32 * blk);
+                        const int32_t R = idot_block(row, type, blk, x->r + 32 * blk);
+                        acc = fma((double)c, fma(s, (double)I, t * (double)R), acc);
+                    }
+                }
             }
+        }
         lane[L] = acc;
     }
     for (unsigned off = PORT_ROW_LANES / 2; off; off >>= 1) {
-        float next[PORT_ROW_LANES];
+        double next[PORT_ROW_LANES];
         for (unsigned L = 0; L < PORT_ROW_LANES; ++L) next[L] = lane[L] + lane[L ^ off];
         memcpy(lane, next, sizeof lane);
     }
@@ -464,19 +518,26 @@ int or_port_run(const or_model *m, unsigned tokens, const uint16_t *expert, cons
     for (unsigned b = 0; b < OR_BLOCKS; ++b) if (m->layer[b]) blocks[S++] = b;
 
     /* Activations: int8 per 64-group scale, per-32 sums. */
-    static int8_t q[OR_MAX_TOKENS][8192];
+    static int8_t q[OR_MAX_TOKENS][8192], res[OR_MAX_TOKENS][8192];
     static float scale[OR_MAX_TOKENS][128];
-    static int32_t sums[OR_MAX_TOKENS][256];
+    static double ulp[OR_MAX_TOKENS][128];
+    static int32_t sums[OR_MAX_TOKENS][256], rsums[OR_MAX_TOKENS][256];
     qx xs[OR_MAX_TOKENS];
     for (unsigned t = 0; t < tokens; ++t) {
         rc = or_q8_quantize(x + (size_t)t * d, d, q[t], scale[t]);
         if (rc) return rc;
+        q8_residuals(q[t], scale[t], d, res[t]);
+        for (unsigned k = 0; k < d / 64; ++k) ulp[t][k] = scale_ulp(scale[t][k]);
         for (unsigned k = 0; k < d / 32; ++k) {
-            int32_t s = 0;
-            for (unsigned j = 0; j < 32; ++j) s += q[t][32 * k + j];
+            int32_t s = 0, sr = 0;
+            for (unsigned j = 0; j < 32; ++j) {
+                s += q[t][32 * k + j];
+                sr += res[t][32 * k + j];
+            }
             sums[t][k] = s;
+            rsums[t][k] = sr;
         }
-        xs[t] = (qx){d, q[t], scale[t], sums[t]};
+        xs[t] = (qx){d, q[t], res[t], scale[t], ulp[t], sums[t], rsums[t]};
     }
 
     size_t need = (size_t)U * S * tokens * OR_NEURONS;
@@ -508,12 +569,13 @@ int or_port_run(const or_model *m, unsigned tokens, const uint16_t *expert, cons
                 const uint8_t *p = m->layer[blocks[si]] + (size_t)uid[u] * slice;
                 float hs[OR_NEURONS], hsc;
                 for (unsigned n = 0; n < OR_NEURONS; ++n) {
+                    double ad, ud;
                     float a, uu;
-                    rc = lane_dot(p + n * in_row, in, &xs[t], &a);
+                    rc = lane_dot(p + n * in_row, in, &xs[t], &ad);
                     if (rc) goto done;
-                    rc = lane_dot(p + proj + n * in_row, in, &xs[t], &uu);
+                    rc = lane_dot(p + proj + n * in_row, in, &xs[t], &ud);
                     if (rc) goto done;
-                    if (!isfinite(a) || !isfinite(uu)) { rc = OR_NUMERIC; goto done; }
+                    if (narrow(ad, &a) || narrow(ud, &uu)) { rc = OR_NUMERIC; goto done; }
                     double sig = a >= 0 ? 1 / (1 + exp(-(double)a)) : exp((double)a) / (1 + exp((double)a));
                     if (narrow((double)a * sig * uu, &hs[n])) { rc = OR_NUMERIC; goto done; }
                 }

@@ -10,9 +10,13 @@
  *                  accumulation, the reference's order.  Pinned bit-for-bit
  *                  against the unmodified reference (compiled from its own
  *                  sources) at d = 2560 and against its golden vectors.
- *   or_port_run  - the exact integer/fp32 arithmetic the CUDA Q8 path performs
- *                  (same operations, same order); the GPU must reproduce its
- *                  hidden activations bit for bit and its output within 1e-5.
+ *   or_port_run  - the arithmetic the CUDA Q8 path performs (same operations,
+ *                  same order): integer block dots of the int8 activations
+ *                  and of their dequantization residuals, exact block terms
+ *                  summed in double (the reference's narrowed gate/up
+ *                  values), fp32 down terms; the GPU must reproduce its hidden
+ *                  activations bit for bit and its output within 1e-5, and it
+ *                  stays within 1e-5 of ref-q8.
  */
 #ifndef FRONK_ORACLE_H
 #define FRONK_ORACLE_H

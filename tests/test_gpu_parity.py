@@ -2,7 +2,8 @@
 
 Bar: bit-exact for activation quantization, block unpacking, integer block
 dots and the hidden activations; output within relative L2 1e-5 per token of
-the oracle (fp32 accumulation; in practice identical).  fp32-activation mode
+the oracle port and of the reference's ref-q8 (or_ref_run q8, pinned to the
+reference bit for bit).  fp32-activation mode
 within 1e-5 of the reference's "ref" arithmetic (or_ref_run, pinned to the
 reference bit for bit)."""
 import numpy as np
@@ -99,6 +100,10 @@ def test_layer_q8_matches_oracle(gpu, oracle, hidden, gt, dt):
             assert np.array_equal(h.view(np.uint32), h_ref.view(np.uint32)), "hidden activations"
             errs = [rel_l2(r, a) for r, a in zip(y_ref, y)]
             assert max(errs) <= TOL, errs
+            rc, y_q8 = oracle.ref_run(m, e, gate, x, 1)   # the reference's ref-q8, bit for bit
+            assert rc == OK
+            errs = [rel_l2(r, a) for r, a in zip(y_q8, y)]
+            assert max(errs) <= TOL, ("vs ref-q8", errs)
 
 
 def test_layer_q8_all_twenty_slices(gpu, oracle):
