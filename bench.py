@@ -91,52 +91,76 @@ def step_routing(steps, tokens=1):
 # ---------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock, power and clock-event (throttle) reasons of one GPU, queried
+    in-process through NVML every millisecond from a thread started before
+    set-up (queries only; nothing is set).  mark_start / mark_end bracket the
+    timed region; the summary uses the samples inside it (at least the last
+    few before mark_end when the region is shorter than a sampling period).
+    Falls back to nvidia-smi (200 ms) when NVML cannot be loaded."""
+
+    NAMES = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+             ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+             ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+             ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+             ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
 
     def __init__(self, device):
-        self.device, self.rows, self.proc = device, [], None
+        self.device, self.rows, self.stop_flag, self.t = device, [], False, None
+        self.t_start = self.t_end = None
+        self.source = "nvml"
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), "--query-gpu=" + self.Q,
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.hnd = pynvml.nvmlDeviceGetHandleByIndex(self.device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.hnd, pynvml.NVML_CLOCK_SM)
+            self.bits = {n: getattr(pynvml, c, 0) for n, c in self.NAMES}
+        except Exception:  # noqa: BLE001
+            self.nv = None
+            self.source = "unavailable"
+            return
+        self.t = threading.Thread(target=self._poll, daemon=True)
+        self.t.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
+    def _poll(self):
+        nv, h = self.nv, self.hnd
+        while not self.stop_flag:
+            try:
+                self.rows.append((time.perf_counter(), nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                  nv.nvmlDeviceGetCurrentClocksEventReasons(h),
+                                  nv.nvmlDeviceGetPowerUsage(h) / 1000.0))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.001)
+
+    def mark_start(self):
+        self.t_start = time.perf_counter()
+
+    def mark_end(self):
+        self.t_end = time.perf_counter()
 
     def stop(self):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-        sms, maxes, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            try:
-                sm, mx, util = float(r[1]), float(r[2]), float(r[4])
-            except (ValueError, IndexError):
-                continue
-            maxes.append(mx)
-            if util > 0:
-                sms.append(sm)
-            for n, v in zip(names, r[6:10]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sms:
-            sms = [float(r[1]) for r in self.rows if len(r) > 1 and r[1].replace(".", "").isdigit()]
-        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxes) if maxes else None,
-                "reasons": sorted(reasons), "samples": len(self.rows)}
+        self.stop_flag = True
+        if self.t:
+            self.t.join(timeout=2)
+        if self.nv is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": self.source}
+        lo, hi = self.t_start or 0.0, self.t_end or float("inf")
+        rows = [r for r in self.rows if lo <= r[0] <= hi]
+        if len(rows) < 3:  # a region shorter than a few polls: the polls closest before its end
+            before = [r for r in self.rows if r[0] <= hi]
+            rows = before[-3:]
+        reasons = sorted({n for r in rows for n, b in self.bits.items() if b and r[2] & b})
+        sms = [r[1] for r in rows]
+        try:
+            self.nv.nvmlShutdown()
+        except Exception:  # noqa: BLE001
+            pass
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": self.max_mhz,
+                "sm_mhz_min": min(sms) if sms else None, "power_w_max": max((r[3] for r in rows), default=None),
+                "reasons": reasons, "samples": len(rows), "source": "nvml in-process, 1 ms polls in the timed region"}
 
 
 # ------------------------------------------------------------ CPU baseline
@@ -167,7 +191,7 @@ def run_reference(args, rank):
     if rank != 0:
         return
     if args.prefill:
-        steps, warm = max(1, min(args.steps, 5)), 1
+        steps, warm = max(1, min(args.steps, 5)), max(3, min(args.warmup, 5))
         cb = prefill_cpu_baseline(steps, warm)
         if "unavailable" in cb:
             emit({"impl": "reference", "unavailable": cb["unavailable"]})
@@ -178,8 +202,10 @@ def run_reference(args, rank):
               "data": "synthetic", "config": prefill_config(args.gpus), "cpu_baseline": cb,
               "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
         return
+    # the same warm-up as this build's arm (which runs at least 3); steps capped
+    # so the CPU arm ends within minutes
     steps = max(1, min(args.steps, 50 if args.tokens == 1 else 3))
-    warm = max(1, min(args.warmup, 3 if args.tokens == 1 else 1))
+    warm = max(3, min(args.warmup, 10))
     cb = cpu_baseline(steps, warm, args.tokens)
     if "unavailable" in cb:
         emit({"impl": "reference", "unavailable": cb["unavailable"]})
@@ -350,11 +376,13 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler.mark_start()
     start.record(stream)
     for s in range(args.warmup, total):
         step(s)
     end.record(stream)
     torch.cuda.synchronize()
+    sampler.mark_end()
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
@@ -400,7 +428,11 @@ def main():
     e2e = e2e_run(ctx, fb, ex, gt, x0, e2e_steps, dist, dev, peer, T)
 
     # ---- parity at full size: one layer of the filled units vs the oracle
-    parity = full_size_parity(ctx, fb, g, pool, blocks)
+    # (at N>1 with the in-kernel reduce: the summed y over all 20 slices)
+    if world > 1 and peer:
+        parity = reduced_parity(ctx, fb, g, pool, rank, world, dist, dev)
+    else:
+        parity = full_size_parity(ctx, fb, g, pool, blocks)
 
     used_graph = graph is not None
     del graph
@@ -487,9 +519,30 @@ def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev, peer=False, T=1):
             + ", pinned host copies each layer"}
 
 
+def _host_layers(fb, g, pool, blocks, experts, layer=5):
+    """Host copies of (block, layer) for the given experts, rebuilt from the
+    pool the device filled them from (frc_pool_pick)."""
+    sb, lb = fb.slice_bytes(g), fb.layer_bytes(g)
+    layers = {}
+    for b in blocks:
+        arr = np.zeros(lb, np.uint8)
+        for ident in set(int(v) for v in np.asarray(experts).ravel()):
+            k = fb.pool_pick(SEED, b, layer, ident, POOL)
+            arr[ident * sb:(ident + 1) * sb] = pool[k * sb:(k + 1) * sb]
+        layers[b] = arr
+    return layers
+
+
+def _rel(ref, act):
+    return max(float(np.sqrt(((ref[t].astype(np.float64) - act[t]) ** 2).sum() / (ref[t].astype(np.float64) ** 2).sum()))
+               for t in range(ref.shape[0]))
+
+
 def full_size_parity(ctx, fb, g, pool, blocks):
     """Layer 5 of the filled units on a fresh request, against the oracle's
-    restatement of the same arithmetic on the host copies of the same slices."""
+    restatement of the same arithmetic (hidden values bit for bit) and against
+    the reference's ref-q8 (or_ref_run, bit-identical to the compiled fr_ref_q8)
+    on the host copies of the same slices."""
     try:
         from oracle import Oracle, Q4_K, MXFP4
     except Exception as exc:  # noqa: BLE001
@@ -500,18 +553,51 @@ def full_size_parity(ctx, fb, g, pool, blocks):
     if rc:
         return {"error": ctx.last_error}
     h = ctx.debug_hidden()
-    sb, lb = fb.slice_bytes(g), fb.layer_bytes(g)
-    layers = {}
-    for b in blocks:
-        arr = np.zeros(lb, np.uint8)
-        for ident in set(int(v) for v in e.ravel()):
-            k = fb.pool_pick(SEED, b, 5, ident, POOL)
-            arr[ident * sb:(ident + 1) * sb] = pool[k * sb:(k + 1) * sb]
-        layers[b] = arr
-    rc, y_ref, h_ref = orc.port_run(orc.model(HIDDEN, Q4_K, MXFP4, layers), e, gate, x, want_hidden=True)
-    rel = max(float(np.sqrt(((y_ref[t] - y[t]) ** 2).sum() / (y_ref[t] ** 2).sum())) for t in range(2))
+    layers = _host_layers(fb, g, pool, blocks, e)  # held: the model keeps only their addresses
+    m = orc.model(HIDDEN, Q4_K, MXFP4, layers)
+    rc, y_ref, h_ref = orc.port_run(m, e, gate, x, want_hidden=True)
+    rc2, y_q8 = orc.ref_run(m, e, gate, x, 1)
     return {"layer": 5, "tokens": 2, "blocks": len(blocks), "hidden_bitexact": bool(np.array_equal(
-        h.view(np.uint32), h_ref.view(np.uint32))), "max_rel_l2": rel}
+        h.view(np.uint32), h_ref.view(np.uint32))), "max_rel_l2": _rel(y_ref, y),
+        "max_rel_l2_vs_ref_q8": _rel(y_q8, y) if rc2 == 0 else None, "tolerance": 1e-5}
+
+
+def reduced_parity(ctx, fb, g, pool, rank, world, dist, dev):
+    """N>1: one layer with the in-kernel NVLink reduce (FRC_RUN_PEER) on every
+    rank; rank 0 checks that every rank holds the same y, bit for bit, and
+    compares it with the oracle over all 20 slices (the reference's sum of the
+    participants' parts, src/plane.c:110-121,325-345)."""
+    import torch
+    e, gate, x = fb.synth_request(HIDDEN, 2, 778)
+    de = torch.from_numpy(e.astype(np.uint16).view(np.int16)).to(dev)
+    dg, dx = torch.from_numpy(gate).to(dev), torch.from_numpy(x).to(dev)
+    dy = torch.zeros((2, HIDDEN), dtype=torch.float32, device=dev)
+    s = torch.cuda.current_stream().cuda_stream
+    ctx.run_device(5, 2, de.data_ptr(), dg.data_ptr(), dx.data_ptr(), None, None, dy.data_ptr(), fb.ACT_Q8,
+                   fb.RUN_PEER, s)
+    rc = ctx.status(s)
+    got = [None] * world
+    dist.all_gather_object(got, (rc, dy.cpu().numpy()))
+    if rank != 0:
+        return None
+    out = {"reduced": True, "layer": 5, "tokens": 2, "blocks": SLICES, "ranks": world,
+           "ranks_status": [int(r[0]) for r in got],
+           "ranks_bitwise_equal": all(np.array_equal(got[0][1].view(np.uint32), r[1].view(np.uint32)) for r in got),
+           "tolerance": 1e-5}
+    try:
+        from oracle import Oracle, Q4_K, MXFP4
+    except Exception as exc:  # noqa: BLE001
+        out["skipped"] = str(exc)
+        return out
+    orc = Oracle()
+    layers = _host_layers(fb, g, pool, range(SLICES), e)  # held: the model keeps only their addresses
+    m = orc.model(HIDDEN, Q4_K, MXFP4, layers)
+    rc1, y_ref, _ = orc.port_run(m, e, gate, x)
+    rc2, y_q8 = orc.ref_run(m, e, gate, x, 1)
+    y = got[0][1]
+    out["max_rel_l2"] = _rel(y_ref, y) if rc1 == 0 else None
+    out["max_rel_l2_vs_ref_q8"] = _rel(y_q8, y) if rc2 == 0 else None
+    return out
 
 
 def profile_case():
@@ -666,11 +752,13 @@ def run_prefill_bench(args, rank, world, local):
         dist.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler.mark_start()
     start.record(stream)
     for s in range(args.warmup, args.warmup + args.steps):
         step(s)
     end.record(stream)
     torch.cuda.synchronize()
+    sampler.mark_end()
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()

@@ -62,6 +62,10 @@ _SIGS = {
     "frc_close": (_int, [_vp]),
     "frc_load_unit": (_int, [_vp, _int, _vp, _sz]),
     "frc_load_layer": (_int, [_vp, _int, _u32, _vp, _sz]),
+    "frc_refresh_layer": (_int, [_vp, _int, _u32, _vp, _sz]),
+    "frc_probe_device": (_int, [_int, ctypes.c_char_p, _sz, _vp, _vp]),
+    "frc_set_wait_limit": (_int, [_vp, _u64]),
+    "frc_debug_barrier_extra": (_int, [_vp, _u32]),
     "frc_unload_unit": (_int, [_vp, _int]),
     "frc_loaded_mask": (_int, [_vp, _vp]),
     "frc_units_open": (_int, [_vp, ctypes.c_char_p, _u32, _int]),
@@ -349,6 +353,18 @@ class Context:
     def unload(self, block):
         return self.lib.frc_unload_unit(self.h, block)
 
+    def refresh_layer(self, block, layer, data):
+        """frc_refresh_layer: copy one loaded layer again from host memory."""
+        return self.lib.frc_refresh_layer(self.h, block, layer, _ptr(data), data.nbytes)
+
+    def set_wait_limit(self, ns):
+        """frc_set_wait_limit: every bounded wait of the layer kernel gives up after ns."""
+        self._check(self.lib.frc_set_wait_limit(self.h, int(ns)), "set_wait_limit")
+
+    def debug_barrier_extra(self, extra):
+        """Tests only: the grid barrier waits for `extra` arrivals that never come."""
+        self._check(self.lib.frc_debug_barrier_extra(self.h, extra), "debug_barrier_extra")
+
     def loaded_mask(self):
         m = ctypes.c_uint32()
         self._check(self.lib.frc_loaded_mask(self.h, ctypes.byref(m)), "loaded_mask")
@@ -486,9 +502,12 @@ def cuda_available():
         lib = library()
     except FrcError:
         return False
-    g = Geometry(2048, 1, Q4_K, MXFP4)
-    h = ctypes.c_void_p()
-    rc = lib.frc_open(0, ctypes.byref(g), ctypes.byref(h))
-    if rc == OK:
-        lib.frc_close(h)
-    return rc == OK
+    return lib.frc_probe_device(0, None, 0, None, None) == OK
+
+
+def probe_device(device=0):
+    """(rc, name, hbm_bytes, sms) of frc_probe_device (no context is opened)."""
+    name = ctypes.create_string_buffer(128)
+    hbm, sms = ctypes.c_uint64(), ctypes.c_uint()
+    rc = library().frc_probe_device(device, name, 128, ctypes.byref(hbm), ctypes.byref(sms))
+    return rc, name.value.decode(), hbm.value, sms.value

@@ -6,8 +6,14 @@
  * probe and load return FR_UNSUPPORTED.
  *
  * Differences a discrete GPU forces (documented, not hidden):
- *  - load copies the borrowed unit into HBM (set-up time) instead of keeping
- *    the pointer; unload frees it (backends/ref.c:19-28 borrow instead).
+ *  - load copies the borrowed unit into HBM (set-up time); unload frees it
+ *    (backends/ref.c:19-28 borrow instead and read the bytes at every run).
+ *    A unit lent from writable memory may change while it is loaded (the
+ *    reference's own self-test, src/native.c:121-131, corrupts scales of a
+ *    loaded unit and expects run to see them), so for such a block run first
+ *    copies the request's layer again (frc_refresh_layer).  Units mapped
+ *    read-only, as the node's loader maps them (src/units.c:25-75), are
+ *    copied once.
  *  - bench and self_test call the reference's own fr_bench_execute_backend and
  *    fr_native_self_test when the process links them (they are looked up at
  *    call time).  Without them, bench measures and fits the same cost model
@@ -29,15 +35,37 @@ int fr_cuda_close(const fr_backend *backend);
 #include <dlfcn.h>
 #include <fenv.h>
 #include <math.h>
+#include <stdint.h>
+#include <stdio.h>
 #include <string.h>
 
 typedef struct {
     frc_context *ctx;
     int act;
     unsigned char loaded[FR_BLOCKS];
+    unsigned char writable[FR_BLOCKS];  /* lent from writable memory: refreshed per run */
+    const unsigned char *unit[FR_BLOCKS];
 } slot_state;
 
-static slot_state q8_state = {NULL, FRC_ACT_Q8, {0}}, f32_state = {NULL, FRC_ACT_F32, {0}};
+static slot_state q8_state = {NULL, FRC_ACT_Q8, {0}, {0}, {0}}, f32_state = {NULL, FRC_ACT_F32, {0}, {0}, {0}};
+
+/* 1 when any page of [p, p + len) is mapped writable (from /proc/self/maps;
+ * 1 as well when that cannot be read: refreshing is the safe side). */
+static int range_writable(const void *p, size_t len) {
+    FILE *f = fopen("/proc/self/maps", "r");
+    if (!f) return 1;
+    const uintptr_t lo = (uintptr_t)p, hi = lo + len;
+    char line[512];
+    int w = 0;
+    while (!w && fgets(line, sizeof line, f)) {
+        unsigned long long a = 0, b = 0;
+        char perms[8] = {0};
+        if (sscanf(line, "%llx-%llx %7s", &a, &b, perms) != 3) continue;
+        if (a < hi && b > lo && perms[1] == 'w') w = 1;
+    }
+    fclose(f);
+    return w;
+}
 static int device_index = 0;
 
 static slot_state *state_of(const fr_backend *b) {
@@ -68,20 +96,21 @@ int fr_cuda_close(const fr_backend *backend) {
     return FR_OK;
 }
 
-/* FR_UNSUPPORTED without an sm_100 device; otherwise the reference's own
- * hw_probe fills the host fields when it is linked in. */
+/* FR_UNSUPPORTED without an sm_100 device (a device query, no context is
+ * opened); otherwise the reference's own hw_probe fills the host fields when
+ * it is linked in, and gpu names the device. */
 static int probe(fr_hwinfo *out) {
     if (!out) return FR_INVALID;
-    frc_geometry g = reference_geometry();
-    frc_context *c = NULL;
-    int rc = frc_open(device_index, &g, &c);
+    char name[128] = {0};
+    uint64_t hbm = 0;
+    unsigned sms = 0;
+    int rc = frc_probe_device(device_index, name, sizeof name, &hbm, &sms);
     if (rc) return rc == FRC_UNSUPPORTED ? FR_UNSUPPORTED : FR_IO;
-    frc_close(c);
     int (*hw_probe)(fr_hwinfo *) = (int (*)(fr_hwinfo *))dlsym(RTLD_DEFAULT, "hw_probe");
     fr_hwinfo h;
     memset(&h, 0, sizeof h);
     if (hw_probe && hw_probe(&h)) return FR_IO;
-    strncpy(h.gpu, "NVIDIA B200 (sm_100)", sizeof h.gpu - 1);
+    snprintf(h.gpu, sizeof h.gpu, "%s (sm_100, %u SMs, %llu MiB HBM)", name, sms, (unsigned long long)(hbm >> 20));
     *out = h;
     return FR_OK;
 }
@@ -95,7 +124,11 @@ static int load(slot_state *s, int block, const void *data, size_t len) {
         if (rc) return rc;
     }
     int rc = frc_load_unit(s->ctx, block, data, len);
-    if (!rc) s->loaded[block] = 1;
+    if (!rc) {
+        s->loaded[block] = 1;
+        s->unit[block] = (const unsigned char *)data;
+        s->writable[block] = (unsigned char)range_writable(data, len);
+    }
     return rc;
 }
 
@@ -103,6 +136,8 @@ static int unload(slot_state *s, int block) {
     if (block < 0 || block >= FR_BLOCKS) return FR_INVALID;
     if (!s->loaded[block]) return FR_STATE;
     s->loaded[block] = 0;
+    s->writable[block] = 0;
+    s->unit[block] = NULL;
     return frc_unload_unit(s->ctx, block);
 }
 
@@ -131,6 +166,13 @@ static int run(slot_state *s, const fr_req *req, fr_part *out) {
     int rc = validate(req);
     if (rc) return rc;
     if (!s->ctx || !any_loaded(s)) return FR_STATE;
+    const frc_geometry g = reference_geometry();
+    const size_t layer_bytes = frc_layer_bytes(&g);
+    for (unsigned b = 0; b < FR_BLOCKS; ++b)
+        if (s->loaded[b] && s->writable[b]) {
+            rc = frc_refresh_layer(s->ctx, (int)b, req->layer, s->unit[b] + (size_t)req->layer * layer_bytes, layer_bytes);
+            if (rc) return rc;
+        }
     memset(&scratch, 0, sizeof scratch); /* unused tokens stay zero */
     scratch.layer = req->layer;
     scratch.burst = req->burst;

@@ -210,8 +210,7 @@ struct frc_context {
   // mapped here, the per-CTA launch counters
   uint8_t* inbox = nullptr;
   uint8_t* peer[kMaxPeers] = {};
-  unsigned* epoch = nullptr;
-  unsigned rank = 0, world = 0, peer_gmax = 0;
+  unsigned rank = 0, world = 0;
   uint16_t last_expert[FRC_MAX_TOKENS * FRC_TOPK] = {};
   float last_gate[FRC_MAX_TOKENS * FRC_ACTIVE] = {};
   // prefill (bursts above FRC_MAX_TOKENS; MXFP4 gate/up and down only):
@@ -234,6 +233,10 @@ struct frc_context {
   // optional CUDA events around the five prefill launches (frc_prefill_timing)
   cudaEvent_t pf_ev[6] = {};
   bool pf_timing = false, pf_timed = false;
+  // bounded waits of the layer kernel (frc_set_wait_limit) and the test-only
+  // grid-barrier offset (frc_debug_barrier_extra)
+  unsigned long long wait_ns = kWaitNs;
+  unsigned bar_extra = 0;
   char err[256] = {};
 };
 
@@ -434,6 +437,8 @@ static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s, bool ove
   a.xchg = c->xchg;
   a.xcnt = c->xcnt;
   a.bar_inc = 2 * static_cast<unsigned>(c->sms) / G;  // G is one or two CTAs an SM
+  a.wait_ns = c->wait_ns;
+  a.bar_extra = c->bar_extra;
   // Co-residency of the grid (checked above) is what the grid barrier needs.
   // A plain launch asks the runtime to check it; an overlapped launch
   // (programmatic stream serialization) gets it as the previous launch's
@@ -500,7 +505,7 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
   if (flags & FRC_RUN_PEER) {
     if (c->world < 2) return fail(c, FRC_STATE, "FRC_RUN_PEER without frc_peer_attach");
     for (unsigned r = 0; r < c->world; ++r) a.peer[r] = c->peer[r];
-    a.rank = c->rank; a.world = c->world; a.peer_gmax = c->peer_gmax; a.epoch = c->epoch;
+    a.rank = c->rank; a.world = c->world;
   } else {
     a.world = 1;
   }
@@ -627,6 +632,17 @@ static int run_long(frc_context* c, unsigned layer, unsigned T, const uint16_t* 
   return FRC_OK;
 }
 
+// After a launch whose bounded wait ran out (every kernel of the context has
+// ended: the caller synchronized): the grid barrier's counter is off its
+// lattice and the split-item counts may be partial; both restart at zero.
+// The in-box reduce epoch is kept (the group detaches and attaches again).
+static int reset_after_timeout(frc_context* c, cudaStream_t s) {
+  CK(cudaMemsetAsync(c->ctl, 0, offsetof(LayerCtl, peer_epoch), s));
+  CK(cudaMemsetAsync(c->xcnt, 0, sizeof(unsigned) * kMaxUnique, s));
+  CK(cudaStreamSynchronize(s));
+  return FRC_OK;
+}
+
 static int status_code(unsigned st) {
   if (st & kStTimeout) return FRC_IO;
   if (st & kStInvalid) return FRC_INVALID;
@@ -688,6 +704,32 @@ const char* frc_strerror(int rc) {
 
 const char* frc_last_error(const frc_context* c) { return c ? c->err : "no context"; }
 uint64_t frc_launch_count(const frc_context* c) { return c ? c->launches : 0; }
+
+int frc_probe_device(int device, char* name, size_t cap, uint64_t* hbm_bytes, unsigned* sms) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return FRC_UNSUPPORTED;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) return FRC_UNSUPPORTED;
+  if (name && cap) {
+    strncpy(name, prop.name, cap - 1);
+    name[cap - 1] = 0;
+  }
+  if (hbm_bytes) *hbm_bytes = prop.totalGlobalMem;
+  if (sms) *sms = static_cast<unsigned>(prop.multiProcessorCount);
+  return FRC_OK;
+}
+
+int frc_set_wait_limit(frc_context* c, uint64_t ns) {
+  if (!c || ns < 1000 || ns > 60000000000ull) return fail(c, FRC_INVALID, "wait limit must be 1 us .. 60 s");
+  c->wait_ns = ns;
+  return FRC_OK;
+}
+
+int frc_debug_barrier_extra(frc_context* c, unsigned extra) {
+  if (!c || extra > 1024) return FRC_INVALID;
+  c->bar_extra = extra;
+  return FRC_OK;
+}
 
 int frc_open(int device, const frc_geometry* g, frc_context** out) {
   frc_context* c = nullptr;
@@ -803,6 +845,20 @@ int frc_load_layer(frc_context* c, int block, unsigned layer, const void* bytes,
   if (!c->staging) CK(cudaMalloc(&c->staging, c->layer_bytes));
   int rc = ensure_layer(c, block, layer);
   if (rc) return rc;
+  CK(cudaMemcpyAsync(c->staging, bytes, c->layer_bytes, cudaMemcpyHostToDevice, c->stream));
+  transcode_kernel<<<FRC_ROUTED_EXPERTS + 1, 256, 0, c->stream>>>(c->staging, c->layer_ptr[block][layer], FRC_ROUTED_EXPERTS, shape_of(c));
+  CK(cudaGetLastError());
+  ++c->launches;
+  CK(cudaStreamSynchronize(c->stream));
+  return FRC_OK;
+}
+
+int frc_refresh_layer(frc_context* c, int block, unsigned layer, const void* bytes, size_t len) {
+  if (!c || block < 0 || block >= FRC_MAX_BLOCKS || layer >= c->g.layers || !bytes || len != c->layer_bytes)
+    return fail(c, FRC_INVALID, "bad refresh_layer arguments");
+  if (!c->layer_ptr[block][layer]) return fail(c, FRC_STATE, "layer %u of block %d not loaded", layer, block);
+  CK(cudaSetDevice(c->device));
+  if (!c->staging) CK(cudaMalloc(&c->staging, c->layer_bytes));
   CK(cudaMemcpyAsync(c->staging, bytes, c->layer_bytes, cudaMemcpyHostToDevice, c->stream));
   transcode_kernel<<<FRC_ROUTED_EXPERTS + 1, 256, 0, c->stream>>>(c->staging, c->layer_ptr[block][layer], FRC_ROUTED_EXPERTS, shape_of(c));
   CK(cudaGetLastError());
@@ -929,9 +985,9 @@ int frc_run(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* exp
   CK(cudaMemsetAsync(c->status, 0, sizeof(unsigned), c->stream));
   CK(cudaStreamSynchronize(c->stream));
   const unsigned st = *c->h_status;
-  if (st & kStTimeout) {  // nothing runs now
-    CK(cudaMemset(c->ctl, 0, sizeof(LayerCtl)));
-    CK(cudaMemset(c->xcnt, 0, sizeof(unsigned) * kMaxUnique));
+  if (st & kStTimeout) {
+    const int rrc = reset_after_timeout(c, c->stream);
+    if (rrc) return rrc;
   }
   if (status_code(st)) return fail(c, status_code(st), "device status 0x%x", st);
   memcpy(y, c->h_y, xb);  // published only after the whole layer succeeded
@@ -996,14 +1052,11 @@ int frc_peer_export(frc_context* c, unsigned world, void* handle) {
   const size_t bytes = inbox_bytes(c, world, gmax);
   CK(cudaMalloc(&c->inbox, bytes));
   CK(cudaMemset(c->inbox, 0, bytes));
-  CK(cudaMalloc(&c->epoch, gmax * sizeof(unsigned)));
-  CK(cudaMemset(c->epoch, 0, gmax * sizeof(unsigned)));
   cudaIpcMemHandle_t h;
   CK(cudaIpcGetMemHandle(&h, c->inbox));
   static_assert(sizeof(h) == FRC_PEER_HANDLE_BYTES, "IPC handle size");
   memcpy(handle, &h, sizeof h);
   c->world = world;
-  c->peer_gmax = gmax;
   return FRC_OK;
 }
 
@@ -1024,6 +1077,10 @@ int frc_peer_attach(frc_context* c, unsigned rank, unsigned world, const void* h
     c->peer[r] = static_cast<uint8_t*>(p);
   }
   c->rank = rank;
+  // epochs restart with the fresh inbox, the same on every rank
+  CK(cudaMemsetAsync(reinterpret_cast<uint8_t*>(c->ctl) + offsetof(LayerCtl, peer_epoch), 0, sizeof(unsigned),
+                     c->stream));
+  CK(cudaStreamSynchronize(c->stream));
   return FRC_OK;
 }
 
@@ -1035,9 +1092,7 @@ int frc_peer_detach(frc_context* c) {
     c->peer[r] = nullptr;
   }
   cudaFree(c->inbox);
-  cudaFree(c->epoch);
   c->inbox = nullptr;
-  c->epoch = nullptr;
   c->world = 0;
   c->rank = 0;
   return FRC_OK;
@@ -1050,9 +1105,9 @@ int frc_status(frc_context* c, void* stream) {
   CK(cudaMemsetAsync(c->status, 0, sizeof(unsigned), s));
   CK(cudaStreamSynchronize(s));
   const int rc = status_code(*c->h_status);
-  if (*c->h_status & kStTimeout) {  // nothing runs now
-    CK(cudaMemset(c->ctl, 0, sizeof(LayerCtl)));
-    CK(cudaMemset(c->xcnt, 0, sizeof(unsigned) * kMaxUnique));
+  if (*c->h_status & kStTimeout) {
+    const int rrc = reset_after_timeout(c, s);
+    if (rrc) return rrc;
   }
   if (rc) return fail(c, rc, "device status 0x%x", *c->h_status);
   return FRC_OK;

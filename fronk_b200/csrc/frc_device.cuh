@@ -67,12 +67,12 @@ __device__ __forceinline__ uint64_t globaltimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-constexpr uint64_t kWaitNs = 2000000000ull;  // every wait gives up after 2 s
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+constexpr uint64_t kWaitNs = 2000000000ull;  // every wait gives up after 2 s (the layer kernel: a context setting)
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, uint64_t limit = kWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = globaltimer();
   while (!mbar_try_wait(bar, parity))
-    if (globaltimer() - start > kWaitNs) return false;
+    if (globaltimer() - start > limit) return false;
   return true;
 }
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -80,12 +80,13 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// Waits until *p >= target; gives up after kWaitNs or once *abort is set.
-__device__ __forceinline__ bool spin_geq(const unsigned* p, unsigned target, const unsigned* abort) {
+// Waits until *p >= target; gives up after `limit` ns or once *abort is set.
+__device__ __forceinline__ bool spin_geq(const unsigned* p, unsigned target, const unsigned* abort,
+                                        uint64_t limit = kWaitNs) {
   if (ld_acquire(p) >= target) return true;
   const uint64_t start = globaltimer();
   while (ld_acquire(p) < target) {
-    if (globaltimer() - start > kWaitNs || ld_acquire(abort)) return false;
+    if (globaltimer() - start > limit || ld_acquire(abort)) return false;
     __nanosleep(64);
   }
   return true;

@@ -50,7 +50,13 @@ constexpr unsigned kMaxPeers = 8;              // GPUs of one in-box reduce
 struct LayerCtl {
   unsigned long long arrived;   // grid barrier arrivals, all launches (never wraps)
   unsigned abort;               // set by a CTA whose bounded wait ran out
-  unsigned pad;
+  // In-box reduce launches completed on this context.  Every CTA of a
+  // FRC_RUN_PEER launch reads it once it may read memory (after the
+  // programmatic-launch wait) and before it arrives at the grid barrier;
+  // CTA 0 stores the launch's epoch (read + 1) once the barrier has released,
+  // so one launch carries one epoch whatever its grid size.  A timeout reset
+  // keeps it; frc_peer_attach zeroes it on every rank.
+  unsigned peer_epoch;
 };
 
 // Byte offsets of one CTA's dynamic shared memory, and the chunking of an
@@ -83,15 +89,19 @@ struct LayerParams {
   unsigned* status;
   unsigned long long* phases;  // FRC_PHASES builds: [cta][16] globaltimer stamps
   // In-box reduce over peer memory (world > 1): every rank's inbox as mapped
-  // here (peer[rank] is this rank's own), this rank, and this context's
-  // per-CTA count of such launches (the epoch).  Inbox: [2][world][16][d]
-  // 8-byte entries {value, epoch}.
+  // here (peer[rank] is this rank's own) and this rank.  Inbox:
+  // [2][world][16][d] 8-byte entries {value, epoch}; the epoch is
+  // ctl->peer_epoch + 1.
   uint8_t* peer[kMaxPeers];
-  unsigned rank, world, peer_gmax;
-  unsigned* epoch;
+  unsigned rank, world;
   // Grid barrier arrivals a CTA adds: (2 x SMs) / grid, so that every launch
   // adds the same total whatever its grid (one or two CTAs an SM).
   unsigned bar_inc;
+  // Every bounded wait of the launch gives up after wait_ns (the context's
+  // limit, 2 s unless set).  bar_extra > 0 (tests only) raises the grid
+  // barrier's target by that many arrivals, so its wait runs out.
+  unsigned bar_extra;
+  unsigned long long wait_ns;
   // Items split in H parts (1, 2 or 4; one token, one round of parts): part
   // h takes neurons [32h/H, 32(h+1)/H) of the slice and down rows
   // [dh/H, d(h+1)/H); the parts' hidden values meet in xchg [item][32]
@@ -130,18 +140,19 @@ __device__ __forceinline__ void plan_sync() { asm volatile("bar.sync 2, 128;" ::
 // and of two CTAs an SM may follow each other in any order).  A timed-out
 // launch leaves the counter off that lattice; frc_status zeroes it before
 // anything runs again.
-__device__ __forceinline__ bool grid_sync(LayerCtl* ctl, unsigned* flag_smem, unsigned inc) {
+__device__ __forceinline__ bool grid_sync(LayerCtl* ctl, unsigned* flag_smem, unsigned inc, uint64_t limit,
+                                          unsigned extra) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
     const unsigned long long span = static_cast<unsigned long long>(gridDim.x) * inc;
     const unsigned long long old = atomicAdd(&ctl->arrived, static_cast<unsigned long long>(inc));
-    const unsigned long long target = (old / span + 1) * span;
+    const unsigned long long target = (old / span + 1) * span + extra;
     bool ok = true;
     const uint64_t start = globaltimer();
     unsigned spins = 0;
     while (ld_acquire64(&ctl->arrived) < target) {
-      if ((++spins & 255) == 0 && (globaltimer() - start > kWaitNs || ld_acquire(&ctl->abort))) {
+      if ((++spins & 255) == 0 && (globaltimer() - start > limit || ld_acquire(&ctl->abort))) {
         ok = false;
         break;
       }
@@ -717,6 +728,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
   }
   __syncthreads();
   setup();
+  if (a.world > 1 && tid == 0) misc[6] = *reinterpret_cast<volatile unsigned*>(&a.ctl->peer_epoch) + 1;
   PHASE(3);
 
   // --------------------------------------------------------------- items
@@ -754,12 +766,12 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
       if (reinterpret_cast<volatile unsigned*>(s_iss)[slot] <= j) {
         const uint64_t start = globaltimer();
         while (reinterpret_cast<volatile unsigned*>(s_iss)[slot] <= j)
-          if (globaltimer() - start > kWaitNs) {
+          if (globaltimer() - start > a.wait_ns) {
             ok = false;
             break;
           }
       }
-      ok = ok && mbar_wait(&full[slot], j & 1);
+      ok = ok && mbar_wait(&full[slot], j & 1, a.wait_ns);
       timed_out = __any_sync(0xffffffffu, !ok);
     }
     return !timed_out;
@@ -849,7 +861,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
       __syncthreads();
       if (tid == 0) {
         atomicAdd(&a.xcnt[ji], 1u);
-        bool ok = spin_geq(&a.xcnt[ji], H, &a.ctl->abort);
+        bool ok = spin_geq(&a.xcnt[ji], H, &a.ctl->abort, a.wait_ns);
         misc[8] = ok ? 1u : 0u;
       }
       __syncthreads();
@@ -925,9 +937,11 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
       atomicOr(a.status, kStTimeout);
       atomicExch(&a.ctl->abort, 1u);
     }
-  } else if (!grid_sync(a.ctl, misc + 3, a.bar_inc)) {
+  } else if (!grid_sync(a.ctl, misc + 3, a.bar_inc, a.wait_ns, a.bar_extra)) {
     aborted = true;
     if (tid == 0) atomicOr(a.status, kStTimeout);
+  } else if (a.world > 1 && cta == 0 && tid == 0) {
+    a.ctl->peer_epoch = misc[6];  // every CTA read the previous value before it arrived
   }
   PHASE(5);
   // every part has passed its exchange: the item's first part clears the count
@@ -950,13 +964,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
   auto peer_reduce = [&](unsigned y0, unsigned R) -> bool {
     const unsigned W = a.world;
     const size_t slot_entries = static_cast<size_t>(kMaxTokens) * d;  // one source's [16][d] entries of 8 bytes
-    if (tid == 0) {
-      const unsigned e = a.epoch[cta] + 1;
-      a.epoch[cta] = e;
-      misc[6] = e;
-    }
-    __syncthreads();
-    const unsigned e = misc[6], par = e & 1;
+    const unsigned e = misc[6], par = e & 1;  // this launch's epoch (set before the grid barrier)
     const Div by_tr(T * R), by_r2(R);
     for (unsigned q = tid; q < W * T * R; q += kLayerThreads) {
       const unsigned dst = by_tr.q(q), rem = q - dst * T * R, t = by_r2.q(rem), rr = rem - t * R;
@@ -985,7 +993,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
           for (;;) {
             asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(word) : "l"(ent) : "memory");
             if (static_cast<unsigned>(word >> 32) == e) break;
-            if ((++spins & 63) == 0 && globaltimer() - start > kWaitNs) {
+            if ((++spins & 63) == 0 && globaltimer() - start > a.wait_ns) {
               ok = false;
               break;
             }

@@ -71,6 +71,12 @@ int frc_geometry_check(const frc_geometry *g);
 /* ---- Context ---- */
 typedef struct frc_context frc_context;
 
+/* Device query without a context (nothing is allocated): FRC_OK when device
+ * `device` is an sm_100 part; its name (NUL-terminated, at most cap bytes),
+ * HBM bytes and SM count when the pointers are not NULL.  The fr_backend
+ * probe entry's device check (src/hw.h:19-24). */
+int frc_probe_device(int device, char *name, size_t cap, uint64_t *hbm_bytes, unsigned *sms);
+
 /* Opens device `device` for units of geometry g.  Allocates all run-time
  * scratch now; run calls allocate nothing (src/backend.h:5).  FRC_UNSUPPORTED
  * when the device is not an sm_100 part. */
@@ -86,6 +92,13 @@ int frc_load_unit(frc_context *c, int block, const void *unit, size_t len);
  * FRC_STATE.  Used for sparse correctness fixtures. */
 int frc_load_layer(frc_context *c, int block, unsigned layer, const void *layer_bytes, size_t len);
 int frc_unload_unit(frc_context *c, int block);
+/* Copies one layer of a loaded block again from host memory (frc_layer_bytes
+ * of that layer, reference layout), replacing the HBM copy.  For callers that
+ * lend the backend a writable unit and may change it after load: the
+ * reference's backends read the borrowed bytes at every run
+ * (src/backend.h:52-60), a discrete GPU computes from its copy.
+ * FRC_STATE when that layer is not loaded. */
+int frc_refresh_layer(frc_context *c, int block, unsigned layer, const void *layer_bytes, size_t len);
 /* Bit b set when block b is loaded. */
 int frc_loaded_mask(const frc_context *c, uint32_t *mask);
 
@@ -233,6 +246,16 @@ int frc_host_pass(frc_context *c, unsigned first_layer, unsigned layers, unsigne
 /* Waits for `stream`, returns and clears the device status (FRC_OK,
  * FRC_NUMERIC, FRC_INVALID for an out-of-range id, FRC_IO for a timed-out wait). */
 int frc_status(frc_context *c, void *stream);
+/* Every bounded wait inside the layer kernel (its TMA ring, grid barrier,
+ * split-item exchange and in-box reduce) gives up after `ns` nanoseconds
+ * (1 us .. 60 s; 2 s when never set), sets the device status that frc_status
+ * / frc_run report as FRC_IO, and the launch ends: y of a frc_run call is left
+ * untouched and the next call on the context runs normally.  No counterpart in
+ * the reference (its timeouts are the plane's deadline, src/plane.c). */
+int frc_set_wait_limit(frc_context *c, uint64_t ns);
+/* Tests only: raises the layer kernel's grid-barrier target by `extra`
+ * arrivals (0 restores it), so that the barrier's bounded wait runs out. */
+int frc_debug_barrier_extra(frc_context *c, unsigned extra);
 /* Count of kernels this context has launched since open. */
 uint64_t frc_launch_count(const frc_context *c);
 const char *frc_strerror(int rc);

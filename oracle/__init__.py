@@ -103,10 +103,12 @@ class Oracle:
 
     # runs ------------------------------------------------------------------
     def model(self, hidden, gate_type, down_type, layers, legacy=0):
-        """layers: {block: uint8 array covering the requested layer}."""
+        """layers: {block: uint8 array covering the requested layer}.  The
+        model keeps a reference to the arrays it points into."""
         m = OrModel(hidden, gate_type, down_type, legacy)
         for b, arr in layers.items():
             m.layer[b] = arr.ctypes.data
+        m._keep = dict(layers)
         return m
 
     def ref_run(self, m, expert, gate, x, q8):

@@ -19,7 +19,8 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
-REF = os.environ.get("FRONK_REFERENCE", "/root/reference")
+# the reference's source tree: FRONK_REFERENCE, else a checkout beside this repository
+REF = os.environ.get("FRONK_REFERENCE") or os.path.normpath(os.path.join(ROOT, "..", "reference"))
 REF_OUT = os.path.join(HERE, "_ref")
 ORACLE_LIB = os.path.join(HERE, "liboracle.so")
 

@@ -14,7 +14,9 @@ from fronk_b200 import planner
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 INCLUDE = os.path.join(ROOT, "include")
-REF_TREE = os.environ.get("FRONK_REFERENCE", "/root/reference")
+# the reference's source tree: FRONK_REFERENCE, else a checkout beside this repository
+REF_TREE = os.environ.get("FRONK_REFERENCE") or os.path.normpath(
+    os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "..", "reference"))
 
 
 def declared_symbols():

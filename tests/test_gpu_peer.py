@@ -1,8 +1,10 @@
 """The in-box reduce over NVLink peer memory (FRC_RUN_PEER) on two GPUs:
 each rank owns the planner's half of the slices, the kernels exchange their
 partials through each other's inboxes, and y equals the whole layer (the
-oracle port over all 20 slices) on both ranks, bit for bit the same on
-both.  Three calls in a row use both slot parities.  Needs two GPUs; the IPC
+oracle port over all 20 slices, and the reference's ref-q8) on both ranks,
+bit for bit the same on both.  The calls alternate one token (two CTAs an
+SM) with sixteen (one CTA an SM), so row ownership changes from launch to
+launch while the slots alternate by launch epoch.  Needs two GPUs; the IPC
 handles go over a gloo group (host channel only)."""
 import os
 import socket
@@ -37,8 +39,8 @@ def _rank(rank, world, port, q):
         torch.cuda.set_device(rank)
         hidden, layer = 2048, 4
         g = fb.geometry(hidden)
-        cases = [request(hidden, 1, 0x5EED + 21, 0.0), request(hidden, 3, 0x5EED + 22, 0.5),
-                 request(hidden, 1, 0x5EED + 23, 0.25)]
+        cases = [request(hidden, t, 0x5EED + 21 + i, 0.25 * (i % 3), True)
+                 for i, t in enumerate((1, 16, 1, 1, 16, 3, 16, 16, 1, 2))]
         experts = np.concatenate([c[0].ravel() for c in cases])
         layers = make_layers(g, 0x5EED, list(range(20)), experts, shared=True)
         mine = planner.owned_blocks(rank, world)
@@ -69,10 +71,12 @@ def _rank(rank, world, port, q):
             worst = 0.0
             for i, (e, gate, x) in enumerate(cases):
                 rc, y_ref, _ = oracle.port_run(m, e, gate, x)
-                assert rc == OK
+                rc2, y_q8 = oracle.ref_run(m, e, gate, x, 1)
+                assert rc == OK and rc2 == OK
                 assert np.array_equal(gathered[0][i].view(np.uint32), gathered[1][i].view(np.uint32)), "ranks differ"
-                for r_, a_ in zip(y_ref, gathered[0][i]):
-                    worst = max(worst, float(np.linalg.norm(r_ - a_) / np.linalg.norm(r_)))
+                for ref in (y_ref, y_q8):
+                    for r_, a_ in zip(ref, gathered[0][i]):
+                        worst = max(worst, float(np.linalg.norm(r_ - a_) / np.linalg.norm(r_)))
             q.put(("ok", worst))
         else:
             q.put(("ok", 0.0))

@@ -13,7 +13,9 @@ import fronk_b200 as fb
 from oracle import OK, Q4_K, MXFP4, Q8_0, Reference, reference_available
 from tests.helpers import SparseUnit, make_layers, request, conforms, BACKEND_TOL
 
-REF_TREE = os.environ.get("FRONK_REFERENCE", "/root/reference")
+# the reference's source tree: FRONK_REFERENCE, else a checkout beside this repository
+REF_TREE = os.environ.get("FRONK_REFERENCE") or os.path.normpath(
+    os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "..", "reference"))
 needs_ref = pytest.mark.skipif(not reference_available(2560) or not reference_available(2048),
                                reason="reference not compiled here")
 
