@@ -39,15 +39,33 @@ HIDDEN, LAYERS, SLICES, TOPK = 2048, 48, 20, 10
 SEED = 0x5EED
 POOL = 64
 SLICE_BYTES = 2 * 32 * (HIDDEN // 256) * 144 + HIDDEN * 17     # 108,544 (Q4_K gate/up + MXFP4 down)
+# --formats: the routed block formats of the pass.  q4k-mxfp4 is the
+# reference's own layout (configs[0], [2], [3]); mxfp4-q80 is configs[1]'s
+# (MXFP4 gate/up, Q8_0 down: 139,264 B a slice).
+FORMATS = {"q4k-mxfp4": (12, 39, "Q4_K gate/up, MXFP4 down"),
+           "mxfp4-q80": (39, 8, "MXFP4 gate/up, Q8_0 down")}
+FMT = "q4k-mxfp4"
+
+
+def set_formats(name):
+    global FMT, SLICE_BYTES
+    FMT = name
+    gt, dt, _ = FORMATS[name]
+    row = {12: HIDDEN // 256 * 144, 39: HIDDEN // 32 * 17, 8: HIDDEN // 32 * 34}
+    SLICE_BYTES = 2 * 32 * row[gt] + HIDDEN * (17 if dt == 39 else 34)
 
 
 def workload(tokens):
+    fmt = FORMATS[FMT][2]
     if tokens == 1:
+        if FMT != "q4k-mxfp4":
+            return ("decode48 in BASELINE configs[1]'s formats: 48 MoE layers, 1 token, d=2048, 512 experts top-10, "
+                    "%s, 20 slices split over the GPUs (1/2/4/8), partial sum after every layer" % fmt)
         return ("decode48 (BASELINE configs[2]): 48 MoE layers, 1 token, d=2048, 512 experts top-10, "
-                "Q4_K gate/up + MXFP4 down, 20 slices split over the GPUs, partial sum after every layer")
+                "%s, 20 slices split over the GPUs, partial sum after every layer" % fmt)
     return ("decode48x%d (BASELINE configs[3]): 48 MoE layers, %d concurrent tokens with independent top-10 "
-            "routing (one launch per layer over the union of their experts), d=2048, 512 experts, Q4_K gate/up "
-            "+ MXFP4 down, 20 slices split over the GPUs, partial sum after every layer" % (tokens, tokens))
+            "routing (one launch per layer over the union of their experts), d=2048, 512 experts, %s, "
+            "20 slices split over the GPUs, partial sum after every layer" % (tokens, tokens, fmt))
 
 
 _out = sys.stdout
@@ -182,12 +200,15 @@ def cpu_baseline(steps, warmup, tokens=1):
     return {"value": tok_s, "unit": "tokens/s", "cores": r["workers"], "kind": "reference",
             "sample": "reference backends/avx2.c (fr_avx2.run), full workload: all 20 slices resident in sparse "
                       "host units, %d timed 48-layer passes of %d token(s) after %d warm-up, d=2048 build"
-                      % (steps, tokens, warmup),
+                      % (steps, tokens, warmup) + (
+                          "; the reference's unit layout fixes routed gate/up rows to Q4_K and down rows to MXFP4, "
+                          "so its pass runs the same routing over that layout" if FMT != "q4k-mxfp4" else ""),
             "host": {"cpu": r["cpu"], "cores": r["cores"], "logical_cores": r["logical_cores"]},
             "ms_per_pass": r["ns_per_pass_mean"] / 1e6, "wall_s": round(time.time() - t0, 1)}
 
 
 def run_reference(args, rank):
+    set_formats(args.formats)
     if rank != 0:
         return
     if args.prefill:
@@ -224,7 +245,8 @@ def config(n, reduce="peer", tokens=1, unique_per_layer=TOPK):
     step_bytes = LAYERS * unique_per_layer * SLICES * SLICE_BYTES
     return {"workload": workload(tokens), "hidden": HIDDEN, "layers": LAYERS, "tokens_per_step": tokens,
             "experts": 512, "top_k": TOPK, "slices": SLICES, "shares": equal_shares(n),
-            "formats": "Q4_K gate/up, MXFP4 down", "activations": "Q8 per 64 (src/q4.c scheme), fp32 accumulate",
+            "formats": FORMATS[FMT][2], "activations": "Q8 per 64 (src/q4.c scheme), exact block terms "
+                                                        "summed in double (gate/up), fp32 down terms",
             "unique_experts_per_layer": unique_per_layer, "weight_bytes_per_step": int(step_bytes),
             "l2": "inputs larger than L2: %.2f GB of expert weights per step, fresh routing every step"
                   % (step_bytes / 1e9),
@@ -248,10 +270,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--reduce", default="peer", choices=["peer", "nccl"],
                     help="per-layer sum of the GPUs' partials: in-kernel over NVLink peer memory, or NCCL all-reduce")
+    ap.add_argument("--formats", default="q4k-mxfp4", choices=sorted(FORMATS),
+                    help="routed block formats: q4k-mxfp4 (the reference layout, configs[2]/[3]) or mxfp4-q80 "
+                         "(configs[1]: MXFP4 gate/up, Q8_0 down)")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu: 2 layers of every slice loaded (2.2 GB), 5 layer launches "
                          "(with --prefill: one layer, three 512-token calls)")
     args = ap.parse_args()
+    set_formats(args.formats)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -289,8 +315,9 @@ def main():
                                 device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     blocks = owned_blocks(rank, world)
-    g = fb.geometry(HIDDEN)
-    ctx = fb.Context(local, HIDDEN)
+    gt_, dt_, _ = FORMATS[FMT]
+    g = fb.geometry(HIDDEN, LAYERS, gt_, dt_)
+    ctx = fb.Context(local, HIDDEN, LAYERS, gt_, dt_)
 
     # units: a pool of distinct synthetic slices, copied on the device into every slot
     t0 = time.time()
@@ -554,7 +581,7 @@ def full_size_parity(ctx, fb, g, pool, blocks):
         return {"error": ctx.last_error}
     h = ctx.debug_hidden()
     layers = _host_layers(fb, g, pool, blocks, e)  # held: the model keeps only their addresses
-    m = orc.model(HIDDEN, Q4_K, MXFP4, layers)
+    m = orc.model(HIDDEN, FORMATS[FMT][0], FORMATS[FMT][1], layers)
     rc, y_ref, h_ref = orc.port_run(m, e, gate, x, want_hidden=True)
     rc2, y_q8 = orc.ref_run(m, e, gate, x, 1)
     return {"layer": 5, "tokens": 2, "blocks": len(blocks), "hidden_bitexact": bool(np.array_equal(
@@ -591,7 +618,7 @@ def reduced_parity(ctx, fb, g, pool, rank, world, dist, dev):
         return out
     orc = Oracle()
     layers = _host_layers(fb, g, pool, range(SLICES), e)  # held: the model keeps only their addresses
-    m = orc.model(HIDDEN, Q4_K, MXFP4, layers)
+    m = orc.model(HIDDEN, FORMATS[FMT][0], FORMATS[FMT][1], layers)
     rc1, y_ref, _ = orc.port_run(m, e, gate, x)
     rc2, y_q8 = orc.ref_run(m, e, gate, x, 1)
     y = got[0][1]

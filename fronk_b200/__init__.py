@@ -66,6 +66,7 @@ _SIGS = {
     "frc_probe_device": (_int, [_int, ctypes.c_char_p, _sz, _vp, _vp]),
     "frc_set_wait_limit": (_int, [_vp, _u64]),
     "frc_debug_barrier_extra": (_int, [_vp, _u32]),
+    "frc_debug_layer_variant": (_int, [_vp, _int]),
     "frc_unload_unit": (_int, [_vp, _int]),
     "frc_loaded_mask": (_int, [_vp, _vp]),
     "frc_units_open": (_int, [_vp, ctypes.c_char_p, _u32, _int]),
@@ -360,6 +361,11 @@ class Context:
     def set_wait_limit(self, ns):
         """frc_set_wait_limit: every bounded wait of the layer kernel gives up after ns."""
         self._check(self.lib.frc_set_wait_limit(self.h, int(ns)), "set_wait_limit")
+
+    def layer_variant(self, variant):
+        """frc_debug_layer_variant: which kernel serves one-token Q8 calls: 1 the default (row-owner up to
+        two slices), 0 always the item kernel, 2 the row-owner kernel whenever it fits."""
+        self._check(self.lib.frc_debug_layer_variant(self.h, variant), "layer_variant")
 
     def debug_barrier_extra(self, extra):
         """Tests only: the grid barrier waits for `extra` arrivals that never come."""

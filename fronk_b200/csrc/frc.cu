@@ -23,6 +23,7 @@
 using namespace frc;
 
 #include "frc_layer.cuh"
+#include "frc_layer_rb.cuh"
 #include "frc_umma.cuh"
 #include "frc_prefill.cuh"
 #include "frc_units.h"
@@ -193,11 +194,17 @@ struct frc_context {
   unsigned* status = nullptr;
   float* xchg = nullptr;    // split items: hidden values [item][32]
   unsigned* xcnt = nullptr; // and the parts that wrote them [item]
+  // row-owner kernel: per-item chunk arrivals (zero between launches) and
+  // the quantized hidden slices [item][32] + scales [item]
+  unsigned* rb_cnt = nullptr;
+  uint8_t* rb_hq = nullptr;
+  float* rb_hs = nullptr;
   // frc_run staging: one copy in ([x][gate][expert], packed for the call's
   // token count) and one copy out ([status word, 16 B][y]).
   uint8_t *d_in = nullptr, *d_out = nullptr, *h_in = nullptr, *h_out = nullptr;
   float *d_y = nullptr, *h_y = nullptr;  // inside d_out / h_out
   unsigned* h_status = nullptr;          // start of h_out
+
   cudaStream_t stream = nullptr;
   uint8_t* pool = nullptr;
   unsigned pool_count = 0;
@@ -237,6 +244,13 @@ struct frc_context {
   // grid-barrier offset (frc_debug_barrier_extra)
   unsigned long long wait_ns = kWaitNs;
   unsigned bar_extra = 0;
+  // one-token Q8 calls: the row-owner kernel (frc_layer_rb.cuh) unless
+  // frc_debug_layer_variant chose the item kernel; its attribute and the
+  // occupancy of its last shared-memory size
+  int rb = 1;  // 0 item kernel, 1 row-owner up to kRbMaxSlices slices, 2 row-owner whenever it fits
+  bool rb_attr = false;
+  unsigned rb_occ_smem = 0;
+  int rb_occ_val = 0;
   char err[256] = {};
 };
 
@@ -267,6 +281,10 @@ static size_t kInBytesPerToken(unsigned d) { return sizeof(float) * (d + FRC_ACT
 
 // fp32 hidden activations of the largest call: [unique expert][slice][token][32]
 constexpr size_t kHiddenBytes = sizeof(float) * kMaxUnique * kMaxBlocks * kMaxTokens * 32;
+// items of a one-token call: eleven experts x 20 slices
+constexpr unsigned kRbItems = 11 * kMaxBlocks;
+// slices loaded up to which one-token calls take the row-owner kernel
+constexpr unsigned kRbMaxSlices = 2;
 
 // Dynamic shared memory a CTA may use with two CTAs an SM (228 KB an SM,
 // 1 KB reserved a CTA), and with one.
@@ -464,6 +482,109 @@ static int launch_layer(frc_context* c, LayerParams& a, cudaStream_t s, bool ove
   return FRC_OK;
 }
 
+// Shared memory of the row-owner kernel within `limit` bytes: plan tables,
+// one token's activations, this CTA's down-row staging (every item's rows
+// [y0, y0 + R), R at most rows_max), and a ring of gate/up chunks (8 routed
+// neurons, 4 shared) that phase B reuses for the hidden values and terms.
+static bool smem_layout_rb(const frc_context* c, unsigned G, unsigned S, bool shared, unsigned limit, LayerSmem* out) {
+  const unsigned d = c->g.hidden, P = d / 64;
+  LayerSmem m{};
+  unsigned o = 64 + 256;
+  auto take = [&](unsigned bytes) { unsigned at = o; o = align_up(o + bytes, 16); return at; };
+  m.uid = take(2 * 11);
+  m.ugate = take(4 * 11);
+  m.rms = take(4);
+  m.rpart = take(4 * kActWarps * ((d / 16 + kActThreads - 1) / kActThreads));
+  const bool mx = c->g.gate_type == FRC_MXFP4;
+  m.xq = take(d);
+  m.xr = take(d);
+  m.xp = mx ? take(d) : 0;
+  m.xrp = mx ? take(d) : 0;
+  m.xst = take(16 * P);
+  m.xvr = take(16 * P);
+  const unsigned NU = d / 4, RM = 4 * ((NU + G - 1) / G);
+  m.rows_max = RM;
+  m.ylocal = take(4 * RM);
+  const unsigned pb_r = c->g.down_type == FRC_Q8_0 ? 32 : 16;
+  m.dnw = (15 + 2 * RM + 15) / 16;  // scale bytes from a 16-byte boundary: at most 15 + 2 x rows
+  m.dnb_r = RM * pb_r + 16 * m.dnw;
+  m.dnb_s = RM * 32 + 16 * m.dnw;
+  m.dnb = take(10 * S * m.dnb_r + (shared ? S * m.dnb_s : 0));
+  o = align_up(o, 128);
+  if (o >= limit) return false;
+  const unsigned rowb = static_cast<unsigned>(c->row_bytes), srow = static_cast<unsigned>(c->shared_row);
+  unsigned slot = 2 * 8 * rowb > 2 * 4 * srow ? 2 * 8 * rowb : 2 * 4 * srow;
+  slot = align_up(slot, 128);
+  unsigned K = (limit - o) / slot;
+  K = K < kRingSlots ? K : kRingSlots;
+  const unsigned NI = (10 + (shared ? 1 : 0)) * S;
+  const unsigned staged = align_up(NI * 32, 16) + 4 * ((NI + 3) & ~3u) + 4 * NI * RM + 4 * ((11 * RM + 3) & ~3u);
+  if (K < 2 || K * slot < staged) return false;
+  if ((48 * S + G - 1) / G > 16) return false;  // chunks a CTA: the kernel lists the items it completes in 16 words
+  m.ring = o;
+  m.slot_bytes = slot;
+  m.slots = K;
+  m.kn_r = 8;
+  m.kn_s = 4;
+  m.total = o + K * slot;
+  *out = m;
+  return true;
+}
+
+static int launch_layer_rb(frc_context* c, LayerParams& a, cudaStream_t s, bool overlap, bool shared) {
+  if (!c->rb_attr) {
+    CK(cudaFuncSetAttribute(moe_layer_rb_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    c->rb_attr = true;
+  }
+  auto occupancy = [&](unsigned bytes, int* per_sm) -> int {
+    if (c->rb_occ_smem != bytes) {
+      CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c->rb_occ_val, moe_layer_rb_kernel, kLayerThreads, bytes));
+      c->rb_occ_smem = bytes;
+    }
+    *per_sm = c->rb_occ_val;
+    return FRC_OK;
+  };
+  // two CTAs an SM when their shared memory fits, else one; all resident
+  unsigned G = 2 * static_cast<unsigned>(c->sms);
+  int per_sm = 0, orc;
+  bool fits = smem_layout_rb(c, G, a.S, shared, kSmemTwoPerSm, &a.sm);
+  if (fits) {
+    if ((orc = occupancy(a.sm.total, &per_sm))) return orc;
+    fits = per_sm >= 2;
+  }
+  if (!fits) {
+    G = static_cast<unsigned>(c->sms);
+    if (!smem_layout_rb(c, G, a.S, shared, kSmemOnePerSm, &a.sm))
+      return fail(c, FRC_INVALID, "one-token layer does not fit shared memory (%u slices)", a.S);
+    if ((orc = occupancy(a.sm.total, &per_sm))) return orc;
+    if (per_sm < 1) return fail(c, FRC_INVALID, "layer kernel does not fit an SM (%u bytes)", a.sm.total);
+  }
+  a.H = 1;
+  a.Hshift = 0;
+  a.bar_inc = 2 * static_cast<unsigned>(c->sms) / G;
+  a.wait_ns = c->wait_ns;
+  a.bar_extra = c->bar_extra;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  if (overlap) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+  } else {
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+  }
+  cfg.gridDim = dim3(G);
+  c->last_G = G;
+  cfg.blockDim = dim3(kLayerThreads);
+  cfg.dynamicSmemBytes = a.sm.total;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CK(cudaLaunchKernelEx(&cfg, moe_layer_rb_kernel, a));
+  ++c->launches;
+  return FRC_OK;
+}
+
 // Device buffers a launch writes and reads back: the down terms and their
 // weights (handed from the item phase to the reduce) and the optional fp32
 // copy of the hidden activations.
@@ -519,6 +640,28 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
   a.slice_bytes = static_cast<unsigned>(c->slice_bytes);
   c->last_S = S;
   const bool overlap = (flags & FRC_RUN_OVERLAP) != 0;
+  LayerSmem probe;
+  // one token over at most kRbMaxSlices slices (an 8-GPU share): the
+  // row-owner kernel, 3 % faster there; with more slices its gather of
+  // every item's down rows costs more than it saves (measured 1..20 slices)
+  if (T == 1 && act == FRC_ACT_Q8 && (c->rb == 2 || (c->rb == 1 && S <= kRbMaxSlices)) &&
+      (smem_layout_rb(c, 2 * static_cast<unsigned>(c->sms), S, true, kSmemTwoPerSm, &probe) ||
+       smem_layout_rb(c, static_cast<unsigned>(c->sms), S, true, kSmemOnePerSm, &probe))) {
+    // the row-owner kernel when its staging fits (all of the benchmark's and
+    // the reference's geometries; very wide layers fall back to the item
+    // kernel).  Hidden values go through global memory (the fixed-scratch
+    // call lends its array, which the down terms do not use); the staging
+    // holds the shared expert's rows too, since its gate is on the device.
+    a.rb_cnt = c->rb_cnt;
+    a.rb_hq = c->rb_hq;
+    a.rb_hs = c->rb_hs;
+    if (!a.hidden) {
+      a.hidden = a.partial;
+      a.rb_hq = reinterpret_cast<uint8_t*>(a.partial + 32 * kRbItems);
+      a.rb_hs = a.partial + 40 * kRbItems;
+    }
+    return launch_layer_rb(c, a, s, overlap, true);
+  }
   if (act == FRC_ACT_Q8) return launch_layer<FRC_ACT_Q8>(c, a, s, overlap);
   return launch_layer<FRC_ACT_F32>(c, a, s, overlap);
 }
@@ -639,6 +782,7 @@ static int run_long(frc_context* c, unsigned layer, unsigned T, const uint16_t* 
 static int reset_after_timeout(frc_context* c, cudaStream_t s) {
   CK(cudaMemsetAsync(c->ctl, 0, offsetof(LayerCtl, peer_epoch), s));
   CK(cudaMemsetAsync(c->xcnt, 0, sizeof(unsigned) * kMaxUnique, s));
+  CK(cudaMemsetAsync(c->rb_cnt, 0, sizeof(unsigned) * kRbItems, s));
   CK(cudaStreamSynchronize(s));
   return FRC_OK;
 }
@@ -725,6 +869,12 @@ int frc_set_wait_limit(frc_context* c, uint64_t ns) {
   return FRC_OK;
 }
 
+int frc_debug_layer_variant(frc_context* c, int variant) {
+  if (!c || variant < 0 || variant > 2) return FRC_INVALID;
+  c->rb = variant;
+  return FRC_OK;
+}
+
 int frc_debug_barrier_extra(frc_context* c, unsigned extra) {
   if (!c || extra > 1024) return FRC_INVALID;
   c->bar_extra = extra;
@@ -761,6 +911,9 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
   alloc(reinterpret_cast<void**>(&c->ctl), sizeof(LayerCtl));
   alloc(reinterpret_cast<void**>(&c->xchg), sizeof(float) * kMaxUnique * 32);
   alloc(reinterpret_cast<void**>(&c->xcnt), sizeof(unsigned) * kMaxUnique);
+  alloc(reinterpret_cast<void**>(&c->rb_cnt), sizeof(unsigned) * kRbItems);
+  alloc(reinterpret_cast<void**>(&c->rb_hq), 32 * kRbItems);
+  alloc(reinterpret_cast<void**>(&c->rb_hs), sizeof(float) * kRbItems);
   alloc(reinterpret_cast<void**>(&c->phases), sizeof(unsigned long long) * 16 * 1024);
   const size_t in_bytes = kInBytesPerToken(d) * FRC_MAX_PREFILL_TOKENS,
                out_bytes = 16 + sizeof(float) * FRC_MAX_PREFILL_TOKENS * d;
@@ -794,6 +947,7 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
   }
   if (rc == FRC_OK && (cudaMemset(c->ctl, 0, sizeof(LayerCtl)) != cudaSuccess ||
                        cudaMemset(c->xcnt, 0, sizeof(unsigned) * kMaxUnique) != cudaSuccess ||
+                       cudaMemset(c->rb_cnt, 0, sizeof(unsigned) * kRbItems) != cudaSuccess ||
                        cudaMemset(c->status, 0, sizeof(unsigned)) != cudaSuccess ||
                        cudaMemset(c->hidden, 0, kHiddenBytes) != cudaSuccess))
     rc = fail(c, FRC_IO, "cudaMemset");
@@ -813,7 +967,7 @@ int frc_close(frc_context* c) {
   for (auto& b : c->layer_ptr)
     for (auto& p : b) if (p) cudaFree(p);
   cudaFree(c->staging); cudaFree(c->hidden); cudaFree(c->partial); cudaFree(c->gsv); cudaFree(c->phases); cudaFree(c->ctl);
-  cudaFree(c->xchg); cudaFree(c->xcnt);
+  cudaFree(c->xchg); cudaFree(c->xcnt); cudaFree(c->rb_cnt); cudaFree(c->rb_hq); cudaFree(c->rb_hs);
   cudaFree(c->d_in); cudaFree(c->d_out); cudaFree(c->pool);
   cudaFree(c->pf_xq); cudaFree(c->pf_xs); cudaFree(c->pf_pair_token); cudaFree(c->pf_slot_pair); cudaFree(c->pf_counts);
   cudaFree(c->pf_items_gu); cudaFree(c->pf_items_dn); cudaFree(c->pf_hq); cudaFree(c->pf_hs); cudaFree(c->pf_ye);

@@ -50,6 +50,7 @@ constexpr unsigned kMaxPeers = 8;              // GPUs of one in-box reduce
 struct LayerCtl {
   unsigned long long arrived;   // grid barrier arrivals, all launches (never wraps)
   unsigned abort;               // set by a CTA whose bounded wait ran out
+  unsigned pad0;
   // In-box reduce launches completed on this context.  Every CTA of a
   // FRC_RUN_PEER launch reads it once it may read memory (after the
   // programmatic-launch wait) and before it arrives at the grid barrier;
@@ -57,6 +58,7 @@ struct LayerCtl {
   // so one launch carries one epoch whatever its grid size.  A timeout reset
   // keeps it; frc_peer_attach zeroes it on every rank.
   unsigned peer_epoch;
+  unsigned pad;
 };
 
 // Byte offsets of one CTA's dynamic shared memory, and the chunking of an
@@ -72,6 +74,10 @@ struct LayerSmem {
   unsigned dn_r, dn_s;  // rows per down chunk: routed, shared items (multiples of 16)
   unsigned mag_ch_r, mag_ch_s;  // div_magic of the chunks per routed / shared item
   unsigned max_unique;          // entries of the plan's per-expert tables (10 x tokens + 1)
+  // row-owner kernel (frc_layer_rb.cuh): down-row staging [item] of dnb_r
+  // (routed) / dnb_s (shared) bytes, rows_max rows a CTA at most, dnw
+  // 16-byte pieces of scales window an item
+  unsigned dnb, dnb_r, dnb_s, rows_max, dnw;
 };
 
 struct LayerParams {
@@ -109,6 +115,11 @@ struct LayerParams {
   unsigned H, Hshift;
   float* xchg;
   unsigned* xcnt;
+  // row-owner kernel: per-item arrival counts of the gate/up chunks (zero
+  // between launches), and the items' quantized hidden slices
+  unsigned* rb_cnt;
+  uint8_t* rb_hq;   // [item][32] int8 (prmt order for MXFP4 down rows)
+  float* rb_hs;     // [item] hidden scale
   LayerSmem sm;
   unsigned S, T, d, norm;
   unsigned mag_S;  // div_magic(S)
@@ -317,6 +328,172 @@ __device__ __forceinline__ void down_terms4(const uint8_t* slot, unsigned nr, co
   h3 = tid + 3 * kLayerThreads < nr ? down_term<DT, ACT>(slot, nr, tid + 3 * kLayerThreads, s_hq, 0, bad) : 0.0f;
 }
 
+// Warps 0-3: the layer input.  Reads x (+ x_add; stores the sum to x_out
+// from CTA 0), applies the optional RMS pre-norm, and quantizes per 64
+// (src/q4.c:37-61) into the activation layout of LayerSmem: v and the
+// dequantization residuals r (natural and, for MXFP4 rows, prmt order),
+// {s, 2^E} per group and {V, RS} per 32-block; fp32 x in the F32 mode.
+// Needs only x, so it runs while the plan warps build the plan and start
+// the weight copies.
+template <int ACT>
+__device__ __forceinline__ void layer_input(const LayerParams& a, uint8_t* smem, unsigned T, unsigned tid,
+                                            unsigned lane, unsigned warp, unsigned cta) {
+  float* s_rms = reinterpret_cast<float*>(smem + a.sm.rms);
+  float* s_rpart = reinterpret_cast<float*>(smem + a.sm.rpart);  // [round][warp] sums of squares
+  const unsigned d = a.d, P = d / 64;
+  (void)P;
+  pdl_wait();
+  // A unit is a quarter of a 64-element x group: 16 floats, one thread.
+  // Four consecutive lanes hold a group, so its max and sums take two
+  // shuffles, and a thread's 16 int8 values are one 16-byte store.
+  const unsigned units = T * d / 16, upt = d / 16;  // units in all, per token
+  const unsigned upt_magic = 0xffffffffu / upt + 1;  // unit / upt by multiply-high (exact: unit < 2^16)
+  auto load_unit = [&](unsigned u, float (&v)[16]) {
+    const float4* x4 = reinterpret_cast<const float4*>(a.x) + 4 * u;
+    const float4* xa4 = a.x_add ? reinterpret_cast<const float4*>(a.x_add) + 4 * u : nullptr;
+#pragma unroll
+    for (unsigned k = 0; k < 4; ++k) {
+      float4 w = x4[k];
+      if (xa4) {
+        const float4 z = xa4[k];
+        w.x = __fadd_rn(w.x, z.x); w.y = __fadd_rn(w.y, z.y); w.z = __fadd_rn(w.z, z.z); w.w = __fadd_rn(w.w, z.w);
+      }
+      v[4 * k] = w.x; v[4 * k + 1] = w.y; v[4 * k + 2] = w.z; v[4 * k + 3] = w.w;
+    }
+  };
+  float v0[16];  // the first unit stays in registers from the sums to the quantization
+  if (tid < units) load_unit(tid, v0);
+  bool bad = false;
+  if (a.norm) {
+    // sums of squares per (pass, warp): a warp-pass covers 512 floats, all in one token
+    for (unsigned u0 = 0; u0 < units; u0 += kActThreads) {
+      const unsigned u = u0 + tid;
+      float ss = 0.0f;
+      if (u < units) {
+        float v[16];
+        if (u0 == 0) {
+#pragma unroll
+          for (unsigned k = 0; k < 16; ++k) v[k] = v0[k];
+        } else {
+          load_unit(u, v);
+        }
+#pragma unroll
+        for (unsigned k = 0; k < 16; ++k) ss = __fmaf_rn(v[k], v[k], ss);
+      }
+#pragma unroll
+      for (unsigned o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      if (lane == 0) s_rpart[u0 / 32 + warp] = ss;
+    }
+    act_sync();
+    PHASE(2);
+    // token t: warp-passes [t * d/512, (t+1) * d/512); warp w takes tokens
+    // w, w+4, ...; lane L adds passes L, L+32, ...; butterfly
+    for (unsigned t = warp; t < T; t += kActWarps) {
+      const unsigned per = d / 512;
+      float tot = 0.0f;
+      for (unsigned b = lane; b < per; b += 32) tot = __fadd_rn(tot, s_rpart[t * per + b]);
+#pragma unroll
+      for (unsigned o = 16; o; o >>= 1) tot = __fadd_rn(tot, __shfl_xor_sync(0xffffffffu, tot, o));
+      if (lane == 0) s_rms[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(d)), 1e-6f)));
+    }
+    act_sync();
+  }
+  for (unsigned u0 = 0; u0 < units; u0 += kActThreads) {
+    const unsigned u = u0 + tid;
+    if (u >= units) break;  // warp-uniform: units is a multiple of 32
+    float v[16];
+    if (u0 == 0) {
+#pragma unroll
+      for (unsigned k = 0; k < 16; ++k) v[k] = v0[k];
+    } else {
+      load_unit(u, v);
+    }
+    const unsigned t = __umulhi(u, upt_magic), j16 = u - t * upt, p = j16 >> 2, qd = j16 & 3;
+#pragma unroll
+    for (unsigned k = 0; k < 16; ++k) bad |= !isfinite(v[k]);
+    if (a.x_out && cta == 0) {
+      float4* xo = reinterpret_cast<float4*>(a.x_out) + 4 * u;
+#pragma unroll
+      for (unsigned k = 0; k < 4; ++k) xo[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+    }
+    if (a.norm) {
+      const float g = s_rms[t];
+#pragma unroll
+      for (unsigned k = 0; k < 16; ++k) v[k] = __fmul_rn(v[k], g);
+    }
+    if (ACT == FRC_ACT_F32) {
+      float4* xf = reinterpret_cast<float4*>(smem + a.sm.xf) + 4 * u;
+#pragma unroll
+      for (unsigned k = 0; k < 4; ++k) xf[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+      continue;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (unsigned k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(v[k]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const Q8Group qg(amax);
+    int qv[16], rv[16], sum = 0, rsum = 0;
+    if (__builtin_expect(qg.mul_ok(), 1)) {
+#pragma unroll
+      for (unsigned k = 0; k < 16; ++k) {
+        qv[k] = qg.qm(v[k]);
+        sum += qv[k];
+      }
+    } else {
+#pragma unroll
+      for (unsigned k = 0; k < 16; ++k) {
+        qv[k] = qg.q(v[k]);
+        sum += qv[k];
+      }
+    }
+    // Residuals of the reference's dequantized values (src/q4.c:54-58):
+    // X = fl32(v * s), capped at FLT_MAX; X - v*s = r * 2^E exactly, E =
+    // ef - 150.  The fma gives X - v*s exactly; two power-of-two scalings
+    // (each representable) take it to r.
+    const unsigned ef = scale_ef(qg.scale), shr = 150 - ef;
+    const float f1 = __uint_as_float((127 + (shr >> 1)) << 23), f2 = __uint_as_float((127 + shr - (shr >> 1)) << 23);
+#pragma unroll
+    for (unsigned k = 0; k < 16; ++k) {
+      const float vf = i2f(qv[k]);
+      float X = __fmul_rn(vf, qg.scale);
+      if (fabsf(X) > 3.40282347e38f) X = copysignf(3.40282347e38f, vf);
+      rv[k] = f2i_small(__fmul_rn(__fmul_rn(__fmaf_rn(-vf, qg.scale, X), f1), f2));
+      rsum += rv[k];
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);  // quarters 0+1 and 2+3: the two 32-element halves
+    rsum += __shfl_xor_sync(0xffffffffu, rsum, 1);
+    uint32_t w[4], wr[4];
+#pragma unroll
+    for (unsigned k = 0; k < 4; ++k) {
+      w[k] = (qv[4 * k] & 0xff) | (qv[4 * k + 1] & 0xff) << 8 | (qv[4 * k + 2] & 0xff) << 16 |
+             static_cast<uint32_t>(qv[4 * k + 3] & 0xff) << 24;
+      wr[k] = (rv[4 * k] & 0xff) | (rv[4 * k + 1] & 0xff) << 8 | (rv[4 * k + 2] & 0xff) << 16 |
+              static_cast<uint32_t>(rv[4 * k + 3] & 0xff) << 24;
+    }
+    const unsigned slot16 = 16 * xslot(p, qd, d / 256);
+    *reinterpret_cast<uint4*>(smem + a.sm.xq + t * d + slot16) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(smem + a.sm.xr + t * d + slot16) = make_uint4(wr[0], wr[1], wr[2], wr[3]);
+    if (qd == 0)
+      reinterpret_cast<double2*>(smem + a.sm.xst)[t * P + p] =
+          make_double2(static_cast<double>(qg.scale), pow2d(static_cast<int>(ef) - 150));
+    if ((qd & 1) == 0)
+      reinterpret_cast<int2*>(smem + a.sm.xvr)[2 * (t * P + p) + (qd >> 1)] = make_int2(sum, rsum);
+    if (a.sm.xp) {
+      uint8_t* xp = smem + a.sm.xp + t * d;
+      uint8_t* xrp = smem + a.sm.xrp + t * d;
+#pragma unroll
+      for (unsigned k = 0; k < 16; ++k) {
+        const unsigned e = 16 * qd + k, wi = (e / 32) * 32 + prmt_pos(e % 32);
+        const unsigned at = 16 * xslot(p, wi / 16, d / 256) + wi % 16;
+        xp[at] = static_cast<uint8_t>(qv[k] & 0xff);
+        xrp[at] = static_cast<uint8_t>(rv[k] & 0xff);
+      }
+    }
+  }
+  if (bad) atomicOr(a.status, kStNumeric);
+}
+
 // ONE: a one-token launch, the token count folded to 1 at compile time (its
 // loops over tokens and the multi-token plan drop out).  SPLIT implies ONE.
 // SPLIT: items may be split in a.H parts (one token); without it H is 1 at
@@ -335,8 +512,6 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
   unsigned* s_umask = reinterpret_cast<unsigned*>(smem + a.sm.umask);
   float* s_ugate = reinterpret_cast<float*>(smem + a.sm.ugate);
   unsigned* s_upre = reinterpret_cast<unsigned*>(smem + a.sm.upre);  // first pair of each expert
-  float* s_rms = reinterpret_cast<float*>(smem + a.sm.rms);
-  float* s_rpart = reinterpret_cast<float*>(smem + a.sm.rpart);      // [round][warp] sums of squares
   uint16_t* s_tokpair = reinterpret_cast<uint16_t*>(smem + a.sm.tokpair);  // [token][11] -> pair
   float* s_gv = reinterpret_cast<float*>(smem + a.sm.gv);            // [neuron][k] hidden values
   uint8_t* s_hq = smem + a.sm.hq;                                    // [k][32] int8, or [k][32] f32
@@ -572,160 +747,7 @@ __global__ void __launch_bounds__(kLayerThreads, 2) moe_layer_kernel(const Layer
     }
     pdl_wait();
   }
-  if (warp < kActWarps) {
-    // ------------------------------------------- warps 0-3: layer input
-    // (needs only x: runs while warps 4-7 plan and start the weight copies)
-    pdl_wait();
-    // A unit is a quarter of a 64-element x group: 16 floats, one thread.
-    // Four consecutive lanes hold a group, so its max and sums take two
-    // shuffles, and a thread's 16 int8 values are one 16-byte store.
-    const unsigned units = T * d / 16, upt = d / 16;  // units in all, per token
-    const unsigned upt_magic = 0xffffffffu / upt + 1;  // unit / upt by multiply-high (exact: unit < 2^16)
-    auto load_unit = [&](unsigned u, float (&v)[16]) {
-      const float4* x4 = reinterpret_cast<const float4*>(a.x) + 4 * u;
-      const float4* xa4 = a.x_add ? reinterpret_cast<const float4*>(a.x_add) + 4 * u : nullptr;
-#pragma unroll
-      for (unsigned k = 0; k < 4; ++k) {
-        float4 w = x4[k];
-        if (xa4) {
-          const float4 z = xa4[k];
-          w.x = __fadd_rn(w.x, z.x); w.y = __fadd_rn(w.y, z.y); w.z = __fadd_rn(w.z, z.z); w.w = __fadd_rn(w.w, z.w);
-        }
-        v[4 * k] = w.x; v[4 * k + 1] = w.y; v[4 * k + 2] = w.z; v[4 * k + 3] = w.w;
-      }
-    };
-    float v0[16];  // the first unit stays in registers from the sums to the quantization
-    if (tid < units) load_unit(tid, v0);
-    bool bad = false;
-    if (a.norm) {
-      // sums of squares per (pass, warp): a warp-pass covers 512 floats, all in one token
-      for (unsigned u0 = 0; u0 < units; u0 += kActThreads) {
-        const unsigned u = u0 + tid;
-        float ss = 0.0f;
-        if (u < units) {
-          float v[16];
-          if (u0 == 0) {
-#pragma unroll
-            for (unsigned k = 0; k < 16; ++k) v[k] = v0[k];
-          } else {
-            load_unit(u, v);
-          }
-#pragma unroll
-          for (unsigned k = 0; k < 16; ++k) ss = __fmaf_rn(v[k], v[k], ss);
-        }
-#pragma unroll
-        for (unsigned o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-        if (lane == 0) s_rpart[u0 / 32 + warp] = ss;
-      }
-      act_sync();
-      PHASE(2);
-      // token t: warp-passes [t * d/512, (t+1) * d/512); warp w takes tokens
-      // w, w+4, ...; lane L adds passes L, L+32, ...; butterfly
-      for (unsigned t = warp; t < T; t += kActWarps) {
-        const unsigned per = d / 512;
-        float tot = 0.0f;
-        for (unsigned b = lane; b < per; b += 32) tot = __fadd_rn(tot, s_rpart[t * per + b]);
-#pragma unroll
-        for (unsigned o = 16; o; o >>= 1) tot = __fadd_rn(tot, __shfl_xor_sync(0xffffffffu, tot, o));
-        if (lane == 0) s_rms[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(d)), 1e-6f)));
-      }
-      act_sync();
-    }
-    for (unsigned u0 = 0; u0 < units; u0 += kActThreads) {
-      const unsigned u = u0 + tid;
-      if (u >= units) break;  // warp-uniform: units is a multiple of 32
-      float v[16];
-      if (u0 == 0) {
-#pragma unroll
-        for (unsigned k = 0; k < 16; ++k) v[k] = v0[k];
-      } else {
-        load_unit(u, v);
-      }
-      const unsigned t = __umulhi(u, upt_magic), j16 = u - t * upt, p = j16 >> 2, qd = j16 & 3;
-#pragma unroll
-      for (unsigned k = 0; k < 16; ++k) bad |= !isfinite(v[k]);
-      if (a.x_out && cta == 0) {
-        float4* xo = reinterpret_cast<float4*>(a.x_out) + 4 * u;
-#pragma unroll
-        for (unsigned k = 0; k < 4; ++k) xo[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-      }
-      if (a.norm) {
-        const float g = s_rms[t];
-#pragma unroll
-        for (unsigned k = 0; k < 16; ++k) v[k] = __fmul_rn(v[k], g);
-      }
-      if (ACT == FRC_ACT_F32) {
-        float4* xf = reinterpret_cast<float4*>(smem + a.sm.xf) + 4 * u;
-#pragma unroll
-        for (unsigned k = 0; k < 4; ++k) xf[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-        continue;
-      }
-      float amax = 0.0f;
-#pragma unroll
-      for (unsigned k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(v[k]));
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-      const Q8Group qg(amax);
-      int qv[16], rv[16], sum = 0, rsum = 0;
-      if (__builtin_expect(qg.mul_ok(), 1)) {
-#pragma unroll
-        for (unsigned k = 0; k < 16; ++k) {
-          qv[k] = qg.qm(v[k]);
-          sum += qv[k];
-        }
-      } else {
-#pragma unroll
-        for (unsigned k = 0; k < 16; ++k) {
-          qv[k] = qg.q(v[k]);
-          sum += qv[k];
-        }
-      }
-      // Residuals of the reference's dequantized values (src/q4.c:54-58):
-      // X = fl32(v * s), capped at FLT_MAX; X - v*s = r * 2^E exactly, E =
-      // ef - 150.  The fma gives X - v*s exactly; two power-of-two scalings
-      // (each representable) take it to r.
-      const unsigned ef = scale_ef(qg.scale), shr = 150 - ef;
-      const float f1 = __uint_as_float((127 + (shr >> 1)) << 23), f2 = __uint_as_float((127 + shr - (shr >> 1)) << 23);
-#pragma unroll
-      for (unsigned k = 0; k < 16; ++k) {
-        const float vf = i2f(qv[k]);
-        float X = __fmul_rn(vf, qg.scale);
-        if (fabsf(X) > 3.40282347e38f) X = copysignf(3.40282347e38f, vf);
-        rv[k] = f2i_small(__fmul_rn(__fmul_rn(__fmaf_rn(-vf, qg.scale, X), f1), f2));
-        rsum += rv[k];
-      }
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);  // quarters 0+1 and 2+3: the two 32-element halves
-      rsum += __shfl_xor_sync(0xffffffffu, rsum, 1);
-      uint32_t w[4], wr[4];
-#pragma unroll
-      for (unsigned k = 0; k < 4; ++k) {
-        w[k] = (qv[4 * k] & 0xff) | (qv[4 * k + 1] & 0xff) << 8 | (qv[4 * k + 2] & 0xff) << 16 |
-               static_cast<uint32_t>(qv[4 * k + 3] & 0xff) << 24;
-        wr[k] = (rv[4 * k] & 0xff) | (rv[4 * k + 1] & 0xff) << 8 | (rv[4 * k + 2] & 0xff) << 16 |
-                static_cast<uint32_t>(rv[4 * k + 3] & 0xff) << 24;
-      }
-      const unsigned slot16 = 16 * xslot(p, qd, d / 256);
-      *reinterpret_cast<uint4*>(smem + a.sm.xq + t * d + slot16) = make_uint4(w[0], w[1], w[2], w[3]);
-      *reinterpret_cast<uint4*>(smem + a.sm.xr + t * d + slot16) = make_uint4(wr[0], wr[1], wr[2], wr[3]);
-      if (qd == 0)
-        reinterpret_cast<double2*>(smem + a.sm.xst)[t * P + p] =
-            make_double2(static_cast<double>(qg.scale), pow2d(static_cast<int>(ef) - 150));
-      if ((qd & 1) == 0)
-        reinterpret_cast<int2*>(smem + a.sm.xvr)[2 * (t * P + p) + (qd >> 1)] = make_int2(sum, rsum);
-      if (a.sm.xp) {
-        uint8_t* xp = smem + a.sm.xp + t * d;
-        uint8_t* xrp = smem + a.sm.xrp + t * d;
-#pragma unroll
-        for (unsigned k = 0; k < 16; ++k) {
-          const unsigned e = 16 * qd + k, wi = (e / 32) * 32 + prmt_pos(e % 32);
-          const unsigned at = 16 * xslot(p, wi / 16, d / 256) + wi % 16;
-          xp[at] = static_cast<uint8_t>(qv[k] & 0xff);
-          xrp[at] = static_cast<uint8_t>(rv[k] & 0xff);
-        }
-      }
-    }
-    if (bad) atomicOr(a.status, kStNumeric);
-  }
+  if (warp < kActWarps) layer_input<ACT>(a, smem, T, tid, lane, warp, cta);
   __syncthreads();
   setup();
   if (a.world > 1 && tid == 0) misc[6] = *reinterpret_cast<volatile unsigned*>(&a.ctl->peer_epoch) + 1;

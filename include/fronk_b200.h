@@ -253,6 +253,14 @@ int frc_status(frc_context *c, void *stream);
  * untouched and the next call on the context runs normally.  No counterpart in
  * the reference (its timeouts are the plane's deadline, src/plane.c). */
 int frc_set_wait_limit(frc_context *c, uint64_t ns);
+/* Tests and measurements: which kernel may serve one-token FRC_ACT_Q8 calls.
+ * 1 (the default): the row-owner kernel (gate/up work dealt to every CTA in
+ * chunks of 8 neurons, each CTA then forms its own rows of y from all
+ * items' hidden values) when at most two slices are loaded, else the item
+ * kernel; 0: always the item kernel that serves larger bursts; 2: the
+ * row-owner kernel whenever its staging fits.  Both kernels compute the same
+ * values in the same order. */
+int frc_debug_layer_variant(frc_context *c, int variant);
 /* Tests only: raises the layer kernel's grid-barrier target by `extra`
  * arrivals (0 restores it), so that the barrier's bounded wait runs out. */
 int frc_debug_barrier_extra(frc_context *c, unsigned extra);
