@@ -75,9 +75,10 @@ _SIGS = {
     "frc_plane_open": (_int, [_vp, _u32, _vp]),
     "frc_plane_run": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _u64, _vp, _vp]),
     "frc_plane_close": (_int, [_vp]),
+    "frc_plane_late_status": (_int, [_vp, _u32, _vp]),
     "frc_round_half": (_int, [_vp, _sz, _vp]),
     "frc_costmodel_fit": (_int, [_vp, _vp, _u32, _vp]),
-    "frc_costmodel_measure": (_int, [_vp, _vp, _u32, _u32, _u32, _vp]),
+    "frc_costmodel_measure": (_int, [_vp, _vp, _u32, _u32, _u32, _int, _vp]),
     "frc_run": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _int]),
     "frc_run_device": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
     "frc_run_device_fixed": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
@@ -217,6 +218,14 @@ class Plane:
                                     ctypes.byref(m))
         return rc, y, m.value
 
+    def late_status(self, participant):
+        """frc_plane_late_status: the device status of the participant's last part that missed its deadline."""
+        st = ctypes.c_int()
+        rc = self.lib.frc_plane_late_status(self.h, participant, ctypes.byref(st))
+        if rc:
+            raise FrcError(rc, "plane_late_status")
+        return st.value
+
     def close(self):
         if self.h:
             self.lib.frc_plane_close(self.h)
@@ -341,10 +350,11 @@ class Context:
         (unit-BB.bin + unit-BB.sha256); returns the status code."""
         return self.lib.frc_units_open(self.h, os.fsencode(directory), mask, 1 if verify else 0)
 
-    def costmodel(self, layer=0, burst_max=4, samples=15):
+    def costmodel(self, layer=0, burst_max=4, samples=15, act=ACT_Q8):
         """(rc, CostModel) of frc_costmodel_measure on this context."""
         m = CostModel()
-        rc = self.lib.frc_costmodel_measure(self.h, ctypes.byref(self.g), layer, burst_max, samples, ctypes.byref(m))
+        rc = self.lib.frc_costmodel_measure(self.h, ctypes.byref(self.g), layer, burst_max, samples, act,
+                                            ctypes.byref(m))
         return rc, m
 
     def load_layer(self, block, layer, data):

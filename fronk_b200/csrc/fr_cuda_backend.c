@@ -197,7 +197,7 @@ static int bench(const fr_backend *b, int burst_max, fr_costmodel *out) {
     if (burst_max < 2 || burst_max > FR_MAX_BURST || burst_max > FRC_COST_MAX_BURST) return FR_INVALID;
     const frc_geometry g = reference_geometry();
     frc_costmodel m;
-    const int rc = frc_costmodel_measure(s->ctx, &g, 0, (unsigned)burst_max, 15, &m);
+    const int rc = frc_costmodel_measure(s->ctx, &g, 0, (unsigned)burst_max, 15, s->act, &m);
     if (rc) return rc;
     memset(out, 0, sizeof *out);
     out->burst_max = m.burst_max;

@@ -1314,6 +1314,7 @@ struct frc_plane {
   float* h_y[kMaxPeers] = {};     // pinned [16][d]
   cudaEvent_t done[kMaxPeers] = {};
   bool pending[kMaxPeers] = {};   // this participant's last call may still be running
+  int late_status[kMaxPeers] = {}; // device status of a part that missed its deadline (read later)
   float* xr = nullptr;            // [16][d] rounded x
 };
 
@@ -1387,6 +1388,9 @@ int frc_plane_run(frc_plane* p, unsigned layer, unsigned tokens, const uint16_t*
           return fail(c, FRC_IO, "plane participant %u still busy with an earlier layer", i);
       if (q != cudaSuccess) return fail(c, FRC_IO, "plane participant %u: %s", i, cudaGetErrorString(q));
       p->pending[i] = false;
+      // that part was left out of its call; its device status belongs to that
+      // call, not to this one: read, clear and keep it (frc_plane_late_status)
+      p->late_status[i] = frc_status(c, c->stream);
     }
     memcpy(p->h_in[i], p->xr, xb);
     memcpy(p->h_in[i] + xb, gate, gb);
@@ -1423,13 +1427,27 @@ int frc_plane_run(frc_plane* p, unsigned layer, unsigned tokens, const uint16_t*
       const int rc = frc_status(p->ctx[i], p->ctx[i]->stream);
       if (rc) return rc;
     }
-  for (size_t k = 0; k < static_cast<size_t>(tokens) * d; ++k) {
+  // Participant 0 is the head's own slice (fp32, as the head adds its local
+  // part).  Every other participant stands for a remote node, whose part the
+  // reference sends as fp16 (src/plane.c:181, src/wire.c:46-67): rounded to
+  // nearest even here, and a part with a value that has no finite fp16 form
+  // is left out and reported missing, as the node drops such a reply.
+  const size_t n = static_cast<size_t>(tokens) * d;
+  for (unsigned i = 1; i < p->n; ++i)
+    if (!(left >> i & 1) && frc_round_half(p->h_y[i], n, p->h_y[i])) left |= 1u << i;
+  for (size_t k = 0; k < n; ++k) {
     float s = 0.0f;
     for (unsigned i = 0; i < p->n; ++i)
       if (!(left >> i & 1)) s += p->h_y[i][k];
     y[k] = s;
   }
   *missing = left;
+  return FRC_OK;
+}
+
+int frc_plane_late_status(const frc_plane* p, unsigned participant, int* status) {
+  if (!p || !status || participant >= p->n) return FRC_INVALID;
+  *status = p->late_status[participant];
   return FRC_OK;
 }
 

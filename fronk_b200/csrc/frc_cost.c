@@ -53,9 +53,9 @@ static int cmp_double(const void *a, const void *b) {
 }
 
 int frc_costmodel_measure(frc_context *c, const frc_geometry *g, unsigned layer, unsigned burst_max,
-                          unsigned samples, frc_costmodel *out) {
+                          unsigned samples, int act, frc_costmodel *out) {
     if (!c || !g || !out || burst_max < 2 || burst_max > FRC_COST_MAX_BURST || samples < 1 || samples > 1000 ||
-        g->hidden == 0 || g->hidden > 8192)
+        g->hidden == 0 || g->hidden > 8192 || (act != FRC_ACT_Q8 && act != FRC_ACT_F32))
         return FRC_INVALID;
     uint32_t mask = 0;
     int rc = frc_loaded_mask(c, &mask);
@@ -75,7 +75,7 @@ int frc_costmodel_measure(frc_context *c, const frc_geometry *g, unsigned layer,
             if (rc) break;
             for (unsigned k = 0; k < b; ++k) gt[k * FRC_ACTIVE + FRC_TOPK] = 0.125f;  /* the shared expert runs */
             const double t0 = now_ns();
-            rc = frc_run(c, layer, b, e, gt, x, y, FRC_ACT_Q8);
+            rc = frc_run(c, layer, b, e, gt, x, y, act);
             if (s) t[s - 1] = now_ns() - t0;
         }
         if (rc) break;

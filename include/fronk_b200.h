@@ -127,7 +127,11 @@ int frc_sha256(const void *data, size_t len, uint8_t out[32]);
  * layer on every participant's stream (Q8 activations), and sums the parts
  * that are done by the deadline in participant order; bit i of *missing is
  * set for a participant that missed it, and its part is left out, as the
- * reference head leaves out a late node.  A late participant's next call
+ * reference head leaves out a late node.  Participant 0 is the head's own
+ * slice (its part is added in fp32); the parts of the others, standing for
+ * remote nodes, are rounded through fp16 as the reference sends them, and a
+ * part with a value that has no finite fp16 form is left out and reported
+ * missing, as the node drops such a reply.  A late participant's next call
  * waits (bounded) for its earlier one.  FRC_INVALID: bad arguments or an x
  * value with no finite fp16 form (nothing runs); a participant's device
  * error fails the call with y untouched.  Contexts must share a geometry and
@@ -138,6 +142,11 @@ int frc_plane_open(frc_context *const *ctx, unsigned count, frc_plane **out);
 int frc_plane_run(frc_plane *p, unsigned layer, unsigned tokens, const uint16_t *expert, const float *gate,
                   const float *x, uint64_t deadline_ns, float *y, uint32_t *missing);
 int frc_plane_close(frc_plane *p);
+/* The device status (FRC_OK or an error code) of participant i's last part
+ * that missed its deadline, read when that participant's next call found it
+ * done: such a part was left out of its own call, so its status is kept here
+ * instead of failing a later layer. */
+int frc_plane_late_status(const frc_plane *p, unsigned participant, int *status);
 /* ---- Cost model (fr_costmodel, src/backend.h:30-35) ----
  * t = t0 + 1e9 * bytes / bw_eff for a burst that reads `bytes` of weights,
  * the form the reference planner weighs participants with.  Same fields and
@@ -155,12 +164,12 @@ typedef struct {
  * nonpositive slope. */
 int frc_costmodel_fit(const double *ns, const uint64_t *bytes, unsigned n, frc_costmodel *out);
 /* Measures and fits it on this context: `samples` synchronous frc_run calls
- * of layer `layer` at each burst 1..burst_max (distinct seeded routing, the
- * shared expert active), medians, bytes = loaded blocks x (10 x burst x
- * slice + shared slice) (src/bench.c:157-160).  g: the context's geometry.
- * FRC_STATE when nothing is loaded. */
+ * of layer `layer` at each burst 1..burst_max in activation mode `act`
+ * (distinct seeded routing, the shared expert active), medians, bytes =
+ * loaded blocks x (10 x burst x slice + shared slice) (src/bench.c:157-160).
+ * g: the context's geometry.  FRC_STATE when nothing is loaded. */
 int frc_costmodel_measure(frc_context *c, const frc_geometry *g, unsigned layer, unsigned burst_max,
-                          unsigned samples, frc_costmodel *out);
+                          unsigned samples, int act, frc_costmodel *out);
 
 /* x rounded through fp16 as the head sends it: round to nearest even;
  * FRC_INVALID when a value is not finite or rounds past 65504, or the

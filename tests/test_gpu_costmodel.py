@@ -25,3 +25,7 @@ def test_costmodel_measure(gpu):
         assert m.burst_max == 4 and m.t0_ns >= 0 and np.isfinite(m.bw_eff) and m.bw_eff > 0
         assert all(np.isfinite(m.ns[b]) and m.ns[b] > 0 for b in range(4))
         print("cost model: t0 %.1f us, bw_eff %.1f GB/s, ns %s" % (m.t0_ns / 1e3, m.bw_eff / 1e9, list(m.ns)[:4]))
+        # the fp32-activation mode is measured in its own arithmetic (the cuda-f32 table's fit)
+        rc, m32 = ctx.costmodel(layer=0, burst_max=2, samples=3, act=fb.ACT_F32)
+        assert rc == fb.OK and m32.burst_max == 2 and all(m32.ns[b] > 0 for b in range(2))
+        assert ctx.costmodel(layer=0, burst_max=2, samples=3, act=7)[0] == fb.INVALID
