@@ -223,7 +223,9 @@ struct frc_context {
   // prefill (bursts above FRC_MAX_TOKENS; MXFP4 gate/up and down only):
   // activations, pairs, work lists, hidden values and expert partials
   int8_t* pf_xq = nullptr;
+  int8_t* pf_xr = nullptr;
   float* pf_xs = nullptr;
+  int2* pf_xme = nullptr;
   uint16_t* pf_pair_token = nullptr;
   unsigned* pf_slot_pair = nullptr;
   unsigned* pf_counts = nullptr;
@@ -726,7 +728,8 @@ static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_
   a.row_bytes = static_cast<unsigned>(c->row_bytes);
   a.slice_bytes = c->slice_bytes;
   a.slice_rows = static_cast<unsigned>(c->slice_bytes / c->row_bytes);
-  a.xq = c->pf_xq; a.xs = c->pf_xs; a.pair_token = c->pf_pair_token; a.slot_pair = c->pf_slot_pair;
+  a.xq = c->pf_xq; a.xr = c->pf_xr; a.xs = c->pf_xs; a.xme = c->pf_xme;
+  a.pair_token = c->pf_pair_token; a.slot_pair = c->pf_slot_pair;
   a.counts = c->pf_counts; a.items_gu = c->pf_items_gu; a.items_dn = c->pf_items_dn;
   a.hq = c->pf_hq; a.hs = c->pf_hs; a.ye = c->pf_ye; a.status = c->status;
   a.phases = c->phases;
@@ -735,6 +738,16 @@ static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_
   if (!c->pf_attr) {
     CK(cudaFuncSetAttribute(prefill_mma_kernel<kGateUp>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(prefill_mma_kernel<kDown>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    // The kernels' setmaxnreg split is sized for 128 registers a thread at
+    // launch: with fewer, the epilogue's increase could never be granted.
+    for (const void* k : {reinterpret_cast<const void*>(prefill_mma_kernel<kGateUp>),
+                          reinterpret_cast<const void*>(prefill_mma_kernel<kDown>)}) {
+      cudaFuncAttributes fa;
+      CK(cudaFuncGetAttributes(&fa, k));
+      if (fa.numRegs != 128)
+        return fail(c, FRC_UNSUPPORTED, "prefill kernel built with %d registers a thread (its split needs 128)",
+                    fa.numRegs);
+    }
     c->pf_attr = true;
   }
   const unsigned groups = T * (d / 64);
@@ -921,7 +934,9 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
       c->layer_bytes % c->row_bytes == 0) {
     const size_t T = FRC_MAX_PREFILL_TOKENS;
     alloc(reinterpret_cast<void**>(&c->pf_xq), T * d);
+    alloc(reinterpret_cast<void**>(&c->pf_xr), T * d);
     alloc(reinterpret_cast<void**>(&c->pf_xs), sizeof(float) * T * (d / 64));
+    alloc(reinterpret_cast<void**>(&c->pf_xme), sizeof(int2) * T * (d / 64));
     alloc(reinterpret_cast<void**>(&c->pf_pair_token), sizeof(uint16_t) * kPfMaxPairs);
     alloc(reinterpret_cast<void**>(&c->pf_slot_pair), sizeof(unsigned) * kPfMaxPairs);
     alloc(reinterpret_cast<void**>(&c->pf_counts), sizeof(unsigned) * 4);
@@ -969,7 +984,7 @@ int frc_close(frc_context* c) {
   cudaFree(c->staging); cudaFree(c->hidden); cudaFree(c->partial); cudaFree(c->gsv); cudaFree(c->phases); cudaFree(c->ctl);
   cudaFree(c->xchg); cudaFree(c->xcnt); cudaFree(c->rb_cnt); cudaFree(c->rb_hq); cudaFree(c->rb_hs);
   cudaFree(c->d_in); cudaFree(c->d_out); cudaFree(c->pool);
-  cudaFree(c->pf_xq); cudaFree(c->pf_xs); cudaFree(c->pf_pair_token); cudaFree(c->pf_slot_pair); cudaFree(c->pf_counts);
+  cudaFree(c->pf_xq); cudaFree(c->pf_xr); cudaFree(c->pf_xs); cudaFree(c->pf_xme); cudaFree(c->pf_pair_token); cudaFree(c->pf_slot_pair); cudaFree(c->pf_counts);
   cudaFree(c->pf_items_gu); cudaFree(c->pf_items_dn); cudaFree(c->pf_hq); cudaFree(c->pf_hs); cudaFree(c->pf_ye);
   cudaFreeHost(c->h_in); cudaFreeHost(c->h_out);
   if (c->stream) cudaStreamDestroy(c->stream);

@@ -62,6 +62,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
       : "memory");
   return ok != 0;
 }
+// The same test, but a thread whose phase is incomplete may sleep up to `ns`
+// nanoseconds (it wakes when the phase completes): a waiting warp then takes
+// no issue slots from the warps that work beside it.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, unsigned parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -207,6 +221,10 @@ __device__ __forceinline__ unsigned xslot(unsigned p, unsigned q, unsigned nspan
 // Exact int32 -> double: 2^52 + 2^51 + k carries k in its low bits.
 __device__ __forceinline__ double i2d(int k) {
   return __hiloint2double(0x43380000 + (k >> 31), k) - 6755399441055744.0;
+}
+// Exact int64 -> double for |z| < 2^51.
+__device__ __forceinline__ double ll2d(long long z) {
+  return __longlong_as_double(0x4338000000000000LL + z) - 6755399441055744.0;
 }
 // 2^e as a double, -1022 <= e <= 1023.
 __device__ __forceinline__ double pow2d(int e) { return __hiloint2double((e + 1023) << 20, 0); }

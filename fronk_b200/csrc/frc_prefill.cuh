@@ -4,16 +4,21 @@
 // One layer call is five launches on one stream:
 //   1. prefill_quantize_kernel: x -> int8 per 64 (the ref-q8 scheme of
 //      src/q4.c:37-61), each 32-block stored in the nibble order of an MXFP4
-//      block (prmt order), plus one fp32 scale per 64;
+//      block (prmt order), plus one fp32 scale s per 64 and, for the exact
+//      block terms, the residuals r = (fl32(v * s) - v * s) / 2^E of the
+//      dequantized values (s = M * 2^E, |r| <= 64);
 //   2. prefill_group_kernel (one CTA): validation, the (expert, token) pairs
 //      expert-major with tokens ascending (a bitmap per expert, ranks by
 //      popcount), and the work lists, biggest experts first;
 //   3. prefill_mma_kernel<kGateUp>: item = (expert, pair of loaded blocks,
 //      up to 64 of its tokens).  A = the 128 gate/up rows of the two slices
-//      (int8: doubled E2M1 values), B = the tokens' int8 activations,
-//      D = int32 in tensor memory, one tcgen05.mma kind::i8 per 32-weight
-//      block; the epilogue applies the block's two scales in fp32, then
-//      SwiGLU (double) and Q8 per 32 give hq / hscale per (pair, block);
+//      (int8: doubled E2M1 values), B = the tokens' int8 activations v
+//      (rows 0-63) and residuals r (rows 64-127), D = int32 in tensor
+//      memory, one tcgen05.mma kind::i8 per 32-weight block (N 128: the dots
+//      I with v and R with r); the epilogue forms each block's exact term
+//      (M * I + R) * 2^(e - 128 + E) and sums the terms in double, narrows
+//      the sum to fp32, then SwiGLU (double) and Q8 per 32 give hq / hscale
+//      per (pair, block);
 //   4. prefill_mma_kernel<kDown>: item = (expert, 128 output rows, tokens);
 //      A = MXFP4 down rows, B = hq, one MMA per loaded block;
 //   5. prefill_combine_kernel: y[t] = sum over the token's experts in
@@ -28,22 +33,38 @@
 //     columns (TMEM lanes 0-127 = A rows);
 //   warp 12 issues the bulk copies; warp 13 owns tensor memory and issues
 //   the MMAs (one thread).
-// Rings: 3 raw stages, 3 A/B stages, 8 accumulator buffers of 64 columns
-// (all of tensor memory) used as two groups of four MMA steps, so that the
-// epilogue takes one barrier and several independent TMEM reads per group.
+// Rings: 3 raw stages, 2 A/B stages (freed by the MMAs' commit), 4 scale
+// stages (freed by the epilogue), and all 512 tensor-memory columns as two
+// groups of accumulator buffers (gate/up: two MMA steps of 128 columns,
+// down: four of 64), so that the epilogue takes one barrier and several
+// independent TMEM reads per group.
 // Every wait gives up after 2 s (kStTimeout) so a fault cannot hang the GPU.
 #pragma once
 #include <cuda.h>
 
 namespace frc {
 
-constexpr unsigned kPfTile = 64;        // tokens per item (MMA N <= 64)
+constexpr unsigned kPfTile = 64;        // tokens per item
 constexpr unsigned kPfRaw = 3;          // raw payload stages
-constexpr unsigned kPfAB = 3;           // A/B operand stages
+constexpr unsigned kPfAB = 2;           // A/B operand stages (released by the MMA's commit)
+constexpr unsigned kPfSc = 4;           // scale stages (released by the epilogue)
 constexpr unsigned kPfRawBytes = 16384; // 128 rows x 128 B (gate/up) or 8 blocks x 128 rows x 16 B (down)
 constexpr unsigned kPfA = 128 * 256;    // A stage: 128 rows x K 256
-constexpr unsigned kPfB = kPfTile * 256;
-constexpr unsigned kPfAcc = 8;          // accumulator buffers (two groups of four MMA steps)
+// B stage: 128 rows x K 256.  Gate/up: rows [0, npad) the tile's tokens'
+// int8 activations v, rows [npad, 2 npad) their dequantization residuals r
+// (npad = tokens rounded up to 16, MMA N 2 npad); down: rows [0, npad) the
+// pairs' quantized hidden values (MMA N npad).
+constexpr unsigned kPfB = 2 * kPfTile * 256;
+constexpr unsigned kPfCols = 512;       // tensor memory columns: two groups of accumulator buffers
+// Accumulator groups: group g takes columns [256 g, 256 g + 256) as GS
+// buffers of BW columns, one MMA step each.  Gate/up: BW = 2 npad (the v
+// then the r results), GS = 128 / npad (a whole 8-step chunk for tiles of
+// up to 16 tokens, so that the epilogue reads many steps at once); down:
+// BW = 64, GS = 4.
+template <unsigned MODE>
+__device__ __forceinline__ unsigned pf_bw(unsigned npad) { return MODE == 0 ? 2 * npad : 64u; }
+template <unsigned MODE>
+__device__ __forceinline__ unsigned pf_gs(unsigned npad) { return MODE == 0 ? 128 / npad : 4u; }
 constexpr unsigned kPfThreads = 448;     // 14 warps
 enum : unsigned { kGateUp = 0, kDown = 1 };
 
@@ -62,7 +83,9 @@ struct PrefillArgs {
   CUtensorMap tmap[kMaxBlocks];
   // scratch
   int8_t* xq;              // [T][d], prmt order per 32-block
+  int8_t* xr;              // [T][d], the residuals of the dequantized values, same order
   float* xs;               // [T][d/64]
+  int2* xme;               // [T][d/64] {M, E << 20}: xs = M * 2^E
   uint16_t* pair_token;    // [P]
   unsigned* slot_pair;     // [T][10]
   unsigned* counts;        // [0] pairs, [1] gate/up items, [2] down items
@@ -75,14 +98,33 @@ struct PrefillArgs {
   unsigned long long* phases;  // FRC_PHASES builds: [cta][64] globaltimer stamps
 };
 
-// FRC_PHASES builds: stamps of each CTA's second gate/up item (0 entry; per chunk k:
-// 1+k converters ready, 9+k raw landed, 17+k A/B staged, 25+k MMA start,
-// 33+k MMAs issued, 41+k epilogue done, 50+k copies issued; 49 item done).
+// FRC_PHASES builds: per CTA, the clock64 cycles that one thread of each role
+// spends in its waits and in its work, summed over the launch, in
+// a.phases[cta][64]: converters (thread 0) 0 raw landed, 1 conversion,
+// 2 free stages, 3 gathers issued, 4 own copies landed; producer (thread 384)
+// 8 free raw stage, 9 copies issued; MMA (thread 416) 12 operands staged,
+// 13 free accumulators, 14 MMAs issued; epilogue warpgroups (threads 128,
+// 256) 16/24 scales staged, 17/25 accumulators ready, 18/26 block terms,
+// 19/27 item tail; 40 the CTA's cycles from entry to exit.
 #ifdef FRC_PHASES
-#define PF_STAMP(k, cond) \
-  do { if (MODE == kGateUp && (cond) && a.phases) a.phases[blockIdx.x * 64 + (k)] = globaltimer(); } while (0)
+__device__ __forceinline__ long long pf_now() { return clock64(); }
+struct PfClock {
+  long long t;
+  long long ph[5];
+  __device__ PfClock() : t(pf_now()), ph{0, 0, 0, 0, 0} {}
+  __device__ void lap(unsigned k) {
+    const long long n = pf_now();
+    ph[k] += n - t;
+    t = n;
+  }
+  __device__ void store(unsigned long long* out, unsigned base, bool who) const {
+    if (out && who)
+      for (unsigned k = 0; k < 5; ++k) out[blockIdx.x * 64 + base + k] = static_cast<unsigned long long>(ph[k]);
+  }
+};
+#define PF_PH(x) x
 #else
-#define PF_STAMP(k, cond) do { } while (0)
+#define PF_PH(x)
 #endif
 
 // ------------------------------------------------------------- helpers
@@ -90,7 +132,7 @@ struct PrefillArgs {
 __device__ __forceinline__ bool pf_wait(uint64_t* bar, unsigned parity, volatile unsigned* abort) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity, 1000000)) {
     if (*abort) return false;
     if (globaltimer() - start > kWaitNs) {
       *abort = 1;
@@ -193,10 +235,31 @@ __global__ void prefill_quantize_kernel(PrefillArgs a) {
   for (unsigned o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   const Q8Group q(amax);
   int8_t* out = a.xq + 64 * static_cast<size_t>(g);
+  int8_t* rout = a.xr + 64 * static_cast<size_t>(g);
   const unsigned n0 = 2 * lane, blk = n0 >> 5, n = n0 & 31;
-  out[32 * blk + prmt_pos(n)] = static_cast<int8_t>(q.q(v.x));
-  out[32 * blk + prmt_pos(n + 1)] = static_cast<int8_t>(q.q(v.y));
-  if (lane == 0) a.xs[g] = q.scale;
+  const int q0 = q.q(v.x), q1 = q.q(v.y);
+  out[32 * blk + prmt_pos(n)] = static_cast<int8_t>(q0);
+  out[32 * blk + prmt_pos(n + 1)] = static_cast<int8_t>(q1);
+  // the residuals X - v * s = r * 2^E of the reference's dequantized values
+  // X = fl32(v * s) (src/q4.c:54-58, the FLT_MAX cap included), as in the
+  // decode kernel's activation pass
+  const unsigned ef = scale_ef(q.scale), shr = 150 - ef;
+  const float f1 = __uint_as_float((127 + (shr >> 1)) << 23), f2 = __uint_as_float((127 + shr - (shr >> 1)) << 23);
+  auto resid = [&](int qv) {
+    const float vf = i2f(qv);
+    float X = __fmul_rn(vf, q.scale);
+    if (fabsf(X) > 3.40282347e38f) X = copysignf(3.40282347e38f, vf);
+    return f2i_small(__fmul_rn(__fmul_rn(__fmaf_rn(-vf, q.scale, X), f1), f2));
+  };
+  rout[32 * blk + prmt_pos(n)] = static_cast<int8_t>(resid(q0));
+  rout[32 * blk + prmt_pos(n + 1)] = static_cast<int8_t>(resid(q1));
+  if (lane == 0) {
+    a.xs[g] = q.scale;
+    const unsigned sb = __float_as_uint(q.scale);
+    // {M, E << 20} (E shifted into a double's exponent field)
+    a.xme[g] = make_int2(static_cast<int>((sb >> 23 & 255u) ? (sb & 0x7fffffu) | 0x800000u : sb & 0x7fffffu),
+                         static_cast<int>((ef - 150u) << 20));
+  }
 }
 
 // ------------------------------------------------------------ 2. group
@@ -305,21 +368,30 @@ __global__ void __launch_bounds__(1024) prefill_group_kernel(PrefillArgs a) {
 
 // ---------------------------------------------------------- 3/4. MMA
 
-struct PfSmem;
+struct PfScales;
 template <unsigned MODE>
-__device__ __forceinline__ void pf_apply16(const PfSmem& s, unsigned ab, unsigned st, unsigned m, unsigned col,
+__device__ __forceinline__ void pf_apply16(const PfScales& sc, unsigned st, unsigned m, unsigned col,
                                            const uint32_t (&v)[16], float* acc, bool live, bool& bad);
+
+// One chunk's scales, in a ring of their own: the epilogue holds a chunk's
+// scales long after the MMAs have released its operand stage.
+struct PfScales {
+  union {
+    float col[8][kPfTile];  // down: per block of the chunk, per pair (hidden scale)
+    int2 me[4][kPfTile];    // gate/up: per x group of the chunk, per token {M, E << 20}
+  };
+  uint8_t row[8 * 128];     // E8M0 per A row and block (gate/up [row][8], down [block][128])
+};
 
 struct PfSmem {
   uint8_t raw[kPfRaw][kPfRawBytes];
   uint8_t A[kPfAB][kPfA];
   uint8_t B[kPfAB][kPfB];
-  float colscale[kPfAB][8][kPfTile];  // per block of the chunk, per token
-  uint8_t rowscale[kPfAB][8][128];    // per block of the chunk, per A row (E8M0)
+  PfScales sc[kPfSc];
   float amax[4][kPfTile];         // gate/up epilogue: per-warp amax per token
   unsigned tok[2][kPfTile];       // converters: token ids of the last two items requested
   uint64_t raw_full[kPfRaw], raw_empty[kPfRaw];
-  uint64_t ab_full[kPfAB], ab_empty[kPfAB], sc_empty[kPfAB];
+  uint64_t ab_full[kPfAB], ab_empty[kPfAB], sc_full[kPfSc], sc_empty[kPfSc];
   uint64_t acc_full[2], acc_empty[2];
   uint32_t taddr;
   unsigned abort;
@@ -349,12 +421,12 @@ __device__ __forceinline__ void fma2(float ax, float ay, float bx, float by, flo
 // block scale 2^(e-128) (E8M0 e; 255 is nonfinite).  float(I) is exact
 // (|I| < 2^22): the bits of I + 1.5 * 2^23 less that constant.
 template <unsigned MODE>
-__device__ __forceinline__ void pf_apply16(const PfSmem& s, unsigned ab, unsigned st, unsigned m, unsigned col,
+__device__ __forceinline__ void pf_apply16(const PfScales& sc, unsigned st, unsigned m, unsigned col,
                                            const uint32_t (&v)[16], float* acc, bool live, bool& bad) {
-  const unsigned e8 = MODE == kGateUp ? (&s.rowscale[ab][0][0])[8 * m + st] : s.rowscale[ab][st][m];
+  const unsigned e8 = sc.row[MODE == kGateUp ? 8 * m + st : 128 * st + m];
   bad |= live && e8 == 255;
   const float ws = pow2_m128(e8);
-  const float4* cs = reinterpret_cast<const float4*>(s.colscale[ab][st] + col);
+  const float4* cs = reinterpret_cast<const float4*>(sc.col[st] + col);
 #pragma unroll
   for (unsigned q4 = 0; q4 < 4; ++q4) {
     const float4 cv = cs[q4];
@@ -386,6 +458,105 @@ __device__ __forceinline__ void gu_row(unsigned m, unsigned pair, unsigned& blk,
   hrow = (l >> 4) * 32 + 16 * (w & 1) + (l & 15);
 }
 
+// One accumulator group's exact gate/up block terms for this thread's row m
+// and its warpgroup's live units q < nq (columns 8q .. 8q + 3 from tg, which
+// carries the warpgroup's offset 4 wg): steps g0 .. g0 + n - 1 of the chunk
+// (n even: the group size divides the chunk's eight steps), two steps (one x
+// group: one {M, E} per token) x two units at a time, eight 4-column TMEM
+// reads and one wait.  With the token's group scale s = M * 2^E and the
+// row's block scale 2^(e - 128), Z = M * I + R is an exact integer
+// (|Z| < 2^47) and the sum takes fma(Z, 2^(e - 128 + E), acc) in double,
+// blocks in order.
+__device__ __forceinline__ void gu_terms(double (&accd)[32], const PfScales& sc, uint32_t tg, unsigned bw,
+                                         unsigned npad, unsigned wg, unsigned m, unsigned g0, unsigned n, unsigned nq,
+                                         bool live, bool& bad) {
+  if (nq == 1) {
+    // one unit (tiles of up to 8 tokens; n is 8 or 4): four steps a read
+    for (unsigned j0 = 0; j0 < n; j0 += 4) {
+      const unsigned st = g0 + j0;  // a multiple of 4: x groups st / 2 and st / 2 + 1
+      uint32_t vi[16], vr[16];      // [step][4 columns]
+#pragma unroll
+      for (unsigned js = 0; js < 4; ++js) {
+        const uint32_t t = tg + (j0 + js) * bw;
+        tmem_ld4(t, vi + 4 * js);
+        tmem_ld4(t + npad, vr + 4 * js);
+      }
+      const unsigned e4 = *reinterpret_cast<const uint32_t*>(sc.row + 8 * m + st);
+      bad |= live && __vcmpeq4(e4, 0xffffffffu) != 0;
+      tmem_wait_ld();
+#pragma unroll
+      for (unsigned h = 0; h < 2; ++h) {
+        const int4* mev = reinterpret_cast<const int4*>(sc.me[(st >> 1) + h]) + 2 * wg;
+        const int4 xa = mev[0], xb = mev[1];
+        const int M[4] = {xa.x, xa.z, xb.x, xb.z}, Eh[4] = {xa.y, xa.w, xb.y, xb.w};
+        const int wb0 = static_cast<int>(((e4 >> (16 * h)) & 255u) + (1023 - 128)) << 20;
+        const int wb1 = static_cast<int>(((e4 >> (16 * h + 8)) & 255u) + (1023 - 128)) << 20;
+#pragma unroll
+        for (unsigned jj = 0; jj < 4; ++jj) {
+          const long long z0 = static_cast<long long>(M[jj]) * static_cast<int>(vi[8 * h + jj]) +
+                               (0x4338000000000000LL + static_cast<int>(vr[8 * h + jj]));
+          const long long z1 = static_cast<long long>(M[jj]) * static_cast<int>(vi[8 * h + 4 + jj]) +
+                               (0x4338000000000000LL + static_cast<int>(vr[8 * h + 4 + jj]));
+          double acc = accd[jj];
+          acc = fma(__longlong_as_double(z0) - 6755399441055744.0, __hiloint2double(wb0 + Eh[jj], 0), acc);
+          acc = fma(__longlong_as_double(z1) - 6755399441055744.0, __hiloint2double(wb1 + Eh[jj], 0), acc);
+          accd[jj] = acc;
+        }
+      }
+    }
+    return;
+  }
+  for (unsigned j0 = 0; j0 < n; j0 += 2) {
+    const unsigned st = g0 + j0;  // even
+    const unsigned e2 = *reinterpret_cast<const uint16_t*>(sc.row + 8 * m + st);
+    const unsigned e0 = e2 & 255u, e1 = e2 >> 8;
+    bad |= live && (e0 == 255 || e1 == 255);
+    // high words of 2^(e - 128 + E): (e - 128 + 1023) << 20 plus the token's
+    // E << 20 (stored shifted)
+    const int wb0 = static_cast<int>(e0 + (1023 - 128)) << 20, wb1 = static_cast<int>(e1 + (1023 - 128)) << 20;
+    const int4* mev = reinterpret_cast<const int4*>(sc.me[st >> 1]) + 2 * wg;  // unit q: mev[4q], mev[4q + 1]
+#pragma unroll
+    for (unsigned q0 = 0; q0 < 8; q0 += 2) {
+      if (q0 >= nq) break;  // warp-uniform
+      uint32_t vi[16], vr[16];  // [unit of the pair][step][4 columns]
+#pragma unroll
+      for (unsigned qb = 0; qb < 2; ++qb)
+        if (q0 + qb < nq) {
+          const uint32_t t = tg + j0 * bw + 8 * (q0 + qb);
+          tmem_ld4(t, vi + 8 * qb);                 // I: the v rows' results
+          tmem_ld4(t + bw, vi + 8 * qb + 4);
+          tmem_ld4(t + npad, vr + 8 * qb);          // R: the r rows' results
+          tmem_ld4(t + bw + npad, vr + 8 * qb + 4);
+        }
+      tmem_wait_ld();
+#pragma unroll
+      for (unsigned qb = 0; qb < 2; ++qb) {
+        const unsigned q = q0 + qb;
+        if (q >= nq) continue;
+        const int4 xa = mev[4 * q], xb = mev[4 * q + 1];  // {M, E << 20} of columns 0-1, 2-3
+        const int M[4] = {xa.x, xa.z, xb.x, xb.z}, Eh[4] = {xa.y, xa.w, xb.y, xb.w};
+#pragma unroll
+        for (unsigned jj = 0; jj < 4; ++jj) {
+          // Z + 1.5 * 2^52 as the bits of a double
+          const long long z0 = static_cast<long long>(M[jj]) * static_cast<int>(vi[8 * qb + jj]) +
+                               (0x4338000000000000LL + static_cast<int>(vr[8 * qb + jj]));
+          const long long z1 = static_cast<long long>(M[jj]) * static_cast<int>(vi[8 * qb + 4 + jj]) +
+                               (0x4338000000000000LL + static_cast<int>(vr[8 * qb + 4 + jj]));
+          double acc = accd[4 * q + jj];
+          acc = fma(__longlong_as_double(z0) - 6755399441055744.0, __hiloint2double(wb0 + Eh[jj], 0), acc);
+          acc = fma(__longlong_as_double(z1) - 6755399441055744.0, __hiloint2double(wb1 + Eh[jj], 0), acc);
+          accd[4 * q + jj] = acc;
+        }
+      }
+    }
+  }
+}
+
+// Register split (setmaxnreg): launched at 128 a thread (448 x 128 =
+// 57,344; each SM sub-partition holds four of the 14 warps at most, 16,384
+// registers), the converter warpgroup gives up 32 a thread (96) and the two
+// epilogue warpgroups take them (144); warps 12-13 keep 128:
+// 128 x 96 + 256 x 144 + 64 x 128 = 57,344.
 template <unsigned MODE>
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid_constant__ PrefillArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -398,22 +569,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
 
   if (tid == 0) {
     for (unsigned i = 0; i < kPfRaw; ++i) { mbar_init(&s.raw_full[i], 1); mbar_init(&s.raw_empty[i], 128); }
-    for (unsigned i = 0; i < kPfAB; ++i) {
-      mbar_init(&s.ab_full[i], 128); mbar_init(&s.ab_empty[i], 1); mbar_init(&s.sc_empty[i], 8);
-    }
+    for (unsigned i = 0; i < kPfAB; ++i) { mbar_init(&s.ab_full[i], 128); mbar_init(&s.ab_empty[i], 1); }
+    for (unsigned i = 0; i < kPfSc; ++i) { mbar_init(&s.sc_full[i], 128); mbar_init(&s.sc_empty[i], 8); }
     for (unsigned i = 0; i < 2; ++i) { mbar_init(&s.acc_full[i], 1); mbar_init(&s.acc_empty[i], 8); }
     s.abort = 0;
     fence_mbar_init();
   }
   if (warp == 13) {
-    tmem_alloc(&s.taddr, kPfAcc * kPfTile);
+    tmem_alloc(&s.taddr, kPfCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.taddr;
-  PF_STAMP(0, tid == 0);
+  PF_PH(const long long t_entry = pf_now(); PfClock clk;)
 
   if (warp == 12) {
     // ------------------------------------------------ producer: bulk copies
@@ -422,7 +592,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
       const uint4 item = items[it];
       for (unsigned k = 0; k < nk; ++k, ++c) {
         const unsigned st = c % kPfRaw;
+        PF_PH(clk.lap(1);)
         if (!pf_wait_warp(&s.raw_empty[st], ((c / kPfRaw) & 1) ^ 1, abort)) break;
+        PF_PH(clk.lap(0);)
         uint8_t* dst = s.raw[st];
         if (MODE == kGateUp) {
           // one 128 B x 64-row box per slice: bytes [nb + 128k, +128) of its
@@ -435,7 +607,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
                           static_cast<int>(item.x * a.slice_rows), &s.raw_full[st]);
           }
           __syncwarp();
-          PF_STAMP(50 + k, lane == 0 && it + gridDim.x >= nitems && k < 8);
         } else {
           const unsigned steps = pf_steps<MODE>(a, k);
           if (lane == 0) mbar_expect_tx(&s.raw_full[st], steps * 2048);
@@ -454,6 +625,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
       if (lane == 0) pf_wait(&s.raw_full[last % kPfRaw], (last / kPfRaw) & 1, abort);
     }
     __syncwarp();
+    PF_PH(clk.store(a.phases, 8, MODE == kGateUp && lane == 0);)
   } else if (warp == 13) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -461,37 +633,41 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
       for (unsigned it = blockIdx.x; it < nitems && !*abort; it += gridDim.x) {
         const uint4 item = items[it];
         const unsigned npad = (item.z + 15) & ~15u;
-        const uint32_t idesc = umma_idesc_i8(128, npad);
+        // gate/up: N = 2 npad (B rows [0, npad) v, [npad, 2 npad) r)
+        const uint32_t idesc = umma_idesc_i8(128, MODE == kGateUp ? 2 * npad : npad);
         for (unsigned k = 0; k < nk && !*abort; ++k, ++c) {
           const unsigned ab = c % kPfAB;
+          PF_PH(clk.lap(2);)
           if (!pf_wait(&s.ab_full[ab], (c / kPfAB) & 1, abort)) break;
-          PF_STAMP(25 + k, it + gridDim.x >= nitems && k < 8);
+          PF_PH(clk.lap(0);)
           tc_fence_after();
           const uint32_t a0 = smem_u32(s.A[ab]), b0 = smem_u32(s.B[ab]);
           const unsigned steps = pf_steps<MODE>(a, k);
-          for (unsigned g0 = 0; g0 < steps; g0 += 4, ++r) {  // groups of up to four steps
-            const unsigned grp = r & 1, n = min(4u, steps - g0);
+          const unsigned GS = pf_gs<MODE>(npad), BW = pf_bw<MODE>(npad);
+          for (unsigned g0 = 0; g0 < steps; g0 += GS, ++r) {  // groups of up to GS steps
+            const unsigned grp = r & 1, n = min(GS, steps - g0);
+            PF_PH(clk.lap(2);)
             if (!pf_wait(&s.acc_empty[grp], ((r >> 1) & 1) ^ 1, abort)) break;
-            PF_STAMP(62, it + gridDim.x >= nitems && k == 1 && g0 == 0);
+            PF_PH(clk.lap(1);)
             tc_fence_after();
             for (unsigned j = 0; j < n; ++j) {
               const unsigned st = g0 + j;
-              umma_i8(tmem + (4 * grp + j) * kPfTile, umma_desc(a0 + 256 * st, 128, 8 * 256),
+              umma_i8(tmem + 256 * grp + j * BW, umma_desc(a0 + 256 * st, 128, 8 * 256),
                       umma_desc(b0 + 256 * st, 128, 8 * 256), idesc, false);
             }
             umma_commit(&s.acc_full[grp]);
-            PF_STAMP(63, it + gridDim.x >= nitems && k == 1 && g0 == 0);
           }
           umma_commit(&s.ab_empty[ab]);
-          PF_STAMP(33 + k, it + gridDim.x >= nitems && k < 8);
         }
       }
       // the last commit's arrive must land before the CTA exits
       if (c) pf_wait(&s.ab_empty[(c - 1) % kPfAB], ((c - 1) / kPfAB) & 1, abort);
+      PF_PH(clk.store(a.phases, 12, MODE == kGateUp);)
     }
     __syncwarp();
   } else if (warp < 4) {
     // ------------------------------------------------ converters
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 96;" ::: "memory");
     // Software-pipelined: the B rows and scales of chunk c + 1 are requested
     // (cp.async) before chunk c's weights are converted, so the gather's L2
     // latency overlaps the conversion.  No abort test on the loops: all
@@ -504,23 +680,28 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
     auto issue = [&]() -> bool {
       if (iit >= nitems) return false;
       const uint4 item = inext;
-      const unsigned k = ik, ab = ic % kPfAB, steps = pf_steps<MODE>(a, k), tb = iitem & 1;
+      const unsigned k = ik, ab = ic % kPfAB, sq = ic % kPfSc, steps = pf_steps<MODE>(a, k), tb = iitem & 1;
+      PF_PH(clk.lap(4);)
       if (k == 0) {  // the item's token ids, read once (no dependent global loads per chunk)
         conv_sync();
         if (MODE == kGateUp && tid < item.z) s.tok[tb][tid] = a.pair_token[item.y + tid];
         conv_sync();
       }
+      PF_PH(clk.lap(3);)
       const bool ok = pf_wait(&s.ab_empty[ab], ((ic / kPfAB) & 1) ^ 1, abort) &&
-                      pf_wait(&s.sc_empty[ab], ((ic / kPfAB) & 1) ^ 1, abort);
+                      pf_wait(&s.sc_empty[sq], ((ic / kPfSc) & 1) ^ 1, abort);
+      PF_PH(clk.lap(2);)
       if (ok) {
-        // B rows: the tile's tokens (gate/up: x of the token; down: hq of the pair)
-        for (unsigned i = tid; i < item.z * 16; i += 128) {
-          const unsigned j = i >> 4, piece = i & 15;
+        // B rows: the tile's tokens (gate/up: x of token j in row j and its
+        // residuals in row npad + j; down: hq of the pair)
+        const unsigned npad = (item.z + 15) & ~15u;
+        for (unsigned i = tid; i < item.z * (MODE == kGateUp ? 32u : 16u); i += 128) {
+          const unsigned j = (i >> 4) % item.z, half = (i >> 4) / item.z, piece = i & 15;
           if (MODE == kDown && piece >= 2 * steps) continue;
           const int8_t* src = MODE == kGateUp
-                                  ? a.xq + static_cast<size_t>(s.tok[tb][j]) * d + 256 * k + 16 * piece
+                                  ? (half ? a.xr : a.xq) + static_cast<size_t>(s.tok[tb][j]) * d + 256 * k + 16 * piece
                                   : a.hq + (static_cast<size_t>(item.y + j) * a.S + 8 * k) * 32 + 16 * piece;
-          cp_async16(s.B[ab] + umma_off(j, 16 * piece, 256), src);
+          cp_async16(s.B[ab] + umma_off(j + half * npad, 16 * piece, 256), src);
         }
         // scales of the chunk's blocks
         if (MODE == kGateUp) {
@@ -528,25 +709,26 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
           gu_row(m, item.w, blk, hrow);
           if (blk < a.S) {
             const uint8_t* row = a.base[blk] + item.x * a.slice_bytes + static_cast<size_t>(hrow) * a.row_bytes;
-            cp_async8(&s.rowscale[ab][0][0] + 8 * m, row + 8 * k);  // gate/up: [row][8 blocks]
+            cp_async8(s.sc[sq].row + 8 * m, row + 8 * k);  // gate/up: [row][8 blocks]
           }
-          for (unsigned i = tid; i < item.z * 8; i += 128) {
-            const unsigned j = i >> 3, b = i & 7;  // block b of the chunk: x group b / 2
-            cp_async4(&s.colscale[ab][b][j], a.xs + static_cast<size_t>(s.tok[tb][j]) * (d / 64) + 4 * k + (b >> 1));
+          for (unsigned i = tid; i < item.z * 4; i += 128) {
+            const unsigned j = i >> 2, g = i & 3;  // x group g of the chunk (blocks 2g, 2g + 1)
+            cp_async8(&s.sc[sq].me[g][j], a.xme + static_cast<size_t>(s.tok[tb][j]) * (d / 64) + 4 * k + g);
           }
         } else {
           for (unsigned i = tid; i < steps * 8; i += 128) {
             const unsigned b = i >> 3, piece = i & 7;
             const uint8_t* down = a.base[8 * k + b] + item.x * a.slice_bytes + 64ull * a.row_bytes;
-            cp_async16(&s.rowscale[ab][b][0] + 16 * piece, down + item.w * 128 + 16 * piece);
+            cp_async16(s.sc[sq].row + 128 * b + 16 * piece, down + item.w * 128 + 16 * piece);
           }
           for (unsigned i = tid; i < item.z * steps; i += 128) {
             const unsigned j = i / steps, b = i % steps;
-            cp_async4(&s.colscale[ab][b][j], a.hs + static_cast<size_t>(item.y + j) * a.S + 8 * k + b);
+            cp_async4(&s.sc[sq].col[b][j], a.hs + static_cast<size_t>(item.y + j) * a.S + 8 * k + b);
           }
         }
       }
       cp_async_commit();  // one group per chunk, empty after a failed wait
+      PF_PH(clk.lap(3);)
       ++ic;
       if (++ik == nk) {
         ik = 0;
@@ -565,11 +747,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
       const bool row_live = MODE != kGateUp || blk < a.S;
       for (unsigned k = 0; k < nk; ++k, ++c) {
         const unsigned st = c % kPfRaw, ab = c % kPfAB, steps = pf_steps<MODE>(a, k);
-        PF_STAMP(1 + k, tid == 0 && it + gridDim.x >= nitems && k < 8);
         const bool more = issue();  // chunk c + 1
         // A: raw payload -> int8
         const bool landed = pf_wait(&s.raw_full[st], (c / kPfRaw) & 1, abort);
-        PF_STAMP(9 + k, tid == 0 && it + gridDim.x >= nitems && k < 8);
+        PF_PH(clk.lap(0);)
         uint8_t* A = s.A[ab];
         if (landed && MODE == kGateUp) {
           if (row_live) {
@@ -592,17 +773,23 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
           }
         }
         mbar_arrive(&s.raw_empty[st]);
+        PF_PH(clk.lap(1);)
         if (more) cp_async_wait_group1(); else cp_async_wait_all();  // chunk c's copies
         fence_proxy_async();
         mbar_arrive(&s.ab_full[ab]);
-        PF_STAMP(17 + k, tid == 0 && it + gridDim.x >= nitems && k < 8);
+        mbar_arrive(&s.sc_full[c % kPfSc]);
       }
     }
     cp_async_wait_all();  // no copy may land after the CTA exits
+    PF_PH(clk.lap(4); clk.store(a.phases, 0, MODE == kGateUp && tid == 0);)
   } else {
     // ------------------------------------------------ epilogue (warps 4-11)
-    // Two warpgroups: warps 4-7 take tile columns 0-31, warps 8-11 columns
-    // 32-63; warp w reads TMEM lanes 32 (w % 4) .. +31 (A rows).
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 144;" ::: "memory");
+    // Two warpgroups split the tile's token columns: down, warps 4-7 take
+    // columns 0-31 and warps 8-11 columns 32-63; gate/up, the columns go in
+    // units of four, alternately (warpgroup wg: units 2q + wg, columns
+    // 8q + 4wg .. +3, accumulators 4q .. 4q + 3), so that both work on the
+    // small tiles.  Warp w reads TMEM lanes 32 (w % 4) .. +31 (A rows).
     const unsigned wg = (warp - 4) >> 2, ew = warp & 3, m = 32 * ew + lane, col0 = 32 * wg;
     const uint32_t lane_base = tmem + ((32 * ew) << 16);
     unsigned c = 0, r = 0;
@@ -611,10 +798,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
     // same number of epi_sync barriers; after an abort every wait fails at once.
     for (unsigned it = blockIdx.x; it < nitems; it += gridDim.x) {
       const uint4 item = items[it];
-      const unsigned ntok = item.z;
+      const unsigned ntok = item.z, npad = (ntok + 15) & ~15u;
+      // gate/up: this warpgroup's live units q < nq (8q + 4wg < ntok)
+      const unsigned nq = ntok > 4 * wg ? (ntok - 4 * wg + 7) / 8 : 0u;
       float acc[32];
+      double accd[32];  // gate/up: the exact block terms' double sums
 #pragma unroll
-      for (unsigned j = 0; j < 32; ++j) acc[j] = 0.0f;
+      for (unsigned j = 0; j < 32; ++j) {
+        acc[j] = 0.0f;
+        accd[j] = 0.0;
+      }
       bool live = true;
       if (MODE == kGateUp) {
         unsigned blk, hrow;
@@ -622,55 +815,83 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         live = blk < a.S;
       }
       for (unsigned k = 0; k < nk; ++k, ++c) {
-        const unsigned ab = c % kPfAB, steps = pf_steps<MODE>(a, k);
-        // the converters' scales of this chunk (acquired directly: the stage
-        // cannot move on before this warp releases sc_empty below)
-        pf_wait_warp(&s.ab_full[ab], (c / kPfAB) & 1, abort);
-        for (unsigned g0 = 0; g0 < steps; g0 += 4, ++r) {
-          const unsigned grp = r & 1, n = min(4u, steps - g0);
-          if (!pf_wait_warp(&s.acc_full[grp], (r >> 1) & 1, abort)) continue;
-          PF_STAMP(58, tid == 128 && it + gridDim.x >= nitems && k == 1 && g0 == 0);
-          tc_fence_after();
-          const uint32_t tg = lane_base + 4 * grp * kPfTile + col0;
-          // one register buffer of four 16-column reads: with at most 16 live
-          // columns here the group's steps are read at once, with 32 two
-          // steps at a time
-          uint32_t v[4][16];
-          if (col0 + 16 < ntok) {  // 32 live columns: two steps at a time
-#pragma unroll
-            for (unsigned jb = 0; jb < 4; jb += 2) {
-              if (jb < n) {
-#pragma unroll
-                for (unsigned i = 0; i < 4; ++i)
-                  if (jb + (i >> 1) < n) tmem_ld16(tg + (jb + (i >> 1)) * kPfTile + 16 * (i & 1), v[i]);
-                tmem_wait_ld();
-#pragma unroll
-                for (unsigned i = 0; i < 4; ++i)
-                  if (jb + (i >> 1) < n)
-                    pf_apply16<MODE>(s, ab, g0 + jb + (i >> 1), m, col0 + 16 * (i & 1), v[i], acc + 16 * (i & 1), live,
-                                     bad);
-              }
-            }
-          } else if (col0 < ntok) {  // at most 16 live columns: the group's steps at once
-#pragma unroll
-            for (unsigned i = 0; i < 4; ++i)
-              if (i < n) tmem_ld16(tg + i * kPfTile, v[i]);
-            tmem_wait_ld();
-            PF_STAMP(60, tid == 128 && it + gridDim.x >= nitems && k == 1 && g0 == 0);
-#pragma unroll
-            for (unsigned i = 0; i < 4; ++i)
-              if (i < n) pf_apply16<MODE>(s, ab, g0 + i, m, col0, v[i], acc, live, bad);
+        const unsigned sq = c % kPfSc, steps = pf_steps<MODE>(a, k);
+        const PfScales& sc = s.sc[sq];
+        // the converters' scales of this chunk (the stage cannot move on
+        // before this warp releases sc_empty below)
+        PF_PH(clk.lap(2);)
+        pf_wait_warp(&s.sc_full[sq], (c / kPfSc) & 1, abort);
+        PF_PH(clk.lap(0);)
+        if (MODE == kGateUp) {
+          // exact block terms (the reference's sum of w * fl32(v * s)), gu_terms
+          const unsigned GS = pf_gs<MODE>(npad), BW = pf_bw<MODE>(npad);
+          for (unsigned g0 = 0; g0 < steps; g0 += GS, ++r) {
+            const unsigned grp = r & 1, n = min(GS, steps - g0);
+            PF_PH(clk.lap(2);)
+            if (!pf_wait_warp(&s.acc_full[grp], (r >> 1) & 1, abort)) continue;
+            PF_PH(clk.lap(1);)
+            tc_fence_after();
+            const uint32_t tg = lane_base + 256 * grp + 4 * wg;
+            if (nq) gu_terms(accd, sc, tg, BW, npad, wg, m, g0, n, nq, live, bad);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.acc_empty[grp]);
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&s.acc_empty[grp]);
-          PF_STAMP(59, tid == 128 && it + gridDim.x >= nitems && k == 1 && g0 == 0);
+        } else {
+          for (unsigned g0 = 0; g0 < steps; g0 += 4, ++r) {
+            const unsigned grp = r & 1, n = min(4u, steps - g0);
+            if (!pf_wait_warp(&s.acc_full[grp], (r >> 1) & 1, abort)) continue;
+            tc_fence_after();
+            const uint32_t tg = lane_base + 4 * grp * kPfTile + col0;
+            // one register buffer of four 16-column reads: with at most 16 live
+            // columns here the group's steps are read at once, with 32 two
+            // steps at a time
+            uint32_t v[4][16];
+            if (col0 + 16 < ntok) {  // 32 live columns: two steps at a time
+  #pragma unroll
+              for (unsigned jb = 0; jb < 4; jb += 2) {
+                if (jb < n) {
+  #pragma unroll
+                  for (unsigned i = 0; i < 4; ++i)
+                    if (jb + (i >> 1) < n) tmem_ld16(tg + (jb + (i >> 1)) * kPfTile + 16 * (i & 1), v[i]);
+                  tmem_wait_ld();
+  #pragma unroll
+                  for (unsigned i = 0; i < 4; ++i)
+                    if (jb + (i >> 1) < n)
+                      pf_apply16<MODE>(sc, g0 + jb + (i >> 1), m, col0 + 16 * (i & 1), v[i], acc + 16 * (i & 1), live,
+                                       bad);
+                }
+              }
+            } else if (col0 < ntok) {  // at most 16 live columns: the group's steps at once
+  #pragma unroll
+              for (unsigned i = 0; i < 4; ++i)
+                if (i < n) tmem_ld16(tg + i * kPfTile, v[i]);
+              tmem_wait_ld();
+  #pragma unroll
+              for (unsigned i = 0; i < 4; ++i)
+                if (i < n) pf_apply16<MODE>(sc, g0 + i, m, col0, v[i], acc, live, bad);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.acc_empty[grp]);
+          }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s.sc_empty[ab]);
-        PF_STAMP(41 + k, tid == 128 && it + gridDim.x >= nitems && k < 8);
+        if (lane == 0) mbar_arrive(&s.sc_empty[sq]);
       }
+      PF_PH(clk.lap(2);)
       const bool ok = !*abort;
+      if (MODE == kGateUp) {
+        // narrowed to fp32 as the reference narrows its double sums
+        // (backends/ref.c:37-40): a nonfinite or overflowing sum is NUMERIC
+#pragma unroll
+        for (unsigned j = 0; j < 32; ++j) {
+          if (j / 4 >= nq) continue;
+          const bool fits = fabs(accd[j]) <= 3.4028234663852886e38;
+          bad |= !fits && live && 8 * (j / 4) + 4 * wg + j % 4 < ntok;
+          acc[j] = __double2float_rn(fits ? accd[j] : 0.0);
+        }
+      }
       if (MODE == kDown) {
         if (!ok) continue;
         float* out = a.ye + (static_cast<size_t>(item.y) + col0) * d + 128 * item.w + m;
@@ -682,74 +903,70 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
               if (col0 + 16 * g + jj < ntok) out[static_cast<size_t>(16 * g + jj) * d] = acc[16 * g + jj];
           }
       } else {
-        // SwiGLU: lane l < 16 holds gate row n, lane l + 16 up row n; of this
-        // warpgroup's 32 tokens lane l takes the even ones col0 + 2i, lane
-        // l + 16 the odd ones col0 + 2i + 1.
+        // SwiGLU: lane l < 16 holds gate row n, lane l + 16 up row n.  Pair i
+        // (accumulators 2i, 2i + 1, unit i / 2) is two adjacent tokens: lane
+        // l takes the even one, lane l + 16 the odd one,
+        // token(i) = 8 (i / 2) + 4 wg + 2 (i % 2) + odd.
         const bool up = lane >= 16;
         const unsigned odd = up ? 1u : 0u;
+        auto token = [&](unsigned i) { return 8 * (i / 2) + 4 * wg + 2 * (i % 2) + odd; };
         float h[16];
 #pragma unroll
-        for (unsigned g = 0; g < 2; ++g) {
-          if (col0 + 16 * g < ntok) {  // tokens col0 + 16g .. +15: warp-uniform
-#pragma unroll
-            for (unsigned i = 8 * g; i < 8 * g + 8; ++i) {
-              const float other = __shfl_xor_sync(0xffffffffu, up ? acc[2 * i] : acc[2 * i + 1], 16);
-              const float gv = up ? other : acc[2 * i], uv = up ? acc[2 * i + 1] : other;
-              bool fail = false;
-              h[i] = swiglu_nb(gv, uv, fail);
-              bad |= fail && live && col0 + 2 * i + odd < ntok;
-            }
-          }
+        for (unsigned i = 0; i < 16; ++i) {
+          if (i / 2 >= nq) continue;  // warp-uniform
+          const float other = __shfl_xor_sync(0xffffffffu, up ? acc[2 * i] : acc[2 * i + 1], 16);
+          const float gv = up ? other : acc[2 * i], uv = up ? acc[2 * i + 1] : other;
+          bool fail = false;
+          h[i] = swiglu_nb(gv, uv, fail);
+          bad |= fail && live && token(i) < ntok;
         }
         // amax per token over the block's 32 neurons (16 here, 16 in the partner warp)
 #pragma unroll
-        for (unsigned g = 0; g < 2; ++g) {
-          if (col0 + 16 * g < ntok) {
+        for (unsigned i = 0; i < 16; ++i) {
+          if (i / 2 >= nq) continue;
+          float am = fabsf(h[i]);
 #pragma unroll
-            for (unsigned i = 8 * g; i < 8 * g + 8; ++i) {
-              float am = fabsf(h[i]);
-#pragma unroll
-              for (unsigned o = 8; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-              if ((lane & 15) == 0) s.amax[ew][col0 + 2 * i + odd] = am;
-            }
-          }
+          for (unsigned o = 8; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+          if ((lane & 15) == 0) s.amax[ew][token(i)] = am;
         }
         epi_sync(wg);
         const unsigned blk = 2 * item.w + (ew >> 1), n = 16 * (ew & 1) + (lane & 15);
         if (live && ok) {
           int8_t* hq = a.hq + static_cast<size_t>(item.y) * a.S * 32 + blk * 32 + prmt_pos(n);
 #pragma unroll
-          for (unsigned g = 0; g < 2; ++g) {
-            if (col0 + 16 * g < ntok) {
-              // the group's two divisions once per token: lane (lane & 16) + i'
-              // of each half computes them for its half's token i = 8g + i'
-              const unsigned tl = col0 + 2 * (8 * g + (lane & 7)) + odd;
-              const float am_l = fmaxf(s.amax[ew][tl], s.amax[ew ^ 1][tl]);
-              const float sc_l = __fdiv_rn(am_l, 127.0f);
-              const float inv_l = sc_l != 0.0f ? __fdiv_rn(127.0f, am_l) : 0.0f;
+          for (unsigned i0 = 0; i0 < 16; i0 += 8) {
+            if (i0 / 2 >= nq) continue;
+            // the group's two divisions once per token: lane (lane & 16) + i'
+            // of each half computes them for its half's pair i = i0 + i'
+            const unsigned tl = token(i0 + (lane & 7));
+            const float am_l = fmaxf(s.amax[ew][tl], s.amax[ew ^ 1][tl]);
+            const float sc_l = __fdiv_rn(am_l, 127.0f);
+            const float inv_l = sc_l != 0.0f ? __fdiv_rn(127.0f, am_l) : 0.0f;
 #pragma unroll
-              for (unsigned i = 8 * g; i < 8 * g + 8; ++i) {
-                const unsigned src = (lane & 16) | (i - 8 * g), t = col0 + 2 * i + odd;
-                const float am = __shfl_sync(0xffffffffu, am_l, src), sc = __shfl_sync(0xffffffffu, sc_l, src);
-                const float inv = __shfl_sync(0xffffffffu, inv_l, src);
-                if (t < ntok) {
-                  hq[static_cast<size_t>(t) * a.S * 32] = static_cast<int8_t>(q8_fast(h[i], am, sc, inv));
-                  if ((ew & 1) == 0 && (lane & 15) == 0) a.hs[static_cast<size_t>(item.y + t) * a.S + blk] = sc;
-                }
+            for (unsigned i = i0; i < i0 + 8; ++i) {
+              if (i / 2 >= nq) continue;
+              const unsigned src = (lane & 16) | (i - i0), t = token(i);
+              const float am = __shfl_sync(0xffffffffu, am_l, src), sc = __shfl_sync(0xffffffffu, sc_l, src);
+              const float inv = __shfl_sync(0xffffffffu, inv_l, src);
+              if (t < ntok) {
+                hq[static_cast<size_t>(t) * a.S * 32] = static_cast<int8_t>(q8_fast(h[i], am, sc, inv));
+                if ((ew & 1) == 0 && (lane & 15) == 0) a.hs[static_cast<size_t>(item.y + t) * a.S + blk] = sc;
               }
             }
           }
         }
         epi_sync(wg);
       }
-      PF_STAMP(49, tid == 128 && it + gridDim.x >= nitems);
+      PF_PH(clk.lap(3);)
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(a.status, kStNumeric);
+    PF_PH(clk.store(a.phases, 16 + 8 * wg, MODE == kGateUp && lane == 0 && ew == 0);)
   }
   if (tid == 0 && *abort) atomicOr(a.status, kStTimeout);
   tc_fence_before();
   __syncthreads();
-  if (warp == 13) tmem_dealloc(tmem, kPfAcc * kPfTile);
+  if (warp == 13) tmem_dealloc(tmem, kPfCols);
+  PF_PH(if (MODE == kGateUp && tid == 0 && a.phases) a.phases[blockIdx.x * 64 + 40] = pf_now() - t_entry;)
 }
 
 // ---------------------------------------------------------- 5. combine

@@ -380,6 +380,16 @@ static double scale_ulp(float s) {
     return ldexp(1.0, (ef ? ef : 1) - 150);
 }
 
+/* A group scale s as M * 2^E: M its 24-bit significand (no hidden bit for a
+ * subnormal), E the exponent of its last bit. */
+static void scale_parts(float s, int64_t *M, int *E) {
+    uint32_t bits;
+    memcpy(&bits, &s, sizeof bits);
+    const int ef = (int)((bits >> 23) & 255u);
+    *M = ef ? (int64_t)((bits & 0x7fffffu) | 0x800000u) : (int64_t)(bits & 0x7fffffu);
+    *E = (ef ? ef : 1) - 150;
+}
+
 /* The residuals r_j of one token (see qx), dequantizing exactly as
  * src/q4.c:54-58 does (the FLT_MAX cap included). */
 static void q8_residuals(const int8_t *v, const float *scale, unsigned d, int8_t *r) {
@@ -627,9 +637,13 @@ done:
  * arithmetic, or_port_run, in bursts of 16).  Each token's result depends only
  * on its own row:
  *   x: per-64 Q8 quantization (src/q4.c:37-61), as or_port_run;
- *   gate/up dot of neuron n: over the row's 32-weight blocks b in order,
- *     acc = fmaf((float)I_b * xscale[b / 2], wscale_b, acc), I_b the exact
- *     integer block dot (the tensor cores' int32 result);
+ *   gate/up dot of neuron n: the reference's sum of w_j * fl32(v_j * s)
+ *     exactly up to double rounding (the tensor cores give the int32 block
+ *     dots I_b against the int8 activations v and R_b against their
+ *     dequantization residuals r): over the row's 32-weight blocks b in
+ *     order, with the group scale s = M * 2^E and the block scale 2^(e-128)
+ *     of the doubled E2M1 table, Z = M * I_b + R_b (an exact integer) and
+ *     acc = fma((double)Z, 2^(e - 128 + E), acc), narrowed to fp32;
  *   h = SwiGLU in double (backends/ref.c:81-83), Q8 per 32 (hq, hscale);
  *   expert partial row r: over the loaded blocks s in ascending order,
  *     acc = fmaf((float)I_{s,r} * hscale_s, wscale_{s,r}, acc);
@@ -660,11 +674,12 @@ int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, c
     /* pairs, expert-major */
     unsigned *pair_t = malloc(sizeof(unsigned) * tokens * OR_TOPK), *pair_e = malloc(sizeof(unsigned) * tokens * OR_TOPK);
     unsigned *slot_pair = malloc(sizeof(unsigned) * tokens * OR_TOPK);
-    int8_t *q = malloc((size_t)tokens * d), *hv = malloc((size_t)tokens * OR_TOPK * S * OR_NEURONS);
+    int8_t *q = malloc((size_t)tokens * d), *res = malloc((size_t)tokens * d);
+    int8_t *hv = malloc((size_t)tokens * OR_TOPK * S * OR_NEURONS);
     float *xsc = malloc(sizeof(float) * tokens * (d / 64)), *hsc = malloc(sizeof(float) * tokens * OR_TOPK * S);
     float *part = malloc(sizeof(float) * (size_t)tokens * OR_TOPK * d), *out = malloc(sizeof(float) * (size_t)tokens * d);
     rc = OR_INVALID;
-    if (!pair_t || !pair_e || !slot_pair || !q || !hv || !xsc || !hsc || !part || !out) goto done;
+    if (!pair_t || !pair_e || !slot_pair || !q || !res || !hv || !xsc || !hsc || !part || !out) goto done;
     unsigned P = 0;
     for (unsigned e = 0; e < OR_ROUTED; ++e)
         for (unsigned t = 0; t < tokens; ++t)
@@ -677,6 +692,7 @@ int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, c
     for (unsigned t = 0; t < tokens; ++t) {
         rc = or_q8_quantize(x + (size_t)t * d, d, q + (size_t)t * d, xsc + (size_t)t * (d / 64));
         if (rc) goto done;
+        q8_residuals(q + (size_t)t * d, xsc + (size_t)t * (d / 64), d, res + (size_t)t * d);
     }
     /* Every referenced block scale must be finite, whatever the gate. */
     rc = OR_NUMERIC;
@@ -692,24 +708,30 @@ int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, c
         }
     for (unsigned p = 0; p < P; ++p) {
         const unsigned t = pair_t[p];
-        const int8_t *qt = q + (size_t)t * d;
+        const int8_t *qt = q + (size_t)t * d, *rt = res + (size_t)t * d;
         const float *xs = xsc + (size_t)t * (d / 64);
         for (unsigned si = 0; si < S; ++si) {
             const uint8_t *sl = m->layer[blocks[si]] + (size_t)pair_e[p] * slice;
             float h[OR_NEURONS];
             for (unsigned n = 0; n < OR_NEURONS; ++n) {
                 float gu[2];
+                double gd[2];
                 for (unsigned w = 0; w < 2; ++w) {
                     const uint8_t *row = sl + (w ? proj : 0) + n * in_row;
-                    float acc = 0, ws;
+                    double acc = 0;
                     for (unsigned b = 0; b < nb; ++b) {
-                        block_scale(row, OR_MXFP4, b, &ws);
-                        const float term = (float)idot_block(row, OR_MXFP4, b, qt + 32 * b) * xs[b / 2];
-                        acc = fmaf(term, ws, acc);
+                        const int e = row[(size_t)b * 17];
+                        const int32_t I = idot_block(row, OR_MXFP4, b, qt + 32 * b);
+                        const int32_t R = idot_block(row, OR_MXFP4, b, rt + 32 * b);
+                        int64_t M;
+                        int E;
+                        scale_parts(xs[b / 2], &M, &E);
+                        const int64_t Z = M * I + R;  /* exact: |Z| < 2^47 */
+                        acc = fma((double)Z, ldexp(1.0, e - 128 + E), acc);
                     }
-                    gu[w] = acc;
+                    gd[w] = acc;
                 }
-                if (!isfinite(gu[0]) || !isfinite(gu[1])) goto done;
+                if (narrow(gd[0], &gu[0]) || narrow(gd[1], &gu[1])) goto done;
                 const double a = gu[0];
                 const double sig = a >= 0 ? 1 / (1 + exp(-a)) : exp(a) / (1 + exp(a));
                 if (narrow(a * sig * gu[1], &h[n])) goto done;
@@ -742,7 +764,7 @@ int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, c
     memcpy(y, out, sizeof(float) * (size_t)tokens * d);
     rc = OR_OK;
 done:
-    free(pair_t); free(pair_e); free(slot_pair); free(q); free(hv); free(xsc); free(hsc); free(part); free(out);
+    free(pair_t); free(pair_e); free(slot_pair); free(q); free(res); free(hv); free(xsc); free(hsc); free(part); free(out);
     return rc;
 }
 

@@ -29,7 +29,8 @@ def _setup(ctx, oracle, blocks, e, hidden=2048):
 @pytest.mark.parametrize("tokens,blocks", [(17, [0]), (40, [0, 3, 7]), (100, [1, 2, 5, 6, 9, 19])])
 def test_prefill_bitexact_with_oracle(gpu, oracle, tokens, blocks):
     """y, the int8 hidden values and their scales, bit for bit (the kernel and
-    the oracle perform the same fp32 operations in the same order)."""
+    the oracle form the same exact block terms, sum them in double in the
+    same order and round once), and y within 1e-5 of the reference's ref-q8."""
     e, gt, x = request(2048, tokens, SEED + tokens)
     with fb.Context(0, 2048, gate_type=MXFP4, down_type=MXFP4) as ctx:
         m, layers = _setup(ctx, oracle, blocks, e)
@@ -42,6 +43,14 @@ def test_prefill_bitexact_with_oracle(gpu, oracle, tokens, blocks):
     assert np.array_equal(hs.view(np.uint32), hs_ref.view(np.uint32))
     assert max(rel_l2(y_ref[t], y[t]) for t in range(tokens)) <= 1e-5
     assert np.array_equal(y.view(np.uint32), y_ref.view(np.uint32))
+    # the reference's ref-q8 (bit-identical restatement, 16 tokens a call;
+    # a token's result depends only on its own row)
+    for t0 in range(0, tokens, 16):
+        sl = slice(t0, min(tokens, t0 + 16))
+        rc, y_q8 = oracle.ref_run(m, e[sl], gt[sl], x[sl], 1)
+        assert rc == OK
+        errs = [rel_l2(r, a) for r, a in zip(y_q8, y[sl])]
+        assert max(errs) <= 1e-5, ("vs ref-q8", errs)
 
 
 @pytest.mark.parametrize("hidden,tokens,distinct", [(2560, 20, True), (2048, 300, False)])
