@@ -799,8 +799,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
     for (unsigned it = blockIdx.x; it < nitems; it += gridDim.x) {
       const uint4 item = items[it];
       const unsigned ntok = item.z, npad = (ntok + 15) & ~15u;
-      // gate/up: this warpgroup's live units q < nq (8q + 4wg < ntok)
-      const unsigned nq = ntok > 4 * wg ? (ntok - 4 * wg + 7) / 8 : 0u;
+      // gate/up: the units of columns 8q + 4wq .. +3 go to this warpgroup,
+      // wq alternating with the CTA's items (one-unit tiles to both); its
+      // live units are q < nq (8q + 4wq < ntok)
+      const unsigned wq = wg ^ (((it - blockIdx.x) / gridDim.x) & 1u);
+      const unsigned nq = ntok > 4 * wq ? (ntok - 4 * wq + 7) / 8 : 0u;
       float acc[32];
       double accd[32];  // gate/up: the exact block terms' double sums
 #pragma unroll
@@ -831,8 +834,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
             if (!pf_wait_warp(&s.acc_full[grp], (r >> 1) & 1, abort)) continue;
             PF_PH(clk.lap(1);)
             tc_fence_after();
-            const uint32_t tg = lane_base + 256 * grp + 4 * wg;
-            if (nq) gu_terms(accd, sc, tg, BW, npad, wg, m, g0, n, nq, live, bad);
+            const uint32_t tg = lane_base + 256 * grp + 4 * wq;
+            if (nq) gu_terms(accd, sc, tg, BW, npad, wq, m, g0, n, nq, live, bad);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s.acc_empty[grp]);
@@ -888,7 +891,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         for (unsigned j = 0; j < 32; ++j) {
           if (j / 4 >= nq) continue;
           const bool fits = fabs(accd[j]) <= 3.4028234663852886e38;
-          bad |= !fits && live && 8 * (j / 4) + 4 * wg + j % 4 < ntok;
+          bad |= !fits && live && 8 * (j / 4) + 4 * wq + j % 4 < ntok;
           acc[j] = __double2float_rn(fits ? accd[j] : 0.0);
         }
       }
@@ -906,14 +909,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         // SwiGLU: lane l < 16 holds gate row n, lane l + 16 up row n.  Pair i
         // (accumulators 2i, 2i + 1, unit i / 2) is two adjacent tokens: lane
         // l takes the even one, lane l + 16 the odd one,
-        // token(i) = 8 (i / 2) + 4 wg + 2 (i % 2) + odd.
+        // token(i) = 8 (i / 2) + 4 wq + 2 (i % 2) + odd; pairs whose even
+        // token is past the tile are skipped (warp-uniform).
         const bool up = lane >= 16;
         const unsigned odd = up ? 1u : 0u;
-        auto token = [&](unsigned i) { return 8 * (i / 2) + 4 * wg + 2 * (i % 2) + odd; };
+        auto token = [&](unsigned i) { return 8 * (i / 2) + 4 * wq + 2 * (i % 2) + odd; };
+        auto live_pair = [&](unsigned i) { return i / 2 < nq && 8 * (i / 2) + 4 * wq + 2 * (i % 2) < ntok; };
         float h[16];
 #pragma unroll
         for (unsigned i = 0; i < 16; ++i) {
-          if (i / 2 >= nq) continue;  // warp-uniform
+          if (!live_pair(i)) continue;
           const float other = __shfl_xor_sync(0xffffffffu, up ? acc[2 * i] : acc[2 * i + 1], 16);
           const float gv = up ? other : acc[2 * i], uv = up ? acc[2 * i + 1] : other;
           bool fail = false;
@@ -923,7 +928,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         // amax per token over the block's 32 neurons (16 here, 16 in the partner warp)
 #pragma unroll
         for (unsigned i = 0; i < 16; ++i) {
-          if (i / 2 >= nq) continue;
+          if (!live_pair(i)) continue;
           float am = fabsf(h[i]);
 #pragma unroll
           for (unsigned o = 8; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
@@ -935,7 +940,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
           int8_t* hq = a.hq + static_cast<size_t>(item.y) * a.S * 32 + blk * 32 + prmt_pos(n);
 #pragma unroll
           for (unsigned i0 = 0; i0 < 16; i0 += 8) {
-            if (i0 / 2 >= nq) continue;
+            if (!live_pair(i0)) continue;
             // the group's two divisions once per token: lane (lane & 16) + i'
             // of each half computes them for its half's pair i = i0 + i'
             const unsigned tl = token(i0 + (lane & 7));
@@ -944,7 +949,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
             const float inv_l = sc_l != 0.0f ? __fdiv_rn(127.0f, am_l) : 0.0f;
 #pragma unroll
             for (unsigned i = i0; i < i0 + 8; ++i) {
-              if (i / 2 >= nq) continue;
+              if (!live_pair(i)) continue;
               const unsigned src = (lane & 16) | (i - i0), t = token(i);
               const float am = __shfl_sync(0xffffffffu, am_l, src), sc = __shfl_sync(0xffffffffu, sc_l, src);
               const float inv = __shfl_sync(0xffffffffu, inv_l, src);
