@@ -672,7 +672,10 @@ def prefill_config(n, unique=None):
                        "tcgen05 kind::i8 grouped GEMMs, partial sum by NCCL all-reduce at N>1",
            "hidden": HIDDEN, "layers": 1, "tokens_per_step": PF_TOKENS, "experts": 512, "top_k": TOPK,
            "zipf": PF_ZIPF, "slices": SLICES, "shares": equal_shares(n), "formats": "MXFP4 gate/up/down",
-           "activations": "Q8 per 64 (src/q4.c scheme), int8 tensor-core dots, fp32 scale application",
+           "activations": "bf16 x on the device (FRC_RUN_X_BF16, widened exactly to fp32; the host call frc_run "
+                          "takes the same values as fp32, as fr_backend.run does), Q8 per 64 (src/q4.c scheme), "
+                          "int8 tensor-core dots of the values and of their dequantization residuals, exact block "
+                          "terms summed in double",
            "routing_sets": PF_SETS,
            "parallelism": "slice-split x%d, NCCL all-reduce of the 512 x 2048 partial" % n if n > 1 else "1 GPU, all slices"}
     if unique is not None:
@@ -728,18 +731,23 @@ def run_prefill_bench(args, rank, world, local):
     ctx.pool_load(pool, fb.synth_shared(g, SEED, 1 << 20))
     for b in blocks:
         ctx.fill_layer(b, 0, SEED)
-    reqs = [fb.synth_request(HIDDEN, PF_TOKENS, fb.rand64(SEED, 7000 + i), zipf=PF_ZIPF) for i in range(PF_SETS)]
+    # configs[4]'s bf16 activations: x rounded to bf16 once (the fp32 copies
+    # hold the same values, for the host call and the parity check)
+    reqs = []
+    for i in range(PF_SETS):
+        e, gt, x = fb.synth_request(HIDDEN, PF_TOKENS, fb.rand64(SEED, 7000 + i), zipf=PF_ZIPF)
+        reqs.append((e, gt, torch.from_numpy(x).to(torch.bfloat16).float().numpy()))
     uniq = [len(np.unique(r[0])) for r in reqs]
     d_ex = torch.from_numpy(np.stack([r[0] for r in reqs]).astype(np.int16)).to(dev)
     d_gt = torch.from_numpy(np.stack([r[1] for r in reqs])).to(dev)
-    d_x = torch.from_numpy(np.stack([r[2] for r in reqs])).to(dev)
+    d_x = torch.from_numpy(np.stack([r[2] for r in reqs])).to(dev).to(torch.bfloat16)
     cur_ex = torch.empty_like(d_ex[0]); cur_gt = torch.empty_like(d_gt[0]); cur_x = torch.empty_like(d_x[0])
     Y = torch.zeros((PF_TOKENS, HIDDEN), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream()
 
     def launch():
         ctx.run_device(0, PF_TOKENS, cur_ex.data_ptr(), cur_gt.data_ptr(), cur_x.data_ptr(), None, None,
-                       Y.data_ptr(), fb.ACT_Q8, 0, torch.cuda.current_stream().cuda_stream)
+                       Y.data_ptr(), fb.ACT_Q8, fb.RUN_X_BF16, torch.cuda.current_stream().cuda_stream)
         if dist is not None:
             dist.all_reduce(Y)
 
@@ -808,7 +816,7 @@ def run_prefill_bench(args, rank, world, local):
     for s in range(2 * PF_SETS):
         load(s)
         ctx.run_device(0, PF_TOKENS, cur_ex.data_ptr(), cur_gt.data_ptr(), cur_x.data_ptr(), None, None,
-                       Y.data_ptr(), fb.ACT_Q8, 0, stream.cuda_stream)
+                       Y.data_ptr(), fb.ACT_Q8, fb.RUN_X_BF16, stream.cuda_stream)
         stage.append(ctx.prefill_times())
     ctx.prefill_timing(False)
     stage = np.mean(np.stack(stage[2:]), axis=0)
@@ -822,7 +830,7 @@ def run_prefill_bench(args, rank, world, local):
 
     # end to end: host buffers through frc_run (N=1) / device call + all-reduce with pinned copies (N>1)
     e2e_steps = max(3, min(args.steps, 20))
-    h2d = PF_TOKENS * (HIDDEN * 4 + TOPK * 2 + 11 * 4)
+    h2d = PF_TOKENS * (HIDDEN * (4 if dist is None else 2) + TOPK * 2 + 11 * 4)
     d2h = PF_TOKENS * HIDDEN * 4 + (16 if dist is None else 0)
     if dist is None:
         # the caller's output buffer is reused from call to call, as a serving
@@ -836,7 +844,7 @@ def run_prefill_bench(args, rank, world, local):
                 raise fb.FrcError(rc, "e2e prefill", ctx.last_error)
         dt = time.perf_counter() - t0
     else:
-        pin_x = torch.empty((PF_TOKENS, HIDDEN), dtype=torch.float32).pin_memory()
+        pin_x = torch.empty((PF_TOKENS, HIDDEN), dtype=torch.bfloat16).pin_memory()
         pin_e = torch.empty((PF_TOKENS, TOPK), dtype=torch.int16).pin_memory()
         pin_g = torch.empty((PF_TOKENS, 11), dtype=torch.float32).pin_memory()
         pin_y = torch.empty((PF_TOKENS, HIDDEN), dtype=torch.float32).pin_memory()
@@ -844,7 +852,7 @@ def run_prefill_bench(args, rank, world, local):
         t0 = time.perf_counter()
         for s in range(e2e_steps):
             e, gt, x = reqs[s % PF_SETS]
-            pin_x.numpy()[:] = x
+            pin_x.copy_(torch.from_numpy(x))  # bf16 words
             pin_e.numpy()[:] = e.astype(np.int16)
             pin_g.numpy()[:] = gt
             cur_x.copy_(pin_x, non_blocking=True)

@@ -21,6 +21,7 @@ ACT_F32, ACT_Q8 = 0, 1
 RUN_RMSNORM = 1
 RUN_OVERLAP = 2
 RUN_PEER = 4
+RUN_X_BF16 = 8
 PEER_HANDLE_BYTES = 64
 MAX_BLOCKS, ROUTED, SHARED, TOPK, ACTIVE, NEURONS, MAX_TOKENS = 20, 512, 512, 10, 11, 32, 16
 MAX_PREFILL_TOKENS = 512

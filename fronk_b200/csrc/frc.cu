@@ -606,6 +606,8 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
   if (!c || !expert || !gate || !x || !y) return fail(c, FRC_INVALID, "null argument");
   if (act != FRC_ACT_Q8 && act != FRC_ACT_F32) return fail(c, FRC_INVALID, "unknown activation mode");
   if (T > FRC_MAX_TOKENS) return run_long(c, layer, T, expert, gate, x, x_add, x_out, y, act, flags, s, scratch, chunks);
+  if (flags & FRC_RUN_X_BF16)
+    return fail(c, FRC_UNSUPPORTED, "bf16 x: only bursts of more than %u tokens", FRC_MAX_TOKENS);
   if (T < 1 || T > FRC_MAX_TOKENS || layer >= c->g.layers) return fail(c, FRC_INVALID, "tokens or layer out of range");
   if (act != FRC_ACT_Q8 && act != FRC_ACT_F32) return fail(c, FRC_INVALID, "unknown activation mode");
   LayerParams a{};
@@ -709,7 +711,7 @@ static int layer_tmap(frc_context* c, unsigned b, unsigned layer, CUtensorMap* o
 }
 
 static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_t* expert, const float* gate,
-                       const float* x, float* y, cudaStream_t s) {
+                       const float* x, float* y, cudaStream_t s, bool x_bf16) {
   PrefillArgs a{};
   unsigned S = 0;
   for (unsigned b = 0; b < FRC_MAX_BLOCKS; ++b) {
@@ -725,6 +727,7 @@ static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_
   const unsigned d = c->g.hidden;
   a.x = x; a.expert = expert; a.gate = gate; a.y = y;
   a.T = T; a.d = d; a.S = S;
+  a.x_bf16 = x_bf16 ? 1u : 0u;
   a.row_bytes = static_cast<unsigned>(c->row_bytes);
   a.slice_bytes = c->slice_bytes;
   a.slice_rows = static_cast<unsigned>(c->slice_bytes / c->row_bytes);
@@ -775,8 +778,10 @@ static int run_long(frc_context* c, unsigned layer, unsigned T, const uint16_t* 
                     const float* x, const float* x_add, float* x_out, float* y, int act, unsigned flags,
                     cudaStream_t s, const RunScratch* scratch, bool chunks) {
   if (T > FRC_MAX_PREFILL_TOKENS || layer >= c->g.layers) return fail(c, FRC_INVALID, "tokens or layer out of range");
-  if (!chunks && act == FRC_ACT_Q8 && !flags && !scratch && c->pf_ye)
-    return run_prefill(c, layer, T, expert, gate, x, y, s);
+  if (!chunks && act == FRC_ACT_Q8 && (flags & ~unsigned(FRC_RUN_X_BF16)) == 0 && !scratch && c->pf_ye)
+    return run_prefill(c, layer, T, expert, gate, x, y, s, (flags & FRC_RUN_X_BF16) != 0);
+  if (flags & FRC_RUN_X_BF16)
+    return fail(c, FRC_UNSUPPORTED, "bf16 x: only bursts on the tensor-core path (MXFP4, Q8, no shared expert, no other flag)");
   const size_t d = c->g.hidden;
   for (unsigned t0 = 0; t0 < T; t0 += FRC_MAX_TOKENS) {
     const unsigned n = T - t0 < FRC_MAX_TOKENS ? T - t0 : FRC_MAX_TOKENS;

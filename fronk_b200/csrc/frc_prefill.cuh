@@ -69,11 +69,12 @@ constexpr unsigned kPfThreads = 448;     // 14 warps
 enum : unsigned { kGateUp = 0, kDown = 1 };
 
 struct PrefillArgs {
-  const float* x;          // [T][d]
+  const float* x;          // [T][d] fp32, or bf16 words when x_bf16
   const uint16_t* expert;  // [T][10]
   const float* gate;       // [T][11]
   float* y;                // [T][d]
   unsigned T, d, S;        // tokens, hidden size, loaded blocks
+  unsigned x_bf16;         // x holds bf16 values (widened exactly)
   unsigned row_bytes;      // MXFP4 gate/up row: d/32 scales + d/2 payload
   unsigned long long slice_bytes;
   unsigned slice_rows;     // slice_bytes / row_bytes
@@ -224,7 +225,13 @@ __global__ void prefill_quantize_kernel(PrefillArgs a) {
   const unsigned g = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
   const unsigned groups = a.T * (a.d / 64);
   if (g >= groups) return;
-  const float2 v = reinterpret_cast<const float2*>(a.x + 64 * static_cast<size_t>(g))[lane];
+  float2 v;
+  if (a.x_bf16) {  // two bf16 words: the upper halves of two fp32 patterns
+    const uint32_t w = reinterpret_cast<const uint32_t*>(a.x)[32 * static_cast<size_t>(g) + lane];
+    v = make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  } else {
+    v = reinterpret_cast<const float2*>(a.x + 64 * static_cast<size_t>(g))[lane];
+  }
   const bool bad = !isfinite(v.x) || !isfinite(v.y);
   if (__any_sync(0xffffffffu, bad)) {
     if (lane == 0) atomicOr(a.status, kStNumeric);

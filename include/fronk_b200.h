@@ -188,6 +188,11 @@ int frc_run(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *exp
             const float *gate, const float *x, float *y, int act);
 
 /* Flags of frc_run_device.
+ * FRC_RUN_X_BF16: x holds bf16 values ([tokens][d] 16-bit words, the upper
+ * half of an fp32 bit pattern), widened exactly to fp32 on the device; the
+ * tensor-core burst path only (more than 16 tokens, Q8, MXFP4 gate/up and
+ * down, no other flag, no shared-expert gate); any other call with it is
+ * FRC_UNSUPPORTED.
  * FRC_RUN_OVERLAP: the launch may start while the kernel before it on the
  * stream is finishing (programmatic dependent launch): it plans and starts
  * streaming this layer's weights at once and waits for that kernel only
@@ -198,7 +203,7 @@ int frc_run(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *exp
  * (frc_peer_attach) of each rank's partial, added in rank order: identical
  * on every rank.  Every rank must make the same sequence of FRC_RUN_PEER
  * calls (same token counts), one process per GPU. */
-enum { FRC_RUN_RMSNORM = 1, FRC_RUN_OVERLAP = 2, FRC_RUN_PEER = 4 };
+enum { FRC_RUN_RMSNORM = 1, FRC_RUN_OVERLAP = 2, FRC_RUN_PEER = 4, FRC_RUN_X_BF16 = 8 };
 
 /* Asynchronous run on device memory, enqueued on `stream` (a cudaStream_t, or
  * NULL for the legacy default stream); nothing is validated on the host and

@@ -130,3 +130,43 @@ def test_prefill_failures_leave_output_untouched(gpu, oracle):
         e2[7, 3] = e2[7, 4]  # the same expert twice in one token
         rc, y = ctx.run(0, e2, gt, x, out=sentinel.copy())
         assert rc == INVALID and np.array_equal(y, sentinel)
+
+
+def test_prefill_bf16_x_is_the_fp32_path_on_the_same_values(gpu, oracle):
+    """configs[4]'s bf16 activations (FRC_RUN_X_BF16): the burst is widened
+    exactly to fp32 on the device, so y equals the fp32 call on the widened
+    values bit for bit (and the oracle); other calls with the flag are
+    UNSUPPORTED and leave y alone."""
+    import torch
+    T = 64
+    e, gt, x = request(2048, T, SEED + 640)
+    xb = torch.from_numpy(x).to(torch.bfloat16)
+    x_up = xb.float().numpy()
+    dev = torch.device("cuda", 0)
+    s = torch.cuda.current_stream().cuda_stream
+    with fb.Context(0, 2048, gate_type=MXFP4, down_type=MXFP4) as ctx:
+        m, layers = _setup(ctx, oracle, [0, 3, 11], e)
+        rc, y32 = ctx.run(0, e, gt, x_up)
+        assert rc == OK, ctx.last_error
+        de = torch.from_numpy(e.astype(np.int16)).to(dev)
+        dg = torch.from_numpy(gt).to(dev)
+        dxb = xb.to(dev)
+        dy = torch.zeros((T, 2048), device=dev)
+        ctx.run_device(0, T, de.data_ptr(), dg.data_ptr(), dxb.data_ptr(), None, None, dy.data_ptr(), fb.ACT_Q8,
+                       fb.RUN_X_BF16, s)
+        torch.cuda.synchronize()
+        assert ctx.status(s) == OK
+        y16 = dy.cpu().numpy()
+        assert np.array_equal(y16.view(np.uint32), y32.view(np.uint32))
+        # a decode-sized call, and a burst with another flag: refused, y untouched
+        sentinel = torch.full((T, 2048), 7.0, device=dev)
+        for tokens, flags in ((8, fb.RUN_X_BF16), (T, fb.RUN_X_BF16 | fb.RUN_RMSNORM)):
+            with pytest.raises(fb.FrcError) as err:
+                ctx.run_device(0, tokens, de.data_ptr(), dg.data_ptr(), dxb.data_ptr(), None, None,
+                               sentinel.data_ptr(), fb.ACT_Q8, flags, s)
+            assert err.value.code == fb.UNSUPPORTED
+        torch.cuda.synchronize()
+        assert bool((sentinel == 7.0).all())
+    rc, y_ref, _, _ = oracle.prefill_run(m, e, gt, x_up)
+    assert rc == OK
+    assert np.array_equal(y16.view(np.uint32), y_ref.view(np.uint32))
