@@ -234,6 +234,7 @@ struct frc_context {
   int8_t* pf_hq = nullptr;
   float* pf_hs = nullptr;
   float* pf_ye = nullptr;
+  int2* pf_xvr = nullptr;  // Q4_K gate/up: per token and 32-block {sum v, sum r}
   bool pf_attr = false;
   unsigned last_pf_S = 0;
   // tensor maps of the loaded layer regions (valid while tmap_of matches layer_ptr)
@@ -696,13 +697,25 @@ static int layer_tmap(frc_context* c, unsigned b, unsigned layer, CUtensorMap* o
         g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
       }
     }
-    const cuuint64_t dims[2] = {c->row_bytes, c->layer_bytes / c->row_bytes};
-    const cuuint64_t strides[1] = {c->row_bytes};
-    const cuuint32_t box[2] = {128, 64}, estr[2] = {1, 1};
-    const CUresult r = g_encode_tiled(&c->tmap[b][layer], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base),
-                                      dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r;
+    if (c->g.gate_type == FRC_Q4_K) {
+      // Q4_K gate/up rows (the reference layout: a slice is not a whole
+      // number of rows): bytes of a row x the slice's 64 gate/up rows x the
+      // 512 routed slices; a 144 B x 64-row box is one super-block of them
+      const cuuint64_t dims[3] = {c->row_bytes, 64, FRC_ROUTED_EXPERTS};
+      const cuuint64_t strides[2] = {c->row_bytes, c->slice_bytes};
+      const cuuint32_t box[3] = {144, 64, 1}, estr[3] = {1, 1, 1};
+      r = g_encode_tiled(&c->tmap[b][layer], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+      const cuuint64_t dims[2] = {c->row_bytes, c->layer_bytes / c->row_bytes};
+      const cuuint64_t strides[1] = {c->row_bytes};
+      const cuuint32_t box[2] = {128, 64}, estr[2] = {1, 1};
+      r = g_encode_tiled(&c->tmap[b][layer], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
     if (r != CUDA_SUCCESS) return fail(c, FRC_IO, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
     c->tmap_of[b][layer] = base;
   }
@@ -728,6 +741,8 @@ static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_
   a.x = x; a.expert = expert; a.gate = gate; a.y = y;
   a.T = T; a.d = d; a.S = S;
   a.x_bf16 = x_bf16 ? 1u : 0u;
+  a.q4k = c->g.gate_type == FRC_Q4_K ? 1u : 0u;
+  a.xvr = a.q4k ? c->pf_xvr : nullptr;
   a.row_bytes = static_cast<unsigned>(c->row_bytes);
   a.slice_bytes = c->slice_bytes;
   a.slice_rows = static_cast<unsigned>(c->slice_bytes / c->row_bytes);
@@ -739,12 +754,14 @@ static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_
   c->last_G = 4 * c->sms;  // frc_debug_phases: [cta][64] stamps
   const unsigned smem = sizeof(PfSmem);
   if (!c->pf_attr) {
-    CK(cudaFuncSetAttribute(prefill_mma_kernel<kGateUp>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    CK(cudaFuncSetAttribute(prefill_mma_kernel<kDown>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(prefill_mma_kernel<kGateUp, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(prefill_mma_kernel<kGateUp, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(prefill_mma_kernel<kDown, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     // The kernels' setmaxnreg split is sized for 128 registers a thread at
     // launch: with fewer, the epilogue's increase could never be granted.
-    for (const void* k : {reinterpret_cast<const void*>(prefill_mma_kernel<kGateUp>),
-                          reinterpret_cast<const void*>(prefill_mma_kernel<kDown>)}) {
+    for (const void* k : {reinterpret_cast<const void*>(prefill_mma_kernel<kGateUp, false>),
+                          reinterpret_cast<const void*>(prefill_mma_kernel<kGateUp, true>),
+                          reinterpret_cast<const void*>(prefill_mma_kernel<kDown, false>)}) {
       cudaFuncAttributes fa;
       CK(cudaFuncGetAttributes(&fa, k));
       if (fa.numRegs != 128)
@@ -761,9 +778,10 @@ static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_
   mark(1);
   prefill_group_kernel<<<1, 1024, 0, s>>>(a);
   mark(2);
-  prefill_mma_kernel<kGateUp><<<c->sms, kPfThreads, smem, s>>>(a);
+  if (a.q4k) prefill_mma_kernel<kGateUp, true><<<c->sms, kPfThreads, smem, s>>>(a);
+  else prefill_mma_kernel<kGateUp, false><<<c->sms, kPfThreads, smem, s>>>(a);
   mark(3);
-  prefill_mma_kernel<kDown><<<c->sms, kPfThreads, smem, s>>>(a);
+  prefill_mma_kernel<kDown, false><<<c->sms, kPfThreads, smem, s>>>(a);
   mark(4);
   prefill_combine_kernel<<<dim3((d / 4 + 255) / 256, T), 256, 0, s>>>(a);
   mark(5);
@@ -935,8 +953,13 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
   alloc(reinterpret_cast<void**>(&c->phases), sizeof(unsigned long long) * 16 * 1024);
   const size_t in_bytes = kInBytesPerToken(d) * FRC_MAX_PREFILL_TOKENS,
                out_bytes = 16 + sizeof(float) * FRC_MAX_PREFILL_TOKENS * d;
-  if (g->gate_type == FRC_MXFP4 && g->down_type == FRC_MXFP4 && c->slice_bytes % c->row_bytes == 0 &&
-      c->layer_bytes % c->row_bytes == 0) {
+  // the tensor-core burst path: MXFP4 gate/up (a 2D map of whole rows over
+  // the layer region) or Q4_K gate/up (a 3D map: byte, row, slice), MXFP4
+  // down rows
+  const bool pf_mx = g->gate_type == FRC_MXFP4 && c->slice_bytes % c->row_bytes == 0 &&
+                     c->layer_bytes % c->row_bytes == 0;
+  const bool pf_q4 = g->gate_type == FRC_Q4_K && d % 256 == 0 && c->slice_bytes % 16 == 0;
+  if (g->down_type == FRC_MXFP4 && (pf_mx || pf_q4)) {
     const size_t T = FRC_MAX_PREFILL_TOKENS;
     alloc(reinterpret_cast<void**>(&c->pf_xq), T * d);
     alloc(reinterpret_cast<void**>(&c->pf_xr), T * d);
@@ -950,6 +973,7 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
     alloc(reinterpret_cast<void**>(&c->pf_hq), kPfMaxPairs * FRC_MAX_BLOCKS * 32);
     alloc(reinterpret_cast<void**>(&c->pf_hs), sizeof(float) * kPfMaxPairs * FRC_MAX_BLOCKS);
     alloc(reinterpret_cast<void**>(&c->pf_ye), sizeof(float) * kPfMaxPairs * d);
+    if (pf_q4) alloc(reinterpret_cast<void**>(&c->pf_xvr), sizeof(int2) * T * (d / 32));
   }
   alloc(reinterpret_cast<void**>(&c->d_in), in_bytes);
   alloc(reinterpret_cast<void**>(&c->d_out), out_bytes);
@@ -991,6 +1015,7 @@ int frc_close(frc_context* c) {
   cudaFree(c->d_in); cudaFree(c->d_out); cudaFree(c->pool);
   cudaFree(c->pf_xq); cudaFree(c->pf_xr); cudaFree(c->pf_xs); cudaFree(c->pf_xme); cudaFree(c->pf_pair_token); cudaFree(c->pf_slot_pair); cudaFree(c->pf_counts);
   cudaFree(c->pf_items_gu); cudaFree(c->pf_items_dn); cudaFree(c->pf_hq); cudaFree(c->pf_hs); cudaFree(c->pf_ye);
+  cudaFree(c->pf_xvr);
   cudaFreeHost(c->h_in); cudaFreeHost(c->h_out);
   if (c->stream) cudaStreamDestroy(c->stream);
   for (auto e : c->pf_ev) if (e) cudaEventDestroy(e);

@@ -48,7 +48,11 @@ constexpr unsigned kPfTile = 64;        // tokens per item
 constexpr unsigned kPfRaw = 3;          // raw payload stages
 constexpr unsigned kPfAB = 2;           // A/B operand stages (released by the MMA's commit)
 constexpr unsigned kPfSc = 4;           // scale stages (released by the epilogue)
-constexpr unsigned kPfRawBytes = 16384; // 128 rows x 128 B (gate/up) or 8 blocks x 128 rows x 16 B (down)
+// raw stage: gate/up MXFP4 128 rows x 128 B (two 128-byte swizzled boxes),
+// gate/up Q4_K 128 rows x 144 B (one super-block a row, two unswizzled
+// boxes), down 8 blocks x 128 rows x 16 B
+constexpr unsigned kPfRawBytes = 18432;
+constexpr unsigned kPfQ4Box = 64 * 144;  // one slice's Q4_K box
 constexpr unsigned kPfA = 128 * 256;    // A stage: 128 rows x K 256
 // B stage: 128 rows x K 256.  Gate/up: rows [0, npad) the tile's tokens'
 // int8 activations v, rows [npad, 2 npad) their dequantization residuals r
@@ -75,6 +79,7 @@ struct PrefillArgs {
   float* y;                // [T][d]
   unsigned T, d, S;        // tokens, hidden size, loaded blocks
   unsigned x_bf16;         // x holds bf16 values (widened exactly)
+  unsigned q4k;            // gate/up rows are Q4_K (the reference's unit layout), else MXFP4
   unsigned row_bytes;      // MXFP4 gate/up row: d/32 scales + d/2 payload
   unsigned long long slice_bytes;
   unsigned slice_rows;     // slice_bytes / row_bytes
@@ -87,6 +92,7 @@ struct PrefillArgs {
   int8_t* xr;              // [T][d], the residuals of the dequantized values, same order
   float* xs;               // [T][d/64]
   int2* xme;               // [T][d/64] {M, E << 20}: xs = M * 2^E
+  int2* xvr;               // [T][d/32] {V, RS}: the block's sums of v and of r (Q4_K mins)
   uint16_t* pair_token;    // [P]
   unsigned* slot_pair;     // [T][10]
   unsigned* counts;        // [0] pairs, [1] gate/up items, [2] down items
@@ -163,6 +169,13 @@ __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
 // Named barrier of one epilogue warpgroup (ids 1 and 2).
 __device__ __forceinline__ void epi_sync(unsigned wg) { asm volatile("bar.sync %0, 128;" ::"r"(wg + 1) : "memory"); }
 // Tiled 2D TMA load (no multicast): box at byte column x, row y of the map.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -217,6 +230,47 @@ __device__ __forceinline__ void mxfp4_to_i8(uint4 q, uint4& lo, uint4& hi) {
   hi = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
+// One Q4_K super-block of an A row (144 bytes: fp16 d, fp16 dmin, 12 bytes
+// of 6-bit scales and mins, 128 bytes of nibbles; src/native.c:14-19) ->
+// 256 int8 q in the B rows' prmt order per 32-block, its eight scales and
+// mins, and {d, dmin}.  Sub-block 2g is the low nibbles of bytes 32g..32g+31,
+// 2g+1 their high nibbles (element i of a sub-block in byte i).
+__device__ __forceinline__ void q4k_row_to_i8(const uint8_t* rowp, uint8_t* A, unsigned m, uint8_t* sm, float2& dd) {
+  const uint4 hdr = *reinterpret_cast<const uint4*>(rowp);
+  dd = make_float2(h2f(hdr.x & 0xffffu), h2f(hdr.x >> 16));
+  const uint32_t sw[3] = {hdr.y, hdr.z, hdr.w};  // scale bytes s[0..11]
+  auto sb = [&](unsigned i) { return (sw[i >> 2] >> (8 * (i & 3))) & 255u; };
+  uint32_t scv[2] = {0, 0}, miv[2] = {0, 0};
+#pragma unroll
+  for (unsigned g = 0; g < 8; ++g) {
+    const unsigned sc = g < 4 ? sb(g) & 63 : (sb(g + 4) & 15) | ((sb(g - 4) >> 6) << 4);
+    const unsigned mi = g < 4 ? sb(g + 4) & 63 : (sb(g + 4) >> 4) | ((sb(g) >> 6) << 4);
+    scv[g >> 2] |= sc << (8 * (g & 3));
+    miv[g >> 2] |= mi << (8 * (g & 3));
+  }
+  *reinterpret_cast<uint4*>(sm) = make_uint4(scv[0], scv[1], miv[0], miv[1]);
+#pragma unroll
+  for (unsigned gp = 0; gp < 4; ++gp) {
+    const uint4 w0 = *reinterpret_cast<const uint4*>(rowp + 16 + 32 * gp);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(rowp + 32 + 32 * gp);
+    const uint32_t W[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    uint32_t lo[8], hi[8];
+#pragma unroll
+    for (unsigned k = 0; k < 4; ++k) {
+      // elements (j, j+16, j+1, j+17) and (j+2, j+18, j+3, j+19), j = 4k
+      const uint32_t o0 = prmt(W[k], W[k + 4], 0x5140u), o1 = prmt(W[k], W[k + 4], 0x7362u);
+      lo[2 * k] = o0 & 0x0f0f0f0fu;
+      lo[2 * k + 1] = o1 & 0x0f0f0f0fu;
+      hi[2 * k] = (o0 >> 4) & 0x0f0f0f0fu;
+      hi[2 * k + 1] = (o1 >> 4) & 0x0f0f0f0fu;
+    }
+    *reinterpret_cast<uint4*>(A + umma_off(m, 64 * gp, 256)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(A + umma_off(m, 64 * gp + 16, 256)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+    *reinterpret_cast<uint4*>(A + umma_off(m, 64 * gp + 32, 256)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(A + umma_off(m, 64 * gp + 48, 256)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+  }
+}
+
 // --------------------------------------------------------- 1. quantize
 
 // One warp per 64-group, two values per lane; the operations of
@@ -258,8 +312,18 @@ __global__ void prefill_quantize_kernel(PrefillArgs a) {
     if (fabsf(X) > 3.40282347e38f) X = copysignf(3.40282347e38f, vf);
     return f2i_small(__fmul_rn(__fmul_rn(__fmaf_rn(-vf, q.scale, X), f1), f2));
   };
-  rout[32 * blk + prmt_pos(n)] = static_cast<int8_t>(resid(q0));
-  rout[32 * blk + prmt_pos(n + 1)] = static_cast<int8_t>(resid(q1));
+  const int r0 = resid(q0), r1 = resid(q1);
+  rout[32 * blk + prmt_pos(n)] = static_cast<int8_t>(r0);
+  rout[32 * blk + prmt_pos(n + 1)] = static_cast<int8_t>(r1);
+  if (a.xvr) {  // Q4_K rows: each 32-block's sums of v and of r (lanes 0-15, 16-31)
+    int sv = q0 + q1, sr = r0 + r1;
+#pragma unroll
+    for (unsigned o = 8; o; o >>= 1) {
+      sv += __shfl_xor_sync(0xffffffffu, sv, o);
+      sr += __shfl_xor_sync(0xffffffffu, sr, o);
+    }
+    if ((lane & 15) == 0) a.xvr[2 * static_cast<size_t>(g) + blk] = make_int2(sv, sr);
+  }
   if (lane == 0) {
     a.xs[g] = q.scale;
     const unsigned sb = __float_as_uint(q.scale);
@@ -387,7 +451,14 @@ struct PfScales {
     float col[8][kPfTile];  // down: per block of the chunk, per pair (hidden scale)
     int2 me[4][kPfTile];    // gate/up: per x group of the chunk, per token {M, E << 20}
   };
-  uint8_t row[8 * 128];     // E8M0 per A row and block (gate/up [row][8], down [block][128])
+  int2 vr[8][kPfTile];      // gate/up Q4_K: per block of the chunk, per token {V, RS}
+  union {
+    uint8_t row[8 * 128];   // E8M0 per A row and block (gate/up MXFP4 [row][8], down [block][128])
+    struct {
+      uint8_t sm[128][16];  // gate/up Q4_K: per A row, the super-block's 6-bit scales then mins
+      float2 dd[128];       // gate/up Q4_K: per A row {d, dmin}
+    } q4;
+  };
 };
 
 struct PfSmem {
@@ -559,12 +630,72 @@ __device__ __forceinline__ void gu_terms(double (&accd)[32], const PfScales& sc,
   }
 }
 
+// The Q4_K form of gu_terms: one accumulator group's steps (n even) in x
+// groups of two blocks (st, st + 1), two units at a time.  With the row's
+// sub-block scales sc and mins mi, the tokens' block sums V, RS of v and r,
+// K1 = sc0 I0 + sc1 I1, K3 = sc0 R0 + sc1 R1, K2 = mi0 V0 + mi1 V1,
+// K4 = mi0 RS0 + mi1 RS1, the group's term of the reference's sum of
+// w * fl32(v * s) is (M K1 + K3) d 2^E - (M K2 + K4) dmin 2^E: two exact
+// integers (|M K1 + K3| < 2^47) times exact doubles, added in that order.
+__device__ __forceinline__ void gu_terms_q4k(double (&accd)[32], const PfScales& sc, uint32_t tg, unsigned bw,
+                                             unsigned npad, unsigned wg, unsigned m, unsigned g0, unsigned n,
+                                             unsigned nq, const float2 dd) {
+  const double dmul = dd.x, mmul = -static_cast<double>(dd.y);
+  for (unsigned j0 = 0; j0 < n; j0 += 2) {
+    const unsigned st = g0 + j0;  // even
+    const unsigned scp = *reinterpret_cast<const uint16_t*>(&sc.q4.sm[m][st]);
+    const unsigned mip = *reinterpret_cast<const uint16_t*>(&sc.q4.sm[m][8 + st]);
+    const int sc0 = scp & 255u, sc1 = scp >> 8, mi0 = mip & 255u, mi1 = mip >> 8;
+    const int4* mev = reinterpret_cast<const int4*>(sc.me[st >> 1]) + 2 * wg;  // unit q: mev[4q], mev[4q + 1]
+    const int2* vr0 = sc.vr[st] + 4 * wg;
+    const int2* vr1 = sc.vr[st + 1] + 4 * wg;
+#pragma unroll
+    for (unsigned q0 = 0; q0 < 8; q0 += 2) {
+      if (q0 >= nq) break;  // warp-uniform
+      uint32_t vi[16], vr[16];  // [unit of the pair][step][4 columns]
+#pragma unroll
+      for (unsigned qb = 0; qb < 2; ++qb)
+        if (q0 + qb < nq) {
+          const uint32_t t = tg + j0 * bw + 8 * (q0 + qb);
+          tmem_ld4(t, vi + 8 * qb);
+          tmem_ld4(t + bw, vi + 8 * qb + 4);
+          tmem_ld4(t + npad, vr + 8 * qb);
+          tmem_ld4(t + bw + npad, vr + 8 * qb + 4);
+        }
+      tmem_wait_ld();
+#pragma unroll
+      for (unsigned qb = 0; qb < 2; ++qb) {
+        const unsigned q = q0 + qb;
+        if (q >= nq) continue;
+        const int4 xa = mev[4 * q], xb = mev[4 * q + 1];  // {M, E << 20} of columns 0-1, 2-3
+        const int M[4] = {xa.x, xa.z, xb.x, xb.z}, Eh[4] = {xa.y, xa.w, xb.y, xb.w};
+#pragma unroll
+        for (unsigned jj = 0; jj < 4; ++jj) {
+          const int2 s0 = vr0[8 * q + jj], s1 = vr1[8 * q + jj];
+          const int K1 = sc0 * static_cast<int>(vi[8 * qb + jj]) + sc1 * static_cast<int>(vi[8 * qb + 4 + jj]);
+          const int K3 = sc0 * static_cast<int>(vr[8 * qb + jj]) + sc1 * static_cast<int>(vr[8 * qb + 4 + jj]);
+          const int K2 = mi0 * s0.x + mi1 * s1.x, K4 = mi0 * s0.y + mi1 * s1.y;
+          // Z + 1.5 * 2^52 as the bits of a double
+          const long long z1 = static_cast<long long>(M[jj]) * K1 + (0x4338000000000000LL + K3);
+          const long long z2 = static_cast<long long>(M[jj]) * K2 + (0x4338000000000000LL + K4);
+          const double P = __hiloint2double(Eh[jj] + (1023 << 20), 0);  // 2^E
+          double acc = accd[4 * q + jj];
+          acc = fma(__longlong_as_double(z1) - 6755399441055744.0, dmul * P, acc);
+          acc = fma(__longlong_as_double(z2) - 6755399441055744.0, mmul * P, acc);
+          accd[4 * q + jj] = acc;
+        }
+      }
+    }
+  }
+}
+
 // Register split (setmaxnreg): launched at 128 a thread (448 x 128 =
 // 57,344; each SM sub-partition holds four of the 14 warps at most, 16,384
 // registers), the converter warpgroup gives up 32 a thread (96) and the two
 // epilogue warpgroups take them (144); warps 12-13 keep 128:
 // 128 x 96 + 256 x 144 + 64 x 128 = 57,344.
-template <unsigned MODE>
+// Q4 (gate/up only): Q4_K gate/up rows, else MXFP4.
+template <unsigned MODE, bool Q4>
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid_constant__ PrefillArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   PfSmem& s = *reinterpret_cast<PfSmem*>(smem_raw);
@@ -603,7 +734,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         if (!pf_wait_warp(&s.raw_empty[st], ((c / kPfRaw) & 1) ^ 1, abort)) break;
         PF_PH(clk.lap(0);)
         uint8_t* dst = s.raw[st];
-        if (MODE == kGateUp) {
+        if (MODE == kGateUp && Q4) {
+          // one 144 B x 64-row box per slice: super-block k of its 32 gate and
+          // 32 up rows (3D map: byte, row of the slice, slice), unswizzled
+          const unsigned nsl = 2 * item.w + 1 < a.S ? 2 : 1;
+          if (lane == 0) {
+            mbar_expect_tx(&s.raw_full[st], nsl * kPfQ4Box);
+            for (unsigned sl = 0; sl < nsl; ++sl)
+              tma_load_3d(dst + kPfQ4Box * sl, &a.tmap[2 * item.w + sl], static_cast<int>(144 * k), 0,
+                          static_cast<int>(item.x), &s.raw_full[st]);
+          }
+          __syncwarp();
+        } else if (MODE == kGateUp) {
           // one 128 B x 64-row box per slice: bytes [nb + 128k, +128) of its
           // 32 gate and 32 up rows, stored 128-byte swizzled
           const unsigned nsl = 2 * item.w + 1 < a.S ? 2 : 1;
@@ -714,7 +856,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         if (MODE == kGateUp) {
           unsigned blk, hrow;
           gu_row(m, item.w, blk, hrow);
-          if (blk < a.S) {
+          if (!Q4 && blk < a.S) {  // (Q4_K row scales come with the payload)
             const uint8_t* row = a.base[blk] + item.x * a.slice_bytes + static_cast<size_t>(hrow) * a.row_bytes;
             cp_async8(s.sc[sq].row + 8 * m, row + 8 * k);  // gate/up: [row][8 blocks]
           }
@@ -722,6 +864,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
             const unsigned j = i >> 2, g = i & 3;  // x group g of the chunk (blocks 2g, 2g + 1)
             cp_async8(&s.sc[sq].me[g][j], a.xme + static_cast<size_t>(s.tok[tb][j]) * (d / 64) + 4 * k + g);
           }
+          if (Q4)
+            for (unsigned i = tid; i < item.z * 8; i += 128) {
+              const unsigned j = i >> 3, b = i & 7;  // block b of the chunk
+              cp_async8(&s.sc[sq].vr[b][j], a.xvr + static_cast<size_t>(s.tok[tb][j]) * (d / 32) + 8 * k + b);
+            }
         } else {
           for (unsigned i = tid; i < steps * 8; i += 128) {
             const unsigned b = i >> 3, piece = i & 7;
@@ -759,7 +906,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         const bool landed = pf_wait(&s.raw_full[st], (c / kPfRaw) & 1, abort);
         PF_PH(clk.lap(0);)
         uint8_t* A = s.A[ab];
-        if (landed && MODE == kGateUp) {
+        if (landed && MODE == kGateUp && Q4) {
+          if (row_live) {
+            PfScales& scw = s.sc[c % kPfSc];
+            q4k_row_to_i8(s.raw[st] + 144 * (64 * (m >> 6) + hrow), A, m, scw.q4.sm[m], scw.q4.dd[m]);
+          }
+        } else if (landed && MODE == kGateUp) {
           if (row_live) {
             const unsigned R = 64 * (m >> 6) + hrow;  // row of the staged boxes
 #pragma unroll
@@ -835,6 +987,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         if (MODE == kGateUp) {
           // exact block terms (the reference's sum of w * fl32(v * s)), gu_terms
           const unsigned GS = pf_gs<MODE>(npad), BW = pf_bw<MODE>(npad);
+          float2 dd = make_float2(0.0f, 0.0f);
+          if (Q4) {  // the super-block's d and dmin of this row: finite, or NUMERIC
+            dd = sc.q4.dd[m];
+            bad |= live && !(isfinite(dd.x) && isfinite(dd.y));
+          }
           for (unsigned g0 = 0; g0 < steps; g0 += GS, ++r) {
             const unsigned grp = r & 1, n = min(GS, steps - g0);
             PF_PH(clk.lap(2);)
@@ -842,7 +999,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
             PF_PH(clk.lap(1);)
             tc_fence_after();
             const uint32_t tg = lane_base + 256 * grp + 4 * wq;
-            if (nq) gu_terms(accd, sc, tg, BW, npad, wq, m, g0, n, nq, live, bad);
+            if (Q4 && nq) gu_terms_q4k(accd, sc, tg, BW, npad, wq, m, g0, n, nq, dd);
+            if (!Q4 && nq) gu_terms(accd, sc, tg, BW, npad, wq, m, g0, n, nq, live, bad);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s.acc_empty[grp]);

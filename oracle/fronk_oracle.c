@@ -657,8 +657,10 @@ static int validate_n(unsigned hidden, unsigned tokens, unsigned max_tokens, con
 
 int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, const float *gate,
                    const float *x, float *y, int8_t *hq, float *hs, size_t pair_cap, size_t *pairs) {
-    if (!model_ok(m) || m->legacy || !y || m->gate_type != OR_MXFP4) return OR_INVALID;
-    const unsigned d = m->hidden;
+    if (!model_ok(m) || m->legacy || !y || (m->gate_type != OR_MXFP4 && m->gate_type != OR_Q4_K) ||
+        m->down_type == OR_Q4_K)
+        return OR_INVALID;
+    const unsigned d = m->hidden, gt = m->gate_type;
     if (d % 512 || d > 8192) return OR_INVALID;
     int rc = validate_n(d, tokens, OR_MAX_PREFILL, expert, gate, x);
     if (rc) return rc;
@@ -668,7 +670,7 @@ int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, c
     unsigned blocks[OR_BLOCKS], S = 0;
     for (unsigned b = 0; b < OR_BLOCKS; ++b) if (m->layer[b]) blocks[S++] = b;
     const unsigned dt = m->down_type, nb = d / 32;
-    const size_t slice = or_slice_bytes(d, m->gate_type, dt), in_row = or_row_bytes(OR_MXFP4, d);
+    const size_t slice = or_slice_bytes(d, gt, dt), in_row = or_row_bytes(gt, d);
     const size_t proj = OR_NEURONS * in_row, down_row = or_row_bytes(dt, OR_NEURONS);
 
     /* pairs, expert-major */
@@ -701,8 +703,13 @@ int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, c
             const uint8_t *sl = m->layer[blocks[si]] + (size_t)pair_e[p] * slice;
             float sc;
             for (unsigned n = 0; n < 2 * OR_NEURONS; ++n)
-                for (unsigned b = 0; b < nb; ++b)
-                    if (!block_scale(sl + n * in_row, OR_MXFP4, b, &sc)) goto done;
+                for (unsigned b = 0; b < nb; ++b) {
+                    if (gt == OR_MXFP4 && !block_scale(sl + n * in_row, OR_MXFP4, b, &sc)) goto done;
+                    if (gt == OR_Q4_K && b % 8 == 0) {  /* d and dmin of each super-block */
+                        const uint8_t *sb = sl + n * in_row + (size_t)(b / 8) * 144;
+                        if (!isfinite(or_f16(le16(sb))) || !isfinite(or_f16(le16(sb + 2)))) goto done;
+                    }
+                }
             for (unsigned r = 0; r < d; ++r)
                 if (!block_scale(sl + 2 * proj + r * down_row, dt, 0, &sc)) goto done;
         }
@@ -719,7 +726,47 @@ int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, c
                 for (unsigned w = 0; w < 2; ++w) {
                     const uint8_t *row = sl + (w ? proj : 0) + n * in_row;
                     double acc = 0;
-                    for (unsigned b = 0; b < nb; ++b) {
+                    if (gt == OR_Q4_K) {
+                        /* Q4_K rows, one 256-weight super-block a chunk, its four
+                         * 64-weight x groups in order: with K1 = sc0*I0 + sc1*I1,
+                         * K3 = sc0*R0 + sc1*R1 (dots against v and r),
+                         * K2 = mi0*V0 + mi1*V1, K4 = mi0*RS0 + mi1*RS1 (the blocks'
+                         * sums of v and r) and s = M * 2^E, the group's term of the
+                         * reference's sum of w * fl32(v * s) (src/native.c:14-30,
+                         * backends/ref.c:74-79) is (M*K1 + K3) * d * 2^E -
+                         * (M*K2 + K4) * dmin * 2^E, both products exact. */
+                        for (unsigned k = 0; k < d / 256; ++k) {
+                            const uint8_t *sb = row + (size_t)k * 144;
+                            const double dd = or_f16(le16(sb)), dm = or_f16(le16(sb + 2));
+                            for (unsigned gp = 0; gp < 4; ++gp) {
+                                const unsigned g = 4 * k + gp;
+                                const int8_t *v = qt + 64 * g, *r = rt + 64 * g;
+                                unsigned sc0, mi0, sc1, mi1;
+                                q4k_scale_min(sb + 4, 2 * gp, &sc0, &mi0);
+                                q4k_scale_min(sb + 4, 2 * gp + 1, &sc1, &mi1);
+                                int32_t i0 = 0, i1 = 0, r0 = 0, r1 = 0, v0 = 0, v1 = 0, s0 = 0, s1 = 0;
+                                for (unsigned j = 0; j < 32; ++j) {
+                                    const uint8_t byte = sb[16 + 32 * gp + j];
+                                    i0 += (int32_t)(byte & 15) * v[j];
+                                    i1 += (int32_t)(byte >> 4) * v[32 + j];
+                                    r0 += (int32_t)(byte & 15) * r[j];
+                                    r1 += (int32_t)(byte >> 4) * r[32 + j];
+                                    v0 += v[j]; v1 += v[32 + j];
+                                    s0 += r[j]; s1 += r[32 + j];
+                                }
+                                const int64_t K1 = (int64_t)sc0 * i0 + (int64_t)sc1 * i1;
+                                const int64_t K3 = (int64_t)sc0 * r0 + (int64_t)sc1 * r1;
+                                const int64_t K2 = (int64_t)mi0 * v0 + (int64_t)mi1 * v1;
+                                const int64_t K4 = (int64_t)mi0 * s0 + (int64_t)mi1 * s1;
+                                int64_t M;
+                                int E;
+                                scale_parts(xs[g], &M, &E);
+                                const double P = ldexp(1.0, E);
+                                acc = fma((double)(M * K1 + K3), dd * P, acc);
+                                acc = fma((double)(M * K2 + K4), -dm * P, acc);
+                            }
+                        }
+                    } else for (unsigned b = 0; b < nb; ++b) {
                         const int e = row[(size_t)b * 17];
                         const int32_t I = idot_block(row, OR_MXFP4, b, qt + 32 * b);
                         const int32_t R = idot_block(row, OR_MXFP4, b, rt + 32 * b);

@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 
 import fronk_b200 as fb
-from oracle import Oracle, MXFP4, OK, INVALID, NUMERIC
+from oracle import Oracle, MXFP4, Q4_K, OK, INVALID, NUMERIC
 from tests.helpers import make_layers, request, rel_l2
 
 pytestmark = pytest.mark.gpu
@@ -18,12 +18,12 @@ def oracle():
     return Oracle()
 
 
-def _setup(ctx, oracle, blocks, e, hidden=2048):
-    g = fb.geometry(hidden, gate_type=MXFP4, down_type=MXFP4)
+def _setup(ctx, oracle, blocks, e, hidden=2048, gate=MXFP4):
+    g = fb.geometry(hidden, gate_type=gate, down_type=MXFP4)
     layers = make_layers(g, SEED, blocks, e, shared=True)
     for b, arr in layers.items():
         assert ctx.load_layer(b, 0, arr) == OK, ctx.last_error
-    return oracle.model(hidden, MXFP4, MXFP4, layers), layers
+    return oracle.model(hidden, gate, MXFP4, layers), layers
 
 
 @pytest.mark.parametrize("tokens,blocks", [(17, [0]), (40, [0, 3, 7]), (100, [1, 2, 5, 6, 9, 19])])
@@ -170,3 +170,43 @@ def test_prefill_bf16_x_is_the_fp32_path_on_the_same_values(gpu, oracle):
     rc, y_ref, _, _ = oracle.prefill_run(m, e, gt, x_up)
     assert rc == OK
     assert np.array_equal(y16.view(np.uint32), y_ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("hidden,tokens,blocks", [(2048, 17, [0]), (2048, 100, [1, 2, 5, 6, 9, 19]),
+                                                  (2560, 40, [0, 3, 7])])
+def test_prefill_q4k_gate_up_bitexact(gpu, oracle, hidden, tokens, blocks):
+    """The reference's own unit layout (Q4_K gate/up, MXFP4 down) on the
+    tensor-core path: Q4_K super-blocks staged by 3D tensor maps, nibbles as
+    int8 operands, the exact per-group terms in double; hq, hscale and y bit
+    for bit against the oracle, y within 1e-5 of ref-q8."""
+    e, gt, x = request(hidden, tokens, SEED + 3 * tokens + hidden)
+    with fb.Context(0, hidden, gate_type=Q4_K, down_type=MXFP4) as ctx:
+        m, layers = _setup(ctx, oracle, blocks, e, hidden, gate=Q4_K)
+        rc, y = ctx.run(0, e, gt, x)
+        assert rc == OK, ctx.last_error
+        hq, hs = ctx.debug_prefill_hidden()
+    rc, y_ref, hq_ref, hs_ref = oracle.prefill_run(m, e, gt, x, want_hidden=True)
+    assert rc == OK
+    assert np.array_equal(hq, hq_ref)
+    assert np.array_equal(hs.view(np.uint32), hs_ref.view(np.uint32))
+    assert np.array_equal(y.view(np.uint32), y_ref.view(np.uint32))
+    for t0 in range(0, tokens, 16):
+        sl = slice(t0, min(tokens, t0 + 16))
+        rc, y_q8 = oracle.ref_run(m, e[sl], gt[sl], x[sl], 1)
+        assert rc == OK
+        assert max(rel_l2(r, a) for r, a in zip(y_q8, y[sl])) <= 1e-5
+
+
+def test_prefill_q4k_nonfinite_scale_is_numeric(gpu, oracle):
+    """An infinite d in one super-block of a referenced Q4_K up row: NUMERIC,
+    y untouched."""
+    e, gt, x = request(2048, 24, SEED + 24)
+    g = fb.geometry(2048, gate_type=Q4_K, down_type=MXFP4)
+    bad = make_layers(g, SEED, [3], e, shared=True)[3]
+    off = int(e[5, 2]) * fb.slice_bytes(g) + (32 + 8) * fb.row_bytes(Q4_K, 2048) + 3 * 144
+    bad[off:off + 2] = [0x00, 0x7c]
+    sentinel = np.full(x.shape, 7.0, np.float32)
+    with fb.Context(0, 2048, gate_type=Q4_K, down_type=MXFP4) as ctx:
+        assert ctx.load_layer(3, 0, bad) == OK
+        rc, y = ctx.run(0, e, gt, x, out=sentinel.copy())
+        assert rc == NUMERIC and np.array_equal(y, sentinel)

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 
 import fronk_b200 as fb
-from oracle import Oracle, MXFP4, Q8_0, OK, INVALID, NUMERIC
+from oracle import Oracle, MXFP4, Q8_0, Q4_K, OK, INVALID, NUMERIC
 from tests.helpers import make_layers, request, BACKEND_TOL, conforms
 
 SEED = 0x5EED
@@ -16,10 +16,10 @@ def oracle():
     return Oracle()
 
 
-def _model(oracle, down, blocks, e, hidden=2048):
-    g = fb.geometry(hidden, gate_type=MXFP4, down_type=down)
+def _model(oracle, down, blocks, e, hidden=2048, gate=MXFP4):
+    g = fb.geometry(hidden, gate_type=gate, down_type=down)
     layers = make_layers(g, SEED, blocks, e, shared=False)
-    return oracle.model(hidden, MXFP4, down, layers), layers, g
+    return oracle.model(hidden, gate, down, layers), layers, g
 
 
 @pytest.mark.parametrize("down", [MXFP4, Q8_0])
@@ -66,3 +66,38 @@ def test_prefill_rejects_shared_expert_and_bad_scales(oracle):
     # E8M0 exponent 255 in the first block of gate row 0 of a referenced slice
     layers[4][int(e[0, 0]) * fb.slice_bytes(g)] = 255
     assert oracle.prefill_run(m, e, gt, x)[0] == NUMERIC
+
+
+@pytest.mark.parametrize("hidden", [2048, 2560])
+def test_prefill_q4k_gate_up_matches_ref_q8(oracle, hidden):
+    """The reference's own unit layout (Q4_K gate/up, MXFP4 down): the exact
+    per-group terms (M*K1 + K3) * d * 2^E - (M*K2 + K4) * dmin * 2^E give
+    y within 1e-5 of ref-q8 per token, and within the conformance limits of
+    ref."""
+    e, gt, x = request(hidden, 16, SEED + 9 + hidden)
+    m, layers, _ = _model(oracle, MXFP4, [0, 4, 9], e, hidden, gate=Q4_K)
+    rc, y, _, _ = oracle.prefill_run(m, e, gt, x)
+    assert rc == OK
+    rc, y_ref = oracle.ref_run(m, e, gt, x, 0)
+    assert rc == OK
+    rc, y_q8 = oracle.ref_run(m, e, gt, x, 1)
+    assert rc == OK
+    for t in range(16):
+        assert conforms(oracle.compare(y_ref[t], y[t])[1], BACKEND_TOL)
+        rel = oracle.compare(y_q8[t], y[t])[1][0]
+        assert rel <= 1e-5, (t, rel)
+
+
+def test_prefill_q4k_nonfinite_super_block_scale_is_numeric(oracle):
+    """A nonfinite d of any super-block of a referenced Q4_K row is NUMERIC,
+    whatever the gate (the reference's rule for every referenced scale)."""
+    e, gt, x = request(2048, 20, SEED + 12)
+    g = fb.geometry(2048, gate_type=Q4_K, down_type=MXFP4)
+    layers = make_layers(g, SEED, [2], e, shared=False)
+    bad = layers[2].copy()
+    # fp16 d = inf (0x7c00) of super-block 3 of up row 5 of a referenced slice
+    off = int(e[4, 1]) * fb.slice_bytes(g) + (32 + 5) * fb.row_bytes(Q4_K, 2048) + 3 * 144
+    bad[off:off + 2] = [0x00, 0x7c]
+    m = oracle.model(2048, Q4_K, MXFP4, {2: bad})
+    rc, _, _, _ = oracle.prefill_run(m, e, gt, x)
+    assert rc == NUMERIC
