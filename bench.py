@@ -273,11 +273,15 @@ def main():
     ap.add_argument("--formats", default="q4k-mxfp4", choices=sorted(FORMATS),
                     help="routed block formats: q4k-mxfp4 (the reference layout, configs[2]/[3]) or mxfp4-q80 "
                          "(configs[1]: MXFP4 gate/up, Q8_0 down)")
+    ap.add_argument("--prefill-gate", default="mxfp4", choices=["mxfp4", "q4k"],
+                    help="gate/up rows of the --prefill workload: MXFP4 (configs[4]) or Q4_K (the reference's "
+                         "unit layout)")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu: 2 layers of every slice loaded (2.2 GB), 5 layer launches "
                          "(with --prefill: one layer, three 512-token calls)")
     args = ap.parse_args()
     set_formats(args.formats)
+    set_prefill_gate(args.prefill_gate)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -660,9 +664,23 @@ def profile_case():
 
 PF_TOKENS, PF_ZIPF, PF_SETS = 512, 1.1, 8
 PF_METRIC = "MoE prefill tokens/s (one layer, 512 tokens) at 1/2/4/8 B200; expert-weight GB/s vs HBM peak"
+PF_GATE = "mxfp4"                                # --prefill-gate: configs[4]'s MXFP4, or q4k (the reference units)
 PF_GU_BYTES = 2 * 32 * (HIDDEN * 17 // 32)       # 69,632: MXFP4 gate + up rows of one slice
 PF_DN_BYTES = HIDDEN * 17                        # 34,816: MXFP4 down rows of one slice
 PF_SLICE_BYTES = PF_GU_BYTES + PF_DN_BYTES       # 104,448
+
+
+def set_prefill_gate(name):
+    """Q4_K gate/up rows (144-byte super-blocks: 73,728 B of gate/up rows a
+    slice, 108,544 B a slice) or MXFP4 ones."""
+    global PF_GATE, PF_GU_BYTES, PF_SLICE_BYTES
+    PF_GATE = name
+    PF_GU_BYTES = 2 * 32 * (HIDDEN // 256 * 144 if name == "q4k" else HIDDEN * 17 // 32)
+    PF_SLICE_BYTES = PF_GU_BYTES + PF_DN_BYTES
+
+
+def pf_gate_type(fb):
+    return fb.Q4_K if PF_GATE == "q4k" else fb.MXFP4
 
 
 def prefill_config(n, unique=None):
@@ -671,7 +689,9 @@ def prefill_config(n, unique=None):
                        "with Zipf(1.1) popularity (seeded), MXFP4 gate/up/down, 20 slices split over the GPUs, "
                        "tcgen05 kind::i8 grouped GEMMs, partial sum by NCCL all-reduce at N>1",
            "hidden": HIDDEN, "layers": 1, "tokens_per_step": PF_TOKENS, "experts": 512, "top_k": TOPK,
-           "zipf": PF_ZIPF, "slices": SLICES, "shares": equal_shares(n), "formats": "MXFP4 gate/up/down",
+           "zipf": PF_ZIPF, "slices": SLICES, "shares": equal_shares(n),
+           "formats": "Q4_K gate/up, MXFP4 down (the reference's unit layout)" if PF_GATE == "q4k"
+                      else "MXFP4 gate/up/down",
            "activations": "bf16 x on the device (FRC_RUN_X_BF16, widened exactly to fp32; the host call frc_run "
                           "takes the same values as fp32, as fr_backend.run does), Q8 per 64 (src/q4.c scheme), "
                           "int8 tensor-core dots of the values and of their dequantization residuals, exact block "
@@ -724,9 +744,9 @@ def run_prefill_bench(args, rank, world, local):
                                 device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     blocks = owned_blocks(rank, world)
-    MX = fb.MXFP4
-    g = fb.geometry(HIDDEN, 1, MX, MX)
-    ctx = fb.Context(local, HIDDEN, layers=1, gate_type=MX, down_type=MX)
+    MX, GT = fb.MXFP4, pf_gate_type(fb)
+    g = fb.geometry(HIDDEN, 1, GT, MX)
+    ctx = fb.Context(local, HIDDEN, layers=1, gate_type=GT, down_type=MX)
     pool = np.concatenate([fb.synth_slice(g, SEED, i) for i in range(POOL)])
     ctx.pool_load(pool, fb.synth_shared(g, SEED, 1 << 20))
     for b in blocks:
@@ -881,8 +901,10 @@ def run_prefill_bench(args, rank, world, local):
             "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": prefill_config(world, unique),
             "weight_gbs": unique * SLICES * PF_SLICE_BYTES * 1e3 / ms_per_step / 1e9,
             "roofline": {"bound": "hbm", "achieved": gu_gbs, "peak": peak, "unit": "GB/s", "frac": gu_gbs / peak,
-                         "traffic": ncu_traffic("prefill_mma_kernels_prefill512_full.md"), "peak_source": peak_src,
-                         "kernel": "prefill_mma_kernel<gate/up> (tcgen05 kind::i8)",
+                         "traffic": ncu_traffic("prefill_mma_kernels_prefill512_full.md") if PF_GATE == "mxfp4"
+                         else None, "peak_source": peak_src,
+                         "kernel": "prefill_mma_kernel<gate/up%s> (tcgen05 kind::i8)" % (
+                             ", Q4_K rows" if PF_GATE == "q4k" else ""),
                          "algorithmic_bytes_per_launch": gu_bytes, "launch_us": float(stage[2] * 1e3),
                          "launch_us_source": "CUDA events around the launch on its stream (eager calls)",
                          "down_kernel": {"bytes": dn_bytes, "us": float(stage[3] * 1e3), "gbs": dn_gbs,
@@ -905,9 +927,9 @@ def prefill_profile_case():
     slices, 1.07 GB on the device): three eager calls of 512 tokens."""
     import torch
     import fronk_b200 as fb
-    MX = fb.MXFP4
-    g = fb.geometry(HIDDEN, 1, MX, MX)
-    ctx = fb.Context(0, HIDDEN, layers=1, gate_type=MX, down_type=MX)
+    MX, GT = fb.MXFP4, pf_gate_type(fb)
+    g = fb.geometry(HIDDEN, 1, GT, MX)
+    ctx = fb.Context(0, HIDDEN, layers=1, gate_type=GT, down_type=MX)
     pool = np.concatenate([fb.synth_slice(g, SEED, i) for i in range(POOL)])
     ctx.pool_load(pool, fb.synth_shared(g, SEED, 1 << 20))
     for b in range(SLICES):
@@ -949,7 +971,7 @@ def prefill_parity(ctx, fb, g, pool, blocks, req):
             arr[ident * sb:(ident + 1) * sb] = pool[k * sb:(k + 1) * sb]
         layers[b] = arr
     orc = Oracle()
-    m = orc.model(HIDDEN, fb.MXFP4, fb.MXFP4, layers)
+    m = orc.model(HIDDEN, pf_gate_type(fb), fb.MXFP4, layers)
     rc, y_ref, _, _ = orc.prefill_run(m, e[sample], gt[sample], x[sample])
     if rc:
         return {"error": "oracle rc %d" % rc}
