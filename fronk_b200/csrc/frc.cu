@@ -799,7 +799,7 @@ static int run_long(frc_context* c, unsigned layer, unsigned T, const uint16_t* 
   if (!chunks && act == FRC_ACT_Q8 && (flags & ~unsigned(FRC_RUN_X_BF16)) == 0 && !scratch && c->pf_ye)
     return run_prefill(c, layer, T, expert, gate, x, y, s, (flags & FRC_RUN_X_BF16) != 0);
   if (flags & FRC_RUN_X_BF16)
-    return fail(c, FRC_UNSUPPORTED, "bf16 x: only bursts on the tensor-core path (MXFP4, Q8, no shared expert, no other flag)");
+    return fail(c, FRC_UNSUPPORTED, "bf16 x: only bursts on the tensor-core path (MXFP4 or Q4_K gate/up, MXFP4 down, Q8, no shared expert, no other flag)");
   const size_t d = c->g.hidden;
   for (unsigned t0 = 0; t0 < T; t0 += FRC_MAX_TOKENS) {
     const unsigned n = T - t0 < FRC_MAX_TOKENS ? T - t0 : FRC_MAX_TOKENS;
