@@ -830,7 +830,8 @@ def run_prefill_bench(args, rank, world, local):
     tokens_s = PF_TOKENS * 1000.0 / ms_per_step
     unique = float(np.mean([uniq[s % PF_SETS] for s in range(args.warmup, args.warmup + args.steps)]))
 
-    # per-kernel durations: events around each of the five launches, eager calls
+    # per-kernel durations: events around each of the five stages (seven launches:
+    # the MMA stages launch the shared expert's items and the routed ones), eager calls
     ctx.prefill_timing(True)
     stage = []
     for s in range(2 * PF_SETS):
@@ -910,7 +911,7 @@ def run_prefill_bench(args, rank, world, local):
                          "down_kernel": {"bytes": dn_bytes, "us": float(stage[3] * 1e3), "gbs": dn_gbs,
                                          "frac": dn_gbs / peak},
                          "stage_us": {n: float(v * 1e3) for n, v in zip(names, stage)}},
-            "gpu_launches": 5 * args.steps, "graph": used_graph, "clocks": clocks,
+            "gpu_launches": 7 * args.steps, "graph": used_graph, "clocks": clocks,
             "e2e": e2e, "parity": parity,
         }
         if world == 1 and not args.no_cpu_baseline:

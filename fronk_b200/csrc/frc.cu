@@ -235,12 +235,14 @@ struct frc_context {
   float* pf_hs = nullptr;
   float* pf_ye = nullptr;
   int2* pf_xvr = nullptr;  // Q4_K gate/up: per token and 32-block {sum v, sum r}
+  int8_t* pf_xqn = nullptr;  // v and r in natural order (the shared expert's Q8_0 rows)
+  int8_t* pf_xrn = nullptr;
   bool pf_attr = false;
   unsigned last_pf_S = 0;
   // tensor maps of the loaded layer regions (valid while tmap_of matches layer_ptr)
   CUtensorMap tmap[FRC_MAX_BLOCKS][FRC_MAX_LAYERS];
   const uint8_t* tmap_of[FRC_MAX_BLOCKS][FRC_MAX_LAYERS] = {};
-  // optional CUDA events around the five prefill launches (frc_prefill_timing)
+  // optional CUDA events around the five prefill stages (frc_prefill_timing)
   cudaEvent_t pf_ev[6] = {};
   bool pf_timing = false, pf_timed = false;
   // bounded waits of the layer kernel (frc_set_wait_limit) and the test-only
@@ -259,8 +261,8 @@ struct frc_context {
 
 // Prefill bounds: pairs of one call, and work items (tiles of 64 tokens of
 // each expert: at most pairs / 64 + 512 of them).
-constexpr size_t kPfMaxPairs = size_t(FRC_MAX_PREFILL_TOKENS) * FRC_TOPK;
-constexpr size_t kPfMaxTiles = kPfMaxPairs / kPfTile + FRC_ROUTED_EXPERTS;
+constexpr size_t kPfMaxPairs = size_t(FRC_MAX_PREFILL_TOKENS) * FRC_ACTIVE;  // ten routed + the shared expert
+constexpr size_t kPfMaxTiles = kPfMaxPairs / kPfTile + FRC_ROUTED_EXPERTS + 1;
 
 static int fail(frc_context* c, int rc, const char* fmt, ...) {
   if (c) {
@@ -671,11 +673,11 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
   return launch_layer<FRC_ACT_F32>(c, a, s, overlap);
 }
 
-// A burst of more than FRC_MAX_TOKENS tokens.  With MXFP4 weights, Q8
-// activations and no run flags it takes the tensor-core prefill path
-// (frc_prefill.cuh; a nonzero shared-expert gate is rejected there);
-// otherwise it runs as bursts of FRC_MAX_TOKENS through the layer kernel
-// (`chunks` forces that).
+// A burst of more than FRC_MAX_TOKENS tokens.  With MXFP4 or Q4_K gate/up
+// rows, MXFP4 down rows, Q8 activations and no run flag but FRC_RUN_X_BF16
+// it takes the tensor-core prefill path (frc_prefill.cuh; the Q8_0 shared
+// expert included); otherwise it runs as bursts of FRC_MAX_TOKENS through
+// the layer kernel (`chunks` forces that).
 // The layer region of (block, layer) as a 2D byte array of row_bytes-long
 // rows (every slice of an MXFP4/MXFP4 layer is a whole number of them), for
 // 128-byte x 64-row tiled TMA boxes, 128-byte swizzle.  Encoded once per
@@ -743,6 +745,9 @@ static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_
   a.x_bf16 = x_bf16 ? 1u : 0u;
   a.q4k = c->g.gate_type == FRC_Q4_K ? 1u : 0u;
   a.xvr = a.q4k ? c->pf_xvr : nullptr;
+  a.xqn = c->pf_xqn; a.xrn = c->pf_xrn;
+  a.shared_row = static_cast<unsigned>(c->shared_row);
+  a.shared_proj = static_cast<unsigned>(c->shared_proj);
   a.row_bytes = static_cast<unsigned>(c->row_bytes);
   a.slice_bytes = c->slice_bytes;
   a.slice_rows = static_cast<unsigned>(c->slice_bytes / c->row_bytes);
@@ -754,14 +759,15 @@ static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_
   c->last_G = 4 * c->sms;  // frc_debug_phases: [cta][64] stamps
   const unsigned smem = sizeof(PfSmem);
   if (!c->pf_attr) {
-    CK(cudaFuncSetAttribute(prefill_mma_kernel<kGateUp, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    CK(cudaFuncSetAttribute(prefill_mma_kernel<kGateUp, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    CK(cudaFuncSetAttribute(prefill_mma_kernel<kDown, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const void* kernels[] = {reinterpret_cast<const void*>(prefill_mma_kernel<kGateUp, false, false>),
+                             reinterpret_cast<const void*>(prefill_mma_kernel<kGateUp, true, false>),
+                             reinterpret_cast<const void*>(prefill_mma_kernel<kGateUp, false, true>),
+                             reinterpret_cast<const void*>(prefill_mma_kernel<kDown, false, false>),
+                             reinterpret_cast<const void*>(prefill_mma_kernel<kDown, false, true>)};
+    for (const void* k : kernels) CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     // The kernels' setmaxnreg split is sized for 128 registers a thread at
     // launch: with fewer, the epilogue's increase could never be granted.
-    for (const void* k : {reinterpret_cast<const void*>(prefill_mma_kernel<kGateUp, false>),
-                          reinterpret_cast<const void*>(prefill_mma_kernel<kGateUp, true>),
-                          reinterpret_cast<const void*>(prefill_mma_kernel<kDown, false>)}) {
+    for (const void* k : kernels) {
       cudaFuncAttributes fa;
       CK(cudaFuncGetAttributes(&fa, k));
       if (fa.numRegs != 128)
@@ -778,16 +784,20 @@ static int run_prefill(frc_context* c, unsigned layer, unsigned T, const uint16_
   mark(1);
   prefill_group_kernel<<<1, 1024, 0, s>>>(a);
   mark(2);
-  if (a.q4k) prefill_mma_kernel<kGateUp, true><<<c->sms, kPfThreads, smem, s>>>(a);
-  else prefill_mma_kernel<kGateUp, false><<<c->sms, kPfThreads, smem, s>>>(a);
+  // the shared expert's items (none unless a token has a shared gate: the
+  // launch then ends at once), then the routed experts'
+  prefill_mma_kernel<kGateUp, false, true><<<c->sms, kPfThreads, smem, s>>>(a);
+  if (a.q4k) prefill_mma_kernel<kGateUp, true, false><<<c->sms, kPfThreads, smem, s>>>(a);
+  else prefill_mma_kernel<kGateUp, false, false><<<c->sms, kPfThreads, smem, s>>>(a);
   mark(3);
-  prefill_mma_kernel<kDown, false><<<c->sms, kPfThreads, smem, s>>>(a);
+  prefill_mma_kernel<kDown, false, true><<<c->sms, kPfThreads, smem, s>>>(a);
+  prefill_mma_kernel<kDown, false, false><<<c->sms, kPfThreads, smem, s>>>(a);
   mark(4);
   prefill_combine_kernel<<<dim3((d / 4 + 255) / 256, T), 256, 0, s>>>(a);
   mark(5);
   c->pf_timed = timed;
   CK(cudaGetLastError());
-  c->launches += 5;
+  c->launches += 7;
   c->last_pf_S = S;
   return FRC_OK;
 }
@@ -799,7 +809,7 @@ static int run_long(frc_context* c, unsigned layer, unsigned T, const uint16_t* 
   if (!chunks && act == FRC_ACT_Q8 && (flags & ~unsigned(FRC_RUN_X_BF16)) == 0 && !scratch && c->pf_ye)
     return run_prefill(c, layer, T, expert, gate, x, y, s, (flags & FRC_RUN_X_BF16) != 0);
   if (flags & FRC_RUN_X_BF16)
-    return fail(c, FRC_UNSUPPORTED, "bf16 x: only bursts on the tensor-core path (MXFP4 or Q4_K gate/up, MXFP4 down, Q8, no shared expert, no other flag)");
+    return fail(c, FRC_UNSUPPORTED, "bf16 x: only bursts on the tensor-core path (MXFP4 or Q4_K gate/up, MXFP4 down, Q8, no other flag)");
   const size_t d = c->g.hidden;
   for (unsigned t0 = 0; t0 < T; t0 += FRC_MAX_TOKENS) {
     const unsigned n = T - t0 < FRC_MAX_TOKENS ? T - t0 : FRC_MAX_TOKENS;
@@ -967,13 +977,15 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
     alloc(reinterpret_cast<void**>(&c->pf_xme), sizeof(int2) * T * (d / 64));
     alloc(reinterpret_cast<void**>(&c->pf_pair_token), sizeof(uint16_t) * kPfMaxPairs);
     alloc(reinterpret_cast<void**>(&c->pf_slot_pair), sizeof(unsigned) * kPfMaxPairs);
-    alloc(reinterpret_cast<void**>(&c->pf_counts), sizeof(unsigned) * 4);
+    alloc(reinterpret_cast<void**>(&c->pf_counts), sizeof(unsigned) * 8);
     alloc(reinterpret_cast<void**>(&c->pf_items_gu), sizeof(uint4) * kPfMaxTiles * ((FRC_MAX_BLOCKS + 1) / 2));
     alloc(reinterpret_cast<void**>(&c->pf_items_dn), sizeof(uint4) * kPfMaxTiles * (d / 128));
     alloc(reinterpret_cast<void**>(&c->pf_hq), kPfMaxPairs * FRC_MAX_BLOCKS * 32);
     alloc(reinterpret_cast<void**>(&c->pf_hs), sizeof(float) * kPfMaxPairs * FRC_MAX_BLOCKS);
     alloc(reinterpret_cast<void**>(&c->pf_ye), sizeof(float) * kPfMaxPairs * d);
     if (pf_q4) alloc(reinterpret_cast<void**>(&c->pf_xvr), sizeof(int2) * T * (d / 32));
+    alloc(reinterpret_cast<void**>(&c->pf_xqn), T * d);
+    alloc(reinterpret_cast<void**>(&c->pf_xrn), T * d);
   }
   alloc(reinterpret_cast<void**>(&c->d_in), in_bytes);
   alloc(reinterpret_cast<void**>(&c->d_out), out_bytes);
@@ -1015,7 +1027,7 @@ int frc_close(frc_context* c) {
   cudaFree(c->d_in); cudaFree(c->d_out); cudaFree(c->pool);
   cudaFree(c->pf_xq); cudaFree(c->pf_xr); cudaFree(c->pf_xs); cudaFree(c->pf_xme); cudaFree(c->pf_pair_token); cudaFree(c->pf_slot_pair); cudaFree(c->pf_counts);
   cudaFree(c->pf_items_gu); cudaFree(c->pf_items_dn); cudaFree(c->pf_hq); cudaFree(c->pf_hs); cudaFree(c->pf_ye);
-  cudaFree(c->pf_xvr);
+  cudaFree(c->pf_xvr); cudaFree(c->pf_xqn); cudaFree(c->pf_xrn);
   cudaFreeHost(c->h_in); cudaFreeHost(c->h_out);
   if (c->stream) cudaStreamDestroy(c->stream);
   for (auto e : c->pf_ev) if (e) cudaEventDestroy(e);
@@ -1160,8 +1172,6 @@ int frc_run(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* exp
     return fail(c, FRC_INVALID, "bad run arguments");
   int rc = validate(c, tokens, expert, gate, x);
   if (rc) return fail(c, rc, "request rejected");
-  bool shared = false;  // the prefill path has no shared expert: such bursts run in chunks
-  for (unsigned t = 0; t < tokens; ++t) shared |= gate[t * FRC_ACTIVE + FRC_TOPK] != 0.0f;
   CK(cudaSetDevice(c->device));
   // one copy in: [x][gate][expert] packed for this call's token count
   const size_t xb = sizeof(float) * tokens * c->g.hidden, gb = sizeof(float) * tokens * FRC_ACTIVE;
@@ -1172,7 +1182,7 @@ int frc_run(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* exp
   CK(cudaMemcpyAsync(c->d_in, c->h_in, xb + gb + eb, cudaMemcpyHostToDevice, c->stream));
   rc = run_device(c, layer, tokens, reinterpret_cast<const uint16_t*>(c->d_in + xb + gb),
                   reinterpret_cast<const float*>(c->d_in + xb), reinterpret_cast<const float*>(c->d_in), nullptr,
-                  nullptr, c->d_y, act, 0, c->stream, nullptr, shared);
+                  nullptr, c->d_y, act, 0, c->stream, nullptr);
   if (rc) return rc;
   if (tokens <= FRC_MAX_TOKENS) {
     c->last_T = tokens;
@@ -1619,8 +1629,9 @@ int frc_debug_prefill_hidden(frc_context* c, int8_t* hq, float* hs, size_t cap, 
   if (!c || !pairs || !c->pf_counts || !c->last_pf_S) return fail(c, FRC_INVALID, "no prefill run to report");
   CK(cudaSetDevice(c->device));
   CK(cudaStreamSynchronize(c->stream));
-  unsigned P = 0;
-  CK(cudaMemcpy(&P, c->pf_counts, sizeof P, cudaMemcpyDeviceToHost));
+  unsigned cnt[4] = {0, 0, 0, 0};
+  CK(cudaMemcpy(cnt, c->pf_counts, sizeof cnt, cudaMemcpyDeviceToHost));
+  const unsigned P = cnt[0], routed = cnt[3];  // the shared expert's pairs follow the routed ones
   *pairs = P;
   if (!hq && !hs) return FRC_OK;
   if (cap < P) return fail(c, FRC_INVALID, "capacity %zu below %u pairs", cap, P);
@@ -1629,9 +1640,9 @@ int frc_debug_prefill_hidden(frc_context* c, int8_t* hq, float* hs, size_t cap, 
     int8_t* tmp = static_cast<int8_t*>(malloc(n));
     if (!tmp) return fail(c, FRC_IO, "host buffer");
     const cudaError_t e = cudaMemcpy(tmp, c->pf_hq, n, cudaMemcpyDeviceToHost);
-    if (e == cudaSuccess)  // device order: prmt order within each 32-block
+    if (e == cudaSuccess)  // device order: prmt order within each 32-block (routed), natural (shared)
       for (size_t blk = 0; blk < n / 32; ++blk)
-        for (unsigned k = 0; k < 32; ++k) hq[32 * blk + k] = tmp[32 * blk + prmt_pos(k)];
+        for (unsigned k = 0; k < 32; ++k) hq[32 * blk + k] = tmp[32 * blk + (blk / S < routed ? prmt_pos(k) : k)];
     free(tmp);
     if (e != cudaSuccess) return fail(c, FRC_IO, "%s", cudaGetErrorString(e));
   }

@@ -1,28 +1,34 @@
 // frc_prefill.cuh - the batched (prefill) path: bursts of up to 512 tokens
-// with MXFP4 gate/up rows on the 5th-generation tensor cores.
+// with MXFP4 or Q4_K gate/up rows and MXFP4 down rows on the 5th-generation
+// tensor cores, the Q8_0 shared expert included.
 //
-// One layer call is five launches on one stream:
-//   1. prefill_quantize_kernel: x -> int8 per 64 (the ref-q8 scheme of
-//      src/q4.c:37-61), each 32-block stored in the nibble order of an MXFP4
-//      block (prmt order), plus one fp32 scale s per 64 and, for the exact
-//      block terms, the residuals r = (fl32(v * s) - v * s) / 2^E of the
-//      dequantized values (s = M * 2^E, |r| <= 64);
+// One layer call is seven launches on one stream:
+//   1. prefill_quantize_kernel: x (fp32 or bf16) -> int8 v per 64 (the ref-q8
+//      scheme of src/q4.c:37-61), each 32-block stored in the nibble order of
+//      an MXFP4 block (prmt order) and in natural order, one fp32 scale s per
+//      64 and, for the exact block terms, the residuals r = (fl32(v * s) -
+//      v * s) / 2^E of the dequantized values (s = M * 2^E, |r| <= 64), and
+//      (Q4_K rows) each block's sums of v and r;
 //   2. prefill_group_kernel (one CTA): validation, the (expert, token) pairs
 //      expert-major with tokens ascending (a bitmap per expert, ranks by
-//      popcount), and the work lists, biggest experts first;
-//   3. prefill_mma_kernel<kGateUp>: item = (expert, pair of loaded blocks,
-//      up to 64 of its tokens).  A = the 128 gate/up rows of the two slices
-//      (int8: doubled E2M1 values), B = the tokens' int8 activations v
-//      (rows 0-63) and residuals r (rows 64-127), D = int32 in tensor
-//      memory, one tcgen05.mma kind::i8 per 32-weight block (N 128: the dots
-//      I with v and R with r); the epilogue forms each block's exact term
-//      (M * I + R) * 2^(e - 128 + E) and sums the terms in double, narrows
-//      the sum to fp32, then SwiGLU (double) and Q8 per 32 give hq / hscale
-//      per (pair, block);
-//   4. prefill_mma_kernel<kDown>: item = (expert, 128 output rows, tokens);
-//      A = MXFP4 down rows, B = hq, one MMA per loaded block;
-//   5. prefill_combine_kernel: y[t] = sum over the token's experts in
-//      request order of gate * partial, fmaf in fp32.
+//      popcount), the shared expert as expert 512 for the tokens whose
+//      shared gate is not zero, and the work lists, its items first, then
+//      the routed experts' biggest first;
+//   3. prefill_mma_kernel<kGateUp, Q4, SH> (SH = the shared expert's items,
+//      then the routed ones): item = (expert, pair of loaded blocks, up to
+//      64 of its tokens).  A = the 128 gate/up rows of the two slices as int8
+//      (doubled E2M1 values, Q4_K nibbles, or the shared expert's Q8_0
+//      values), B = the tokens' v (rows [0, npad)) and r (rows [npad,
+//      2 npad)), D = int32 in tensor memory, one tcgen05.mma kind::i8 per
+//      32-weight block (the dots I with v and R with r); the epilogue forms
+//      each block's (or Q4_K x group's) exact term from M * I + R and the
+//      scales, sums the terms in double, narrows the sum to fp32, then
+//      SwiGLU (double) and Q8 per 32 give hq / hscale per (pair, block);
+//   4. prefill_mma_kernel<kDown, false, SH>: item = (expert, 128 output rows,
+//      tokens); A = MXFP4 (or the shared expert's Q8_0) down rows, B = hq,
+//      one MMA per loaded block;
+//   5. prefill_combine_kernel: y[t] = sum over the token's routed experts in
+//      request order, then its shared expert, of gate * partial, fmaf in fp32.
 // The arithmetic is restated step for step by the oracle's or_prefill_run.
 //
 // Inside an MMA kernel (one CTA per SM, 448 threads) warps have roles:
@@ -93,9 +99,13 @@ struct PrefillArgs {
   float* xs;               // [T][d/64]
   int2* xme;               // [T][d/64] {M, E << 20}: xs = M * 2^E
   int2* xvr;               // [T][d/32] {V, RS}: the block's sums of v and of r (Q4_K mins)
+  int8_t* xqn;             // [T][d] v in natural order (the shared expert's Q8_0 rows)
+  int8_t* xrn;             // [T][d] r in natural order
+  unsigned shared_row, shared_proj;  // the shared slice's Q8_0 gate/up row and 32 rows, bytes
   uint16_t* pair_token;    // [P]
-  unsigned* slot_pair;     // [T][10]
-  unsigned* counts;        // [0] pairs, [1] gate/up items, [2] down items
+  unsigned* slot_pair;     // [T][11]: each routed slot's pair, then the shared expert's (or ~0)
+  unsigned* counts;        // [0] pairs, [1] gate/up items, [2] down items, [3] routed pairs,
+                           // [4] / [5] the shared expert's gate/up / down items
   uint4* items_gu;         // {expert, first pair, tokens, block pair}
   uint4* items_dn;         // {expert, first pair, tokens, row tile}
   int8_t* hq;              // [P][S][32], prmt order per block
@@ -315,6 +325,12 @@ __global__ void prefill_quantize_kernel(PrefillArgs a) {
   const int r0 = resid(q0), r1 = resid(q1);
   rout[32 * blk + prmt_pos(n)] = static_cast<int8_t>(r0);
   rout[32 * blk + prmt_pos(n + 1)] = static_cast<int8_t>(r1);
+  // natural order too, for the shared expert's rows (copied to the operand
+  // tiles as they are)
+  reinterpret_cast<char2*>(a.xqn + 64 * static_cast<size_t>(g))[lane] =
+      make_char2(static_cast<char>(q0), static_cast<char>(q1));
+  reinterpret_cast<char2*>(a.xrn + 64 * static_cast<size_t>(g))[lane] =
+      make_char2(static_cast<char>(r0), static_cast<char>(r1));
   if (a.xvr) {  // Q4_K rows: each 32-block's sums of v and of r (lanes 0-15, 16-31)
     int sv = q0 + q1, sr = r0 + r1;
 #pragma unroll
@@ -367,10 +383,12 @@ __device__ __forceinline__ unsigned scan512(unsigned v, unsigned* ws, unsigned& 
 // gates finite and >= 0, shared gate 0), pairs, work lists.
 __global__ void __launch_bounds__(1024) prefill_group_kernel(PrefillArgs a) {
   __shared__ uint32_t bits[512][16];  // token bitmap per expert (T <= 512)
+  __shared__ uint32_t shbits[16];     // tokens whose shared-expert gate is not zero
   __shared__ unsigned cnt[512], rank_of[512], ibase_gu[513], ibase_dn[513], poff[513];
-  __shared__ unsigned by_rank[512], scan_ws[16];
+  __shared__ unsigned by_rank[512], scan_ws[16], nsh_s;
   const unsigned tid = threadIdx.x, T = a.T, words = (T + 31) / 32;
   for (unsigned i = tid; i < 512 * 16; i += blockDim.x) (&bits[0][0])[i] = 0;
+  if (tid < 16) shbits[tid] = 0;
   __syncthreads();
   unsigned st = 0;
   for (unsigned i = tid; i < T * 10; i += blockDim.x) {
@@ -383,10 +401,15 @@ __global__ void __launch_bounds__(1024) prefill_group_kernel(PrefillArgs a) {
     const float g = a.gate[i];
     if (!isfinite(g)) st |= kStNumeric;
     else if (g < 0.0f) st |= kStInvalid;
-    else if (i % 11 == 10 && g != 0.0f) st |= kStInvalid;  // shared expert: decode path only
+    else if (i % 11 == 10 && g != 0.0f) atomicOr(&shbits[(i / 11) >> 5], 1u << ((i / 11) & 31));
   }
   if (st) atomicOr(a.status, st);
   __syncthreads();
+  if (tid == 0) {
+    unsigned n = 0;
+    for (unsigned w = 0; w < words; ++w) n += __popc(shbits[w]);
+    nsh_s = n;
+  }
   for (unsigned e = tid; e < 512; e += blockDim.x) {
     unsigned c = 0;
     for (unsigned w = 0; w < words; ++w) c += __popc(bits[e][w]);
@@ -402,37 +425,61 @@ __global__ void __launch_bounds__(1024) prefill_group_kernel(PrefillArgs a) {
     by_rank[r] = e;
   }
   __syncthreads();
+  // The shared expert (id 512, Q8_0 rows) takes the pairs after the routed
+  // ones (tokens ascending) and the first items of both work lists (it is
+  // the biggest expert of a burst that uses it).
+  const unsigned npairs = (a.S + 1) / 2, nrt = a.d / 128;
+  const unsigned nsh = nsh_s, tiles_sh = (nsh + kPfTile - 1) / kPfTile;
   {
     // pair offsets in expert order, item offsets in rank order: block scans
-    const unsigned npairs = (a.S + 1) / 2, nrt = a.d / 128;
     unsigned tp, tgu, tdn;
     const unsigned ep = scan512(tid < 512 ? cnt[tid] : 0u, scan_ws, tp);
     const unsigned tiles = tid < 512 ? (cnt[by_rank[tid]] + kPfTile - 1) / kPfTile : 0u;
     const unsigned eg = scan512(tiles * npairs, scan_ws, tgu);
     const unsigned ed = scan512(tiles * nrt, scan_ws, tdn);
-    if (tid < 512) { poff[tid] = ep; ibase_gu[tid] = eg; ibase_dn[tid] = ed; }
+    if (tid < 512) {
+      poff[tid] = ep;
+      ibase_gu[tid] = eg + tiles_sh * npairs;
+      ibase_dn[tid] = ed + tiles_sh * nrt;
+    }
     if (tid == 0) {
       poff[512] = tp;
-      a.counts[0] = tp; a.counts[1] = tgu; a.counts[2] = tdn;
+      a.counts[0] = tp + nsh;
+      a.counts[1] = tgu + tiles_sh * npairs;
+      a.counts[2] = tdn + tiles_sh * nrt;
+      a.counts[3] = tp;  // routed pairs
+      a.counts[4] = tiles_sh * npairs;  // the shared expert's gate/up items (first in the list)
+      a.counts[5] = tiles_sh * nrt;     // its down items
     }
   }
   __syncthreads();
   for (unsigned i = tid; i < T * 10; i += blockDim.x) {
     const unsigned t = i / 10, e = a.expert[i];
-    if (e >= 512) { a.slot_pair[i] = 0xffffffffu; continue; }
+    if (e >= 512) { a.slot_pair[t * 11 + i % 10] = 0xffffffffu; continue; }
     unsigned r = __popc(bits[e][t >> 5] & ((1u << (t & 31)) - 1));
     for (unsigned w = 0; w < (t >> 5); ++w) r += __popc(bits[e][w]);
     const unsigned p = poff[e] + r;
     a.pair_token[p] = static_cast<uint16_t>(t);
-    a.slot_pair[i] = p;
+    a.slot_pair[t * 11 + i % 10] = p;
   }
-  const unsigned npairs = (a.S + 1) / 2, nrt = a.d / 128;
-  for (unsigned e = tid; e < 512; e += blockDim.x) {
-    const unsigned c = cnt[e], tiles = (c + kPfTile - 1) / kPfTile, r = rank_of[e];
+  for (unsigned t = tid; t < T; t += blockDim.x) {
+    unsigned p = 0xffffffffu;
+    if (shbits[t >> 5] >> (t & 31) & 1u) {
+      unsigned r = __popc(shbits[t >> 5] & ((1u << (t & 31)) - 1));
+      for (unsigned w = 0; w < (t >> 5); ++w) r += __popc(shbits[w]);
+      p = poff[512] + r;
+      a.pair_token[p] = static_cast<uint16_t>(t);
+    }
+    a.slot_pair[t * 11 + 10] = p;
+  }
+  for (unsigned e = tid; e < 513; e += blockDim.x) {
+    const bool sh = e == 512;
+    const unsigned c = sh ? nsh : cnt[e], tiles = (c + kPfTile - 1) / kPfTile;
+    const unsigned bgu = sh ? 0u : ibase_gu[rank_of[e]], bdn = sh ? 0u : ibase_dn[rank_of[e]];
     for (unsigned k = 0; k < tiles; ++k) {
       const unsigned n = min(kPfTile, c - k * kPfTile), p0 = poff[e] + k * kPfTile;
-      for (unsigned q = 0; q < npairs; ++q) a.items_gu[ibase_gu[r] + k * npairs + q] = make_uint4(e, p0, n, q);
-      for (unsigned q = 0; q < nrt; ++q) a.items_dn[ibase_dn[r] + k * nrt + q] = make_uint4(e, p0, n, q);
+      for (unsigned q = 0; q < npairs; ++q) a.items_gu[bgu + k * npairs + q] = make_uint4(e, p0, n, q);
+      for (unsigned q = 0; q < nrt; ++q) a.items_dn[bdn + k * nrt + q] = make_uint4(e, p0, n, q);
     }
   }
 }
@@ -442,7 +489,8 @@ __global__ void __launch_bounds__(1024) prefill_group_kernel(PrefillArgs a) {
 struct PfScales;
 template <unsigned MODE>
 __device__ __forceinline__ void pf_apply16(const PfScales& sc, unsigned st, unsigned m, unsigned col,
-                                           const uint32_t (&v)[16], float* acc, bool live, bool& bad);
+                                           const uint32_t (&v)[16], float* acc, bool live, bool& bad,
+                                           bool q8 = false);
 
 // One chunk's scales, in a ring of their own: the epilogue holds a chunk's
 // scales long after the MMAs have released its operand stage.
@@ -458,6 +506,8 @@ struct PfScales {
       uint8_t sm[128][16];  // gate/up Q4_K: per A row, the super-block's 6-bit scales then mins
       float2 dd[128];       // gate/up Q4_K: per A row {d, dmin}
     } q4;
+    uint16_t hg[128][8];    // gate/up, shared expert (Q8_0): per A row, the chunk's fp16 block scales
+    uint16_t hd[8][128];    // down, shared expert (Q8_0): per block of the chunk, per A row, fp16 scale
   };
 };
 
@@ -500,10 +550,16 @@ __device__ __forceinline__ void fma2(float ax, float ay, float bx, float by, flo
 // (|I| < 2^22): the bits of I + 1.5 * 2^23 less that constant.
 template <unsigned MODE>
 __device__ __forceinline__ void pf_apply16(const PfScales& sc, unsigned st, unsigned m, unsigned col,
-                                           const uint32_t (&v)[16], float* acc, bool live, bool& bad) {
-  const unsigned e8 = sc.row[MODE == kGateUp ? 8 * m + st : 128 * st + m];
-  bad |= live && e8 == 255;
-  const float ws = pow2_m128(e8);
+                                           const uint32_t (&v)[16], float* acc, bool live, bool& bad, bool q8) {
+  float ws;
+  if (q8) {  // the shared expert's Q8_0 down row: its fp16 scale
+    ws = h2f(sc.hd[st][m]);
+    bad |= live && !isfinite(ws);
+  } else {
+    const unsigned e8 = sc.row[MODE == kGateUp ? 8 * m + st : 128 * st + m];
+    bad |= live && e8 == 255;
+    ws = pow2_m128(e8);
+  }
   const float4* cs = reinterpret_cast<const float4*>(sc.col[st] + col);
 #pragma unroll
   for (unsigned q4 = 0; q4 < 4; ++q4) {
@@ -689,19 +745,73 @@ __device__ __forceinline__ void gu_terms_q4k(double (&accd)[32], const PfScales&
   }
 }
 
+// The shared expert's form of gu_terms (Q8_0 rows, operands in natural
+// order): each block's exact Z = M I + R times the exact double d_b 2^E (d_b
+// the block's fp16 scale), blocks in order; two steps x two units a read.
+__device__ __forceinline__ void gu_terms_q8(double (&accd)[32], const PfScales& sc, uint32_t tg, unsigned bw,
+                                            unsigned npad, unsigned wg, unsigned m, unsigned g0, unsigned n,
+                                            unsigned nq, bool live, bool& bad) {
+  for (unsigned j0 = 0; j0 < n; j0 += 2) {
+    const unsigned st = g0 + j0;  // even
+    const uint32_t hp = *reinterpret_cast<const uint32_t*>(&sc.hg[m][st]);
+    const float f0 = h2f(hp & 0xffffu), f1 = h2f(hp >> 16);
+    bad |= live && !(isfinite(f0) && isfinite(f1));
+    const double d0 = f0, d1 = f1;
+    const int4* mev = reinterpret_cast<const int4*>(sc.me[st >> 1]) + 2 * wg;
+#pragma unroll
+    for (unsigned q0 = 0; q0 < 8; q0 += 2) {
+      if (q0 >= nq) break;  // warp-uniform
+      uint32_t vi[16], vr[16];
+#pragma unroll
+      for (unsigned qb = 0; qb < 2; ++qb)
+        if (q0 + qb < nq) {
+          const uint32_t t = tg + j0 * bw + 8 * (q0 + qb);
+          tmem_ld4(t, vi + 8 * qb);
+          tmem_ld4(t + bw, vi + 8 * qb + 4);
+          tmem_ld4(t + npad, vr + 8 * qb);
+          tmem_ld4(t + bw + npad, vr + 8 * qb + 4);
+        }
+      tmem_wait_ld();
+#pragma unroll
+      for (unsigned qb = 0; qb < 2; ++qb) {
+        const unsigned q = q0 + qb;
+        if (q >= nq) continue;
+        const int4 xa = mev[4 * q], xb = mev[4 * q + 1];
+        const int M[4] = {xa.x, xa.z, xb.x, xb.z}, Eh[4] = {xa.y, xa.w, xb.y, xb.w};
+#pragma unroll
+        for (unsigned jj = 0; jj < 4; ++jj) {
+          const long long z0 = static_cast<long long>(M[jj]) * static_cast<int>(vi[8 * qb + jj]) +
+                               (0x4338000000000000LL + static_cast<int>(vr[8 * qb + jj]));
+          const long long z1 = static_cast<long long>(M[jj]) * static_cast<int>(vi[8 * qb + 4 + jj]) +
+                               (0x4338000000000000LL + static_cast<int>(vr[8 * qb + 4 + jj]));
+          const double P = __hiloint2double(Eh[jj] + (1023 << 20), 0);  // 2^E
+          double acc = accd[4 * q + jj];
+          acc = fma(__longlong_as_double(z0) - 6755399441055744.0, d0 * P, acc);
+          acc = fma(__longlong_as_double(z1) - 6755399441055744.0, d1 * P, acc);
+          accd[4 * q + jj] = acc;
+        }
+      }
+    }
+  }
+}
+
 // Register split (setmaxnreg): launched at 128 a thread (448 x 128 =
 // 57,344; each SM sub-partition holds four of the 14 warps at most, 16,384
 // registers), the converter warpgroup gives up 32 a thread (96) and the two
 // epilogue warpgroups take them (144); warps 12-13 keep 128:
 // 128 x 96 + 256 x 144 + 64 x 128 = 57,344.
-// Q4 (gate/up only): Q4_K gate/up rows, else MXFP4.
-template <unsigned MODE, bool Q4>
+// Q4 (gate/up only): Q4_K gate/up rows, else MXFP4.  SH: the launch over the
+// shared expert's items (the first counts[4] / counts[5] of the work lists,
+// Q8_0 rows), else over the routed experts' items; the two are separate
+// instantiations so that neither carries the other's code and registers.
+template <unsigned MODE, bool Q4, bool SH>
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid_constant__ PrefillArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   PfSmem& s = *reinterpret_cast<PfSmem*>(smem_raw);
   const unsigned tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const unsigned nitems = a.counts[MODE == kGateUp ? 1 : 2];
-  const uint4* items = MODE == kGateUp ? a.items_gu : a.items_dn;
+  const unsigned nall = a.counts[MODE == kGateUp ? 1 : 2], nsh = a.counts[MODE == kGateUp ? 4 : 5];
+  const unsigned nitems = SH ? nsh : nall - nsh;
+  const uint4* items = (MODE == kGateUp ? a.items_gu : a.items_dn) + (SH ? 0 : nsh);
   const unsigned nk = pf_chunks<MODE>(a), d = a.d, nb = d / 32;
   volatile unsigned* abort = &s.abort;
 
@@ -734,7 +844,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         if (!pf_wait_warp(&s.raw_empty[st], ((c / kPfRaw) & 1) ^ 1, abort)) break;
         PF_PH(clk.lap(0);)
         uint8_t* dst = s.raw[st];
-        if (MODE == kGateUp && Q4) {
+        if (SH) {
+          // the shared expert's rows reach the operand tiles by cp.async
+          // from the converters: the stage completes with no bytes
+          if (lane == 0) mbar_expect_tx(&s.raw_full[st], 0);
+          __syncwarp();
+        } else if (MODE == kGateUp && Q4) {
           // one 144 B x 64-row box per slice: super-block k of its 32 gate and
           // 32 up rows (3D map: byte, row of the slice, slice), unswizzled
           const unsigned nsl = 2 * item.w + 1 < a.S ? 2 : 1;
@@ -847,8 +962,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         for (unsigned i = tid; i < item.z * (MODE == kGateUp ? 32u : 16u); i += 128) {
           const unsigned j = (i >> 4) % item.z, half = (i >> 4) / item.z, piece = i & 15;
           if (MODE == kDown && piece >= 2 * steps) continue;
+          const int8_t* xsrc = SH ? (half ? a.xrn : a.xqn) : (half ? a.xr : a.xq);
           const int8_t* src = MODE == kGateUp
-                                  ? (half ? a.xr : a.xq) + static_cast<size_t>(s.tok[tb][j]) * d + 256 * k + 16 * piece
+                                  ? xsrc + static_cast<size_t>(s.tok[tb][j]) * d + 256 * k + 16 * piece
                                   : a.hq + (static_cast<size_t>(item.y + j) * a.S + 8 * k) * 32 + 16 * piece;
           cp_async16(s.B[ab] + umma_off(j + half * npad, 16 * piece, 256), src);
         }
@@ -856,7 +972,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         if (MODE == kGateUp) {
           unsigned blk, hrow;
           gu_row(m, item.w, blk, hrow);
-          if (!Q4 && blk < a.S) {  // (Q4_K row scales come with the payload)
+          if (SH) {
+            // the shared expert's Q8_0 row (transcoded: [d/32 fp16 scales][d
+            // int8]): chunk k's eight scales and its 256 values, in natural
+            // order, straight into the operand tile
+            if (blk < a.S) {
+              const uint8_t* row = a.base[blk] + 512ull * a.slice_bytes + static_cast<size_t>(hrow) * a.shared_row;
+              cp_async16(s.sc[sq].hg[m], row + 16 * k);
+              const uint8_t* qs = row + 2 * (d / 32) + 256 * k;
+#pragma unroll
+              for (unsigned i = 0; i < 16; ++i) cp_async16(s.A[ab] + umma_off(m, 16 * i, 256), qs + 16 * i);
+            }
+          } else if (!Q4 && blk < a.S) {  // (Q4_K row scales come with the payload)
             const uint8_t* row = a.base[blk] + item.x * a.slice_bytes + static_cast<size_t>(hrow) * a.row_bytes;
             cp_async8(s.sc[sq].row + 8 * m, row + 8 * k);  // gate/up: [row][8 blocks]
           }
@@ -864,11 +991,30 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
             const unsigned j = i >> 2, g = i & 3;  // x group g of the chunk (blocks 2g, 2g + 1)
             cp_async8(&s.sc[sq].me[g][j], a.xme + static_cast<size_t>(s.tok[tb][j]) * (d / 64) + 4 * k + g);
           }
-          if (Q4)
+          if (Q4 && !SH)
             for (unsigned i = tid; i < item.z * 8; i += 128) {
               const unsigned j = i >> 3, b = i & 7;  // block b of the chunk
               cp_async8(&s.sc[sq].vr[b][j], a.xvr + static_cast<size_t>(s.tok[tb][j]) * (d / 32) + 8 * k + b);
             }
+        } else if (SH) {
+          // the shared expert's Q8_0 down rows 128 w + m of each loaded slice
+          // (transcoded: [d fp16 scales][d x 32 int8]): 32 values into the
+          // operand tile, and the 128 rows' scales
+          for (unsigned b = 0; b < steps; ++b) {
+            const uint8_t* down = a.base[8 * k + b] + 512ull * a.slice_bytes + 2ull * a.shared_proj;
+            const uint8_t* qs = down + 2 * d + 32 * (static_cast<size_t>(item.w) * 128 + m);
+            cp_async16(s.A[ab] + umma_off(m, 32 * b, 256), qs);
+            cp_async16(s.A[ab] + umma_off(m, 32 * b + 16, 256), qs + 16);
+          }
+          for (unsigned i = tid; i < steps * 16; i += 128) {
+            const unsigned b = i >> 4, piece = i & 15;
+            const uint8_t* down = a.base[8 * k + b] + 512ull * a.slice_bytes + 2ull * a.shared_proj;
+            cp_async16(&s.sc[sq].hd[b][8 * piece], down + 2 * (item.w * 128 + 8 * piece));
+          }
+          for (unsigned i = tid; i < item.z * steps; i += 128) {
+            const unsigned j = i / steps, b = i % steps;
+            cp_async4(&s.sc[sq].col[b][j], a.hs + static_cast<size_t>(item.y + j) * a.S + 8 * k + b);
+          }
         } else {
           for (unsigned i = tid; i < steps * 8; i += 128) {
             const unsigned b = i >> 3, piece = i & 7;
@@ -906,7 +1052,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         const bool landed = pf_wait(&s.raw_full[st], (c / kPfRaw) & 1, abort);
         PF_PH(clk.lap(0);)
         uint8_t* A = s.A[ab];
-        if (landed && MODE == kGateUp && Q4) {
+        if (SH) {
+          // shared expert: the operand tile arrives by cp.async
+        } else if (landed && MODE == kGateUp && Q4) {
           if (row_live) {
             PfScales& scw = s.sc[c % kPfSc];
             q4k_row_to_i8(s.raw[st] + 144 * (64 * (m >> 6) + hrow), A, m, scw.q4.sm[m], scw.q4.dd[m]);
@@ -958,6 +1106,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
     for (unsigned it = blockIdx.x; it < nitems; it += gridDim.x) {
       const uint4 item = items[it];
       const unsigned ntok = item.z, npad = (ntok + 15) & ~15u;
+      constexpr bool shi = SH;  // the shared expert (Q8_0 rows)
       // gate/up: the units of columns 8q + 4wq .. +3 go to this warpgroup,
       // wq alternating with the CTA's items (one-unit tiles to both); its
       // live units are q < nq (8q + 4wq < ntok)
@@ -988,7 +1137,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
           // exact block terms (the reference's sum of w * fl32(v * s)), gu_terms
           const unsigned GS = pf_gs<MODE>(npad), BW = pf_bw<MODE>(npad);
           float2 dd = make_float2(0.0f, 0.0f);
-          if (Q4) {  // the super-block's d and dmin of this row: finite, or NUMERIC
+          if (Q4 && !shi) {  // the super-block's d and dmin of this row: finite, or NUMERIC
             dd = sc.q4.dd[m];
             bad |= live && !(isfinite(dd.x) && isfinite(dd.y));
           }
@@ -999,8 +1148,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
             PF_PH(clk.lap(1);)
             tc_fence_after();
             const uint32_t tg = lane_base + 256 * grp + 4 * wq;
-            if (Q4 && nq) gu_terms_q4k(accd, sc, tg, BW, npad, wq, m, g0, n, nq, dd);
-            if (!Q4 && nq) gu_terms(accd, sc, tg, BW, npad, wq, m, g0, n, nq, live, bad);
+            if (shi) {
+              if (nq) gu_terms_q8(accd, sc, tg, BW, npad, wq, m, g0, n, nq, live, bad);
+            } else if (Q4) {
+              if (nq) gu_terms_q4k(accd, sc, tg, BW, npad, wq, m, g0, n, nq, dd);
+            } else if (nq) {
+              gu_terms(accd, sc, tg, BW, npad, wq, m, g0, n, nq, live, bad);
+            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s.acc_empty[grp]);
@@ -1027,7 +1181,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
                   for (unsigned i = 0; i < 4; ++i)
                     if (jb + (i >> 1) < n)
                       pf_apply16<MODE>(sc, g0 + jb + (i >> 1), m, col0 + 16 * (i & 1), v[i], acc + 16 * (i & 1), live,
-                                       bad);
+                                       bad, shi);
                 }
               }
             } else if (col0 < ntok) {  // at most 16 live columns: the group's steps at once
@@ -1037,7 +1191,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
               tmem_wait_ld();
   #pragma unroll
               for (unsigned i = 0; i < 4; ++i)
-                if (i < n) pf_apply16<MODE>(sc, g0 + i, m, col0, v[i], acc, live, bad);
+                if (i < n) pf_apply16<MODE>(sc, g0 + i, m, col0, v[i], acc, live, bad, shi);
             }
             tc_fence_before();
             __syncwarp();
@@ -1102,7 +1256,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_mma_kernel(const __grid
         epi_sync(wg);
         const unsigned blk = 2 * item.w + (ew >> 1), n = 16 * (ew & 1) + (lane & 15);
         if (live && ok) {
-          int8_t* hq = a.hq + static_cast<size_t>(item.y) * a.S * 32 + blk * 32 + prmt_pos(n);
+          // prmt order for the routed experts' MXFP4 down rows, natural order
+          // for the shared expert's Q8_0 ones
+          int8_t* hq = a.hq + static_cast<size_t>(item.y) * a.S * 32 + blk * 32 + (shi ? n : prmt_pos(n));
 #pragma unroll
           for (unsigned i0 = 0; i0 < 16; i0 += 8) {
             if (!live_pair(i0)) continue;
@@ -1148,9 +1304,11 @@ __global__ void prefill_combine_kernel(PrefillArgs a) {
   if (r >= a.d) return;
   const unsigned P = a.counts[0];
   float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  // the ten routed experts in request order, then the shared expert
 #pragma unroll
-  for (unsigned j = 0; j < 10; ++j) {
-    const unsigned p = a.slot_pair[t * 10 + j];
+  for (unsigned j = 0; j < 11; ++j) {
+    const unsigned p = a.slot_pair[t * 11 + j];
+    if (j == 10 && p == 0xffffffffu) break;  // no shared expert for this token
     if (p >= P) {  // an id the group kernel rejected (status already set)
       acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       break;

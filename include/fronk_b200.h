@@ -334,7 +334,7 @@ int frc_debug_quantize(frc_context *c, unsigned tokens, const float *x, int8_t *
 int frc_debug_umma(frc_context *c, unsigned n, unsigned k, const int8_t *a, const int8_t *b, int32_t *d);
 /* Event timing of the prefill path (bursts above FRC_MAX_TOKENS on the
  * tensor cores): while enabled, every prefill call records CUDA events on its
- * stream around its five launches (quantize, group, gate/up MMA, down MMA,
+ * stream around its five stages (quantize, group, gate/up MMA, down MMA,
  * combine); frc_prefill_times waits for the last call's final event and
  * writes the five durations in ms.  For measurement; leave it disabled in
  * captured graphs. */

@@ -145,7 +145,7 @@ class Oracle:
             return self.L.or_prefill_run(ctypes.byref(m), x.shape[0], _p(e), _p(g), _p(x), _p(y), None, None, 0,
                                          None), y, None, None
         S = sum(1 for p in m.layer if p)
-        cap = x.shape[0] * 10
+        cap = x.shape[0] * 11  # ten routed pairs a token, and the shared expert's
         hq = np.zeros((cap, S, 32), np.int8)
         hs = np.zeros((cap, S), np.float32)
         n = ctypes.c_size_t()

@@ -664,22 +664,24 @@ int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, c
     if (d % 512 || d > 8192) return OR_INVALID;
     int rc = validate_n(d, tokens, OR_MAX_PREFILL, expert, gate, x);
     if (rc) return rc;
-    for (unsigned t = 0; t < tokens; ++t)
-        if (gate[(size_t)t * OR_ACTIVE + OR_TOPK] != 0) return OR_INVALID;
     if (!any_loaded(m)) return OR_STATE;
     unsigned blocks[OR_BLOCKS], S = 0;
     for (unsigned b = 0; b < OR_BLOCKS; ++b) if (m->layer[b]) blocks[S++] = b;
     const unsigned dt = m->down_type, nb = d / 32;
     const size_t slice = or_slice_bytes(d, gt, dt), in_row = or_row_bytes(gt, d);
     const size_t proj = OR_NEURONS * in_row, down_row = or_row_bytes(dt, OR_NEURONS);
+    /* the shared expert's slice (Q8_0 gate/up and down rows, src/native.h:1-3) */
+    const size_t sh_row = or_row_bytes(OR_Q8_0, d), sh_proj = (size_t)d * 34;
 
-    /* pairs, expert-major */
-    unsigned *pair_t = malloc(sizeof(unsigned) * tokens * OR_TOPK), *pair_e = malloc(sizeof(unsigned) * tokens * OR_TOPK);
-    unsigned *slot_pair = malloc(sizeof(unsigned) * tokens * OR_TOPK);
+    /* pairs, expert-major; the shared expert (512) last, for the tokens whose
+     * shared gate is not zero */
+    const unsigned PMAX = tokens * OR_ACTIVE;
+    unsigned *pair_t = malloc(sizeof(unsigned) * PMAX), *pair_e = malloc(sizeof(unsigned) * PMAX);
+    unsigned *slot_pair = malloc(sizeof(unsigned) * PMAX);
     int8_t *q = malloc((size_t)tokens * d), *res = malloc((size_t)tokens * d);
-    int8_t *hv = malloc((size_t)tokens * OR_TOPK * S * OR_NEURONS);
-    float *xsc = malloc(sizeof(float) * tokens * (d / 64)), *hsc = malloc(sizeof(float) * tokens * OR_TOPK * S);
-    float *part = malloc(sizeof(float) * (size_t)tokens * OR_TOPK * d), *out = malloc(sizeof(float) * (size_t)tokens * d);
+    int8_t *hv = malloc((size_t)PMAX * S * OR_NEURONS);
+    float *xsc = malloc(sizeof(float) * tokens * (d / 64)), *hsc = malloc(sizeof(float) * PMAX * S);
+    float *part = malloc(sizeof(float) * (size_t)PMAX * d), *out = malloc(sizeof(float) * (size_t)tokens * d);
     rc = OR_INVALID;
     if (!pair_t || !pair_e || !slot_pair || !q || !res || !hv || !xsc || !hsc || !part || !out) goto done;
     unsigned P = 0;
@@ -687,8 +689,14 @@ int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, c
         for (unsigned t = 0; t < tokens; ++t)
             for (unsigned j = 0; j < OR_TOPK; ++j)
                 if (expert[(size_t)t * OR_TOPK + j] == e) {
-                    pair_t[P] = t; pair_e[P] = e; slot_pair[t * OR_TOPK + j] = P; ++P;
+                    pair_t[P] = t; pair_e[P] = e; slot_pair[t * OR_ACTIVE + j] = P; ++P;
                 }
+    for (unsigned t = 0; t < tokens; ++t) {
+        slot_pair[t * OR_ACTIVE + OR_TOPK] = ~0u;
+        if (gate[(size_t)t * OR_ACTIVE + OR_TOPK] != 0) {
+            pair_t[P] = t; pair_e[P] = OR_SHARED; slot_pair[t * OR_ACTIVE + OR_TOPK] = P; ++P;
+        }
+    }
     if (pairs) *pairs = P;
     if ((hq || hs) && pair_cap < P) goto done;
     for (unsigned t = 0; t < tokens; ++t) {
@@ -702,6 +710,14 @@ int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, c
         for (unsigned si = 0; si < S; ++si) {
             const uint8_t *sl = m->layer[blocks[si]] + (size_t)pair_e[p] * slice;
             float sc;
+            if (pair_e[p] == OR_SHARED) {
+                for (unsigned n = 0; n < 2 * OR_NEURONS; ++n)
+                    for (unsigned b = 0; b < nb; ++b)
+                        if (!block_scale(sl + n * sh_row, OR_Q8_0, b, &sc)) goto done;
+                for (unsigned r = 0; r < d; ++r)
+                    if (!block_scale(sl + 2 * sh_proj, OR_Q8_0, r, &sc)) goto done;
+                continue;
+            }
             for (unsigned n = 0; n < 2 * OR_NEURONS; ++n)
                 for (unsigned b = 0; b < nb; ++b) {
                     if (gt == OR_MXFP4 && !block_scale(sl + n * in_row, OR_MXFP4, b, &sc)) goto done;
@@ -724,9 +740,23 @@ int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, c
                 float gu[2];
                 double gd[2];
                 for (unsigned w = 0; w < 2; ++w) {
-                    const uint8_t *row = sl + (w ? proj : 0) + n * in_row;
+                    const int sh = pair_e[p] == OR_SHARED;
+                    const uint8_t *row = sh ? sl + (w ? sh_proj : 0) + n * sh_row : sl + (w ? proj : 0) + n * in_row;
                     double acc = 0;
-                    if (gt == OR_Q4_K) {
+                    if (sh) {
+                        /* Q8_0 rows of the shared expert: each block's exact
+                         * integer Z = M*I + R times the exact double d * 2^E */
+                        for (unsigned b = 0; b < nb; ++b) {
+                            float db;
+                            block_scale(row, OR_Q8_0, b, &db);
+                            const int32_t I = idot_block(row, OR_Q8_0, b, qt + 32 * b);
+                            const int32_t R = idot_block(row, OR_Q8_0, b, rt + 32 * b);
+                            int64_t M;
+                            int E;
+                            scale_parts(xs[b / 2], &M, &E);
+                            acc = fma((double)(M * I + R), (double)db * ldexp(1.0, E), acc);
+                        }
+                    } else if (gt == OR_Q4_K) {
                         /* Q4_K rows, one 256-weight super-block a chunk, its four
                          * 64-weight x groups in order: with K1 = sc0*I0 + sc1*I1,
                          * K3 = sc0*R0 + sc1*R1 (dots against v and r),
@@ -786,13 +816,16 @@ int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, c
             int8_t *hp = hv + ((size_t)p * S + si) * OR_NEURONS;
             if (or_q8_quantize(h, OR_NEURONS, hp, hsc + (size_t)p * S + si)) goto done;
         }
+        const int shp = pair_e[p] == OR_SHARED;
+        const unsigned pdt = shp ? OR_Q8_0 : dt;
+        const size_t pdrow = shp ? 34 : down_row, pproj = shp ? sh_proj : proj;
         for (unsigned r = 0; r < d; ++r) {
             float acc = 0;
             for (unsigned si = 0; si < S; ++si) {
-                const uint8_t *down = m->layer[blocks[si]] + (size_t)pair_e[p] * slice + 2 * proj;
+                const uint8_t *down = m->layer[blocks[si]] + (size_t)pair_e[p] * slice + 2 * pproj;
                 float ws;
-                block_scale(down + r * down_row, dt, 0, &ws);
-                const int32_t I = idot_block(down + r * down_row, dt, 0, hv + ((size_t)p * S + si) * OR_NEURONS);
+                block_scale(down + r * pdrow, pdt, 0, &ws);
+                const int32_t I = idot_block(down + r * pdrow, pdt, 0, hv + ((size_t)p * S + si) * OR_NEURONS);
                 acc = fmaf((float)I * hsc[(size_t)p * S + si], ws, acc);
             }
             part[(size_t)p * d + r] = acc;
@@ -802,7 +835,9 @@ int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, c
         for (unsigned r = 0; r < d; ++r) {
             float acc = 0;
             for (unsigned j = 0; j < OR_TOPK; ++j)
-                acc = fmaf(gate[(size_t)t * OR_ACTIVE + j], part[(size_t)slot_pair[t * OR_TOPK + j] * d + r], acc);
+                acc = fmaf(gate[(size_t)t * OR_ACTIVE + j], part[(size_t)slot_pair[t * OR_ACTIVE + j] * d + r], acc);
+            if (slot_pair[t * OR_ACTIVE + OR_TOPK] != ~0u)  /* then the shared expert */
+                acc = fmaf(gate[(size_t)t * OR_ACTIVE + OR_TOPK], part[(size_t)slot_pair[t * OR_ACTIVE + OR_TOPK] * d + r], acc);
             if (!isfinite(acc)) goto done;
             out[(size_t)t * d + r] = acc;
         }

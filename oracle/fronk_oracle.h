@@ -72,8 +72,8 @@ int or_port_run(const or_model *m, unsigned tokens, const uint16_t *expert, cons
                 const float *x, float *y, float *h, size_t h_cap, size_t *h_count);
 
 /* The CUDA prefill path's arithmetic (bursts of up to OR_MAX_PREFILL tokens,
- * MXFP4 or Q4_K gate/up, MXFP4 or Q8_0 down, no shared expert): see
- * fronk_oracle.c.
+ * MXFP4 or Q4_K gate/up, MXFP4 or Q8_0 down, the Q8_0 shared expert as
+ * expert 512 for tokens with a shared gate): see fronk_oracle.c.
  * hq [pair][loaded block][32] / hs [pair][loaded block] (pairs expert-major,
  * tokens ascending) receive the quantized hidden values when not NULL. */
 int or_prefill_run(const or_model *m, unsigned tokens, const uint16_t *expert, const float *gate,

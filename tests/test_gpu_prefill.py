@@ -70,15 +70,17 @@ def test_prefill_other_shapes(gpu, oracle, hidden, tokens, distinct):
     assert np.array_equal(y.view(np.uint32), y_ref.view(np.uint32))
 
 
-def test_prefill_zipf_512_tokens_all_blocks(gpu, oracle):
+@pytest.mark.parametrize("gate", [MXFP4, Q4_K])
+def test_prefill_zipf_512_tokens_all_blocks(gpu, oracle, gate):
     """configs[4]'s shape: 512 tokens, Zipf(1.1) expert popularity, all 20
-    blocks (device-filled units).  Tokens are independent, so a sample of
-    them is checked against the oracle bit for bit."""
-    g = fb.geometry(2048, gate_type=MXFP4, down_type=MXFP4)
+    blocks (device-filled units), on MXFP4 and on the reference's Q4_K
+    gate/up rows.  Tokens are independent, so a sample of them is checked
+    against the oracle bit for bit."""
+    g = fb.geometry(2048, gate_type=gate, down_type=MXFP4)
     e, gt, x = fb.synth_request(2048, 512, SEED + 512, zipf=1.1)
     pool = np.concatenate([fb.synth_slice(g, SEED, i) for i in range(16)])
     sb = fb.slice_bytes(g)
-    with fb.Context(0, 2048, gate_type=MXFP4, down_type=MXFP4) as ctx:
+    with fb.Context(0, 2048, gate_type=gate, down_type=MXFP4) as ctx:
         ctx.pool_load(pool, fb.synth_shared(g, SEED, 1 << 20))
         for b in range(20):
             ctx.fill_layer(b, 0, SEED)
@@ -94,25 +96,55 @@ def test_prefill_zipf_512_tokens_all_blocks(gpu, oracle):
             k = fb.pool_pick(SEED, b, 0, ident, 16)
             arr[ident * sb:(ident + 1) * sb] = pool[k * sb:(k + 1) * sb]
         layers[b] = arr
-    m = oracle.model(2048, MXFP4, MXFP4, layers)
+    m = oracle.model(2048, gate, MXFP4, layers)
     rc, y_ref, _, _ = oracle.prefill_run(m, e[sample], gt[sample], x[sample])
     assert rc == OK
     assert np.array_equal(y[sample].view(np.uint32), y_ref.view(np.uint32))
 
 
-def test_long_bursts_with_a_shared_expert_run_in_chunks(gpu, oracle):
-    """A nonzero shared-expert gate sends a long host burst through the decode
-    kernel, 16 tokens at a time: each chunk matches the decode arithmetic."""
-    e, gt, x = request(2048, 36, SEED + 36, shared_gate=0.3)
-    with fb.Context(0, 2048, gate_type=MXFP4, down_type=MXFP4) as ctx:
-        m, layers = _setup(ctx, oracle, [2, 4], e)
+@pytest.mark.parametrize("gate,tokens", [(MXFP4, 36), (Q4_K, 100)])
+def test_prefill_with_the_shared_expert(gpu, oracle, gate, tokens):
+    """A nonzero shared-expert gate keeps a long burst on the tensor-core path:
+    the Q8_0 shared expert is expert 512 (its pairs after the routed ones,
+    operands in natural order, each block's exact Z times d * 2^E, added
+    after the token's routed experts).  hq, hscale and y bit for bit against
+    the oracle, y within 1e-5 of ref-q8; a token without a shared gate skips
+    it."""
+    e, gt, x = request(2048, tokens, SEED + tokens + 7, shared_gate=0.3)
+    gt[5, 10] = 0.0
+    with fb.Context(0, 2048, gate_type=gate, down_type=MXFP4) as ctx:
+        m, layers = _setup(ctx, oracle, [2, 4, 13], e, gate=gate)
         rc, y = ctx.run(0, e, gt, x)
         assert rc == OK, ctx.last_error
-    for t0 in range(0, 36, 16):
-        sl = slice(t0, min(36, t0 + 16))
-        rc, y_ref, _ = oracle.port_run(m, e[sl], gt[sl], x[sl])
+        hq, hs = ctx.debug_prefill_hidden()
+    rc, y_ref, hq_ref, hs_ref = oracle.prefill_run(m, e, gt, x, want_hidden=True)
+    assert rc == OK
+    assert hq.shape[0] == tokens * 10 + tokens - 1
+    assert np.array_equal(hq, hq_ref)
+    assert np.array_equal(hs.view(np.uint32), hs_ref.view(np.uint32))
+    assert np.array_equal(y.view(np.uint32), y_ref.view(np.uint32))
+    for t0 in range(0, tokens, 16):
+        sl = slice(t0, min(tokens, t0 + 16))
+        rc, y_q8 = oracle.ref_run(m, e[sl], gt[sl], x[sl], 1)
         assert rc == OK
-        assert max(rel_l2(y_ref[t], y[sl][t]) for t in range(y_ref.shape[0])) <= 1e-5
+        assert max(rel_l2(r, a) for r, a in zip(y_q8, y[sl])) <= 1e-5
+
+
+def test_prefill_shared_expert_nonfinite_scale_is_numeric(gpu, oracle):
+    """An infinite fp16 scale in a block of the shared expert's Q8_0 down rows:
+    NUMERIC whatever the gate, y untouched."""
+    e, gt, x = request(2048, 20, SEED + 21, shared_gate=0.2)
+    g = fb.geometry(2048, gate_type=MXFP4, down_type=MXFP4)
+    bad = make_layers(g, SEED, [1], e, shared=True)[1]
+    # reference layout of the shared slice: 64 gate/up rows of d/32 34-byte
+    # Q8_0 blocks, then d down rows of one block; down row 77's fp16 scale
+    off = 512 * fb.slice_bytes(g) + 2 * 32 * (2048 // 32) * 34 + 77 * 34
+    bad[off:off + 2] = [0x00, 0x7c]
+    sentinel = np.full(x.shape, 7.0, np.float32)
+    with fb.Context(0, 2048, gate_type=MXFP4, down_type=MXFP4) as ctx:
+        assert ctx.load_layer(1, 0, bad) == OK
+        rc, y = ctx.run(0, e, gt, x, out=sentinel.copy())
+        assert rc == NUMERIC and np.array_equal(y, sentinel)
 
 
 def test_prefill_failures_leave_output_untouched(gpu, oracle):

@@ -57,11 +57,11 @@ def test_prefill_tokens_are_independent(oracle):
     assert np.array_equal(ys.view(np.uint32), y[sub].view(np.uint32))
 
 
-def test_prefill_rejects_shared_expert_and_bad_scales(oracle):
+def test_prefill_rejects_bad_gates_and_scales(oracle):
     e, gt, x = request(2048, 20, SEED + 7)
     m, layers, g = _model(oracle, MXFP4, [4], e)
     gs = gt.copy()
-    gs[5, 10] = 0.25
+    gs[5, 10] = -0.25  # a negative (shared) gate
     assert oracle.prefill_run(m, e, gs, x)[0] == INVALID
     # E8M0 exponent 255 in the first block of gate row 0 of a referenced slice
     layers[4][int(e[0, 0]) * fb.slice_bytes(g)] = 255
@@ -101,3 +101,23 @@ def test_prefill_q4k_nonfinite_super_block_scale_is_numeric(oracle):
     m = oracle.model(2048, Q4_K, MXFP4, {2: bad})
     rc, _, _, _ = oracle.prefill_run(m, e, gt, x)
     assert rc == NUMERIC
+
+
+@pytest.mark.parametrize("gate_type", [MXFP4, Q4_K])
+def test_prefill_shared_expert_matches_ref_q8(oracle, gate_type):
+    """The Q8_0 shared expert inside a burst (the reference's units always
+    carry it): its pairs follow the routed ones, its Q8_0 block terms are
+    exact integers times d * 2^E, and it is added after the token's routed
+    experts; y within 1e-5 of ref-q8 per token."""
+    e, gt, x = request(2048, 16, SEED + 33, shared_gate=0.4)
+    gt[3, 10] = 0.0  # a token without the shared expert
+    g = fb.geometry(2048, gate_type=gate_type, down_type=MXFP4)
+    layers = make_layers(g, SEED, [0, 5, 11], e, shared=True)
+    m = oracle.model(2048, gate_type, MXFP4, layers)
+    rc, y, hq, hs = oracle.prefill_run(m, e, gt, x, want_hidden=True)
+    assert rc == OK
+    assert hq.shape[0] == 16 * 10 + 15
+    rc, y_q8 = oracle.ref_run(m, e, gt, x, 1)
+    assert rc == OK
+    for t in range(16):
+        assert oracle.compare(y_q8[t], y[t])[1][0] <= 1e-5, t
