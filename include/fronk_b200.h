@@ -191,8 +191,8 @@ int frc_run(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *exp
  * FRC_RUN_X_BF16: x holds bf16 values ([tokens][d] 16-bit words, the upper
  * half of an fp32 bit pattern), widened exactly to fp32 on the device; the
  * tensor-core burst path only (more than 16 tokens, Q8, MXFP4 or Q4_K
- * gate/up rows, MXFP4 down rows, no other flag, no shared-expert gate); any
- * other call with it is FRC_UNSUPPORTED.
+ * gate/up rows, MXFP4 down rows, no other flag); any other call with it is
+ * FRC_UNSUPPORTED.
  * FRC_RUN_OVERLAP: the launch may start while the kernel before it on the
  * stream is finishing (programmatic dependent launch): it plans and starts
  * streaming this layer's weights at once and waits for that kernel only
