@@ -238,8 +238,9 @@ __device__ __forceinline__ unsigned scale_ef(float s) { return max((__float_as_u
 
 // One token's quantized activations in shared memory.  v and r are stored in
 // the same swizzled layout (xslot), in natural order for Q4_K / Q8_0 rows and
-// in prmt order for MXFP4 rows; st[p] = {s_p, 2^E_p} per 64-group; vr[p] =
-// {V, RS} of its two 32-blocks (sums of v and of r).
+// in prmt order for MXFP4 rows; st[p] = {2^E_p, M_p (the low word)} per
+// 64-group (its scale s_p = M_p 2^E_p); vr[p] = {V, RS} of its two 32-blocks
+// (sums of v and of r).
 struct XAct {
   const uint8_t* v;
   const uint8_t* r;
@@ -338,7 +339,11 @@ __device__ __forceinline__ void idot2_mxfp4_16(const uint4 q, const uint32_t* x,
 // acc + c * (s * I + t * R): the inner value is exact (|s * I| < 2^40 ulps of
 // t), one rounding in the fma.
 __device__ __forceinline__ double block_acc(double acc, double c, const double2 st, int I, int R) {
-  return fma(c, fma(st.x, i2d(I), st.y * i2d(R)), acc);
+  // Z = M I + R exactly (|Z| < 2^51) as the bits of Z + 1.5 * 2^52, then
+  // acc += Z * (c 2^E) with one rounding (c 2^E exact: c is a power of two or
+  // an fp16 value)
+  const long long zm = static_cast<long long>(__double2loint(st.y)) * I + (0x4338000000000000LL + R);
+  return fma(__longlong_as_double(zm) - 6755399441055744.0, c * st.x, acc);
 }
 
 // Exact group terms (64 weights = blocks 2p, 2p+1) of an MXFP4 row.

@@ -191,9 +191,10 @@ __device__ __forceinline__ bool grid_sync(LayerCtl* ctl, unsigned* flag_smem, un
 // (Q8 activations, groups in order), in double and exact up to double
 // rounding (see the row terms in frc_device.cuh).  Q4_K spans are
 // super-blocks: per group p the integer combinations K1 = sc0*I0 + sc1*I1,
-// K3 = sc0*R0 + sc1*R1, K2 = mi0*V0 + mi1*V1, K4 = mi0*RS0 + mi1*RS1 enter
-// PP = s*K1 + 2^E*K3 and QQ = s*K2 + 2^E*K4 (fma each), and the span adds
-// d*PP - dmin*QQ.  One instantiation per weight type, so the code a launch
+// K3 = sc0*R0 + sc1*R1, K2 = mi0*V0 + mi1*V1, K4 = mi0*RS0 + mi1*RS1 give
+// the exact integers M*K1 + K3 and M*K2 + K4 (s = M 2^E), which enter
+// PP += (M*K1 + K3) 2^E and QQ += (M*K2 + K4) 2^E (one fma each), and the
+// span adds d*PP - dmin*QQ.  One instantiation per weight type, so the code a launch
 // runs is one contiguous block.
 template <unsigned TYPE>
 __device__ __forceinline__ void gu_sums(const uint8_t* gr, const uint8_t* ur, const XAct& xa, unsigned l8,
@@ -215,24 +216,25 @@ __device__ __forceinline__ void gu_sums(const uint8_t* gr, const uint8_t* ur, co
         load_x8(xa.r, p, 2, nspan, rhi);
         const double2 st = xa.st[p];
         const int4 vr = xa.vr[p];
+        const long long M = __double2loint(st.y);  // s = M 2^E, st.x = 2^E
+        // the exact integer M K + K' as a double (|.| < 2^51: magic 1.5 * 2^52)
+        auto zd = [&](int K, int Kr) {
+          return __longlong_as_double(M * K + (0x4338000000000000LL + Kr)) - 6755399441055744.0;
+        };
         int i0, i1, r0, r1;
         q4k_idots(bg + 16 + 32 * gp, xlo, rlo, xhi, rhi, i0, i1, r0, r1);
         {
           const int sc0 = (hg.sc[half] >> sh) & 0xff, sc1 = (hg.sc[half] >> (sh + 8)) & 0xff;
           const int mi0 = (hg.mi[half] >> sh) & 0xff, mi1 = (hg.mi[half] >> (sh + 8)) & 0xff;
-          pg = fma(st.x, i2d(sc0 * i0 + sc1 * i1), pg);
-          pg = fma(st.y, i2d(sc0 * r0 + sc1 * r1), pg);
-          qg = fma(st.x, i2d(mi0 * vr.x + mi1 * vr.z), qg);
-          qg = fma(st.y, i2d(mi0 * vr.y + mi1 * vr.w), qg);
+          pg = fma(zd(sc0 * i0 + sc1 * i1, sc0 * r0 + sc1 * r1), st.x, pg);
+          qg = fma(zd(mi0 * vr.x + mi1 * vr.z, mi0 * vr.y + mi1 * vr.w), st.x, qg);
         }
         q4k_idots(bu + 16 + 32 * gp, xlo, rlo, xhi, rhi, i0, i1, r0, r1);
         {
           const int sc0 = (hu.sc[half] >> sh) & 0xff, sc1 = (hu.sc[half] >> (sh + 8)) & 0xff;
           const int mi0 = (hu.mi[half] >> sh) & 0xff, mi1 = (hu.mi[half] >> (sh + 8)) & 0xff;
-          pu = fma(st.x, i2d(sc0 * i0 + sc1 * i1), pu);
-          pu = fma(st.y, i2d(sc0 * r0 + sc1 * r1), pu);
-          qu = fma(st.x, i2d(mi0 * vr.x + mi1 * vr.z), qu);
-          qu = fma(st.y, i2d(mi0 * vr.y + mi1 * vr.w), qu);
+          pu = fma(zd(sc0 * i0 + sc1 * i1, sc0 * r0 + sc1 * r1), st.x, pu);
+          qu = fma(zd(mi0 * vr.x + mi1 * vr.z, mi0 * vr.y + mi1 * vr.w), st.x, qu);
         }
       }
       ag = fma(static_cast<double>(hg.d), pg, ag);
@@ -475,8 +477,11 @@ __device__ __forceinline__ void layer_input(const LayerParams& a, uint8_t* smem,
     *reinterpret_cast<uint4*>(smem + a.sm.xq + t * d + slot16) = make_uint4(w[0], w[1], w[2], w[3]);
     *reinterpret_cast<uint4*>(smem + a.sm.xr + t * d + slot16) = make_uint4(wr[0], wr[1], wr[2], wr[3]);
     if (qd == 0)
-      reinterpret_cast<double2*>(smem + a.sm.xst)[t * P + p] =
-          make_double2(static_cast<double>(qg.scale), pow2d(static_cast<int>(ef) - 150));
+      reinterpret_cast<double2*>(smem + a.sm.xst)[t * P + p] =  // {2^E, M}: scale = M 2^E
+          make_double2(pow2d(static_cast<int>(ef) - 150),
+                       __hiloint2double(0, static_cast<int>((__float_as_uint(qg.scale) >> 23 & 255u)
+                                                                ? (__float_as_uint(qg.scale) & 0x7fffffu) | 0x800000u
+                                                                : __float_as_uint(qg.scale) & 0x7fffffu)));
     if ((qd & 1) == 0)
       reinterpret_cast<int2*>(smem + a.sm.xvr)[2 * (t * P + p) + (qd >> 1)] = make_int2(sum, rsum);
     if (a.sm.xp) {

@@ -450,25 +450,32 @@ static int lane_dot(const uint8_t *row, unsigned type, const qx *x, double *out)
                     const int32_t K1 = (int32_t)sc0 * i0 + (int32_t)sc1 * i1, K3 = (int32_t)sc0 * r0 + (int32_t)sc1 * r1;
                     const int32_t K2 = (int32_t)mi0 * x->sum[2 * p] + (int32_t)mi1 * x->sum[2 * p + 1];
                     const int32_t K4 = (int32_t)mi0 * x->rsum[2 * p] + (int32_t)mi1 * x->rsum[2 * p + 1];
-                    const double s = x->scale[p], t = x->ulp[p];
-                    PP = fma(s, (double)K1, PP);
-                    PP = fma(t, (double)K3, PP);
-                    QQ = fma(s, (double)K2, QQ);
-                    QQ = fma(t, (double)K4, QQ);
+                    int64_t M;
+                    int E;
+                    scale_parts(x->scale[p], &M, &E);
+                    const double t = x->ulp[p];
+                    /* s*K1 + 2^E*K3 = (M*K1 + K3) * 2^E: an exact integer, one fma */
+                    PP = fma((double)(M * K1 + K3), t, PP);
+                    QQ = fma((double)(M * K2 + K4), t, QQ);
                 }
                 acc = fma((double)d, PP, acc);
                 acc = fma(-(double)dm, QQ, acc);
             } else {
                 for (unsigned gp = 0; gp < 4; ++gp) {
                     const unsigned p = 4 * q + gp;
-                    const double s = x->scale[p], t = x->ulp[p];
+                    const double t = x->ulp[p];
                     for (unsigned k = 0; k < 2; ++k) {
                         const unsigned blk = 2 * p + k;
                         float c;
                         if (!block_scale(row, type, blk, &c)) return OR_NUMERIC;
                         const int32_t I = idot_block(row, type, blk, x->q + 32 * blk);
                         const int32_t R = idot_block(row, type, blk, x->r + 32 * blk);
-                        acc = fma((double)c, fma(s, (double)I, t * (double)R), acc);
+                        int64_t M;
+                        int E;
+                        scale_parts(x->scale[p], &M, &E);
+                        /* c * (s*I + 2^E*R) = (M*I + R) * (c * 2^E): exact integer
+                         * times an exact double, one fma */
+                        acc = fma((double)(M * I + R), (double)c * t, acc);
                     }
                 }
             }
