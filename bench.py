@@ -484,6 +484,7 @@ def main():
                                              + (" (includes the all-reduce)" if world > 1 else ""),
                          "kernel_alone_us": kernel_ms * 1e3, "kernel_alone_gbs": alone},
             "gpu_launches": launches, "graph": used_graph, "clocks": clocks, "e2e": e2e, "parity": parity,
+            "limiter": decode_limiter(bytes_per_launch, peak, launch_us, kernel_ms * 1e3, world, T),
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(3, 1) if T == 1 else cpu_baseline(1, 1, T)
@@ -492,6 +493,39 @@ def main():
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def decode_limiter(bytes_per_launch, peak, launch_us, alone_us, world, T):
+    """What bounds a layer launch, from this run's numbers: the time its
+    weight bytes take at the measured HBM peak against the measured launch
+    time.  Far above it, a layer is its chain of dependent steps (activation
+    pass, gate/up, grid barrier, down terms, reduce) rather than HBM."""
+    hbm_us = bytes_per_launch / (peak * 1e9) * 1e6
+    if launch_us > 2 * hbm_us:
+        what = ("the layer's dependent chain (activation pass, gate/up dot products, grid barrier, down terms, "
+                "reduce: latency, %s), not HBM" % ("CUDA-core dot products of %d tokens" % T if T > 1
+                                                   else "one token"))
+        if world > 1:
+            what += "; plus the in-kernel NVLink exchange of the partial rows each layer"
+    else:
+        what = "HBM bandwidth"
+    return {"hbm_time_us": hbm_us, "launch_us": launch_us, "kernel_alone_us": alone_us,
+            "launch_over_hbm": launch_us / hbm_us, "bound": what}
+
+
+def prefill_limiter(stage_ms, gu_bytes, peak, world):
+    """The prefill step's split: the tensor-core kernels against their HBM time,
+    and the fixed stages (quantize, grouping, combine) that do not shrink with
+    the slices a GPU holds."""
+    gu_us, dn_us = stage_ms[2] * 1e3, stage_ms[3] * 1e3
+    fixed_us = (stage_ms[0] + stage_ms[1] + stage_ms[4]) * 1e3
+    hbm_us = gu_bytes / (peak * 1e9) * 1e6
+    what = ("CUDA-core work around the MMAs in the gate/up kernel (exact block terms, SwiGLU, Q8 of the hidden "
+            "slices) and the operand conversion; tensor pipe and HBM are mostly idle")
+    if world > 1:
+        what += "; the fixed stages and the NCCL all-reduce of the 4 MB partial grow as a share with N"
+    return {"gate_up_us": gu_us, "gate_up_hbm_time_us": hbm_us, "down_us": dn_us, "fixed_stages_us": fixed_us,
+            "bound": what}
 
 
 def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev, peer=False, T=1):
@@ -912,6 +946,7 @@ def run_prefill_bench(args, rank, world, local):
                                          "frac": dn_gbs / peak},
                          "stage_us": {n: float(v * 1e3) for n, v in zip(names, stage)}},
             "gpu_launches": 7 * args.steps, "graph": used_graph, "clocks": clocks,
+            "limiter": prefill_limiter(stage, gu_bytes, peak, world),
             "e2e": e2e, "parity": parity,
         }
         if world == 1 and not args.no_cpu_baseline:
