@@ -605,7 +605,8 @@ static int run_long(frc_context* c, unsigned layer, unsigned T, const uint16_t* 
 
 static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t* expert, const float* gate,
                       const float* x, const float* x_add, float* x_out, float* y, int act, unsigned flags,
-                      cudaStream_t s, const RunScratch* scratch = nullptr, bool chunks = false) {
+                      cudaStream_t s, const RunScratch* scratch = nullptr, bool chunks = false,
+                      unsigned* status = nullptr) {
   if (!c || !expert || !gate || !x || !y) return fail(c, FRC_INVALID, "null argument");
   if (act != FRC_ACT_Q8 && act != FRC_ACT_F32) return fail(c, FRC_INVALID, "unknown activation mode");
   if (T > FRC_MAX_TOKENS) return run_long(c, layer, T, expert, gate, x, x_add, x_out, y, act, flags, s, scratch, chunks);
@@ -629,7 +630,7 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
   } else {
     a.partial = c->partial; a.gsv = c->gsv; a.hidden = c->hidden;
   }
-  a.ctl = c->ctl; a.status = c->status;
+  a.ctl = c->ctl; a.status = status ? status : c->status;
   if (flags & FRC_RUN_PEER) {
     if (c->world < 2) return fail(c, FRC_STATE, "FRC_RUN_PEER without frc_peer_attach");
     for (unsigned r = 0; r < c->world; ++r) a.peer[r] = c->peer[r];
@@ -1179,6 +1180,32 @@ int frc_run(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* exp
   memcpy(c->h_in, x, xb);
   memcpy(c->h_in + xb, gate, gb);
   memcpy(c->h_in + xb + gb, expert, eb);
+  if (tokens <= FRC_MAX_TOKENS) {
+    // The layer kernel's status word and y follow the request in the same
+    // device buffer: the copy in zeroes the status word (no separate memset),
+    // and one copy out brings back [status][y].
+    const size_t st_off = (xb + gb + eb + 15) & ~size_t(15);
+    memset(c->h_in + st_off, 0, 16);
+    CK(cudaMemcpyAsync(c->d_in, c->h_in, st_off + 16, cudaMemcpyHostToDevice, c->stream));
+    unsigned* d_st = reinterpret_cast<unsigned*>(c->d_in + st_off);
+    rc = run_device(c, layer, tokens, reinterpret_cast<const uint16_t*>(c->d_in + xb + gb),
+                    reinterpret_cast<const float*>(c->d_in + xb), reinterpret_cast<const float*>(c->d_in), nullptr,
+                    nullptr, reinterpret_cast<float*>(c->d_in + st_off + 16), act, 0, c->stream, nullptr, false, d_st);
+    if (rc) return rc;
+    c->last_T = tokens;
+    memcpy(c->last_expert, expert, eb);
+    memcpy(c->last_gate, gate, gb);
+    CK(cudaMemcpyAsync(c->h_out, c->d_in + st_off, 16 + xb, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    const unsigned st = *c->h_status;
+    if (st & kStTimeout) {
+      const int rrc = reset_after_timeout(c, c->stream);
+      if (rrc) return rrc;
+    }
+    if (status_code(st)) return fail(c, status_code(st), "device status 0x%x", st);
+    memcpy(y, c->h_y, xb);  // published only after the whole layer succeeded
+    return FRC_OK;
+  }
   CK(cudaMemcpyAsync(c->d_in, c->h_in, xb + gb + eb, cudaMemcpyHostToDevice, c->stream));
   rc = run_device(c, layer, tokens, reinterpret_cast<const uint16_t*>(c->d_in + xb + gb),
                   reinterpret_cast<const float*>(c->d_in + xb), reinterpret_cast<const float*>(c->d_in), nullptr,
