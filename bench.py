@@ -535,14 +535,23 @@ def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev, peer=False, T=1):
     import torch
     h2d = LAYERS * T * (HIDDEN * 4 + TOPK * 2 + 11 * 4)
     d2h = LAYERS * (T * HIDDEN * 4 + (16 if dist is None else 0))  # y (+ the status word frc_run reads with it)
-    if dist is None:
-        # the layer loop in C over the host-buffer call (frc_host_pass -> frc_run per layer)
+    if dist is None or peer:
+        # the layer loop in C over the host-buffer call (frc_host_pass_flags ->
+        # frc_run_flags per layer; at N>1 each rank holds its share of the
+        # slices and the kernel sums every layer over the ranks: FRC_RUN_PEER)
         hs = [np.ascontiguousarray(x0[s], np.float32).copy() for s in range(steps)]
         es = [np.ascontiguousarray(ex[s], np.uint16) for s in range(steps)]
+        flags = fb.RUN_PEER if dist is not None else 0
+        if dist is not None:
+            dist.barrier()
         t0 = time.perf_counter()
         for s in range(steps):
-            ctx.host_pass(0, es[s], gt[s], hs[s], fb.ACT_Q8)
+            ctx.host_pass(0, es[s], gt[s], hs[s], fb.ACT_Q8, flags)
         dt = time.perf_counter() - t0
+        if dist is not None:
+            t = torch.tensor([dt], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt = float(t.item())
     else:
         pin_x = torch.empty((T, HIDDEN), dtype=torch.float32).pin_memory()
         pin_e = torch.empty((T, TOPK), dtype=torch.int16).pin_memory()
@@ -580,8 +589,9 @@ def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev, peer=False, T=1):
         raise fb.FrcError(rc, "e2e", ctx.last_error)
     return {"value": T * steps / dt, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": steps, "api": "frc_host_pass: frc_run per layer (host buffers, synchronous)" if dist is None else
-            ("frc_run_device with the in-kernel NVLink reduce" if peer else "frc_run_device + NCCL all_reduce")
-            + ", pinned host copies each layer"}
+            ("frc_host_pass_flags(FRC_RUN_PEER): frc_run_flags per layer on every rank, host buffers, the "
+             "in-kernel NVLink reduce" if peer else
+             "frc_run_device + NCCL all_reduce, pinned host copies each layer")}
 
 
 def _host_layers(fb, g, pool, blocks, experts, layer=5):

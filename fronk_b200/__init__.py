@@ -84,6 +84,8 @@ _SIGS = {
     "frc_run_device": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
     "frc_run_device_fixed": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _int, _u32, _vp]),
     "frc_host_pass": (_int, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _u32, _int]),
+    "frc_host_pass_flags": (_int, [_vp, _u32, _u32, _u32, _vp, _vp, _vp, _u32, _int, _u32]),
+    "frc_run_flags": (_int, [_vp, _u32, _u32, _vp, _vp, _vp, _vp, _int, _u32]),
     "frc_peer_export": (_int, [_vp, _u32, _vp]),
     "frc_peer_attach": (_int, [_vp, _u32, _u32, _vp]),
     "frc_peer_detach": (_int, [_vp]),
@@ -387,15 +389,19 @@ class Context:
         self._check(self.lib.frc_loaded_mask(self.h, ctypes.byref(m)), "loaded_mask")
         return m.value
 
-    def run(self, layer, expert, gate, x, act=ACT_Q8, out=None):
-        """Synchronous host-memory run (fr_backend.run semantics).  Returns
-        (rc, y); on failure y is the untouched `out` (or None)."""
+    def run(self, layer, expert, gate, x, act=ACT_Q8, out=None, flags=0):
+        """Synchronous host-memory run (fr_backend.run semantics; flags:
+        frc_run_flags, RUN_PEER).  Returns (rc, y); on failure y is the
+        untouched `out` (or None)."""
         expert = np.ascontiguousarray(expert, np.uint16)
         gate = np.ascontiguousarray(gate, np.float32)
         x = np.ascontiguousarray(x, np.float32)
         tokens = x.shape[0]
         y = out if out is not None else np.zeros((tokens, self.hidden), np.float32)
-        rc = self.lib.frc_run(self.h, layer, tokens, _ptr(expert), _ptr(gate), _ptr(x), _ptr(y), act)
+        if flags:
+            rc = self.lib.frc_run_flags(self.h, layer, tokens, _ptr(expert), _ptr(gate), _ptr(x), _ptr(y), act, flags)
+        else:
+            rc = self.lib.frc_run(self.h, layer, tokens, _ptr(expert), _ptr(gate), _ptr(x), _ptr(y), act)
         return rc, y
 
     def run_device(self, layer, tokens, expert_ptr, gate_ptr, x_ptr, x_add_ptr, x_out_ptr, y_ptr, act=ACT_Q8,
@@ -412,16 +418,17 @@ class Context:
                                            x_out_ptr, y_ptr, act, flags, stream)
         self._check(rc, "run_device_fixed")
 
-    def host_pass(self, first_layer, expert, gate, h, act=ACT_Q8):
-        """Decode pass from the host (frc_host_pass).  expert: [layers][10] or
-        [layers][tokens][10]; h ([hidden] or [tokens][hidden], fp32) is updated in place."""
+    def host_pass(self, first_layer, expert, gate, h, act=ACT_Q8, flags=0):
+        """Decode pass from the host (frc_host_pass_flags).  expert: [layers][10] or
+        [layers][tokens][10]; h ([hidden] or [tokens][hidden], fp32) is updated in place.
+        flags: RUN_PEER sums every layer over the in-box reduce group."""
         expert = np.ascontiguousarray(expert, np.uint16)
         gate = np.ascontiguousarray(gate, np.float32)
         assert h.dtype == np.float32 and h.flags.c_contiguous
         tokens = expert.shape[1] if expert.ndim == 3 else 1
         hidden = h.shape[-1]
-        rc = self.lib.frc_host_pass(self.h, first_layer, expert.shape[0], tokens, _ptr(expert), _ptr(gate), _ptr(h),
-                                    hidden, act)
+        rc = self.lib.frc_host_pass_flags(self.h, first_layer, expert.shape[0], tokens, _ptr(expert), _ptr(gate),
+                                          _ptr(h), hidden, act, flags)
         self._check(rc, "host_pass")
 
     def peer_export(self, world):

@@ -1168,9 +1168,17 @@ static int validate(const frc_context* c, unsigned T, const uint16_t* expert, co
 
 int frc_run(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* expert, const float* gate, const float* x,
             float* y, int act) {
+  return frc_run_flags(c, layer, tokens, expert, gate, x, y, act, 0);
+}
+
+int frc_run_flags(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* expert, const float* gate,
+                  const float* x, float* y, int act, unsigned flags) {
   if (!c || !expert || !gate || !x || !y || tokens < 1 || tokens > FRC_MAX_PREFILL_TOKENS || layer >= c->g.layers ||
       (act != FRC_ACT_Q8 && act != FRC_ACT_F32))
     return fail(c, FRC_INVALID, "bad run arguments");
+  if (flags & ~unsigned(FRC_RUN_PEER)) return fail(c, FRC_INVALID, "frc_run_flags: only FRC_RUN_PEER");
+  if ((flags & FRC_RUN_PEER) && tokens > FRC_MAX_TOKENS)
+    return fail(c, FRC_UNSUPPORTED, "FRC_RUN_PEER: up to %u tokens a call", FRC_MAX_TOKENS);
   int rc = validate(c, tokens, expert, gate, x);
   if (rc) return fail(c, rc, "request rejected");
   CK(cudaSetDevice(c->device));
@@ -1190,7 +1198,8 @@ int frc_run(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* exp
     unsigned* d_st = reinterpret_cast<unsigned*>(c->d_in + st_off);
     rc = run_device(c, layer, tokens, reinterpret_cast<const uint16_t*>(c->d_in + xb + gb),
                     reinterpret_cast<const float*>(c->d_in + xb), reinterpret_cast<const float*>(c->d_in), nullptr,
-                    nullptr, reinterpret_cast<float*>(c->d_in + st_off + 16), act, 0, c->stream, nullptr, false, d_st);
+                    nullptr, reinterpret_cast<float*>(c->d_in + st_off + 16), act, flags, c->stream, nullptr, false,
+                    d_st);
     if (rc) return rc;
     c->last_T = tokens;
     memcpy(c->last_expert, expert, eb);

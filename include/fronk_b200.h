@@ -186,6 +186,13 @@ int frc_round_half(const float *x, size_t n, float *out);
  * referenced block even with gate 0, fp32 overflow), FRC_STATE (nothing loaded). */
 int frc_run(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *expert,
             const float *gate, const float *x, float *y, int act);
+/* frc_run with run flags; no counterpart in the reference.  The one flag
+ * taken is FRC_RUN_PEER (up to 16 tokens a call): y is the sum over every
+ * rank of the in-box reduce group (frc_peer_attach), so each process of a
+ * box can drive its share of the slices from host buffers; every rank makes
+ * the same sequence of calls. */
+int frc_run_flags(frc_context *c, unsigned layer, unsigned tokens, const uint16_t *expert,
+                  const float *gate, const float *x, float *y, int act, unsigned flags);
 
 /* Flags of frc_run_device.
  * FRC_RUN_X_BF16: x holds bf16 values ([tokens][d] 16-bit words, the upper
@@ -257,6 +264,12 @@ int frc_peer_detach(frc_context *c);
  * Not reentrant (static staging). */
 int frc_host_pass(frc_context *c, unsigned first_layer, unsigned layers, unsigned tokens,
                   const uint16_t *expert, const float *gate, float *h, unsigned hidden, int act);
+/* frc_host_pass through frc_run_flags (FRC_RUN_PEER: one process per GPU of
+ * a box, each holding its share of the slices, every layer summed over the
+ * ranks inside the kernel, so every rank's h stays identical). */
+int frc_host_pass_flags(frc_context *c, unsigned first_layer, unsigned layers, unsigned tokens,
+                        const uint16_t *expert, const float *gate, float *h, unsigned hidden, int act,
+                        unsigned flags);
 /* Waits for `stream`, returns and clears the device status (FRC_OK,
  * FRC_NUMERIC, FRC_INVALID for an out-of-range id, FRC_IO for a timed-out wait). */
 int frc_status(frc_context *c, void *stream);

@@ -5,7 +5,8 @@ oracle port over all 20 slices, and the reference's ref-q8) on both ranks,
 bit for bit the same on both.  The calls alternate one token (two CTAs an
 SM) with sixteen (one CTA an SM), so row ownership changes from launch to
 launch while the slots alternate by launch epoch.  Needs two GPUs; the IPC
-handles go over a gloo group (host channel only)."""
+handles go over a gloo group (host channel only).  The same calls through
+the host-buffer entry point (frc_run_flags) give the same bits."""
 import os
 import socket
 
@@ -61,6 +62,12 @@ def _rank(rank, world, port, q):
                                fb.ACT_Q8, fb.RUN_PEER, stream)
                 assert ctx.status(stream) == OK, ctx.last_error
                 ys.append(y.cpu().numpy())
+            # the same calls from host buffers (frc_run_flags, FRC_RUN_PEER):
+            # the same kernel and reduce, so the same bits
+            for i, (e, gate, x) in enumerate(cases):
+                rc, yh = ctx.run(layer, e, gate, x, flags=fb.RUN_PEER)
+                assert rc == OK, ctx.last_error
+                assert np.array_equal(yh.view(np.uint32), ys[i].view(np.uint32)), "host-buffer call differs"
             dist.barrier()
             ctx.peer_detach()
         gathered = [None] * world
