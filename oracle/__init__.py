@@ -49,6 +49,7 @@ class Oracle:
             "or_layer_bytes": (ctypes.c_size_t, [ctypes.c_uint, ctypes.c_uint, ctypes.c_uint]),
             "or_legacy_layer_bytes": (ctypes.c_size_t, [ctypes.c_uint]),
             "or_ref_run": (ctypes.c_int, [_vp, ctypes.c_uint, _vp, _vp, _vp, _vp, ctypes.c_int]),
+            "or_avx2_run": (ctypes.c_int, [_vp, ctypes.c_uint, _vp, _vp, _vp, _vp, ctypes.c_uint, ctypes.c_int]),
             "or_port_run": (ctypes.c_int, [_vp, ctypes.c_uint, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
             "or_prefill_run": (ctypes.c_int, [_vp, ctypes.c_uint, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t,
                                               _vp]),
@@ -116,6 +117,16 @@ class Oracle:
         y = np.zeros_like(x)
         rc = self.L.or_ref_run(ctypes.byref(m), x.shape[0], _p(np.ascontiguousarray(expert, np.uint16)),
                                _p(np.ascontiguousarray(gate, np.float32)), _p(x), _p(y), int(q8))
+        return rc, y
+
+    def avx2_run(self, m, expert, gate, x, workers=1, libm_expf=True):
+        """The AVX2 backend's arithmetic (backends/avx2.c) with `workers`
+        workers; libm_expf False gives the CUDA AVX2 mode's SiLU."""
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.zeros_like(x)
+        rc = self.L.or_avx2_run(ctypes.byref(m), x.shape[0], _p(np.ascontiguousarray(expert, np.uint16)),
+                                _p(np.ascontiguousarray(gate, np.float32)), _p(x), _p(y), int(workers),
+                                int(bool(libm_expf)))
         return rc, y
 
     def port_run(self, m, expert, gate, x, want_hidden=False):
@@ -219,6 +230,22 @@ class Reference:
     def backend(self, name):
         sym = {"ref": "fr_ref", "ref-q8": "fr_ref_q8", "avx2": "fr_avx2"}[name]
         return self.Backend.in_dll(self.L, sym)
+
+    def configure_avx2(self, blocks, workers):
+        """Fix fr_avx2's worker count for its next engine, which it makes at
+        the first load (backends/avx2.c:561-566, :729-742); no block may be
+        loaded.  Both reference builds are loaded RTLD_GLOBAL, so the
+        fr_avx2_close inside one build's fr_avx2_configure can bind to the
+        other build's: this build's engine is closed through its own handle
+        first."""
+        self.L.fr_avx2_set_tuning.argtypes = [ctypes.c_uint] * 4
+        self.L.fr_avx2_configure.argtypes = [ctypes.c_uint, ctypes.c_uint]
+        rc = self.L.fr_avx2_close()
+        if rc:
+            return rc
+        for burst in range(1, 9):
+            self.L.fr_avx2_set_tuning(blocks, burst, workers, 0)
+        return self.L.fr_avx2_configure(blocks, 1)
 
     def backend_addr(self, sym, lib=None):
         return ctypes.addressof(self.Backend.in_dll(lib or self.L, sym))

@@ -316,6 +316,221 @@ int or_ref_run(const or_model *m, unsigned tokens, const uint16_t *expert, const
     return OR_OK;
 }
 
+/* --------------------------------------------- the AVX2 backend's arithmetic */
+
+/* backends/avx2.c:184-203 (quantize8): one fp32 scale per `group` values,
+ * amax / 127; the values x * (127 / amax) rounded to nearest even and
+ * saturated to int8 (cvtps, packs); when s is not NULL the int16 sum of the
+ * rounded values of each 32. */
+static void avx2_quantize8(const float *x, unsigned n, unsigned group, int8_t *q, float *d, int16_t *s) {
+    for (unsigned i = 0; i < n; i += group) {
+        float amax = 0;
+        for (unsigned j = 0; j < group; ++j) {
+            const float a = fabsf(x[i + j]);
+            if (a > amax) amax = a;
+        }
+        d[i / group] = amax / 127.0f;
+        const float inv = amax != 0 ? 127.0f / amax : 0;
+        for (unsigned j = 0; j < group; j += 32) {
+            int sum = 0;
+            for (unsigned k = 0; k < 32; ++k) {
+                const int v = (int)nearbyintf(x[i + j + k] * inv);
+                sum += v;
+                q[i + j + k] = (int8_t)(v > 127 ? 127 : v < -128 ? -128 : v);
+            }
+            if (s) s[(i + j) / 32] = (int16_t)sum;
+        }
+    }
+}
+
+/* native_sum (backends/avx2.c:178-181): lanes i and i + 4 added, then two
+ * horizontal adds. */
+static float avx2_hsum8(const float v[8]) {
+    const float a0 = v[0] + v[4], a1 = v[1] + v[5], a2 = v[2] + v[6], a3 = v[3] + v[7];
+    return (a0 + a1) + (a2 + a3);
+}
+
+/* One Q4_K row against one token, as q4k_pair (backends/avx2.c:262-319)
+ * computes each of its two rows: per super-block eight int32 lanes (lane k:
+ * bytes 4k..4k+3 of every 32-byte nibble run, times the group scale), fmadd
+ * into eight fp32 lanes with d * xd; the min terms as four int32 lanes
+ * (mins of groups 2j, 2j+1 against the activation sums), fmadd with
+ * dmin * xd; result native_sum(lanes) - ((m0 + m1) + (m2 + m3)). */
+static float avx2_q4k_row(const uint8_t *row, const int8_t *xq, const float *xd, const int16_t *xs, unsigned d) {
+    float acc[8] = {0}, mins[4] = {0};
+    for (unsigned sb = 0; sb < d / 256; ++sb) {
+        const uint8_t *b = row + (size_t)sb * 144;
+        const float dd = or_f16(le16(b)), dm = or_f16(le16(b + 2));
+        unsigned sc[8], mi[8];
+        for (unsigned g = 0; g < 8; ++g) q4k_scale_min(b + 4, g, &sc[g], &mi[g]);
+        int32_t is[8] = {0};
+        for (unsigned gp = 0; gp < 4; ++gp) {
+            const uint8_t *qs = b + 16 + gp * 32;
+            const int8_t *xl = xq + sb * 256 + gp * 64, *xh = xl + 32;
+            for (unsigned k = 0; k < 8; ++k) {
+                int32_t lo = 0, hi = 0;
+                for (unsigned i = 0; i < 4; ++i) {
+                    lo += (qs[4 * k + i] & 15) * xl[4 * k + i];
+                    hi += (qs[4 * k + i] >> 4) * xh[4 * k + i];
+                }
+                is[k] += (int32_t)sc[2 * gp] * lo + (int32_t)sc[2 * gp + 1] * hi;
+            }
+        }
+        const float dxd = dd * xd[sb], mxd = dm * xd[sb];
+        for (unsigned k = 0; k < 8; ++k) acc[k] = fmaf((float)is[k], dxd, acc[k]);
+        for (unsigned j = 0; j < 4; ++j) {
+            const int32_t mm = (int32_t)mi[2 * j] * xs[sb * 8 + 2 * j] + (int32_t)mi[2 * j + 1] * xs[sb * 8 + 2 * j + 1];
+            mins[j] = fmaf((float)mm, mxd, mins[j]);
+        }
+    }
+    return avx2_hsum8(acc) - ((mins[0] + mins[1]) + (mins[2] + mins[3]));
+}
+
+/* One Q8_0 row (reference bytes) against one token, the Q8_0 branch of row4
+ * (backends/avx2.c:239-247): per 32-block eight int32 lanes of four products,
+ * fmadd into eight fp32 lanes with d * xd of the super-block; a nonfinite
+ * block scale is NUMERIC. */
+static int avx2_q80_row(const uint8_t *row, const int8_t *xq, const float *xd, unsigned d, float *out) {
+    float acc[8] = {0};
+    for (unsigned blk = 0; blk < d / 32; ++blk) {
+        const uint8_t *b = row + (size_t)blk * 34;
+        const float sc = or_f16(le16(b));
+        if (!isfinite(sc)) return OR_NUMERIC;
+        const float s = sc * xd[blk / 8];
+        for (unsigned j = 0; j < 8; ++j) {
+            int32_t dot = 0;
+            for (unsigned i = 0; i < 4; ++i) dot += (int8_t)b[2 + 4 * j + i] * xq[blk * 32 + 4 * j + i];
+            acc[j] = fmaf((float)dot, s, acc[j]);
+        }
+    }
+    *out = avx2_hsum8(acc);
+    return OR_OK;
+}
+
+/* The SiLU product of native_job (backends/avx2.c:427-429), fp32 throughout.
+ * libm_expf selects the C library's expf, as the backend calls it; otherwise
+ * exp in double rounded once to fp32 (the correctly rounded value but for
+ * double-rounding ties), the CUDA path's form. */
+static float avx2_swiglu(float v, float u, int libm_expf) {
+    const float e = libm_expf ? expf(-v) : (float)exp(-(double)v);
+    return v / (1 + e) * u;
+}
+
+/* backends/avx2.c:615-715 (run) and :404-458 (native_job) with the default
+ * build (no ranked or union mode): x quantized per 256; experts in the
+ * order the tokens first name them (routed ranks 0-9, then the shared expert
+ * when its gate is nonzero); jobs (block, expert) block-major over the loaded
+ * blocks in ascending order, dealt round robin to `workers` workers; each
+ * worker accumulates its jobs' down terms with fmadd into its own zeroed
+ * output in job order, and y is the fp32 sum of the workers' outputs in
+ * worker order.  Gate/up: Q4_K routed rows, Q8_0 shared rows; hidden slice
+ * quantized per 32; down: MXFP4 routed, Q8_0 shared. */
+int or_avx2_run(const or_model *m, unsigned tokens, const uint16_t *expert, const float *gate,
+                const float *x, float *y, unsigned workers, int libm_expf) {
+    if (!model_ok(m) || m->legacy || m->gate_type != OR_Q4_K || m->down_type != OR_MXFP4 || !y || !workers ||
+        workers > 32)
+        return OR_INVALID;
+    const unsigned d = m->hidden;
+    int rc = validate(d, tokens, expert, gate, x);
+    if (rc) return rc;
+    if (!any_loaded(m)) return OR_STATE;
+    if (d > 8192) return OR_INVALID;
+    unsigned blocks[OR_BLOCKS], nb = 0;
+    for (unsigned b = 0; b < OR_BLOCKS; ++b) if (m->layer[b]) blocks[nb++] = b;
+    /* experts in first-named order, per-token gates and token masks */
+    enum { MAXE = OR_MAX_TOKENS * OR_ACTIVE };
+    unsigned ids[MAXE], mask[MAXE], ne = 0;
+    float eg[MAXE][OR_MAX_TOKENS];
+    for (unsigned t = 0; t < tokens; ++t)
+        for (unsigned j = 0; j < OR_ACTIVE; ++j) {
+            const float g = gate[(size_t)t * OR_ACTIVE + j];
+            if (j == OR_TOPK && g == 0) continue;
+            const unsigned id = j == OR_TOPK ? OR_SHARED : expert[(size_t)t * OR_TOPK + j];
+            unsigned e = 0;
+            while (e < ne && ids[e] != id) ++e;
+            if (e == ne) { ids[ne] = id; mask[ne] = 0; ++ne; }
+            mask[e] |= 1u << t;
+            eg[e][t] = g;
+        }
+    int8_t *xq = malloc((size_t)tokens * d);
+    float *xd = malloc(sizeof(float) * tokens * (d / 256));
+    int16_t *xs = malloc(sizeof(int16_t) * tokens * (d / 32));
+    float *out = calloc((size_t)workers * tokens * d, sizeof(float));
+    if (!xq || !xd || !xs || !out) { rc = OR_INVALID; goto done; }
+    for (unsigned t = 0; t < tokens; ++t)
+        avx2_quantize8(x + (size_t)t * d, d, 256, xq + (size_t)t * d, xd + t * (d / 256), xs + t * (d / 32));
+    const size_t slice = or_slice_bytes(d, OR_Q4_K, OR_MXFP4), row = or_row_bytes(OR_Q4_K, d);
+    const size_t srow = or_row_bytes(OR_Q8_0, d);
+    const unsigned jobs = nb * ne;
+    for (unsigned w = 0; w < workers; ++w)
+        for (unsigned index = w; index < jobs; index += workers) {
+            const unsigned e = index % ne, id = ids[e];
+            const int shared = id == OR_SHARED;
+            const uint8_t *p = m->layer[blocks[index / ne]] + (size_t)id * slice;
+            const size_t in_row = shared ? srow : row, proj = OR_NEURONS * in_row;
+            float *o = out + (size_t)w * tokens * d;
+            for (unsigned t = 0; t < tokens; ++t) {
+                if (!(mask[e] >> t & 1)) continue;
+                const int8_t *q = xq + (size_t)t * d;
+                float h[OR_NEURONS], md;
+                int8_t mid[OR_NEURONS];
+                for (unsigned n = 0; n < OR_NEURONS; ++n) {
+                    float a, u;
+                    if (shared) {
+                        if (avx2_q80_row(p + n * in_row, q, xd + t * (d / 256), d, &a) ||
+                            avx2_q80_row(p + proj + n * in_row, q, xd + t * (d / 256), d, &u)) {
+                            rc = OR_NUMERIC;
+                            goto done;
+                        }
+                    } else {
+                        a = avx2_q4k_row(p + n * in_row, q, xd + t * (d / 256), xs + t * (d / 32), d);
+                        u = avx2_q4k_row(p + proj + n * in_row, q, xd + t * (d / 256), xs + t * (d / 32), d);
+                    }
+                    h[n] = avx2_swiglu(a, u, libm_expf);
+                }
+                for (unsigned n = 0; n < OR_NEURONS; ++n)
+                    if (!isfinite(h[n])) { rc = OR_NUMERIC; goto done; }
+                avx2_quantize8(h, OR_NEURONS, OR_NEURONS, mid, &md, NULL);
+                const float c = md * eg[e][t];
+                const uint8_t *down = p + 2 * proj;
+                for (unsigned r = 0; r < d; ++r) {
+                    int32_t sum = 0;
+                    float yr;
+                    if (shared) {
+                        const uint8_t *b = down + (size_t)r * 34;
+                        const float sc = or_f16(le16(b));
+                        if (!isfinite(sc)) { rc = OR_NUMERIC; goto done; }
+                        for (unsigned n = 0; n < OR_NEURONS; ++n) sum += (int8_t)b[2 + n] * mid[n];
+                        yr = (float)sum * sc;
+                    } else {
+                        /* down8_mxfp4 (backends/avx2.c:331-362): the scale
+                         * byte e gives 2^(e-127) (e = 0: 2^-127), halved */
+                        const uint8_t *b = down + (size_t)r * 17;
+                        const uint32_t bits = b[0] ? (uint32_t)b[0] << 23 : 0x00400000u;
+                        float rs;
+                        memcpy(&rs, &bits, sizeof rs);
+                        rs *= .5f;
+                        for (unsigned j = 0; j < 16; ++j)
+                            sum += kE2M1x2[b[1 + j] & 15] * mid[j] + kE2M1x2[b[1 + j] >> 4] * mid[j + 16];
+                        yr = (float)sum * rs;
+                    }
+                    o[(size_t)t * d + r] = fmaf(yr, c, o[(size_t)t * d + r]);
+                }
+            }
+        }
+    for (unsigned t = 0; t < tokens; ++t)
+        for (unsigned r = 0; r < d; ++r) {
+            float v = 0;
+            for (unsigned w = 0; w < workers; ++w) v += out[((size_t)w * tokens + t) * d + r];
+            if (!isfinite(v)) { rc = OR_NUMERIC; goto done; }
+            out[(size_t)t * d + r] = v;  /* worker 0's row is no longer read */
+        }
+    memcpy(y, out, (size_t)tokens * d * sizeof(float));
+done:
+    free(xq); free(xd); free(xs); free(out);
+    return rc;
+}
+
 /* ------------------------------------------------------ GPU Q8 arithmetic */
 
 /* Integer dot of one 32-weight block against 32 int8 activations. */

@@ -64,6 +64,17 @@ size_t or_legacy_layer_bytes(unsigned hidden);
 int or_ref_run(const or_model *m, unsigned tokens, const uint16_t *expert, const float *gate,
                const float *x, float *y, int q8);
 
+/* The reference's AVX2 backend (backends/avx2.c, default build) restated
+ * portably: int8 activations with one fp32 scale per 256 and int16 sums per
+ * 32, its lane-wise fp32 accumulation and horizontal-add order, fp32 SiLU,
+ * the hidden slice per 32, jobs dealt round robin to `workers` workers
+ * (1-32) and the workers' outputs summed in order.  Native Q4_K / MXFP4
+ * layout only.  libm_expf = 1 uses the C library's expf (bit-identical to
+ * the compiled backend at the same worker count); 0 uses exp in double
+ * rounded to fp32, the CUDA path's form.  y is written only on OR_OK. */
+int or_avx2_run(const or_model *m, unsigned tokens, const uint16_t *expert, const float *gate,
+                const float *x, float *y, unsigned workers, int libm_expf);
+
 /* The CUDA Q8 path's arithmetic.  y as above.  When h is not NULL it receives
  * the hidden activations in the kernel's item order
  * [unique expert][loaded block][token][32] (zeros for tokens not routed to the

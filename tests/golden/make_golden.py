@@ -1,6 +1,8 @@
 """Generates tests/golden/native_ref.npz: outputs of the reference's own
-"ref" and "ref-q8" backends (backends/ref.c, compiled from the reference's
-sources into oracle/_ref by oracle/build.py) on seeded native-format units.
+"ref" and "ref-q8" backends (backends/ref.c) and of its AVX2 backend
+(backends/avx2.c) with one and with four workers, all compiled from the
+reference's sources into oracle/_ref by oracle/build.py, on seeded
+native-format units.
 
 The reference commits golden vectors only for its legacy Q4_0 layout
 (tests/vectors); these fixtures pin the native Q4_K + MXFP4 path at the
@@ -75,6 +77,21 @@ def generate(hidden):
         for be in backs.values():
             for b in units:
                 be.unload(b)
+    avx2 = ref.backend("avx2")
+    try:
+        for workers in (1, 4):
+            assert ref.configure_avx2(len(BLOCKS), workers) == OK
+            for b in BLOCKS:  # ascending: the backend's job order follows load order
+                assert avx2.load(b, units[b].addr, ref.unit_bytes()) == OK
+            try:
+                for i, (e, gt, x) in enumerate(cases):
+                    rc, y = ref.run(avx2, ref.request(LAYER, e, gt, x))
+                    assert rc == OK, ("avx2", workers, rc)
+                    out["d%d_c%d_y_avx2_w%d" % (hidden, i, workers)] = y
+            finally:
+                for b in BLOCKS:
+                    avx2.unload(b)
+    finally:
         for u in units.values():
             u.close()
     out["d%d_weights_sha256" % hidden] = np.array(weights_digest(layers))

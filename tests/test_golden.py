@@ -1,6 +1,7 @@
 """Parity against the committed golden outputs of the reference's own "ref"
-and "ref-q8" backends (tests/golden/native_ref.npz, written by
-tests/golden/make_golden.py from the reference compiled from its sources).
+and "ref-q8" backends and of its AVX2 backend with one and four workers
+(tests/golden/native_ref.npz, written by tests/golden/make_golden.py from the
+reference compiled from its sources).
 These pin the native Q4_K + MXFP4 path where the reference itself is absent:
 the oracle bit for bit on the CPU, the CUDA path on the GPU."""
 import hashlib
@@ -51,6 +52,20 @@ def test_oracle_reproduces_reference_goldens(oracle, hidden):
         assert rc == OK and np.array_equal(y.view(np.uint32), y_ref.view(np.uint32))
         rc, y = oracle.ref_run(m, e, gt, x, 1)
         assert rc == OK and np.array_equal(y.view(np.uint32), y_q8.view(np.uint32))
+
+
+@pytest.mark.parametrize("hidden", [2560, 2048])
+def test_oracle_reproduces_avx2_goldens(oracle, hidden):
+    """or_avx2_run with the C library's expf is the AVX2 backend bit for bit
+    at its worker count."""
+    z = _load()
+    _, layers, cases = _layers(z, hidden)
+    m = oracle.model(hidden, Q4_K, MXFP4, layers)
+    for i, (e, gt, x, _, _) in enumerate(cases):
+        for workers in (1, 4):
+            rc, y = oracle.avx2_run(m, e, gt, x, workers=workers, libm_expf=True)
+            want = z["d%d_c%d_y_avx2_w%d" % (hidden, i, workers)]
+            assert rc == OK and np.array_equal(y.view(np.uint32), want.view(np.uint32)), (i, workers)
 
 
 @pytest.mark.gpu
