@@ -17,7 +17,7 @@ LIB_PATH = os.environ.get("FRONK_B200_LIB") or os.path.join(HERE, "libfronk_b200
 OK, INVALID, STATE, NUMERIC, IO, UNSUPPORTED, MISMATCH = 0, -1, -2, -3, -4, -5, -6
 # src/native.h:8
 Q8_0, Q4_K, MXFP4 = 8, 12, 39
-ACT_F32, ACT_Q8 = 0, 1
+ACT_F32, ACT_Q8, ACT_AVX2 = 0, 1, 2
 RUN_RMSNORM = 1
 RUN_OVERLAP = 2
 RUN_PEER = 4
@@ -66,6 +66,7 @@ _SIGS = {
     "frc_refresh_layer": (_int, [_vp, _int, _u32, _vp, _sz]),
     "frc_probe_device": (_int, [_int, ctypes.c_char_p, _sz, _vp, _vp]),
     "frc_set_wait_limit": (_int, [_vp, _u64]),
+    "frc_set_avx2_workers": (_int, [_vp, ctypes.c_uint]),
     "frc_debug_barrier_extra": (_int, [_vp, _u32]),
     "frc_debug_layer_variant": (_int, [_vp, _int]),
     "frc_unload_unit": (_int, [_vp, _int]),
@@ -112,7 +113,8 @@ _SIGS = {
     "frc_prefill_times": (_int, [_vp, _vp]),
     "frc_debug_phases": (_int, [_vp, _vp, _sz, _vp]),
 }
-EXPORTS = sorted(_SIGS) + ["fr_cuda", "fr_cuda_f32", "fr_cuda_select_device", "fr_cuda_close"]
+EXPORTS = sorted(_SIGS) + ["fr_cuda", "fr_cuda_f32", "fr_cuda_avx2", "fr_cuda_select_device", "fr_cuda_close",
+                          "fr_cuda_avx2_workers"]
 
 
 def library():
@@ -370,6 +372,10 @@ class Context:
     def refresh_layer(self, block, layer, data):
         """frc_refresh_layer: copy one loaded layer again from host memory."""
         return self.lib.frc_refresh_layer(self.h, block, layer, _ptr(data), data.nbytes)
+
+    def set_avx2_workers(self, workers):
+        """frc_set_avx2_workers: the AVX2 backend worker count ACT_AVX2 reproduces."""
+        self._check(self.lib.frc_set_avx2_workers(self.h, int(workers)), "set_avx2_workers")
 
     def set_wait_limit(self, ns):
         """frc_set_wait_limit: every bounded wait of the layer kernel gives up after ns."""

@@ -25,9 +25,10 @@
 #ifdef FR_USE_REFERENCE_HEADERS
 #include "backend.h"
 #include "native.h"
-extern const fr_backend fr_cuda, fr_cuda_f32;
+extern const fr_backend fr_cuda, fr_cuda_f32, fr_cuda_avx2;
 int fr_cuda_select_device(int device);
 int fr_cuda_close(const fr_backend *backend);
+int fr_cuda_avx2_workers(unsigned workers);
 #else
 #include "../../include/fr_backend_abi.h"
 #endif
@@ -47,7 +48,9 @@ typedef struct {
     const unsigned char *unit[FR_BLOCKS];
 } slot_state;
 
-static slot_state q8_state = {NULL, FRC_ACT_Q8, {0}, {0}, {0}}, f32_state = {NULL, FRC_ACT_F32, {0}, {0}, {0}};
+static slot_state q8_state = {NULL, FRC_ACT_Q8, {0}, {0}, {0}}, f32_state = {NULL, FRC_ACT_F32, {0}, {0}, {0}},
+                  avx2_state = {NULL, FRC_ACT_AVX2, {0}, {0}, {0}};
+static unsigned avx2_workers = 1; /* fr_cuda_avx2's worker count (frc_set_avx2_workers) */
 
 /* 1 when any page of [p, p + len) is mapped writable (from /proc/self/maps;
  * 1 as well when that cannot be read: refreshing is the safe side). */
@@ -69,7 +72,7 @@ static int range_writable(const void *p, size_t len) {
 static int device_index = 0;
 
 static slot_state *state_of(const fr_backend *b) {
-    return b == &fr_cuda ? &q8_state : b == &fr_cuda_f32 ? &f32_state : NULL;
+    return b == &fr_cuda ? &q8_state : b == &fr_cuda_f32 ? &f32_state : b == &fr_cuda_avx2 ? &avx2_state : NULL;
 }
 static int any_loaded(const slot_state *s) {
     for (unsigned b = 0; b < FR_BLOCKS; ++b) if (s->loaded[b]) return 1;
@@ -82,9 +85,17 @@ static frc_geometry reference_geometry(void) {
 
 int fr_cuda_select_device(int device) {
     if (device < 0) return FR_INVALID;
-    if (q8_state.ctx || f32_state.ctx) return FR_STATE;
+    if (q8_state.ctx || f32_state.ctx || avx2_state.ctx) return FR_STATE;
     device_index = device;
     return FR_OK;
+}
+
+/* The worker count whose job dealing and summation order fr_cuda_avx2
+ * reproduces (fr_avx2 takes it from fr_avx2_configure, backends/avx2.c:732-742). */
+int fr_cuda_avx2_workers(unsigned workers) {
+    if (workers < 1 || workers > 32) return FR_INVALID;
+    avx2_workers = workers;
+    return avx2_state.ctx ? frc_set_avx2_workers(avx2_state.ctx, workers) : FR_OK;
 }
 
 int fr_cuda_close(const fr_backend *backend) {
@@ -122,6 +133,7 @@ static int load(slot_state *s, int block, const void *data, size_t len) {
     if (!s->ctx) {
         int rc = frc_open(device_index, &g, &s->ctx);
         if (rc) return rc;
+        if (s->act == FRC_ACT_AVX2 && (rc = frc_set_avx2_workers(s->ctx, avx2_workers))) return rc;
     }
     int rc = frc_load_unit(s->ctx, block, data, len);
     if (!rc) {
@@ -228,6 +240,14 @@ static int q8_bench(int b, fr_costmodel *o) { return bench(&fr_cuda, b, o); }
 static int f32_bench(int b, fr_costmodel *o) { return bench(&fr_cuda_f32, b, o); }
 static int q8_test(const char *d) { return self_test(&fr_cuda, d); }
 static int f32_test(const char *d) { return self_test(&fr_cuda_f32, d); }
+static int avx2_load(int b, const void *p, size_t n) { return load(&avx2_state, b, p, n); }
+static int avx2_unload(int b) { return unload(&avx2_state, b); }
+static int avx2_run(const fr_req *r, fr_part *o) { return run(&avx2_state, r, o); }
+static int avx2_bench(int b, fr_costmodel *o) { return bench(&fr_cuda_avx2, b, o); }
+static int avx2_test(const char *d) { return self_test(&fr_cuda_avx2, d); }
 
 const fr_backend fr_cuda = {"cuda", probe, q8_load, q8_unload, q8_run, q8_bench, q8_test};
 const fr_backend fr_cuda_f32 = {"cuda-f32", probe, f32_load, f32_unload, f32_run, f32_bench, f32_test};
+/* The arithmetic of the reference's AVX2 backend (FRC_ACT_AVX2): a drop-in for
+ * fr_avx2 whose results equal its own at the same worker count. */
+const fr_backend fr_cuda_avx2 = {"cuda-avx2", probe, avx2_load, avx2_unload, avx2_run, avx2_bench, avx2_test};

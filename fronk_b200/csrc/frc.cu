@@ -26,6 +26,7 @@ using namespace frc;
 #include "frc_layer_rb.cuh"
 #include "frc_umma.cuh"
 #include "frc_prefill.cuh"
+#include "frc_avx2.cuh"
 #include "frc_units.h"
 
 // ===================================================== set-up kernels
@@ -218,6 +219,15 @@ struct frc_context {
   uint8_t *d_in = nullptr, *d_out = nullptr, *h_in = nullptr, *h_out = nullptr, *h_out_dev = nullptr;
   float *d_y = nullptr, *h_y = nullptr;  // inside d_out / h_out
   unsigned* h_status = nullptr;          // start of h_out
+
+  // FRC_ACT_AVX2: the activation quantization [T][d] int8, [T][d/256] f32,
+  // [T][d/32] i16 (kMaxTokens rows each), the worker count whose job
+  // dealing it reproduces, and the blocks in load order (the AVX2 backend's
+  // job order: appended at load, ascending again after an unload)
+  uint8_t* avx2_x = nullptr;
+  unsigned avx2_workers = 1;
+  uint8_t slot_order[FRC_MAX_BLOCKS] = {};
+  unsigned slot_count = 0;
 
   cudaStream_t stream = nullptr;
   uint8_t* pool = nullptr;
@@ -622,6 +632,7 @@ static int run_device(frc_context* c, unsigned layer, unsigned T, const uint16_t
                       cudaStream_t s, const RunScratch* scratch = nullptr, bool chunks = false,
                       unsigned* status = nullptr) {
   if (!c || !expert || !gate || !x || !y) return fail(c, FRC_INVALID, "null argument");
+  if (act == FRC_ACT_AVX2) return fail(c, FRC_UNSUPPORTED, "FRC_ACT_AVX2: through frc_run (host buffers) only");
   if (act != FRC_ACT_Q8 && act != FRC_ACT_F32) return fail(c, FRC_INVALID, "unknown activation mode");
   if (T > FRC_MAX_TOKENS) return run_long(c, layer, T, expert, gate, x, x_add, x_out, y, act, flags, s, scratch, chunks);
   if (flags & FRC_RUN_X_BF16)
@@ -969,6 +980,7 @@ int frc_open(int device, const frc_geometry* g, frc_context** out) {
   alloc(reinterpret_cast<void**>(&c->hidden), kHiddenBytes);
   alloc(reinterpret_cast<void**>(&c->partial), sizeof(float) * kMaxPairs * kMaxBlocks * d);
   alloc(reinterpret_cast<void**>(&c->gsv), sizeof(float) * kMaxPairs * kMaxBlocks);
+  alloc(reinterpret_cast<void**>(&c->avx2_x), kMaxTokens * (static_cast<size_t>(d) + d / 256 * 4 + d / 32 * 2));
   alloc(reinterpret_cast<void**>(&c->ctl), sizeof(LayerCtl));
   alloc(reinterpret_cast<void**>(&c->xchg), sizeof(float) * kMaxUnique * 32);
   alloc(reinterpret_cast<void**>(&c->xcnt), sizeof(unsigned) * kMaxUnique);
@@ -1043,7 +1055,7 @@ int frc_close(frc_context* c) {
   cudaFree(c->d_in); cudaFree(c->d_out); cudaFree(c->pool);
   cudaFree(c->pf_xq); cudaFree(c->pf_xr); cudaFree(c->pf_xs); cudaFree(c->pf_xme); cudaFree(c->pf_pair_token); cudaFree(c->pf_slot_pair); cudaFree(c->pf_counts);
   cudaFree(c->pf_items_gu); cudaFree(c->pf_items_dn); cudaFree(c->pf_hq); cudaFree(c->pf_hs); cudaFree(c->pf_ye);
-  cudaFree(c->pf_xvr); cudaFree(c->pf_xqn); cudaFree(c->pf_xrn);
+  cudaFree(c->pf_xvr); cudaFree(c->pf_xqn); cudaFree(c->pf_xrn); cudaFree(c->avx2_x);
   cudaFreeHost(c->h_in); cudaFreeHost(c->h_out);
   if (c->stream) cudaStreamDestroy(c->stream);
   for (auto e : c->pf_ev) if (e) cudaEventDestroy(e);
@@ -1059,8 +1071,14 @@ static SliceShape shape_of(const frc_context* c) {
   return s;
 }
 
+// Allocates the region of (block, layer) if it is not there; a block's first
+// region appends the block to the load order.
 static int ensure_layer(frc_context* c, int block, unsigned layer) {
-  if (!c->layer_ptr[block][layer]) CK(cudaMalloc(&c->layer_ptr[block][layer], c->layer_bytes));
+  if (c->layer_ptr[block][layer]) return FRC_OK;
+  bool first = true;
+  for (unsigned l = 0; l < FRC_MAX_LAYERS; ++l) first &= c->layer_ptr[block][l] == nullptr;
+  CK(cudaMalloc(&c->layer_ptr[block][layer], c->layer_bytes));
+  if (first) c->slot_order[c->slot_count++] = static_cast<uint8_t>(block);
   return FRC_OK;
 }
 
@@ -1120,6 +1138,12 @@ int frc_unload_unit(frc_context* c, int block) {
       c->layer_ptr[block][l] = nullptr;
       any = true;
     }
+  // the remaining blocks ascending, as the AVX2 backend rebuilds its slots
+  // after an unload (backends/avx2.c:607-613)
+  c->slot_count = 0;
+  for (unsigned b = 0; b < FRC_MAX_BLOCKS; ++b)
+    for (unsigned l = 0; l < FRC_MAX_LAYERS; ++l)
+      if (c->layer_ptr[b][l]) { c->slot_order[c->slot_count++] = static_cast<uint8_t>(b); break; }
   return any ? FRC_OK : fail(c, FRC_STATE, "block %d not loaded", block);
 }
 
@@ -1181,6 +1205,121 @@ static int validate(const frc_context* c, unsigned T, const uint16_t* expert, co
   return FRC_OK;
 }
 
+// The end of a call of up to FRC_MAX_TOKENS tokens whose status word and y
+// sit at d_in + st_off: the publish kernel stores [status][y] into the mapped
+// h_out, the stream is synchronised, and y is handed over only when the
+// status is clean.
+static int finish_small(frc_context* c, size_t st_off, size_t xb, float* y) {
+  const unsigned n16 = static_cast<unsigned>((16 + xb) / 16);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(std::min(8u, (n16 + 1023) / 1024));  // up to 8 CTAs of 512 threads
+  cfg.blockDim = dim3(512);
+  cfg.stream = c->stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CK(cudaLaunchKernelEx(&cfg, publish_kernel, reinterpret_cast<const uint4*>(c->d_in + st_off),
+                        reinterpret_cast<uint4*>(c->h_out_dev), n16));
+  CK(cudaStreamSynchronize(c->stream));
+  const unsigned st = *c->h_status;
+  if (st & kStTimeout) {
+    const int rrc = reset_after_timeout(c, c->stream);
+    if (rrc) return rrc;
+  }
+  if (status_code(st)) return fail(c, status_code(st), "device status 0x%x", st);
+  memcpy(y, c->h_y, xb);  // published only after the whole layer succeeded
+  return FRC_OK;
+}
+
+// FRC_ACT_AVX2 (frc_avx2.cuh) through host buffers: the experts in the order
+// the tokens first name them (routed ranks 0-9, then the shared expert when
+// its gate is nonzero: backends/avx2.c:660-672), their token masks and the
+// (expert, token) pairs are planned here and travel in the request's copy:
+// [x][plan] then the status word and y.
+static int run_avx2(frc_context* c, unsigned layer, unsigned T, const uint16_t* expert, const float* gate,
+                    const float* x, float* y, unsigned flags) {
+  if (flags) return fail(c, FRC_UNSUPPORTED, "FRC_ACT_AVX2 takes no run flags");
+  if (T > FRC_MAX_TOKENS) return fail(c, FRC_UNSUPPORTED, "FRC_ACT_AVX2: up to %u tokens a call", FRC_MAX_TOKENS);
+  if (c->g.gate_type != FRC_Q4_K || c->g.down_type != FRC_MXFP4)
+    return fail(c, FRC_UNSUPPORTED, "FRC_ACT_AVX2: the reference's native layout (Q4_K gate/up, MXFP4 down) only");
+  int rc = validate(c, T, expert, gate, x);
+  if (rc) return fail(c, rc, "request rejected");
+  CK(cudaSetDevice(c->device));
+  Avx2Params a{};
+  unsigned S = 0;
+  for (unsigned i = 0; i < c->slot_count; ++i) {
+    const unsigned b = c->slot_order[i];
+    if (!c->layer_ptr[b][layer]) return fail(c, FRC_STATE, "block %u is loaded but not layer %u", b, layer);
+    a.base[S++] = c->layer_ptr[b][layer];
+  }
+  if (!S) return fail(c, FRC_STATE, "no block loaded");
+  uint16_t ids[kMaxPairs], pbase[kMaxPairs];
+  uint32_t mask[kMaxPairs];
+  float eg[kMaxPairs][kMaxTokens], pgate[kMaxPairs];
+  unsigned E = 0, P = 0;
+  for (unsigned t = 0; t < T; ++t)
+    for (unsigned j = 0; j < FRC_ACTIVE; ++j) {
+      const float g = gate[t * FRC_ACTIVE + j];
+      if (j == FRC_TOPK && g == 0) continue;
+      const unsigned id = j == FRC_TOPK ? FRC_ROUTED_EXPERTS : expert[t * FRC_TOPK + j];
+      unsigned e = 0;
+      while (e < E && ids[e] != id) ++e;
+      if (e == E) {
+        ids[E] = static_cast<uint16_t>(id);
+        mask[E++] = 0;
+      }
+      mask[e] |= 1u << t;
+      eg[e][t] = g;
+    }
+  for (unsigned e = 0; e < E; ++e) {
+    pbase[e] = static_cast<uint16_t>(P);
+    for (unsigned t = 0; t < T; ++t)
+      if (mask[e] >> t & 1u) pgate[P++] = eg[e][t];
+  }
+  const unsigned d = c->g.hidden;
+  const size_t xb = sizeof(float) * T * d, po = (xb + 15) & ~size_t(15);
+  const size_t st_off = (po + 12 * kMaxPairs + 15) & ~size_t(15);
+  uint8_t* h = c->h_in;
+  memcpy(h, x, xb);
+  memcpy(h + po, mask, 4 * E);
+  memcpy(h + po + 4 * kMaxPairs, pgate, 4 * P);
+  memcpy(h + po + 8 * kMaxPairs, ids, 2 * E);
+  memcpy(h + po + 10 * kMaxPairs, pbase, 2 * E);
+  memset(h + st_off, 0, 16);
+  CK(cudaMemcpyAsync(c->d_in, h, st_off + 16, cudaMemcpyHostToDevice, c->stream));
+  const uint8_t* dp = c->d_in + po;
+  a.x = reinterpret_cast<const float*>(c->d_in);
+  a.mask = reinterpret_cast<const uint32_t*>(dp);
+  a.pgate = reinterpret_cast<const float*>(dp + 4 * kMaxPairs);
+  a.ids = reinterpret_cast<const uint16_t*>(dp + 8 * kMaxPairs);
+  a.pbase = reinterpret_cast<const uint16_t*>(dp + 10 * kMaxPairs);
+  a.xq = reinterpret_cast<int8_t*>(c->avx2_x);
+  a.xd = reinterpret_cast<float*>(c->avx2_x + static_cast<size_t>(kMaxTokens) * d);
+  a.xs = reinterpret_cast<int16_t*>(c->avx2_x + static_cast<size_t>(kMaxTokens) * (d + d / 256 * 4));
+  a.terms = c->partial;
+  a.coef = c->gsv;
+  a.status = reinterpret_cast<unsigned*>(c->d_in + st_off);
+  a.y = reinterpret_cast<float*>(c->d_in + st_off + 16);
+  a.d = d; a.T = T; a.S = S; a.E = E; a.P = P; a.W = c->avx2_workers;
+  a.row_bytes = static_cast<unsigned>(c->row_bytes); a.proj_bytes = static_cast<unsigned>(c->proj_bytes);
+  a.slice_bytes = static_cast<unsigned>(c->slice_bytes);
+  a.shared_row = static_cast<unsigned>(c->shared_row); a.shared_proj = static_cast<unsigned>(c->shared_proj);
+  avx2_quantize_kernel<<<T, 256, 0, c->stream>>>(a);
+  avx2_job_kernel<<<S * E, 256, 0, c->stream>>>(a);
+  avx2_reduce_kernel<<<(T * d + 255) / 256, 256, 0, c->stream>>>(a);
+  CK(cudaGetLastError());
+  c->launches += 3;
+  return finish_small(c, st_off, xb, y);
+}
+
+int frc_set_avx2_workers(frc_context* c, unsigned workers) {
+  if (!c || workers < 1 || workers > 32) return fail(c, FRC_INVALID, "FRC_ACT_AVX2 workers: 1-32");
+  c->avx2_workers = workers;
+  return FRC_OK;
+}
+
 int frc_run(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* expert, const float* gate, const float* x,
             float* y, int act) {
   return frc_run_flags(c, layer, tokens, expert, gate, x, y, act, 0);
@@ -1189,9 +1328,10 @@ int frc_run(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* exp
 int frc_run_flags(frc_context* c, unsigned layer, unsigned tokens, const uint16_t* expert, const float* gate,
                   const float* x, float* y, int act, unsigned flags) {
   if (!c || !expert || !gate || !x || !y || tokens < 1 || tokens > FRC_MAX_PREFILL_TOKENS || layer >= c->g.layers ||
-      (act != FRC_ACT_Q8 && act != FRC_ACT_F32))
+      (act != FRC_ACT_Q8 && act != FRC_ACT_F32 && act != FRC_ACT_AVX2))
     return fail(c, FRC_INVALID, "bad run arguments");
   if (flags & ~unsigned(FRC_RUN_PEER)) return fail(c, FRC_INVALID, "frc_run_flags: only FRC_RUN_PEER");
+  if (act == FRC_ACT_AVX2) return run_avx2(c, layer, tokens, expert, gate, x, y, flags);
   if ((flags & FRC_RUN_PEER) && tokens > FRC_MAX_TOKENS)
     return fail(c, FRC_UNSUPPORTED, "FRC_RUN_PEER: up to %u tokens a call", FRC_MAX_TOKENS);
   int rc = validate(c, tokens, expert, gate, x);
@@ -1219,31 +1359,7 @@ int frc_run_flags(frc_context* c, unsigned layer, unsigned tokens, const uint16_
     c->last_T = tokens;
     memcpy(c->last_expert, expert, eb);
     memcpy(c->last_gate, gate, gb);
-    {
-      // [status][y] (16 + xb bytes, 16-byte aligned at both ends) to the
-      // mapped h_out by the publish kernel, up to 8 CTAs of 512 threads
-      const unsigned n16 = static_cast<unsigned>((16 + xb) / 16);
-      cudaLaunchConfig_t cfg = {};
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-      attr[0].val.programmaticStreamSerializationAllowed = 1;
-      cfg.gridDim = dim3(std::min(8u, (n16 + 1023) / 1024));
-      cfg.blockDim = dim3(512);
-      cfg.stream = c->stream;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      CK(cudaLaunchKernelEx(&cfg, publish_kernel, reinterpret_cast<const uint4*>(c->d_in + st_off),
-                            reinterpret_cast<uint4*>(c->h_out_dev), n16));
-    }
-    CK(cudaStreamSynchronize(c->stream));
-    const unsigned st = *c->h_status;
-    if (st & kStTimeout) {
-      const int rrc = reset_after_timeout(c, c->stream);
-      if (rrc) return rrc;
-    }
-    if (status_code(st)) return fail(c, status_code(st), "device status 0x%x", st);
-    memcpy(y, c->h_y, xb);  // published only after the whole layer succeeded
-    return FRC_OK;
+    return finish_small(c, st_off, xb, y);
   }
   CK(cudaMemcpyAsync(c->d_in, c->h_in, xb + gb + eb, cudaMemcpyHostToDevice, c->stream));
   rc = run_device(c, layer, tokens, reinterpret_cast<const uint16_t*>(c->d_in + xb + gb),

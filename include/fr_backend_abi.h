@@ -65,12 +65,18 @@ typedef struct fr_backend {
     int (*self_test)(const char *vectors_dir);
 } fr_backend;
 
-/* The two B200 backends.  "cuda": Q8 activations (the production path).
- * "cuda-f32": fp32 activations, the arithmetic of the reference's "ref". */
-extern const fr_backend fr_cuda, fr_cuda_f32;
+/* The B200 backends.  "cuda": Q8 activations (the production path).
+ * "cuda-f32": fp32 activations, the arithmetic of the reference's "ref".
+ * "cuda-avx2": the arithmetic of the reference's "avx2" backend
+ * (backends/avx2.c), its results at the worker count fr_cuda_avx2_workers
+ * sets. */
+extern const fr_backend fr_cuda, fr_cuda_f32, fr_cuda_avx2;
 
 /* Device the backends open on first load (default 0); FR_STATE once open. */
 int fr_cuda_select_device(int device);
 /* Releases the backend's device context; FR_STATE while blocks are loaded. */
 int fr_cuda_close(const fr_backend *backend);
+/* fr_cuda_avx2: the AVX2 backend worker count (1-32, default 1) whose job
+ * dealing and summation order it reproduces. */
+int fr_cuda_avx2_workers(unsigned workers);
 #endif

@@ -33,8 +33,18 @@ enum { FRC_Q8_0 = 8, FRC_Q4_K = 12, FRC_MXFP4 = 39 };
  * weights by fp32 activations (the arithmetic of backends/ref.c "ref").
  * FRC_ACT_Q8 first quantizes x per 64 and each 32-neuron hidden slice to int8
  * with the scheme of src/q4.c:37-61 (the "ref-q8" activation format,
- * backends/ref.c:66,85) and takes integer block dot products. */
-enum { FRC_ACT_F32 = 0, FRC_ACT_Q8 = 1 };
+ * backends/ref.c:66,85) and takes integer block dot products.
+ * FRC_ACT_AVX2 is the arithmetic of the reference's AVX2 backend
+ * (backends/avx2.c, default build): x as int8 with one fp32 scale per 256
+ * and int16 sums per 32 (quantize8, :184-203), its lane-wise fp32 sums in its
+ * order, fp32 SiLU, the hidden slice per 32, and the jobs (block, expert)
+ * dealt to frc_set_avx2_workers workers, whose sums are added in worker
+ * order.  Its results equal fr_avx2's at that worker count bit for bit, but
+ * for the C library's rare last-bit expf roundings (here exp is evaluated in
+ * double and rounded once).  frc_run / frc_run_flags (no run flag) only, up
+ * to FRC_MAX_TOKENS tokens, on the reference's native layout (Q4_K gate/up,
+ * MXFP4 down); FRC_UNSUPPORTED otherwise. */
+enum { FRC_ACT_F32 = 0, FRC_ACT_Q8 = 1, FRC_ACT_AVX2 = 2 };
 
 /* Model constants of src/model.h:18-27. */
 enum { FRC_MAX_BLOCKS = 20, FRC_ROUTED_EXPERTS = 512, FRC_SHARED_EXPERT = 512,
@@ -280,6 +290,12 @@ int frc_status(frc_context *c, void *stream);
  * untouched and the next call on the context runs normally.  No counterpart in
  * the reference (its timeouts are the plane's deadline, src/plane.c). */
 int frc_set_wait_limit(frc_context *c, uint64_t ns);
+/* FRC_ACT_AVX2: the worker count (1-32, default 1) whose job dealing and
+ * worker-ordered sum the run reproduces (backends/avx2.c:506-529, :703-708;
+ * fr_avx2 picks it with fr_avx2_configure).  Jobs are block-major over the
+ * blocks in load order, which becomes ascending after an unload, as the AVX2
+ * backend keeps its slots (backends/avx2.c:602-613). */
+int frc_set_avx2_workers(frc_context *c, unsigned workers);
 /* Tests and measurements: which kernel may serve one-token FRC_ACT_Q8 calls.
  * 1 (the default): the row-owner kernel (gate/up work dealt to every CTA in
  * chunks of 8 neurons, each CTA then forms its own rows of y from all

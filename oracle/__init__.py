@@ -49,7 +49,8 @@ class Oracle:
             "or_layer_bytes": (ctypes.c_size_t, [ctypes.c_uint, ctypes.c_uint, ctypes.c_uint]),
             "or_legacy_layer_bytes": (ctypes.c_size_t, [ctypes.c_uint]),
             "or_ref_run": (ctypes.c_int, [_vp, ctypes.c_uint, _vp, _vp, _vp, _vp, ctypes.c_int]),
-            "or_avx2_run": (ctypes.c_int, [_vp, ctypes.c_uint, _vp, _vp, _vp, _vp, ctypes.c_uint, ctypes.c_int]),
+            "or_avx2_run": (ctypes.c_int, [_vp, ctypes.c_uint, _vp, _vp, _vp, _vp, ctypes.c_uint, ctypes.c_int, _vp,
+                                           ctypes.c_uint]),
             "or_port_run": (ctypes.c_int, [_vp, ctypes.c_uint, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
             "or_prefill_run": (ctypes.c_int, [_vp, ctypes.c_uint, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t,
                                               _vp]),
@@ -119,14 +120,16 @@ class Oracle:
                                _p(np.ascontiguousarray(gate, np.float32)), _p(x), _p(y), int(q8))
         return rc, y
 
-    def avx2_run(self, m, expert, gate, x, workers=1, libm_expf=True):
+    def avx2_run(self, m, expert, gate, x, workers=1, libm_expf=True, order=None):
         """The AVX2 backend's arithmetic (backends/avx2.c) with `workers`
-        workers; libm_expf False gives the CUDA AVX2 mode's SiLU."""
+        workers; libm_expf False gives the CUDA AVX2 mode's SiLU; order: the
+        blocks in load order (None: ascending)."""
         x = np.ascontiguousarray(x, np.float32)
         y = np.zeros_like(x)
+        o = None if order is None else np.ascontiguousarray(order, np.uint8)
         rc = self.L.or_avx2_run(ctypes.byref(m), x.shape[0], _p(np.ascontiguousarray(expert, np.uint16)),
                                 _p(np.ascontiguousarray(gate, np.float32)), _p(x), _p(y), int(workers),
-                                int(bool(libm_expf)))
+                                int(bool(libm_expf)), None if o is None else _p(o), 0 if o is None else o.size)
         return rc, y
 
     def port_run(self, m, expert, gate, x, want_hidden=False):

@@ -424,9 +424,11 @@ static float avx2_swiglu(float v, float u, int libm_expf) {
  * worker accumulates its jobs' down terms with fmadd into its own zeroed
  * output in job order, and y is the fp32 sum of the workers' outputs in
  * worker order.  Gate/up: Q4_K routed rows, Q8_0 shared rows; hidden slice
- * quantized per 32; down: MXFP4 routed, Q8_0 shared. */
+ * quantized per 32; down: MXFP4 routed, Q8_0 shared.  `order` (norder
+ * entries) gives the blocks' load order, the backend's slot order
+ * (backends/avx2.c:602-606); NULL: ascending. */
 int or_avx2_run(const or_model *m, unsigned tokens, const uint16_t *expert, const float *gate,
-                const float *x, float *y, unsigned workers, int libm_expf) {
+                const float *x, float *y, unsigned workers, int libm_expf, const uint8_t *order, unsigned norder) {
     if (!model_ok(m) || m->legacy || m->gate_type != OR_Q4_K || m->down_type != OR_MXFP4 || !y || !workers ||
         workers > 32)
         return OR_INVALID;
@@ -436,7 +438,17 @@ int or_avx2_run(const or_model *m, unsigned tokens, const uint16_t *expert, cons
     if (!any_loaded(m)) return OR_STATE;
     if (d > 8192) return OR_INVALID;
     unsigned blocks[OR_BLOCKS], nb = 0;
-    for (unsigned b = 0; b < OR_BLOCKS; ++b) if (m->layer[b]) blocks[nb++] = b;
+    if (order) { /* the backend's slots in load order: every loaded block once */
+        unsigned seen = 0;
+        for (unsigned i = 0; i < norder; ++i) {
+            if (order[i] >= OR_BLOCKS || !m->layer[order[i]] || (seen >> order[i] & 1)) return OR_INVALID;
+            seen |= 1u << order[i];
+            blocks[nb++] = order[i];
+        }
+        for (unsigned b = 0; b < OR_BLOCKS; ++b) if (m->layer[b] && !(seen >> b & 1)) return OR_INVALID;
+    } else {
+        for (unsigned b = 0; b < OR_BLOCKS; ++b) if (m->layer[b]) blocks[nb++] = b;
+    }
     /* experts in first-named order, per-token gates and token masks */
     enum { MAXE = OR_MAX_TOKENS * OR_ACTIVE };
     unsigned ids[MAXE], mask[MAXE], ne = 0;

@@ -71,9 +71,11 @@ int or_ref_run(const or_model *m, unsigned tokens, const uint16_t *expert, const
  * (1-32) and the workers' outputs summed in order.  Native Q4_K / MXFP4
  * layout only.  libm_expf = 1 uses the C library's expf (bit-identical to
  * the compiled backend at the same worker count); 0 uses exp in double
- * rounded to fp32, the CUDA path's form.  y is written only on OR_OK. */
+ * rounded to fp32, the CUDA path's form.  order / norder: the blocks in
+ * load order (the backend's job order); NULL: ascending.  y is written only
+ * on OR_OK. */
 int or_avx2_run(const or_model *m, unsigned tokens, const uint16_t *expert, const float *gate,
-                const float *x, float *y, unsigned workers, int libm_expf);
+                const float *x, float *y, unsigned workers, int libm_expf, const uint8_t *order, unsigned norder);
 
 /* The CUDA Q8 path's arithmetic.  y as above.  When h is not NULL it receives
  * the hidden activations in the kernel's item order

@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol(built):
     assert "frc_run_device" in names and "fr_cuda" in names and len(names) > 30
     missing = [n for n in sorted(names) if not hasattr(lib, n)]
     assert not missing, missing
-    assert set(fb.EXPORTS) <= names | {"fr_cuda", "fr_cuda_f32"}
+    assert set(fb.EXPORTS) <= names | {"fr_cuda", "fr_cuda_f32", "fr_cuda_avx2"}
 
 
 def test_status_strings_and_geometry_without_gpu(built):

@@ -1,5 +1,7 @@
-"""The drop-in plugin tables fr_cuda ("cuda", Q8 activations) and fr_cuda_f32
-("cuda-f32") driven through their function pointers, as the reference's
+"""The drop-in plugin tables fr_cuda ("cuda", Q8 activations), fr_cuda_f32
+("cuda-f32") and fr_cuda_avx2 ("cuda-avx2", the AVX2 backend's arithmetic,
+against fr_avx2 at the same worker count) driven through their function
+pointers, as the reference's
 registry and node call a backend (src/backend.h:52-67), with the reference
 compiled from its own sources loaded into the same process
 (oracle/_ref/libfronk_ref.so, RTLD_GLOBAL): probe; load of full-size sparse
@@ -28,10 +30,13 @@ def _table(ref, name):
 
 
 @needs_ref
-@pytest.mark.parametrize("name,ref_name", [("fr_cuda", "ref-q8"), ("fr_cuda_f32", "ref")])
+@pytest.mark.parametrize("name,ref_name", [("fr_cuda", "ref-q8"), ("fr_cuda_f32", "ref"), ("fr_cuda_avx2", "avx2")])
 def test_table_against_reference(gpu, name, ref_name):
     ref = Reference(2560)
     be, rb = _table(ref, name), ref.backend(ref_name)
+    if name == "fr_cuda_avx2":  # both at two workers: the same job dealing and summation order
+        assert ref.configure_avx2(2, 2) == OK
+        assert fb.library().fr_cuda_avx2_workers(2) == OK
     hw = ref.Hw()
     assert be.probe(ctypes.byref(hw)) == OK
     assert b"B200" in hw.gpu or b"sm_100" in hw.gpu, hw.gpu

@@ -69,6 +69,44 @@ def test_avx2_restatement_matches_backend_bitwise(oracle, hidden):
 
 
 @needs_ref
+def test_avx2_restatement_follows_load_order(oracle):
+    """The backend deals jobs over its blocks in load order; after an unload
+    the remaining blocks are ascending again (backends/avx2.c:602-613)."""
+    hidden = 2048
+    ref = Reference(hidden)
+    g = fb.geometry(hidden)
+    layer, order = 6, [13, 2, 5]
+    e, gt, x = request(hidden, 3, SEED + 21, 0.5)
+    layers = make_layers(g, SEED, order, e, shared=True)
+    units = {}
+    for b, arr in layers.items():
+        u = SparseUnit(ref.unit_bytes())
+        u.write(layer * fb.layer_bytes(g), arr)
+        units[b] = u
+    be = ref.backend("avx2")
+    try:
+        _configure(ref, len(order), 2)
+        for b in order:
+            assert be.load(b, units[b].addr, ref.unit_bytes()) == OK
+        rc, y_ref = ref.run(be, ref.request(layer, e, gt, x))
+        m = oracle.model(hidden, Q4_K, MXFP4, layers)
+        rc2, y = oracle.avx2_run(m, e, gt, x, workers=2, order=order)
+        _, y_asc = oracle.avx2_run(m, e, gt, x, workers=2)
+        assert rc == rc2 == OK and np.array_equal(y.view(np.uint32), y_ref.view(np.uint32))
+        assert not np.array_equal(y_asc.view(np.uint32), y_ref.view(np.uint32))  # the order is visible
+        be.unload(2)
+        rest = {13: layers[13], 5: layers[5]}
+        rc, y_ref = ref.run(be, ref.request(layer, e, gt, x))
+        rc2, y = oracle.avx2_run(oracle.model(hidden, Q4_K, MXFP4, rest), e, gt, x, workers=2)
+        assert rc == rc2 == OK and np.array_equal(y.view(np.uint32), y_ref.view(np.uint32))
+    finally:
+        for b in (13, 5):
+            be.unload(b)
+        for u in units.values():
+            u.close()
+
+
+@needs_ref
 def test_avx2_restatement_numeric_cases(oracle):
     """A nonfinite Q8_0 scale of the shared expert and a reserved MXFP4
     exponent in a routed down row are NUMERIC in both."""
