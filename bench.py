@@ -276,6 +276,11 @@ def main():
     ap.add_argument("--prefill-gate", default="mxfp4", choices=["mxfp4", "q4k"],
                     help="gate/up rows of the --prefill workload: MXFP4 (configs[4]) or Q4_K (the reference's "
                          "unit layout)")
+    ap.add_argument("--act", default="q8", choices=["q8", "avx2"],
+                    help="avx2: the decode workload through FRC_ACT_AVX2, the arithmetic of the reference's AVX2 "
+                         "backend (host-buffer calls; 1 GPU)")
+    ap.add_argument("--avx2-workers", type=int, default=1,
+                    help="with --act avx2: the AVX2 backend worker count whose results the mode reproduces")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu: 2 layers of every slice loaded (2.2 GB), 5 layer launches "
                          "(with --prefill: one layer, three 512-token calls)")
@@ -302,6 +307,9 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.prefill:
         run_prefill_bench(args, rank, world, local)
+        return
+    if args.act == "avx2":
+        run_avx2_bench(args, rank, world, local)
         return
 
     import torch
@@ -528,10 +536,11 @@ def prefill_limiter(stage_ms, gu_bytes, peak, world):
             "bound": what}
 
 
-def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev, peer=False, T=1):
+def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev, peer=False, T=1, act=None):
     """tokens/s through the public call with host buffers: per layer the
     request is copied in, the layer runs, y is copied out (frc_run; at N>1
     the device entry point plus the all-reduce)."""
+    act = fb.ACT_Q8 if act is None else act
     import torch
     h2d = LAYERS * T * (HIDDEN * 4 + TOPK * 2 + 11 * 4)
     d2h = LAYERS * (T * HIDDEN * 4 + (16 if dist is None else 0))  # y (+ the status word frc_run reads with it)
@@ -546,7 +555,7 @@ def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev, peer=False, T=1):
             dist.barrier()
         t0 = time.perf_counter()
         for s in range(steps):
-            ctx.host_pass(0, es[s], gt[s], hs[s], fb.ACT_Q8, flags)
+            ctx.host_pass(0, es[s], gt[s], hs[s], act, flags)
         dt = time.perf_counter() - t0
         if dist is not None:
             t = torch.tensor([dt], device=dev)
@@ -592,6 +601,96 @@ def e2e_run(ctx, fb, ex, gt, x0, steps, dist, dev, peer=False, T=1):
             ("frc_host_pass_flags(FRC_RUN_PEER): frc_run_flags per layer on every rank, host buffers, the "
              "in-kernel NVLink reduce" if peer else
              "frc_run_device + NCCL all_reduce, pinned host copies each layer")}
+
+
+def run_avx2_bench(args, rank, world, local):
+    """The decode workload through FRC_ACT_AVX2 (fronk_b200/csrc/frc_avx2.cuh),
+    the arithmetic of the reference's AVX2 backend: one GPU, all 20 slices of
+    48 Q4_K/MXFP4 layers.  value: tokens/s of the device work of a pass, the
+    CUDA-event durations of each layer call's three launches (activation
+    quantization, one CTA a (block, expert) job, the worker-ordered
+    reduction) summed over the 48 layers; e2e: frc_host_pass with host
+    buffers, the call this mode is used through.  Parity: one full-size
+    layer against the oracle's restatement at the same worker count."""
+    import torch
+    import fronk_b200 as fb
+    from fronk_b200 import build as fbuild
+    if world > 1 or FMT != "q4k-mxfp4":
+        raise SystemExit("--act avx2: one GPU, the reference's native layout (--formats q4k-mxfp4)")
+    fbuild.build()
+    torch.cuda.set_device(local)
+    blocks = list(range(SLICES))
+    g = fb.geometry(HIDDEN, LAYERS, fb.Q4_K, fb.MXFP4)
+    ctx = fb.Context(local, HIDDEN, LAYERS, fb.Q4_K, fb.MXFP4)
+    pool = np.concatenate([fb.synth_slice(g, SEED, i) for i in range(POOL)])
+    ctx.pool_load(pool, fb.synth_shared(g, SEED, 1 << 20))
+    for b in blocks:
+        for l in range(LAYERS):
+            ctx.fill_layer(b, l, SEED)
+    ctx.set_avx2_workers(args.avx2_workers)
+    ctx.avx2_timing(True)
+    T = args.tokens
+    steps = max(3, min(args.steps, 20))
+    total = args.warmup + steps
+    ex, gt, x0 = step_routing(total, T)
+    stage = []
+    sampler = ClockSampler(local)
+    sampler.start()
+    for s in range(total):
+        if s == args.warmup:
+            sampler.mark_start()
+        for l in range(LAYERS):
+            rc, _ = ctx.run(l, ex[s, l], gt[s, l], x0[s], fb.ACT_AVX2)
+            if rc:
+                raise fb.FrcError(rc, "avx2 run", ctx.last_error)
+            if s >= args.warmup:
+                stage.append(ctx.avx2_times())
+    sampler.mark_end()
+    clocks = sampler.stop()
+    stage = np.array(stage, np.float64)                      # [steps * layers][3] ms
+    layer_ms = stage.sum(axis=1).mean()
+    ms_per_step = layer_ms * LAYERS
+    unique = float(np.mean([len(np.unique(ex[s, l])) for s in range(args.warmup, total) for l in range(LAYERS)]))
+    bytes_per_launch = unique * len(blocks) * SLICE_BYTES
+    job_ms = stage[:, 1].mean()
+    peak, peak_src = peaks()
+    achieved = bytes_per_launch / (job_ms * 1e-3) / 1e9
+    e2e = e2e_run(ctx, fb, ex, gt, x0, max(3, min(args.steps, 20)), None, None, False, T, act=fb.ACT_AVX2)
+    # parity: one full-size layer of the filled units against the restatement
+    from oracle import Oracle
+    orc = Oracle()
+    e, gte, x = fb.synth_request(HIDDEN, 2, 777)      # no shared gate: the host copies hold routed slices
+    layers = _host_layers(fb, g, pool, blocks, e)
+    m = orc.model(HIDDEN, fb.Q4_K, fb.MXFP4, layers)
+    rc, y = ctx.run(5, e, gte, x, fb.ACT_AVX2)
+    rc2, want = orc.avx2_run(m, e, gte, x, workers=args.avx2_workers, libm_expf=False)
+    parity = {"vs": "or_avx2_run (oracle restatement of backends/avx2.c, same worker count and exp form)",
+              "layer": 5, "tokens": 2, "blocks": len(blocks),
+              "bitwise_equal": bool(rc == rc2 == 0 and np.array_equal(np.asarray(y, np.float32).view(np.uint32),
+                                                                      want.view(np.uint32))),
+              "max_rel_l2": _rel(want, y) if rc == rc2 == 0 else None}
+    if rank == 0:
+        cfg = config(1, tokens=T, unique_per_layer=unique)
+        cfg["activations"] = ("FRC_ACT_AVX2: the reference AVX2 backend's quantize8 (int8 per 256, int16 sums "
+                              "per 32), its fp32 lane order, jobs dealt to %d worker(s)" % args.avx2_workers)
+        line = {
+            "metric": METRIC + " (FRC_ACT_AVX2)", "value": T * 1000.0 / ms_per_step, "unit": "tokens/s",
+            "n_gpus": 1, "steps": steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic", "config": cfg,
+            "value_source": "sum over the 48 layer calls of the CUDA-event durations of their three launches",
+            "stage_us": {"quantize": stage[:, 0].mean() * 1e3, "jobs": job_ms * 1e3,
+                         "reduce": stage[:, 2].mean() * 1e3},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                         "kernel": "avx2_job_kernel (one CTA a (block, expert) job)",
+                         "algorithmic_bytes_per_launch": bytes_per_launch, "launch_us": job_ms * 1e3},
+            "gpu_launches": 4 * LAYERS * steps, "clocks": clocks, "e2e": e2e, "parity": parity,
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(3, 1) if T == 1 else cpu_baseline(1, 1, T)
+        emit(line)
+    ctx.close()
 
 
 def _host_layers(fb, g, pool, blocks, experts, layer=5):

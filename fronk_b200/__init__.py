@@ -67,6 +67,8 @@ _SIGS = {
     "frc_probe_device": (_int, [_int, ctypes.c_char_p, _sz, _vp, _vp]),
     "frc_set_wait_limit": (_int, [_vp, _u64]),
     "frc_set_avx2_workers": (_int, [_vp, ctypes.c_uint]),
+    "frc_avx2_timing": (_int, [_vp, _int]),
+    "frc_avx2_times": (_int, [_vp, _vp]),
     "frc_debug_barrier_extra": (_int, [_vp, _u32]),
     "frc_debug_layer_variant": (_int, [_vp, _int]),
     "frc_unload_unit": (_int, [_vp, _int]),
@@ -376,6 +378,16 @@ class Context:
     def set_avx2_workers(self, workers):
         """frc_set_avx2_workers: the AVX2 backend worker count ACT_AVX2 reproduces."""
         self._check(self.lib.frc_set_avx2_workers(self.h, int(workers)), "set_avx2_workers")
+
+    def avx2_timing(self, enable=True):
+        """frc_avx2_timing: CUDA events around the three ACT_AVX2 launches of each call."""
+        self._check(self.lib.frc_avx2_timing(self.h, 1 if enable else 0), "avx2_timing")
+
+    def avx2_times(self):
+        """ms of the last ACT_AVX2 call's quantization, job and reduction launches."""
+        ms = np.zeros(3, np.float32)
+        self._check(self.lib.frc_avx2_times(self.h, _ptr(ms)), "avx2_times")
+        return ms
 
     def set_wait_limit(self, ns):
         """frc_set_wait_limit: every bounded wait of the layer kernel gives up after ns."""

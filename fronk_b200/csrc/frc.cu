@@ -268,6 +268,10 @@ struct frc_context {
   const uint8_t* tmap_of[FRC_MAX_BLOCKS][FRC_MAX_LAYERS] = {};
   // optional CUDA events around the five prefill stages (frc_prefill_timing)
   cudaEvent_t pf_ev[6] = {};
+  // and around the three FRC_ACT_AVX2 launches (frc_avx2_timing)
+  cudaEvent_t av_ev[4] = {};
+  bool av_timing = false, av_timed = false, av_attr = false;
+  int av_stage_per_sm = 0;  // CTAs of the staged AVX2 job kernel an SM holds
   bool pf_timing = false, pf_timed = false;
   // bounded waits of the layer kernel (frc_set_wait_limit) and the test-only
   // grid-barrier offset (frc_debug_barrier_extra)
@@ -1059,6 +1063,7 @@ int frc_close(frc_context* c) {
   cudaFreeHost(c->h_in); cudaFreeHost(c->h_out);
   if (c->stream) cudaStreamDestroy(c->stream);
   for (auto e : c->pf_ev) if (e) cudaEventDestroy(e);
+  for (auto e : c->av_ev) if (e) cudaEventDestroy(e);
   delete c;
   return FRC_OK;
 }
@@ -1278,15 +1283,35 @@ static int run_avx2(frc_context* c, unsigned layer, unsigned T, const uint16_t* 
     for (unsigned t = 0; t < T; ++t)
       if (mask[e] >> t & 1u) pgate[P++] = eg[e][t];
   }
+  // each token's fmadd chains: its term slots (s * P + pair) in job order,
+  // jobs (slot s, expert j) block-major and dealt round robin to W workers
+  const unsigned W = c->avx2_workers, jobs = S * E, stride = S * FRC_ACTIVE;
+  constexpr unsigned kBound = kAvx2MaxWorkers + 1;
+  uint16_t bounds[kMaxTokens * kBound], chain[kMaxTokens * kMaxBlocks * FRC_ACTIVE];
+  for (unsigned t = 0; t < T; ++t) {
+    unsigned n = 0;
+    for (unsigned w = 0; w < W; ++w) {
+      bounds[t * kBound + w] = static_cast<uint16_t>(n);
+      for (unsigned idx = w; idx < jobs; idx += W) {
+        const unsigned s = idx / E, j = idx % E;
+        if (mask[j] >> t & 1u)
+          chain[t * stride + n++] = static_cast<uint16_t>(s * P + pbase[j] + __builtin_popcount(mask[j] & ((1u << t) - 1u)));
+      }
+    }
+    bounds[t * kBound + W] = static_cast<uint16_t>(n);
+  }
   const unsigned d = c->g.hidden;
   const size_t xb = sizeof(float) * T * d, po = (xb + 15) & ~size_t(15);
-  const size_t st_off = (po + 12 * kMaxPairs + 15) & ~size_t(15);
+  const size_t bo = po + 12 * kMaxPairs, co = bo + 2 * kMaxTokens * kBound;
+  const size_t st_off = (co + 2 * static_cast<size_t>(T) * stride + 15) & ~size_t(15);
   uint8_t* h = c->h_in;
   memcpy(h, x, xb);
   memcpy(h + po, mask, 4 * E);
   memcpy(h + po + 4 * kMaxPairs, pgate, 4 * P);
   memcpy(h + po + 8 * kMaxPairs, ids, 2 * E);
   memcpy(h + po + 10 * kMaxPairs, pbase, 2 * E);
+  memcpy(h + bo, bounds, 2 * static_cast<size_t>(T) * kBound);
+  memcpy(h + co, chain, 2 * static_cast<size_t>(T) * stride);
   memset(h + st_off, 0, 16);
   CK(cudaMemcpyAsync(c->d_in, h, st_off + 16, cudaMemcpyHostToDevice, c->stream));
   const uint8_t* dp = c->d_in + po;
@@ -1295,6 +1320,9 @@ static int run_avx2(frc_context* c, unsigned layer, unsigned T, const uint16_t* 
   a.pgate = reinterpret_cast<const float*>(dp + 4 * kMaxPairs);
   a.ids = reinterpret_cast<const uint16_t*>(dp + 8 * kMaxPairs);
   a.pbase = reinterpret_cast<const uint16_t*>(dp + 10 * kMaxPairs);
+  a.bounds = reinterpret_cast<const uint16_t*>(c->d_in + bo);
+  a.chain = reinterpret_cast<const uint16_t*>(c->d_in + co);
+  a.chain_stride = stride;
   a.xq = reinterpret_cast<int8_t*>(c->avx2_x);
   a.xd = reinterpret_cast<float*>(c->avx2_x + static_cast<size_t>(kMaxTokens) * d);
   a.xs = reinterpret_cast<int16_t*>(c->avx2_x + static_cast<size_t>(kMaxTokens) * (d + d / 256 * 4));
@@ -1302,20 +1330,63 @@ static int run_avx2(frc_context* c, unsigned layer, unsigned T, const uint16_t* 
   a.coef = c->gsv;
   a.status = reinterpret_cast<unsigned*>(c->d_in + st_off);
   a.y = reinterpret_cast<float*>(c->d_in + st_off + 16);
-  a.d = d; a.T = T; a.S = S; a.E = E; a.P = P; a.W = c->avx2_workers;
+  a.d = d; a.T = T; a.S = S; a.E = E; a.P = P; a.W = W;
   a.row_bytes = static_cast<unsigned>(c->row_bytes); a.proj_bytes = static_cast<unsigned>(c->proj_bytes);
   a.slice_bytes = static_cast<unsigned>(c->slice_bytes);
   a.shared_row = static_cast<unsigned>(c->shared_row); a.shared_proj = static_cast<unsigned>(c->shared_proj);
+  const bool timed = c->av_timing;
+  auto mark = [&](unsigned i) { if (timed) cudaEventRecord(c->av_ev[i], c->stream); };
+  mark(0);
   avx2_quantize_kernel<<<T, 256, 0, c->stream>>>(a);
-  avx2_job_kernel<<<S * E, 256, 0, c->stream>>>(a);
-  avx2_reduce_kernel<<<(T * d + 255) / 256, 256, 0, c->stream>>>(a);
+  mark(1);
+  // Staging the routed slices in shared memory holds one or two CTAs on an
+  // SM, with no overlap of a CTA's copy and its arithmetic: it pays when all
+  // the jobs run in one wave (one token: 22 us against 29 us for the jobs of
+  // a decode48 layer) and costs when they do not (16 tokens: 171 against 137).
+  bool stage = false;
+  if (c->slice_bytes <= kAvx2StageMax) {
+    if (!c->av_attr) {
+      CK(cudaFuncSetAttribute(avx2_job_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kAvx2StageMax)));
+      CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c->av_stage_per_sm, avx2_job_kernel<true>, 256,
+                                                       c->slice_bytes));
+      c->av_attr = true;
+    }
+    stage = static_cast<unsigned>(c->av_stage_per_sm) * static_cast<unsigned>(c->sms) >= S * E;
+  }
+  if (stage) {
+    avx2_job_kernel<true><<<S * E, 256, c->slice_bytes, c->stream>>>(a);
+  } else {
+    avx2_job_kernel<false><<<S * E, 256, 0, c->stream>>>(a);
+  }
+  mark(2);
+  avx2_reduce_kernel<<<T * d / 64, 64, 0, c->stream>>>(a);
+  mark(3);
   CK(cudaGetLastError());
+  c->av_timed = timed;
   c->launches += 3;
   return finish_small(c, st_off, xb, y);
 }
 
+int frc_avx2_timing(frc_context* c, int enable) {
+  if (!c) return FRC_INVALID;
+  CK(cudaSetDevice(c->device));
+  if (enable && !c->av_ev[0])
+    for (auto& e : c->av_ev) CK(cudaEventCreate(&e));
+  c->av_timing = enable != 0;
+  return FRC_OK;
+}
+
+int frc_avx2_times(frc_context* c, float* ms) {
+  if (!c || !ms || !c->av_timed) return fail(c, FRC_INVALID, "no timed FRC_ACT_AVX2 run");
+  CK(cudaSetDevice(c->device));
+  CK(cudaEventSynchronize(c->av_ev[3]));
+  for (unsigned i = 0; i < 3; ++i) CK(cudaEventElapsedTime(&ms[i], c->av_ev[i], c->av_ev[i + 1]));
+  return FRC_OK;
+}
+
 int frc_set_avx2_workers(frc_context* c, unsigned workers) {
-  if (!c || workers < 1 || workers > 32) return fail(c, FRC_INVALID, "FRC_ACT_AVX2 workers: 1-32");
+  if (!c || workers < 1 || workers > kAvx2MaxWorkers) return fail(c, FRC_INVALID, "FRC_ACT_AVX2 workers: 1-32");
   c->avx2_workers = workers;
   return FRC_OK;
 }

@@ -31,6 +31,8 @@
 #pragma once
 #include "frc_device.cuh"
 
+constexpr unsigned kAvx2MaxWorkers = 32;
+
 struct Avx2Params {
   const uint8_t* base[kMaxBlocks];  // the layer region of each loaded block, in job order
   const float* x;                   // [T][d]
@@ -44,8 +46,10 @@ struct Avx2Params {
   float* terms;                     // [S][P][d] down terms of each job and token
   float* coef;                      // [S][P] md * gate
   float* y;                         // [T][d]
+  const uint16_t* chain;            // [T][chain_stride] per token: its term slots (s * P + pair) in job order, worker by worker
+  const uint16_t* bounds;           // [T][kAvx2MaxWorkers + 1] where each worker's part of the chain starts
   unsigned* status;
-  unsigned d, T, S, E, P, W;
+  unsigned d, T, S, E, P, W, chain_stride;
   unsigned row_bytes, proj_bytes, slice_bytes, shared_row, shared_proj;
 };
 
@@ -103,15 +107,49 @@ __device__ __forceinline__ float av_hsum8(float v) {
   return __fadd_rn(b, __shfl_down_sync(0xffffffffu, b, 2, 8));
 }
 
+constexpr unsigned kAvx2StageMax = 220u * 1024u;  // routed slices up to this size are staged in shared memory
+constexpr unsigned kAvx2Chunk = 32768u;           // bytes a bulk copy of the staging moves
+
 // One job: 32 neurons of expert ids[j] in block slot s, for every token of
-// the expert.  Thread = neuron (tid / 8) x lane (tid % 8).
+// the expert.  Thread = neuron (tid / 8) x lane (tid % 8).  STAGE: a routed
+// job first brings its whole slice (gate rows, up rows, down rows: one
+// contiguous run of slice_bytes, dynamic shared memory of that size) into
+// shared memory with bulk copies on one mbarrier, then reads only shared
+// memory; the shared expert's slice, which is larger, is read from global
+// memory.  The wait for the copies is bounded: on a timeout the CTA records
+// it, waits once more (bounded) for its own copies, and returns.
+template <bool STAGE>
 __global__ void __launch_bounds__(256) avx2_job_kernel(Avx2Params a) {
+  extern __shared__ __align__(128) uint8_t av_slice[];
   __shared__ float sh_h[32];
   __shared__ __align__(16) int8_t sh_mid[32];
+  __shared__ uint64_t av_bar;
+  __shared__ int av_ok;
   const unsigned tid = threadIdx.x, n = tid >> 3, k = tid & 7, lane = tid & 31;
   const unsigned s = blockIdx.x / a.E, j = blockIdx.x % a.E, d = a.d, id = a.ids[j];
   const bool shared = id >= FRC_ROUTED_EXPERTS;
   const uint8_t* p = a.base[s] + static_cast<size_t>(id) * a.slice_bytes;
+  if (STAGE && !shared) {
+    if (tid == 0) {
+      mbar_init(&av_bar, 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+      mbar_expect_tx(&av_bar, a.slice_bytes);
+      for (unsigned o = 0; o < a.slice_bytes; o += kAvx2Chunk)
+        bulk_g2s(av_slice + o, p + o, min(kAvx2Chunk, a.slice_bytes - o), &av_bar);
+      const bool ok = mbar_wait(&av_bar, 0);
+      if (!ok) {
+        atomicOr(a.status, kStTimeout);
+        mbar_wait(&av_bar, 0);  // its own copies end before the CTA does
+      }
+      av_ok = ok;
+    }
+    __syncthreads();
+    if (!av_ok) return;
+    p = av_slice;
+  }
   const unsigned in_row = shared ? a.shared_row : a.row_bytes, proj = shared ? a.shared_proj : a.proj_bytes;
   const uint8_t* grow = p + static_cast<size_t>(n) * in_row;
   const uint8_t* urow = grow + proj;
@@ -126,6 +164,7 @@ __global__ void __launch_bounds__(256) avx2_job_kernel(Avx2Params a) {
     if (!shared) {
       const int16_t* xs = a.xs + t * (d / 32);
       float accg = 0.f, accu = 0.f, mins = 0.f;
+#pragma unroll 4
       for (unsigned sb = 0; sb < d / 256; ++sb) {
         const uint8_t* gb = grow + sb * 144;
         const uint8_t* ub = urow + sb * 144;
@@ -156,7 +195,7 @@ __global__ void __launch_bounds__(256) avx2_job_kernel(Avx2Params a) {
         accu = __fmaf_rn(__int2float_rn(isu), __fmul_rn(av_half(uh), xds), accu);
         // lanes 0-3: the gate row's min lanes, lanes 4-7: the up row's
         const unsigned mj = k & 3;
-        const uint32_t mw = k < 4 ? gm[mj >> 1] : um[mj >> 1];
+        const uint32_t mw = k < 4 ? (mj >> 1 ? gm[1] : gm[0]) : (mj >> 1 ? um[1] : um[0]);
         const unsigned msh = 16 * (mj & 1);
         const int mm = static_cast<int>((mw >> msh) & 0xff) * xs[sb * 8 + 2 * mj] +
                        static_cast<int>((mw >> (msh + 8)) & 0xff) * xs[sb * 8 + 2 * mj + 1];
@@ -245,23 +284,40 @@ __global__ void __launch_bounds__(256) avx2_job_kernel(Avx2Params a) {
 }
 
 // y[t][r]: the workers' fmadd chains over their jobs, added in worker order.
-__global__ void __launch_bounds__(256) avx2_reduce_kernel(Avx2Params a) {
-  const unsigned i = blockIdx.x * 256 + threadIdx.x;
-  if (i >= a.T * a.d) return;
-  const unsigned t = i / a.d, r = i % a.d, jobs = a.S * a.E;
+// The chains come from the plan (each token's term slots in job order,
+// worker by worker).  A CTA covers 64 values of one token (d is a multiple
+// of 64): it first stages the token's slots and their md * gate factors in
+// shared memory, then each thread issues its term loads 32 at a time and
+// applies the fmadds in order.
+__global__ void __launch_bounds__(64) avx2_reduce_kernel(Avx2Params a) {
+  constexpr unsigned kBatch = 32, kMaxChain = kMaxBlocks * FRC_ACTIVE;
+  __shared__ uint16_t sq[kMaxChain];
+  __shared__ float sc[kMaxChain];
+  __shared__ uint16_t sb[kAvx2MaxWorkers + 1];
+  const unsigned i = blockIdx.x * 64 + threadIdx.x;  // every CTA lies within one token
+  const unsigned t = blockIdx.x * 64 / a.d, r = i % a.d;
+  const uint16_t* bound = a.bounds + t * (kAvx2MaxWorkers + 1);
+  const unsigned n = bound[a.W];
+  for (unsigned e = threadIdx.x; e < n; e += 64) {
+    const unsigned q = a.chain[t * a.chain_stride + e];
+    sq[e] = static_cast<uint16_t>(q);
+    sc[e] = a.coef[q];
+  }
+  for (unsigned w = threadIdx.x; w <= a.W; w += 64) sb[w] = bound[w];
+  __syncthreads();
   float value = 0.f;
   for (unsigned w = 0; w < a.W; ++w) {
     float o = 0.f;
-    unsigned s = w / a.E, j = w % a.E;
-    for (unsigned idx = w; idx < jobs; idx += a.W) {
-      const uint32_t mk = a.mask[j];
-      if (mk >> t & 1u) {
-        const unsigned p = a.pbase[j] + __popc(mk & ((1u << t) - 1u));
-        o = __fmaf_rn(a.terms[(static_cast<size_t>(s) * a.P + p) * a.d + r], a.coef[s * a.P + p], o);
-      }
-      j += a.W;
-      while (j >= a.E) { j -= a.E; ++s; }
+    unsigned e = sb[w];
+    const unsigned end = sb[w + 1];
+    for (; e + kBatch <= end; e += kBatch) {
+      float tv[kBatch];
+#pragma unroll
+      for (unsigned k = 0; k < kBatch; ++k) tv[k] = a.terms[static_cast<size_t>(sq[e + k]) * a.d + r];
+#pragma unroll
+      for (unsigned k = 0; k < kBatch; ++k) o = __fmaf_rn(tv[k], sc[e + k], o);
     }
+    for (; e < end; ++e) o = __fmaf_rn(a.terms[static_cast<size_t>(sq[e]) * a.d + r], sc[e], o);
     value = __fadd_rn(value, o);
   }
   if (!isfinite(value)) atomicOr(a.status, kStNumeric);

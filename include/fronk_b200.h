@@ -296,6 +296,12 @@ int frc_set_wait_limit(frc_context *c, uint64_t ns);
  * blocks in load order, which becomes ascending after an unload, as the AVX2
  * backend keeps its slots (backends/avx2.c:602-613). */
 int frc_set_avx2_workers(frc_context *c, unsigned workers);
+/* Event timing of FRC_ACT_AVX2 calls: while enabled, each records CUDA events
+ * on the context's stream around its three launches (activation
+ * quantization, jobs, reduction); frc_avx2_times writes the last call's three
+ * durations in ms.  For measurement. */
+int frc_avx2_timing(frc_context *c, int enable);
+int frc_avx2_times(frc_context *c, float *ms);
 /* Tests and measurements: which kernel may serve one-token FRC_ACT_Q8 calls.
  * 1 (the default): the row-owner kernel (gate/up work dealt to every CTA in
  * chunks of 8 neurons, each CTA then forms its own rows of y from all
