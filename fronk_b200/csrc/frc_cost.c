@@ -55,7 +55,7 @@ static int cmp_double(const void *a, const void *b) {
 int frc_costmodel_measure(frc_context *c, const frc_geometry *g, unsigned layer, unsigned burst_max,
                           unsigned samples, int act, frc_costmodel *out) {
     if (!c || !g || !out || burst_max < 2 || burst_max > FRC_COST_MAX_BURST || samples < 1 || samples > 1000 ||
-        g->hidden == 0 || g->hidden > 8192 || (act != FRC_ACT_Q8 && act != FRC_ACT_F32))
+        g->hidden == 0 || g->hidden > 8192 || (act != FRC_ACT_Q8 && act != FRC_ACT_F32 && act != FRC_ACT_AVX2))
         return FRC_INVALID;
     uint32_t mask = 0;
     int rc = frc_loaded_mask(c, &mask);

@@ -174,7 +174,8 @@ typedef struct {
  * nonpositive slope. */
 int frc_costmodel_fit(const double *ns, const uint64_t *bytes, unsigned n, frc_costmodel *out);
 /* Measures and fits it on this context: `samples` synchronous frc_run calls
- * of layer `layer` at each burst 1..burst_max in activation mode `act`
+ * of layer `layer` at each burst 1..burst_max in activation mode `act` (any
+ * of the three; the fallback bench of each plugin table measures its own)
  * (distinct seeded routing, the shared expert active), medians, bytes =
  * loaded blocks x (10 x burst x slice + shared slice) (src/bench.c:157-160).
  * g: the context's geometry.  FRC_STATE when nothing is loaded. */
