@@ -250,6 +250,21 @@ class Reference:
             self.L.fr_avx2_set_tuning(blocks, burst, workers, 0)
         return self.L.fr_avx2_configure(blocks, 1)
 
+    def avx2_engine_workers(self):
+        """The worker count of fr_avx2's current engine (fr_avx2_sample_get,
+        src/avx2.h:11-15): fr_avx2_configure caps the configured count at the
+        host's logical CPUs minus one (backends/avx2.c:739-741)."""
+        class Sample(ctypes.Structure):
+            _fields_ = [("runs", ctypes.c_uint64), ("weight_bytes", ctypes.c_uint64),
+                        ("hot_allocations", ctypes.c_uint64), ("blocks", ctypes.c_uint),
+                        ("unique_experts", ctypes.c_uint), ("workers", ctypes.c_uint), ("features", ctypes.c_uint),
+                        ("prefetch", ctypes.c_uint), ("total_ns", ctypes.c_double)]
+        smp = Sample()
+        self.L.fr_avx2_sample_get.argtypes = [ctypes.c_void_p]
+        if self.L.fr_avx2_sample_get(ctypes.byref(smp)):
+            raise RuntimeError("fr_avx2_sample_get failed")
+        return smp.workers
+
     def backend_addr(self, sym, lib=None):
         return ctypes.addressof(self.Backend.in_dll(lib or self.L, sym))
 

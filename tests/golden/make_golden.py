@@ -83,6 +83,9 @@ def generate(hidden):
             assert ref.configure_avx2(len(BLOCKS), workers) == OK
             for b in BLOCKS:  # ascending: the backend's job order follows load order
                 assert avx2.load(b, units[b].addr, ref.unit_bytes()) == OK
+            # fr_avx2_configure leaves the host one logical CPU: the engine
+            # must run the worker count the fixture is named for
+            assert ref.avx2_engine_workers() == workers, "host too small for %d AVX2 workers" % workers
             try:
                 for i, (e, gt, x) in enumerate(cases):
                     rc, y = ref.run(avx2, ref.request(LAYER, e, gt, x))

@@ -69,6 +69,50 @@ def test_avx2_restatement_matches_backend_bitwise(oracle, hidden):
 
 
 @needs_ref
+def test_avx2_restatement_worker_sweep(oracle):
+    """Seeded sweep of worker counts (up to 16), bursts and shared gates at
+    d = 2048: the restatement equals the compiled backend bit for bit in
+    every case, at the worker count the backend's engine actually runs
+    (fr_avx2_configure leaves the host one logical CPU)."""
+    hidden = 2048
+    ref = Reference(hidden)
+    g = fb.geometry(hidden)
+    layer, blocks = 17, [0, 4, 9, 19]
+    rng = np.random.default_rng(SEED)
+    cases = [(int(rng.integers(1, 9)), float(rng.choice([0.0, 0.3])), bool(rng.integers(0, 2)), int(seed))
+             for seed in rng.integers(1, 1 << 30, size=8)]
+    reqs = [request(hidden, t, s, sh, distinct) for t, sh, distinct, s in cases]
+    experts = np.concatenate([r[0].ravel() for r in reqs])
+    layers = make_layers(g, SEED + 1, blocks, experts, shared=True)
+    units = {}
+    for b, arr in layers.items():
+        u = SparseUnit(ref.unit_bytes())
+        u.write(layer * fb.layer_bytes(g), arr)
+        units[b] = u
+    m = oracle.model(hidden, Q4_K, MXFP4, layers)
+    be = ref.backend("avx2")
+    try:
+        for workers in (2, 4, 5, 7, 8, 16):
+            _configure(ref, len(blocks), workers)
+            for b in blocks:
+                assert be.load(b, units[b].addr, ref.unit_bytes()) == OK
+            engine = ref.avx2_engine_workers()
+            assert 1 <= engine <= workers
+            try:
+                for e, gt, x in reqs:
+                    rc, y_ref = ref.run(be, ref.request(layer, e, gt, x))
+                    rc2, y = oracle.avx2_run(m, e, gt, x, workers=engine, libm_expf=True)
+                    assert rc == rc2 == OK
+                    assert np.array_equal(y.view(np.uint32), y_ref.view(np.uint32)), (workers, engine, x.shape)
+            finally:
+                for b in blocks:
+                    be.unload(b)
+    finally:
+        for u in units.values():
+            u.close()
+
+
+@needs_ref
 def test_avx2_restatement_follows_load_order(oracle):
     """The backend deals jobs over its blocks in load order; after an unload
     the remaining blocks are ascending again (backends/avx2.c:602-613)."""
